@@ -1,0 +1,172 @@
+/*
+ * myl_w8a16.h — C ABI of libmyl_w8a16.so, the B200 (sm_100a) implementation of
+ * Myelith's W8A16 integer linear layer (int8 weights x int16 activations,
+ * exact integer accumulation, power-of-two round-to-nearest-even requant).
+ *
+ * Every entry point is bit-exact against the reference CPU path. The
+ * reference counterpart of each entry point is cited beside it, as
+ * <file>:<line> inside the Myelith project (INTEGER_LLM/...).
+ *
+ * Conventions
+ *  - Return value: 0 (MYL_OK) or an MYL_ERR_* code; myl_last_error() gives a
+ *    message for the calling thread. The reference panics in the same cases
+ *    (shape asserts, debug-build integer overflow); its Rust binding turns a
+ *    nonzero status back into a panic.
+ *  - W is row-major [out_features][in_features] int8 (one row per output
+ *    channel), as QTensor.data holds it (runtime/src/model.rs:28-35).
+ *  - Activations are row-major [M][in_features] int16; M is the number of
+ *    independent rows (tokens). Every output row equals the reference's
+ *    per-token GEMV result (the reference loops forward_token per token).
+ *  - Entry points named *_dev take device pointers and a cudaStream_t (passed
+ *    as void*), enqueue work and return without synchronising. All other
+ *    entry points take host pointers and return after the result is in host
+ *    memory.
+ *  - A context belongs to one device. Calls on one context are serialised by
+ *    the caller (the reference callers are single-threaded).
+ *  - There is no CPU fallback: without a usable sm_100 device myl_init fails.
+ */
+#ifndef MYL_W8A16_H
+#define MYL_W8A16_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MYL_ABI_VERSION 1
+
+enum myl_status {
+  MYL_OK = 0,
+  MYL_ERR_SHAPE = 1,       /* length/shape mismatch: assert_eq! in linear.rs:51-58, :95-107 */
+  MYL_ERR_OVERFLOW = 2,    /* u8/i8 overflow or shift >= width in the requant (debug panic) */
+  MYL_ERR_CUDA = 3,        /* a CUDA runtime call failed */
+  MYL_ERR_ARG = 4,         /* null pointer, bad handle or bad enum */
+  MYL_ERR_DEVICE = 5,      /* a kernel reported an error (e.g. a bounded wait ran out) */
+  MYL_ERR_UNSUPPORTED = 6, /* device is not sm_100 or a size is beyond a kernel limit */
+};
+
+/* Requant modes (myl_requant_create). */
+enum myl_rq_mode {
+  MYL_RQ_SHIFT_I16 = 0, /* clamp_i16(rescale_i64(acc, w_shift+act_frac, out_frac)) linear.rs:66,115 */
+  MYL_RQ_SHIFT_I32 = 1, /* clamp_i32(rescale_i64(...)), the LM head runtime/src/model.rs:303-305 */
+  MYL_RQ_MULT_I16 = 2,  /* clamp_i16(rne_i128(acc * mult[r], shift[r])), shift in [0,126] */
+};
+
+typedef struct myl_ctx myl_ctx;
+typedef struct myl_weight myl_weight;
+typedef struct myl_requant myl_requant;
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* myl_last_error(void);
+int myl_abi_version(void);
+
+/* Replaces CudaBackend::init (kernels/src/backends/cuda.rs:93-107): selects
+ * the device, checks for sm_100, creates the stream and workspaces. */
+int myl_init(int device, myl_ctx** out);
+int myl_destroy(myl_ctx* ctx);
+/* Replaces CudaBackend::sm_version / device_id (cuda.rs:109-115). */
+int myl_device_info(const myl_ctx* ctx, int* device, int* sm_version, int* num_sms);
+
+/* Uploads one weight matrix once (the reference keeps it in host memory for
+ * the model's lifetime, runtime/src/model.rs:28-35). W rows are ldw bytes
+ * apart (ldw >= in_features; a column slice of a larger matrix for
+ * row-parallel sharding is W + k0 with ldw = full width). */
+int myl_weight_register(myl_ctx* ctx, const int8_t* W, int64_t out_features, int64_t in_features,
+                        int64_t ldw, const uint8_t* w_shifts, myl_weight** out);
+int myl_weight_release(myl_ctx* ctx, myl_weight* w);
+
+/* --- Free-function mirrors (host pointers, synchronous) --------------------- */
+
+/* linear_w8a16 (kernels/src/linear.rs:43-70): y[M][N] int16. */
+int myl_linear_w8a16(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
+                     uint8_t act_frac_bits, uint8_t out_frac_bits, int16_t* y);
+
+/* linear_w8a16_pc (linear.rs:87-119): out_frac_bits[N], one per output channel. */
+int myl_linear_w8a16_pc(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
+                        uint8_t act_frac_bits, const uint8_t* out_frac_bits, int16_t* y);
+
+/* LM head, path B (runtime/src/model.rs:297-307): logits[M][N] int32. */
+int myl_lm_head_w8a16_i32(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
+                          uint8_t final_norm_frac, uint8_t logit_frac, int32_t* logits);
+
+/* Multiplier requant: y = clamp_i16(rne_i128(acc * mult[r], shift[r])).
+ * No counterpart in the reference linear layer; with mult = 2^m and
+ * shift = s + m it equals the pure shift (fixed_point.rs:365-379). */
+int myl_linear_w8a16_mult(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
+                          const int32_t* mult, const uint8_t* shift, int16_t* y);
+
+/* Backend::linear_w8a16 (kernels/src/backend.rs:39-49), same arguments and
+ * meaning: one activation row, raw host weight pointer. The weight is
+ * uploaded on first use and found again by (W, in, out, w_shifts) address and
+ * length; a caller that changes a weight's bytes in place must call
+ * myl_backend_forget(ctx, W) first. */
+int myl_backend_linear_w8a16(myl_ctx* ctx, const int16_t* x, const int8_t* W, int16_t* out,
+                             uint64_t in_features, uint64_t out_features, const uint8_t* w_shifts,
+                             uint8_t act_frac, uint8_t out_frac);
+int myl_backend_forget(myl_ctx* ctx, const int8_t* W);
+
+/* --- Device path ------------------------------------------------------------- */
+
+/* A requant plan for one weight: per-channel signed total shift (and
+ * multiplier), validated on the host and kept on the device.
+ *  MYL_RQ_SHIFT_*: act_frac plus out_frac (out_frac_pc[N] if per_channel,
+ *                  else out_frac_pc[0]); mult/shift ignored.
+ *  MYL_RQ_MULT_I16: mult[N], shift[N]; act_frac/out_frac ignored. */
+int myl_requant_create(myl_ctx* ctx, const myl_weight* w, int mode, uint8_t act_frac,
+                       const uint8_t* out_frac_pc, int per_channel, const int32_t* mult,
+                       const uint8_t* shift, myl_requant** out);
+int myl_requant_release(myl_ctx* ctx, myl_requant* rq);
+
+/* y[M][ldy] = requant(W x) with device pointers. y is int16 for the *_I16
+ * modes and int32 for MYL_RQ_SHIFT_I32. x rows are ldx elements apart. */
+int myl_linear_dev(myl_ctx* ctx, const myl_weight* w, const myl_requant* rq, const int16_t* x,
+                   int64_t M, int64_t ldx, void* y, int64_t ldy, void* stream);
+
+/* acc[M][N] = W x as exact int64 partial sums (no requant). Row-parallel
+ * tensor parallelism sums these across ranks, then calls myl_requant_acc_dev. */
+int myl_linear_acc_dev(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
+                       int64_t ldx, int64_t* acc, void* stream);
+int myl_requant_acc_dev(myl_ctx* ctx, const myl_requant* rq, const int64_t* acc, int64_t M,
+                        void* y, int64_t ldy, void* stream);
+
+/* Splits int16 activations into the byte planes the tensor-core GEMM reads:
+ * x = 256*hi + lo, hi = x >> 8 (int8), lo = x & 255 (uint8); planes are
+ * [M][ldp] (ldp a multiple of 16, columns K..ldp-1 zeroed, 16-byte aligned).
+ * A producer kernel that writes the planes directly skips this pass. */
+int myl_split_hilo_dev(myl_ctx* ctx, const int16_t* x, int64_t M, int64_t K, int64_t ldx,
+                       int8_t* xhi, uint8_t* xlo, int64_t ldp, void* stream);
+
+/* Tensor-core GEMM from byte planes (any M >= 1). rq = NULL stores exact
+ * int64 accumulators into y (as myl_linear_acc_dev); otherwise y is the
+ * requantised output of rq's mode. */
+int myl_linear_planes_dev(myl_ctx* ctx, const myl_weight* w, const myl_requant* rq,
+                          const int8_t* xhi, const uint8_t* xlo, int64_t ldp, int64_t M, void* y,
+                          int64_t ldy, void* stream);
+
+/* Waits for the context's work and reports kernel-side errors (bounded waits
+ * that ran out) as MYL_ERR_DEVICE; the context stays usable afterwards. */
+int myl_synchronize(myl_ctx* ctx);
+
+/* Bound of every device-side wait, in nanoseconds (default 2e9). */
+int myl_set_wait_timeout_ns(myl_ctx* ctx, uint64_t ns);
+
+/* Kernel selection thresholds, for tests and tuning: M <= gemv_max_m runs the
+ * CUDA-core GEMV, larger M the tcgen05 GEMM; split_k = 0 picks automatically. */
+int myl_set_dispatch(myl_ctx* ctx, int gemv_max_m, int force_split_k, int force_swap);
+
+/* Number of this library's kernels launched on the context since init. */
+int64_t myl_launch_count(const myl_ctx* ctx);
+
+/* Test hook for failure detection without a GPU fault: while on, every
+ * tensor-core launch makes its epilogue wait on a barrier that nothing
+ * arrives at; the wait runs out after the wait timeout, the kernel writes an
+ * error code, frees its resources and returns, and the next host-synchronising
+ * call reports MYL_ERR_DEVICE. The context stays usable. */
+int myl_debug_inject_wait_fault(myl_ctx* ctx, int on);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MYL_W8A16_H */

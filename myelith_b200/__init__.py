@@ -1,0 +1,416 @@
+"""myelith_b200 — B200-native W8A16 integer linear layer for Myelith.
+
+Host-side mirror of the reference's operator interface for this path, over
+the C ABI of ``libmyl_w8a16.so`` (include/myl_w8a16.h):
+
+  linear_w8a16(x, W, in_features, w_shifts, act_frac_bits, out_frac_bits)
+      INTEGER_LLM/kernels/src/linear.rs:43
+  linear_w8a16_pc(x, W, in_features, w_shifts, act_frac_bits, out_frac_bits)
+      linear.rs:87
+  lm_head_w8a16_i32(x, W, in_features, w_shifts, final_norm_frac, logit_frac)
+      runtime/src/model.rs:297-307 (LM head, path B)
+  CudaBackend.init(device_id) / .linear_w8a16(x, W, out, in_features,
+      out_features, w_shifts, act_frac, out_frac)
+      kernels/src/backends/cuda.rs:93, backend.rs:39-49
+
+Arguments have the reference's names and meanings; where the reference
+panics (shape assert, debug-build integer overflow) these raise
+``MylError`` with the library's status code. Inputs are numpy arrays (one row
+[K] or a batch [M, K]; every row gives the reference's per-token result).
+
+The device path (``Context``, ``Weight``, ``Requant`` with torch CUDA tensors)
+is what the runtime, the tensor-parallel layer and the benchmark use.
+
+There is no CPU fallback: importing works anywhere, but every compute call
+needs the built library and an sm_100 GPU and raises otherwise.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libmyl_w8a16.so")
+
+MYL_OK = 0
+MYL_ERR_SHAPE = 1
+MYL_ERR_OVERFLOW = 2
+MYL_ERR_CUDA = 3
+MYL_ERR_ARG = 4
+MYL_ERR_DEVICE = 5
+MYL_ERR_UNSUPPORTED = 6
+
+RQ_SHIFT_I16 = 0
+RQ_SHIFT_I32 = 1
+RQ_MULT_I16 = 2
+
+_STATUS = {1: "shape", 2: "overflow", 3: "cuda", 4: "argument", 5: "device", 6: "unsupported"}
+
+
+class MylError(RuntimeError):
+    def __init__(self, fn: str, code: int, msg: str):
+        super().__init__(f"{fn}: {_STATUS.get(code, 'error')} error ({code}): {msg}")
+        self.code = code
+
+
+_lib = None
+_lib_lock = threading.Lock()
+
+
+def load_library(path: str | None = None):
+    """Loads libmyl_w8a16.so (raises if it is missing: there is no fallback)."""
+    global _lib
+    with _lib_lock:
+        if _lib is not None:
+            return _lib
+        p = path or LIB_PATH
+        if not os.path.exists(p):
+            raise MylError("load_library", MYL_ERR_UNSUPPORTED,
+                           f"{p} is missing; build it with `python -m myelith_b200.build`")
+        L = C.CDLL(p)
+        vp, i64, u8, i32 = C.c_void_p, C.c_int64, C.c_uint8, C.c_int
+        sig = {
+            "myl_last_error": ([], C.c_char_p),
+            "myl_abi_version": ([], i32),
+            "myl_init": ([i32, C.POINTER(vp)], i32),
+            "myl_destroy": ([vp], i32),
+            "myl_device_info": ([vp, C.POINTER(i32), C.POINTER(i32), C.POINTER(i32)], i32),
+            "myl_weight_register": ([vp, vp, i64, i64, i64, vp, C.POINTER(vp)], i32),
+            "myl_weight_release": ([vp, vp], i32),
+            "myl_linear_w8a16": ([vp, vp, vp, i64, u8, u8, vp], i32),
+            "myl_linear_w8a16_pc": ([vp, vp, vp, i64, u8, vp, vp], i32),
+            "myl_lm_head_w8a16_i32": ([vp, vp, vp, i64, u8, u8, vp], i32),
+            "myl_linear_w8a16_mult": ([vp, vp, vp, i64, vp, vp, vp], i32),
+            "myl_backend_linear_w8a16": ([vp, vp, vp, vp, C.c_uint64, C.c_uint64, vp, u8, u8], i32),
+            "myl_backend_forget": ([vp, vp], i32),
+            "myl_requant_create": ([vp, vp, i32, u8, vp, i32, vp, vp, C.POINTER(vp)], i32),
+            "myl_requant_release": ([vp, vp], i32),
+            "myl_linear_dev": ([vp, vp, vp, vp, i64, i64, vp, i64, vp], i32),
+            "myl_linear_acc_dev": ([vp, vp, vp, i64, i64, vp, vp], i32),
+            "myl_requant_acc_dev": ([vp, vp, vp, i64, vp, i64, vp], i32),
+            "myl_synchronize": ([vp], i32),
+            "myl_set_wait_timeout_ns": ([vp, C.c_uint64], i32),
+            "myl_set_dispatch": ([vp, i32, i32, i32], i32),
+            "myl_launch_count": ([vp], i64),
+            "myl_debug_inject_wait_fault": ([vp, i32], i32),
+        }
+        for name, (args, res) in sig.items():
+            f = getattr(L, name)
+            f.argtypes = args
+            f.restype = res
+        _lib = L
+        return L
+
+
+def _check(fn: str, rc: int) -> None:
+    if rc != MYL_OK:
+        msg = load_library().myl_last_error().decode(errors="replace")
+        raise MylError(fn, rc, msg)
+
+
+def _p(a) -> int | None:
+    if a is None:
+        return None
+    if isinstance(a, np.ndarray):
+        return a.ctypes.data
+    return int(a.data_ptr())  # torch tensor
+
+
+def _c(a, dtype) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=dtype))
+
+
+class Context:
+    """One device context (CudaBackend::init, kernels/src/backends/cuda.rs:93)."""
+
+    def __init__(self, device: int = 0):
+        L = load_library()
+        h = C.c_void_p()
+        _check("myl_init", L.myl_init(device, C.byref(h)))
+        self._h = h
+        self.device = device
+        d, sm, nsm = C.c_int(), C.c_int(), C.c_int()
+        _check("myl_device_info", L.myl_device_info(h, C.byref(d), C.byref(sm), C.byref(nsm)))
+        self.sm_version = sm.value
+        self.num_sms = nsm.value
+
+    @property
+    def handle(self):
+        return self._h
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            load_library().myl_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def synchronize(self) -> None:
+        _check("myl_synchronize", load_library().myl_synchronize(self._h))
+
+    def set_wait_timeout_ns(self, ns: int) -> None:
+        _check("myl_set_wait_timeout_ns", load_library().myl_set_wait_timeout_ns(self._h, ns))
+
+    def set_dispatch(self, gemv_max_m: int = 4, force_split_k: int = 0, force_swap: int = -1) -> None:
+        _check("myl_set_dispatch",
+               load_library().myl_set_dispatch(self._h, gemv_max_m, force_split_k, force_swap))
+
+    def inject_wait_fault(self, on: bool) -> None:
+        _check("myl_debug_inject_wait_fault",
+               load_library().myl_debug_inject_wait_fault(self._h, 1 if on else 0))
+
+    @property
+    def launch_count(self) -> int:
+        return int(load_library().myl_launch_count(self._h))
+
+    def weight(self, W, in_features: int, w_shifts, ldw: int | None = None) -> "Weight":
+        return Weight(self, W, in_features, w_shifts, ldw)
+
+
+class Weight:
+    """A weight matrix uploaded once ([out_features][in_features] int8 plus
+    one power-of-two shift per output row, runtime/src/model.rs:28-35)."""
+
+    def __init__(self, ctx: Context, W, in_features: int, w_shifts, ldw: int | None = None):
+        self.ctx = ctx
+        w_shifts = _c(w_shifts, np.uint8)
+        W = np.asarray(W, dtype=np.int8)
+        if W.ndim == 2 and ldw is None:
+            ldw = W.shape[1]
+            W = np.ascontiguousarray(W)
+        ldw = in_features if ldw is None else ldw
+        W = np.ascontiguousarray(W).reshape(-1)
+        N = w_shifts.size
+        if in_features <= 0 or ldw < in_features or (N > 0 and W.size < (N - 1) * ldw + in_features):
+            raise MylError("myl_weight_register", MYL_ERR_SHAPE,
+                           f"{W.size} weights do not hold {N} rows of {in_features}")
+        h = C.c_void_p()
+        _check("myl_weight_register", load_library().myl_weight_register(
+            ctx.handle, _p(W), N, in_features, ldw, _p(w_shifts), C.byref(h)))
+        self._h = h
+        self.out_features = N
+        self.in_features = in_features
+        self.w_shifts = w_shifts
+
+    @property
+    def handle(self):
+        return self._h
+
+    def release(self) -> None:
+        if getattr(self, "_h", None) and self.ctx.handle:
+            load_library().myl_weight_release(self.ctx.handle, self._h)
+        self._h = None
+
+    def __del__(self):
+        try:
+            self.release()
+        except Exception:
+            pass
+
+    # ---- host-pointer calls (synchronous) ----
+    def _rows(self, x):
+        x = _c(x, np.int16)
+        single = x.ndim == 1
+        xs = x.reshape(1, -1) if single else x
+        if xs.shape[1] != self.in_features:
+            raise MylError("linear", MYL_ERR_SHAPE,
+                           f"x rows have {xs.shape[1]} elements, weight expects {self.in_features}")
+        return np.ascontiguousarray(xs), single
+
+    def linear(self, x, act_frac_bits: int, out_frac_bits) -> np.ndarray:
+        """linear_w8a16 (scalar out_frac) or linear_w8a16_pc (array out_frac)."""
+        xs, single = self._rows(x)
+        y = np.zeros((xs.shape[0], self.out_features), np.int16)
+        L = load_library()
+        if np.ndim(out_frac_bits) == 0:
+            _check("myl_linear_w8a16", L.myl_linear_w8a16(
+                self.ctx.handle, self._h, _p(xs), xs.shape[0], act_frac_bits, int(out_frac_bits), _p(y)))
+        else:
+            of = _c(out_frac_bits, np.uint8)
+            if of.size != self.out_features:
+                raise MylError("myl_linear_w8a16_pc", MYL_ERR_SHAPE, "one out_frac per channel")
+            _check("myl_linear_w8a16_pc", L.myl_linear_w8a16_pc(
+                self.ctx.handle, self._h, _p(xs), xs.shape[0], act_frac_bits, _p(of), _p(y)))
+        return y[0] if single else y
+
+    def lm_head(self, x, final_norm_frac: int, logit_frac: int) -> np.ndarray:
+        xs, single = self._rows(x)
+        y = np.zeros((xs.shape[0], self.out_features), np.int32)
+        _check("myl_lm_head_w8a16_i32", load_library().myl_lm_head_w8a16_i32(
+            self.ctx.handle, self._h, _p(xs), xs.shape[0], final_norm_frac, logit_frac, _p(y)))
+        return y[0] if single else y
+
+    def linear_mult(self, x, mult, shift) -> np.ndarray:
+        xs, single = self._rows(x)
+        mult = _c(mult, np.int32)
+        shift = _c(shift, np.uint8)
+        if mult.size != self.out_features or shift.size != self.out_features:
+            raise MylError("myl_linear_w8a16_mult", MYL_ERR_SHAPE, "one mult/shift per channel")
+        y = np.zeros((xs.shape[0], self.out_features), np.int16)
+        _check("myl_linear_w8a16_mult", load_library().myl_linear_w8a16_mult(
+            self.ctx.handle, self._h, _p(xs), xs.shape[0], _p(mult), _p(shift), _p(y)))
+        return y[0] if single else y
+
+    # ---- device path (torch CUDA tensors) ----
+    def requant(self, mode: int = RQ_SHIFT_I16, act_frac: int = 0, out_frac=0, mult=None,
+                shift=None) -> "Requant":
+        return Requant(self, mode, act_frac, out_frac, mult, shift)
+
+    def linear_dev(self, rq: "Requant", x, y, stream=None) -> None:
+        """y[M, N] = requant(W x) for torch CUDA tensors x [M, >=K] int16."""
+        M = x.shape[0]
+        _check("myl_linear_dev", load_library().myl_linear_dev(
+            self.ctx.handle, self._h, rq.handle, _p(x), M, x.stride(0), _p(y), y.stride(0),
+            _stream_ptr(stream)))
+
+    def linear_acc_dev(self, x, acc, stream=None) -> None:
+        """acc[M, N] int64 = exact W x (no requant)."""
+        _check("myl_linear_acc_dev", load_library().myl_linear_acc_dev(
+            self.ctx.handle, self._h, _p(x), x.shape[0], x.stride(0), _p(acc), _stream_ptr(stream)))
+
+
+class Requant:
+    """Per-channel requant plan kept on the device (myl_requant_create)."""
+
+    def __init__(self, w: Weight, mode: int, act_frac: int, out_frac, mult, shift):
+        self.w = w
+        per_channel = np.ndim(out_frac) > 0
+        of = _c(np.atleast_1d(out_frac), np.uint8)
+        m = None if mult is None else _c(mult, np.int32)
+        s = None if shift is None else _c(shift, np.uint8)
+        h = C.c_void_p()
+        _check("myl_requant_create", load_library().myl_requant_create(
+            w.ctx.handle, w.handle, mode, act_frac, _p(of), 1 if per_channel else 0, _p(m), _p(s),
+            C.byref(h)))
+        self._h = h
+        self.mode = mode
+
+    @property
+    def handle(self):
+        return self._h
+
+    def release(self) -> None:
+        if getattr(self, "_h", None):
+            load_library().myl_requant_release(self.w.ctx.handle, self._h)
+        self._h = None
+
+    def __del__(self):
+        try:
+            self.release()
+        except Exception:
+            pass
+
+    def apply_acc_dev(self, acc, y, stream=None) -> None:
+        _check("myl_requant_acc_dev", load_library().myl_requant_acc_dev(
+            self.w.ctx.handle, self._h, _p(acc), acc.shape[0], _p(y), y.stride(0),
+            _stream_ptr(stream)))
+
+
+def _stream_ptr(stream) -> int | None:
+    if stream is None:
+        try:
+            import torch
+            return int(torch.cuda.current_stream().cuda_stream) or None
+        except Exception:
+            return None
+    if hasattr(stream, "cuda_stream"):
+        return int(stream.cuda_stream) or None
+    return int(stream) or None
+
+
+# ---- the reference's free functions ---------------------------------------------
+
+_default_ctx: Context | None = None
+_cache: dict = {}
+
+
+def default_context() -> Context:
+    global _default_ctx
+    if _default_ctx is None:
+        _default_ctx = Context(0)
+    return _default_ctx
+
+
+def _cached_weight(W, in_features: int, w_shifts) -> Weight:
+    W = np.asarray(W, dtype=np.int8)
+    w_shifts = _c(w_shifts, np.uint8)
+    if in_features <= 0 or W.size != in_features * w_shifts.size:
+        # linear.rs:51-58: "{} Gewichte passen nicht zu {} Zeilen à {} Elementen"
+        raise MylError("linear_w8a16", MYL_ERR_SHAPE,
+                       f"{W.size} weights do not fit {w_shifts.size} rows of {in_features} elements")
+    key = (W.__array_interface__["data"][0], W.size, in_features, w_shifts.tobytes())
+    w = _cache.get(key)
+    if w is None:
+        w = Weight(default_context(), W.reshape(-1), in_features, w_shifts)
+        _cache[key] = w
+    return w
+
+
+def clear_weight_cache() -> None:
+    _cache.clear()
+
+
+def linear_w8a16(x, W, in_features: int, w_shifts, act_frac_bits: int, out_frac_bits: int) -> np.ndarray:
+    """kernels/src/linear.rs:43 on the B200 (x: [K] or [M, K])."""
+    return _cached_weight(W, in_features, w_shifts).linear(x, act_frac_bits, int(out_frac_bits))
+
+
+def linear_w8a16_pc(x, W, in_features: int, w_shifts, act_frac_bits: int, out_frac_bits) -> np.ndarray:
+    """kernels/src/linear.rs:87 (one out_frac per output channel)."""
+    of = _c(out_frac_bits, np.uint8)
+    if of.size != np.asarray(w_shifts).size:
+        raise MylError("linear_w8a16_pc", MYL_ERR_SHAPE, "one out_frac per channel (Fund 20)")
+    return _cached_weight(W, in_features, w_shifts).linear(x, act_frac_bits, of)
+
+
+def lm_head_w8a16_i32(x, W, in_features: int, w_shifts, final_norm_frac: int, logit_frac: int) -> np.ndarray:
+    """runtime/src/model.rs:297-307: logits clamped to i32."""
+    return _cached_weight(W, in_features, w_shifts).lm_head(x, final_norm_frac, logit_frac)
+
+
+class CudaBackend:
+    """The reference's Backend trait slot for CUDA (kernels/src/backends/cuda.rs),
+    with a real computing path for linear_w8a16 (backend.rs:39-49)."""
+
+    def __init__(self, device_id: int = 0):
+        self._ctx = Context(device_id)
+
+    @classmethod
+    def init(cls, device_id: int = 0) -> "CudaBackend":
+        return cls(device_id)
+
+    def name(self) -> str:
+        return "cuda"
+
+    def hardware_family(self) -> str:
+        return "nvidia-gpu"
+
+    def feature_tag(self) -> str:
+        return "cuda-sm100a"
+
+    def device_id(self) -> int:
+        return self._ctx.device
+
+    def sm_version(self) -> int:
+        return self._ctx.sm_version
+
+    def linear_w8a16(self, x, W, out, in_features: int, out_features: int, w_shifts,
+                     act_frac: int, out_frac: int) -> None:
+        x = _c(x, np.int16)
+        W = np.ascontiguousarray(np.asarray(W, dtype=np.int8))
+        w_shifts = _c(w_shifts, np.uint8)
+        if not (isinstance(out, np.ndarray) and out.dtype == np.int16 and out.flags.c_contiguous):
+            raise MylError("linear_w8a16", MYL_ERR_ARG, "out must be a contiguous int16 numpy array")
+        if (W.size != in_features * out_features or w_shifts.size < out_features
+                or out.size < out_features or x.size < in_features):
+            raise MylError("linear_w8a16", MYL_ERR_SHAPE, "argument lengths do not match the shape")
+        _check("myl_backend_linear_w8a16", load_library().myl_backend_linear_w8a16(
+            self._ctx.handle, _p(x), _p(W), _p(out), in_features, out_features, _p(w_shifts),
+            act_frac, out_frac))

@@ -1,0 +1,270 @@
+// common.cuh — device helpers shared by the W8A16 kernels (sm_100a only).
+//
+// Requant semantics (the epilogue of every kernel) restate the reference:
+//   rshift_round_i64   INTEGER_LLM/kernels/src/fixed_point.rs:57-71
+//   rescale_i64        fixed_point.rs:184-191 (negative shift = left shift)
+//   clamp_i16_from_i64 fixed_point.rs:23-27, LM head i32 clamp runtime/src/model.rs:305
+// The signed total shift s = (w_shift + act_frac) - out_frac is computed and
+// range-checked on the host (one int8 per output channel); the device only
+// applies it.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "libmyl_w8a16 is written for sm_100a (B200) only"
+#endif
+
+namespace myl {
+
+// ---- kernel error codes written to the context's device error word --------
+enum DeviceError : int {
+  DEV_OK = 0,
+  DEV_WAIT_PRODUCER = 0x101,  // producer gave up waiting for a free stage
+  DEV_WAIT_MMA = 0x102,       // MMA issuer gave up waiting for a loaded stage
+  DEV_WAIT_EPILOGUE = 0x103,  // epilogue gave up waiting for the accumulator
+  DEV_WAIT_DRAIN = 0x104,     // clean-up gave up waiting for copies / MMAs in flight
+  DEV_WAIT_INJECTED = 0x105,  // test hook: a wait on a barrier nothing arrives at
+};
+
+// Epilogue modes.
+enum EpiMode : int {
+  EPI_ACC_I64 = 0,    // store exact int64 partial sums
+  EPI_SHIFT = 1,      // reference requant (pure shift)
+  EPI_MULT = 2,       // multiplier requant (i128 product)
+};
+
+struct Epilogue {
+  int mode;               // EpiMode
+  int out_i32;            // 1: clamp to i32 and store int32, 0: clamp to i16, store int16
+  const int8_t* shift;    // [N]: signed total shift (EPI_SHIFT) / uint8 shift (EPI_MULT)
+  const int32_t* mult;    // [N] (EPI_MULT)
+  void* y;                // [M][ldy] int16/int32 (requant modes) or int64 (EPI_ACC_I64)
+  int64_t ldy;
+};
+
+// ---- requant -----------------------------------------------------------------
+
+// fixed_point.rs:57-71: RNE right shift of a two's-complement value, s in [1, 62].
+__device__ __forceinline__ int64_t rshift_rne_i64(int64_t v, int s) {
+  const int64_t q = v >> s;
+  const int64_t r = v & ((int64_t(1) << s) - 1);
+  const int64_t h = int64_t(1) << (s - 1);
+  return q + ((r > h) | ((r == h) & (q & 1)));
+}
+
+// fixed_point.rs:184-191 with the host-validated signed shift s in [-63, 62].
+__device__ __forceinline__ int64_t rescale_i64_signed(int64_t acc, int s) {
+  if (s > 0) return rshift_rne_i64(acc, s);
+  if (s == 0) return acc;
+  return int64_t(uint64_t(acc) << (-s));
+}
+
+__device__ __forceinline__ int64_t clamp_i64(int64_t v, int64_t lo, int64_t hi) {
+  return v < lo ? lo : (v > hi ? hi : v);
+}
+
+// Multiplier mode: rne(acc * m, s) in 128-bit, s in [0, 126], saturated to
+// [lo, hi]. The i128 RNE restates fixed_point.rs:155-169.
+__device__ __forceinline__ int64_t requant_mult(int64_t acc, int32_t m, int s, int64_t lo,
+                                                int64_t hi) {
+  __int128 p = (__int128)acc * (__int128)m;
+  if (s > 0) {
+    const __int128 one = 1;
+    const __int128 q = p >> s;
+    const __int128 r = p & ((one << s) - 1);
+    const __int128 h = one << (s - 1);
+    p = q + (((r > h) || (r == h && (q & 1))) ? 1 : 0);
+  }
+  if (p < (__int128)lo) return lo;
+  if (p > (__int128)hi) return hi;
+  return (int64_t)p;
+}
+
+// Applies the epilogue to one exact accumulator of output (m, n).
+__device__ __forceinline__ void epilogue_store(const Epilogue& ep, int64_t m, int64_t n,
+                                               int64_t acc) {
+  if (ep.mode == EPI_ACC_I64) {
+    static_cast<int64_t*>(ep.y)[m * ep.ldy + n] = acc;
+    return;
+  }
+  const int64_t lo = ep.out_i32 ? int64_t(INT32_MIN) : -32768;
+  const int64_t hi = ep.out_i32 ? int64_t(INT32_MAX) : 32767;
+  int64_t v;
+  if (ep.mode == EPI_SHIFT) {
+    v = clamp_i64(rescale_i64_signed(acc, ep.shift[n]), lo, hi);
+  } else {
+    v = requant_mult(acc, ep.mult[n], int(uint8_t(ep.shift[n])), lo, hi);
+  }
+  if (ep.out_i32) static_cast<int32_t*>(ep.y)[m * ep.ldy + n] = int32_t(v);
+  else static_cast<int16_t*>(ep.y)[m * ep.ldy + n] = int16_t(v);
+}
+
+// Per-channel requant with the channel's parameters already in registers.
+struct ChannelRequant {
+  int mode, out_i32, shift;
+  int32_t mult;
+  __device__ __forceinline__ void load(const Epilogue& ep, int64_t n) {
+    mode = ep.mode;
+    out_i32 = ep.out_i32;
+    shift = 0;
+    mult = 1;
+    if (mode == EPI_SHIFT) shift = ep.shift[n];
+    else if (mode == EPI_MULT) { shift = int(uint8_t(ep.shift[n])); mult = ep.mult[n]; }
+  }
+  __device__ __forceinline__ int64_t apply(int64_t acc) const {
+    const int64_t lo = out_i32 ? int64_t(INT32_MIN) : -32768;
+    const int64_t hi = out_i32 ? int64_t(INT32_MAX) : 32767;
+    if (mode == EPI_SHIFT) return clamp_i64(rescale_i64_signed(acc, shift), lo, hi);
+    return requant_mult(acc, mult, shift, lo, hi);
+  }
+};
+
+// ---- PTX wrappers ----------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: returns false (and leaves the barrier alone) once timeout_ns
+// has passed or *abort (if given) became nonzero.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
+                                                  uint64_t timeout_ns, volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (abort != nullptr && *abort) return false;
+    if (globaltimer_ns() - t0 > timeout_ns) return false;
+  }
+}
+
+// 2D tiled TMA load global -> shared, completion counted on an mbarrier.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int32_t c0, int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ---- tcgen05 (5th-generation tensor core, TMEM accumulators) -------------------
+
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D(tmem) (+)= A(smem desc) x B(smem desc)^T, int8 kind, int32 accumulate.
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives on an mbarrier once all previously issued MMAs of this thread are done.
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+      : "memory");
+}
+
+// 32 lanes x 32 columns of 32-bit words: thread t of the warp receives the 32
+// consecutive columns of TMEM lane (lane_base + t).
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor for a K-major operand tile written by TMA
+// with 128-byte swizzle: rows of 128 bytes, 8-row (1024-byte) swizzle atoms.
+// Fields: start address >> 4 [0,14), leading byte offset >> 4 [16,30) (unused
+// for swizzled K-major, 1), stride byte offset >> 4 [32,46) (1024 B between
+// 8-row groups), version 1 [46,48), layout type 2 = 128B swizzle [61,64).
+__device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= uint64_t((saddr & 0x3FFFF) >> 4);
+  d |= uint64_t(1) << 16;
+  d |= uint64_t(1024 >> 4) << 32;
+  d |= uint64_t(1) << 46;
+  d |= uint64_t(2) << 61;
+  return d;
+}
+
+// Instruction descriptor, kind::i8: D = s32, A/B signedness, both K-major,
+// N >> 3 at [17,23), M >> 4 at [24,29).
+__host__ __device__ constexpr uint32_t idesc_i8(int m, int n, bool a_signed, bool b_signed) {
+  return (2u << 4) | (uint32_t(a_signed) << 7) | (uint32_t(b_signed) << 10) |
+         (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
+}
+
+}  // namespace myl

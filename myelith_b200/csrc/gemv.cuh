@@ -1,0 +1,172 @@
+// gemv.cuh — decode GEMV for W8A16 (M <= 4 activation rows), HBM-bound.
+//
+// Computes, per output channel r and activation row m,
+//   acc = sum_k W[r,k] * x[m,k]      (exact, dot.rs:403-409)
+// and applies the requant epilogue (linear.rs:61-68). Any summation order is
+// allowed because the accumulation is exact (|acc| < 2^37 for K <= 32768;
+// kernels/src/backends/cuda.rs:17-61 states the same contract).
+//
+// Layout and schedule
+//  - W is the registered device copy: [N][ldw] int8, ldw a multiple of 16,
+//    zero-padded beyond K. Each warp owns R output rows; lane l streams the
+//    16-byte chunks l, l+32, ... of each row with 128-bit non-coherent loads
+//    that bypass L1 (a row's 32 lanes read 512 contiguous bytes).
+//  - The activation slice x[:, k0:k0+KS] is staged once per block in shared
+//    memory (zero-filled beyond K), so ragged K needs no padding by the caller.
+//  - Products use dp2a (two int16 x int8 products per instruction) into int32
+//    lanes that are flushed to int64 every U chunks (U*16 products of at most
+//    2^22 each stay below 2^31). Lanes are combined with a 64-bit shuffle tree.
+//  - gridDim.y > 1 splits K; each slice then writes exact int64 partial sums
+//    (EPI_ACC_I64) that reduce_requant_kernel adds and requantises.
+#pragma once
+
+#include "common.cuh"
+
+namespace myl {
+
+__device__ __forceinline__ int4 ldg_stream_v4(const void* p) {
+  int4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ int dot16_dp2a(const int4 w, const int4 xa, const int4 xb, int acc) {
+  // w bytes 4q..4q+3 pair with x words 2q (lo half of w) and 2q+1 (hi half).
+  acc = __dp2a_lo(xa.x, w.x, acc);
+  acc = __dp2a_hi(xa.y, w.x, acc);
+  acc = __dp2a_lo(xa.z, w.y, acc);
+  acc = __dp2a_hi(xa.w, w.y, acc);
+  acc = __dp2a_lo(xb.x, w.z, acc);
+  acc = __dp2a_hi(xb.y, w.z, acc);
+  acc = __dp2a_lo(xb.z, w.w, acc);
+  acc = __dp2a_hi(xb.w, w.w, acc);
+  return acc;
+}
+
+constexpr int GEMV_THREADS = 256;
+constexpr int GEMV_WARPS = GEMV_THREADS / 32;
+
+// MT activation rows, R rows per warp, U chunks per lane in flight.
+template <int MT, int R, int U>
+__global__ void __launch_bounds__(GEMV_THREADS)
+    gemv_w8a16_kernel(const int8_t* __restrict__ W, int64_t ldw, int64_t N,
+                      const int16_t* __restrict__ X, int64_t ldx, int64_t K, int64_t k_slice,
+                      Epilogue ep, int64_t slice_stride) {
+  extern __shared__ __align__(16) int16_t xs[];  // [MT][KS]
+  const int64_t k0 = int64_t(blockIdx.y) * k_slice;
+  const int64_t kn = (K - k0) < k_slice ? (K - k0) : k_slice;  // valid elements in slice
+  const int KS = int((kn + 15) & ~int64_t(15));                 // staged, multiple of 16
+  const int nchunk = KS >> 4;
+
+  // ---- stage x[:, k0:k0+KS] (zero beyond K) ---------------------------------
+  const bool vec_ok = ((reinterpret_cast<uintptr_t>(X) & 15) == 0) && (ldx % 8 == 0) && (k0 % 8 == 0);
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+    const int16_t* xr = X + int64_t(m) * ldx + k0;
+    int16_t* dst = xs + m * KS;
+    if (vec_ok) {
+      for (int i = threadIdx.x * 8; i < KS; i += GEMV_THREADS * 8) {
+        int4 v;
+        if (i + 8 <= kn) {
+          v = __ldg(reinterpret_cast<const int4*>(xr + i));
+        } else {
+          alignas(16) int16_t t[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) t[e] = (i + e < kn) ? xr[i + e] : int16_t(0);
+          v = *reinterpret_cast<const int4*>(t);
+        }
+        *reinterpret_cast<int4*>(dst + i) = v;
+      }
+    } else {
+      for (int i = threadIdx.x; i < KS; i += GEMV_THREADS) dst[i] = (i < kn) ? xr[i] : int16_t(0);
+    }
+  }
+  __syncthreads();
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row0 = (int64_t(blockIdx.x) * GEMV_WARPS + warp) * R;
+  if (row0 >= N) return;
+
+  int64_t acc[R][MT];
+#pragma unroll
+  for (int j = 0; j < R; ++j)
+#pragma unroll
+    for (int m = 0; m < MT; ++m) acc[j][m] = 0;
+
+  const int8_t* wrow[R];
+#pragma unroll
+  for (int j = 0; j < R; ++j) {
+    const int64_t r = (row0 + j < N) ? row0 + j : N - 1;  // clamp: duplicate rows are not stored
+    wrow[j] = W + r * ldw + k0;
+  }
+
+  for (int c = lane; c < nchunk; c += 32 * U) {
+    int4 wv[U][R];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int cc = c + 32 * u;
+#pragma unroll
+      for (int j = 0; j < R; ++j)
+        wv[u][j] = (cc < nchunk) ? ldg_stream_v4(wrow[j] + cc * 16) : make_int4(0, 0, 0, 0);
+    }
+    int a32[R][MT];
+#pragma unroll
+    for (int j = 0; j < R; ++j)
+#pragma unroll
+      for (int m = 0; m < MT; ++m) a32[j][m] = 0;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int cc = c + 32 * u;
+      if (cc < nchunk) {
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          const int4* xp = reinterpret_cast<const int4*>(xs + m * KS + cc * 16);
+          const int4 xa = xp[0], xb = xp[1];
+#pragma unroll
+          for (int j = 0; j < R; ++j) a32[j][m] = dot16_dp2a(wv[u][j], xa, xb, a32[j][m]);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < R; ++j)
+#pragma unroll
+      for (int m = 0; m < MT; ++m) acc[j][m] += a32[j][m];
+  }
+
+  // ---- warp reduction (exact, any order) and epilogue --------------------------
+#pragma unroll
+  for (int j = 0; j < R; ++j)
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      int64_t v = acc[j][m];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      acc[j][m] = v;
+    }
+  Epilogue e = ep;
+  if (e.mode == EPI_ACC_I64)
+    e.y = static_cast<int64_t*>(e.y) + int64_t(blockIdx.y) * slice_stride;
+#pragma unroll
+  for (int j = 0; j < R; ++j)
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+      if (lane == ((j * MT + m) & 31) && row0 + j < N) epilogue_store(e, m, row0 + j, acc[j][m]);
+}
+
+// Sums nsplit exact int64 partial slices [nsplit][M][N] (slice_stride apart)
+// and applies the epilogue. Summation order is irrelevant (exact integers).
+__global__ void reduce_requant_kernel(const int64_t* __restrict__ part, int nsplit,
+                                      int64_t slice_stride, int64_t M, int64_t N, Epilogue ep) {
+  const int64_t total = M * N;
+  for (int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+       e += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t m = e / N, n = e % N;
+    int64_t s = 0;
+    for (int i = 0; i < nsplit; ++i) s += part[i * slice_stride + m * N + n];
+    epilogue_store(ep, m, n, s);
+  }
+}
+
+}  // namespace myl

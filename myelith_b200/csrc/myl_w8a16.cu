@@ -1,0 +1,739 @@
+// myl_w8a16.cu — libmyl_w8a16.so: C ABI, weight registry and kernel dispatch.
+//
+// The ABI (include/myl_w8a16.h) replaces the CUDA slot of the reference's
+// Backend trait (INTEGER_LLM/kernels/src/backends/cuda.rs:80-261) and the free
+// functions the runtime calls (kernels/src/linear.rs:43, :87; the LM-head loop
+// of runtime/src/model.rs:297-307). There is no CPU path in this library.
+//
+// Dispatch for y = requant(W x), x with M rows:
+//   M <= gemv_max_m (default 4)  CUDA-core GEMV (gemv.cuh), HBM-bound decode.
+//   otherwise                    split x into hi/lo byte planes and run the
+//                                tcgen05 split-byte GEMM (gemm_tc.cuh):
+//                                M <= 256: weight-as-A tiles (SWAP), BN = next
+//                                power of two >= M; M > 256: 128x256 tiles.
+//   Too few tiles for the 148 SMs, or K > 65536, splits K; the slices write
+//   exact int64 partials that reduce_requant_kernel adds and requantises.
+#include "../../include/myl_w8a16.h"
+
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "common.cuh"
+#include "gemm_tc.cuh"
+#include "gemv.cuh"
+
+using namespace myl;
+
+// ---------------------------------------------------------------------------------
+// errors
+
+static thread_local std::string g_last_error;
+
+static int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+static int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+#define CUDA_TRY(expr)                                                                     \
+  do {                                                                                     \
+    cudaError_t e_ = (expr);                                                               \
+    if (e_ != cudaSuccess)                                                                 \
+      return fail(MYL_ERR_CUDA, "%s failed: %s (%s:%d)", #expr, cudaGetErrorString(e_),    \
+                  __FILE__, __LINE__);                                                     \
+  } while (0)
+
+#define TRY(expr)                  \
+  do {                             \
+    int rc_ = (expr);              \
+    if (rc_ != MYL_OK) return rc_; \
+  } while (0)
+
+// ---------------------------------------------------------------------------------
+// objects
+
+struct DevBuf {
+  void* p = nullptr;
+  size_t cap = 0;
+};
+
+struct myl_weight {
+  int64_t N = 0, K = 0, ldp = 0;  // device copy is [N][ldp] int8, ldp = round_up(K, 16)
+  int8_t* d_W = nullptr;
+  std::vector<uint8_t> w_shifts;
+  CUtensorMap tm128{}, tm256{};   // TMA maps with 128- and 256-row boxes
+  // Backend-trait cache key.
+  const int8_t* host_W = nullptr;
+  const uint8_t* host_shifts = nullptr;
+};
+
+struct myl_requant {
+  int64_t N = 0;
+  int mode = 0;
+  int8_t* d_shift = nullptr;
+  int32_t* d_mult = nullptr;
+};
+
+struct myl_ctx {
+  int device = 0, sm = 0, num_sms = 0;
+  cudaStream_t stream = nullptr;
+  int* d_err = nullptr;
+  int* h_err = nullptr;  // pinned
+  uint64_t timeout_ns = 2000000000ull;
+  int gemv_max_m = 4, force_split_k = 0, force_swap = -1, inject_fault = 0;
+  int64_t launches = 0;
+  PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  DevBuf x, y, rq, planes, part;
+  // The workspace buffers are shared by every call on the context; calls on
+  // different streams are ordered through this event.
+  cudaEvent_t ws_event = nullptr;
+  cudaStream_t ws_last = nullptr;
+  bool ws_used = false;
+  std::unordered_map<const int8_t*, myl_weight*> backend_cache;
+};
+
+static bool capturing(cudaStream_t st) {
+  cudaStreamCaptureStatus s = cudaStreamCaptureStatusNone;
+  return cudaStreamIsCapturing(st, &s) == cudaSuccess && s != cudaStreamCaptureStatusNone;
+}
+
+static int ws_acquire(myl_ctx* ctx, cudaStream_t st) {
+  if (ctx->ws_used && ctx->ws_last != st && !capturing(st))
+    CUDA_TRY(cudaStreamWaitEvent(st, ctx->ws_event, 0));
+  return MYL_OK;
+}
+
+static int ws_release(myl_ctx* ctx, cudaStream_t st) {
+  if (capturing(st)) return MYL_OK;
+  CUDA_TRY(cudaEventRecord(ctx->ws_event, st));
+  ctx->ws_last = st;
+  ctx->ws_used = true;
+  return MYL_OK;
+}
+
+static int ensure(DevBuf& b, size_t bytes) {
+  if (b.cap >= bytes) return MYL_OK;
+  if (b.p) CUDA_TRY(cudaFree(b.p));
+  b.p = nullptr;
+  b.cap = 0;
+  size_t cap = std::max<size_t>(bytes, 4096);
+  CUDA_TRY(cudaMalloc(&b.p, cap));
+  b.cap = cap;
+  return MYL_OK;
+}
+
+static int encode_map(myl_ctx* ctx, CUtensorMap* map, const void* base, int64_t cols, int64_t rows,
+                      int64_t ld_bytes, int box_rows) {
+  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(ld_bytes)};
+  cuuint32_t box[2] = {cuuint32_t(TC_BK), cuuint32_t(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = ctx->encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MYL_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return MYL_OK;
+}
+
+// ---------------------------------------------------------------------------------
+// requant parameter validation (host). Restates the overflow behaviour of the
+// reference's debug build: u8 addition w_shift + act_frac (linear.rs:66),
+// i8 subtraction and shift widths in rescale_i64 (fixed_point.rs:184-191,
+// :57-71).
+
+static int signed_total_shift(uint8_t w_shift, uint8_t act_frac, uint8_t out_frac, int8_t* s) {
+  unsigned in_frac = unsigned(w_shift) + unsigned(act_frac);
+  if (in_frac > 255u) return fail(MYL_ERR_OVERFLOW, "w_shift + act_frac = %u overflows u8", in_frac);
+  int d = int(int8_t(uint8_t(in_frac))) - int(int8_t(out_frac));
+  if (d < -128 || d > 127) return fail(MYL_ERR_OVERFLOW, "in_frac - out_frac overflows i8");
+  if (d > 62) return fail(MYL_ERR_OVERFLOW, "right shift %d overflows the i64 mask", d);
+  if (d < -63) return fail(MYL_ERR_OVERFLOW, "left shift %d exceeds i64 width", -d);
+  *s = int8_t(d);
+  return MYL_OK;
+}
+
+static int shift_plan(const myl_weight* w, uint8_t act_frac, const uint8_t* out_frac, int per_channel,
+                      std::vector<int8_t>& s) {
+  s.resize(size_t(w->N));
+  for (int64_t r = 0; r < w->N; ++r)
+    TRY(signed_total_shift(w->w_shifts[size_t(r)], act_frac, per_channel ? out_frac[r] : out_frac[0],
+                           &s[size_t(r)]));
+  return MYL_OK;
+}
+
+// ---------------------------------------------------------------------------------
+// kernel launchers
+
+using GemvFn = void (*)(const int8_t*, int64_t, int64_t, const int16_t*, int64_t, int64_t, int64_t,
+                        Epilogue, int64_t);
+
+template <int MT, int R, int U>
+static void* gemv_ptr() {
+  return reinterpret_cast<void*>(&gemv_w8a16_kernel<MT, R, U>);
+}
+
+struct GemvVariant {
+  void* fn;
+  int R;
+};
+
+static GemvVariant gemv_variant(int M) {
+  switch (M) {
+    case 1: return {gemv_ptr<1, 1, 4>(), 1};
+    case 2: return {gemv_ptr<2, 2, 2>(), 2};
+    case 3: return {gemv_ptr<3, 2, 2>(), 2};
+    default: return {gemv_ptr<4, 2, 2>(), 2};
+  }
+}
+
+static constexpr int GEMV_SMEM_BUDGET = 64 * 1024;
+
+static inline int64_t round_up16(int64_t v) { return (v + 15) & ~int64_t(15); }
+
+static int launch_gemv(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M, int64_t ldx,
+                       const Epilogue& ep_final, cudaStream_t st) {
+  GemvVariant v = gemv_variant(int(M));
+  const int64_t K = w->K;
+  const int64_t ks_max = (GEMV_SMEM_BUDGET / (2 * M)) & ~int64_t(15);
+  int ksplit = int((round_up16(K) + ks_max - 1) / ks_max);
+  if (ctx->force_split_k > 0) ksplit = ctx->force_split_k;
+  int64_t k_slice = round_up16((K + ksplit - 1) / ksplit);
+  ksplit = int((K + k_slice - 1) / k_slice);
+  const size_t smem = size_t(M) * size_t(k_slice) * 2;
+  CUDA_TRY(cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  dim3 grid(unsigned((w->N + GEMV_WARPS * v.R - 1) / (GEMV_WARPS * v.R)), unsigned(ksplit));
+  Epilogue ep = ep_final;
+  int64_t slice_stride = 0;
+  if (ksplit > 1) {
+    TRY(ensure(ctx->part, size_t(ksplit) * size_t(M) * size_t(w->N) * 8));
+    ep.mode = EPI_ACC_I64;
+    ep.y = ctx->part.p;
+    ep.ldy = w->N;
+    slice_stride = M * w->N;
+  }
+  const int8_t* dW = w->d_W;
+  int64_t ldw = w->ldp, N = w->N;
+  void* args[] = {(void*)&dW, (void*)&ldw, (void*)&N, (void*)&x, (void*)&ldx,
+                  (void*)&K, (void*)&k_slice, (void*)&ep, (void*)&slice_stride};
+  CUDA_TRY(cudaLaunchKernel(v.fn, grid, dim3(GEMV_THREADS), args, smem, st));
+  ctx->launches++;
+  if (ksplit > 1) {
+    const int64_t total = M * w->N;
+    unsigned blocks = unsigned(std::min<int64_t>((total + 255) / 256, int64_t(ctx->num_sms) * 8));
+    reduce_requant_kernel<<<blocks, 256, 0, st>>>(static_cast<const int64_t*>(ctx->part.p), ksplit,
+                                                   slice_stride, M, w->N, ep_final);
+    CUDA_TRY(cudaGetLastError());
+    ctx->launches++;
+  }
+  return MYL_OK;
+}
+
+template <int BN, bool SWAP, int STAGES>
+static int launch_tc_variant(myl_ctx* ctx, const myl_weight* w, const CUtensorMap& tm_xhi,
+                             const CUtensorMap& tm_xlo, int64_t M, int ksplit, int per,
+                             int k_tiles, const Epilogue& ep, int64_t slice_stride, cudaStream_t st) {
+  using Cfg = TcCfg<BN, SWAP, STAGES>;
+  auto fn = gemm_w8a16_tc_kernel<BN, SWAP, STAGES>;
+  CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
+  const CUtensorMap& tm_w = (Cfg::ROWS_W == 128) ? w->tm128 : w->tm256;
+  dim3 grid;
+  if (SWAP) grid = dim3(unsigned((w->N + 127) / 128), unsigned((M + BN - 1) / BN), unsigned(ksplit));
+  else grid = dim3(unsigned((w->N + BN - 1) / BN), unsigned((M + 127) / 128), unsigned(ksplit));
+  fn<<<grid, TC_THREADS, Cfg::SMEM_BYTES, st>>>(tm_w, tm_xhi, tm_xlo, M, w->N, k_tiles, per, ep,
+                                                 slice_stride, ctx->d_err, ctx->timeout_ns,
+                                                 ctx->inject_fault);
+  CUDA_TRY(cudaGetLastError());
+  ctx->launches++;
+  return MYL_OK;
+}
+
+static int launch_split(myl_ctx* ctx, const int16_t* x, int64_t M, int64_t K, int64_t ldx,
+                        int8_t* xhi, uint8_t* xlo, int64_t ldp, cudaStream_t st) {
+  const int64_t groups = M * (ldp / 8);
+  unsigned blocks = unsigned(std::min<int64_t>((groups + 255) / 256, int64_t(ctx->num_sms) * 16));
+  split_hilo_kernel<<<blocks, 256, 0, st>>>(x, ldx, M, K, xhi, xlo, ldp);
+  CUDA_TRY(cudaGetLastError());
+  ctx->launches++;
+  return MYL_OK;
+}
+
+// tcgen05 GEMM from hi/lo planes ([M][ldp] each, ldp a multiple of 16).
+static int launch_tc_planes(myl_ctx* ctx, const myl_weight* w, const int8_t* xhi, const uint8_t* xlo,
+                            int64_t ldp, int64_t M, const Epilogue& ep_final, cudaStream_t st) {
+  const int64_t K = w->K;
+  bool swap = (ctx->force_swap >= 0) ? (ctx->force_swap != 0) : (M <= 256);
+  int BN = 256;
+  if (swap) {
+    BN = 32;
+    while (BN < M && BN < 256) BN *= 2;
+  }
+  const int rows_x = swap ? BN : 128;
+  CUtensorMap tm_xhi, tm_xlo;
+  TRY(encode_map(ctx, &tm_xhi, xhi, K, M, ldp, rows_x));
+  TRY(encode_map(ctx, &tm_xlo, xlo, K, M, ldp, rows_x));
+  // K split: enough CTAs for the SMs, and int32-exact slices (<= 65536).
+  const int k_tiles = int((K + TC_BK - 1) / TC_BK);
+  const int64_t tiles = swap ? ((w->N + 127) / 128) * ((M + BN - 1) / BN)
+                             : ((w->N + BN - 1) / BN) * ((M + 127) / 128);
+  int ksplit = 1;
+  if (ctx->force_split_k > 0) {
+    ksplit = ctx->force_split_k;
+  } else if (tiles < ctx->num_sms && k_tiles >= 8) {
+    ksplit = int(std::min<int64_t>(ctx->num_sms / tiles, k_tiles / 4));
+  }
+  ksplit = std::max(ksplit, int((K + 65535) / 65536));
+  ksplit = std::max(1, std::min(ksplit, k_tiles));
+  const int per = (k_tiles + ksplit - 1) / ksplit;
+  ksplit = (k_tiles + per - 1) / per;  // no empty slice
+  Epilogue ep = ep_final;
+  int64_t slice_stride = 0;
+  if (ksplit > 1) {
+    TRY(ensure(ctx->part, size_t(ksplit) * size_t(M) * size_t(w->N) * 8));
+    ep.mode = EPI_ACC_I64;
+    ep.y = ctx->part.p;
+    ep.ldy = w->N;
+    slice_stride = M * w->N;
+  }
+  int rc;
+  if (!swap) rc = launch_tc_variant<256, false, 3>(ctx, w, tm_xhi, tm_xlo, M, ksplit, per, k_tiles, ep, slice_stride, st);
+  else if (BN == 32) rc = launch_tc_variant<32, true, 8>(ctx, w, tm_xhi, tm_xlo, M, ksplit, per, k_tiles, ep, slice_stride, st);
+  else if (BN == 64) rc = launch_tc_variant<64, true, 6>(ctx, w, tm_xhi, tm_xlo, M, ksplit, per, k_tiles, ep, slice_stride, st);
+  else if (BN == 128) rc = launch_tc_variant<128, true, 4>(ctx, w, tm_xhi, tm_xlo, M, ksplit, per, k_tiles, ep, slice_stride, st);
+  else rc = launch_tc_variant<256, true, 2>(ctx, w, tm_xhi, tm_xlo, M, ksplit, per, k_tiles, ep, slice_stride, st);
+  TRY(rc);
+  if (ksplit > 1) {
+    const int64_t total = M * w->N;
+    unsigned blocks = unsigned(std::min<int64_t>((total + 255) / 256, int64_t(ctx->num_sms) * 8));
+    reduce_requant_kernel<<<blocks, 256, 0, st>>>(static_cast<const int64_t*>(ctx->part.p), ksplit,
+                                                   slice_stride, M, w->N, ep_final);
+    CUDA_TRY(cudaGetLastError());
+    ctx->launches++;
+  }
+  return MYL_OK;
+}
+
+static int launch_tc(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M, int64_t ldx,
+                     const Epilogue& ep_final, cudaStream_t st) {
+  const int64_t ldp = w->ldp;
+  TRY(ensure(ctx->planes, size_t(2) * size_t(M) * size_t(ldp)));
+  int8_t* xhi = static_cast<int8_t*>(ctx->planes.p);
+  uint8_t* xlo = reinterpret_cast<uint8_t*>(xhi + M * ldp);
+  TRY(launch_split(ctx, x, M, w->K, ldx, xhi, xlo, ldp, st));
+  return launch_tc_planes(ctx, w, xhi, xlo, ldp, M, ep_final, st);
+}
+
+static int run_linear(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M, int64_t ldx,
+                      const Epilogue& ep, cudaStream_t st) {
+  if (M == 0 || w->N == 0) return MYL_OK;
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  TRY(ws_acquire(ctx, st));
+  int rc = (M <= ctx->gemv_max_m && M <= 4) ? launch_gemv(ctx, w, x, M, ldx, ep, st)
+                                            : launch_tc(ctx, w, x, M, ldx, ep, st);
+  TRY(rc);
+  return ws_release(ctx, st);
+}
+
+static int check_device_error(myl_ctx* ctx) {
+  CUDA_TRY(cudaMemcpyAsync(ctx->h_err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+  CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  int e = *ctx->h_err;
+  if (e != 0) {
+    CUDA_TRY(cudaMemsetAsync(ctx->d_err, 0, sizeof(int), ctx->stream));
+    CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    return fail(MYL_ERR_DEVICE, "kernel reported error 0x%x (a bounded wait ran out)", e);
+  }
+  return MYL_OK;
+}
+
+// Host-pointer linear: upload x and the requant table, run, download y.
+static int host_linear(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M, int mode,
+                       int out_i32, const int8_t* shift, const int32_t* mult, void* y) {
+  if (!ctx || !w || (M > 0 && (!x || !y))) return fail(MYL_ERR_ARG, "null argument");
+  if (M < 0) return fail(MYL_ERR_SHAPE, "M = %lld is negative", (long long)M);
+  if (M == 0 || w->N == 0) return MYL_OK;
+  const int64_t N = w->N, K = w->K;
+  const size_t osz = out_i32 ? 4 : 2;
+  TRY(ensure(ctx->x, size_t(M) * size_t(K) * 2));
+  TRY(ensure(ctx->y, size_t(M) * size_t(N) * osz));
+  TRY(ensure(ctx->rq, size_t(N) * 5 + 64));
+  int32_t* d_mult = reinterpret_cast<int32_t*>(ctx->rq.p);
+  int8_t* d_shift = reinterpret_cast<int8_t*>(d_mult + N);
+  cudaStream_t st = ctx->stream;
+  CUDA_TRY(cudaMemcpyAsync(ctx->x.p, x, size_t(M) * size_t(K) * 2, cudaMemcpyHostToDevice, st));
+  CUDA_TRY(cudaMemcpyAsync(d_shift, shift, size_t(N), cudaMemcpyHostToDevice, st));
+  if (mult) CUDA_TRY(cudaMemcpyAsync(d_mult, mult, size_t(N) * 4, cudaMemcpyHostToDevice, st));
+  Epilogue ep{};
+  ep.mode = mode;
+  ep.out_i32 = out_i32;
+  ep.shift = d_shift;
+  ep.mult = mult ? d_mult : nullptr;
+  ep.y = ctx->y.p;
+  ep.ldy = N;
+  TRY(run_linear(ctx, w, static_cast<const int16_t*>(ctx->x.p), M, K, ep, st));
+  CUDA_TRY(cudaMemcpyAsync(y, ctx->y.p, size_t(M) * size_t(N) * osz, cudaMemcpyDeviceToHost, st));
+  return check_device_error(ctx);
+}
+
+// ---------------------------------------------------------------------------------
+// C ABI
+
+extern "C" {
+
+const char* myl_last_error(void) { return g_last_error.c_str(); }
+int myl_abi_version(void) { return MYL_ABI_VERSION; }
+
+int myl_init(int device, myl_ctx** out) {
+  if (!out) return fail(MYL_ERR_ARG, "out is null");
+  *out = nullptr;
+  int n = 0;
+  CUDA_TRY(cudaGetDeviceCount(&n));
+  if (device < 0 || device >= n) return fail(MYL_ERR_ARG, "device %d not present (%d devices)", device, n);
+  CUDA_TRY(cudaSetDevice(device));
+  cudaDeviceProp prop;
+  CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10)
+    return fail(MYL_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a only",
+                device, prop.major, prop.minor);
+  myl_ctx* c = new myl_ctx();
+  c->device = device;
+  c->sm = prop.major * 10 + prop.minor;
+  c->num_sms = prop.multiProcessorCount;
+  cudaDriverEntryPointQueryResult q;
+  void* fn = nullptr;
+  cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000,
+                                                   cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) {
+    delete c;
+    return fail(MYL_ERR_CUDA, "cuTensorMapEncodeTiled not available from the driver");
+  }
+  c->encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&c->ws_event, cudaEventDisableTiming) != cudaSuccess ||
+      cudaMalloc(&c->d_err, sizeof(int)) != cudaSuccess ||
+      cudaMallocHost(&c->h_err, sizeof(int)) != cudaSuccess ||
+      cudaMemset(c->d_err, 0, sizeof(int)) != cudaSuccess) {
+    myl_destroy(c);
+    return fail(MYL_ERR_CUDA, "context allocation failed");
+  }
+  *out = c;
+  return MYL_OK;
+}
+
+int myl_destroy(myl_ctx* ctx) {
+  if (!ctx) return MYL_OK;
+  cudaSetDevice(ctx->device);
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  for (auto& kv : ctx->backend_cache) myl_weight_release(ctx, kv.second);
+  ctx->backend_cache.clear();
+  for (DevBuf* b : {&ctx->x, &ctx->y, &ctx->rq, &ctx->planes, &ctx->part})
+    if (b->p) cudaFree(b->p);
+  if (ctx->d_err) cudaFree(ctx->d_err);
+  if (ctx->h_err) cudaFreeHost(ctx->h_err);
+  if (ctx->ws_event) cudaEventDestroy(ctx->ws_event);
+  if (ctx->stream) cudaStreamDestroy(ctx->stream);
+  delete ctx;
+  return MYL_OK;
+}
+
+int myl_device_info(const myl_ctx* ctx, int* device, int* sm_version, int* num_sms) {
+  if (!ctx) return fail(MYL_ERR_ARG, "ctx is null");
+  if (device) *device = ctx->device;
+  if (sm_version) *sm_version = ctx->sm;
+  if (num_sms) *num_sms = ctx->num_sms;
+  return MYL_OK;
+}
+
+int myl_weight_register(myl_ctx* ctx, const int8_t* W, int64_t out_features, int64_t in_features,
+                        int64_t ldw, const uint8_t* w_shifts, myl_weight** out) {
+  if (!ctx || !out || (out_features > 0 && (!W || !w_shifts))) return fail(MYL_ERR_ARG, "null argument");
+  *out = nullptr;
+  // linear.rs:61 W.chunks_exact(in_features) panics for 0; the row count must fit the TMA map.
+  if (in_features <= 0 || out_features < 0 || ldw < in_features)
+    return fail(MYL_ERR_SHAPE, "bad weight shape [%lld][%lld] ld %lld", (long long)out_features,
+                (long long)in_features, (long long)ldw);
+  if (out_features > (int64_t(1) << 31) || in_features > (int64_t(1) << 31))
+    return fail(MYL_ERR_UNSUPPORTED, "weight dimension beyond 2^31");
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  myl_weight* w = new myl_weight();
+  w->N = out_features;
+  w->K = in_features;
+  w->ldp = (in_features + 15) & ~int64_t(15);
+  w->w_shifts.assign(w_shifts, w_shifts + out_features);
+  const size_t bytes = size_t(std::max<int64_t>(out_features, 1)) * size_t(w->ldp);
+  if (cudaMalloc(&w->d_W, bytes) != cudaSuccess) {
+    delete w;
+    return fail(MYL_ERR_CUDA, "cudaMalloc of %zu weight bytes failed", bytes);
+  }
+  int rc = MYL_OK;
+  if (cudaMemsetAsync(w->d_W, 0, bytes, ctx->stream) != cudaSuccess ||
+      (out_features > 0 &&
+       cudaMemcpy2DAsync(w->d_W, size_t(w->ldp), W, size_t(ldw), size_t(in_features),
+                         size_t(out_features), cudaMemcpyHostToDevice, ctx->stream) != cudaSuccess) ||
+      cudaStreamSynchronize(ctx->stream) != cudaSuccess)
+    rc = fail(MYL_ERR_CUDA, "weight upload failed: %s", cudaGetErrorString(cudaGetLastError()));
+  if (rc == MYL_OK && out_features > 0) {
+    rc = encode_map(ctx, &w->tm128, w->d_W, w->K, w->N, w->ldp, 128);
+    if (rc == MYL_OK) rc = encode_map(ctx, &w->tm256, w->d_W, w->K, w->N, w->ldp, 256);
+  }
+  if (rc != MYL_OK) {
+    cudaFree(w->d_W);
+    delete w;
+    return rc;
+  }
+  *out = w;
+  return MYL_OK;
+}
+
+int myl_weight_release(myl_ctx* ctx, myl_weight* w) {
+  if (!ctx || !w) return MYL_OK;
+  cudaSetDevice(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  if (w->d_W) cudaFree(w->d_W);
+  delete w;
+  return MYL_OK;
+}
+
+int myl_linear_w8a16(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
+                     uint8_t act_frac_bits, uint8_t out_frac_bits, int16_t* y) {
+  if (!ctx || !w) return fail(MYL_ERR_ARG, "null argument");
+  std::vector<int8_t> s;
+  TRY(shift_plan(w, act_frac_bits, &out_frac_bits, 0, s));
+  return host_linear(ctx, w, x, M, EPI_SHIFT, 0, s.data(), nullptr, y);
+}
+
+int myl_linear_w8a16_pc(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
+                        uint8_t act_frac_bits, const uint8_t* out_frac_bits, int16_t* y) {
+  if (!ctx || !w || (w->N > 0 && !out_frac_bits)) return fail(MYL_ERR_ARG, "null argument");
+  std::vector<int8_t> s;
+  TRY(shift_plan(w, act_frac_bits, out_frac_bits, 1, s));
+  return host_linear(ctx, w, x, M, EPI_SHIFT, 0, s.data(), nullptr, y);
+}
+
+int myl_lm_head_w8a16_i32(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
+                          uint8_t final_norm_frac, uint8_t logit_frac, int32_t* logits) {
+  if (!ctx || !w) return fail(MYL_ERR_ARG, "null argument");
+  std::vector<int8_t> s;
+  TRY(shift_plan(w, final_norm_frac, &logit_frac, 0, s));
+  return host_linear(ctx, w, x, M, EPI_SHIFT, 1, s.data(), nullptr, logits);
+}
+
+int myl_linear_w8a16_mult(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
+                          const int32_t* mult, const uint8_t* shift, int16_t* y) {
+  if (!ctx || !w || (w->N > 0 && (!mult || !shift))) return fail(MYL_ERR_ARG, "null argument");
+  for (int64_t r = 0; r < w->N; ++r)
+    if (shift[r] > 126) return fail(MYL_ERR_OVERFLOW, "multiplier shift %u > 126", unsigned(shift[r]));
+  return host_linear(ctx, w, x, M, EPI_MULT, 0, reinterpret_cast<const int8_t*>(shift), mult, y);
+}
+
+int myl_backend_linear_w8a16(myl_ctx* ctx, const int16_t* x, const int8_t* W, int16_t* out,
+                             uint64_t in_features, uint64_t out_features, const uint8_t* w_shifts,
+                             uint8_t act_frac, uint8_t out_frac) {
+  if (!ctx || !W || !x || !out || !w_shifts) return fail(MYL_ERR_ARG, "null argument");
+  myl_weight* w = nullptr;
+  auto it = ctx->backend_cache.find(W);
+  if (it != ctx->backend_cache.end()) {
+    myl_weight* c = it->second;
+    if (uint64_t(c->K) == in_features && uint64_t(c->N) == out_features &&
+        c->host_shifts == w_shifts &&
+        std::memcmp(c->w_shifts.data(), w_shifts, size_t(out_features)) == 0) {
+      w = c;
+    } else {
+      myl_weight_release(ctx, c);
+      ctx->backend_cache.erase(it);
+    }
+  }
+  if (!w) {
+    TRY(myl_weight_register(ctx, W, int64_t(out_features), int64_t(in_features),
+                            int64_t(in_features), w_shifts, &w));
+    w->host_W = W;
+    w->host_shifts = w_shifts;
+    ctx->backend_cache[W] = w;
+  }
+  return myl_linear_w8a16(ctx, w, x, 1, act_frac, out_frac, out);
+}
+
+int myl_backend_forget(myl_ctx* ctx, const int8_t* W) {
+  if (!ctx) return fail(MYL_ERR_ARG, "ctx is null");
+  auto it = ctx->backend_cache.find(W);
+  if (it != ctx->backend_cache.end()) {
+    myl_weight_release(ctx, it->second);
+    ctx->backend_cache.erase(it);
+  }
+  return MYL_OK;
+}
+
+int myl_requant_create(myl_ctx* ctx, const myl_weight* w, int mode, uint8_t act_frac,
+                       const uint8_t* out_frac_pc, int per_channel, const int32_t* mult,
+                       const uint8_t* shift, myl_requant** out) {
+  if (!ctx || !w || !out) return fail(MYL_ERR_ARG, "null argument");
+  *out = nullptr;
+  const int64_t N = w->N;
+  std::vector<int8_t> s;
+  std::vector<int32_t> m;
+  if (mode == MYL_RQ_SHIFT_I16 || mode == MYL_RQ_SHIFT_I32) {
+    if (N > 0 && !out_frac_pc) return fail(MYL_ERR_ARG, "out_frac is null");
+    if (N > 0) TRY(shift_plan(w, act_frac, out_frac_pc, per_channel, s));
+  } else if (mode == MYL_RQ_MULT_I16) {
+    if (N > 0 && (!mult || !shift)) return fail(MYL_ERR_ARG, "mult/shift is null");
+    s.resize(size_t(N));
+    m.assign(mult, mult + N);
+    for (int64_t r = 0; r < N; ++r) {
+      if (shift[r] > 126) return fail(MYL_ERR_OVERFLOW, "multiplier shift %u > 126", unsigned(shift[r]));
+      s[size_t(r)] = int8_t(shift[r]);
+    }
+  } else {
+    return fail(MYL_ERR_ARG, "unknown requant mode %d", mode);
+  }
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  myl_requant* rq = new myl_requant();
+  rq->N = N;
+  rq->mode = mode;
+  const size_t nb = size_t(std::max<int64_t>(N, 1));
+  if (cudaMalloc(&rq->d_shift, nb) != cudaSuccess ||
+      (!m.empty() && cudaMalloc(&rq->d_mult, nb * 4) != cudaSuccess)) {
+    myl_requant_release(ctx, rq);
+    return fail(MYL_ERR_CUDA, "requant allocation failed");
+  }
+  if ((N > 0 && cudaMemcpy(rq->d_shift, s.data(), size_t(N), cudaMemcpyHostToDevice) != cudaSuccess) ||
+      (!m.empty() && cudaMemcpy(rq->d_mult, m.data(), size_t(N) * 4, cudaMemcpyHostToDevice) != cudaSuccess)) {
+    myl_requant_release(ctx, rq);
+    return fail(MYL_ERR_CUDA, "requant upload failed");
+  }
+  *out = rq;
+  return MYL_OK;
+}
+
+int myl_requant_release(myl_ctx* ctx, myl_requant* rq) {
+  if (!rq) return MYL_OK;
+  if (ctx) cudaSetDevice(ctx->device);
+  if (rq->d_shift) cudaFree(rq->d_shift);
+  if (rq->d_mult) cudaFree(rq->d_mult);
+  delete rq;
+  return MYL_OK;
+}
+
+static Epilogue make_ep(const myl_requant* rq, void* y, int64_t ldy) {
+  Epilogue ep{};
+  ep.mode = (rq->mode == MYL_RQ_MULT_I16) ? EPI_MULT : EPI_SHIFT;
+  ep.out_i32 = (rq->mode == MYL_RQ_SHIFT_I32) ? 1 : 0;
+  ep.shift = rq->d_shift;
+  ep.mult = rq->d_mult;
+  ep.y = y;
+  ep.ldy = ldy;
+  return ep;
+}
+
+int myl_linear_dev(myl_ctx* ctx, const myl_weight* w, const myl_requant* rq, const int16_t* x,
+                   int64_t M, int64_t ldx, void* y, int64_t ldy, void* stream) {
+  if (!ctx || !w || !rq || (M > 0 && (!x || !y))) return fail(MYL_ERR_ARG, "null argument");
+  if (rq->N != w->N) return fail(MYL_ERR_SHAPE, "requant has %lld channels, weight %lld",
+                                 (long long)rq->N, (long long)w->N);
+  if (M < 0 || ldx < w->K || ldy < w->N) return fail(MYL_ERR_SHAPE, "bad M/ldx/ldy");
+  return run_linear(ctx, w, x, M, ldx, make_ep(rq, y, ldy), static_cast<cudaStream_t>(stream));
+}
+
+int myl_linear_acc_dev(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M, int64_t ldx,
+                       int64_t* acc, void* stream) {
+  if (!ctx || !w || (M > 0 && (!x || !acc))) return fail(MYL_ERR_ARG, "null argument");
+  if (M < 0 || ldx < w->K) return fail(MYL_ERR_SHAPE, "bad M/ldx");
+  Epilogue ep{};
+  ep.mode = EPI_ACC_I64;
+  ep.y = acc;
+  ep.ldy = w->N;
+  return run_linear(ctx, w, x, M, ldx, ep, static_cast<cudaStream_t>(stream));
+}
+
+int myl_requant_acc_dev(myl_ctx* ctx, const myl_requant* rq, const int64_t* acc, int64_t M, void* y,
+                        int64_t ldy, void* stream) {
+  if (!ctx || !rq || (M > 0 && (!acc || !y))) return fail(MYL_ERR_ARG, "null argument");
+  if (M < 0 || ldy < rq->N) return fail(MYL_ERR_SHAPE, "bad M/ldy");
+  if (M == 0 || rq->N == 0) return MYL_OK;
+  const int64_t total = M * rq->N;
+  unsigned blocks = unsigned(std::min<int64_t>((total + 255) / 256, int64_t(ctx->num_sms) * 8));
+  reduce_requant_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      acc, 1, 0, M, rq->N, make_ep(rq, y, ldy));
+  CUDA_TRY(cudaGetLastError());
+  ctx->launches++;
+  return MYL_OK;
+}
+
+int myl_split_hilo_dev(myl_ctx* ctx, const int16_t* x, int64_t M, int64_t K, int64_t ldx,
+                       int8_t* xhi, uint8_t* xlo, int64_t ldp, void* stream) {
+  if (!ctx || (M > 0 && (!x || !xhi || !xlo))) return fail(MYL_ERR_ARG, "null argument");
+  if (M < 0 || K <= 0 || ldx < K || ldp < K || ldp % 16 != 0)
+    return fail(MYL_ERR_SHAPE, "bad split shape (ldp must be a multiple of 16 and >= K)");
+  if ((reinterpret_cast<uintptr_t>(xhi) | reinterpret_cast<uintptr_t>(xlo)) & 15)
+    return fail(MYL_ERR_ARG, "plane pointers must be 16-byte aligned");
+  if (M == 0) return MYL_OK;
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  return launch_split(ctx, x, M, K, ldx, xhi, xlo, ldp, static_cast<cudaStream_t>(stream));
+}
+
+int myl_linear_planes_dev(myl_ctx* ctx, const myl_weight* w, const myl_requant* rq,
+                          const int8_t* xhi, const uint8_t* xlo, int64_t ldp, int64_t M, void* y,
+                          int64_t ldy, void* stream) {
+  if (!ctx || !w || (M > 0 && (!xhi || !xlo || !y))) return fail(MYL_ERR_ARG, "null argument");
+  if (M < 0 || ldp < w->K || ldp % 16 != 0 || ldy < w->N)
+    return fail(MYL_ERR_SHAPE, "bad M/ldp/ldy");
+  if ((reinterpret_cast<uintptr_t>(xhi) | reinterpret_cast<uintptr_t>(xlo)) & 15)
+    return fail(MYL_ERR_ARG, "plane pointers must be 16-byte aligned");
+  if (rq && rq->N != w->N) return fail(MYL_ERR_SHAPE, "requant/weight channel mismatch");
+  if (M == 0 || w->N == 0) return MYL_OK;
+  Epilogue ep{};
+  if (rq) {
+    ep = make_ep(rq, y, ldy);
+  } else {
+    ep.mode = EPI_ACC_I64;
+    ep.y = y;
+    ep.ldy = ldy;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  TRY(ws_acquire(ctx, st));
+  TRY(launch_tc_planes(ctx, w, xhi, xlo, ldp, M, ep, st));
+  return ws_release(ctx, st);
+}
+
+int myl_synchronize(myl_ctx* ctx) {
+  if (!ctx) return fail(MYL_ERR_ARG, "ctx is null");
+  CUDA_TRY(cudaDeviceSynchronize());
+  return check_device_error(ctx);
+}
+
+int myl_set_wait_timeout_ns(myl_ctx* ctx, uint64_t ns) {
+  if (!ctx || ns == 0) return fail(MYL_ERR_ARG, "bad argument");
+  ctx->timeout_ns = ns;
+  return MYL_OK;
+}
+
+int myl_set_dispatch(myl_ctx* ctx, int gemv_max_m, int force_split_k, int force_swap) {
+  if (!ctx) return fail(MYL_ERR_ARG, "ctx is null");
+  ctx->gemv_max_m = gemv_max_m;
+  ctx->force_split_k = force_split_k;
+  ctx->force_swap = force_swap;
+  return MYL_OK;
+}
+
+int myl_debug_inject_wait_fault(myl_ctx* ctx, int on) {
+  if (!ctx) return fail(MYL_ERR_ARG, "ctx is null");
+  ctx->inject_fault = on ? 1 : 0;
+  return MYL_OK;
+}
+
+int64_t myl_launch_count(const myl_ctx* ctx) { return ctx ? ctx->launches : -1; }
+
+}  // extern "C"
