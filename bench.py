@@ -1,0 +1,492 @@
+#!/usr/bin/env python
+"""W8A16 hot-path benchmark: prints one JSON line on rank 0.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: the W8A16 linear at the Qwen2.5-7B MLP shapes,
+gate/up (K=3584 -> N=18944) and down (K=18944 -> N=3584), M=2048 activation
+rows. One step = both shapes once: split x into byte planes, tcgen05 GEMM,
+requant epilogue. Int8 weights uniform in [-127, 127], int16 activations
+rounded N(0, 1024^2) clipped to +-32767, per-channel power-of-two requant;
+synthetic, seeded, random-init.
+
+N GPUs (torchrun): Megatron tensor parallelism of the same step. The gate/up
+shape is column-parallel (N split), the down shape row-parallel (K split):
+each rank writes exact int64 partial sums, NCCL sums them (int64 all-reduce)
+and the requant runs once after the sum, so the result is bit-identical at
+every GPU count. Total work is fixed: strong scaling.
+
+value      whole-job algorithmic int TOPS (2*M*K*N per linear) over the timed
+           steps, device time, max over ranks. Inputs are resident in HBM.
+e2e        the same metric through the reference-facing host-pointer C ABI
+           (myl_linear_w8a16 with pinned host buffers; at N>1 the host input
+           and output copies around the tensor-parallel device step).
+roofline   the tcgen05 GEMM kernel: algorithmic TOPS per launch from CUDA
+           events around each launch, against the effective split-byte peak.
+gemv       decode GEMV (M=1) at both shapes: weight-streaming GB/s vs HBM.
+cpu_baseline  the CPU oracle (C restatement of the reference's Rust loop) on a
+           bounded row sample, all host cores, rank 0 at N=1.
+L2: 4 rotating weight sets per shape (>= 4x the 126 MB L2 per step cycle), so
+every weight byte comes from HBM.
+
+--impl reference runs only the CPU oracle (the reference's algorithm; the Rust
+original cannot be built here) with the same metric, config and unit.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "W8A16 GEMM TOPS & GEMV GB/s; 7B-shape int decode tok/s at 1/2/4/8 GPU"
+SHAPES = [(3584, 18944), (18944, 3584)]  # (K, N): gate/up, down
+M_HEAD = 2048
+SWEEP_M = [1, 16, 128, 512, 2048]
+L2_BYTES = 126 * 1024 * 1024
+ACT_FRAC, OUT_FRAC = 8, 8
+
+
+def kbits(K: int) -> int:
+    """Per-row weight shift that keeps outputs unsaturated: round(log2(73.6*sqrt(K)))."""
+    return int(round(math.log2(73.6 * math.sqrt(K))))
+
+
+def load_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        d["source"] = "measured"
+        return d
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+def load_traffic() -> dict:
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, reasons, power = [], None, set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_max": max(power) if power else None}
+
+
+# ---------------------------------------------------------------------------------------
+# CPU oracle (the reference's algorithm): bounded samples
+
+
+def cpu_sample_tops(target_s: float, rng) -> dict:
+    """Times the oracle's linear_w8a16 on a row sample of the step (both shapes),
+    sized to about target_s seconds, on all host threads."""
+    import oracle as O
+
+    ws = {}
+    for K, N in SHAPES:
+        W = rng.integers(-127, 128, size=N * K, dtype=np.int8)
+        s = rng.integers(kbits(K) - 1, kbits(K) + 2, size=N).astype(np.uint8)
+        ws[(K, N)] = (W, s)
+
+    def run(rows: int) -> float:
+        t0 = time.perf_counter()
+        for K, N in SHAPES:
+            W, s = ws[(K, N)]
+            x = np.clip(np.rint(rng.normal(0, 1024, size=(rows, K))), -32767, 32767).astype(np.int16)
+            O.linear_w8a16(x, W, K, s, ACT_FRAC, OUT_FRAC)
+        return time.perf_counter() - t0
+
+    run(1)  # warm-up (page-in, thread pool)
+    t1 = run(1)
+    rows = max(1, min(M_HEAD, int(target_s / max(t1, 1e-6))))
+    t = run(rows)
+    ops = 2.0 * rows * sum(K * N for K, N in SHAPES)
+    return {"value": ops / t / 1e12, "unit": "TOPS", "cores": O.num_threads(), "kind": "port",
+            "sample": f"{rows} of {M_HEAD} rows at both shapes (K,N)={SHAPES}, {t:.1f} s",
+            "seconds": t}
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    rng = np.random.default_rng(1234)
+    import oracle as O
+
+    O.build()
+    per_step = float(os.environ.get("MYL_REF_STEP_S", "4.0"))
+    for _ in range(args.warmup):
+        cpu_sample_tops(per_step / 4, rng)
+    vals, secs = [], 0.0
+    for _ in range(args.steps):
+        r = cpu_sample_tops(per_step, rng)
+        vals.append(r["value"])
+        secs += r["seconds"]
+    v = statistics.mean(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "TOPS", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * secs / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int8xint16->int64", "data": "synthetic",
+        "config": {"workload": "config1: W8A16 linear, Qwen2.5-7B MLP shapes", "M": M_HEAD,
+                   "shapes_KN": SHAPES, "parallelism": "cpu"},
+        "cpu_baseline": {"value": v, "unit": "TOPS", "cores": O.num_threads(), "kind": "port",
+                         "sample": r["sample"]},
+        "e2e": {"value": v, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "CPU restatement of the reference's Rust loop (dot_scalar + rescale_i64 + clamp), "
+                "OpenMP over output rows; the Rust crate cannot be built in this image",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------
+# GPU arm
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--m", type=int, default=M_HEAD)
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import myelith_b200 as myl
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    tp, r = world, rank
+    ctx = myl.Context(local)
+    stream = torch.cuda.Stream(device=dev)
+    M = args.m
+    peaks = load_peaks()
+
+    # ---- weights: TP shards, NSETS rotating sets ----
+    rng = np.random.default_rng(1000 + r)
+    K1, N1 = SHAPES[0]
+    K2, N2 = SHAPES[1]
+    assert N1 % tp == 0 and K2 % tp == 0
+    n1, k2 = N1 // tp, K2 // tp
+    per_set = n1 * K1 + N2 * k2
+    nsets = max(2, math.ceil(4 * L2_BYTES / per_set))
+    s1 = rng.integers(kbits(K1) - 1, kbits(K1) + 2, size=N1).astype(np.uint8)[r * n1:(r + 1) * n1]
+    s2 = rng.integers(kbits(K2) - 1, kbits(K2) + 2, size=N2).astype(np.uint8)
+    W1s, W2s, R1s, R2s = [], [], [], []
+    for _ in range(nsets):
+        w1 = ctx.weight(rng.integers(-127, 128, size=(n1, K1), dtype=np.int8), K1, s1)
+        w2 = ctx.weight(rng.integers(-127, 128, size=(N2, k2), dtype=np.int8), k2, s2)
+        W1s.append(w1)
+        W2s.append(w2)
+        R1s.append(w1.requant(myl.RQ_SHIFT_I16, ACT_FRAC, OUT_FRAC))
+        R2s.append(w2.requant(myl.RQ_SHIFT_I16, ACT_FRAC, OUT_FRAC))
+
+    def act(shape):
+        return np.clip(np.rint(rng.normal(0, 1024, size=shape)), -32767, 32767).astype(np.int16)
+
+    x1_h, x2_h = act((M, K1)), act((M, k2))
+    with torch.cuda.stream(stream):
+        x1 = torch.from_numpy(x1_h).to(dev)
+        x2 = torch.from_numpy(x2_h).to(dev)
+        ldp1, ldp2 = (K1 + 15) // 16 * 16, (k2 + 15) // 16 * 16
+        p1h = torch.empty((M, ldp1), dtype=torch.int8, device=dev)
+        p1l = torch.empty((M, ldp1), dtype=torch.uint8, device=dev)
+        p2h = torch.empty((M, ldp2), dtype=torch.int8, device=dev)
+        p2l = torch.empty((M, ldp2), dtype=torch.uint8, device=dev)
+        y1 = torch.empty((M, n1), dtype=torch.int16, device=dev)
+        y2 = torch.empty((M, N2), dtype=torch.int16, device=dev)
+        acc2 = torch.empty((M, N2), dtype=torch.int64, device=dev) if tp > 1 else None
+    stream.synchronize()
+
+    gemm_events: list = []
+
+    def step(i: int, record: bool) -> None:
+        s = i % nsets
+        ctx.split_hilo_dev(x1, p1h, p1l, stream)
+        if record:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        W1s[s].linear_planes_dev(R1s[s], p1h, p1l, M, y1, stream)
+        if record:
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record(stream)
+        ctx.split_hilo_dev(x2, p2h, p2l, stream)
+        if record:
+            e2 = torch.cuda.Event(enable_timing=True)
+            e2.record(stream)
+        if tp == 1:
+            W2s[s].linear_planes_dev(R2s[s], p2h, p2l, M, y2, stream)
+        else:
+            W2s[s].linear_planes_dev(None, p2h, p2l, M, acc2, stream)
+        if record:
+            e3 = torch.cuda.Event(enable_timing=True)
+            e3.record(stream)
+            gemm_events.append((e0, e1))
+            gemm_events.append((e2, e3))
+        if tp > 1:
+            dist.all_reduce(acc2, op=dist.ReduceOp.SUM)
+            R2s[s].apply_acc_dev(acc2, y2, stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i, False)
+        stream.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        sampler = ClockSampler(local)
+        sampler.start()
+        time.sleep(0.3)
+        launches0 = ctx.launch_count
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record(stream)
+        w0 = time.perf_counter()
+        for i in range(args.steps):
+            step(args.warmup + i, True)
+        t_end.record(stream)
+        stream.synchronize()
+        wall = time.perf_counter() - w0
+        launches = ctx.launch_count - launches0
+        clocks = sampler.stop()
+        barrier()
+        torch.cuda.synchronize()
+    ctx.synchronize()
+    dev_ms = t_start.elapsed_time(t_end)
+    dev_ms = max_over_ranks(dev_ms)
+    ops_step = 2.0 * M * sum(K * N for K, N in SHAPES)
+    value = ops_step * args.steps / (dev_ms * 1e-3) / 1e12
+    gemm_ms = [a.elapsed_time(b) for a, b in gemm_events]
+    gemm_avg_ms = statistics.mean(gemm_ms)
+    gemm_ops = 2.0 * M * (n1 * K1)  # per launch; both shapes carry the same work per rank
+    achieved = gemm_ops / (gemm_avg_ms * 1e-3) / 1e12
+    long_step = dev_ms > 1000.0
+    int8_dense = 2.0 * (peaks["bf16_tflops_sustained"] if long_step else peaks["bf16_tflops"])
+    eff_peak = int8_dense / 2.0
+    traffic = load_traffic().get(f"gemm_tc_M{M}_tp{tp}")
+
+    # ---- e2e: host buffers through the reference-facing call ----
+    e2e = None
+    if tp == 1:
+        x1_pin = torch.from_numpy(x1_h).pin_memory().numpy()
+        x2_pin = torch.from_numpy(x2_h).pin_memory().numpy()
+        y1_pin = torch.empty((M, n1), dtype=torch.int16).pin_memory().numpy()
+        y2_pin = torch.empty((M, N2), dtype=torch.int16).pin_memory().numpy()
+        L = myl.load_library()
+
+        def e2e_step(i):
+            s = i % nsets
+            myl._check("myl_linear_w8a16", L.myl_linear_w8a16(
+                ctx.handle, W1s[s].handle, x1_pin.ctypes.data, M, ACT_FRAC, OUT_FRAC, y1_pin.ctypes.data))
+            myl._check("myl_linear_w8a16", L.myl_linear_w8a16(
+                ctx.handle, W2s[s].handle, x2_pin.ctypes.data, M, ACT_FRAC, OUT_FRAC, y2_pin.ctypes.data))
+
+        for i in range(args.warmup):
+            e2e_step(i)
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            e2e_step(i)
+        e2e_s = time.perf_counter() - t0
+        e2e = {"value": ops_step * args.steps / e2e_s / 1e12, "unit": "TOPS",
+               "h2d_bytes_per_step": int(x1_h.nbytes + x2_h.nbytes),
+               "d2h_bytes_per_step": int(y1_pin.nbytes + y2_pin.nbytes),
+               "path": "myl_linear_w8a16 (host pointers, pinned), both shapes"}
+    else:
+        x1_pin = torch.from_numpy(x1_h).pin_memory()
+        x2_pin = torch.from_numpy(x2_h).pin_memory()
+        y2_pin = torch.empty((M, N2), dtype=torch.int16).pin_memory()
+        y1_pin = torch.empty((M, n1), dtype=torch.int16).pin_memory()
+
+        def e2e_step(i):
+            x1.copy_(x1_pin, non_blocking=True)
+            x2.copy_(x2_pin, non_blocking=True)
+            step(i, False)
+            y1_pin.copy_(y1, non_blocking=True)
+            y2_pin.copy_(y2, non_blocking=True)
+            stream.synchronize()
+
+        with torch.cuda.stream(stream):
+            for i in range(args.warmup):
+                e2e_step(i)
+            barrier()
+            t0 = time.perf_counter()
+            for i in range(args.steps):
+                e2e_step(i)
+            e2e_s = max_over_ranks(time.perf_counter() - t0)
+        e2e = {"value": ops_step * args.steps / e2e_s / 1e12, "unit": "TOPS",
+               "h2d_bytes_per_step": int(x1_h.nbytes + x2_h.nbytes),
+               "d2h_bytes_per_step": int(y1_pin.numel() * 2 + y2_pin.numel() * 2),
+               "path": "host copies + tensor-parallel device step per rank"}
+
+    # ---- M sweep and decode GEMV (N=1 only) ----
+    sweep, gemv = None, None
+    if tp == 1 and not args.no_sweep:
+        sweep = []
+        gemv_gbs = []
+        for Ms in SWEEP_M:
+            xs = {K: torch.from_numpy(act((Ms, K))).to(dev) for K, _ in SHAPES}
+            ys = {N: torch.empty((Ms, N), dtype=torch.int16, device=dev) for _, N in SHAPES}
+            res = {}
+            for j, (K, N) in enumerate(SHAPES):
+                Ws, Rs = (W1s, R1s) if j == 0 else (W2s, R2s)
+                iters = 20 if Ms <= 128 else 8
+                with torch.cuda.stream(stream):
+                    for i in range(3):
+                        Ws[i % nsets].linear_dev(Rs[i % nsets], xs[K], ys[N], stream)
+                    a = torch.cuda.Event(enable_timing=True)
+                    b = torch.cuda.Event(enable_timing=True)
+                    a.record(stream)
+                    for i in range(iters):
+                        Ws[i % nsets].linear_dev(Rs[i % nsets], xs[K], ys[N], stream)
+                    b.record(stream)
+                    stream.synchronize()
+                ms = a.elapsed_time(b) / iters
+                tops = 2.0 * Ms * K * N / (ms * 1e-3) / 1e12
+                bytes_ = N * K + 2 * Ms * K + 2 * Ms * N + N
+                gbs = bytes_ / (ms * 1e-3) / 1e9
+                res[f"{K}x{N}"] = {"us": round(ms * 1e3, 2), "tops": round(tops, 2), "gbs": round(gbs, 1)}
+                if Ms == 1:
+                    gemv_gbs.append(gbs)
+            sweep.append({"M": Ms, **res})
+        ctx.synchronize()
+        gemv = {"gbs": round(statistics.mean(gemv_gbs), 1), "peak_gbs": peaks["hbm_gbs"],
+                "frac": round(statistics.mean(gemv_gbs) / peaks["hbm_gbs"], 3),
+                "per_shape_gbs": [round(g, 1) for g in gemv_gbs],
+                "bytes": "N*K weights + 2K act + 2N out + N shift bytes per launch"}
+
+    # ---- CPU baseline (rank 0, N=1) ----
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_sample_tops(float(os.environ.get("MYL_CPU_SAMPLE_S", "8.0")),
+                              np.random.default_rng(77))
+        cpu.pop("seconds", None)
+
+    if world > 1:
+        barrier()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "TOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int8xint16->int64", "data": "synthetic",
+            "config": {"workload": "config1: W8A16 linear at Qwen2.5-7B MLP shapes, gate/up + down per step",
+                       "M": M, "shapes_KN": SHAPES, "parallelism": f"tp{tp}",
+                       "l2": f"inputs larger than L2: {nsets} rotating weight sets "
+                             f"({nsets * per_set / 2**20:.0f} MiB per rank)"},
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(eff_peak, 1),
+                         "unit": "TFLOP/s", "frac": round(achieved / eff_peak, 4),
+                         "traffic": traffic,
+                         "kernel": "gemm_w8a16_tc_kernel", "launches": len(gemm_ms),
+                         "avg_us": round(gemm_avg_ms * 1e3, 2),
+                         "peak_basis": ("effective split-byte peak = int8 dense / 2; int8 dense = 2 x "
+                                        f"cuBLAS bf16 {'sustained' if long_step else 'burst'} "
+                                        f"({peaks['source']} MEASURED_PEAKS)"),
+                         "ops": "integer ops, 2 per algorithmic MAC; the tensor pipe runs 2x these"},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+            "wall_s_timed": round(wall, 4),
+            "gemv": gemv,
+            "sweep": sweep,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

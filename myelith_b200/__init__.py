@@ -91,6 +91,8 @@ def load_library(path: str | None = None):
             "myl_linear_dev": ([vp, vp, vp, vp, i64, i64, vp, i64, vp], i32),
             "myl_linear_acc_dev": ([vp, vp, vp, i64, i64, vp, vp], i32),
             "myl_requant_acc_dev": ([vp, vp, vp, i64, vp, i64, vp], i32),
+            "myl_split_hilo_dev": ([vp, vp, i64, i64, i64, vp, vp, i64, vp], i32),
+            "myl_linear_planes_dev": ([vp, vp, vp, vp, vp, i64, i64, vp, i64, vp], i32),
             "myl_synchronize": ([vp], i32),
             "myl_set_wait_timeout_ns": ([vp, C.c_uint64], i32),
             "myl_set_dispatch": ([vp, i32, i32, i32], i32),
@@ -172,6 +174,12 @@ class Context:
 
     def weight(self, W, in_features: int, w_shifts, ldw: int | None = None) -> "Weight":
         return Weight(self, W, in_features, w_shifts, ldw)
+
+    def split_hilo_dev(self, x, xhi, xlo, stream=None) -> None:
+        """x [M, K] int16 (torch CUDA) -> byte planes xhi int8 / xlo uint8 [M, ldp]."""
+        M, K = x.shape
+        _check("myl_split_hilo_dev", load_library().myl_split_hilo_dev(
+            self._h, _p(x), M, K, x.stride(0), _p(xhi), _p(xlo), xhi.stride(0), _stream_ptr(stream)))
 
 
 class Weight:
@@ -269,6 +277,12 @@ class Weight:
         _check("myl_linear_dev", load_library().myl_linear_dev(
             self.ctx.handle, self._h, rq.handle, _p(x), M, x.stride(0), _p(y), y.stride(0),
             _stream_ptr(stream)))
+
+    def linear_planes_dev(self, rq, xhi, xlo, M: int, y, stream=None) -> None:
+        """Tensor-core GEMM from byte planes; rq=None stores int64 accumulators."""
+        _check("myl_linear_planes_dev", load_library().myl_linear_planes_dev(
+            self.ctx.handle, self._h, None if rq is None else rq.handle, _p(xhi), _p(xlo),
+            xhi.stride(0), M, _p(y), y.stride(0), _stream_ptr(stream)))
 
     def linear_acc_dev(self, x, acc, stream=None) -> None:
         """acc[M, N] int64 = exact W x (no requant)."""

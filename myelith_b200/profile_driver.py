@@ -1,0 +1,57 @@
+"""Runs one W8A16 linear shape repeatedly, for profiler captures (ncu).
+
+    python -m myelith_b200.profile_driver --M 1 --K 3584 --N 18944 --iters 6
+
+Uses the device path (myl_linear_dev) with rotating weight sets whose total
+size exceeds the 126 MB L2, so that DRAM counters reflect HBM traffic. Prints
+the average CUDA-event time per call (not a benchmark number when run under a
+profiler).
+"""
+from __future__ import annotations
+
+import argparse
+import math
+
+import numpy as np
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--M", type=int, default=1)
+    ap.add_argument("--K", type=int, default=3584)
+    ap.add_argument("--N", type=int, default=18944)
+    ap.add_argument("--iters", type=int, default=6)
+    ap.add_argument("--sets", type=int, default=0, help="weight sets (0: enough to exceed 2x L2)")
+    args = ap.parse_args()
+
+    import torch
+
+    import myelith_b200 as myl
+
+    M, K, N = args.M, args.K, args.N
+    ctx = myl.Context(0)
+    rng = np.random.default_rng(5)
+    sets = args.sets or max(2, math.ceil(2 * 126 * 2**20 / (N * K)))
+    sh = int(round(math.log2(73.6 * math.sqrt(K))))
+    ws = rng.integers(sh - 1, sh + 2, size=N).astype(np.uint8)
+    Ws = [ctx.weight(rng.integers(-127, 128, size=(N, K), dtype=np.int8), K, ws) for _ in range(sets)]
+    Rs = [w.requant(myl.RQ_SHIFT_I16, 8, 8) for w in Ws]
+    x = torch.from_numpy(np.clip(np.rint(rng.normal(0, 1024, size=(M, K))), -32767, 32767)
+                         .astype(np.int16)).cuda()
+    y = torch.empty((M, N), dtype=torch.int16, device="cuda")
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(s)
+        for i in range(args.iters):
+            Ws[i % sets].linear_dev(Rs[i % sets], x, y, s)
+        b.record(s)
+        s.synchronize()
+    ctx.synchronize()
+    print(f"M={M} K={K} N={N} sets={sets}: {a.elapsed_time(b) / args.iters * 1e3:.2f} us/call, "
+          f"{ctx.launch_count} launches")
+
+
+if __name__ == "__main__":
+    main()
