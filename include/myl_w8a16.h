@@ -165,6 +165,31 @@ int64_t myl_launch_count(const myl_ctx* ctx);
  * call reports MYL_ERR_DEVICE. The context stays usable. */
 int myl_debug_inject_wait_fault(myl_ctx* ctx, int on);
 
+/* --- Allocation-free variant ------------------------------------------------------
+ * No counterpart in the reference: its CPU path never allocates device memory.
+ *
+ * For callers that must not have a library allocate device memory: a runtime
+ * that reserves its device budget in its own arena at start-up, so that a long
+ * job cannot fail half-way on a late allocation, or a loop that cannot afford
+ * the device-wide synchronisation of cudaMalloc/cudaFree.
+ *
+ * myl_linear_noalloc_dev computes the same result as myl_linear_dev with the
+ * tensor-core kernel (for every M), but calls no cudaMalloc, cudaFree or other
+ * allocating routine: the activation byte planes live in a fixed array of
+ * MYL_NOALLOC_SCRATCH_BYTES inside the library's device image, which every
+ * GPU that loads the library holds until the process exits.
+ *  - Limits: 2 * M * round_up(in_features, 16) <= MYL_NOALLOC_SCRATCH_BYTES
+ *    and in_features <= 65536; larger calls fail with MYL_ERR_UNSUPPORTED.
+ *  - The first call on a device looks up the array's device address on that
+ *    device; make that first call before any stream capture.
+ *  - The array is shared by all calls on a device and keeps the last call's
+ *    contents; calls whose work overlaps on the GPU (different streams or
+ *    host threads) race on it and must be serialised by the caller. */
+#define MYL_NOALLOC_SCRATCH_BYTES (16 * 1024 * 1024)
+int myl_linear_noalloc_dev(myl_ctx* ctx, const myl_weight* w, const myl_requant* rq,
+                           const int16_t* x, int64_t M, int64_t ldx, void* y, int64_t ldy,
+                           void* stream);
+
 #ifdef __cplusplus
 }
 #endif

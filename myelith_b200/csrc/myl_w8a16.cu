@@ -737,3 +737,88 @@ int myl_debug_inject_wait_fault(myl_ctx* ctx, int on) {
 int64_t myl_launch_count(const myl_ctx* ctx) { return ctx ? ctx->launches : -1; }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------
+// Allocation-free tensor-core linear.
+//
+// Some callers cannot let a library allocate device memory: a runtime that
+// reserves its whole device budget in its own arena at start-up (so a long
+// inference or mining job cannot fail half-way on a late cudaMalloc), or a
+// loop that must not stall, since cudaMalloc/cudaFree synchronise the whole
+// device and would hold up every other stream. The regular entry points grow
+// a per-context workspace on demand; myl_linear_noalloc_dev instead keeps the
+// activation byte planes in the fixed array below, which is part of this
+// library's device image: every GPU that loads the library holds these
+// MYL_NOALLOC_SCRATCH_BYTES until the process exits.
+//
+// The array is one per device and shared by every call: calls whose work
+// overlaps on the GPU (other streams, other host threads) race on it. Nothing
+// in it needs to start at zero: the split pass writes every plane byte the
+// GEMM reads before the GEMM runs, on the same stream.
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[MYL_NOALLOC_SCRATCH_BYTES];
+
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_ptr[64] = {};
+
+// Host code cannot use g_noalloc_scratch as an address (it names a host-side
+// stand-in); the device address is looked up once per device, with that
+// device current.
+static int noalloc_scratch(int device, void** out) {
+  if (device < 0 || device >= 64) return fail(MYL_ERR_UNSUPPORTED, "device index %d", device);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[device]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(MYL_ERR_CUDA, "cudaGetSymbolAddress(g_noalloc_scratch) failed: %s",
+                  cudaGetErrorString(e));
+    g_noalloc_ptr[device] = p;
+  }
+  *out = g_noalloc_ptr[device];
+  return MYL_OK;
+}
+
+extern "C" int myl_linear_noalloc_dev(myl_ctx* ctx, const myl_weight* w, const myl_requant* rq,
+                                      const int16_t* x, int64_t M, int64_t ldx, void* y,
+                                      int64_t ldy, void* stream) {
+  if (!ctx || !w || !rq || (M > 0 && (!x || !y))) return fail(MYL_ERR_ARG, "null argument");
+  if (rq->N != w->N) return fail(MYL_ERR_SHAPE, "requant/weight channel mismatch");
+  if (M < 0 || ldx < w->K || ldy < w->N) return fail(MYL_ERR_SHAPE, "bad M/ldx/ldy");
+  if (w->K > 65536)
+    return fail(MYL_ERR_UNSUPPORTED,
+                "myl_linear_noalloc_dev: in_features %lld > 65536 would need K-slice partial sums",
+                (long long)w->K);
+  const size_t need = size_t(2) * size_t(M) * size_t(w->ldp);
+  if (need > size_t(MYL_NOALLOC_SCRATCH_BYTES))
+    return fail(MYL_ERR_UNSUPPORTED,
+                "myl_linear_noalloc_dev: 2 * M * round_up(K, 16) = %zu bytes exceeds the fixed "
+                "scratch of %d bytes; use fewer rows per call",
+                need, MYL_NOALLOC_SCRATCH_BYTES);
+  if (M == 0 || w->N == 0) return MYL_OK;
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  void* scratch = nullptr;
+  TRY(noalloc_scratch(ctx->device, &scratch));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int8_t* xhi = static_cast<int8_t*>(scratch);
+  uint8_t* xlo = reinterpret_cast<uint8_t*>(xhi + M * w->ldp);
+  TRY(launch_split(ctx, x, M, w->K, ldx, xhi, xlo, w->ldp, st));
+  // Same tile choice as the regular path, but always one K slice: no int64
+  // partial buffer is needed.
+  const bool swap = (ctx->force_swap >= 0) ? (ctx->force_swap != 0) : (M <= 256);
+  int BN = 256;
+  if (swap) {
+    BN = 32;
+    while (BN < M && BN < 256) BN *= 2;
+  }
+  CUtensorMap tm_xhi, tm_xlo;
+  TRY(encode_map(ctx, &tm_xhi, xhi, w->K, M, w->ldp, swap ? BN : 128));
+  TRY(encode_map(ctx, &tm_xlo, xlo, w->K, M, w->ldp, swap ? BN : 128));
+  const int k_tiles = int((w->K + TC_BK - 1) / TC_BK);
+  const Epilogue ep = make_ep(rq, y, ldy);
+  if (!swap) return launch_tc_variant<256, false, 3>(ctx, w, tm_xhi, tm_xlo, M, 1, k_tiles, k_tiles, ep, 0, st);
+  if (BN == 32) return launch_tc_variant<32, true, 8>(ctx, w, tm_xhi, tm_xlo, M, 1, k_tiles, k_tiles, ep, 0, st);
+  if (BN == 64) return launch_tc_variant<64, true, 6>(ctx, w, tm_xhi, tm_xlo, M, 1, k_tiles, k_tiles, ep, 0, st);
+  if (BN == 128) return launch_tc_variant<128, true, 4>(ctx, w, tm_xhi, tm_xlo, M, 1, k_tiles, k_tiles, ep, 0, st);
+  return launch_tc_variant<256, true, 2>(ctx, w, tm_xhi, tm_xlo, M, 1, k_tiles, k_tiles, ep, 0, st);
+}
