@@ -151,9 +151,10 @@ int myl_synchronize(myl_ctx* ctx);
 /* Bound of every device-side wait, in nanoseconds (default 2e9). */
 int myl_set_wait_timeout_ns(myl_ctx* ctx, uint64_t ns);
 
-/* Kernel selection thresholds, for tests and tuning: M <= gemv_max_m runs the
- * CUDA-core GEMV, larger M the tcgen05 GEMM; split_k = 0 picks automatically. */
-int myl_set_dispatch(myl_ctx* ctx, int gemv_max_m, int force_split_k, int force_swap);
+/* Kernel selection, for tests and tuning: M <= gemv_max_m (at most 4) runs the
+ * CUDA-core GEMV, larger M the tcgen05 GEMM; force_split_k = 0 and
+ * force_token_tile = 0 choose automatically (token tile 32, 64 or 128). */
+int myl_set_dispatch(myl_ctx* ctx, int gemv_max_m, int force_split_k, int force_token_tile);
 
 /* Number of this library's kernels launched on the context since init. */
 int64_t myl_launch_count(const myl_ctx* ctx);

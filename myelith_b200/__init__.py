@@ -160,9 +160,9 @@ class Context:
     def set_wait_timeout_ns(self, ns: int) -> None:
         _check("myl_set_wait_timeout_ns", load_library().myl_set_wait_timeout_ns(self._h, ns))
 
-    def set_dispatch(self, gemv_max_m: int = 4, force_split_k: int = 0, force_swap: int = -1) -> None:
+    def set_dispatch(self, gemv_max_m: int = 4, force_split_k: int = 0, force_token_tile: int = 0) -> None:
         _check("myl_set_dispatch",
-               load_library().myl_set_dispatch(self._h, gemv_max_m, force_split_k, force_swap))
+               load_library().myl_set_dispatch(self._h, gemv_max_m, force_split_k, force_token_tile))
 
     def inject_wait_fault(self, on: bool) -> None:
         _check("myl_debug_inject_wait_fault",

@@ -9,22 +9,27 @@
 // hi = x >> 8 (signed byte) and lo = x & 255 (unsigned byte), so
 //   sum_k w*x = 256 * sum_k w*hi + sum_k w*lo.
 // Two kind::i8 MMAs (s8 x s8 and s8 x u8) accumulate the two sums in two int32
-// TMEM accumulators. |w*hi| <= 128*128 = 2^14 and |w*lo| <= 128*255 < 2^15, so
-// both int32 sums are exact for K <= 65536 (the host enforces K <= 65536 per
-// launch; longer K is split into slices whose exact int64 partials are added).
-// The epilogue forms 256*S_hi + S_lo in int64, which is the reference's exact
-// i64 accumulator, and applies the requant once (fixed_point.rs:184-191).
-// The tensor pipe therefore does 2x the algorithmic MACs.
+// TMEM accumulators H and L. |w*hi| <= 2^14 and |w*lo| < 2^15, so both int32
+// sums are exact for K <= 65536 (the host splits longer K into slices whose
+// exact int64 partials are added). The epilogue's value 256*H + L is the
+// reference's exact i64 accumulator; the requant is applied to it once
+// (fixed_point.rs:184-191). The tensor pipe does 2x the algorithmic MACs.
 //
-// Schedule (one output tile per CTA, 192 threads):
-//   warp 0        TMA producer: W tile + X_hi tile + X_lo tile per 128-byte K
-//                 step into a STAGES-deep ring of 128B-swizzled smem stages.
-//   warp 1        TMEM allocator; lane 0 issues the MMAs (4 K-steps of 32 x 2).
-//   warps 2..5    epilogue: tcgen05.ld of both accumulators, combine, requant,
-//                 store. Warp w reads TMEM lanes 32*(w%4)..32*(w%4)+31.
-// SWAP=false: MMA A = X (128 tokens), B = W (BN channels); lanes = tokens.
-// SWAP=true : MMA A = W (128 channels), B = X (BN tokens); lanes = channels
-//             (small-M decode / prefill chunks: the weight fills the MMA M).
+// Tiles. The weight is the MMA's A operand (M = 128 output channels, TMEM lane
+// = channel) and the activations are B (BN tokens, BN in {32, 64, 128}), so
+// each epilogue thread owns one channel and keeps its requant parameters in
+// registers, and a warp's stores for one token are 64 contiguous bytes.
+//
+// Schedule: persistent, one CTA per SM looping over work units
+// (channel tile, token tile, K slice), 320 threads:
+//   warp 0      TMA producer: W tile + x_hi tile + x_lo tile per 128-byte K
+//               step into a STAGES-deep ring of 128B-swizzled smem stages.
+//   warp 1      TMEM allocator; lane 0 issues 2 x 4 MMAs per K step and
+//               commits each smem stage back to the producer.
+//   warps 2..9  epilogue: tcgen05.ld of H and L, requant, store. Warp w reads
+//               TMEM lanes 32*(w%4)..32*(w%4)+31 and half of the BN columns.
+// Two accumulator buffers (2 x (H, L) x BN columns) let the epilogue of one
+// unit run while the MMAs of the next unit accumulate into the other buffer.
 //
 // Every mbarrier wait is bounded (timeout_ns, globaltimer); a wait that runs
 // out writes an error code to *err, the CTA drains its own TMA copies and
@@ -36,34 +41,48 @@
 namespace myl {
 
 constexpr int TC_BK = 128;  // K bytes per stage = one 128-byte swizzle row
-constexpr int TC_THREADS = 192;
+constexpr int TC_EPI_WARPS = 8;  // two per TMEM lane quarter, each owning half the columns
+constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;
 
-template <int BN, bool SWAP, int STAGES>
+template <int BN, int STAGES>
 struct TcCfg {
-  static constexpr int ROWS_W = SWAP ? 128 : BN;
-  static constexpr int ROWS_X = SWAP ? BN : 128;
-  static constexpr int W_BYTES = ROWS_W * TC_BK;
-  static constexpr int X_BYTES = ROWS_X * TC_BK;
+  static constexpr int W_BYTES = 128 * TC_BK;
+  static constexpr int X_BYTES = BN * TC_BK;
   static constexpr int STAGE_BYTES = W_BYTES + 2 * X_BYTES;
-  static constexpr int ACC_COLS = 2 * BN;  // hi accumulator | lo accumulator
-  static constexpr int TMEM_COLS = ACC_COLS <= 32 ? 32 : ACC_COLS <= 64 ? 64 : ACC_COLS <= 128 ? 128
-                                   : ACC_COLS <= 256 ? 256 : 512;
+  static constexpr int BUF_COLS = 2 * BN;  // H | L of one accumulator buffer
+  static constexpr int TMEM_COLS = 2 * BUF_COLS <= 32 ? 32 : 2 * BUF_COLS;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack
-  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256,
-                "MMA N (M=128) is a multiple of 16 in [16,256]; the epilogue reads 32 columns at a time");
-  static_assert(ACC_COLS <= 512, "TMEM has 512 columns");
-  // A: SWAP ? W (s8) : X_hi/X_lo; B: SWAP ? X_hi/X_lo : W (s8).
-  static constexpr uint32_t IDESC_HI = idesc_i8(128, BN, true, true);
-  static constexpr uint32_t IDESC_LO = SWAP ? idesc_i8(128, BN, true, false) : idesc_i8(128, BN, false, true);
+  static_assert(BN == 32 || BN == 64 || BN == 128, "token tile");
+  static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM allocation");
+  static_assert(STAGES >= 2 && STAGES <= 16, "stage ring");
+  static_assert(SMEM_BYTES <= 227 * 1024 - 512, "shared memory");
+  static constexpr uint32_t IDESC_HI = idesc_i8(128, BN, true, true);   // W s8 x x_hi s8
+  static constexpr uint32_t IDESC_LO = idesc_i8(128, BN, true, false);  // W s8 x x_lo u8
 };
 
-struct TcSmemCtl {
+struct TcCtl {
   uint64_t full[16];
   uint64_t empty[16];
-  uint64_t accum_full;
-  uint64_t never;  // test hook: nothing ever arrives here
+  uint64_t tfull[2];   // accumulator buffer b holds a finished unit
+  uint64_t tempty[2];  // accumulator buffer b has been read by the epilogue
+  uint64_t never;      // test hook: nothing ever arrives here
   uint32_t tmem_base;
   int abort;
+};
+
+struct TcWork {
+  int tiles_n, tiles_m, ksplit, k_tiles_total, k_tiles_per_split;
+  __device__ __forceinline__ int units() const { return tiles_n * tiles_m * ksplit; }
+  // Unit u -> (channel tile, token tile, K slice). Channel tiles vary fastest:
+  // the CTAs of one wave share a token tile and sweep the weight.
+  __device__ __forceinline__ void decode(int u, int& nt, int& mt, int& ks, int& kt0, int& nkt) const {
+    nt = u % tiles_n;
+    const int r = u / tiles_n;
+    mt = r % tiles_m;
+    ks = r / tiles_m;
+    kt0 = ks * k_tiles_per_split;
+    nkt = min(k_tiles_per_split, k_tiles_total - kt0);
+  }
 };
 
 __device__ __forceinline__ void tc_fail(int* err, volatile int* abort, int code) {
@@ -71,37 +90,95 @@ __device__ __forceinline__ void tc_fail(int* err, volatile int* abort, int code)
   atomicCAS(err, 0, code);
 }
 
-template <int BN, bool SWAP, int STAGES>
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// Requant of the exact accumulator V = 256*H + L by a right shift s = 8 + t,
+// t in [0, 30], in 32-bit arithmetic. With h = H + (L >> 8) and l = L & 255,
+// V = 256*h + l and 0 <= l < 256, so V >> s = h >> t. Round-to-nearest-even
+// (fixed_point.rs:57-71) is (V + 2^(s-1) - 1 + odd) >> s with odd = (V >> s) & 1;
+// the bias splits as 256*bh + bl with bh = 2^(t-1) - 1, bl = 255 (t >= 1) or
+// bh = 0, bl = 127 (t = 0), giving (h + bh + ((l + bl + odd) >> 8)) >> t.
+// |h| < 2^30 + 2^23 (K <= 65536), so no step leaves int32.
+struct Requant32 {
+  int t, bh, bl, lo_b, hi_b;
+  __device__ __forceinline__ void init(int s, bool out_i32) {
+    t = s - 8;
+    bh = t > 0 ? (1 << (t - 1)) - 1 : 0;
+    bl = t > 0 ? 255 : 127;
+    lo_b = out_i32 ? INT32_MIN : -32768;
+    hi_b = out_i32 ? INT32_MAX : 32767;
+  }
+  __device__ __forceinline__ int apply(int32_t H, int32_t L) const {
+    const int32_t h = H + (L >> 8);
+    const int32_t l = L & 255;
+    const int32_t odd = (h >> t) & 1;
+    const int32_t v = (h + bh + ((l + bl + odd) >> 8)) >> t;
+    return v < lo_b ? lo_b : (v > hi_b ? hi_b : v);
+  }
+};
+
+// Loads NC (16 or 32) columns of the H and L accumulators of this thread's lane.
+template <int NC>
+__device__ __forceinline__ void tmem_ld_pair(uint32_t taddr_h, uint32_t taddr_l, uint32_t (&h)[NC],
+                                             uint32_t (&l)[NC]) {
+  if constexpr (NC == 32) {
+    tmem_ld_32x32b_x32(taddr_h, h);
+    tmem_ld_32x32b_x32(taddr_l, l);
+  } else {
+    tmem_ld_32x32b_x16(taddr_h, h);
+    tmem_ld_32x32b_x16(taddr_l, l);
+  }
+  tmem_ld_wait();
+}
+
+// Writes NC consecutive tokens (rows m0.. of y) of channel n.
+template <int NC, typename T, typename F>
+__device__ __forceinline__ void store_column(T* yp, int64_t ldy, int64_t m0, int64_t M, F&& value) {
+  if (m0 + NC <= M) {
+#pragma unroll
+    for (int j = 0; j < NC; ++j) {
+      *yp = value(j);
+      yp += ldy;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < NC; ++j) {
+      if (m0 + j < M) *yp = value(j);
+      yp += ldy;
+    }
+  }
+}
+
+template <int BN, int STAGES>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_w8a16_tc_kernel(const __grid_constant__ CUtensorMap tm_w,
                          const __grid_constant__ CUtensorMap tm_xhi,
                          const __grid_constant__ CUtensorMap tm_xlo, int64_t M, int64_t N,
-                         int k_tiles_total, int k_tiles_per_split, Epilogue ep,
-                         int64_t slice_stride, int* err, uint64_t timeout_ns, int inject_fault) {
-  using Cfg = TcCfg<BN, SWAP, STAGES>;
-  static_assert(STAGES <= 16, "barrier array size");
+                         TcWork work, Epilogue ep, int64_t slice_stride, int* err,
+                         uint64_t timeout_ns, int inject_fault) {
+  using Cfg = TcCfg<BN, STAGES>;
   extern __shared__ uint8_t dyn_smem[];
-  __shared__ TcSmemCtl ctl;
+  __shared__ TcCtl ctl;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t smem_base = (smem_addr(dyn_smem) + 1023u) & ~1023u;
   auto sm_w = [&](int s) { return smem_base + uint32_t(s) * Cfg::STAGE_BYTES; };
   auto sm_xh = [&](int s) { return sm_w(s) + Cfg::W_BYTES; };
   auto sm_xl = [&](int s) { return sm_w(s) + Cfg::W_BYTES + Cfg::X_BYTES; };
-
-  const int64_t n0 = SWAP ? int64_t(blockIdx.x) * 128 : int64_t(blockIdx.x) * BN;
-  const int64_t m0 = SWAP ? int64_t(blockIdx.y) * BN : int64_t(blockIdx.y) * 128;
-  const int kt0 = int(blockIdx.z) * k_tiles_per_split;
-  const int kt1 = min(kt0 + k_tiles_per_split, k_tiles_total);
-  const int nkt = kt1 - kt0;  // >= 1, guaranteed by the host
   volatile int* abort = &ctl.abort;
+  const int units = work.units();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(smem_addr(&ctl.full[s]), 1);
       mbar_init(smem_addr(&ctl.empty[s]), 1);
     }
-    mbar_init(smem_addr(&ctl.accum_full), 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_addr(&ctl.tfull[b]), 1);
+      mbar_init(smem_addr(&ctl.tempty[b]), TC_EPI_WARPS);
+    }
     mbar_init(smem_addr(&ctl.never), 1);
     ctl.abort = 0;
     fence_barrier_init();
@@ -121,26 +198,31 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      int issued = 0;
-      for (int i = 0; i < nkt; ++i) {
-        const int s = i % STAGES;
-        const uint32_t ph = uint32_t(i / STAGES) & 1u;
-        if (!mbar_wait_bounded(smem_addr(&ctl.empty[s]), ph ^ 1u, timeout_ns, abort)) {
-          tc_fail(err, abort, DEV_WAIT_PRODUCER);
-          break;
+      int g = 0;  // K steps issued by this CTA (ring position)
+      bool stop = false;
+      for (int u = blockIdx.x; u < units && !stop; u += gridDim.x) {
+        int nt, mt, ks, kt0, nkt;
+        work.decode(u, nt, mt, ks, kt0, nkt);
+        for (int i = 0; i < nkt; ++i, ++g) {
+          const int s = g % STAGES;
+          const uint32_t ph = uint32_t(g / STAGES) & 1u;
+          if (!mbar_wait_bounded(smem_addr(&ctl.empty[s]), ph ^ 1u, timeout_ns, abort)) {
+            tc_fail(err, abort, DEV_WAIT_PRODUCER);
+            stop = true;
+            break;
+          }
+          const uint32_t fb = smem_addr(&ctl.full[s]);
+          mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
+          const int32_t kx = (kt0 + i) * TC_BK;
+          tma_load_2d(sm_w(s), &tm_w, fb, kx, nt * 128);
+          tma_load_2d(sm_xh(s), &tm_xhi, fb, kx, mt * BN);
+          tma_load_2d(sm_xl(s), &tm_xlo, fb, kx, mt * BN);
         }
-        const uint32_t fb = smem_addr(&ctl.full[s]);
-        mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
-        const int32_t kx = (kt0 + i) * TC_BK;
-        tma_load_2d(sm_w(s), &tm_w, fb, kx, int32_t(n0));
-        tma_load_2d(sm_xh(s), &tm_xhi, fb, kx, int32_t(m0));
-        tma_load_2d(sm_xl(s), &tm_xlo, fb, kx, int32_t(m0));
-        issued = i + 1;
       }
       if (*abort) {
         // Drain: the last load issued into each stage must land before exit.
-        for (int s = 0; s < STAGES && s < issued; ++s) {
-          const int last = s + ((issued - 1 - s) / STAGES) * STAGES;
+        for (int s = 0; s < STAGES && s < g; ++s) {
+          const int last = s + ((g - 1 - s) / STAGES) * STAGES;
           if (!mbar_wait_bounded(smem_addr(&ctl.full[s]), uint32_t(last / STAGES) & 1u, timeout_ns,
                                  nullptr))
             atomicCAS(err, 0, DEV_WAIT_DRAIN);
@@ -150,137 +232,132 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t d_hi = tmem, d_lo = tmem + BN;
-      for (int i = 0; i < nkt; ++i) {
-        const int s = i % STAGES;
-        const uint32_t ph = uint32_t(i / STAGES) & 1u;
-        if (!mbar_wait_bounded(smem_addr(&ctl.full[s]), ph, timeout_ns, abort)) {
+      int g = 0, lt = 0;
+      bool stop = false;
+      for (int u = blockIdx.x; u < units && !stop; u += gridDim.x, ++lt) {
+        int nt, mt, ks, kt0, nkt;
+        work.decode(u, nt, mt, ks, kt0, nkt);
+        const int b = lt & 1;
+        const uint32_t tph = uint32_t(lt >> 1) & 1u;
+        if (!mbar_wait_bounded(smem_addr(&ctl.tempty[b]), tph ^ 1u, timeout_ns, abort)) {
           tc_fail(err, abort, DEV_WAIT_MMA);
           break;
         }
         tc_fence_after();
-        const uint32_t aw = sm_w(s), axh = sm_xh(s), axl = sm_xl(s);
-#pragma unroll
-        for (int kk = 0; kk < TC_BK / 32; ++kk) {
-          const uint32_t off = uint32_t(kk) * 32u;
-          const uint64_t dw = smem_desc_k_sw128(aw + off);
-          const uint64_t dxh = smem_desc_k_sw128(axh + off);
-          const uint64_t dxl = smem_desc_k_sw128(axl + off);
-          const uint32_t accum = (i > 0 || kk > 0) ? 1u : 0u;
-          if (SWAP) {
-            mma_i8(d_hi, dw, dxh, Cfg::IDESC_HI, accum);
-            mma_i8(d_lo, dw, dxl, Cfg::IDESC_LO, accum);
-          } else {
-            mma_i8(d_hi, dxh, dw, Cfg::IDESC_HI, accum);
-            mma_i8(d_lo, dxl, dw, Cfg::IDESC_LO, accum);
+        const uint32_t d_hi = tmem + uint32_t(b * Cfg::BUF_COLS), d_lo = d_hi + BN;
+        for (int i = 0; i < nkt; ++i, ++g) {
+          const int s = g % STAGES;
+          const uint32_t ph = uint32_t(g / STAGES) & 1u;
+          if (!mbar_wait_bounded(smem_addr(&ctl.full[s]), ph, timeout_ns, abort)) {
+            tc_fail(err, abort, DEV_WAIT_MMA);
+            stop = true;
+            break;
           }
+          tc_fence_after();
+          const uint32_t aw = sm_w(s), axh = sm_xh(s), axl = sm_xl(s);
+#pragma unroll
+          for (int kk = 0; kk < TC_BK / 32; ++kk) {
+            const uint32_t off = uint32_t(kk) * 32u;
+            const uint64_t dw = smem_desc_k_sw128(aw + off);
+            const uint32_t accum = (i > 0 || kk > 0) ? 1u : 0u;
+            mma_i8(d_hi, dw, smem_desc_k_sw128(axh + off), Cfg::IDESC_HI, accum);
+            mma_i8(d_lo, dw, smem_desc_k_sw128(axl + off), Cfg::IDESC_LO, accum);
+          }
+          mma_commit(smem_addr(&ctl.empty[s]));  // frees the stage when these MMAs finish
         }
-        mma_commit(smem_addr(&ctl.empty[s]));  // frees the stage when these MMAs finish
+        mma_commit(smem_addr(&ctl.tfull[b]));  // also signals on abort: the epilogue checks
       }
-      mma_commit(smem_addr(&ctl.accum_full));
-      // The issuer itself sees every MMA finish before TMEM can be released.
-      if (!mbar_wait_bounded(smem_addr(&ctl.accum_full), 0u, timeout_ns, nullptr))
-        atomicCAS(err, 0, DEV_WAIT_DRAIN);
+      // The issuer itself sees its last MMAs finish before TMEM can be released.
+      if (lt > 0) {
+        const int b = (lt - 1) & 1;
+        if (!mbar_wait_bounded(smem_addr(&ctl.tfull[b]), uint32_t((lt - 1) >> 1) & 1u, timeout_ns,
+                               nullptr))
+          atomicCAS(err, 0, DEV_WAIT_DRAIN);
+      }
     }
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
+    // ---------------- epilogue (warps 2..9) ----------------
+    constexpr int HALF = BN / 2;                 // columns per epilogue warp
+    constexpr int NC = HALF < 32 ? HALF : 32;    // columns per TMEM load
     const int q = warp & 3;
-    bool ok = mbar_wait_bounded(smem_addr(&ctl.accum_full), 0u, timeout_ns, abort);
-    int code = DEV_WAIT_EPILOGUE;
-    if (ok && inject_fault) {
-      ok = mbar_wait_bounded(smem_addr(&ctl.never), 0u, timeout_ns, nullptr);
-      code = DEV_WAIT_INJECTED;
-    }
-    if (!ok) {
-      tc_fail(err, abort, code);
-    } else if (!*abort) {
+    const int col0 = ((warp - 2) >> 2) * HALF;
+    const int row = q * 32 + lane;
+    int lt = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++lt) {
+      int nt, mt, ks, kt0, nkt;
+      work.decode(u, nt, mt, ks, kt0, nkt);
+      const int b = lt & 1;
+      const uint32_t tph = uint32_t(lt >> 1) & 1u;
+      bool ok = mbar_wait_bounded(smem_addr(&ctl.tfull[b]), tph, timeout_ns, abort);
+      int code = DEV_WAIT_EPILOGUE;
+      if (ok && inject_fault) {
+        ok = mbar_wait_bounded(smem_addr(&ctl.never), 0u, timeout_ns, nullptr);
+        code = DEV_WAIT_INJECTED;
+      }
+      if (!ok) {
+        tc_fail(err, abort, code);
+        break;
+      }
+      if (*abort) break;
       tc_fence_after();
-      const int row = q * 32 + lane;
-      const uint32_t tq = tmem + (uint32_t(q * 32) << 16);
+      const int64_t n = int64_t(nt) * 128 + row;
+      const int64_t m0 = int64_t(mt) * BN + col0;
+      const uint32_t tq = tmem + (uint32_t(q * 32) << 16) + uint32_t(b * Cfg::BUF_COLS + col0);
       Epilogue e = ep;
-      if (e.mode == EPI_ACC_I64)
-        e.y = static_cast<int64_t*>(e.y) + int64_t(blockIdx.z) * slice_stride;
+      if (e.mode == EPI_ACC_I64) e.y = static_cast<int64_t*>(e.y) + int64_t(ks) * slice_stride;
+      // Channel parameters, once per unit.
+      int shift = 0;
+      const int mode = e.mode;
+      if (n < N && mode != EPI_ACC_I64) shift = e.shift[n];
+      const bool fast = (mode == EPI_SHIFT) && shift >= 8 && shift <= 38;
+      Requant32 r32;
+      r32.init(fast ? shift : 8, e.out_i32 != 0);
       ChannelRequant rq;
-      if (SWAP && n0 + row < N) rq.load(e, n0 + row);
-      const bool vec16 = !SWAP && e.mode != EPI_ACC_I64 && !e.out_i32 &&
-                         ((reinterpret_cast<uintptr_t>(e.y) & 15) == 0) && (e.ldy % 8 == 0);
+      if (n < N && !fast && mode != EPI_ACC_I64) rq.load(e, n);
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t hi[32], lo[32];
-        tmem_ld_32x32b_x32(tq + c, hi);
-        tmem_ld_32x32b_x32(tq + BN + c, lo);
-        tmem_ld_wait();
-        if (SWAP) {
-          const int64_t n = n0 + row;
-          if (n < N) {
-            // One unrolled loop per mode keeps the live ranges short.
-            if (e.mode == EPI_ACC_I64) {
-              int64_t* yp = static_cast<int64_t*>(e.y) + n;
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (m0 + c + j < M)
-                  yp[(m0 + c + j) * e.ldy] = int64_t(int32_t(hi[j])) * 256 + int64_t(int32_t(lo[j]));
-            } else if (e.mode == EPI_SHIFT) {
-              const int64_t lo_b = e.out_i32 ? int64_t(INT32_MIN) : -32768;
-              const int64_t hi_b = e.out_i32 ? int64_t(INT32_MAX) : 32767;
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const int64_t m = m0 + c + j;
-                if (m < M) {
-                  const int64_t a = int64_t(int32_t(hi[j])) * 256 + int64_t(int32_t(lo[j]));
-                  const int64_t v = clamp_i64(rescale_i64_signed(a, rq.shift), lo_b, hi_b);
-                  if (e.out_i32) static_cast<int32_t*>(e.y)[m * e.ldy + n] = int32_t(v);
-                  else static_cast<int16_t*>(e.y)[m * e.ldy + n] = int16_t(v);
-                }
-              }
-            } else {
-#pragma unroll 1
-              for (int j = 0; j < 32; j += 8) {
-                int64_t a[8];
-#pragma unroll
-                for (int t = 0; t < 8; ++t) a[t] = 0;
-#pragma unroll
-                for (int jj = 0; jj < 32; ++jj)
-                  if (jj >= j && jj < j + 8)
-                    a[jj - j] = int64_t(int32_t(hi[jj])) * 256 + int64_t(int32_t(lo[jj]));
-#pragma unroll
-                for (int t = 0; t < 8; ++t) {
-                  const int64_t m = m0 + c + j + t;
-                  if (m < M) static_cast<int16_t*>(e.y)[m * e.ldy + n] = int16_t(rq.apply(a[t]));
-                }
-              }
-            }
+      for (int c = 0; c < HALF; c += NC) {
+        uint32_t hi[NC], lo[NC];
+        tmem_ld_pair<NC>(tq + c, tq + BN + c, hi, lo);
+        if (n >= N) continue;
+        const int64_t mc = m0 + c;
+        if (mode == EPI_ACC_I64) {
+          store_column<NC>(static_cast<int64_t*>(e.y) + mc * e.ldy + n, e.ldy, mc, M, [&](int j) {
+            return int64_t(int32_t(hi[j])) * 256 + int64_t(int32_t(lo[j]));
+          });
+        } else if (fast) {
+          if (e.out_i32) {
+            store_column<NC>(static_cast<int32_t*>(e.y) + mc * e.ldy + n, e.ldy, mc, M,
+                             [&](int j) { return int32_t(r32.apply(int32_t(hi[j]), int32_t(lo[j]))); });
+          } else {
+            store_column<NC>(static_cast<int16_t*>(e.y) + mc * e.ldy + n, e.ldy, mc, M,
+                             [&](int j) { return int16_t(r32.apply(int32_t(hi[j]), int32_t(lo[j]))); });
           }
         } else {
-          const int64_t m = m0 + row;
-          const int64_t nb = n0 + c;
-          int64_t acc[32];
+#pragma unroll 1
+          for (int j0 = 0; j0 < NC; j0 += 8) {
+            int64_t a[8];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) acc[j] = int64_t(int32_t(hi[j])) * 256 + int64_t(int32_t(lo[j]));
-          if (m < M) {
-            if (vec16 && nb + 32 <= N) {
-              uint32_t pk[16];
+            for (int t = 0; t < 8; ++t) a[t] = 0;
 #pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                ChannelRequant r0, r1;
-                r0.load(e, nb + 2 * j);
-                r1.load(e, nb + 2 * j + 1);
-                const uint32_t a = uint16_t(int16_t(r0.apply(acc[2 * j])));
-                const uint32_t b = uint16_t(int16_t(r1.apply(acc[2 * j + 1])));
-                pk[j] = a | (b << 16);
+            for (int jj = 0; jj < NC; ++jj)
+              if (jj >= j0 && jj < j0 + 8)
+                a[jj - j0] = int64_t(int32_t(hi[jj])) * 256 + int64_t(int32_t(lo[jj]));
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+              const int64_t m = mc + j0 + t;
+              if (m < M) {
+                const int64_t v = rq.apply(a[t]);
+                if (e.out_i32) static_cast<int32_t*>(e.y)[m * e.ldy + n] = int32_t(v);
+                else static_cast<int16_t*>(e.y)[m * e.ldy + n] = int16_t(v);
               }
-              int4* dst = reinterpret_cast<int4*>(static_cast<int16_t*>(e.y) + m * e.ldy + nb);
-#pragma unroll
-              for (int v = 0; v < 4; ++v)
-                dst[v] = make_int4(int(pk[4 * v]), int(pk[4 * v + 1]), int(pk[4 * v + 2]), int(pk[4 * v + 3]));
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (nb + j < N) epilogue_store(e, m, nb + j, acc[j]);
             }
           }
         }
       }
+      // Hand the buffer back to the MMA issuer.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&ctl.tempty[b]));
     }
     tc_fence_before();
   }

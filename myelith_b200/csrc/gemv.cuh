@@ -8,7 +8,8 @@
 //
 // Layout and schedule
 //  - W is the registered device copy: [N][ldw] int8, ldw a multiple of 16,
-//    zero-padded beyond K. Each warp owns R output rows; lane l streams the
+//    zero-padded beyond K. Each warp takes R output rows at a time (grid-stride
+//    over rows, grid sized to the resident blocks); lane l streams the
 //    16-byte chunks l, l+32, ... of each row with 128-bit non-coherent loads
 //    that bypass L1 (a row's 32 lanes read 512 contiguous bytes).
 //  - The activation slice x[:, k0:k0+KS] is staged once per block in shared
@@ -86,73 +87,76 @@ __global__ void __launch_bounds__(GEMV_THREADS)
   __syncthreads();
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t row0 = (int64_t(blockIdx.x) * GEMV_WARPS + warp) * R;
-  if (row0 >= N) return;
-
-  int64_t acc[R][MT];
-#pragma unroll
-  for (int j = 0; j < R; ++j)
-#pragma unroll
-    for (int m = 0; m < MT; ++m) acc[j][m] = 0;
-
-  const int8_t* wrow[R];
-#pragma unroll
-  for (int j = 0; j < R; ++j) {
-    const int64_t r = (row0 + j < N) ? row0 + j : N - 1;  // clamp: duplicate rows are not stored
-    wrow[j] = W + r * ldw + k0;
-  }
-
-  for (int c = lane; c < nchunk; c += 32 * U) {
-    int4 wv[U][R];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int cc = c + 32 * u;
-#pragma unroll
-      for (int j = 0; j < R; ++j)
-        wv[u][j] = (cc < nchunk) ? ldg_stream_v4(wrow[j] + cc * 16) : make_int4(0, 0, 0, 0);
-    }
-    int a32[R][MT];
-#pragma unroll
-    for (int j = 0; j < R; ++j)
-#pragma unroll
-      for (int m = 0; m < MT; ++m) a32[j][m] = 0;
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int cc = c + 32 * u;
-      if (cc < nchunk) {
-#pragma unroll
-        for (int m = 0; m < MT; ++m) {
-          const int4* xp = reinterpret_cast<const int4*>(xs + m * KS + cc * 16);
-          const int4 xa = xp[0], xb = xp[1];
-#pragma unroll
-          for (int j = 0; j < R; ++j) a32[j][m] = dot16_dp2a(wv[u][j], xa, xb, a32[j][m]);
-        }
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < R; ++j)
-#pragma unroll
-      for (int m = 0; m < MT; ++m) acc[j][m] += a32[j][m];
-  }
-
-  // ---- warp reduction (exact, any order) and epilogue --------------------------
-#pragma unroll
-  for (int j = 0; j < R; ++j)
-#pragma unroll
-    for (int m = 0; m < MT; ++m) {
-      int64_t v = acc[j][m];
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-      acc[j][m] = v;
-    }
   Epilogue e = ep;
   if (e.mode == EPI_ACC_I64)
     e.y = static_cast<int64_t*>(e.y) + int64_t(blockIdx.y) * slice_stride;
+  const int64_t row_step = int64_t(gridDim.x) * GEMV_WARPS * R;
+
+  // Grid-stride loop over row groups: the grid is sized to the resident
+  // blocks, so x is staged once per block and the warps keep streaming.
+  for (int64_t row0 = (int64_t(blockIdx.x) * GEMV_WARPS + warp) * R; row0 < N; row0 += row_step) {
+    int64_t acc[R][MT];
 #pragma unroll
-  for (int j = 0; j < R; ++j)
+    for (int j = 0; j < R; ++j)
 #pragma unroll
-    for (int m = 0; m < MT; ++m)
-      if (lane == ((j * MT + m) & 31) && row0 + j < N) epilogue_store(e, m, row0 + j, acc[j][m]);
+      for (int m = 0; m < MT; ++m) acc[j][m] = 0;
+
+    const int8_t* wrow[R];
+#pragma unroll
+    for (int j = 0; j < R; ++j) {
+      const int64_t r = (row0 + j < N) ? row0 + j : N - 1;  // clamp: duplicate rows are not stored
+      wrow[j] = W + r * ldw + k0;
+    }
+
+    for (int c = lane; c < nchunk; c += 32 * U) {
+      int4 wv[U][R];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int cc = c + 32 * u;
+#pragma unroll
+        for (int j = 0; j < R; ++j)
+          wv[u][j] = (cc < nchunk) ? ldg_stream_v4(wrow[j] + cc * 16) : make_int4(0, 0, 0, 0);
+      }
+      int a32[R][MT];
+#pragma unroll
+      for (int j = 0; j < R; ++j)
+#pragma unroll
+        for (int m = 0; m < MT; ++m) a32[j][m] = 0;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int cc = c + 32 * u;
+        if (cc < nchunk) {
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            const int4* xp = reinterpret_cast<const int4*>(xs + m * KS + cc * 16);
+            const int4 xa = xp[0], xb = xp[1];
+#pragma unroll
+            for (int j = 0; j < R; ++j) a32[j][m] = dot16_dp2a(wv[u][j], xa, xb, a32[j][m]);
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < R; ++j)
+#pragma unroll
+        for (int m = 0; m < MT; ++m) acc[j][m] += a32[j][m];
+    }
+
+    // ---- warp reduction (exact, any order) and epilogue ------------------------
+#pragma unroll
+    for (int j = 0; j < R; ++j)
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        int64_t v = acc[j][m];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        acc[j][m] = v;
+      }
+#pragma unroll
+    for (int j = 0; j < R; ++j)
+#pragma unroll
+      for (int m = 0; m < MT; ++m)
+        if (lane == ((j * MT + m) & 31) && row0 + j < N) epilogue_store(e, m, row0 + j, acc[j][m]);
+  }
 }
 
 // Sums nsplit exact int64 partial slices [nsplit][M][N] (slice_stride apart)

@@ -8,9 +8,8 @@
 // Dispatch for y = requant(W x), x with M rows:
 //   M <= gemv_max_m (default 4)  CUDA-core GEMV (gemv.cuh), HBM-bound decode.
 //   otherwise                    split x into hi/lo byte planes and run the
-//                                tcgen05 split-byte GEMM (gemm_tc.cuh):
-//                                M <= 256: weight-as-A tiles (SWAP), BN = next
-//                                power of two >= M; M > 256: 128x256 tiles.
+//                                persistent tcgen05 split-byte GEMM (gemm_tc.cuh)
+//                                on 128-channel x BN-token tiles, BN = 32/64/128.
 //   Too few tiles for the 148 SMs, or K > 65536, splits K; the slices write
 //   exact int64 partials that reduce_requant_kernel adds and requantises.
 #include "../../include/myl_w8a16.h"
@@ -74,7 +73,7 @@ struct myl_weight {
   int64_t N = 0, K = 0, ldp = 0;  // device copy is [N][ldp] int8, ldp = round_up(K, 16)
   int8_t* d_W = nullptr;
   std::vector<uint8_t> w_shifts;
-  CUtensorMap tm128{}, tm256{};   // TMA maps with 128- and 256-row boxes
+  CUtensorMap tm128{};             // TMA map with a 128-row box (one channel tile)
   // Backend-trait cache key.
   const int8_t* host_W = nullptr;
   const uint8_t* host_shifts = nullptr;
@@ -93,7 +92,7 @@ struct myl_ctx {
   int* d_err = nullptr;
   int* h_err = nullptr;  // pinned
   uint64_t timeout_ns = 2000000000ull;
-  int gemv_max_m = 4, force_split_k = 0, force_swap = -1, inject_fault = 0;
+  int gemv_max_m = 4, force_split_k = 0, force_tile = 0, inject_fault = 0;
   int64_t launches = 0;
   PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   DevBuf x, y, rq, planes, part;
@@ -215,7 +214,11 @@ static int launch_gemv(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int6
   ksplit = int((K + k_slice - 1) / k_slice);
   const size_t smem = size_t(M) * size_t(k_slice) * 2;
   CUDA_TRY(cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-  dim3 grid(unsigned((w->N + GEMV_WARPS * v.R - 1) / (GEMV_WARPS * v.R)), unsigned(ksplit));
+  int resident = 0;
+  CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, v.fn, GEMV_THREADS, smem));
+  const int64_t row_blocks = (w->N + GEMV_WARPS * v.R - 1) / (GEMV_WARPS * v.R);
+  const int64_t per_slice = std::max<int64_t>(1, int64_t(std::max(resident, 1)) * ctx->num_sms / ksplit);
+  dim3 grid(unsigned(std::min<int64_t>(row_blocks, per_slice)), unsigned(ksplit));
   Epilogue ep = ep_final;
   int64_t slice_stride = 0;
   if (ksplit > 1) {
@@ -242,23 +245,42 @@ static int launch_gemv(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int6
   return MYL_OK;
 }
 
-template <int BN, bool SWAP, int STAGES>
+// Stage-ring depth per token tile: 192 KB of smem (one CTA per SM).
+template <int BN>
+struct TcStages;
+template <> struct TcStages<32> { static constexpr int value = 8; };
+template <> struct TcStages<64> { static constexpr int value = 6; };
+template <> struct TcStages<128> { static constexpr int value = 4; };
+
+template <int BN>
 static int launch_tc_variant(myl_ctx* ctx, const myl_weight* w, const CUtensorMap& tm_xhi,
-                             const CUtensorMap& tm_xlo, int64_t M, int ksplit, int per,
-                             int k_tiles, const Epilogue& ep, int64_t slice_stride, cudaStream_t st) {
-  using Cfg = TcCfg<BN, SWAP, STAGES>;
-  auto fn = gemm_w8a16_tc_kernel<BN, SWAP, STAGES>;
+                             const CUtensorMap& tm_xlo, int64_t M, const TcWork& work,
+                             const Epilogue& ep, int64_t slice_stride, cudaStream_t st) {
+  constexpr int STAGES = TcStages<BN>::value;
+  using Cfg = TcCfg<BN, STAGES>;
+  auto fn = gemm_w8a16_tc_kernel<BN, STAGES>;
   CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
-  const CUtensorMap& tm_w = (Cfg::ROWS_W == 128) ? w->tm128 : w->tm256;
-  dim3 grid;
-  if (SWAP) grid = dim3(unsigned((w->N + 127) / 128), unsigned((M + BN - 1) / BN), unsigned(ksplit));
-  else grid = dim3(unsigned((w->N + BN - 1) / BN), unsigned((M + 127) / 128), unsigned(ksplit));
-  fn<<<grid, TC_THREADS, Cfg::SMEM_BYTES, st>>>(tm_w, tm_xhi, tm_xlo, M, w->N, k_tiles, per, ep,
+  const int64_t units = int64_t(work.tiles_n) * work.tiles_m * work.ksplit;
+  const unsigned grid = unsigned(std::min<int64_t>(units, ctx->num_sms));
+  fn<<<grid, TC_THREADS, Cfg::SMEM_BYTES, st>>>(w->tm128, tm_xhi, tm_xlo, M, w->N, work, ep,
                                                  slice_stride, ctx->d_err, ctx->timeout_ns,
                                                  ctx->inject_fault);
   CUDA_TRY(cudaGetLastError());
   ctx->launches++;
   return MYL_OK;
+}
+
+static int tc_token_tile(const myl_ctx* ctx, int64_t M) {
+  if (ctx->force_tile == 32 || ctx->force_tile == 64 || ctx->force_tile == 128) return ctx->force_tile;
+  return M <= 32 ? 32 : (M <= 64 ? 64 : 128);
+}
+
+static int launch_tc_any(myl_ctx* ctx, const myl_weight* w, const CUtensorMap& tm_xhi,
+                         const CUtensorMap& tm_xlo, int64_t M, int BN, const TcWork& work,
+                         const Epilogue& ep, int64_t slice_stride, cudaStream_t st) {
+  if (BN == 32) return launch_tc_variant<32>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
+  if (BN == 64) return launch_tc_variant<64>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
+  return launch_tc_variant<128>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
 }
 
 static int launch_split(myl_ctx* ctx, const int16_t* x, int64_t M, int64_t K, int64_t ldx,
@@ -275,20 +297,13 @@ static int launch_split(myl_ctx* ctx, const int16_t* x, int64_t M, int64_t K, in
 static int launch_tc_planes(myl_ctx* ctx, const myl_weight* w, const int8_t* xhi, const uint8_t* xlo,
                             int64_t ldp, int64_t M, const Epilogue& ep_final, cudaStream_t st) {
   const int64_t K = w->K;
-  bool swap = (ctx->force_swap >= 0) ? (ctx->force_swap != 0) : (M <= 256);
-  int BN = 256;
-  if (swap) {
-    BN = 32;
-    while (BN < M && BN < 256) BN *= 2;
-  }
-  const int rows_x = swap ? BN : 128;
+  const int BN = tc_token_tile(ctx, M);
   CUtensorMap tm_xhi, tm_xlo;
-  TRY(encode_map(ctx, &tm_xhi, xhi, K, M, ldp, rows_x));
-  TRY(encode_map(ctx, &tm_xlo, xlo, K, M, ldp, rows_x));
-  // K split: enough CTAs for the SMs, and int32-exact slices (<= 65536).
+  TRY(encode_map(ctx, &tm_xhi, xhi, K, M, ldp, BN));
+  TRY(encode_map(ctx, &tm_xlo, xlo, K, M, ldp, BN));
+  // K split: enough work units for the SMs, and int32-exact slices (<= 65536).
   const int k_tiles = int((K + TC_BK - 1) / TC_BK);
-  const int64_t tiles = swap ? ((w->N + 127) / 128) * ((M + BN - 1) / BN)
-                             : ((w->N + BN - 1) / BN) * ((M + 127) / 128);
+  const int64_t tiles = ((w->N + 127) / 128) * ((M + BN - 1) / BN);
   int ksplit = 1;
   if (ctx->force_split_k > 0) {
     ksplit = ctx->force_split_k;
@@ -299,6 +314,7 @@ static int launch_tc_planes(myl_ctx* ctx, const myl_weight* w, const int8_t* xhi
   ksplit = std::max(1, std::min(ksplit, k_tiles));
   const int per = (k_tiles + ksplit - 1) / ksplit;
   ksplit = (k_tiles + per - 1) / per;  // no empty slice
+  TcWork work{int((w->N + 127) / 128), int((M + BN - 1) / BN), ksplit, k_tiles, per};
   Epilogue ep = ep_final;
   int64_t slice_stride = 0;
   if (ksplit > 1) {
@@ -308,13 +324,7 @@ static int launch_tc_planes(myl_ctx* ctx, const myl_weight* w, const int8_t* xhi
     ep.ldy = w->N;
     slice_stride = M * w->N;
   }
-  int rc;
-  if (!swap) rc = launch_tc_variant<256, false, 3>(ctx, w, tm_xhi, tm_xlo, M, ksplit, per, k_tiles, ep, slice_stride, st);
-  else if (BN == 32) rc = launch_tc_variant<32, true, 8>(ctx, w, tm_xhi, tm_xlo, M, ksplit, per, k_tiles, ep, slice_stride, st);
-  else if (BN == 64) rc = launch_tc_variant<64, true, 6>(ctx, w, tm_xhi, tm_xlo, M, ksplit, per, k_tiles, ep, slice_stride, st);
-  else if (BN == 128) rc = launch_tc_variant<128, true, 4>(ctx, w, tm_xhi, tm_xlo, M, ksplit, per, k_tiles, ep, slice_stride, st);
-  else rc = launch_tc_variant<256, true, 2>(ctx, w, tm_xhi, tm_xlo, M, ksplit, per, k_tiles, ep, slice_stride, st);
-  TRY(rc);
+  TRY(launch_tc_any(ctx, w, tm_xhi, tm_xlo, M, BN, work, ep, slice_stride, st));
   if (ksplit > 1) {
     const int64_t total = M * w->N;
     unsigned blocks = unsigned(std::min<int64_t>((total + 255) / 256, int64_t(ctx->num_sms) * 8));
@@ -487,7 +497,6 @@ int myl_weight_register(myl_ctx* ctx, const int8_t* W, int64_t out_features, int
     rc = fail(MYL_ERR_CUDA, "weight upload failed: %s", cudaGetErrorString(cudaGetLastError()));
   if (rc == MYL_OK && out_features > 0) {
     rc = encode_map(ctx, &w->tm128, w->d_W, w->K, w->N, w->ldp, 128);
-    if (rc == MYL_OK) rc = encode_map(ctx, &w->tm256, w->d_W, w->K, w->N, w->ldp, 256);
   }
   if (rc != MYL_OK) {
     cudaFree(w->d_W);
@@ -720,11 +729,11 @@ int myl_set_wait_timeout_ns(myl_ctx* ctx, uint64_t ns) {
   return MYL_OK;
 }
 
-int myl_set_dispatch(myl_ctx* ctx, int gemv_max_m, int force_split_k, int force_swap) {
+int myl_set_dispatch(myl_ctx* ctx, int gemv_max_m, int force_split_k, int force_token_tile) {
   if (!ctx) return fail(MYL_ERR_ARG, "ctx is null");
   ctx->gemv_max_m = gemv_max_m;
   ctx->force_split_k = force_split_k;
-  ctx->force_swap = force_swap;
+  ctx->force_tile = force_token_tile;
   return MYL_OK;
 }
 
@@ -805,20 +814,11 @@ extern "C" int myl_linear_noalloc_dev(myl_ctx* ctx, const myl_weight* w, const m
   TRY(launch_split(ctx, x, M, w->K, ldx, xhi, xlo, w->ldp, st));
   // Same tile choice as the regular path, but always one K slice: no int64
   // partial buffer is needed.
-  const bool swap = (ctx->force_swap >= 0) ? (ctx->force_swap != 0) : (M <= 256);
-  int BN = 256;
-  if (swap) {
-    BN = 32;
-    while (BN < M && BN < 256) BN *= 2;
-  }
+  const int BN = tc_token_tile(ctx, M);
   CUtensorMap tm_xhi, tm_xlo;
-  TRY(encode_map(ctx, &tm_xhi, xhi, w->K, M, w->ldp, swap ? BN : 128));
-  TRY(encode_map(ctx, &tm_xlo, xlo, w->K, M, w->ldp, swap ? BN : 128));
+  TRY(encode_map(ctx, &tm_xhi, xhi, w->K, M, w->ldp, BN));
+  TRY(encode_map(ctx, &tm_xlo, xlo, w->K, M, w->ldp, BN));
   const int k_tiles = int((w->K + TC_BK - 1) / TC_BK);
-  const Epilogue ep = make_ep(rq, y, ldy);
-  if (!swap) return launch_tc_variant<256, false, 3>(ctx, w, tm_xhi, tm_xlo, M, 1, k_tiles, k_tiles, ep, 0, st);
-  if (BN == 32) return launch_tc_variant<32, true, 8>(ctx, w, tm_xhi, tm_xlo, M, 1, k_tiles, k_tiles, ep, 0, st);
-  if (BN == 64) return launch_tc_variant<64, true, 6>(ctx, w, tm_xhi, tm_xlo, M, 1, k_tiles, k_tiles, ep, 0, st);
-  if (BN == 128) return launch_tc_variant<128, true, 4>(ctx, w, tm_xhi, tm_xlo, M, 1, k_tiles, k_tiles, ep, 0, st);
-  return launch_tc_variant<256, true, 2>(ctx, w, tm_xhi, tm_xlo, M, 1, k_tiles, k_tiles, ep, 0, st);
+  const TcWork work{int((w->N + 127) / 128), int((M + BN - 1) / BN), 1, k_tiles, k_tiles};
+  return launch_tc_any(ctx, w, tm_xhi, tm_xlo, M, BN, work, make_ep(rq, y, ldy), 0, st);
 }

@@ -135,15 +135,15 @@ def test_forced_split_k(ctx, split, mode, M):
     assert np.array_equal(y, O.linear_w8a16(x, W.reshape(-1), K, w_shifts, 6, 6))
 
 
-@pytest.mark.parametrize("swap", [0, 1])
+@pytest.mark.parametrize("tile", [32, 64, 128])
 @pytest.mark.parametrize("M", [5, 40, 130, 256, 400])
-def test_tile_shapes(ctx, swap, M):
-    rng = np.random.default_rng(M + 17 * swap)
+def test_tile_shapes(ctx, tile, M):
+    rng = np.random.default_rng(M + 17 * tile)
     K, N = 1152, 640
     W = rng.integers(-128, 128, size=(N, K), dtype=np.int8)
     x = rng.integers(-32768, 32768, size=(M, K), dtype=np.int16)  # full int16 range
     w_shifts = rng.integers(16, 20, size=N).astype(np.uint8)
-    set_mode(ctx, "tc", force_swap=swap)
+    set_mode(ctx, "tc", force_token_tile=tile)
     try:
         y = ctx.weight(W, K, w_shifts).linear(x, 4, 4)
     finally:
@@ -253,6 +253,54 @@ def test_multiplier_requant(ctx, mode):
     ws = rng.integers(10, 13, size=N).astype(np.uint8)
     y = w.linear_mult(x, np.full(N, 1 << 12, np.int32), (ws + 12).astype(np.uint8))
     assert np.array_equal(y, O.linear_w8a16(x, W.reshape(-1), K, ws, 0, 0))
+
+
+def _tie_tokens(rng):
+    """Activations x = [a, b] with 127*a + b equal to exact RNE ties (2k+1)*2^(s-1)
+    for s = 1..22, both signs, plus random values."""
+    accs = []
+    for s in range(1, 23):
+        for k in (0, 1, 2, 5):
+            v = (2 * k + 1) << (s - 1)
+            if v <= 127 * 32000:
+                accs += [v, -v, v + 1, -v - 1]
+    accs += rng.integers(-127 * 32000, 127 * 32000, size=200).tolist()
+    x = []
+    for acc in accs:
+        a = int(np.floor(acc / 127.0))
+        b = acc - 127 * a
+        if b > 100:
+            a, b = a + 1, b - 127
+        x.append([a, b])
+    return np.array(x, np.int16)
+
+
+@pytest.mark.parametrize("mode", ["gemv", "tc"])
+def test_requant_every_shift_with_ties(ctx, mode):
+    """Channel r uses the signed total shift s = r - 5 (s in [-5, 45]); the
+    tensor-core epilogue's 32-bit fast path covers s in [8, 38], the rest runs
+    in 64-bit. Ties are constructed exactly (K = 2, row [127, 1])."""
+    rng = np.random.default_rng(123)
+    N = 51
+    ws = np.arange(N, dtype=np.uint8)
+    of = np.full(N, 5, np.uint8)
+    W2 = np.tile(np.array([127, 1], np.int8), (N, 1))
+    x = _tie_tokens(rng)
+    xs = [x[:2], x[:4]] if mode == "gemv" else [x]
+    set_mode(ctx, mode)
+    w = ctx.weight(W2, 2, ws)
+    for xx in xs:
+        assert np.array_equal(w.linear(xx, 0, of), O.linear_w8a16_pc(xx, W2.reshape(-1), 2, ws, 0, of))
+        assert np.array_equal(w.lm_head(xx, 0, 5), O.lm_head_w8a16_i32(xx, W2.reshape(-1), 2, ws, 0, 5))
+    # large accumulators (~2^35) for the upper shifts
+    K = 4096
+    Wb = rng.integers(64, 128, size=(N, K), dtype=np.int8)
+    xb = rng.integers(16384, 32768, size=(2 if mode == "gemv" else 40, K), dtype=np.int16)
+    xb[1::2] *= -1
+    wb = ctx.weight(Wb, K, ws)
+    assert np.array_equal(wb.linear(xb, 0, of), O.linear_w8a16_pc(xb, Wb.reshape(-1), K, ws, 0, of))
+    assert np.array_equal(wb.lm_head(xb, 0, 5), O.lm_head_w8a16_i32(xb, Wb.reshape(-1), K, ws, 0, 5))
+    ctx.set_dispatch()
 
 
 def test_numpy_requant_matches_oracle():
