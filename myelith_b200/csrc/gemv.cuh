@@ -13,7 +13,8 @@
 //    16-byte chunks l, l+32, ... of each row with 128-bit non-coherent loads
 //    that bypass L1 (a row's 32 lanes read 512 contiguous bytes).
 //  - The activation slice x[:, k0:k0+KS] is staged once per block in shared
-//    memory (zero-filled beyond K), so ragged K needs no padding by the caller.
+//    memory (zero-filled beyond K, split into two 16-byte planes per chunk),
+//    so ragged K needs no padding by the caller.
 //  - Products use dp2a (two int16 x int8 products per instruction) into int32
 //    lanes that are flushed to int64 every U chunks (U*16 products of at most
 //    2^22 each stay below 2^31). Lanes are combined with a 64-bit shuffle tree.
@@ -49,39 +50,45 @@ __device__ __forceinline__ int dot16_dp2a(const int4 w, const int4 xa, const int
 constexpr int GEMV_THREADS = 256;
 constexpr int GEMV_WARPS = GEMV_THREADS / 32;
 
-// MT activation rows, R rows per warp, U chunks per lane in flight.
-template <int MT, int R, int U>
+// MT activation rows, R rows per warp, U chunks per lane in flight, KW warps
+// sharing one row group (each takes 1/KW of the chunks; their exact partials
+// are added through shared memory).
+template <int MT, int R, int U, int KW>
 __global__ void __launch_bounds__(GEMV_THREADS)
     gemv_w8a16_kernel(const int8_t* __restrict__ W, int64_t ldw, int64_t N,
                       const int16_t* __restrict__ X, int64_t ldx, int64_t K, int64_t k_slice,
                       Epilogue ep, int64_t slice_stride) {
+  static_assert(GEMV_WARPS % KW == 0, "warps per row group");
   extern __shared__ __align__(16) int16_t xs[];  // [MT][KS]
+  __shared__ int64_t red[GEMV_WARPS][R][MT];
   const int64_t k0 = int64_t(blockIdx.y) * k_slice;
   const int64_t kn = (K - k0) < k_slice ? (K - k0) : k_slice;  // valid elements in slice
   const int KS = int((kn + 15) & ~int64_t(15));                 // staged, multiple of 16
   const int nchunk = KS >> 4;
 
   // ---- stage x[:, k0:k0+KS] (zero beyond K) ---------------------------------
+  // Layout per activation row: plane A = elements 16c..16c+7 of every chunk c,
+  // then plane B = elements 16c+8..16c+15, so that lanes reading consecutive
+  // chunks read consecutive 16-byte words (no shared-memory bank conflicts).
   const bool vec_ok = ((reinterpret_cast<uintptr_t>(X) & 15) == 0) && (ldx % 8 == 0) && (k0 % 8 == 0);
 #pragma unroll
   for (int m = 0; m < MT; ++m) {
     const int16_t* xr = X + int64_t(m) * ldx + k0;
-    int16_t* dst = xs + m * KS;
-    if (vec_ok) {
-      for (int i = threadIdx.x * 8; i < KS; i += GEMV_THREADS * 8) {
-        int4 v;
-        if (i + 8 <= kn) {
-          v = __ldg(reinterpret_cast<const int4*>(xr + i));
-        } else {
-          alignas(16) int16_t t[8];
+    int4* dst = reinterpret_cast<int4*>(xs + m * KS);
+    const int halves = KS >> 3;  // 8-element halves
+    for (int hh = threadIdx.x; hh < halves; hh += GEMV_THREADS) {
+      const int i = hh * 8;  // first element of this half
+      int4 v;
+      if (vec_ok && i + 8 <= kn) {
+        v = __ldg(reinterpret_cast<const int4*>(xr + i));
+      } else {
+        alignas(16) int16_t t[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) t[e] = (i + e < kn) ? xr[i + e] : int16_t(0);
-          v = *reinterpret_cast<const int4*>(t);
-        }
-        *reinterpret_cast<int4*>(dst + i) = v;
+        for (int e = 0; e < 8; ++e) t[e] = (i + e < kn) ? xr[i + e] : int16_t(0);
+        v = *reinterpret_cast<const int4*>(t);
       }
-    } else {
-      for (int i = threadIdx.x; i < KS; i += GEMV_THREADS) dst[i] = (i < kn) ? xr[i] : int16_t(0);
+      const int c = hh >> 1;
+      dst[(hh & 1) * (KS >> 4) + c] = v;
     }
   }
   __syncthreads();
@@ -90,11 +97,17 @@ __global__ void __launch_bounds__(GEMV_THREADS)
   Epilogue e = ep;
   if (e.mode == EPI_ACC_I64)
     e.y = static_cast<int64_t*>(e.y) + int64_t(blockIdx.y) * slice_stride;
-  const int64_t row_step = int64_t(gridDim.x) * GEMV_WARPS * R;
+  constexpr int GROUPS = GEMV_WARPS / KW;  // row groups per block
+  const int rg = warp / KW, kw = warp % KW;
+  const int cpw = (nchunk + KW - 1) / KW;  // chunks per warp of a row group
+  const int c_begin = kw * cpw, c_end = min(nchunk, c_begin + cpw);
+  const int64_t block_rows = int64_t(GROUPS) * R;
+  const int64_t row_step = int64_t(gridDim.x) * block_rows;
 
-  // Grid-stride loop over row groups: the grid is sized to the resident
-  // blocks, so x is staged once per block and the warps keep streaming.
-  for (int64_t row0 = (int64_t(blockIdx.x) * GEMV_WARPS + warp) * R; row0 < N; row0 += row_step) {
+  // Grid-stride loop over row groups (uniform across the block: the grid is
+  // sized to the resident blocks, so x is staged once per block).
+  for (int64_t base = int64_t(blockIdx.x) * block_rows; base < N; base += row_step) {
+    const int64_t row0 = base + int64_t(rg) * R;
     int64_t acc[R][MT];
 #pragma unroll
     for (int j = 0; j < R; ++j)
@@ -108,14 +121,14 @@ __global__ void __launch_bounds__(GEMV_THREADS)
       wrow[j] = W + r * ldw + k0;
     }
 
-    for (int c = lane; c < nchunk; c += 32 * U) {
+    for (int c = c_begin + lane; c < c_end; c += 32 * U) {
       int4 wv[U][R];
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int cc = c + 32 * u;
 #pragma unroll
         for (int j = 0; j < R; ++j)
-          wv[u][j] = (cc < nchunk) ? ldg_stream_v4(wrow[j] + cc * 16) : make_int4(0, 0, 0, 0);
+          wv[u][j] = (cc < c_end) ? ldg_stream_v4(wrow[j] + cc * 16) : make_int4(0, 0, 0, 0);
       }
       int a32[R][MT];
 #pragma unroll
@@ -125,11 +138,11 @@ __global__ void __launch_bounds__(GEMV_THREADS)
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int cc = c + 32 * u;
-        if (cc < nchunk) {
+        if (cc < c_end) {
 #pragma unroll
           for (int m = 0; m < MT; ++m) {
-            const int4* xp = reinterpret_cast<const int4*>(xs + m * KS + cc * 16);
-            const int4 xa = xp[0], xb = xp[1];
+            const int4* xp = reinterpret_cast<const int4*>(xs + m * KS);
+            const int4 xa = xp[cc], xb = xp[nchunk + cc];
 #pragma unroll
             for (int j = 0; j < R; ++j) a32[j][m] = dot16_dp2a(wv[u][j], xa, xb, a32[j][m]);
           }
@@ -141,7 +154,7 @@ __global__ void __launch_bounds__(GEMV_THREADS)
         for (int m = 0; m < MT; ++m) acc[j][m] += a32[j][m];
     }
 
-    // ---- warp reduction (exact, any order) and epilogue ------------------------
+    // ---- warp reduction (exact, any order), row-group reduction, epilogue ----
 #pragma unroll
     for (int j = 0; j < R; ++j)
 #pragma unroll
@@ -151,11 +164,34 @@ __global__ void __launch_bounds__(GEMV_THREADS)
         for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
         acc[j][m] = v;
       }
+    if (KW > 1) {
+      if (lane == 0) {
 #pragma unroll
-    for (int j = 0; j < R; ++j)
+        for (int j = 0; j < R; ++j)
 #pragma unroll
-      for (int m = 0; m < MT; ++m)
-        if (lane == ((j * MT + m) & 31) && row0 + j < N) epilogue_store(e, m, row0 + j, acc[j][m]);
+          for (int m = 0; m < MT; ++m) red[warp][j][m] = acc[j][m];
+      }
+      __syncthreads();
+      if (kw == 0) {
+#pragma unroll
+        for (int j = 0; j < R; ++j)
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            int64_t v = 0;
+#pragma unroll
+            for (int t = 0; t < KW; ++t) v += red[warp + t][j][m];
+            acc[j][m] = v;
+          }
+      }
+      __syncthreads();
+    }
+    if (kw == 0) {
+#pragma unroll
+      for (int j = 0; j < R; ++j)
+#pragma unroll
+        for (int m = 0; m < MT; ++m)
+          if (lane == ((j * MT + m) & 31) && row0 + j < N) epilogue_store(e, m, row0 + j, acc[j][m]);
+    }
   }
 }
 

@@ -20,6 +20,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 #include <unordered_map>
@@ -180,32 +181,83 @@ static int shift_plan(const myl_weight* w, uint8_t act_frac, const uint8_t* out_
 using GemvFn = void (*)(const int8_t*, int64_t, int64_t, const int16_t*, int64_t, int64_t, int64_t,
                         Epilogue, int64_t);
 
-template <int MT, int R, int U>
+template <int MT, int R, int U, int KW>
 static void* gemv_ptr() {
-  return reinterpret_cast<void*>(&gemv_w8a16_kernel<MT, R, U>);
+  return reinterpret_cast<void*>(&gemv_w8a16_kernel<MT, R, U, KW>);
 }
 
 struct GemvVariant {
   void* fn;
-  int R;
+  int R, KW;
 };
 
-static GemvVariant gemv_variant(int M) {
+// Rows per warp R, 16-byte chunks per lane in flight U and warps per row group
+// KW, from measurements on B200: two rows per warp and ~128 KB of loads in
+// flight per SM; long rows (K >= 8192) want twice the chunks per lane; when
+// the rows alone give too few warp jobs (N/R*KW below ~40 warps per SM) the
+// warps of a block share rows and split K.
+static GemvVariant gemv_variant(int M, int64_t K, int64_t N, int num_sms) {
+  const int64_t chunks = (K + 15) / 16;
+  int kw = 1;
+  while (kw < 8 && (N / 2) * kw < int64_t(40) * num_sms && chunks / (kw * 2) >= 64) kw *= 2;
   switch (M) {
-    case 1: return {gemv_ptr<1, 1, 4>(), 1};
-    case 2: return {gemv_ptr<2, 2, 2>(), 2};
-    case 3: return {gemv_ptr<3, 2, 2>(), 2};
-    default: return {gemv_ptr<4, 2, 2>(), 2};
+    case 1:
+      if (K >= 8192) {
+        if (kw >= 8) return {gemv_ptr<1, 2, 8, 8>(), 2, 8};
+        if (kw == 4) return {gemv_ptr<1, 2, 8, 4>(), 2, 4};
+        if (kw == 2) return {gemv_ptr<1, 2, 8, 2>(), 2, 2};
+        return {gemv_ptr<1, 2, 8, 1>(), 2, 1};
+      }
+      if (kw >= 4) return {gemv_ptr<1, 2, 4, 4>(), 2, 4};
+      if (kw == 2) return {gemv_ptr<1, 2, 4, 2>(), 2, 2};
+      return {gemv_ptr<1, 2, 4, 1>(), 2, 1};
+    case 2:
+      if (kw >= 4) return {gemv_ptr<2, 2, 4, 4>(), 2, 4};
+      if (kw == 2) return {gemv_ptr<2, 2, 4, 2>(), 2, 2};
+      return {gemv_ptr<2, 2, 4, 1>(), 2, 1};
+    case 3:
+      if (kw >= 4) return {gemv_ptr<3, 2, 2, 4>(), 2, 4};
+      if (kw == 2) return {gemv_ptr<3, 2, 2, 2>(), 2, 2};
+      return {gemv_ptr<3, 2, 2, 1>(), 2, 1};
+    default:
+      if (kw >= 4) return {gemv_ptr<4, 2, 2, 4>(), 2, 4};
+      if (kw == 2) return {gemv_ptr<4, 2, 2, 2>(), 2, 2};
+      return {gemv_ptr<4, 2, 2, 1>(), 2, 1};
   }
 }
 
-static constexpr int GEMV_SMEM_BUDGET = 64 * 1024;
+// Per-(device, kernel) launch facts cached across calls: the dynamic shared
+// memory attribute (device state) and the resident blocks per SM.
+struct LaunchCache {
+  std::mutex mu;
+  std::map<std::pair<int, const void*>, std::pair<int, int>> smem_occ;  // -> (smem set, blocks/SM)
+};
+static LaunchCache g_launch_cache;
+
+static int kernel_smem_occupancy(int device, const void* fn, int threads, size_t smem,
+                                 int* resident) {
+  std::lock_guard<std::mutex> lock(g_launch_cache.mu);
+  const auto key = std::make_pair(device, fn);
+  auto it = g_launch_cache.smem_occ.find(key);
+  if (it != g_launch_cache.smem_occ.end() && it->second.first == int(smem)) {
+    if (resident) *resident = it->second.second;
+    return MYL_OK;
+  }
+  CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  int r = 0;
+  CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, fn, threads, smem));
+  g_launch_cache.smem_occ[key] = {int(smem), r};
+  if (resident) *resident = r;
+  return MYL_OK;
+}
+
+static constexpr int GEMV_SMEM_BUDGET = 100 * 1024;
 
 static inline int64_t round_up16(int64_t v) { return (v + 15) & ~int64_t(15); }
 
 static int launch_gemv(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M, int64_t ldx,
                        const Epilogue& ep_final, cudaStream_t st) {
-  GemvVariant v = gemv_variant(int(M));
+  GemvVariant v = gemv_variant(int(M), w->K, w->N, ctx->num_sms);
   const int64_t K = w->K;
   const int64_t ks_max = (GEMV_SMEM_BUDGET / (2 * M)) & ~int64_t(15);
   int ksplit = int((round_up16(K) + ks_max - 1) / ks_max);
@@ -213,12 +265,14 @@ static int launch_gemv(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int6
   int64_t k_slice = round_up16((K + ksplit - 1) / ksplit);
   ksplit = int((K + k_slice - 1) / k_slice);
   const size_t smem = size_t(M) * size_t(k_slice) * 2;
-  CUDA_TRY(cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   int resident = 0;
-  CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, v.fn, GEMV_THREADS, smem));
-  const int64_t row_blocks = (w->N + GEMV_WARPS * v.R - 1) / (GEMV_WARPS * v.R);
+  TRY(kernel_smem_occupancy(ctx->device, v.fn, GEMV_THREADS, smem, &resident));
+  const int64_t rows_per_block = int64_t(GEMV_WARPS / v.KW) * v.R;
+  const int64_t row_blocks = (w->N + rows_per_block - 1) / rows_per_block;
+  // Balanced grid: every block runs the same number of row-group iterations.
   const int64_t per_slice = std::max<int64_t>(1, int64_t(std::max(resident, 1)) * ctx->num_sms / ksplit);
-  dim3 grid(unsigned(std::min<int64_t>(row_blocks, per_slice)), unsigned(ksplit));
+  const int64_t iters = (row_blocks + per_slice - 1) / per_slice;
+  dim3 grid(unsigned((row_blocks + iters - 1) / iters), unsigned(ksplit));
   Epilogue ep = ep_final;
   int64_t slice_stride = 0;
   if (ksplit > 1) {
@@ -259,7 +313,8 @@ static int launch_tc_variant(myl_ctx* ctx, const myl_weight* w, const CUtensorMa
   constexpr int STAGES = TcStages<BN>::value;
   using Cfg = TcCfg<BN, STAGES>;
   auto fn = gemm_w8a16_tc_kernel<BN, STAGES>;
-  CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
+  TRY(kernel_smem_occupancy(ctx->device, reinterpret_cast<const void*>(fn), TC_THREADS,
+                            Cfg::SMEM_BYTES, nullptr));
   const int64_t units = int64_t(work.tiles_n) * work.tiles_m * work.ksplit;
   const unsigned grid = unsigned(std::min<int64_t>(units, ctx->num_sms));
   fn<<<grid, TC_THREADS, Cfg::SMEM_BYTES, st>>>(w->tm128, tm_xhi, tm_xlo, M, w->N, work, ep,
@@ -351,8 +406,12 @@ static int run_linear(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64
   if (M == 0 || w->N == 0) return MYL_OK;
   CUDA_TRY(cudaSetDevice(ctx->device));
   TRY(ws_acquire(ctx, st));
-  int rc = (M <= ctx->gemv_max_m && M <= 4) ? launch_gemv(ctx, w, x, M, ldx, ep, st)
-                                            : launch_tc(ctx, w, x, M, ldx, ep, st);
+  int rc;
+  if (M <= ctx->gemv_max_m && M <= 4) {
+    rc = launch_gemv(ctx, w, x, M, ldx, ep, st);
+  } else {
+    rc = launch_tc(ctx, w, x, M, ldx, ep, st);
+  }
   TRY(rc);
   return ws_release(ctx, st);
 }

@@ -182,6 +182,37 @@ def test_k_beyond_int32_slice_limit(ctx):
     assert np.array_equal(y, O.lm_head_w8a16_i32(x, W.reshape(-1), K, np.full(N, 20), 0, 0))
 
 
+@pytest.mark.parametrize("M", [1, 2, 3, 4])
+@pytest.mark.parametrize("K,N", [(18944, 64), (18944, 3584), (4096, 2048), (3584, 18944),
+                                 (8192, 200), (1000, 777)])
+def test_gemv_variants(ctx, M, K, N):
+    """Shapes that select each GEMV variant: rows per warp, chunks in flight and
+    warps per row group (K split inside a block)."""
+    rng = np.random.default_rng(M * 7 + K + N)
+    W = rng.integers(-128, 128, size=(N, K), dtype=np.int8)
+    x = normal_x(rng, M, K, 3000.0)
+    ks = gen.nominal_shift(K, 13)
+    ws = rng.integers(ks - 1, ks + 2, size=N).astype(np.uint8)
+    set_mode(ctx, "gemv")
+    y = ctx.weight(W, K, ws).linear(x, 8, 8)
+    ctx.set_dispatch()
+    assert np.array_equal(y, O.linear_w8a16(x, W.reshape(-1), K, ws, 8, 8))
+
+
+@pytest.mark.parametrize("M", [1, 3])
+def test_gemv_k_split_across_blocks(ctx, M):
+    """x rows too long for one block's shared memory: the GEMV splits K
+    across blocks and adds the exact int64 partials."""
+    rng = np.random.default_rng(70 + M)
+    K, N = 70000, 64
+    W = rng.integers(-128, 128, size=(N, K), dtype=np.int8)
+    x = rng.integers(-32768, 32768, size=(M, K), dtype=np.int16)
+    set_mode(ctx, "gemv")
+    y = ctx.weight(W, K, np.full(N, 22, np.uint8)).linear(x, 0, 0)
+    ctx.set_dispatch()
+    assert np.array_equal(y, O.linear_w8a16(x, W.reshape(-1), K, np.full(N, 22), 0, 0))
+
+
 def test_negative_shift_and_saturation(ctx):
     rng = np.random.default_rng(3)
     K, N = 640, 256
