@@ -90,6 +90,13 @@ int myl_linear_w8a16_pc(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int
 int myl_lm_head_w8a16_i32(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
                           uint8_t final_norm_frac, uint8_t logit_frac, int32_t* logits);
 
+/* linear_w8a16 followed by add_bias_i16 (linear.rs:132-145) as the runtime
+ * does for q/k/v (runtime/src/model.rs:438-453), fused into one epilogue:
+ * y = clamp_i16(clamp_i16(requant(acc)) + rescale(bias[r], bias_shifts[r], out_frac)). */
+int myl_linear_w8a16_bias(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
+                          uint8_t act_frac_bits, uint8_t out_frac_bits, const int16_t* bias,
+                          const uint8_t* bias_shifts, int16_t* y);
+
 /* Multiplier requant: y = clamp_i16(rne_i128(acc * mult[r], shift[r])).
  * No counterpart in the reference linear layer; with mult = 2^m and
  * shift = s + m it equals the pure shift (fixed_point.rs:365-379). */
@@ -117,6 +124,9 @@ int myl_requant_create(myl_ctx* ctx, const myl_weight* w, int mode, uint8_t act_
                        const uint8_t* out_frac_pc, int per_channel, const int32_t* mult,
                        const uint8_t* shift, myl_requant** out);
 int myl_requant_release(myl_ctx* ctx, myl_requant* rq);
+/* Adds the q/k/v bias of add_bias_i16 (linear.rs:132-145) to an int16 plan. */
+int myl_requant_set_bias(myl_ctx* ctx, myl_requant* rq, const int16_t* bias,
+                         const uint8_t* bias_shifts, uint8_t out_frac);
 
 /* y[M][ldy] = requant(W x) with device pointers. y is int16 for the *_I16
  * modes and int32 for MYL_RQ_SHIFT_I32. x rows are ldx elements apart. */
@@ -143,6 +153,29 @@ int myl_split_hilo_dev(myl_ctx* ctx, const int16_t* x, int64_t M, int64_t K, int
 int myl_linear_planes_dev(myl_ctx* ctx, const myl_weight* w, const myl_requant* rq,
                           const int8_t* xhi, const uint8_t* xlo, int64_t ldp, int64_t M, void* y,
                           int64_t ldy, void* stream);
+
+/* --- MLP: mlp_int (kernels/src/mlp.rs:28-74) ----------------------------------
+ * gate = linear_w8a16(x, W_gate), up = linear_w8a16(x, W_up),
+ * h = clamp_i16(rescale_i64(silu_lut[idx(gate)] * up, silu_out + up_out, down_in)),
+ * y = linear_w8a16_pc(h, W_down, out_frac[H]).
+ * Registration uploads W_gate/W_up interleaved (row 2i = gate_i, 2i+1 = up_i),
+ * so one kernel computes both projections and the SiLU product (and, for
+ * M > 4, writes h straight into the down projection's byte planes). Every
+ * shift is validated as the reference's debug build would. */
+typedef struct myl_mlp myl_mlp;
+int myl_mlp_register(myl_ctx* ctx, const int8_t* W_gate, const int8_t* W_up, const int8_t* W_down,
+                     int64_t hidden, int64_t intermediate, const uint8_t* gate_w_shifts,
+                     const uint8_t* up_w_shifts, const uint8_t* down_w_shifts,
+                     const int16_t* silu_lut, int64_t silu_lut_len, uint8_t in_frac,
+                     uint8_t gate_out_frac, uint8_t up_out_frac, uint8_t down_in_frac,
+                     uint8_t silu_in_frac, int16_t silu_lut_offset, uint8_t silu_out_frac,
+                     const uint8_t* out_frac, myl_mlp** out);
+int myl_mlp_release(myl_ctx* ctx, myl_mlp* mlp);
+/* Host pointers: x [M][hidden] -> y [M][hidden]. */
+int myl_mlp_int(myl_ctx* ctx, const myl_mlp* mlp, const int16_t* x, int64_t M, int16_t* y);
+/* Device pointers on a stream. */
+int myl_mlp_dev(myl_ctx* ctx, const myl_mlp* mlp, const int16_t* x, int64_t M, int64_t ldx,
+                int16_t* y, int64_t ldy, void* stream);
 
 /* Waits for the context's work and reports kernel-side errors (bounded waits
  * that ran out) as MYL_ERR_DEVICE; the context stays usable afterwards. */

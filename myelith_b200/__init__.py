@@ -93,6 +93,13 @@ def load_library(path: str | None = None):
             "myl_requant_acc_dev": ([vp, vp, vp, i64, vp, i64, vp], i32),
             "myl_split_hilo_dev": ([vp, vp, i64, i64, i64, vp, vp, i64, vp], i32),
             "myl_linear_planes_dev": ([vp, vp, vp, vp, vp, i64, i64, vp, i64, vp], i32),
+            "myl_linear_w8a16_bias": ([vp, vp, vp, i64, u8, u8, vp, vp, vp], i32),
+            "myl_requant_set_bias": ([vp, vp, vp, vp, u8], i32),
+            "myl_mlp_register": ([vp, vp, vp, vp, i64, i64, vp, vp, vp, vp, i64, u8, u8, u8, u8, u8,
+                                  C.c_int16, u8, vp, C.POINTER(vp)], i32),
+            "myl_mlp_release": ([vp, vp], i32),
+            "myl_mlp_int": ([vp, vp, vp, i64, vp], i32),
+            "myl_mlp_dev": ([vp, vp, vp, i64, i64, vp, i64, vp], i32),
             "myl_synchronize": ([vp], i32),
             "myl_set_wait_timeout_ns": ([vp, C.c_uint64], i32),
             "myl_set_dispatch": ([vp, i32, i32, i32], i32),
@@ -255,6 +262,19 @@ class Weight:
             self.ctx.handle, self._h, _p(xs), xs.shape[0], final_norm_frac, logit_frac, _p(y)))
         return y[0] if single else y
 
+    def linear_bias(self, x, act_frac_bits: int, out_frac_bits: int, bias, bias_shifts) -> np.ndarray:
+        """linear_w8a16 then add_bias_i16, fused (runtime/src/model.rs:438-453)."""
+        xs, single = self._rows(x)
+        b = _c(bias, np.int16)
+        bs = _c(bias_shifts, np.uint8)
+        if b.size != self.out_features or bs.size != self.out_features:
+            raise MylError("add_bias_i16", MYL_ERR_SHAPE, "one bias and shift per channel")
+        y = np.zeros((xs.shape[0], self.out_features), np.int16)
+        _check("myl_linear_w8a16_bias", load_library().myl_linear_w8a16_bias(
+            self.ctx.handle, self._h, _p(xs), xs.shape[0], act_frac_bits, out_frac_bits, _p(b), _p(bs),
+            _p(y)))
+        return y[0] if single else y
+
     def linear_mult(self, x, mult, shift) -> np.ndarray:
         xs, single = self._rows(x)
         mult = _c(mult, np.int32)
@@ -321,9 +341,70 @@ class Requant:
         except Exception:
             pass
 
+    def set_bias(self, bias, bias_shifts, out_frac: int) -> None:
+        b = _c(bias, np.int16)
+        bs = _c(bias_shifts, np.uint8)
+        _check("myl_requant_set_bias", load_library().myl_requant_set_bias(
+            self.w.ctx.handle, self._h, _p(b), _p(bs), out_frac))
+
     def apply_acc_dev(self, acc, y, stream=None) -> None:
         _check("myl_requant_acc_dev", load_library().myl_requant_acc_dev(
             self.w.ctx.handle, self._h, _p(acc), acc.shape[0], _p(y), y.stride(0),
+            _stream_ptr(stream)))
+
+
+class Mlp:
+    """mlp_int (kernels/src/mlp.rs:28-74) with its weights and scales
+    registered once (gate/up interleaved on the device)."""
+
+    def __init__(self, ctx: Context, W_gate, W_up, W_down, hidden_size: int, intermediate_size: int,
+                 gate_w_shifts, up_w_shifts, down_w_shifts, silu_lut, in_frac_bits: int,
+                 gate_out_frac: int, up_out_frac: int, down_in_frac: int, silu_in_frac: int,
+                 silu_lut_offset: int, silu_out_frac: int, out_frac_bits):
+        H, I = hidden_size, intermediate_size
+        Wg, Wu, Wd = (_c(a, np.int8).reshape(-1) for a in (W_gate, W_up, W_down))
+        gs, us, ds = (_c(a, np.uint8) for a in (gate_w_shifts, up_w_shifts, down_w_shifts))
+        lut = _c(silu_lut, np.int16)
+        of = _c(out_frac_bits, np.uint8)
+        if (H <= 0 or I <= 0 or Wg.size != H * I or Wu.size != H * I or Wd.size != H * I
+                or gs.size != I or us.size != I or ds.size != H or of.size != H):
+            raise MylError("mlp_int", MYL_ERR_SHAPE, "weight/shift lengths do not match the shape")
+        h = C.c_void_p()
+        _check("myl_mlp_register", load_library().myl_mlp_register(
+            ctx.handle, _p(Wg), _p(Wu), _p(Wd), H, I, _p(gs), _p(us), _p(ds), _p(lut), lut.size,
+            in_frac_bits, gate_out_frac, up_out_frac, down_in_frac, silu_in_frac, silu_lut_offset,
+            silu_out_frac, _p(of), C.byref(h)))
+        self.ctx, self._h, self.hidden, self.intermediate = ctx, h, H, I
+
+    @property
+    def handle(self):
+        return self._h
+
+    def release(self) -> None:
+        if getattr(self, "_h", None) and self.ctx.handle:
+            load_library().myl_mlp_release(self.ctx.handle, self._h)
+        self._h = None
+
+    def __del__(self):
+        try:
+            self.release()
+        except Exception:
+            pass
+
+    def __call__(self, x) -> np.ndarray:
+        x = _c(x, np.int16)
+        single = x.ndim == 1
+        xs = np.ascontiguousarray(x.reshape(1, -1) if single else x)
+        if xs.shape[1] != self.hidden:
+            raise MylError("mlp_int", MYL_ERR_SHAPE, "x rows must have hidden_size elements")
+        y = np.zeros_like(xs)
+        _check("myl_mlp_int", load_library().myl_mlp_int(self.ctx.handle, self._h, _p(xs),
+                                                           xs.shape[0], _p(y)))
+        return y[0] if single else y
+
+    def dev(self, x, y, stream=None) -> None:
+        _check("myl_mlp_dev", load_library().myl_mlp_dev(
+            self.ctx.handle, self._h, _p(x), x.shape[0], x.stride(0), _p(y), y.stride(0),
             _stream_ptr(stream)))
 
 
@@ -369,6 +450,7 @@ def _cached_weight(W, in_features: int, w_shifts) -> Weight:
 
 def clear_weight_cache() -> None:
     _cache.clear()
+    _mlp_cache.clear()
 
 
 def linear_w8a16(x, W, in_features: int, w_shifts, act_frac_bits: int, out_frac_bits: int) -> np.ndarray:
@@ -382,6 +464,37 @@ def linear_w8a16_pc(x, W, in_features: int, w_shifts, act_frac_bits: int, out_fr
     if of.size != np.asarray(w_shifts).size:
         raise MylError("linear_w8a16_pc", MYL_ERR_SHAPE, "one out_frac per channel (Fund 20)")
     return _cached_weight(W, in_features, w_shifts).linear(x, act_frac_bits, of)
+
+
+def add_bias_linear_w8a16(x, W, in_features: int, w_shifts, act_frac_bits: int, out_frac_bits: int,
+                          bias, bias_shifts) -> np.ndarray:
+    """linear_w8a16 followed by add_bias_i16 (linear.rs:43, :132), as q/k/v use it."""
+    return _cached_weight(W, in_features, w_shifts).linear_bias(x, act_frac_bits, int(out_frac_bits),
+                                                                bias, bias_shifts)
+
+
+_mlp_cache: dict = {}
+
+
+def mlp_int(x, W_gate, W_up, W_down, hidden_size: int, intermediate_size: int, gate_w_shifts,
+            up_w_shifts, down_w_shifts, silu_lut, in_frac_bits: int, gate_out_frac: int,
+            up_out_frac: int, down_in_frac: int, silu_in_frac: int, silu_lut_offset: int,
+            silu_out_frac: int, out_frac_bits) -> np.ndarray:
+    """kernels/src/mlp.rs:28 on the B200 (x: [hidden] or [M, hidden])."""
+    arrs = [np.asarray(a) for a in (W_gate, W_up, W_down, gate_w_shifts, up_w_shifts, down_w_shifts,
+                                    silu_lut, out_frac_bits)]
+    key = tuple((a.__array_interface__["data"][0], a.size, a.dtype.str) for a in arrs) + (
+        hidden_size, intermediate_size, in_frac_bits, gate_out_frac, up_out_frac, down_in_frac,
+        silu_in_frac, silu_lut_offset, silu_out_frac,
+        np.asarray(gate_w_shifts).tobytes(), np.asarray(up_w_shifts).tobytes(),
+        np.asarray(down_w_shifts).tobytes(), np.asarray(out_frac_bits).tobytes())
+    m = _mlp_cache.get(key)
+    if m is None:
+        m = Mlp(default_context(), W_gate, W_up, W_down, hidden_size, intermediate_size, gate_w_shifts,
+                up_w_shifts, down_w_shifts, silu_lut, in_frac_bits, gate_out_frac, up_out_frac,
+                down_in_frac, silu_in_frac, silu_lut_offset, silu_out_frac, out_frac_bits)
+        _mlp_cache[key] = m
+    return m(x)
 
 
 def lm_head_w8a16_i32(x, W, in_features: int, w_shifts, final_norm_frac: int, logit_frac: int) -> np.ndarray:
@@ -428,3 +541,16 @@ class CudaBackend:
         _check("myl_backend_linear_w8a16", load_library().myl_backend_linear_w8a16(
             self._ctx.handle, _p(x), _p(W), _p(out), in_features, out_features, _p(w_shifts),
             act_frac, out_frac))
+
+    def mlp(self, x, W_gate, W_up, W_down, out, gate_w_shifts, up_w_shifts, down_w_shifts, silu_lut,
+            in_frac: int, gate_out_frac: int, up_out_frac: int, down_in_frac: int, silu_in_frac: int,
+            silu_lut_offset: int, silu_out_frac: int, out_frac) -> None:
+        """Backend::mlp (kernels/src/backend.rs:107-126): hidden = x.len(),
+        intermediate = W_gate.len() / hidden; writes into out."""
+        x = _c(x, np.int16)
+        hidden = x.size
+        inter = np.asarray(W_gate).size // max(hidden, 1)
+        y = mlp_int(x, W_gate, W_up, W_down, hidden, inter, gate_w_shifts, up_w_shifts, down_w_shifts,
+                    silu_lut, in_frac, gate_out_frac, up_out_frac, down_in_frac, silu_in_frac,
+                    silu_lut_offset, silu_out_frac, out_frac)
+        out[:hidden] = y

@@ -34,15 +34,30 @@ enum EpiMode : int {
   EPI_ACC_I64 = 0,    // store exact int64 partial sums
   EPI_SHIFT = 1,      // reference requant (pure shift)
   EPI_MULT = 2,       // multiplier requant (i128 product)
+  EPI_SILU = 3,       // MLP: rows 2i / 2i+1 are gate_i / up_i; store h_i (mlp.rs:49-64)
+};
+
+// Parameters of the SiLU-LUT product of mlp.rs:52-64 (validated on the host).
+struct SiluParams {
+  const int16_t* lut;
+  int lut_hi;        // index upper bound: (lut.len() as i16) - 1, Rust release wrapping
+  int offset;        // silu_lut_offset (i16)
+  int s1;            // gate_out_frac - silu_in_frac, signed, in [-31, 30]
+  int s2;            // silu_out_frac + up_out_frac - down_in_frac, signed, in [-63, 62]
+  int8_t* h_hi;      // optional byte planes of h for the down projection: [M][ldp]
+  uint8_t* h_lo;
+  int64_t ldp;
 };
 
 struct Epilogue {
   int mode;               // EpiMode
   int out_i32;            // 1: clamp to i32 and store int32, 0: clamp to i16, store int16
-  const int8_t* shift;    // [N]: signed total shift (EPI_SHIFT) / uint8 shift (EPI_MULT)
+  const int8_t* shift;    // [N]: signed total shift (EPI_SHIFT, EPI_SILU) / uint8 shift (EPI_MULT)
   const int32_t* mult;    // [N] (EPI_MULT)
-  void* y;                // [M][ldy] int16/int32 (requant modes) or int64 (EPI_ACC_I64)
+  void* y;                // [M][ldy] int16/int32 (requant modes), int64 (EPI_ACC_I64), h (EPI_SILU)
   int64_t ldy;
+  const int32_t* bias;    // optional [N]: rescaled bias added after the i16 clamp (linear.rs:132-145)
+  SiluParams silu;
 };
 
 // ---- requant -----------------------------------------------------------------
@@ -83,6 +98,55 @@ __device__ __forceinline__ int64_t requant_mult(int64_t acc, int32_t m, int s, i
   return (int64_t)p;
 }
 
+// fixed_point.rs:39-53 for i32, s in [1, 30].
+__device__ __forceinline__ int32_t rshift_rne_i32(int32_t v, int s) {
+  const int32_t q = v >> s;
+  const int32_t r = v & ((1 << s) - 1);
+  const int32_t h = 1 << (s - 1);
+  return q + ((r > h) | ((r == h) & (q & 1)));
+}
+
+// mlp.rs:52-63 for one channel pair: gate g and up u are the clamped int16
+// outputs of the two projections. g goes to the LUT domain with rescale (i32,
+// fixed_point.rs:173-180), is truncated to i16 and offset with Rust release
+// (wrapping) i16 arithmetic, clamped to the table (integer_math.rs:166-170);
+// the LUT value times u is rescaled in i64 to the down projection's input
+// scale and clamped to i16.
+__device__ __forceinline__ int16_t silu_combine(const SiluParams& sp, int32_t g, int32_t u) {
+  int32_t gd;
+  if (sp.s1 > 0) gd = rshift_rne_i32(g, sp.s1);
+  else if (sp.s1 == 0) gd = g;
+  else gd = int32_t(uint32_t(g) << (-sp.s1));
+  const int16_t g16 = int16_t(uint16_t(uint32_t(gd)));
+  int idx = int(int16_t(uint16_t(uint16_t(g16) + uint16_t(sp.offset))));
+  idx = idx < 0 ? 0 : idx;
+  idx = idx > sp.lut_hi ? sp.lut_hi : idx;
+  const int64_t prod = int64_t(sp.lut[idx]) * int64_t(u);
+  return int16_t(clamp_i64(rescale_i64_signed(prod, sp.s2), -32768, 32767));
+}
+
+// Stores h for (m, channel pair i) (if y is given) and its byte planes (if
+// requested).
+__device__ __forceinline__ void silu_store(const Epilogue& ep, int64_t m, int64_t i, int16_t h) {
+  if (ep.y) static_cast<int16_t*>(ep.y)[m * ep.ldy + i] = h;
+  if (ep.silu.h_hi) {
+    ep.silu.h_hi[m * ep.silu.ldp + i] = int8_t(h >> 8);
+    ep.silu.h_lo[m * ep.silu.ldp + i] = uint8_t(h & 0xFF);
+  }
+}
+
+// Requant of one accumulator of channel n to its clamped output value
+// (shift or multiplier mode; the bias, if any, is added after the clamp).
+__device__ __forceinline__ int64_t requant_value(const Epilogue& ep, int64_t n, int64_t acc) {
+  const int64_t lo = ep.out_i32 ? int64_t(INT32_MIN) : -32768;
+  const int64_t hi = ep.out_i32 ? int64_t(INT32_MAX) : 32767;
+  int64_t v;
+  if (ep.mode == EPI_MULT) v = requant_mult(acc, ep.mult[n], int(uint8_t(ep.shift[n])), lo, hi);
+  else v = clamp_i64(rescale_i64_signed(acc, ep.shift[n]), lo, hi);
+  if (ep.bias) v = clamp_i64(v + ep.bias[n], lo, hi);
+  return v;
+}
+
 // Applies the epilogue to one exact accumulator of output (m, n).
 __device__ __forceinline__ void epilogue_store(const Epilogue& ep, int64_t m, int64_t n,
                                                int64_t acc) {
@@ -90,35 +154,31 @@ __device__ __forceinline__ void epilogue_store(const Epilogue& ep, int64_t m, in
     static_cast<int64_t*>(ep.y)[m * ep.ldy + n] = acc;
     return;
   }
-  const int64_t lo = ep.out_i32 ? int64_t(INT32_MIN) : -32768;
-  const int64_t hi = ep.out_i32 ? int64_t(INT32_MAX) : 32767;
-  int64_t v;
-  if (ep.mode == EPI_SHIFT) {
-    v = clamp_i64(rescale_i64_signed(acc, ep.shift[n]), lo, hi);
-  } else {
-    v = requant_mult(acc, ep.mult[n], int(uint8_t(ep.shift[n])), lo, hi);
-  }
+  const int64_t v = requant_value(ep, n, acc);
   if (ep.out_i32) static_cast<int32_t*>(ep.y)[m * ep.ldy + n] = int32_t(v);
   else static_cast<int16_t*>(ep.y)[m * ep.ldy + n] = int16_t(v);
 }
 
-// Per-channel requant with the channel's parameters already in registers.
+// Per-channel requant with the channel's parameters already in registers
+// (EPI_SHIFT / EPI_SILU use the shift, EPI_MULT the multiplier too).
 struct ChannelRequant {
   int mode, out_i32, shift;
-  int32_t mult;
+  int32_t mult, bias;
   __device__ __forceinline__ void load(const Epilogue& ep, int64_t n) {
     mode = ep.mode;
     out_i32 = ep.out_i32;
     shift = 0;
     mult = 1;
-    if (mode == EPI_SHIFT) shift = ep.shift[n];
-    else if (mode == EPI_MULT) { shift = int(uint8_t(ep.shift[n])); mult = ep.mult[n]; }
+    bias = ep.bias ? ep.bias[n] : 0;
+    if (mode == EPI_MULT) { shift = int(uint8_t(ep.shift[n])); mult = ep.mult[n]; }
+    else shift = ep.shift[n];
   }
   __device__ __forceinline__ int64_t apply(int64_t acc) const {
     const int64_t lo = out_i32 ? int64_t(INT32_MIN) : -32768;
     const int64_t hi = out_i32 ? int64_t(INT32_MAX) : 32767;
-    if (mode == EPI_SHIFT) return clamp_i64(rescale_i64_signed(acc, shift), lo, hi);
-    return requant_mult(acc, mult, shift, lo, hi);
+    const int64_t v = (mode == EPI_MULT) ? requant_mult(acc, mult, shift, lo, hi)
+                                         : clamp_i64(rescale_i64_signed(acc, shift), lo, hi);
+    return bias ? clamp_i64(v + bias, lo, hi) : v;
   }
 };
 

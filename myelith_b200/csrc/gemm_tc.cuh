@@ -101,21 +101,29 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
 // the bias splits as 256*bh + bl with bh = 2^(t-1) - 1, bl = 255 (t >= 1) or
 // bh = 0, bl = 127 (t = 0), giving (h + bh + ((l + bl + odd) >> 8)) >> t.
 // |h| < 2^30 + 2^23 (K <= 65536), so no step leaves int32.
+// The optional per-channel bias (linear.rs:132-145) is added after the first
+// clamp and clamped again, as the reference adds it to the clamped output.
 struct Requant32 {
-  int t, bh, bl, lo_b, hi_b;
-  __device__ __forceinline__ void init(int s, bool out_i32) {
+  int t, bh, bl, lo_b, hi_b, bias;
+  __device__ __forceinline__ void init(int s, bool out_i32, int b) {
     t = s - 8;
     bh = t > 0 ? (1 << (t - 1)) - 1 : 0;
     bl = t > 0 ? 255 : 127;
     lo_b = out_i32 ? INT32_MIN : -32768;
     hi_b = out_i32 ? INT32_MAX : 32767;
+    bias = b;
   }
   __device__ __forceinline__ int apply(int32_t H, int32_t L) const {
     const int32_t h = H + (L >> 8);
     const int32_t l = L & 255;
     const int32_t odd = (h >> t) & 1;
-    const int32_t v = (h + bh + ((l + bl + odd) >> 8)) >> t;
-    return v < lo_b ? lo_b : (v > hi_b ? hi_b : v);
+    int32_t v = (h + bh + ((l + bl + odd) >> 8)) >> t;
+    v = v < lo_b ? lo_b : (v > hi_b ? hi_b : v);
+    if (lo_b == -32768) {  // bias only exists for int16 outputs
+      v += bias;
+      v = v < lo_b ? lo_b : (v > hi_b ? hi_b : v);
+    }
+    return v;
   }
 };
 
@@ -309,17 +317,35 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       int shift = 0;
       const int mode = e.mode;
       if (n < N && mode != EPI_ACC_I64) shift = e.shift[n];
-      const bool fast = (mode == EPI_SHIFT) && shift >= 8 && shift <= 38;
+      const bool fast = (mode == EPI_SHIFT || mode == EPI_SILU) && shift >= 8 && shift <= 38;
       Requant32 r32;
-      r32.init(fast ? shift : 8, e.out_i32 != 0);
+      r32.init(fast ? shift : 8, e.out_i32 != 0, (n < N && e.bias) ? e.bias[n] : 0);
       ChannelRequant rq;
       if (n < N && !fast && mode != EPI_ACC_I64) rq.load(e, n);
 #pragma unroll 1
       for (int c = 0; c < HALF; c += NC) {
         uint32_t hi[NC], lo[NC];
         tmem_ld_pair<NC>(tq + c, tq + BN + c, hi, lo);
-        if (n >= N) continue;
         const int64_t mc = m0 + c;
+        if (mode == EPI_SILU) {
+          // Gate (even row) and up (odd row) of channel pair n/2 sit in
+          // adjacent lanes; every lane takes part in the shuffles, even lanes
+          // store the first half of the tokens, odd lanes the second.
+          const bool even = (row & 1) == 0;
+#pragma unroll
+          for (int j = 0; j < NC; ++j) {
+            int32_t v = 0;
+            if (n < N)
+              v = fast ? r32.apply(int32_t(hi[j]), int32_t(lo[j]))
+                       : int32_t(rq.apply(int64_t(int32_t(hi[j])) * 256 + int64_t(int32_t(lo[j]))));
+            const int32_t p = __shfl_xor_sync(0xffffffffu, v, 1);
+            const int64_t m = mc + j;
+            if (((j < NC / 2) == even) && n < N && m < M)
+              silu_store(e, m, n >> 1, silu_combine(e.silu, even ? v : p, even ? p : v));
+          }
+          continue;
+        }
+        if (n >= N) continue;
         if (mode == EPI_ACC_I64) {
           store_column<NC>(static_cast<int64_t*>(e.y) + mc * e.ldy + n, e.ldy, mc, M, [&](int j) {
             return int64_t(int32_t(hi[j])) * 256 + int64_t(int32_t(lo[j]));

@@ -186,11 +186,22 @@ __global__ void __launch_bounds__(GEMV_THREADS)
       __syncthreads();
     }
     if (kw == 0) {
-#pragma unroll
-      for (int j = 0; j < R; ++j)
+      if (e.mode == EPI_SILU) {
+        // Rows row0 (gate) and row0 + 1 (up) of channel pair row0/2 (R == 2).
 #pragma unroll
         for (int m = 0; m < MT; ++m)
-          if (lane == ((j * MT + m) & 31) && row0 + j < N) epilogue_store(e, m, row0 + j, acc[j][m]);
+          if (R == 2 && lane == m && row0 + 1 < N) {
+            const int32_t g = int32_t(requant_value(e, row0, acc[0][m]));
+            const int32_t u = int32_t(requant_value(e, row0 + 1, acc[R - 1][m]));
+            silu_store(e, m, row0 >> 1, silu_combine(e.silu, g, u));
+          }
+      } else {
+#pragma unroll
+        for (int j = 0; j < R; ++j)
+#pragma unroll
+          for (int m = 0; m < MT; ++m)
+            if (lane == ((j * MT + m) & 31) && row0 + j < N) epilogue_store(e, m, row0 + j, acc[j][m]);
+      }
     }
   }
 }
@@ -199,6 +210,22 @@ __global__ void __launch_bounds__(GEMV_THREADS)
 // and applies the epilogue. Summation order is irrelevant (exact integers).
 __global__ void reduce_requant_kernel(const int64_t* __restrict__ part, int nsplit,
                                       int64_t slice_stride, int64_t M, int64_t N, Epilogue ep) {
+  if (ep.mode == EPI_SILU) {  // one thread per (token, channel pair)
+    const int64_t I = N / 2, total = M * I;
+    for (int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+         e += int64_t(gridDim.x) * blockDim.x) {
+      const int64_t m = e / I, i = e % I;
+      int64_t ag = 0, au = 0;
+      for (int k = 0; k < nsplit; ++k) {
+        ag += part[k * slice_stride + m * N + 2 * i];
+        au += part[k * slice_stride + m * N + 2 * i + 1];
+      }
+      const int32_t g = int32_t(requant_value(ep, 2 * i, ag));
+      const int32_t u = int32_t(requant_value(ep, 2 * i + 1, au));
+      silu_store(ep, m, i, silu_combine(ep.silu, g, u));
+    }
+    return;
+  }
   const int64_t total = M * N;
   for (int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
        e += int64_t(gridDim.x) * blockDim.x) {

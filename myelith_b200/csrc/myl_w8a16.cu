@@ -85,6 +85,17 @@ struct myl_requant {
   int mode = 0;
   int8_t* d_shift = nullptr;
   int32_t* d_mult = nullptr;
+  int32_t* d_bias = nullptr;  // rescaled bias (myl_requant_set_bias)
+};
+
+struct myl_mlp {
+  int64_t H = 0, I = 0;
+  myl_weight* w_gu = nullptr;    // [2I][H]: row 2i = gate_i, row 2i+1 = up_i
+  myl_weight* w_down = nullptr;  // [H][I]
+  int8_t* d_shift_gu = nullptr;  // [2I] signed total shifts of the gate/up rows
+  int8_t* d_shift_down = nullptr;  // [H]
+  int16_t* d_lut = nullptr;
+  int lut_hi = 0, offset = 0, s1 = 0, s2 = 0;
 };
 
 struct myl_ctx {
@@ -96,7 +107,7 @@ struct myl_ctx {
   int gemv_max_m = 4, force_split_k = 0, force_tile = 0, inject_fault = 0;
   int64_t launches = 0;
   PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-  DevBuf x, y, rq, planes, part;
+  DevBuf x, y, rq, planes, part, h, hplanes;
   // The workspace buffers are shared by every call on the context; calls on
   // different streams are ordered through this event.
   cudaEvent_t ws_event = nullptr;
@@ -430,7 +441,8 @@ static int check_device_error(myl_ctx* ctx) {
 
 // Host-pointer linear: upload x and the requant table, run, download y.
 static int host_linear(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M, int mode,
-                       int out_i32, const int8_t* shift, const int32_t* mult, void* y) {
+                       int out_i32, const int8_t* shift, const int32_t* mult, void* y,
+                       const int32_t* bias = nullptr) {
   if (!ctx || !w || (M > 0 && (!x || !y))) return fail(MYL_ERR_ARG, "null argument");
   if (M < 0) return fail(MYL_ERR_SHAPE, "M = %lld is negative", (long long)M);
   if (M == 0 || w->N == 0) return MYL_OK;
@@ -438,14 +450,17 @@ static int host_linear(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int6
   const size_t osz = out_i32 ? 4 : 2;
   TRY(ensure(ctx->x, size_t(M) * size_t(K) * 2));
   TRY(ensure(ctx->y, size_t(M) * size_t(N) * osz));
-  TRY(ensure(ctx->rq, size_t(N) * 5 + 64));
+  TRY(ensure(ctx->rq, size_t(N) * 9 + 64));
   int32_t* d_mult = reinterpret_cast<int32_t*>(ctx->rq.p);
-  int8_t* d_shift = reinterpret_cast<int8_t*>(d_mult + N);
+  int32_t* d_bias = d_mult + N;
+  int8_t* d_shift = reinterpret_cast<int8_t*>(d_bias + N);
   cudaStream_t st = ctx->stream;
   CUDA_TRY(cudaMemcpyAsync(ctx->x.p, x, size_t(M) * size_t(K) * 2, cudaMemcpyHostToDevice, st));
   CUDA_TRY(cudaMemcpyAsync(d_shift, shift, size_t(N), cudaMemcpyHostToDevice, st));
   if (mult) CUDA_TRY(cudaMemcpyAsync(d_mult, mult, size_t(N) * 4, cudaMemcpyHostToDevice, st));
+  if (bias) CUDA_TRY(cudaMemcpyAsync(d_bias, bias, size_t(N) * 4, cudaMemcpyHostToDevice, st));
   Epilogue ep{};
+  ep.bias = bias ? d_bias : nullptr;
   ep.mode = mode;
   ep.out_i32 = out_i32;
   ep.shift = d_shift;
@@ -508,7 +523,7 @@ int myl_destroy(myl_ctx* ctx) {
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   for (auto& kv : ctx->backend_cache) myl_weight_release(ctx, kv.second);
   ctx->backend_cache.clear();
-  for (DevBuf* b : {&ctx->x, &ctx->y, &ctx->rq, &ctx->planes, &ctx->part})
+  for (DevBuf* b : {&ctx->x, &ctx->y, &ctx->rq, &ctx->planes, &ctx->part, &ctx->h, &ctx->hplanes})
     if (b->p) cudaFree(b->p);
   if (ctx->d_err) cudaFree(ctx->d_err);
   if (ctx->h_err) cudaFreeHost(ctx->h_err);
@@ -690,6 +705,7 @@ int myl_requant_release(myl_ctx* ctx, myl_requant* rq) {
   if (ctx) cudaSetDevice(ctx->device);
   if (rq->d_shift) cudaFree(rq->d_shift);
   if (rq->d_mult) cudaFree(rq->d_mult);
+  if (rq->d_bias) cudaFree(rq->d_bias);
   delete rq;
   return MYL_OK;
 }
@@ -700,6 +716,7 @@ static Epilogue make_ep(const myl_requant* rq, void* y, int64_t ldy) {
   ep.out_i32 = (rq->mode == MYL_RQ_SHIFT_I32) ? 1 : 0;
   ep.shift = rq->d_shift;
   ep.mult = rq->d_mult;
+  ep.bias = rq->d_bias;
   ep.y = y;
   ep.ldy = ldy;
   return ep;
@@ -737,6 +754,204 @@ int myl_requant_acc_dev(myl_ctx* ctx, const myl_requant* rq, const int64_t* acc,
   CUDA_TRY(cudaGetLastError());
   ctx->launches++;
   return MYL_OK;
+}
+
+// linear.rs:142: rescale(b as i32, b_shift, out_frac) with the debug-build
+// overflow checks of fixed_point.rs:173-180 (i32 width).
+static int rescale_bias(const int16_t* bias, const uint8_t* bias_shifts, int64_t N, uint8_t out_frac,
+                        std::vector<int32_t>& out) {
+  out.resize(size_t(N));
+  for (int64_t i = 0; i < N; ++i) {
+    const int d = int(int8_t(bias_shifts[i])) - int(int8_t(out_frac));
+    if (d < -128 || d > 127 || d > 30 || d < -31)
+      return fail(MYL_ERR_OVERFLOW, "bias shift %u -> out_frac %u overflows i32 rescale",
+                  unsigned(bias_shifts[i]), unsigned(out_frac));
+    const int32_t b = bias[i];
+    int32_t v;
+    if (d > 0) {
+      const int32_t q = b >> d, r = b & ((1 << d) - 1), h = 1 << (d - 1);
+      v = q + ((r > h || (r == h && (q & 1))) ? 1 : 0);
+    } else if (d == 0) {
+      v = b;
+    } else {
+      v = int32_t(uint32_t(b) << (-d));
+    }
+    out[size_t(i)] = v;
+  }
+  return MYL_OK;
+}
+
+int myl_linear_w8a16_bias(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
+                          uint8_t act_frac_bits, uint8_t out_frac_bits, const int16_t* bias,
+                          const uint8_t* bias_shifts, int16_t* y) {
+  if (!ctx || !w || (w->N > 0 && (!bias || !bias_shifts))) return fail(MYL_ERR_ARG, "null argument");
+  std::vector<int8_t> s;
+  TRY(shift_plan(w, act_frac_bits, &out_frac_bits, 0, s));
+  std::vector<int32_t> b;
+  TRY(rescale_bias(bias, bias_shifts, w->N, out_frac_bits, b));
+  return host_linear(ctx, w, x, M, EPI_SHIFT, 0, s.data(), nullptr, y, b.data());
+}
+
+int myl_requant_set_bias(myl_ctx* ctx, myl_requant* rq, const int16_t* bias,
+                         const uint8_t* bias_shifts, uint8_t out_frac) {
+  if (!ctx || !rq || (rq->N > 0 && (!bias || !bias_shifts))) return fail(MYL_ERR_ARG, "null argument");
+  if (rq->mode == MYL_RQ_SHIFT_I32) return fail(MYL_ERR_ARG, "bias applies to int16 outputs only");
+  std::vector<int32_t> b;
+  TRY(rescale_bias(bias, bias_shifts, rq->N, out_frac, b));
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  if (!rq->d_bias) CUDA_TRY(cudaMalloc(&rq->d_bias, size_t(std::max<int64_t>(rq->N, 1)) * 4));
+  if (rq->N > 0) CUDA_TRY(cudaMemcpy(rq->d_bias, b.data(), size_t(rq->N) * 4, cudaMemcpyHostToDevice));
+  return MYL_OK;
+}
+
+// ---- mlp_int (kernels/src/mlp.rs:28-74) -----------------------------------------
+
+int myl_mlp_release(myl_ctx* ctx, myl_mlp* mlp) {
+  if (!mlp) return MYL_OK;
+  if (ctx) {
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    if (mlp->w_gu) myl_weight_release(ctx, mlp->w_gu);
+    if (mlp->w_down) myl_weight_release(ctx, mlp->w_down);
+  }
+  if (mlp->d_shift_gu) cudaFree(mlp->d_shift_gu);
+  if (mlp->d_shift_down) cudaFree(mlp->d_shift_down);
+  if (mlp->d_lut) cudaFree(mlp->d_lut);
+  delete mlp;
+  return MYL_OK;
+}
+
+int myl_mlp_register(myl_ctx* ctx, const int8_t* W_gate, const int8_t* W_up, const int8_t* W_down,
+                     int64_t hidden, int64_t intermediate, const uint8_t* gate_w_shifts,
+                     const uint8_t* up_w_shifts, const uint8_t* down_w_shifts,
+                     const int16_t* silu_lut, int64_t silu_lut_len, uint8_t in_frac,
+                     uint8_t gate_out_frac, uint8_t up_out_frac, uint8_t down_in_frac,
+                     uint8_t silu_in_frac, int16_t silu_lut_offset, uint8_t silu_out_frac,
+                     const uint8_t* out_frac, myl_mlp** out) {
+  if (!ctx || !out || !W_gate || !W_up || !W_down || !gate_w_shifts || !up_w_shifts ||
+      !down_w_shifts || !silu_lut || !out_frac)
+    return fail(MYL_ERR_ARG, "null argument");
+  *out = nullptr;
+  const int64_t H = hidden, I = intermediate;
+  if (H <= 0 || I <= 0) return fail(MYL_ERR_SHAPE, "mlp_int: hidden %lld / intermediate %lld",
+                                    (long long)H, (long long)I);
+  // The table index is computed in i16 (integer_math.rs:166-170): lengths the
+  // reference can index without a panic are 1 .. 32768.
+  if (silu_lut_len < 1 || silu_lut_len > 32768)
+    return fail(MYL_ERR_SHAPE, "silu_lut length %lld", (long long)silu_lut_len);
+  // Every shift the reference computes, validated as its debug build would.
+  std::vector<int8_t> sgu(static_cast<size_t>(2 * I));
+  std::vector<int8_t> sdown(static_cast<size_t>(H));
+  for (int64_t i = 0; i < I; ++i) {
+    TRY(signed_total_shift(gate_w_shifts[i], in_frac, gate_out_frac, &sgu[size_t(2 * i)]));
+    TRY(signed_total_shift(up_w_shifts[i], in_frac, up_out_frac, &sgu[size_t(2 * i + 1)]));
+  }
+  for (int64_t r = 0; r < H; ++r)
+    TRY(signed_total_shift(down_w_shifts[r], down_in_frac, out_frac[r], &sdown[size_t(r)]));
+  const int s1 = int(int8_t(gate_out_frac)) - int(int8_t(silu_in_frac));
+  if (s1 > 30 || s1 < -31) return fail(MYL_ERR_OVERFLOW, "gate_out_frac -> silu_in_frac shift %d", s1);
+  const unsigned prod_frac = unsigned(silu_out_frac) + unsigned(up_out_frac);
+  if (prod_frac > 255u) return fail(MYL_ERR_OVERFLOW, "silu_out_frac + up_out_frac overflows u8");
+  int8_t s2 = 0;
+  TRY(signed_total_shift(uint8_t(prod_frac), 0, down_in_frac, &s2));
+  // Interleave gate and up rows: row 2i = gate_i, row 2i + 1 = up_i.
+  std::vector<int8_t> wgu(size_t(2 * I) * size_t(H));
+  std::vector<uint8_t> gu_shifts(size_t(2 * I));
+  for (int64_t i = 0; i < I; ++i) {
+    std::memcpy(&wgu[size_t(2 * i) * size_t(H)], W_gate + i * H, size_t(H));
+    std::memcpy(&wgu[size_t(2 * i + 1) * size_t(H)], W_up + i * H, size_t(H));
+    gu_shifts[size_t(2 * i)] = gate_w_shifts[i];
+    gu_shifts[size_t(2 * i + 1)] = up_w_shifts[i];
+  }
+  myl_mlp* m = new myl_mlp();
+  m->H = H;
+  m->I = I;
+  m->lut_hi = int(int16_t(uint16_t(uint16_t(silu_lut_len) - 1u)));
+  m->offset = silu_lut_offset;
+  m->s1 = s1;
+  m->s2 = s2;
+  int rc = myl_weight_register(ctx, wgu.data(), 2 * I, H, H, gu_shifts.data(), &m->w_gu);
+  if (rc == MYL_OK) rc = myl_weight_register(ctx, W_down, H, I, I, down_w_shifts, &m->w_down);
+  if (rc == MYL_OK &&
+      (cudaMalloc(&m->d_shift_gu, size_t(2 * I)) != cudaSuccess ||
+       cudaMalloc(&m->d_shift_down, size_t(H)) != cudaSuccess ||
+       cudaMalloc(&m->d_lut, size_t(silu_lut_len) * 2) != cudaSuccess ||
+       cudaMemcpy(m->d_shift_gu, sgu.data(), size_t(2 * I), cudaMemcpyHostToDevice) != cudaSuccess ||
+       cudaMemcpy(m->d_shift_down, sdown.data(), size_t(H), cudaMemcpyHostToDevice) != cudaSuccess ||
+       cudaMemcpy(m->d_lut, silu_lut, size_t(silu_lut_len) * 2, cudaMemcpyHostToDevice) != cudaSuccess))
+    rc = fail(MYL_ERR_CUDA, "mlp upload failed");
+  if (rc != MYL_OK) {
+    myl_mlp_release(ctx, m);
+    return rc;
+  }
+  *out = m;
+  return MYL_OK;
+}
+
+static int run_mlp(myl_ctx* ctx, const myl_mlp* mlp, const int16_t* x, int64_t M, int64_t ldx,
+                   int16_t* y, int64_t ldy, cudaStream_t st) {
+  if (M == 0) return MYL_OK;
+  const int64_t I = mlp->I;
+  Epilogue ep_gu{};
+  ep_gu.mode = EPI_SILU;
+  ep_gu.shift = mlp->d_shift_gu;
+  ep_gu.silu.lut = mlp->d_lut;
+  ep_gu.silu.lut_hi = mlp->lut_hi;
+  ep_gu.silu.offset = mlp->offset;
+  ep_gu.silu.s1 = mlp->s1;
+  ep_gu.silu.s2 = mlp->s2;
+  Epilogue ep_down{};
+  ep_down.mode = EPI_SHIFT;
+  ep_down.shift = mlp->d_shift_down;
+  ep_down.y = y;
+  ep_down.ldy = ldy;
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  TRY(ws_acquire(ctx, st));
+  if (M <= ctx->gemv_max_m && M <= 4) {
+    // Decode: GEMV with the SiLU pair epilogue writes h [M][I]; GEMV down.
+    TRY(ensure(ctx->h, size_t(M) * size_t(I) * 2));
+    ep_gu.y = ctx->h.p;
+    ep_gu.ldy = I;
+    TRY(launch_gemv(ctx, mlp->w_gu, x, M, ldx, ep_gu, st));
+    TRY(launch_gemv(ctx, mlp->w_down, static_cast<const int16_t*>(ctx->h.p), M, I, ep_down, st));
+  } else {
+    // Prefill: the gate/up GEMM writes h straight into the byte planes the
+    // down GEMM reads; h itself never goes to memory as int16.
+    const int64_t ldp_h = mlp->w_down->ldp;
+    TRY(ensure(ctx->hplanes, size_t(2) * size_t(M) * size_t(ldp_h)));
+    int8_t* hhi = static_cast<int8_t*>(ctx->hplanes.p);
+    uint8_t* hlo = reinterpret_cast<uint8_t*>(hhi + M * ldp_h);
+    ep_gu.y = nullptr;  // only the planes are needed
+    ep_gu.ldy = I;
+    ep_gu.silu.h_hi = hhi;
+    ep_gu.silu.h_lo = hlo;
+    ep_gu.silu.ldp = ldp_h;
+    TRY(launch_tc(ctx, mlp->w_gu, x, M, ldx, ep_gu, st));
+    TRY(launch_tc_planes(ctx, mlp->w_down, hhi, hlo, ldp_h, M, ep_down, st));
+  }
+  return ws_release(ctx, st);
+}
+
+int myl_mlp_dev(myl_ctx* ctx, const myl_mlp* mlp, const int16_t* x, int64_t M, int64_t ldx,
+                int16_t* y, int64_t ldy, void* stream) {
+  if (!ctx || !mlp || (M > 0 && (!x || !y))) return fail(MYL_ERR_ARG, "null argument");
+  if (M < 0 || ldx < mlp->H || ldy < mlp->H) return fail(MYL_ERR_SHAPE, "bad M/ldx/ldy");
+  return run_mlp(ctx, mlp, x, M, ldx, y, ldy, static_cast<cudaStream_t>(stream));
+}
+
+int myl_mlp_int(myl_ctx* ctx, const myl_mlp* mlp, const int16_t* x, int64_t M, int16_t* y) {
+  if (!ctx || !mlp || (M > 0 && (!x || !y))) return fail(MYL_ERR_ARG, "null argument");
+  if (M < 0) return fail(MYL_ERR_SHAPE, "M = %lld is negative", (long long)M);
+  if (M == 0) return MYL_OK;
+  const int64_t H = mlp->H;
+  TRY(ensure(ctx->x, size_t(M) * size_t(H) * 2));
+  TRY(ensure(ctx->y, size_t(M) * size_t(H) * 2));
+  cudaStream_t st = ctx->stream;
+  CUDA_TRY(cudaMemcpyAsync(ctx->x.p, x, size_t(M) * size_t(H) * 2, cudaMemcpyHostToDevice, st));
+  TRY(run_mlp(ctx, mlp, static_cast<const int16_t*>(ctx->x.p), M, H, static_cast<int16_t*>(ctx->y.p),
+              H, st));
+  CUDA_TRY(cudaMemcpyAsync(y, ctx->y.p, size_t(M) * size_t(H) * 2, cudaMemcpyDeviceToHost, st));
+  return check_device_error(ctx);
 }
 
 int myl_split_hilo_dev(myl_ctx* ctx, const int16_t* x, int64_t M, int64_t K, int64_t ldx,
