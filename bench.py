@@ -163,6 +163,7 @@ def cpu_sample_tops(target_s: float, rng) -> dict:
             O.linear_w8a16(x, W, K, s, ACT_FRAC, OUT_FRAC)
         return time.perf_counter() - t0
 
+    O.set_num_threads(os.cpu_count() or 1)  # torchrun sets OMP_NUM_THREADS=1 per process
     run(1)  # warm-up (page-in, thread pool)
     t1 = run(1)
     rows = max(1, min(M_HEAD, int(target_s / max(t1, 1e-6))))

@@ -177,6 +177,16 @@ int myl_mlp_int(myl_ctx* ctx, const myl_mlp* mlp, const int16_t* x, int64_t M, i
 int myl_mlp_dev(myl_ctx* ctx, const myl_mlp* mlp, const int16_t* x, int64_t M, int64_t ldx,
                 int16_t* y, int64_t ldy, void* stream);
 
+/* Tensor parallelism over intermediate channels: a rank registers its slice
+ * (gate/up rows and down columns of channels [i0, i1)) and gets the exact
+ * int64 down-projection partial sums; the caller adds them across ranks and
+ * applies the down requant once (myl_mlp_requant_dev), so the result is
+ * bit-identical to the unsharded mlp_int. */
+int myl_mlp_partial_dev(myl_ctx* ctx, const myl_mlp* mlp, const int16_t* x, int64_t M, int64_t ldx,
+                        int64_t* acc, void* stream);
+int myl_mlp_requant_dev(myl_ctx* ctx, const myl_mlp* mlp, const int64_t* acc, int64_t M, int16_t* y,
+                        int64_t ldy, void* stream);
+
 /* Waits for the context's work and reports kernel-side errors (bounded waits
  * that ran out) as MYL_ERR_DEVICE; the context stays usable afterwards. */
 int myl_synchronize(myl_ctx* ctx);

@@ -100,6 +100,8 @@ def load_library(path: str | None = None):
             "myl_mlp_release": ([vp, vp], i32),
             "myl_mlp_int": ([vp, vp, vp, i64, vp], i32),
             "myl_mlp_dev": ([vp, vp, vp, i64, i64, vp, i64, vp], i32),
+            "myl_mlp_partial_dev": ([vp, vp, vp, i64, i64, vp, vp], i32),
+            "myl_mlp_requant_dev": ([vp, vp, vp, i64, vp, i64, vp], i32),
             "myl_synchronize": ([vp], i32),
             "myl_set_wait_timeout_ns": ([vp, C.c_uint64], i32),
             "myl_set_dispatch": ([vp, i32, i32, i32], i32),
@@ -406,6 +408,15 @@ class Mlp:
         _check("myl_mlp_dev", load_library().myl_mlp_dev(
             self.ctx.handle, self._h, _p(x), x.shape[0], x.stride(0), _p(y), y.stride(0),
             _stream_ptr(stream)))
+
+    def partial_dev(self, x, acc, stream=None) -> None:
+        """acc [M, hidden] int64: exact down-projection sums of this slice."""
+        _check("myl_mlp_partial_dev", load_library().myl_mlp_partial_dev(
+            self.ctx.handle, self._h, _p(x), x.shape[0], x.stride(0), _p(acc), _stream_ptr(stream)))
+
+    def requant_dev(self, acc, y, stream=None) -> None:
+        _check("myl_mlp_requant_dev", load_library().myl_mlp_requant_dev(
+            self.ctx.handle, self._h, _p(acc), acc.shape[0], _p(y), y.stride(0), _stream_ptr(stream)))
 
 
 def _stream_ptr(stream) -> int | None:

@@ -888,8 +888,10 @@ int myl_mlp_register(myl_ctx* ctx, const int8_t* W_gate, const int8_t* W_up, con
   return MYL_OK;
 }
 
+// y != nullptr: requantised output; otherwise acc receives the exact int64
+// down-projection sums (tensor-parallel partials).
 static int run_mlp(myl_ctx* ctx, const myl_mlp* mlp, const int16_t* x, int64_t M, int64_t ldx,
-                   int16_t* y, int64_t ldy, cudaStream_t st) {
+                   int16_t* y, int64_t ldy, cudaStream_t st, int64_t* acc = nullptr) {
   if (M == 0) return MYL_OK;
   const int64_t I = mlp->I;
   Epilogue ep_gu{};
@@ -901,10 +903,10 @@ static int run_mlp(myl_ctx* ctx, const myl_mlp* mlp, const int16_t* x, int64_t M
   ep_gu.silu.s1 = mlp->s1;
   ep_gu.silu.s2 = mlp->s2;
   Epilogue ep_down{};
-  ep_down.mode = EPI_SHIFT;
+  ep_down.mode = acc ? EPI_ACC_I64 : EPI_SHIFT;
   ep_down.shift = mlp->d_shift_down;
-  ep_down.y = y;
-  ep_down.ldy = ldy;
+  ep_down.y = acc ? static_cast<void*>(acc) : static_cast<void*>(y);
+  ep_down.ldy = acc ? mlp->H : ldy;
   CUDA_TRY(cudaSetDevice(ctx->device));
   TRY(ws_acquire(ctx, st));
   if (M <= ctx->gemv_max_m && M <= 4) {
@@ -937,6 +939,32 @@ int myl_mlp_dev(myl_ctx* ctx, const myl_mlp* mlp, const int16_t* x, int64_t M, i
   if (!ctx || !mlp || (M > 0 && (!x || !y))) return fail(MYL_ERR_ARG, "null argument");
   if (M < 0 || ldx < mlp->H || ldy < mlp->H) return fail(MYL_ERR_SHAPE, "bad M/ldx/ldy");
   return run_mlp(ctx, mlp, x, M, ldx, y, ldy, static_cast<cudaStream_t>(stream));
+}
+
+int myl_mlp_partial_dev(myl_ctx* ctx, const myl_mlp* mlp, const int16_t* x, int64_t M, int64_t ldx,
+                        int64_t* acc, void* stream) {
+  if (!ctx || !mlp || (M > 0 && (!x || !acc))) return fail(MYL_ERR_ARG, "null argument");
+  if (M < 0 || ldx < mlp->H) return fail(MYL_ERR_SHAPE, "bad M/ldx");
+  return run_mlp(ctx, mlp, x, M, ldx, nullptr, 0, static_cast<cudaStream_t>(stream), acc);
+}
+
+int myl_mlp_requant_dev(myl_ctx* ctx, const myl_mlp* mlp, const int64_t* acc, int64_t M, int16_t* y,
+                        int64_t ldy, void* stream) {
+  if (!ctx || !mlp || (M > 0 && (!acc || !y))) return fail(MYL_ERR_ARG, "null argument");
+  if (M < 0 || ldy < mlp->H) return fail(MYL_ERR_SHAPE, "bad M/ldy");
+  if (M == 0) return MYL_OK;
+  Epilogue ep{};
+  ep.mode = EPI_SHIFT;
+  ep.shift = mlp->d_shift_down;
+  ep.y = y;
+  ep.ldy = ldy;
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  const int64_t total = M * mlp->H;
+  unsigned blocks = unsigned(std::min<int64_t>((total + 255) / 256, int64_t(ctx->num_sms) * 8));
+  reduce_requant_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(acc, 1, 0, M, mlp->H, ep);
+  CUDA_TRY(cudaGetLastError());
+  ctx->launches++;
+  return MYL_OK;
 }
 
 int myl_mlp_int(myl_ctx* ctx, const myl_mlp* mlp, const int16_t* x, int64_t M, int16_t* y) {

@@ -1,0 +1,219 @@
+"""Megatron-style tensor parallelism for the W8A16 path (one process per GPU).
+
+The reference distributes only by layer ranges over TCP
+(INTEGER_LLM/pipeline/src/stage.rs:94); inside a layer everything is one
+dot product per output element (kernels/src/linear.rs:61-68). Splitting a
+layer across GPUs keeps the result bit-identical because the accumulator is an
+exact integer:
+
+  column-parallel  rank r owns output rows [lo_r, hi_r): its outputs are final
+                   (same requant per row), no exchange;
+  row-parallel     rank r owns input columns [lo_r, hi_r): it produces exact
+                   int64 partial sums, the ranks add them (all-reduce, int64,
+                   SUM; integer addition is associative) and the requant and
+                   clamp run once, after the sum, as the reference's clamp at
+                   the very end requires (fixed_point.rs:184-191);
+  MLP              gate/up column-parallel and down row-parallel over the same
+                   intermediate channels, so h never leaves its rank.
+
+int32 is not wide enough for the partial sums (up to ~1e10 for 7B shapes).
+
+The per-rank arithmetic is behind ``Local``: ``LibLocal`` calls the sm_100a
+kernels (torch CUDA tensors, NCCL); tests can supply another implementation
+of the same three methods to run the sharding and exchange logic with gloo on
+CPU.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+
+
+def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
+    """[lo, hi) of rank's share of n items: equal parts, the first n % world
+    ranks take one more."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} of {world}")
+    base, extra = divmod(n, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+class Local:
+    """Per-rank arithmetic used by the tensor-parallel layers. The layers hand
+    their shards over with add_linear / add_mlp and then call linear / acc /
+    requant with the same key."""
+
+    def add_linear(self, key, W, in_features, w_shifts, act_frac, out_frac):
+        raise NotImplementedError
+
+    def add_mlp(self, key, args: dict):  # ParallelMlp.args of this rank's slice
+        raise NotImplementedError
+
+    def linear(self, key, x):  # requantised output of a weight shard
+        raise NotImplementedError
+
+    def acc(self, key, x):  # exact int64 partial sums of a weight shard
+        raise NotImplementedError
+
+    def requant(self, key, acc):  # requant of summed int64 accumulators
+        raise NotImplementedError
+
+
+@dataclass
+class LinearSpec:
+    """One W8A16 linear: W [N][K] int8 (host), one shift per row, scales."""
+
+    W: np.ndarray
+    w_shifts: np.ndarray
+    act_frac: int
+    out_frac: object  # int, or per-channel array (linear_w8a16_pc)
+
+
+class LibLocal(Local):
+    """The sm_100a kernels through libmyl_w8a16 (torch CUDA tensors)."""
+
+    def __init__(self, ctx):
+        import torch
+
+        self.ctx = ctx
+        self.torch = torch
+        self.weights = {}
+        self.plans = {}
+        self.mlps = {}
+
+    def add_linear(self, key, W, in_features, w_shifts, act_frac, out_frac):
+        import myelith_b200 as myl
+
+        w = myl.Weight(self.ctx, W, in_features, w_shifts)
+        self.weights[key] = w
+        self.plans[key] = w.requant(myl.RQ_SHIFT_I16, act_frac, out_frac)
+
+    def add_mlp(self, key, a: dict):
+        import myelith_b200 as myl
+
+        self.mlps[key] = myl.Mlp(self.ctx, a["W_gate"], a["W_up"], a["W_down"], a["hidden"],
+                                 a["intermediate"], a["gate_w_shifts"], a["up_w_shifts"],
+                                 a["down_w_shifts"], a["silu_lut"], a["in_frac"], a["gate_out_frac"],
+                                 a["up_out_frac"], a["down_in_frac"], a["silu_in_frac"],
+                                 a["silu_lut_offset"], a["silu_out_frac"], a["out_frac"])
+
+    def linear(self, key, x):
+        w = self.weights[key]
+        y = self.torch.empty((x.shape[0], w.out_features), dtype=self.torch.int16, device=x.device)
+        w.linear_dev(self.plans[key], x, y)
+        return y
+
+    def acc(self, key, x):
+        if key in self.mlps:
+            m = self.mlps[key]
+            acc = self.torch.empty((x.shape[0], m.hidden), dtype=self.torch.int64, device=x.device)
+            m.partial_dev(x, acc)
+            return acc
+        w = self.weights[key]
+        acc = self.torch.empty((x.shape[0], w.out_features), dtype=self.torch.int64, device=x.device)
+        w.linear_acc_dev(x, acc)
+        return acc
+
+    def requant(self, key, acc):
+        y = self.torch.empty(acc.shape, dtype=self.torch.int16, device=acc.device)
+        if key in self.mlps:
+            self.mlps[key].requant_dev(acc, y)
+        else:
+            self.plans[key].apply_acc_dev(acc, y)
+        return y
+
+
+class ColumnParallelLinear:
+    """Rank owns output rows [lo, hi) of W; y shard = linear of those rows."""
+
+    def __init__(self, local: Local, key, spec: LinearSpec, rank: int, world: int, group=None):
+        N, K = spec.W.shape
+        self.lo, self.hi = shard_range(N, rank, world)
+        self.local, self.key, self.group, self.world = local, key, group, world
+        self.N = N
+        of = spec.out_frac
+        of_shard = of if np.ndim(of) == 0 else np.asarray(of)[self.lo:self.hi]
+        local.add_linear(key, np.ascontiguousarray(spec.W[self.lo:self.hi]), K,
+                         np.asarray(spec.w_shifts)[self.lo:self.hi], spec.act_frac, of_shard)
+
+    def __call__(self, x):
+        return self.local.linear(self.key, x)
+
+    def gather(self, x):
+        """Full output [M][N] on every rank (all-gather of the shards)."""
+        import torch
+        import torch.distributed as dist
+
+        y = self(x)
+        if self.world == 1:
+            return y
+        # all_gather wants equal sizes: pad every shard to the widest one.
+        ranges = [shard_range(self.N, r, self.world) for r in range(self.world)]
+        width = max(b - a for a, b in ranges)
+        mine = torch.zeros((x.shape[0], width), dtype=y.dtype, device=y.device)
+        mine[:, : y.shape[1]] = y
+        # NCCL and gloo have no int16 type: move the shards as bytes.
+        raw = mine.view(torch.uint8)
+        parts = [torch.empty_like(raw) for _ in range(self.world)]
+        dist.all_gather(parts, raw, group=self.group)
+        return torch.cat([p.view(y.dtype)[:, : b - a] for p, (a, b) in zip(parts, ranges)], dim=1)
+
+
+class RowParallelLinear:
+    """Rank owns input columns [lo, hi) of W; all ranks get the full output:
+    int64 partials -> all-reduce (SUM) -> one requant."""
+
+    def __init__(self, local: Local, key, spec: LinearSpec, rank: int, world: int, group=None):
+        N, K = spec.W.shape
+        self.lo, self.hi = shard_range(K, rank, world)
+        self.local, self.key, self.group, self.world = local, key, group, world
+        # The column slice keeps every row, so the per-row shifts and the
+        # requant plan are those of the full weight.
+        local.add_linear(key, np.ascontiguousarray(spec.W[:, self.lo:self.hi]), self.hi - self.lo,
+                         spec.w_shifts, spec.act_frac, spec.out_frac)
+
+    def x_shard(self, x):
+        return x[:, self.lo:self.hi].contiguous()
+
+    def __call__(self, x_shard):
+        import torch.distributed as dist
+
+        acc = self.local.acc(self.key, x_shard)
+        if self.world > 1:
+            dist.all_reduce(acc, op=dist.ReduceOp.SUM, group=self.group)
+        return self.local.requant(self.key, acc)
+
+
+class ParallelMlp:
+    """mlp_int (kernels/src/mlp.rs:28-74) over intermediate channels [lo, hi):
+    gate/up rows and down columns of the same channels stay on one rank, the
+    down projection's int64 partials are all-reduced, the requant runs once."""
+
+    def __init__(self, local: Local, key, W_gate, W_up, W_down, hidden, intermediate,
+                 gate_w_shifts, up_w_shifts, down_w_shifts, silu_lut, in_frac, gate_out_frac,
+                 up_out_frac, down_in_frac, silu_in_frac, silu_lut_offset, silu_out_frac, out_frac,
+                 rank: int, world: int, group=None):
+        self.lo, self.hi = shard_range(intermediate, rank, world)
+        self.local, self.key, self.group, self.world = local, key, group, world
+        lo, hi = self.lo, self.hi
+        self.args = dict(
+            W_gate=np.ascontiguousarray(np.asarray(W_gate).reshape(intermediate, hidden)[lo:hi]),
+            W_up=np.ascontiguousarray(np.asarray(W_up).reshape(intermediate, hidden)[lo:hi]),
+            W_down=np.ascontiguousarray(np.asarray(W_down).reshape(hidden, intermediate)[:, lo:hi]),
+            hidden=hidden, intermediate=hi - lo,
+            gate_w_shifts=np.asarray(gate_w_shifts)[lo:hi], up_w_shifts=np.asarray(up_w_shifts)[lo:hi],
+            down_w_shifts=np.asarray(down_w_shifts), silu_lut=silu_lut, in_frac=in_frac,
+            gate_out_frac=gate_out_frac, up_out_frac=up_out_frac, down_in_frac=down_in_frac,
+            silu_in_frac=silu_in_frac, silu_lut_offset=silu_lut_offset, silu_out_frac=silu_out_frac,
+            out_frac=np.asarray(out_frac))
+        local.add_mlp(key, self.args)
+
+    def __call__(self, x):
+        import torch.distributed as dist
+
+        acc = self.local.acc(self.key, x)
+        if self.world > 1:
+            dist.all_reduce(acc, op=dist.ReduceOp.SUM, group=self.group)
+        return self.local.requant(self.key, acc)

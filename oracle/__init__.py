@@ -77,6 +77,8 @@ def lib():
         L.mylo_lut_lookup.restype = C.c_int16
         L.mylo_mlp_int.argtypes = [p, i64, p, p, p, i64, i64, p, p, p, p, i64,
                                    u8, u8, u8, u8, u8, C.c_int16, u8, p, p, p]
+        L.mylo_mlp_hidden.argtypes = [p, i64, p, p, i64, i64, p, p, p, i64,
+                                      u8, u8, u8, u8, u8, C.c_int16, u8, p, p]
         L.mylo_argmax_i32.argtypes = [p, i64]
         L.mylo_argmax_i32.restype = i64
         L.mylo_splitmix64.argtypes = [C.c_uint64, p]
@@ -268,6 +270,27 @@ def mlp_int(x, W_gate, W_up, W_down, hidden_size: int, intermediate_size: int,
         silu_lut_offset, silu_out_frac, _ptr(of), _ptr(y), _ptr(wraps)))
     out = y[0] if single else y
     return (out, int(wraps[0])) if return_wraps else out
+
+
+def mlp_hidden(x, W_gate, W_up, hidden_size: int, intermediate_size: int, gate_w_shifts,
+               up_w_shifts, silu_lut, in_frac_bits: int, gate_out_frac: int, up_out_frac: int,
+               down_in_frac: int, silu_in_frac: int, silu_lut_offset: int,
+               silu_out_frac: int) -> np.ndarray:
+    """mlp.rs:49-64: h [M, I], the input of the down projection."""
+    H, I = hidden_size, intermediate_size
+    Wg = _c(W_gate, np.int8).reshape(-1)
+    Wu = _c(W_up, np.int8).reshape(-1)
+    gs, us = _c(gate_w_shifts, np.uint8), _c(up_w_shifts, np.uint8)
+    lut = _c(silu_lut, np.int16)
+    if Wg.size != H * I or Wu.size != H * I or gs.size != I or us.size != I:
+        raise OracleError("mlp_hidden", ERR_SHAPE)
+    xs, single = _rows(x, H)
+    h = np.zeros((xs.shape[0], I), np.int16)
+    _check("mlp_hidden", lib().mylo_mlp_hidden(
+        _ptr(xs), xs.shape[0], _ptr(Wg), _ptr(Wu), H, I, _ptr(gs), _ptr(us), _ptr(lut), lut.size,
+        in_frac_bits, gate_out_frac, up_out_frac, down_in_frac, silu_in_frac, silu_lut_offset,
+        silu_out_frac, _ptr(h), None))
+    return h[0] if single else h
 
 
 def argmax_int(values) -> int:

@@ -271,20 +271,18 @@ int16_t mylo_lut_lookup(int16_t x, const int16_t* lut, int64_t lut_len, uint8_t 
   return lut[idx];
 }
 
-/* ---- mlp.rs:28-74 on M rows --------------------------------------------- */
+/* ---- mlp.rs:49-64 on M rows: the hidden activation h ---------------------- */
 
-int mylo_mlp_int(const int16_t* x, int64_t M, const int8_t* W_gate, const int8_t* W_up,
-                 const int8_t* W_down, int64_t H, int64_t I, const uint8_t* gate_w_shifts,
-                 const uint8_t* up_w_shifts, const uint8_t* down_w_shifts,
-                 const int16_t* silu_lut, int64_t silu_lut_len, uint8_t in_frac,
-                 uint8_t gate_out_frac, uint8_t up_out_frac, uint8_t down_in_frac,
-                 uint8_t silu_in_frac, int16_t silu_lut_offset, uint8_t silu_out_frac,
-                 const uint8_t* out_frac, int16_t* y, int64_t* silu_wraps) {
+int mylo_mlp_hidden(const int16_t* x, int64_t M, const int8_t* W_gate, const int8_t* W_up,
+                    int64_t H, int64_t I, const uint8_t* gate_w_shifts, const uint8_t* up_w_shifts,
+                    const int16_t* silu_lut, int64_t silu_lut_len, uint8_t in_frac,
+                    uint8_t gate_out_frac, uint8_t up_out_frac, uint8_t down_in_frac,
+                    uint8_t silu_in_frac, int16_t silu_lut_offset, uint8_t silu_out_frac,
+                    int16_t* h, int64_t* silu_wraps) {
   int rc;
   if (M < 0 || H <= 0 || I <= 0 || silu_lut_len <= 0) return MYLO_ERR_SHAPE;
   if ((rc = check_linear(M, H, I, gate_w_shifts, in_frac, NULL, gate_out_frac))) return rc;
   if ((rc = check_linear(M, H, I, up_w_shifts, in_frac, NULL, up_out_frac))) return rc;
-  if ((rc = check_linear(M, I, H, down_w_shifts, down_in_frac, out_frac, 0))) return rc;
   int s;
   if (signed_shift(gate_out_frac, silu_in_frac, 32, &s)) return MYLO_ERR_OVERFLOW;
   uint8_t prod_frac;
@@ -293,7 +291,6 @@ int mylo_mlp_int(const int16_t* x, int64_t M, const int8_t* W_gate, const int8_t
 
   int16_t* gate = (int16_t*)malloc(sizeof(int16_t) * (size_t)(M * I));
   int16_t* up = (int16_t*)malloc(sizeof(int16_t) * (size_t)(M * I));
-  int16_t* h = (int16_t*)malloc(sizeof(int16_t) * (size_t)(M * I));
   linear_rows(x, M, W_gate, H, I, gate_w_shifts, in_frac, NULL, gate_out_frac, gate);
   linear_rows(x, M, W_up, H, I, up_w_shifts, in_frac, NULL, up_out_frac, up);
   int64_t wraps = 0;
@@ -309,12 +306,31 @@ int mylo_mlp_int(const int16_t* x, int64_t M, const int8_t* W_gate, const int8_t
     mylo_rescale_i64(prod, prod_frac, down_in_frac, &v);
     h[e] = mylo_clamp_i16_from_i64(v);
   }
-  linear_rows(h, M, W_down, I, H, down_w_shifts, down_in_frac, out_frac, 0, y);
   free(gate);
   free(up);
-  free(h);
   if (silu_wraps) *silu_wraps = wraps;
   return MYLO_OK;
+}
+
+/* ---- mlp.rs:28-74 on M rows --------------------------------------------- */
+
+int mylo_mlp_int(const int16_t* x, int64_t M, const int8_t* W_gate, const int8_t* W_up,
+                 const int8_t* W_down, int64_t H, int64_t I, const uint8_t* gate_w_shifts,
+                 const uint8_t* up_w_shifts, const uint8_t* down_w_shifts,
+                 const int16_t* silu_lut, int64_t silu_lut_len, uint8_t in_frac,
+                 uint8_t gate_out_frac, uint8_t up_out_frac, uint8_t down_in_frac,
+                 uint8_t silu_in_frac, int16_t silu_lut_offset, uint8_t silu_out_frac,
+                 const uint8_t* out_frac, int16_t* y, int64_t* silu_wraps) {
+  int rc;
+  if (M < 0 || H <= 0 || I <= 0 || silu_lut_len <= 0) return MYLO_ERR_SHAPE;
+  if ((rc = check_linear(M, I, H, down_w_shifts, down_in_frac, out_frac, 0))) return rc;
+  int16_t* h = (int16_t*)malloc(sizeof(int16_t) * (size_t)(M * I) + 1);
+  rc = mylo_mlp_hidden(x, M, W_gate, W_up, H, I, gate_w_shifts, up_w_shifts, silu_lut, silu_lut_len,
+                       in_frac, gate_out_frac, up_out_frac, down_in_frac, silu_in_frac,
+                       silu_lut_offset, silu_out_frac, h, silu_wraps);
+  if (rc == MYLO_OK) linear_rows(h, M, W_down, I, H, down_w_shifts, down_in_frac, out_frac, 0, y);
+  free(h);
+  return rc;
 }
 
 /* ---- sampling.rs:8-18 ---------------------------------------------------- */

@@ -15,7 +15,8 @@
  *   fixed_point.rs:173-191 rescale{,_i64}  dot.rs:403-409        dot_scalar
  *   linear.rs:43-70        linear_w8a16    linear.rs:87-119      linear_w8a16_pc
  *   linear.rs:132-145      add_bias_i16    integer_math.rs:166   lut_lookup
- *   mlp.rs:28-74           mlp_int         runtime/src/model.rs:297-307 LM head (i32 clamp)
+ *   mlp.rs:28-74           mlp_int (mlp.rs:49-64 mlp_hidden)
+ *   runtime/src/model.rs:297-307 LM head (i32 clamp)
  *   sampling.rs:8-18       argmax_int      prng.rs:7-15          splitmix64
  *
  * Where the reference panics (Rust debug build: shape assert, integer
@@ -109,6 +110,14 @@ int mylo_mlp_int(const int16_t* x, int64_t M, const int8_t* W_gate, const int8_t
                  uint8_t gate_out_frac, uint8_t up_out_frac, uint8_t down_in_frac,
                  uint8_t silu_in_frac, int16_t silu_lut_offset, uint8_t silu_out_frac,
                  const uint8_t* out_frac, int16_t* y, int64_t* silu_wraps);
+
+/* mlp.rs:49-64: the hidden activation h [M][I] (input of the down projection). */
+int mylo_mlp_hidden(const int16_t* x, int64_t M, const int8_t* W_gate, const int8_t* W_up,
+                    int64_t H, int64_t I, const uint8_t* gate_w_shifts, const uint8_t* up_w_shifts,
+                    const int16_t* silu_lut, int64_t silu_lut_len, uint8_t in_frac,
+                    uint8_t gate_out_frac, uint8_t up_out_frac, uint8_t down_in_frac,
+                    uint8_t silu_in_frac, int16_t silu_lut_offset, uint8_t silu_out_frac,
+                    int16_t* h, int64_t* silu_wraps);
 
 /* sampling.rs:8-18: first index of the maximum. */
 int64_t mylo_argmax_i32(const int32_t* v, int64_t n);
