@@ -187,6 +187,73 @@ int myl_mlp_partial_dev(myl_ctx* ctx, const myl_mlp* mlp, const int16_t* x, int6
 int myl_mlp_requant_dev(myl_ctx* ctx, const myl_mlp* mlp, const int64_t* acc, int64_t M, int16_t* y,
                         int64_t ldy, void* stream);
 
+/* --- MoE layer --------------------------------------------------------------------
+ * No counterpart in the reference, which has no MoE; the layer is composed of
+ * its primitives only:
+ *   logits[t][e] = clamp_i32(rescale_i64(dot(W_router[e], x[t]),
+ *                  router_w_shifts[e] + router_in_frac, router_frac))
+ *                  (the LM-head linear, runtime/src/model.rs:297-307)
+ *   topk[t]      = k times argmax over the experts not yet chosen, ties to the
+ *                  lowest index (sampling.rs:8-18)
+ *   p[t][j]      = softmax_int(logits[t][topk[t]], exp_lut, exp_lut_shift,
+ *                  prob_frac)                        (softmax.rs:24-64)
+ *   y[t][j]      = mlp_int(x[t], expert topk[t][j])  (mlp.rs:28-74)
+ *   out[t][h]    = clamp_i16(rescale_i64(sum_j p[t][j] * y[t][j][h], prob_frac, 0)
+ *                  + shared[t][h])   shared = mlp_int of the shared expert, or 0
+ * The experts share the scalar fractions and SiLU table; shifts are per channel.
+ * Expert weights: W_gate / W_up [num_local][intermediate][hidden], W_down
+ * [num_local][hidden][intermediate], gate/up_w_shifts [num_local][intermediate],
+ * down_w_shifts and out_frac [num_local][hidden]; the object holds experts
+ * [first_expert, first_expert + num_local) of num_experts (expert parallelism:
+ * the router covers all num_experts, each rank holds its share).
+ * Limits: top_k <= 8, num_experts <= 256, and every exp_lut entry times
+ * 2^prob_frac inside i32 (where softmax_int's i32 product never overflows). */
+typedef struct myl_moe myl_moe;
+typedef struct myl_moe_spec {
+  int64_t hidden, intermediate, num_experts, top_k, first_expert, num_local;
+  /* router */
+  const int8_t* W_router;          /* [num_experts][hidden] */
+  const uint8_t* router_w_shifts;  /* [num_experts] */
+  uint8_t router_in_frac, router_frac;
+  const int16_t* exp_lut;
+  int64_t exp_lut_len;
+  uint8_t exp_lut_shift, prob_frac;
+  /* experts (mlp_int parameters, see above) */
+  const int8_t *W_gate, *W_up, *W_down;
+  const uint8_t *gate_w_shifts, *up_w_shifts, *down_w_shifts, *out_frac;
+  const int16_t* silu_lut;
+  int64_t silu_lut_len;
+  uint8_t in_frac, gate_out_frac, up_out_frac, down_in_frac, silu_in_frac, silu_out_frac;
+  int16_t silu_lut_offset;
+  /* shared expert: borrowed, may be NULL; it must outlive the MoE object */
+  const myl_mlp* shared;
+} myl_moe_spec;
+int myl_moe_register(myl_ctx* ctx, const myl_moe_spec* spec, myl_moe** out);
+int myl_moe_release(myl_ctx* ctx, myl_moe* moe);
+/* The whole layer on one GPU (num_local == num_experts). Host pointers:
+ * x [T][hidden] -> out [T][hidden]. */
+int myl_moe_forward(myl_ctx* ctx, const myl_moe* moe, const int16_t* x, int64_t T, int16_t* out);
+/* Device pointers on a stream. topk_idx / topk_prob ([T][top_k] int32) may be
+ * NULL; when given they receive the routing. */
+int myl_moe_dev(myl_ctx* ctx, const myl_moe* moe, const int16_t* x, int64_t T, int64_t ldx,
+                int16_t* out, int64_t ldo, int32_t* topk_idx, int32_t* topk_prob, void* stream);
+/* The stages, for expert parallelism (device pointers):
+ *   route    x [T] -> topk_idx, topk_prob [T][top_k]
+ *   experts  rows x [P][hidden] with global expert ids [P], all held by this
+ *            object -> y [P][hidden] = mlp_int(x[q], expert ids[q]); an id
+ *            outside the object's experts reports MYL_ERR_DEVICE at the next
+ *            synchronising call and gives a zero row
+ *   shared   myl_mlp_dev of the shared expert on x [T] -> shared_out [T][hidden]
+ *   combine  y rows in (token, choice) order [T * top_k][hidden], topk_prob,
+ *            shared_out (may be NULL) -> out [T][hidden] */
+int myl_moe_route_dev(myl_ctx* ctx, const myl_moe* moe, const int16_t* x, int64_t T, int64_t ldx,
+                      int32_t* topk_idx, int32_t* topk_prob, void* stream);
+int myl_moe_experts_dev(myl_ctx* ctx, const myl_moe* moe, const int16_t* x, int64_t P, int64_t ldx,
+                        const int32_t* expert_ids, int16_t* y, int64_t ldy, void* stream);
+int myl_moe_combine_dev(myl_ctx* ctx, const myl_moe* moe, const int16_t* y, int64_t ldy,
+                        const int32_t* topk_prob, const int16_t* shared_out, int64_t ld_shared,
+                        int64_t T, int16_t* out, int64_t ldo, void* stream);
+
 /* Waits for the context's work and reports kernel-side errors (bounded waits
  * that ran out) as MYL_ERR_DEVICE; the context stays usable afterwards. */
 int myl_synchronize(myl_ctx* ctx);

@@ -107,6 +107,13 @@ def load_library(path: str | None = None):
             "myl_set_dispatch": ([vp, i32, i32, i32], i32),
             "myl_launch_count": ([vp], i64),
             "myl_debug_inject_wait_fault": ([vp, i32], i32),
+            "myl_moe_register": ([vp, C.POINTER(MoeSpec), C.POINTER(vp)], i32),
+            "myl_moe_release": ([vp, vp], i32),
+            "myl_moe_forward": ([vp, vp, vp, i64, vp], i32),
+            "myl_moe_dev": ([vp, vp, vp, i64, i64, vp, i64, vp, vp, vp], i32),
+            "myl_moe_route_dev": ([vp, vp, vp, i64, i64, vp, vp, vp], i32),
+            "myl_moe_experts_dev": ([vp, vp, vp, i64, i64, vp, vp, i64, vp], i32),
+            "myl_moe_combine_dev": ([vp, vp, vp, i64, vp, vp, i64, i64, vp, i64, vp], i32),
         }
         for name, (args, res) in sig.items():
             f = getattr(L, name)
@@ -417,6 +424,124 @@ class Mlp:
     def requant_dev(self, acc, y, stream=None) -> None:
         _check("myl_mlp_requant_dev", load_library().myl_mlp_requant_dev(
             self.ctx.handle, self._h, _p(acc), acc.shape[0], _p(y), y.stride(0), _stream_ptr(stream)))
+
+
+class MoeSpec(C.Structure):
+    """myl_moe_spec (include/myl_w8a16.h)."""
+
+    _fields_ = [
+        ("hidden", C.c_int64), ("intermediate", C.c_int64), ("num_experts", C.c_int64),
+        ("top_k", C.c_int64), ("first_expert", C.c_int64), ("num_local", C.c_int64),
+        ("W_router", C.c_void_p), ("router_w_shifts", C.c_void_p),
+        ("router_in_frac", C.c_uint8), ("router_frac", C.c_uint8),
+        ("exp_lut", C.c_void_p), ("exp_lut_len", C.c_int64),
+        ("exp_lut_shift", C.c_uint8), ("prob_frac", C.c_uint8),
+        ("W_gate", C.c_void_p), ("W_up", C.c_void_p), ("W_down", C.c_void_p),
+        ("gate_w_shifts", C.c_void_p), ("up_w_shifts", C.c_void_p), ("down_w_shifts", C.c_void_p),
+        ("out_frac", C.c_void_p),
+        ("silu_lut", C.c_void_p), ("silu_lut_len", C.c_int64),
+        ("in_frac", C.c_uint8), ("gate_out_frac", C.c_uint8), ("up_out_frac", C.c_uint8),
+        ("down_in_frac", C.c_uint8), ("silu_in_frac", C.c_uint8), ("silu_out_frac", C.c_uint8),
+        ("silu_lut_offset", C.c_int16),
+        ("shared", C.c_void_p),
+    ]
+
+
+class Moe:
+    """MoE layer built from the reference's primitives (router = LM-head
+    linear, integer top-k with the lowest index winning ties, softmax_int,
+    experts = mlp_int, combine = rescale_i64 of the probability-weighted sum
+    plus the shared expert). The object holds experts
+    [first_expert, first_expert + num_local) of num_experts; the router always
+    covers all of them.
+
+    Expert arrays: W_gate / W_up [num_local, I, H], W_down [num_local, H, I],
+    gate/up_w_shifts [num_local, I], down_w_shifts / out_frac [num_local, H].
+    ``shared`` is an ``Mlp`` (kept alive by this object) or None."""
+
+    def __init__(self, ctx: Context, hidden: int, intermediate: int, num_experts: int, top_k: int,
+                 W_router, router_w_shifts, router_in_frac: int, router_frac: int,
+                 exp_lut, exp_lut_shift: int, prob_frac: int,
+                 W_gate, W_up, W_down, gate_w_shifts, up_w_shifts, down_w_shifts, out_frac,
+                 silu_lut, in_frac: int, gate_out_frac: int, up_out_frac: int, down_in_frac: int,
+                 silu_in_frac: int, silu_lut_offset: int, silu_out_frac: int,
+                 shared: "Mlp | None" = None, first_expert: int = 0, num_local: int | None = None):
+        H, I, E = hidden, intermediate, num_experts
+        Lc = E if num_local is None else num_local
+        arrs = dict(
+            W_router=_c(W_router, np.int8).reshape(-1), router_w_shifts=_c(router_w_shifts, np.uint8),
+            exp_lut=_c(exp_lut, np.int16).reshape(-1),
+            W_gate=_c(W_gate, np.int8).reshape(-1), W_up=_c(W_up, np.int8).reshape(-1),
+            W_down=_c(W_down, np.int8).reshape(-1),
+            gate_w_shifts=_c(gate_w_shifts, np.uint8).reshape(-1),
+            up_w_shifts=_c(up_w_shifts, np.uint8).reshape(-1),
+            down_w_shifts=_c(down_w_shifts, np.uint8).reshape(-1),
+            out_frac=_c(out_frac, np.uint8).reshape(-1), silu_lut=_c(silu_lut, np.int16).reshape(-1))
+        want = dict(W_router=E * H, router_w_shifts=E, W_gate=Lc * I * H, W_up=Lc * I * H,
+                    W_down=Lc * H * I, gate_w_shifts=Lc * I, up_w_shifts=Lc * I,
+                    down_w_shifts=Lc * H, out_frac=Lc * H)
+        for k, n in want.items():
+            if arrs[k].size != n:
+                raise MylError("moe", MYL_ERR_SHAPE, f"{k} has {arrs[k].size} elements, expected {n}")
+        spec = MoeSpec(hidden=H, intermediate=I, num_experts=E, top_k=top_k, first_expert=first_expert,
+                       num_local=Lc, router_in_frac=router_in_frac, router_frac=router_frac,
+                       exp_lut_len=arrs["exp_lut"].size, exp_lut_shift=exp_lut_shift,
+                       prob_frac=prob_frac, silu_lut_len=arrs["silu_lut"].size, in_frac=in_frac,
+                       gate_out_frac=gate_out_frac, up_out_frac=up_out_frac,
+                       down_in_frac=down_in_frac, silu_in_frac=silu_in_frac,
+                       silu_out_frac=silu_out_frac, silu_lut_offset=silu_lut_offset,
+                       shared=shared.handle.value if shared is not None else None)
+        for k, a in arrs.items():
+            setattr(spec, k, _p(a) if a.size else None)
+        h = C.c_void_p()
+        _check("myl_moe_register", load_library().myl_moe_register(ctx.handle, C.byref(spec), C.byref(h)))
+        self.ctx, self._h, self.shared = ctx, h, shared
+        self.hidden, self.intermediate, self.num_experts, self.top_k = H, I, E, top_k
+        self.first_expert, self.num_local = first_expert, Lc
+
+    @property
+    def handle(self):
+        return self._h
+
+    def release(self) -> None:
+        if getattr(self, "_h", None) and self.ctx.handle:
+            load_library().myl_moe_release(self.ctx.handle, self._h)
+        self._h = None
+
+    def __del__(self):
+        try:
+            self.release()
+        except Exception:
+            pass
+
+    def __call__(self, x) -> np.ndarray:
+        """Host arrays: x [T, hidden] int16 -> [T, hidden] int16."""
+        xs = np.ascontiguousarray(_c(x, np.int16).reshape(-1, self.hidden))
+        y = np.zeros_like(xs)
+        _check("myl_moe_forward", load_library().myl_moe_forward(self.ctx.handle, self._h, _p(xs),
+                                                                 xs.shape[0], _p(y)))
+        return y
+
+    def dev(self, x, out, topk_idx=None, topk_prob=None, stream=None) -> None:
+        _check("myl_moe_dev", load_library().myl_moe_dev(
+            self.ctx.handle, self._h, _p(x), x.shape[0], x.stride(0), _p(out), out.stride(0),
+            _p(topk_idx), _p(topk_prob), _stream_ptr(stream)))
+
+    def route_dev(self, x, topk_idx, topk_prob, stream=None) -> None:
+        _check("myl_moe_route_dev", load_library().myl_moe_route_dev(
+            self.ctx.handle, self._h, _p(x), x.shape[0], x.stride(0), _p(topk_idx), _p(topk_prob),
+            _stream_ptr(stream)))
+
+    def experts_dev(self, x, expert_ids, y, stream=None) -> None:
+        _check("myl_moe_experts_dev", load_library().myl_moe_experts_dev(
+            self.ctx.handle, self._h, _p(x), x.shape[0], x.stride(0), _p(expert_ids), _p(y),
+            y.stride(0), _stream_ptr(stream)))
+
+    def combine_dev(self, y, topk_prob, shared_out, out, stream=None) -> None:
+        _check("myl_moe_combine_dev", load_library().myl_moe_combine_dev(
+            self.ctx.handle, self._h, _p(y), y.stride(0), _p(topk_prob), _p(shared_out),
+            shared_out.stride(0) if shared_out is not None else 0, out.shape[0], _p(out),
+            out.stride(0), _stream_ptr(stream)))
 
 
 def _stream_ptr(stream) -> int | None:

@@ -27,6 +27,7 @@ enum DeviceError : int {
   DEV_WAIT_EPILOGUE = 0x103,  // epilogue gave up waiting for the accumulator
   DEV_WAIT_DRAIN = 0x104,     // clean-up gave up waiting for copies / MMAs in flight
   DEV_WAIT_INJECTED = 0x105,  // test hook: a wait on a barrier nothing arrives at
+  DEV_BAD_EXPERT = 0x201,     // an expert id outside the experts this object holds
 };
 
 // Epilogue modes.

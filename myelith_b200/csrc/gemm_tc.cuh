@@ -70,18 +70,64 @@ struct TcCtl {
   int abort;
 };
 
+// One work unit: a 128-channel x BN-token output tile over one K slice.
+struct TcUnit {
+  int nt, ks, kt0, nkt;
+  int64_t m_begin;   // first activation row (token) of the tile
+  int64_t m_end;     // rows >= m_end are not stored (end of the group / of M)
+  int64_t w_row;     // first weight row of the tile
+  int64_t p_off;     // offset of the tile's group into the per-channel parameters
+};
+
+// Work decomposition. Dense: units (channel tile, token tile, K slice), channel
+// tiles varying fastest (a wave shares a token tile and sweeps the weight).
+// Grouped (MoE experts, groups > 0): group g owns activation rows
+// [row_start[g], row_start[g] + rows[g]) and weight rows
+// [g * group_w_rows, (g + 1) * group_w_rows) of a stacked weight; its units are
+// [tile_start[g], tile_start[g + 1]) (device table written by the router), one
+// K slice each. A token tile may run past its group's rows into the next
+// group's: those columns are computed and not stored.
 struct TcWork {
   int tiles_n, tiles_m, ksplit, k_tiles_total, k_tiles_per_split;
-  __device__ __forceinline__ int units() const { return tiles_n * tiles_m * ksplit; }
-  // Unit u -> (channel tile, token tile, K slice). Channel tiles vary fastest:
-  // the CTAs of one wave share a token tile and sweep the weight.
-  __device__ __forceinline__ void decode(int u, int& nt, int& mt, int& ks, int& kt0, int& nkt) const {
-    nt = u % tiles_n;
-    const int r = u / tiles_n;
-    mt = r % tiles_m;
-    ks = r / tiles_m;
-    kt0 = ks * k_tiles_per_split;
-    nkt = min(k_tiles_per_split, k_tiles_total - kt0);
+  int groups;
+  const int* tile_start;
+  const int* row_start;
+  const int* rows;
+  int64_t group_w_rows;
+  __device__ __forceinline__ int units() const {
+    return groups > 0 ? tile_start[groups] : tiles_n * tiles_m * ksplit;
+  }
+  __device__ __forceinline__ TcUnit decode(int u, int BN, int64_t M) const {
+    TcUnit w;
+    if (groups == 0) {
+      w.nt = u % tiles_n;
+      const int r = u / tiles_n;
+      const int mt = r % tiles_m;
+      w.ks = r / tiles_m;
+      w.kt0 = w.ks * k_tiles_per_split;
+      w.nkt = min(k_tiles_per_split, k_tiles_total - w.kt0);
+      w.m_begin = int64_t(mt) * BN;
+      w.m_end = M;
+      w.w_row = int64_t(w.nt) * 128;
+      w.p_off = 0;
+      return w;
+    }
+    int lo = 0, hi = groups - 1;  // last group with tile_start[g] <= u
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (tile_start[mid] <= u) lo = mid;
+      else hi = mid - 1;
+    }
+    const int local = u - tile_start[lo];
+    w.nt = local % tiles_n;
+    w.ks = 0;
+    w.kt0 = 0;
+    w.nkt = k_tiles_total;
+    w.m_begin = int64_t(row_start[lo]) + int64_t(local / tiles_n) * BN;
+    w.m_end = int64_t(row_start[lo]) + rows[lo];
+    w.p_off = int64_t(lo) * group_w_rows;
+    w.w_row = w.p_off + int64_t(w.nt) * 128;
+    return w;
   }
 };
 
@@ -209,9 +255,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       int g = 0;  // K steps issued by this CTA (ring position)
       bool stop = false;
       for (int u = blockIdx.x; u < units && !stop; u += gridDim.x) {
-        int nt, mt, ks, kt0, nkt;
-        work.decode(u, nt, mt, ks, kt0, nkt);
-        for (int i = 0; i < nkt; ++i, ++g) {
+        const TcUnit wu = work.decode(u, BN, M);
+        for (int i = 0; i < wu.nkt; ++i, ++g) {
           const int s = g % STAGES;
           const uint32_t ph = uint32_t(g / STAGES) & 1u;
           if (!mbar_wait_bounded(smem_addr(&ctl.empty[s]), ph ^ 1u, timeout_ns, abort)) {
@@ -221,10 +266,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
           const uint32_t fb = smem_addr(&ctl.full[s]);
           mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
-          const int32_t kx = (kt0 + i) * TC_BK;
-          tma_load_2d(sm_w(s), &tm_w, fb, kx, nt * 128);
-          tma_load_2d(sm_xh(s), &tm_xhi, fb, kx, mt * BN);
-          tma_load_2d(sm_xl(s), &tm_xlo, fb, kx, mt * BN);
+          const int32_t kx = (wu.kt0 + i) * TC_BK;
+          tma_load_2d(sm_w(s), &tm_w, fb, kx, int32_t(wu.w_row));
+          tma_load_2d(sm_xh(s), &tm_xhi, fb, kx, int32_t(wu.m_begin));
+          tma_load_2d(sm_xl(s), &tm_xlo, fb, kx, int32_t(wu.m_begin));
         }
       }
       if (*abort) {
@@ -243,8 +288,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       int g = 0, lt = 0;
       bool stop = false;
       for (int u = blockIdx.x; u < units && !stop; u += gridDim.x, ++lt) {
-        int nt, mt, ks, kt0, nkt;
-        work.decode(u, nt, mt, ks, kt0, nkt);
+        const int nkt = work.decode(u, BN, M).nkt;
         const int b = lt & 1;
         const uint32_t tph = uint32_t(lt >> 1) & 1u;
         if (!mbar_wait_bounded(smem_addr(&ctl.tempty[b]), tph ^ 1u, timeout_ns, abort)) {
@@ -292,8 +336,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int row = q * 32 + lane;
     int lt = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++lt) {
-      int nt, mt, ks, kt0, nkt;
-      work.decode(u, nt, mt, ks, kt0, nkt);
+      const TcUnit wu = work.decode(u, BN, M);
       const int b = lt & 1;
       const uint32_t tph = uint32_t(lt >> 1) & 1u;
       bool ok = mbar_wait_bounded(smem_addr(&ctl.tfull[b]), tph, timeout_ns, abort);
@@ -308,11 +351,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
       if (*abort) break;
       tc_fence_after();
-      const int64_t n = int64_t(nt) * 128 + row;
-      const int64_t m0 = int64_t(mt) * BN + col0;
+      const int64_t n = int64_t(wu.nt) * 128 + row;  // channel within the group
+      const int64_t m0 = wu.m_begin + col0;
+      const int64_t Mend = wu.m_end;
       const uint32_t tq = tmem + (uint32_t(q * 32) << 16) + uint32_t(b * Cfg::BUF_COLS + col0);
       Epilogue e = ep;
-      if (e.mode == EPI_ACC_I64) e.y = static_cast<int64_t*>(e.y) + int64_t(ks) * slice_stride;
+      if (e.mode == EPI_ACC_I64) e.y = static_cast<int64_t*>(e.y) + int64_t(wu.ks) * slice_stride;
+      if (wu.p_off) {  // per-channel parameters of this group
+        e.shift = e.shift ? e.shift + wu.p_off : nullptr;
+        e.mult = e.mult ? e.mult + wu.p_off : nullptr;
+        e.bias = e.bias ? e.bias + wu.p_off : nullptr;
+      }
       // Channel parameters, once per unit.
       int shift = 0;
       const int mode = e.mode;
@@ -340,22 +389,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                        : int32_t(rq.apply(int64_t(int32_t(hi[j])) * 256 + int64_t(int32_t(lo[j]))));
             const int32_t p = __shfl_xor_sync(0xffffffffu, v, 1);
             const int64_t m = mc + j;
-            if (((j < NC / 2) == even) && n < N && m < M)
+            if (((j < NC / 2) == even) && n < N && m < Mend)
               silu_store(e, m, n >> 1, silu_combine(e.silu, even ? v : p, even ? p : v));
           }
           continue;
         }
         if (n >= N) continue;
         if (mode == EPI_ACC_I64) {
-          store_column<NC>(static_cast<int64_t*>(e.y) + mc * e.ldy + n, e.ldy, mc, M, [&](int j) {
+          store_column<NC>(static_cast<int64_t*>(e.y) + mc * e.ldy + n, e.ldy, mc, Mend, [&](int j) {
             return int64_t(int32_t(hi[j])) * 256 + int64_t(int32_t(lo[j]));
           });
         } else if (fast) {
           if (e.out_i32) {
-            store_column<NC>(static_cast<int32_t*>(e.y) + mc * e.ldy + n, e.ldy, mc, M,
+            store_column<NC>(static_cast<int32_t*>(e.y) + mc * e.ldy + n, e.ldy, mc, Mend,
                              [&](int j) { return int32_t(r32.apply(int32_t(hi[j]), int32_t(lo[j]))); });
           } else {
-            store_column<NC>(static_cast<int16_t*>(e.y) + mc * e.ldy + n, e.ldy, mc, M,
+            store_column<NC>(static_cast<int16_t*>(e.y) + mc * e.ldy + n, e.ldy, mc, Mend,
                              [&](int j) { return int16_t(r32.apply(int32_t(hi[j]), int32_t(lo[j]))); });
           }
         } else {
@@ -371,7 +420,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
             for (int t = 0; t < 8; ++t) {
               const int64_t m = mc + j0 + t;
-              if (m < M) {
+              if (m < Mend) {
                 const int64_t v = rq.apply(a[t]);
                 if (e.out_i32) static_cast<int32_t*>(e.y)[m * e.ldy + n] = int32_t(v);
                 else static_cast<int16_t*>(e.y)[m * e.ldy + n] = int16_t(v);

@@ -29,6 +29,7 @@
 #include "common.cuh"
 #include "gemm_tc.cuh"
 #include "gemv.cuh"
+#include "moe.cuh"
 
 using namespace myl;
 
@@ -107,7 +108,7 @@ struct myl_ctx {
   int gemv_max_m = 4, force_split_k = 0, force_tile = 0, inject_fault = 0;
   int64_t launches = 0;
   PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-  DevBuf x, y, rq, planes, part, h, hplanes;
+  DevBuf x, y, rq, planes, part, h, hplanes, moe;
   // The workspace buffers are shared by every call on the context; calls on
   // different streams are ordered through this event.
   cudaEvent_t ws_event = nullptr;
@@ -326,9 +327,13 @@ static int launch_tc_variant(myl_ctx* ctx, const myl_weight* w, const CUtensorMa
   auto fn = gemm_w8a16_tc_kernel<BN, STAGES>;
   TRY(kernel_smem_occupancy(ctx->device, reinterpret_cast<const void*>(fn), TC_THREADS,
                             Cfg::SMEM_BYTES, nullptr));
-  const int64_t units = int64_t(work.tiles_n) * work.tiles_m * work.ksplit;
+  // Grouped work is sized on the device (the router's tile table): one CTA per
+  // SM, CTAs without a unit exit after setup.
+  const int64_t units = work.groups > 0 ? int64_t(ctx->num_sms)
+                                        : int64_t(work.tiles_n) * work.tiles_m * work.ksplit;
   const unsigned grid = unsigned(std::min<int64_t>(units, ctx->num_sms));
-  fn<<<grid, TC_THREADS, Cfg::SMEM_BYTES, st>>>(w->tm128, tm_xhi, tm_xlo, M, w->N, work, ep,
+  const int64_t N = work.groups > 0 ? work.group_w_rows : w->N;  // channels per group
+  fn<<<grid, TC_THREADS, Cfg::SMEM_BYTES, st>>>(w->tm128, tm_xhi, tm_xlo, M, N, work, ep,
                                                  slice_stride, ctx->d_err, ctx->timeout_ns,
                                                  ctx->inject_fault);
   CUDA_TRY(cudaGetLastError());
@@ -412,18 +417,18 @@ static int launch_tc(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_
   return launch_tc_planes(ctx, w, xhi, xlo, ldp, M, ep_final, st);
 }
 
+static int dispatch_linear(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
+                           int64_t ldx, const Epilogue& ep, cudaStream_t st) {
+  if (M <= ctx->gemv_max_m && M <= 4) return launch_gemv(ctx, w, x, M, ldx, ep, st);
+  return launch_tc(ctx, w, x, M, ldx, ep, st);
+}
+
 static int run_linear(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M, int64_t ldx,
                       const Epilogue& ep, cudaStream_t st) {
   if (M == 0 || w->N == 0) return MYL_OK;
   CUDA_TRY(cudaSetDevice(ctx->device));
   TRY(ws_acquire(ctx, st));
-  int rc;
-  if (M <= ctx->gemv_max_m && M <= 4) {
-    rc = launch_gemv(ctx, w, x, M, ldx, ep, st);
-  } else {
-    rc = launch_tc(ctx, w, x, M, ldx, ep, st);
-  }
-  TRY(rc);
+  TRY(dispatch_linear(ctx, w, x, M, ldx, ep, st));
   return ws_release(ctx, st);
 }
 
@@ -434,7 +439,9 @@ static int check_device_error(myl_ctx* ctx) {
   if (e != 0) {
     CUDA_TRY(cudaMemsetAsync(ctx->d_err, 0, sizeof(int), ctx->stream));
     CUDA_TRY(cudaStreamSynchronize(ctx->stream));
-    return fail(MYL_ERR_DEVICE, "kernel reported error 0x%x (a bounded wait ran out)", e);
+    return fail(MYL_ERR_DEVICE, "kernel reported error 0x%x (%s)", e,
+                e == DEV_BAD_EXPERT ? "an expert id outside this object's experts"
+                                    : "a bounded wait ran out");
   }
   return MYL_OK;
 }
@@ -523,7 +530,8 @@ int myl_destroy(myl_ctx* ctx) {
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   for (auto& kv : ctx->backend_cache) myl_weight_release(ctx, kv.second);
   ctx->backend_cache.clear();
-  for (DevBuf* b : {&ctx->x, &ctx->y, &ctx->rq, &ctx->planes, &ctx->part, &ctx->h, &ctx->hplanes})
+  for (DevBuf* b : {&ctx->x, &ctx->y, &ctx->rq, &ctx->planes, &ctx->part, &ctx->h, &ctx->hplanes,
+                    &ctx->moe})
     if (b->p) cudaFree(b->p);
   if (ctx->d_err) cudaFree(ctx->d_err);
   if (ctx->h_err) cudaFreeHost(ctx->h_err);
@@ -1124,3 +1132,410 @@ extern "C" int myl_linear_noalloc_dev(myl_ctx* ctx, const myl_weight* w, const m
   const TcWork work{int((w->N + 127) / 128), int((M + BN - 1) / BN), 1, k_tiles, k_tiles};
   return launch_tc_any(ctx, w, tm_xhi, tm_xlo, M, BN, work, make_ep(rq, y, ldy), 0, st);
 }
+
+// ---------------------------------------------------------------------------------
+// MoE layer (moe.cuh): router linear, integer top-k + softmax_int, counting
+// sort of the (token, choice) pairs by expert, grouped tensor-core GEMMs over
+// the experts' row segments, combine.
+
+struct myl_moe {
+  int64_t H = 0, I = 0, E = 0, k = 0, first = 0, L = 0;
+  myl_weight* w_router = nullptr;  // [E][H]
+  myl_requant* rq_router = nullptr;  // i32 logits
+  myl_weight* w_gu = nullptr;      // [L * 2I][H], per expert rows 2i = gate_i, 2i + 1 = up_i
+  myl_weight* w_down = nullptr;    // [L * H][I]
+  int8_t* d_shift_gu = nullptr;    // [L * 2I]
+  int8_t* d_shift_down = nullptr;  // [L * H]
+  int16_t* d_silu_lut = nullptr;
+  int lut_hi = 0, offset = 0, s1 = 0, s2 = 0;
+  int16_t* d_exp_lut = nullptr;
+  int exp_lut_len = 0, exp_lut_shift = 0, prob_frac = 0;
+  const myl_mlp* shared = nullptr;
+};
+
+// Carves 256-byte aligned pieces out of ctx->moe.
+struct MoeArena {
+  size_t off = 0;
+  template <typename T>
+  size_t take(int64_t n) {
+    const size_t at = off;
+    off = (off + size_t(std::max<int64_t>(n, 1)) * sizeof(T) + 255) & ~size_t(255);
+    return at;
+  }
+};
+
+struct MoeExpertsWs {
+  int *counts, *row_start, *rows, *tile_a, *tile_b, *cursor;
+  int32_t *src, *pos;
+  int8_t* xhi;
+  uint8_t* xlo;
+  int8_t* hhi;
+  uint8_t* hlo;
+  int16_t* y_perm;
+};
+
+struct MoeWs {
+  MoeExpertsWs ex;
+  int32_t *logits, *topk_idx, *topk_prob;
+  int16_t* shared_out;
+};
+
+// Workspace for P pairs (and, with T > 0, the router and shared output of T
+// tokens) inside ctx->moe.
+static int moe_workspace(myl_ctx* ctx, const myl_moe* m, int64_t P, int64_t T, MoeWs* w) {
+  const int64_t L = m->L, ldp_h = m->w_gu->ldp, ldp_i = m->w_down->ldp;
+  MoeArena a;
+  const size_t o_counts = a.take<int>(L), o_row_start = a.take<int>(L), o_rows = a.take<int>(L),
+               o_tile_a = a.take<int>(L + 1), o_tile_b = a.take<int>(L + 1),
+               o_cursor = a.take<int>(L), o_src = a.take<int32_t>(P), o_pos = a.take<int32_t>(P),
+               o_xhi = a.take<int8_t>(P * ldp_h), o_xlo = a.take<uint8_t>(P * ldp_h),
+               o_hhi = a.take<int8_t>(P * ldp_i), o_hlo = a.take<uint8_t>(P * ldp_i),
+               o_y = a.take<int16_t>(P * m->H), o_logits = a.take<int32_t>(T * m->E),
+               o_idx = a.take<int32_t>(T * m->k), o_prob = a.take<int32_t>(T * m->k),
+               o_shared = a.take<int16_t>(T * m->H);
+  TRY(ensure(ctx->moe, a.off));
+  uint8_t* b = static_cast<uint8_t*>(ctx->moe.p);
+  w->ex.counts = reinterpret_cast<int*>(b + o_counts);
+  w->ex.row_start = reinterpret_cast<int*>(b + o_row_start);
+  w->ex.rows = reinterpret_cast<int*>(b + o_rows);
+  w->ex.tile_a = reinterpret_cast<int*>(b + o_tile_a);
+  w->ex.tile_b = reinterpret_cast<int*>(b + o_tile_b);
+  w->ex.cursor = reinterpret_cast<int*>(b + o_cursor);
+  w->ex.src = reinterpret_cast<int32_t*>(b + o_src);
+  w->ex.pos = reinterpret_cast<int32_t*>(b + o_pos);
+  w->ex.xhi = reinterpret_cast<int8_t*>(b + o_xhi);
+  w->ex.xlo = b + o_xlo;
+  w->ex.hhi = reinterpret_cast<int8_t*>(b + o_hhi);
+  w->ex.hlo = b + o_hlo;
+  w->ex.y_perm = reinterpret_cast<int16_t*>(b + o_y);
+  w->logits = reinterpret_cast<int32_t*>(b + o_logits);
+  w->topk_idx = reinterpret_cast<int32_t*>(b + o_idx);
+  w->topk_prob = reinterpret_cast<int32_t*>(b + o_prob);
+  w->shared_out = reinterpret_cast<int16_t*>(b + o_shared);
+  return MYL_OK;
+}
+
+static unsigned grid_for(const myl_ctx* ctx, int64_t items, int per_sm = 8) {
+  return unsigned(std::max<int64_t>(1, std::min<int64_t>((items + 255) / 256,
+                                                         int64_t(ctx->num_sms) * per_sm)));
+}
+
+// Token tile of the grouped GEMMs from the mean rows per expert.
+static int moe_token_tile(const myl_ctx* ctx, int64_t P, int64_t L) {
+  if (ctx->force_tile == 32 || ctx->force_tile == 64 || ctx->force_tile == 128) return ctx->force_tile;
+  const int64_t mean = (P + L - 1) / std::max<int64_t>(L, 1);
+  return mean <= 32 ? 32 : (mean <= 64 ? 64 : 128);
+}
+
+static int moe_route(myl_ctx* ctx, const myl_moe* m, const int16_t* x, int64_t T, int64_t ldx,
+                     int32_t* logits, int32_t* idx, int32_t* prob, cudaStream_t st) {
+  Epilogue ep{};
+  ep.mode = EPI_SHIFT;
+  ep.out_i32 = 1;
+  ep.shift = m->rq_router->d_shift;
+  ep.y = logits;
+  ep.ldy = m->E;
+  TRY(dispatch_linear(ctx, m->w_router, x, T, ldx, ep, st));
+  MoeRouteParams rp{m->d_exp_lut, m->exp_lut_len, m->exp_lut_shift, m->prob_frac};
+  moe_route_kernel<<<grid_for(ctx, T), 256, 0, st>>>(logits, m->E, T, int(m->E), int(m->k), rp, idx,
+                                                      prob);
+  CUDA_TRY(cudaGetLastError());
+  ctx->launches++;
+  return MYL_OK;
+}
+
+// Pairs q in [0, P) with expert ids[q] read source row q / div of x; y_perm
+// row pos[q] receives mlp_int(x[q / div], expert ids[q]).
+static int moe_experts(myl_ctx* ctx, const myl_moe* m, const int16_t* x, int64_t ldx,
+                       const int32_t* ids, int64_t P, int div, const MoeExpertsWs& w,
+                       cudaStream_t st) {
+  const int L = int(m->L);
+  const int BN = moe_token_tile(ctx, P, L);
+  const int tiles_gu = int((2 * m->I + 127) / 128), tiles_down = int((m->H + 127) / 128);
+  CUDA_TRY(cudaMemsetAsync(w.counts, 0, size_t(L) * sizeof(int), st));
+  moe_count_kernel<<<grid_for(ctx, P, 2), 256, 0, st>>>(ids, P, int(m->first), L, w.counts,
+                                                        ctx->d_err);
+  CUDA_TRY(cudaGetLastError());
+  moe_plan_kernel<<<1, 1, 0, st>>>(w.counts, L, BN, tiles_gu, tiles_down, w.row_start, w.rows,
+                                   w.tile_a, w.tile_b, w.cursor);
+  CUDA_TRY(cudaGetLastError());
+  // The scatter fills src[0, valid rows); with bad ids the tail up to P is
+  // still read by the gather (and never stored), so it starts as row 0.
+  CUDA_TRY(cudaMemsetAsync(w.src, 0, size_t(P) * sizeof(int32_t), st));
+  moe_scatter_kernel<<<grid_for(ctx, P), 256, 0, st>>>(ids, P, int(m->first), L, div, w.cursor,
+                                                        w.src, w.pos);
+  CUDA_TRY(cudaGetLastError());
+  const int64_t H = m->H, ldp_h = m->w_gu->ldp, ldp_i = m->w_down->ldp;
+  moe_gather_split_kernel<<<grid_for(ctx, P * (ldp_h / 8), 16), 256, 0, st>>>(
+      x, ldx, P, H, w.src, w.xhi, w.xlo, ldp_h);
+  CUDA_TRY(cudaGetLastError());
+  ctx->launches += 4;
+  // Gate/up: grouped GEMM with the SiLU pair epilogue into the down planes.
+  CUtensorMap tm_xhi, tm_xlo, tm_hhi, tm_hlo;
+  TRY(encode_map(ctx, &tm_xhi, w.xhi, H, P, ldp_h, BN));
+  TRY(encode_map(ctx, &tm_xlo, w.xlo, H, P, ldp_h, BN));
+  TRY(encode_map(ctx, &tm_hhi, w.hhi, m->I, P, ldp_i, BN));
+  TRY(encode_map(ctx, &tm_hlo, w.hlo, m->I, P, ldp_i, BN));
+  TcWork wk{};
+  wk.tiles_n = tiles_gu;
+  wk.tiles_m = 1;
+  wk.ksplit = 1;
+  wk.k_tiles_total = int((H + TC_BK - 1) / TC_BK);
+  wk.k_tiles_per_split = wk.k_tiles_total;
+  wk.groups = L;
+  wk.tile_start = w.tile_a;
+  wk.row_start = w.row_start;
+  wk.rows = w.rows;
+  wk.group_w_rows = 2 * m->I;
+  Epilogue ep_gu{};
+  ep_gu.mode = EPI_SILU;
+  ep_gu.shift = m->d_shift_gu;
+  ep_gu.silu.lut = m->d_silu_lut;
+  ep_gu.silu.lut_hi = m->lut_hi;
+  ep_gu.silu.offset = m->offset;
+  ep_gu.silu.s1 = m->s1;
+  ep_gu.silu.s2 = m->s2;
+  ep_gu.silu.h_hi = w.hhi;
+  ep_gu.silu.h_lo = w.hlo;
+  ep_gu.silu.ldp = ldp_i;
+  ep_gu.ldy = m->I;
+  TRY(launch_tc_any(ctx, m->w_gu, tm_xhi, tm_xlo, P, BN, wk, ep_gu, 0, st));
+  // Down: grouped GEMM, reference requant, rows in expert order.
+  wk.tiles_n = tiles_down;
+  wk.k_tiles_total = int((m->I + TC_BK - 1) / TC_BK);
+  wk.k_tiles_per_split = wk.k_tiles_total;
+  wk.tile_start = w.tile_b;
+  wk.group_w_rows = H;
+  Epilogue ep_down{};
+  ep_down.mode = EPI_SHIFT;
+  ep_down.shift = m->d_shift_down;
+  ep_down.y = w.y_perm;
+  ep_down.ldy = H;
+  return launch_tc_any(ctx, m->w_down, tm_hhi, tm_hlo, P, BN, wk, ep_down, 0, st);
+}
+
+extern "C" {
+
+int myl_moe_release(myl_ctx* ctx, myl_moe* m) {
+  if (!m) return MYL_OK;
+  if (ctx) {
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    if (m->w_router) myl_weight_release(ctx, m->w_router);
+    if (m->rq_router) myl_requant_release(ctx, m->rq_router);
+    if (m->w_gu) myl_weight_release(ctx, m->w_gu);
+    if (m->w_down) myl_weight_release(ctx, m->w_down);
+  }
+  for (void* p : {static_cast<void*>(m->d_shift_gu), static_cast<void*>(m->d_shift_down),
+                  static_cast<void*>(m->d_silu_lut), static_cast<void*>(m->d_exp_lut)})
+    if (p) cudaFree(p);
+  delete m;
+  return MYL_OK;
+}
+
+int myl_moe_register(myl_ctx* ctx, const myl_moe_spec* s, myl_moe** out) {
+  if (!ctx || !s || !out) return fail(MYL_ERR_ARG, "null argument");
+  *out = nullptr;
+  const int64_t H = s->hidden, I = s->intermediate, E = s->num_experts, L = s->num_local;
+  if (H <= 0 || I <= 0 || E <= 0 || L <= 0 || s->first_expert < 0 || s->first_expert + L > E)
+    return fail(MYL_ERR_SHAPE, "moe: hidden %lld intermediate %lld experts %lld local [%lld, +%lld)",
+                (long long)H, (long long)I, (long long)E, (long long)s->first_expert, (long long)L);
+  if (E > MOE_MAX_EXPERTS || s->top_k < 1 || s->top_k > MOE_MAX_K || s->top_k > E)
+    return fail(MYL_ERR_UNSUPPORTED, "moe: %lld experts, top-%lld (limits: 256 experts, top-8)",
+                (long long)E, (long long)s->top_k);
+  if (H > 65536 || I > 65536)
+    return fail(MYL_ERR_UNSUPPORTED, "moe: hidden/intermediate beyond 65536");
+  if (!s->W_router || !s->router_w_shifts || !s->W_gate || !s->W_up || !s->W_down ||
+      !s->gate_w_shifts || !s->up_w_shifts || !s->down_w_shifts || !s->out_frac || !s->silu_lut ||
+      (s->exp_lut_len > 0 && !s->exp_lut))
+    return fail(MYL_ERR_ARG, "moe: null table or weight");
+  if (s->silu_lut_len < 1 || s->silu_lut_len > 32768)
+    return fail(MYL_ERR_SHAPE, "silu_lut length %lld", (long long)s->silu_lut_len);
+  if (s->exp_lut_len < 0 || s->exp_lut_len > (int64_t(1) << 30) || s->exp_lut_shift > 31 ||
+      s->prob_frac > 30)
+    return fail(MYL_ERR_SHAPE, "exp_lut length %lld, shift %u, prob_frac %u",
+                (long long)s->exp_lut_len, unsigned(s->exp_lut_shift), unsigned(s->prob_frac));
+  // softmax_int multiplies e * 2^prob_frac in i32 (softmax.rs:52): every value
+  // e can take (the table's entries, and 1 for an empty table) must keep it in
+  // range, so the kernel never meets the overflow the reference would panic on.
+  {
+    const int64_t one = int64_t(1) << s->prob_frac;
+    int64_t lo = s->exp_lut_len > 0 ? 0 : 1, hi = lo;
+    for (int64_t i = 0; i < s->exp_lut_len; ++i) {
+      lo = std::min<int64_t>(lo, s->exp_lut[i]);
+      hi = std::max<int64_t>(hi, s->exp_lut[i]);
+    }
+    if (hi * one > INT32_MAX || lo * one < INT32_MIN)
+      return fail(MYL_ERR_OVERFLOW, "exp_lut entry * 2^prob_frac overflows i32");
+  }
+  // Shifts, validated as the reference's debug build would (mlp.rs:28-74).
+  std::vector<int8_t> sgu(size_t(L * 2 * I)), sdown(size_t(L * H));
+  for (int64_t e = 0; e < L; ++e) {
+    for (int64_t i = 0; i < I; ++i) {
+      TRY(signed_total_shift(s->gate_w_shifts[e * I + i], s->in_frac, s->gate_out_frac,
+                             &sgu[size_t(e * 2 * I + 2 * i)]));
+      TRY(signed_total_shift(s->up_w_shifts[e * I + i], s->in_frac, s->up_out_frac,
+                             &sgu[size_t(e * 2 * I + 2 * i + 1)]));
+    }
+    for (int64_t r = 0; r < H; ++r)
+      TRY(signed_total_shift(s->down_w_shifts[e * H + r], s->down_in_frac, s->out_frac[e * H + r],
+                             &sdown[size_t(e * H + r)]));
+  }
+  const int s1 = int(int8_t(s->gate_out_frac)) - int(int8_t(s->silu_in_frac));
+  if (s1 > 30 || s1 < -31) return fail(MYL_ERR_OVERFLOW, "gate_out_frac -> silu_in_frac shift %d", s1);
+  const unsigned prod_frac = unsigned(s->silu_out_frac) + unsigned(s->up_out_frac);
+  if (prod_frac > 255u) return fail(MYL_ERR_OVERFLOW, "silu_out_frac + up_out_frac overflows u8");
+  int8_t s2 = 0;
+  TRY(signed_total_shift(uint8_t(prod_frac), 0, s->down_in_frac, &s2));
+  // Stacked, interleaved gate/up rows per expert.
+  std::vector<int8_t> wgu(size_t(L * 2 * I) * size_t(H));
+  std::vector<uint8_t> gu_shifts(size_t(L * 2 * I));
+  for (int64_t e = 0; e < L; ++e)
+    for (int64_t i = 0; i < I; ++i) {
+      const int64_t r = e * 2 * I + 2 * i;
+      std::memcpy(&wgu[size_t(r) * size_t(H)], s->W_gate + (e * I + i) * H, size_t(H));
+      std::memcpy(&wgu[size_t(r + 1) * size_t(H)], s->W_up + (e * I + i) * H, size_t(H));
+      gu_shifts[size_t(r)] = s->gate_w_shifts[e * I + i];
+      gu_shifts[size_t(r + 1)] = s->up_w_shifts[e * I + i];
+    }
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  myl_moe* m = new myl_moe();
+  m->H = H;
+  m->I = I;
+  m->E = E;
+  m->k = s->top_k;
+  m->first = s->first_expert;
+  m->L = L;
+  m->lut_hi = int(int16_t(uint16_t(uint16_t(s->silu_lut_len) - 1u)));
+  m->offset = s->silu_lut_offset;
+  m->s1 = s1;
+  m->s2 = s2;
+  m->exp_lut_len = int(s->exp_lut_len);
+  m->exp_lut_shift = s->exp_lut_shift;
+  m->prob_frac = s->prob_frac;
+  m->shared = s->shared;
+  const uint8_t router_frac = s->router_frac;
+  int rc = myl_weight_register(ctx, s->W_router, E, H, H, s->router_w_shifts, &m->w_router);
+  if (rc == MYL_OK)
+    rc = myl_requant_create(ctx, m->w_router, MYL_RQ_SHIFT_I32, s->router_in_frac, &router_frac, 0,
+                            nullptr, nullptr, &m->rq_router);
+  if (rc == MYL_OK) rc = myl_weight_register(ctx, wgu.data(), L * 2 * I, H, H, gu_shifts.data(), &m->w_gu);
+  if (rc == MYL_OK)
+    rc = myl_weight_register(ctx, s->W_down, L * H, I, I, s->down_w_shifts, &m->w_down);
+  const size_t lut_bytes = size_t(std::max<int64_t>(s->exp_lut_len, 1)) * 2;
+  if (rc == MYL_OK &&
+      (cudaMalloc(&m->d_shift_gu, sgu.size()) != cudaSuccess ||
+       cudaMalloc(&m->d_shift_down, sdown.size()) != cudaSuccess ||
+       cudaMalloc(&m->d_silu_lut, size_t(s->silu_lut_len) * 2) != cudaSuccess ||
+       cudaMalloc(&m->d_exp_lut, lut_bytes) != cudaSuccess ||
+       cudaMemcpy(m->d_shift_gu, sgu.data(), sgu.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
+       cudaMemcpy(m->d_shift_down, sdown.data(), sdown.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
+       cudaMemcpy(m->d_silu_lut, s->silu_lut, size_t(s->silu_lut_len) * 2, cudaMemcpyHostToDevice) !=
+           cudaSuccess ||
+       (s->exp_lut_len > 0 && cudaMemcpy(m->d_exp_lut, s->exp_lut, size_t(s->exp_lut_len) * 2,
+                                         cudaMemcpyHostToDevice) != cudaSuccess)))
+    rc = fail(MYL_ERR_CUDA, "moe upload failed");
+  if (rc != MYL_OK) {
+    myl_moe_release(ctx, m);
+    return rc;
+  }
+  *out = m;
+  return MYL_OK;
+}
+
+int myl_moe_route_dev(myl_ctx* ctx, const myl_moe* m, const int16_t* x, int64_t T, int64_t ldx,
+                      int32_t* topk_idx, int32_t* topk_prob, void* stream) {
+  if (!ctx || !m || (T > 0 && (!x || !topk_idx || !topk_prob))) return fail(MYL_ERR_ARG, "null argument");
+  if (T < 0 || ldx < m->H) return fail(MYL_ERR_SHAPE, "bad T/ldx");
+  if (T == 0) return MYL_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  TRY(ws_acquire(ctx, st));
+  MoeWs w;
+  TRY(moe_workspace(ctx, m, 0, T, &w));
+  TRY(moe_route(ctx, m, x, T, ldx, w.logits, topk_idx, topk_prob, st));
+  return ws_release(ctx, st);
+}
+
+int myl_moe_experts_dev(myl_ctx* ctx, const myl_moe* m, const int16_t* x, int64_t P, int64_t ldx,
+                        const int32_t* ids, int16_t* y, int64_t ldy, void* stream) {
+  if (!ctx || !m || (P > 0 && (!x || !ids || !y))) return fail(MYL_ERR_ARG, "null argument");
+  if (P < 0 || P > INT32_MAX || ldx < m->H || ldy < m->H) return fail(MYL_ERR_SHAPE, "bad P/ldx/ldy");
+  if (P == 0) return MYL_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  TRY(ws_acquire(ctx, st));
+  MoeWs w;
+  TRY(moe_workspace(ctx, m, P, 0, &w));
+  TRY(moe_experts(ctx, m, x, ldx, ids, P, 1, w.ex, st));
+  moe_unpermute_kernel<<<grid_for(ctx, P * m->H), 256, 0, st>>>(w.ex.y_perm, m->H, w.ex.pos, P, m->H,
+                                                                 y, ldy);
+  CUDA_TRY(cudaGetLastError());
+  ctx->launches++;
+  return ws_release(ctx, st);
+}
+
+int myl_moe_combine_dev(myl_ctx* ctx, const myl_moe* m, const int16_t* y, int64_t ldy,
+                        const int32_t* prob, const int16_t* shared_out, int64_t ld_shared, int64_t T,
+                        int16_t* out, int64_t ldo, void* stream) {
+  if (!ctx || !m || (T > 0 && (!y || !prob || !out))) return fail(MYL_ERR_ARG, "null argument");
+  if (T < 0 || ldy < m->H || ldo < m->H || (shared_out && ld_shared < m->H))
+    return fail(MYL_ERR_SHAPE, "bad T/ldy/ldo/ld_shared");
+  if (T == 0) return MYL_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  moe_combine_kernel<<<grid_for(ctx, T * m->H), 256, 0, st>>>(y, ldy, nullptr, prob, shared_out,
+                                                               ld_shared, T, int(m->k), m->H,
+                                                               m->prob_frac, out, ldo);
+  CUDA_TRY(cudaGetLastError());
+  ctx->launches++;
+  return MYL_OK;
+}
+
+int myl_moe_dev(myl_ctx* ctx, const myl_moe* m, const int16_t* x, int64_t T, int64_t ldx,
+                int16_t* out, int64_t ldo, int32_t* topk_idx, int32_t* topk_prob, void* stream) {
+  if (!ctx || !m || (T > 0 && (!x || !out))) return fail(MYL_ERR_ARG, "null argument");
+  if (m->L != m->E)
+    return fail(MYL_ERR_ARG, "myl_moe_dev needs every expert (this object holds %lld of %lld)",
+                (long long)m->L, (long long)m->E);
+  if (T < 0 || T * m->k > INT32_MAX || ldx < m->H || ldo < m->H) return fail(MYL_ERR_SHAPE, "bad T/ldx/ldo");
+  if (T == 0) return MYL_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  TRY(ws_acquire(ctx, st));
+  const int64_t P = T * m->k;
+  MoeWs w;
+  TRY(moe_workspace(ctx, m, P, T, &w));
+  int32_t* idx = topk_idx ? topk_idx : w.topk_idx;
+  int32_t* prob = topk_prob ? topk_prob : w.topk_prob;
+  TRY(moe_route(ctx, m, x, T, ldx, w.logits, idx, prob, st));
+  TRY(moe_experts(ctx, m, x, ldx, idx, P, int(m->k), w.ex, st));
+  const int16_t* shared_out = nullptr;
+  if (m->shared) {
+    TRY(run_mlp(ctx, m->shared, x, T, ldx, w.shared_out, m->H, st));
+    shared_out = w.shared_out;
+  }
+  moe_combine_kernel<<<grid_for(ctx, T * m->H), 256, 0, st>>>(w.ex.y_perm, m->H, w.ex.pos, prob,
+                                                               shared_out, m->H, T, int(m->k), m->H,
+                                                               m->prob_frac, out, ldo);
+  CUDA_TRY(cudaGetLastError());
+  ctx->launches++;
+  return ws_release(ctx, st);
+}
+
+int myl_moe_forward(myl_ctx* ctx, const myl_moe* m, const int16_t* x, int64_t T, int16_t* out) {
+  if (!ctx || !m || (T > 0 && (!x || !out))) return fail(MYL_ERR_ARG, "null argument");
+  if (T < 0) return fail(MYL_ERR_SHAPE, "T = %lld is negative", (long long)T);
+  if (T == 0) return MYL_OK;
+  const size_t bytes = size_t(T) * size_t(m->H) * 2;
+  TRY(ensure(ctx->x, bytes));
+  TRY(ensure(ctx->y, bytes));
+  cudaStream_t st = ctx->stream;
+  CUDA_TRY(cudaMemcpyAsync(ctx->x.p, x, bytes, cudaMemcpyHostToDevice, st));
+  TRY(myl_moe_dev(ctx, m, static_cast<const int16_t*>(ctx->x.p), T, m->H,
+                  static_cast<int16_t*>(ctx->y.p), m->H, nullptr, nullptr, st));
+  CUDA_TRY(cudaMemcpyAsync(out, ctx->y.p, bytes, cudaMemcpyDeviceToHost, st));
+  return check_device_error(ctx);
+}
+
+}  // extern "C"

@@ -79,6 +79,9 @@ def lib():
                                    u8, u8, u8, u8, u8, C.c_int16, u8, p, p, p]
         L.mylo_mlp_hidden.argtypes = [p, i64, p, p, i64, i64, p, p, p, i64,
                                       u8, u8, u8, u8, u8, C.c_int16, u8, p, p]
+        L.mylo_softmax_int.argtypes = [p, i64, p, i64, u8, u8, p]
+        L.mylo_moe_route.argtypes = [p, i64, i64, i64, p, i64, u8, u8, p, p]
+        L.mylo_moe_combine.argtypes = [p, p, p, i64, i64, i64, u8, p]
         L.mylo_argmax_i32.argtypes = [p, i64]
         L.mylo_argmax_i32.restype = i64
         L.mylo_splitmix64.argtypes = [C.c_uint64, p]
@@ -291,6 +294,41 @@ def mlp_hidden(x, W_gate, W_up, hidden_size: int, intermediate_size: int, gate_w
         in_frac_bits, gate_out_frac, up_out_frac, down_in_frac, silu_in_frac, silu_lut_offset,
         silu_out_frac, _ptr(h), None))
     return h[0] if single else h
+
+
+def softmax_int(logits, exp_lut, lut_shift: int, frac_bits: int) -> np.ndarray:
+    """softmax.rs:24-64."""
+    lg = _c(logits, np.int32)
+    lut = _c(exp_lut, np.int16)
+    out = np.zeros(lg.size, np.int32)
+    _check("softmax_int", lib().mylo_softmax_int(_ptr(lg), lg.size, _ptr(lut), lut.size, lut_shift,
+                                                 frac_bits, _ptr(out)))
+    return out
+
+
+def moe_route(logits, k: int, exp_lut, lut_shift: int, prob_frac: int):
+    """Top-k experts per token (argmax_int repeated, lowest index on ties) and
+    softmax_int of their logits. logits [T, E] int32 -> (idx [T, k], prob [T, k])."""
+    lg = _c(logits, np.int32)
+    T, E = lg.shape
+    lut = _c(exp_lut, np.int16)
+    idx = np.zeros((T, k), np.int32)
+    prob = np.zeros((T, k), np.int32)
+    _check("moe_route", lib().mylo_moe_route(_ptr(lg), T, E, k, _ptr(lut), lut.size, lut_shift,
+                                             prob_frac, _ptr(idx), _ptr(prob)))
+    return idx, prob
+
+
+def moe_combine(y_experts, topk_prob, shared, prob_frac: int) -> np.ndarray:
+    """y_experts [T, k, H] int16, topk_prob [T, k], shared [T, H] -> out [T, H]."""
+    y = _c(y_experts, np.int16)
+    p = _c(topk_prob, np.int32)
+    sh = _c(shared, np.int16)
+    T, k, H = y.shape
+    out = np.zeros((T, H), np.int16)
+    _check("moe_combine", lib().mylo_moe_combine(_ptr(y), _ptr(p), _ptr(sh), T, k, H, prob_frac,
+                                                 _ptr(out)))
+    return out
 
 
 def argmax_int(values) -> int:

@@ -333,6 +333,100 @@ int mylo_mlp_int(const int16_t* x, int64_t M, const int8_t* W_gate, const int8_t
   return rc;
 }
 
+/* ---- softmax.rs:12-64 ----------------------------------------------------- */
+
+static int32_t exp_lut_lookup(int32_t x, const int16_t* exp_lut, int64_t lut_len, uint8_t lut_shift,
+                              int32_t one) {
+  if (x <= 0) return one;
+  uint32_t idx = (uint32_t)x >> lut_shift;
+  if ((int64_t)idx >= lut_len) return 0;
+  return (int32_t)exp_lut[idx];
+}
+
+int mylo_softmax_int(const int32_t* logits, int64_t n, const int16_t* exp_lut, int64_t lut_len,
+                     uint8_t lut_shift, uint8_t frac_bits, int32_t* out) {
+  if (n <= 0 || frac_bits > 30) return MYLO_ERR_SHAPE;
+  int32_t one = (int32_t)1 << frac_bits;
+  int32_t lut_one = lut_len > 0 ? (int32_t)exp_lut[0] : 1;
+  int32_t m = logits[0];
+  for (int64_t i = 1; i < n; ++i)
+    if (logits[i] > m) m = logits[i];
+  int64_t s64 = 0;
+  for (int64_t i = 0; i < n; ++i) {
+    int64_t d = (int64_t)m - (int64_t)logits[i];          /* saturating_sub */
+    int32_t diff = d > INT32_MAX ? INT32_MAX : (int32_t)d;
+    out[i] = exp_lut_lookup(diff, exp_lut, lut_len, lut_shift, lut_one);
+    s64 += out[i];
+  }
+  if (s64 > INT32_MAX || s64 < INT32_MIN) return MYLO_ERR_OVERFLOW; /* i32 sum */
+  int32_t s = (int32_t)s64;
+  if (s == 0) {
+    int32_t base = one / (int32_t)n;
+    int32_t rem = one - base * (int32_t)n;
+    for (int64_t i = 0; i < n; ++i) out[i] = base + (i < rem ? 1 : 0);
+    return MYLO_OK;
+  }
+  for (int64_t i = 0; i < n; ++i) {
+    int64_t num64 = (int64_t)out[i] * one;
+    if (num64 > INT32_MAX || num64 < INT32_MIN) return MYLO_ERR_OVERFLOW; /* e * one in i32 */
+    int32_t num = (int32_t)num64;
+    int32_t q = num / s, r = num % s;                      /* truncating, as Rust */
+    int32_t twice = (r < 0 ? -r : r) * 2, den_abs = s < 0 ? -s : s;
+    if (twice > den_abs || (twice == den_abs && (q & 1) != 0)) q = ((num > 0) == (s > 0)) ? q + 1 : q - 1;
+    out[i] = q;
+  }
+  return MYLO_OK;
+}
+
+/* ---- MoE layer composed from the reference primitives --------------------
+ * (the reference has no MoE; every step below is one of its functions)
+ *   logits[e] = clamp_i32(rescale_i64(dot(W_r[e], x), r_shift[e] + act_frac, router_frac))
+ *               (runtime/src/model.rs:297-307 semantics)
+ *   top-k     = k times argmax_int over the not yet chosen experts (sampling.rs:8-18:
+ *               ties go to the lowest index)
+ *   p         = softmax_int(logits[top-k], exp_lut, lut_shift, prob_frac) (softmax.rs:24-64)
+ *   y_j       = mlp_int(x, expert top-k[j])                          (mlp.rs:28-74)
+ *   out[h]    = clamp_i16(rescale_i64(sum_j p_j * y_j[h], prob_frac, 0) + shared[h])
+ *               with shared = mlp_int(x, shared expert). */
+int mylo_moe_route(const int32_t* logits, int64_t T, int64_t E, int64_t k, const int16_t* exp_lut,
+                   int64_t lut_len, uint8_t lut_shift, uint8_t prob_frac, int32_t* topk_idx,
+                   int32_t* topk_prob) {
+  if (T < 0 || E <= 0 || k <= 0 || k > E || k > 64) return MYLO_ERR_SHAPE;
+  for (int64_t t = 0; t < T; ++t) {
+    const int32_t* lg = logits + t * E;
+    unsigned char chosen[4096];
+    if (E > 4096) return MYLO_ERR_SHAPE;
+    memset(chosen, 0, (size_t)E);
+    int32_t sel[64];
+    for (int64_t j = 0; j < k; ++j) {
+      int64_t best = -1;
+      for (int64_t e = 0; e < E; ++e)
+        if (!chosen[e] && (best < 0 || lg[e] > lg[best])) best = e;
+      chosen[best] = 1;
+      topk_idx[t * k + j] = (int32_t)best;
+      sel[j] = lg[best];
+    }
+    int rc = mylo_softmax_int(sel, k, exp_lut, lut_len, lut_shift, prob_frac, topk_prob + t * k);
+    if (rc) return rc;
+  }
+  return MYLO_OK;
+}
+
+int mylo_moe_combine(const int16_t* y_experts, const int32_t* topk_prob, const int16_t* shared,
+                     int64_t T, int64_t k, int64_t H, uint8_t prob_frac, int16_t* out) {
+  if (T < 0 || k <= 0 || H <= 0 || prob_frac > 62) return MYLO_ERR_SHAPE;
+  for (int64_t t = 0; t < T; ++t)
+    for (int64_t h = 0; h < H; ++h) {
+      int64_t acc = 0;
+      for (int64_t j = 0; j < k; ++j)
+        acc += (int64_t)topk_prob[t * k + j] * (int64_t)y_experts[(t * k + j) * H + h];
+      int64_t v = 0;
+      mylo_rescale_i64(acc, prob_frac, 0, &v);
+      out[t * H + h] = mylo_clamp_i16_from_i64(v + (int64_t)shared[t * H + h]);
+    }
+  return MYLO_OK;
+}
+
 /* ---- sampling.rs:8-18 ---------------------------------------------------- */
 
 int64_t mylo_argmax_i32(const int32_t* v, int64_t n) {

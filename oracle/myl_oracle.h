@@ -119,6 +119,22 @@ int mylo_mlp_hidden(const int16_t* x, int64_t M, const int8_t* W_gate, const int
                     uint8_t silu_in_frac, int16_t silu_lut_offset, uint8_t silu_out_frac,
                     int16_t* h, int64_t* silu_wraps);
 
+/* softmax.rs:24-64 (exp LUT lookup softmax.rs:12-21, RNE division). */
+int mylo_softmax_int(const int32_t* logits, int64_t n, const int16_t* exp_lut, int64_t lut_len,
+                     uint8_t lut_shift, uint8_t frac_bits, int32_t* out);
+
+/* MoE routing (no counterpart in the reference; composed from its primitives):
+ * per token, k times argmax_int over the not yet chosen experts (lowest index
+ * wins ties, sampling.rs:8-18), then softmax_int over the k chosen logits. */
+int mylo_moe_route(const int32_t* logits, int64_t T, int64_t E, int64_t k, const int16_t* exp_lut,
+                   int64_t lut_len, uint8_t lut_shift, uint8_t prob_frac, int32_t* topk_idx,
+                   int32_t* topk_prob);
+
+/* MoE combine: out[t][h] = clamp_i16(rescale_i64(sum_j p[t][j] * y[t][j][h], prob_frac, 0)
+ *                                    + shared[t][h]); y is [T][k][H]. */
+int mylo_moe_combine(const int16_t* y_experts, const int32_t* topk_prob, const int16_t* shared,
+                     int64_t T, int64_t k, int64_t H, uint8_t prob_frac, int16_t* out);
+
 /* sampling.rs:8-18: first index of the maximum. */
 int64_t mylo_argmax_i32(const int32_t* v, int64_t n);
 

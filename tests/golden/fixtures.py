@@ -61,5 +61,9 @@ def op_vectors():
     return _load("op_vectors.json")
 
 
+def softmax_cases():
+    return _load("softmax_cases.json")
+
+
 def splitmix_kat():
     return _load("splitmix_kat.json")

@@ -279,6 +279,26 @@ def main():
     with open(os.path.join(HERE, "op_vectors.json"), "w") as f:
         json.dump(op, f, indent=1)
 
+    # softmax_int: the op golden vector softmax_basic plus cases computed by
+    # generate.py:119 softmax_int_ref (its LUT's first entry equals 2^frac_bits,
+    # where the reference's exp(0) lookup and `one` coincide).
+    sm_path = os.path.join(args.reference, "INTEGER_LLM", "conformance", "vectors", "op",
+                           "softmax_basic.golden.json")
+    with open(sm_path) as f:
+        sv = json.load(f)
+    softmax = [{"name": sv["name"], "logits": sv["inputs"]["logits"]["data"],
+                "exp_lut": sv["metadata"]["exp_lut"], "lut_shift": sv["metadata"]["lut_shift"],
+                "frac_bits": sv["metadata"]["frac_bits"], "probs": sv["outputs"]["probs"]["data"]}]
+    lut14 = [int(round(np.exp(-i / 256.0) * (1 << 14))) for i in range(16384)]
+    rng = np.random.default_rng(99)
+    for n, spread in ((4, 300), (4, 3000), (8, 50), (2, 0), (4, 40000)):
+        lg = [int(v) for v in rng.integers(-spread - 1, spread + 1, size=n)]
+        softmax.append({"name": f"softmax_n{n}_spread{spread}", "logits": lg, "exp_lut": lut14,
+                        "lut_shift": 0, "frac_bits": 14,
+                        "probs": [int(v) for v in G.softmax_int_ref(lg, lut14, 0, 14)]})
+    with open(os.path.join(HERE, "softmax_cases.json"), "w") as f:
+        json.dump(softmax, f, separators=(",", ":"))
+
     with open(os.path.join(HERE, "linear_cases.json"), "w") as f:
         json.dump(make_linear(G), f, separators=(",", ":"))
     with open(os.path.join(HERE, "mlp_cases.json"), "w") as f:

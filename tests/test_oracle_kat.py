@@ -242,6 +242,20 @@ def test_backend_parity_fixtures():  # test_backend_parity.rs:160-255
     assert y.tolist() == mlp["y"]
 
 
+@pytest.mark.parametrize("case", fixtures.softmax_cases(), ids=lambda c: c["name"])
+def test_softmax_int_fixture(case):  # softmax.rs:24-64, golden vector softmax_basic
+    out = O.softmax_int(case["logits"], case["exp_lut"], case["lut_shift"], case["frac_bits"])
+    assert out.tolist() == case["probs"]
+
+
+def test_moe_route_ties_go_to_lowest_index():
+    lut = [int(round(np.exp(-i / 256.0) * (1 << 14))) for i in range(16384)]
+    logits = np.array([[5, 9, 9, 1, 9, 3], [0, 0, 0, 0, 0, 0]], np.int32)
+    idx, prob = O.moe_route(logits, 3, lut, 0, 14)
+    assert idx.tolist() == [[1, 2, 4], [0, 1, 2]]
+    assert prob[1].tolist() == O.softmax_int([0, 0, 0], lut, 0, 14).tolist()
+
+
 def test_thread_count_does_not_change_results():
     K, N, M = 896, 300, 4
     W = gen.int8_tensor(91, N * K)
