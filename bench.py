@@ -49,6 +49,8 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+from myelith_b200.synthetic import MOE_CONFIG4 as MOE, moe_layer  # noqa: E402
+
 METRIC = "W8A16 GEMM TOPS & GEMV GB/s; 7B-shape int decode tok/s at 1/2/4/8 GPU"
 SHAPES = [(3584, 18944), (18944, 3584)]  # (K, N): gate/up, down
 M_HEAD = 2048
@@ -207,6 +209,93 @@ def run_reference(args, rank: int, world: int) -> None:
 
 
 # ---------------------------------------------------------------------------------------
+# MoE layer
+
+def moe_ops(T: int) -> float:
+    """Algorithmic integer ops of one MoE layer over T tokens (2 per MAC):
+    router, the top-k experts' gate/up/down and the shared expert."""
+    H, I, E, k, Is = MOE["H"], MOE["I"], MOE["E"], MOE["k"], MOE["shared_I"]
+    return 2.0 * T * (E * H + k * 3 * I * H + 3 * Is * H)
+
+
+def bench_moe(ctx, dev, stream, rank: int, world: int, local: int, steps: int, warmup: int,
+              max_over_ranks, barrier) -> dict:
+    """The MoE layer at config 4: 4096 tokens per step in total. One GPU: the
+    fused layer (myl_moe_dev). N GPUs: expert parallelism, each rank holds
+    E/N experts and 4096/N tokens, NCCL all_to_all dispatch and return."""
+    import torch
+
+    import myelith_b200 as myl
+    from myelith_b200 import ep
+
+    H, I, E, k, Is, T = (MOE[n] for n in ("H", "I", "E", "k", "shared_I", "T"))
+    first, last = ep.shard_range(E, rank, world)
+    moe, shared = moe_layer(ctx, H, I, E, k, Is, first, last - first, attach_shared=world == 1)
+    Tr = T // world
+    xr = np.random.default_rng(4100 + rank)
+    x_h = np.clip(np.rint(xr.normal(0, 1024, size=(Tr, H))), -32767, 32767).astype(np.int16)
+    with torch.cuda.stream(stream):
+        x = torch.from_numpy(x_h).to(dev)
+        out = torch.empty_like(x)
+        idx = torch.empty((Tr, k), dtype=torch.int32, device=dev)
+        prob = torch.empty_like(idx)
+    stream.synchronize()
+    if world == 1:
+        def layer():
+            moe.dev(x, out, idx, prob, stream)
+    else:
+        epl = ep.ExpertParallelMoe(ep.LibMoeLocal(moe, shared), E, k, H, rank, world)
+
+        def layer():
+            out.copy_(epl(x))
+
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            layer()
+        stream.synchronize()
+        barrier()
+        l0 = ctx.launch_count
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(steps):
+            layer()
+        b.record(stream)
+        stream.synchronize()
+        launches = ctx.launch_count - l0
+    ctx.synchronize()
+    ms = max_over_ranks(a.elapsed_time(b) / steps)
+    load = torch.bincount(idx.reshape(-1).long(), minlength=E).cpu().numpy()
+    res = {"workload": "config4: MoE layer, hidden 2048, 64 experts x MLP 1408, top-4, shared "
+                       "expert 5632, 4096 tokens per step",
+           "parallelism": "single GPU (myl_moe_dev)" if world == 1 else f"ep{world} (NCCL all_to_all)",
+           "tokens_per_rank": Tr, "ms_per_layer": round(ms, 4),
+           "tops": round(moe_ops(T) / (ms * 1e-3) / 1e12, 2),
+           "tokens_per_s": round(T / (ms * 1e-3), 1),
+           "ops_per_layer": moe_ops(T), "gpu_launches_per_layer": launches / steps,
+           "expert_rows_min_max_rank0": [int(load.min()), int(load.max())]}
+    if world == 1:
+        # end to end through the host-pointer entry point (myl_moe_forward)
+        xp = torch.from_numpy(x_h).pin_memory().numpy()
+        yp = torch.empty((Tr, H), dtype=torch.int16).pin_memory().numpy()
+        L = myl.load_library()
+        for _ in range(warmup):
+            myl._check("myl_moe_forward", L.myl_moe_forward(ctx.handle, moe.handle, xp.ctypes.data, Tr,
+                                                            yp.ctypes.data))
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            myl._check("myl_moe_forward", L.myl_moe_forward(ctx.handle, moe.handle, xp.ctypes.data, Tr,
+                                                            yp.ctypes.data))
+        e2e_s = (time.perf_counter() - t0) / steps
+        res["e2e"] = {"ms_per_layer": round(e2e_s * 1e3, 4),
+                      "tops": round(moe_ops(T) / e2e_s / 1e12, 2),
+                      "h2d_bytes_per_step": int(x_h.nbytes), "d2h_bytes_per_step": int(yp.nbytes)}
+    moe.release()
+    shared.release()
+    return res
+
+
+# ---------------------------------------------------------------------------------------
 # GPU arm
 
 
@@ -219,6 +308,7 @@ def main() -> None:
     ap.add_argument("--m", type=int, default=M_HEAD)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-moe", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -448,6 +538,12 @@ def main() -> None:
                 "per_shape_gbs": [round(g, 1) for g in gemv_gbs],
                 "bytes": "N*K weights + 2K act + 2N out + N shift bytes per launch"}
 
+    # ---- MoE layer (config 4): every rank takes part (all_to_all at N > 1) ----
+    moe = None
+    if not args.no_moe:
+        moe = bench_moe(ctx, dev, stream, rank, world, local, max(3, args.steps // 2), args.warmup,
+                        max_over_ranks, barrier)
+
     # ---- CPU baseline (rank 0, N=1) ----
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -483,6 +579,7 @@ def main() -> None:
             "wall_s_timed": round(wall, 4),
             "gemv": gemv,
             "sweep": sweep,
+            "moe": moe,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -126,6 +126,28 @@ __device__ __forceinline__ int16_t silu_combine(const SiluParams& sp, int32_t g,
   return int16_t(clamp_i64(rescale_i64_signed(prod, sp.s2), -32768, 32767));
 }
 
+// silu_combine split for the tensor-core epilogue, where g and u are already
+// clamped to int16: silu_index gives the table index of g (branch-free in
+// s1), silu_product rescales lut[idx] * u. |lut * u| <= 2^30 fits in i32, so
+// the i64 rescale of mlp.rs:60-62 equals the i32 round-half-even shift for
+// s2 in [1, 30]; s2 >= 31 always rounds |prod| <= 2^30 to 0 (2^30 / 2^31 is a
+// tie that goes to the even 0); s2 <= 0 takes the i64 path.
+__device__ __forceinline__ int silu_index(const SiluParams& sp, int32_t g) {
+  const int32_t right = rshift_rne_i32(g, max(sp.s1, 1));
+  const int32_t gd = sp.s1 > 0 ? right : int32_t(uint32_t(g) << max(-sp.s1, 0));
+  const int idx = int(int16_t(uint16_t(uint32_t(gd) + uint32_t(sp.offset))));
+  return max(0, min(idx, sp.lut_hi));
+}
+
+__device__ __forceinline__ int32_t silu_product(const SiluParams& sp, int32_t lut_value, int32_t u) {
+  const int32_t prod = lut_value * u;
+  if (sp.s2 > 0) {
+    if (sp.s2 >= 31) return 0;
+    return max(-32768, min(rshift_rne_i32(prod, sp.s2), 32767));
+  }
+  return int32_t(clamp_i64(rescale_i64_signed(int64_t(prod), sp.s2), -32768, 32767));
+}
+
 // Stores h for (m, channel pair i) (if y is given) and its byte planes (if
 // requested).
 __device__ __forceinline__ void silu_store(const Epilogue& ep, int64_t m, int64_t i, int16_t h) {

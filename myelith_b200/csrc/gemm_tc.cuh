@@ -378,19 +378,51 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int64_t mc = m0 + c;
         if (mode == EPI_SILU) {
           // Gate (even row) and up (odd row) of channel pair n/2 sit in
-          // adjacent lanes; every lane takes part in the shuffles, even lanes
-          // store the first half of the tokens, odd lanes the second.
+          // adjacent lanes. One exchange per token pair gives the even lane
+          // (gate, up) of the first NC/2 tokens and the odd lane those of the
+          // last NC/2, so every lane computes and stores NC/2 products. The
+          // steps run over all NC/2 tokens at a time (independent table loads
+          // in flight together).
+          constexpr int NH = NC / 2;
           const bool even = (row & 1) == 0;
+          int32_t v[NC];
 #pragma unroll
           for (int j = 0; j < NC; ++j) {
-            int32_t v = 0;
+            v[j] = 0;
             if (n < N)
-              v = fast ? r32.apply(int32_t(hi[j]), int32_t(lo[j]))
-                       : int32_t(rq.apply(int64_t(int32_t(hi[j])) * 256 + int64_t(int32_t(lo[j]))));
-            const int32_t p = __shfl_xor_sync(0xffffffffu, v, 1);
-            const int64_t m = mc + j;
-            if (((j < NC / 2) == even) && n < N && m < Mend)
-              silu_store(e, m, n >> 1, silu_combine(e.silu, even ? v : p, even ? p : v));
+              v[j] = fast ? r32.apply(int32_t(hi[j]), int32_t(lo[j]))
+                          : int32_t(rq.apply(int64_t(int32_t(hi[j])) * 256 + int64_t(int32_t(lo[j]))));
+          }
+          int32_t g[NH], u[NH];
+#pragma unroll
+          for (int j = 0; j < NH; ++j) {
+            const int32_t mine = even ? v[j] : v[j + NH];
+            const int32_t other = __shfl_xor_sync(0xffffffffu, even ? v[j + NH] : v[j], 1);
+            g[j] = even ? mine : other;
+            u[j] = even ? other : mine;
+          }
+          const SiluParams& sp = e.silu;
+#pragma unroll
+          for (int j = 0; j < NH; ++j) g[j] = __ldg(sp.lut + silu_index(sp, g[j]));
+          const int64_t mh = mc + (even ? 0 : NH);
+          const int64_t jlim = n < N ? Mend - mh : 0;  // tokens mh + j < Mend are stored
+          if (e.y == nullptr && sp.h_hi != nullptr && sp.s2 >= 1 && sp.s2 <= 30) {
+            int8_t* ph = sp.h_hi + mh * sp.ldp + (n >> 1);
+            uint8_t* pl = sp.h_lo + mh * sp.ldp + (n >> 1);
+#pragma unroll
+            for (int j = 0; j < NH; ++j) {
+              const int32_t h = max(-32768, min(rshift_rne_i32(g[j] * u[j], sp.s2), 32767));
+              if (j < jlim) {
+                *ph = int8_t(h >> 8);
+                *pl = uint8_t(h & 0xFF);
+              }
+              ph += sp.ldp;
+              pl += sp.ldp;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < NH; ++j)
+              if (j < jlim) silu_store(e, mh + j, n >> 1, int16_t(silu_product(sp, g[j], u[j])));
           }
           continue;
         }

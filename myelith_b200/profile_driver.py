@@ -1,6 +1,7 @@
 """Runs one W8A16 linear shape repeatedly, for profiler captures (ncu).
 
     python -m myelith_b200.profile_driver --M 1 --K 3584 --N 18944 --iters 6
+    python -m myelith_b200.profile_driver --moe --iters 4      (config-4 MoE layer)
 
 Uses the device path (myl_linear_dev) with rotating weight sets whose total
 size exceeds the 126 MB L2, so that DRAM counters reflect HBM traffic. Three
@@ -23,7 +24,11 @@ def main() -> None:
     ap.add_argument("--N", type=int, default=18944)
     ap.add_argument("--iters", type=int, default=6)
     ap.add_argument("--sets", type=int, default=0, help="weight sets (0: enough to exceed 2x L2)")
+    ap.add_argument("--moe", action="store_true", help="the config-4 MoE layer (myl_moe_dev)")
+    ap.add_argument("--tokens", type=int, default=0, help="MoE tokens (0: 4096)")
     args = ap.parse_args()
+    if args.moe:
+        return moe(args)
 
     import torch
 
@@ -53,6 +58,33 @@ def main() -> None:
         s.synchronize()
     ctx.synchronize()
     print(f"M={M} K={K} N={N} sets={sets}: {a.elapsed_time(b) / args.iters * 1e3:.2f} us/call, "
+          f"{ctx.launch_count} launches")
+
+
+def moe(args) -> None:
+    import torch
+
+    import myelith_b200 as myl
+    from myelith_b200.synthetic import MOE_CONFIG4 as C, activations, moe_layer
+
+    ctx = myl.Context(0)
+    layer, shared = moe_layer(ctx, C["H"], C["I"], C["E"], C["k"], C["shared_I"])
+    T = args.tokens or C["T"]
+    x = torch.from_numpy(activations(np.random.default_rng(6), (T, C["H"]))).cuda()
+    y = torch.empty_like(x)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            layer.dev(x, y, stream=s)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(s)
+        for _ in range(args.iters):
+            layer.dev(x, y, stream=s)
+        b.record(s)
+        s.synchronize()
+    ctx.synchronize()
+    print(f"moe T={T}: {a.elapsed_time(b) / args.iters * 1e3:.2f} us/layer, "
           f"{ctx.launch_count} launches")
 
 

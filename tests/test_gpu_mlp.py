@@ -190,3 +190,24 @@ def test_requant_plan_bias_device(ctx):
     lin = O.linear_w8a16(x, W.reshape(-1), K, ws, 6, 5)
     ref = np.stack([O.add_bias_i16(row, bias, bsh, 5) for row in lin])
     assert np.array_equal(yd.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("silu_out,up_out,down_in", [(8, 7, 7), (8, 7, 15), (16, 16, 1), (15, 16, 0),
+                                                     (2, 2, 8), (8, 7, 0), (4, 4, 12)])
+def test_mlp_product_rescale_range(ctx, silu_out, up_out, down_in):
+    """The SiLU product rescale s2 = silu_out + up_out - down_in across the
+    32-bit epilogue's cases: s2 in [1, 30], s2 >= 31 (always 0), s2 = 0 and
+    s2 < 0 (left shift, clamped)."""
+    rng = np.random.default_rng(silu_out * 100 + up_out * 10 + down_in)
+    c, p = _random_case(rng, 256, 320)
+    p = dict(p, silu_out=silu_out, up_out=up_out, down_in=down_in)
+    m = _mlp(ctx, c, p)
+    x = np.clip(np.rint(rng.normal(0, 3000, size=(70, 256))), -32767, 32767).astype(np.int16)
+    ref = _oracle(c, p, x)[0]
+    for mode in ("gemv", "tc"):
+        ctx.set_dispatch(**MODES[mode])
+        try:
+            xs = x[:3] if mode == "gemv" else x
+            assert np.array_equal(m(xs), ref[: len(xs)]), mode
+        finally:
+            ctx.set_dispatch()
