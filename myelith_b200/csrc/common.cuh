@@ -107,6 +107,14 @@ __device__ __forceinline__ int32_t rshift_rne_i32(int32_t v, int s) {
   return q + ((r > h) | ((r == h) & (q & 1)));
 }
 
+// Round-half-even right shift by s in [1, 30] with one add: for q = v >> s,
+// (v + c + (q & 1)) >> s with c = 2^(s-1) - 1 adds 1 to q exactly when the
+// remainder is above half, or equal to half with q odd (fixed_point.rs:39-53).
+// Needs v + 2^(s-1) inside i32.
+__device__ __forceinline__ int32_t rne_add_i32(int32_t v, int s, int32_t c) {
+  return (v + c + ((v >> s) & 1)) >> s;
+}
+
 // mlp.rs:52-63 for one channel pair: gate g and up u are the clamped int16
 // outputs of the two projections. g goes to the LUT domain with rescale (i32,
 // fixed_point.rs:173-180), is truncated to i16 and offset with Rust release
@@ -133,7 +141,8 @@ __device__ __forceinline__ int16_t silu_combine(const SiluParams& sp, int32_t g,
 // s2 in [1, 30]; s2 >= 31 always rounds |prod| <= 2^30 to 0 (2^30 / 2^31 is a
 // tie that goes to the even 0); s2 <= 0 takes the i64 path.
 __device__ __forceinline__ int silu_index(const SiluParams& sp, int32_t g) {
-  const int32_t right = rshift_rne_i32(g, max(sp.s1, 1));
+  const int s = max(sp.s1, 1);
+  const int32_t right = rne_add_i32(g, s, (1 << (s - 1)) - 1);  // |g| <= 2^15
   const int32_t gd = sp.s1 > 0 ? right : int32_t(uint32_t(g) << max(-sp.s1, 0));
   const int idx = int(int16_t(uint16_t(uint32_t(gd) + uint32_t(sp.offset))));
   return max(0, min(idx, sp.lut_hi));
@@ -332,6 +341,14 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
         "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+// 32 lanes x 8 columns.
+__device__ __forceinline__ void tmem_ld_32x32b_x8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7])
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() {

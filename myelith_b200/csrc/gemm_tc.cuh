@@ -21,13 +21,15 @@
 // registers, and a warp's stores for one token are 64 contiguous bytes.
 //
 // Schedule: persistent, one CTA per SM looping over work units
-// (channel tile, token tile, K slice), 320 threads:
+// (channel tile, token tile, K slice), 576 threads:
 //   warp 0      TMA producer: W tile + x_hi tile + x_lo tile per 128-byte K
 //               step into a STAGES-deep ring of 128B-swizzled smem stages.
 //   warp 1      TMEM allocator; lane 0 issues 2 x 4 MMAs per K step and
 //               commits each smem stage back to the producer.
-//   warps 2..9  epilogue: tcgen05.ld of H and L, requant, store. Warp w reads
-//               TMEM lanes 32*(w%4)..32*(w%4)+31 and half of the BN columns.
+//   warps 2..17 epilogue: tcgen05.ld of H and L, requant, store. Warp w reads
+//               TMEM lanes 32*(w%4)..32*(w%4)+31 and a quarter of the BN
+//               columns; four warps per SM sub-partition hide the latency of
+//               the epilogue's dependent integer steps.
 // Two accumulator buffers (2 x (H, L) x BN columns) let the epilogue of one
 // unit run while the MMAs of the next unit accumulate into the other buffer.
 //
@@ -41,7 +43,7 @@
 namespace myl {
 
 constexpr int TC_BK = 128;  // K bytes per stage = one 128-byte swizzle row
-constexpr int TC_EPI_WARPS = 8;  // two per TMEM lane quarter, each owning half the columns
+constexpr int TC_EPI_WARPS = 16;  // four per TMEM lane quarter, each owning a quarter of the columns
 constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;
 
 template <int BN, int STAGES>
@@ -173,13 +175,16 @@ struct Requant32 {
   }
 };
 
-// Loads NC (16 or 32) columns of the H and L accumulators of this thread's lane.
+// Loads NC (8, 16 or 32) columns of the H and L accumulators of this thread's lane.
 template <int NC>
 __device__ __forceinline__ void tmem_ld_pair(uint32_t taddr_h, uint32_t taddr_l, uint32_t (&h)[NC],
                                              uint32_t (&l)[NC]) {
   if constexpr (NC == 32) {
     tmem_ld_32x32b_x32(taddr_h, h);
     tmem_ld_32x32b_x32(taddr_l, l);
+  } else if constexpr (NC == 8) {
+    tmem_ld_32x32b_x8(taddr_h, h);
+    tmem_ld_32x32b_x8(taddr_l, l);
   } else {
     tmem_ld_32x32b_x16(taddr_h, h);
     tmem_ld_32x32b_x16(taddr_l, l);
@@ -205,7 +210,9 @@ __device__ __forceinline__ void store_column(T* yp, int64_t ldy, int64_t m0, int
   }
 }
 
-template <int BN, int STAGES>
+// MODE (EpiMode) is a template parameter so that each instantiation carries
+// only its own epilogue: smaller code and fewer registers per kernel.
+template <int BN, int STAGES, int MODE>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_w8a16_tc_kernel(const __grid_constant__ CUtensorMap tm_w,
                          const __grid_constant__ CUtensorMap tm_xhi,
@@ -288,7 +295,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       int g = 0, lt = 0;
       bool stop = false;
       for (int u = blockIdx.x; u < units && !stop; u += gridDim.x, ++lt) {
-        const int nkt = work.decode(u, BN, M).nkt;
+        const TcUnit wu = work.decode(u, BN, M);
+        const int nkt = wu.nkt;
+        // A tile with fewer valid tokens than BN (the end of M or of an expert's
+        // rows) runs N = valid rounded up to 16 (kind::i8 with M = 128 takes N
+        // in multiples of 16); the columns above are never read back.
+        const int64_t valid = wu.m_end - wu.m_begin;
+        const uint32_t nmma = valid >= BN ? uint32_t(BN) : uint32_t((valid + 15) & ~int64_t(15));
+        const uint32_t idesc_hi = (Cfg::IDESC_HI & ~(0x3Fu << 17)) | ((nmma >> 3) << 17);
+        const uint32_t idesc_lo = (Cfg::IDESC_LO & ~(0x3Fu << 17)) | ((nmma >> 3) << 17);
         const int b = lt & 1;
         const uint32_t tph = uint32_t(lt >> 1) & 1u;
         if (!mbar_wait_bounded(smem_addr(&ctl.tempty[b]), tph ^ 1u, timeout_ns, abort)) {
@@ -312,8 +327,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const uint32_t off = uint32_t(kk) * 32u;
             const uint64_t dw = smem_desc_k_sw128(aw + off);
             const uint32_t accum = (i > 0 || kk > 0) ? 1u : 0u;
-            mma_i8(d_hi, dw, smem_desc_k_sw128(axh + off), Cfg::IDESC_HI, accum);
-            mma_i8(d_lo, dw, smem_desc_k_sw128(axl + off), Cfg::IDESC_LO, accum);
+            mma_i8(d_hi, dw, smem_desc_k_sw128(axh + off), idesc_hi, accum);
+            mma_i8(d_lo, dw, smem_desc_k_sw128(axl + off), idesc_lo, accum);
           }
           mma_commit(smem_addr(&ctl.empty[s]));  // frees the stage when these MMAs finish
         }
@@ -328,11 +343,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
     }
   } else {
-    // ---------------- epilogue (warps 2..9) ----------------
-    constexpr int HALF = BN / 2;                 // columns per epilogue warp
-    constexpr int NC = HALF < 32 ? HALF : 32;    // columns per TMEM load
+    // ---------------- epilogue (warps 2..17) ----------------
+    constexpr int QCOLS = BN / 4;                // columns per epilogue warp
+    constexpr int NC = QCOLS < 16 ? QCOLS : 16;  // columns per TMEM load
     const int q = warp & 3;
-    const int col0 = ((warp - 2) >> 2) * HALF;
+    const int col0 = ((warp - 2) >> 2) * QCOLS;
     const int row = q * 32 + lane;
     int lt = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++lt) {
@@ -356,7 +371,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int64_t Mend = wu.m_end;
       const uint32_t tq = tmem + (uint32_t(q * 32) << 16) + uint32_t(b * Cfg::BUF_COLS + col0);
       Epilogue e = ep;
-      if (e.mode == EPI_ACC_I64) e.y = static_cast<int64_t*>(e.y) + int64_t(wu.ks) * slice_stride;
+      if (MODE == EPI_ACC_I64) e.y = static_cast<int64_t*>(e.y) + int64_t(wu.ks) * slice_stride;
       if (wu.p_off) {  // per-channel parameters of this group
         e.shift = e.shift ? e.shift + wu.p_off : nullptr;
         e.mult = e.mult ? e.mult + wu.p_off : nullptr;
@@ -364,7 +379,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
       // Channel parameters, once per unit.
       int shift = 0;
-      const int mode = e.mode;
+      constexpr int mode = MODE;
       if (n < N && mode != EPI_ACC_I64) shift = e.shift[n];
       const bool fast = (mode == EPI_SHIFT || mode == EPI_SILU) && shift >= 8 && shift <= 38;
       Requant32 r32;
@@ -372,7 +387,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       ChannelRequant rq;
       if (n < N && !fast && mode != EPI_ACC_I64) rq.load(e, n);
 #pragma unroll 1
-      for (int c = 0; c < HALF; c += NC) {
+      for (int c = 0; c < QCOLS; c += NC) {
+        if (m0 + c >= Mend) break;  // warp-uniform: no stored token left in this warp's columns
         uint32_t hi[NC], lo[NC];
         tmem_ld_pair<NC>(tq + c, tq + BN + c, hi, lo);
         const int64_t mc = m0 + c;
@@ -409,15 +425,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           if (e.y == nullptr && sp.h_hi != nullptr && sp.s2 >= 1 && sp.s2 <= 30) {
             int8_t* ph = sp.h_hi + mh * sp.ldp + (n >> 1);
             uint8_t* pl = sp.h_lo + mh * sp.ldp + (n >> 1);
+            const int32_t c2 = (1 << (sp.s2 - 1)) - 1;
+            const int ld = int(sp.ldp);  // NH rows of planes: offsets fit in 32 bits
 #pragma unroll
             for (int j = 0; j < NH; ++j) {
-              const int32_t h = max(-32768, min(rshift_rne_i32(g[j] * u[j], sp.s2), 32767));
+              // |lut * u| <= 2^30: the one-add rounding stays inside i32
+              const int32_t h = max(-32768, min(rne_add_i32(g[j] * u[j], sp.s2, c2), 32767));
               if (j < jlim) {
-                *ph = int8_t(h >> 8);
-                *pl = uint8_t(h & 0xFF);
+                ph[j * ld] = int8_t(h >> 8);
+                pl[j * ld] = uint8_t(h & 0xFF);
               }
-              ph += sp.ldp;
-              pl += sp.ldp;
             }
           } else {
 #pragma unroll

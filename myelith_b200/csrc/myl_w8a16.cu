@@ -318,13 +318,13 @@ template <> struct TcStages<32> { static constexpr int value = 8; };
 template <> struct TcStages<64> { static constexpr int value = 6; };
 template <> struct TcStages<128> { static constexpr int value = 4; };
 
-template <int BN>
-static int launch_tc_variant(myl_ctx* ctx, const myl_weight* w, const CUtensorMap& tm_xhi,
-                             const CUtensorMap& tm_xlo, int64_t M, const TcWork& work,
-                             const Epilogue& ep, int64_t slice_stride, cudaStream_t st) {
+template <int BN, int MODE>
+static int launch_tc_mode(myl_ctx* ctx, const myl_weight* w, const CUtensorMap& tm_xhi,
+                          const CUtensorMap& tm_xlo, int64_t M, const TcWork& work,
+                          const Epilogue& ep, int64_t slice_stride, cudaStream_t st) {
   constexpr int STAGES = TcStages<BN>::value;
   using Cfg = TcCfg<BN, STAGES>;
-  auto fn = gemm_w8a16_tc_kernel<BN, STAGES>;
+  auto fn = gemm_w8a16_tc_kernel<BN, STAGES, MODE>;
   TRY(kernel_smem_occupancy(ctx->device, reinterpret_cast<const void*>(fn), TC_THREADS,
                             Cfg::SMEM_BYTES, nullptr));
   // Grouped work is sized on the device (the router's tile table): one CTA per
@@ -339,6 +339,24 @@ static int launch_tc_variant(myl_ctx* ctx, const myl_weight* w, const CUtensorMa
   CUDA_TRY(cudaGetLastError());
   ctx->launches++;
   return MYL_OK;
+}
+
+template <int BN>
+static int launch_tc_variant(myl_ctx* ctx, const myl_weight* w, const CUtensorMap& tm_xhi,
+                             const CUtensorMap& tm_xlo, int64_t M, const TcWork& work,
+                             const Epilogue& ep, int64_t slice_stride, cudaStream_t st) {
+  switch (ep.mode) {
+    case EPI_ACC_I64:
+      return launch_tc_mode<BN, EPI_ACC_I64>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
+    case EPI_SHIFT:
+      return launch_tc_mode<BN, EPI_SHIFT>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
+    case EPI_MULT:
+      return launch_tc_mode<BN, EPI_MULT>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
+    case EPI_SILU:
+      return launch_tc_mode<BN, EPI_SILU>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
+    default:
+      return fail(MYL_ERR_ARG, "unknown epilogue mode %d", ep.mode);
+  }
 }
 
 static int tc_token_tile(const myl_ctx* ctx, int64_t M) {
