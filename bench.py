@@ -363,9 +363,9 @@ def main() -> None:
         x1 = torch.from_numpy(x1_h).to(dev)
         x2 = torch.from_numpy(x2_h).to(dev)
         ldp1, ldp2 = (K1 + 15) // 16 * 16, (k2 + 15) // 16 * 16
-        p1h = torch.empty((M, ldp1), dtype=torch.int8, device=dev)
+        p1h = torch.empty((M, ldp1), dtype=torch.uint8, device=dev)
         p1l = torch.empty((M, ldp1), dtype=torch.uint8, device=dev)
-        p2h = torch.empty((M, ldp2), dtype=torch.int8, device=dev)
+        p2h = torch.empty((M, ldp2), dtype=torch.uint8, device=dev)
         p2l = torch.empty((M, ldp2), dtype=torch.uint8, device=dev)
         y1 = torch.empty((M, n1), dtype=torch.int16, device=dev)
         y2 = torch.empty((M, N2), dtype=torch.int16, device=dev)

@@ -141,17 +141,18 @@ int myl_requant_acc_dev(myl_ctx* ctx, const myl_requant* rq, const int64_t* acc,
                         void* y, int64_t ldy, void* stream);
 
 /* Splits int16 activations into the byte planes the tensor-core GEMM reads:
- * x = 256*hi + lo, hi = x >> 8 (int8), lo = x & 255 (uint8); planes are
- * [M][ldp] (ldp a multiple of 16, columns K..ldp-1 zeroed, 16-byte aligned).
+ * two unsigned bytes hi = (x >> 8) + 128 (offset binary) and lo = x & 255,
+ * x = 256*hi + lo - 32768; planes are [M][ldp] (ldp a multiple of 16,
+ * 16-byte aligned; columns K..ldp-1 hold x = 0, i.e. hi = 128, lo = 0).
  * A producer kernel that writes the planes directly skips this pass. */
 int myl_split_hilo_dev(myl_ctx* ctx, const int16_t* x, int64_t M, int64_t K, int64_t ldx,
-                       int8_t* xhi, uint8_t* xlo, int64_t ldp, void* stream);
+                       uint8_t* xhi, uint8_t* xlo, int64_t ldp, void* stream);
 
 /* Tensor-core GEMM from byte planes (any M >= 1). rq = NULL stores exact
  * int64 accumulators into y (as myl_linear_acc_dev); otherwise y is the
  * requantised output of rq's mode. */
 int myl_linear_planes_dev(myl_ctx* ctx, const myl_weight* w, const myl_requant* rq,
-                          const int8_t* xhi, const uint8_t* xlo, int64_t ldp, int64_t M, void* y,
+                          const uint8_t* xhi, const uint8_t* xlo, int64_t ldp, int64_t M, void* y,
                           int64_t ldy, void* stream);
 
 /* --- MLP: mlp_int (kernels/src/mlp.rs:28-74) ----------------------------------

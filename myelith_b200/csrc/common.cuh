@@ -45,8 +45,8 @@ struct SiluParams {
   int offset;        // silu_lut_offset (i16)
   int s1;            // gate_out_frac - silu_in_frac, signed, in [-31, 30]
   int s2;            // silu_out_frac + up_out_frac - down_in_frac, signed, in [-63, 62]
-  int8_t* h_hi;      // optional byte planes of h for the down projection: [M][ldp]
-  uint8_t* h_lo;
+  uint8_t* h_hi;     // optional byte planes of h for the down projection: [M][ldp],
+  uint8_t* h_lo;     // hi = (h >> 8) + 128, lo = h & 255 (as split_hilo_kernel)
   int64_t ldp;
 };
 
@@ -162,7 +162,7 @@ __device__ __forceinline__ int32_t silu_product(const SiluParams& sp, int32_t lu
 __device__ __forceinline__ void silu_store(const Epilogue& ep, int64_t m, int64_t i, int16_t h) {
   if (ep.y) static_cast<int16_t*>(ep.y)[m * ep.ldy + i] = h;
   if (ep.silu.h_hi) {
-    ep.silu.h_hi[m * ep.silu.ldp + i] = int8_t(h >> 8);
+    ep.silu.h_hi[m * ep.silu.ldp + i] = uint8_t((h >> 8) + 128);
     ep.silu.h_lo[m * ep.silu.ldp + i] = uint8_t(h & 0xFF);
   }
 }

@@ -5,15 +5,23 @@
 // must equal linear.rs:61-68 for its (token, channel).
 //
 // Split-byte exactness. The tensor core multiplies 8-bit operands, the
-// activations are int16. Each activation is split as x = 256*hi + lo with
-// hi = x >> 8 (signed byte) and lo = x & 255 (unsigned byte), so
-//   sum_k w*x = 256 * sum_k w*hi + sum_k w*lo.
-// Two kind::i8 MMAs (s8 x s8 and s8 x u8) accumulate the two sums in two int32
-// TMEM accumulators H and L. |w*hi| <= 2^14 and |w*lo| < 2^15, so both int32
-// sums are exact for K <= 65536 (the host splits longer K into slices whose
-// exact int64 partials are added). The epilogue's value 256*H + L is the
-// reference's exact i64 accumulator; the requant is applied to it once
-// (fixed_point.rs:184-191). The tensor pipe does 2x the algorithmic MACs.
+// activations are int16. Each activation is split into two unsigned bytes,
+// hi = (x >> 8) + 128 (offset binary) and lo = x & 255, so that
+// x = 256*hi + lo - 32768 and
+//   sum_k w*x = 256*H' + L - 32768*S,  H' = sum_k w*hi, L = sum_k w*lo,
+// S = sum_k w (the weight row's sum over the K slice). Both bytes are
+// unsigned, so one kind::i8 MMA (s8 weights x u8 activations) with N = 2*BN
+// computes H' and L together: the B operand is the x_hi tile followed by the
+// x_lo tile, and the accumulator's columns are H' | L. |w*hi|, |w*lo| <= 32640,
+// so both int32 sums are exact for K <= 65536 (the host splits longer K into
+// slices whose exact int64 partials are added). The epilogue forms
+// H = H' - 128*S in wrapping 32-bit arithmetic, which is exact because the
+// true H = sum_k w*(x >> 8) fits in int32; S comes from a per-row prefix sum
+// over K tiles made at registration. 256*H + L is the reference's exact i64
+// accumulator; the requant is applied to it once (fixed_point.rs:184-191).
+// The tensor pipe does 2x the algorithmic MACs; one MMA of N = 256 reads 12 KB
+// of shared memory per 128 x 256 x 32 step instead of the 16 KB that two
+// MMAs of N = 128 sharing the A tile read.
 //
 // Tiles. The weight is the MMA's A operand (M = 128 output channels, TMEM lane
 // = channel) and the activations are B (BN tokens, BN in {32, 64, 128}), so
@@ -24,8 +32,9 @@
 // (channel tile, token tile, K slice), 576 threads:
 //   warp 0      TMA producer: W tile + x_hi tile + x_lo tile per 128-byte K
 //               step into a STAGES-deep ring of 128B-swizzled smem stages.
-//   warp 1      TMEM allocator; lane 0 issues 2 x 4 MMAs per K step and
-//               commits each smem stage back to the producer.
+//   warp 1      TMEM allocator; lane 0 issues 4 MMAs per K step (8 of half
+//               width for a partial token tile) and commits each smem stage
+//               back to the producer.
 //   warps 2..17 epilogue: tcgen05.ld of H and L, requant, store. Warp w reads
 //               TMEM lanes 32*(w%4)..32*(w%4)+31 and a quarter of the BN
 //               columns; four warps per SM sub-partition hide the latency of
@@ -58,8 +67,7 @@ struct TcCfg {
   static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM allocation");
   static_assert(STAGES >= 2 && STAGES <= 16, "stage ring");
   static_assert(SMEM_BYTES <= 227 * 1024 - 512, "shared memory");
-  static constexpr uint32_t IDESC_HI = idesc_i8(128, BN, true, true);   // W s8 x x_hi s8
-  static constexpr uint32_t IDESC_LO = idesc_i8(128, BN, true, false);  // W s8 x x_lo u8
+  static constexpr uint32_t IDESC = idesc_i8(128, 2 * BN, true, false);  // W s8 x [x_hi | x_lo] u8
 };
 
 struct TcCtl {
@@ -96,6 +104,10 @@ struct TcWork {
   const int* row_start;
   const int* rows;
   int64_t group_w_rows;
+  // Per weight row r, wsum[r * wsum_ld + t] = sum of the row's weights over K
+  // tiles [0, t) (wrapping int32): the correction term of the offset-binary hi.
+  const int32_t* wsum;
+  int64_t wsum_ld;
   __device__ __forceinline__ int units() const {
     return groups > 0 ? tile_start[groups] : tiles_n * tiles_m * ksplit;
   }
@@ -297,13 +309,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       for (int u = blockIdx.x; u < units && !stop; u += gridDim.x, ++lt) {
         const TcUnit wu = work.decode(u, BN, M);
         const int nkt = wu.nkt;
-        // A tile with fewer valid tokens than BN (the end of M or of an expert's
-        // rows) runs N = valid rounded up to 16 (kind::i8 with M = 128 takes N
-        // in multiples of 16); the columns above are never read back.
+        // A full tile runs one MMA of N = 2*BN over [x_hi | x_lo]. A tile with
+        // fewer valid tokens than BN (the end of M or of an expert's rows) runs
+        // one MMA per byte plane with N = valid rounded up to 16 (kind::i8
+        // with M = 128 takes N in multiples of 16); columns above are never read.
         const int64_t valid = wu.m_end - wu.m_begin;
-        const uint32_t nmma = valid >= BN ? uint32_t(BN) : uint32_t((valid + 15) & ~int64_t(15));
-        const uint32_t idesc_hi = (Cfg::IDESC_HI & ~(0x3Fu << 17)) | ((nmma >> 3) << 17);
-        const uint32_t idesc_lo = (Cfg::IDESC_LO & ~(0x3Fu << 17)) | ((nmma >> 3) << 17);
+        const bool full = valid >= BN;
+        const uint32_t nmma = full ? uint32_t(BN) : uint32_t((valid + 15) & ~int64_t(15));
+        const uint32_t idesc_part = (Cfg::IDESC & ~(0x3Fu << 17)) | ((nmma >> 3) << 17);
         const int b = lt & 1;
         const uint32_t tph = uint32_t(lt >> 1) & 1u;
         if (!mbar_wait_bounded(smem_addr(&ctl.tempty[b]), tph ^ 1u, timeout_ns, abort)) {
@@ -327,8 +340,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const uint32_t off = uint32_t(kk) * 32u;
             const uint64_t dw = smem_desc_k_sw128(aw + off);
             const uint32_t accum = (i > 0 || kk > 0) ? 1u : 0u;
-            mma_i8(d_hi, dw, smem_desc_k_sw128(axh + off), idesc_hi, accum);
-            mma_i8(d_lo, dw, smem_desc_k_sw128(axl + off), idesc_lo, accum);
+            if (full) {
+              mma_i8(d_hi, dw, smem_desc_k_sw128(axh + off), Cfg::IDESC, accum);
+            } else {
+              mma_i8(d_hi, dw, smem_desc_k_sw128(axh + off), idesc_part, accum);
+              mma_i8(d_lo, dw, smem_desc_k_sw128(axl + off), idesc_part, accum);
+            }
           }
           mma_commit(smem_addr(&ctl.empty[s]));  // frees the stage when these MMAs finish
         }
@@ -386,11 +403,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       r32.init(fast ? shift : 8, e.out_i32 != 0, (n < N && e.bias) ? e.bias[n] : 0);
       ChannelRequant rq;
       if (n < N && !fast && mode != EPI_ACC_I64) rq.load(e, n);
+      // H = H' - 128 * S over this unit's K tiles (wrapping; the true H fits).
+      uint32_t corr = 0;
+      if (n < N) {
+        const int32_t* ws = work.wsum + (wu.w_row + row) * work.wsum_ld;
+        corr = (uint32_t(ws[wu.kt0 + wu.nkt]) - uint32_t(ws[wu.kt0])) << 7;
+      }
 #pragma unroll 1
       for (int c = 0; c < QCOLS; c += NC) {
         if (m0 + c >= Mend) break;  // warp-uniform: no stored token left in this warp's columns
         uint32_t hi[NC], lo[NC];
         tmem_ld_pair<NC>(tq + c, tq + BN + c, hi, lo);
+#pragma unroll
+        for (int j = 0; j < NC; ++j) hi[j] -= corr;
         const int64_t mc = m0 + c;
         if (mode == EPI_SILU) {
           // Gate (even row) and up (odd row) of channel pair n/2 sit in
@@ -423,7 +448,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           const int64_t mh = mc + (even ? 0 : NH);
           const int64_t jlim = n < N ? Mend - mh : 0;  // tokens mh + j < Mend are stored
           if (e.y == nullptr && sp.h_hi != nullptr && sp.s2 >= 1 && sp.s2 <= 30) {
-            int8_t* ph = sp.h_hi + mh * sp.ldp + (n >> 1);
+            uint8_t* ph = sp.h_hi + mh * sp.ldp + (n >> 1);
             uint8_t* pl = sp.h_lo + mh * sp.ldp + (n >> 1);
             const int32_t c2 = (1 << (sp.s2 - 1)) - 1;
             const int ld = int(sp.ldp);  // NH rows of planes: offsets fit in 32 bits
@@ -432,7 +457,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
               // |lut * u| <= 2^30: the one-add rounding stays inside i32
               const int32_t h = max(-32768, min(rne_add_i32(g[j] * u[j], sp.s2, c2), 32767));
               if (j < jlim) {
-                ph[j * ld] = int8_t(h >> 8);
+                ph[j * ld] = uint8_t((h >> 8) + 128);  // offset-binary high byte
                 pl[j * ld] = uint8_t(h & 0xFF);
               }
             }
@@ -493,10 +518,52 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   }
 }
 
-// X int16 [M][ldx] -> X_hi int8 [M][ldp], X_lo uint8 [M][ldp] with
-// x = 256*hi + lo; columns K..ldp-1 are written as zero.
+// out[r * ld + t] = sum of row r's weights over K tiles [0, t), t = 0..k_tiles,
+// in wrapping int32 (only differences over at most 65536 columns are used).
+__global__ void weight_tile_sums_kernel(const int8_t* __restrict__ W, int64_t ldp, int64_t N,
+                                        int64_t K, int k_tiles, int32_t* __restrict__ out,
+                                        int64_t ld) {
+  for (int64_t r = blockIdx.x; r < N; r += gridDim.x) {
+    const int8_t* wr = W + r * ldp;
+    int32_t* o = out + r * ld;
+    for (int t = threadIdx.x; t < k_tiles; t += blockDim.x) {
+      const int64_t k0 = int64_t(t) * TC_BK;
+      const int64_t k1 = k0 + TC_BK < K ? k0 + TC_BK : K;
+      int32_t sum = 0;
+      for (int64_t k = k0; k < k1; ++k) sum += wr[k];
+      o[t + 1] = sum;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t acc = 0;
+      o[0] = 0;
+      for (int t = 1; t <= k_tiles; ++t) {
+        acc += uint32_t(o[t]);
+        o[t] = int32_t(acc);
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// X int16 [M][ldx] -> X_hi, X_lo uint8 [M][ldp] with hi = (x >> 8) + 128
+// (offset binary) and lo = x & 255, x = 256*hi + lo - 32768; columns
+// K..ldp-1 are written as x = 0 (hi = 128, lo = 0), whose weights are zero.
+__device__ __forceinline__ void split8(const int16_t (&v)[8], uint2& hi, uint2& lo) {
+  uint32_t h0 = 0, h1 = 0, l0 = 0, l1 = 0;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    h0 |= (uint32_t(uint8_t(v[e] >> 8)) ^ 0x80u) << (8 * e);
+    l0 |= uint32_t(uint8_t(v[e] & 0xFF)) << (8 * e);
+    h1 |= (uint32_t(uint8_t(v[e + 4] >> 8)) ^ 0x80u) << (8 * e);
+    l1 |= uint32_t(uint8_t(v[e + 4] & 0xFF)) << (8 * e);
+  }
+  hi = make_uint2(h0, h1);
+  lo = make_uint2(l0, l1);
+}
+
 __global__ void split_hilo_kernel(const int16_t* __restrict__ X, int64_t ldx, int64_t M, int64_t K,
-                                  int8_t* __restrict__ Xhi, uint8_t* __restrict__ Xlo, int64_t ldp) {
+                                  uint8_t* __restrict__ Xhi, uint8_t* __restrict__ Xlo, int64_t ldp) {
   const int64_t groups = ldp >> 3;  // 8 elements per thread step
   const int64_t total = M * groups;
   const bool vec = ((reinterpret_cast<uintptr_t>(X) & 15) == 0) && (ldx % 8 == 0);
@@ -511,16 +578,10 @@ __global__ void split_hilo_kernel(const int16_t* __restrict__ X, int64_t ldx, in
 #pragma unroll
       for (int e = 0; e < 8; ++e) v[e] = (k + e < K) ? xr[k + e] : int16_t(0);
     }
-    uint32_t h0 = 0, h1 = 0, l0 = 0, l1 = 0;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      h0 |= (uint32_t(uint8_t(v[e] >> 8))) << (8 * e);
-      l0 |= (uint32_t(uint8_t(v[e] & 0xFF))) << (8 * e);
-      h1 |= (uint32_t(uint8_t(v[e + 4] >> 8))) << (8 * e);
-      l1 |= (uint32_t(uint8_t(v[e + 4] & 0xFF))) << (8 * e);
-    }
-    *reinterpret_cast<uint2*>(Xhi + m * ldp + k) = make_uint2(h0, h1);
-    *reinterpret_cast<uint2*>(Xlo + m * ldp + k) = make_uint2(l0, l1);
+    uint2 hi, lo;
+    split8(v, hi, lo);
+    *reinterpret_cast<uint2*>(Xhi + m * ldp + k) = hi;
+    *reinterpret_cast<uint2*>(Xlo + m * ldp + k) = lo;
   }
 }
 

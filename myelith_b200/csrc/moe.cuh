@@ -18,6 +18,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "gemm_tc.cuh"
 
 namespace myl {
 
@@ -40,37 +41,54 @@ __device__ __forceinline__ int32_t exp_lut_lookup_dev(int32_t x, const MoeRouteP
   return int32_t(p.exp_lut[idx]);
 }
 
-// One thread per token: top-k experts (lowest index on ties) and softmax_int
+// One warp per token: top-k experts (lowest index on ties) and softmax_int
 // of their logits (softmax.rs:24-64, Rust's truncating i32 division followed
-// by the round-half-even correction).
+// by the round-half-even correction). Lane l holds experts l, l + 32, ...; each
+// of the k rounds is a warp arg-max over the experts not yet chosen.
 __global__ void moe_route_kernel(const int32_t* __restrict__ logits, int64_t ldl, int64_t T, int E,
                                  int k, MoeRouteParams p, int32_t* __restrict__ topk_idx,
                                  int32_t* __restrict__ topk_prob) {
-  for (int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; t < T;
-       t += int64_t(gridDim.x) * blockDim.x) {
+  constexpr int PER = MOE_MAX_EXPERTS / 32;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t t = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T; t += warps) {
     const int32_t* lg = logits + t * ldl;
-    uint32_t chosen[MOE_MAX_EXPERTS / 32];
+    int32_t v[PER];
+    unsigned live = 0;  // bit i: expert lane + 32 i exists and is not chosen yet
 #pragma unroll
-    for (int i = 0; i < MOE_MAX_EXPERTS / 32; ++i) chosen[i] = 0u;
+    for (int i = 0; i < PER; ++i) {
+      const int e = lane + 32 * i;
+      v[i] = e < E ? lg[e] : 0;
+      if (e < E) live |= 1u << i;
+    }
     int32_t sel[MOE_MAX_K];
     int idx[MOE_MAX_K];
 #pragma unroll
     for (int j = 0; j < MOE_MAX_K; ++j) {
       if (j >= k) break;
-      int best = -1;
-      int32_t bv = 0;
-      for (int e = 0; e < E; ++e) {
-        if (chosen[e >> 5] & (1u << (e & 31))) continue;
-        const int32_t v = lg[e];
-        if (best < 0 || v > bv) {
-          best = e;
-          bv = v;
+      // this lane's best: highest value, lowest expert id on ties
+      int best = INT32_MAX;
+      int32_t bv = INT32_MIN;
+#pragma unroll
+      for (int i = 0; i < PER; ++i)
+        if (((live >> i) & 1u) && (best == INT32_MAX || v[i] > bv)) {
+          bv = v[i];
+          best = lane + 32 * i;
+        }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const int32_t ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int ob = __shfl_xor_sync(0xffffffffu, best, o);
+        if (ob != INT32_MAX && (best == INT32_MAX || ov > bv || (ov == bv && ob < best))) {
+          bv = ov;
+          best = ob;
         }
       }
-      chosen[best >> 5] |= 1u << (best & 31);
+      if ((best & 31) == lane) live &= ~(1u << (best >> 5));
       idx[j] = best;
       sel[j] = bv;
     }
+    if (lane != 0) continue;
     const int32_t one = int32_t(1) << p.prob_frac;
     const int32_t lut_one = p.exp_lut_len > 0 ? int32_t(p.exp_lut[0]) : 1;
     int32_t m = sel[0];
@@ -169,18 +187,17 @@ __global__ void moe_scatter_kernel(const int32_t* __restrict__ ids, int64_t P, i
   }
 }
 
-// Row p of the planes = source row src[p] of X split as x = 256*hi + lo;
-// columns K..ldp-1 are zero.
+// Row p of the planes = source row src[p] of X split into the offset-binary
+// byte planes of split_hilo_kernel. blockIdx.y walks rows, threads 8 columns
+// each.
 __global__ void moe_gather_split_kernel(const int16_t* __restrict__ X, int64_t ldx, int64_t P,
                                         int64_t K, const int32_t* __restrict__ src,
-                                        int8_t* __restrict__ Xhi, uint8_t* __restrict__ Xlo,
+                                        uint8_t* __restrict__ Xhi, uint8_t* __restrict__ Xlo,
                                         int64_t ldp) {
-  const int64_t groups = ldp >> 3;
-  const int64_t total = P * groups;
   const bool vec = ((reinterpret_cast<uintptr_t>(X) & 15) == 0) && (ldx % 8 == 0);
-  for (int64_t g = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; g < total;
-       g += int64_t(gridDim.x) * blockDim.x) {
-    const int64_t p = g / groups, k0 = (g % groups) * 8;
+  const int64_t k0 = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
+  if (k0 >= ldp) return;
+  for (int64_t p = blockIdx.y; p < P; p += gridDim.y) {
     const int16_t* xr = X + int64_t(src[p]) * ldx;
     alignas(16) int16_t v[8];
     if (vec && k0 + 8 <= K) {
@@ -189,16 +206,10 @@ __global__ void moe_gather_split_kernel(const int16_t* __restrict__ X, int64_t l
 #pragma unroll
       for (int e = 0; e < 8; ++e) v[e] = (k0 + e < K) ? xr[k0 + e] : int16_t(0);
     }
-    uint32_t h0 = 0, h1 = 0, l0 = 0, l1 = 0;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      h0 |= uint32_t(uint8_t(v[e] >> 8)) << (8 * e);
-      l0 |= uint32_t(uint8_t(v[e] & 0xFF)) << (8 * e);
-      h1 |= uint32_t(uint8_t(v[e + 4] >> 8)) << (8 * e);
-      l1 |= uint32_t(uint8_t(v[e + 4] & 0xFF)) << (8 * e);
-    }
-    *reinterpret_cast<uint2*>(Xhi + p * ldp + k0) = make_uint2(h0, h1);
-    *reinterpret_cast<uint2*>(Xlo + p * ldp + k0) = make_uint2(l0, l1);
+    uint2 hi, lo;
+    split8(v, hi, lo);
+    *reinterpret_cast<uint2*>(Xhi + p * ldp + k0) = hi;
+    *reinterpret_cast<uint2*>(Xlo + p * ldp + k0) = lo;
   }
 }
 
@@ -217,24 +228,63 @@ __global__ void moe_unpermute_kernel(const int16_t* __restrict__ y_perm, int64_t
 
 // out[t][h] = clamp_i16(rescale_i64(sum_j p[t][j] * y[pos[t][j]][h], prob_frac, 0)
 //                       + shared[t][h]); pos == nullptr reads y row t*k + j.
+// blockIdx.y walks tokens; a thread owns 8 consecutive h (16-byte accesses
+// when every row start is 16-byte aligned, else element by element).
 __global__ void moe_combine_kernel(const int16_t* __restrict__ y, int64_t ldyp,
                                    const int32_t* __restrict__ pos, const int32_t* __restrict__ prob,
                                    const int16_t* __restrict__ shared, int64_t ld_shared, int64_t T,
                                    int k, int64_t H, int prob_frac, int16_t* __restrict__ out,
                                    int64_t ldo) {
-  const int64_t total = T * H;
-  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += int64_t(gridDim.x) * blockDim.x) {
-    const int64_t t = i / H, h = i % H;
-    int64_t acc = 0;
+  const int64_t h0 = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
+  if (h0 >= H) return;
+  const bool vec = h0 + 8 <= H && ((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(out) |
+                                     reinterpret_cast<uintptr_t>(shared)) & 15) == 0 &&
+                   ldyp % 8 == 0 && ldo % 8 == 0 && (shared == nullptr || ld_shared % 8 == 0);
+  const int n = vec ? 8 : int(H - h0 < 8 ? H - h0 : 8);
+  for (int64_t t = blockIdx.y; t < T; t += gridDim.y) {
+    int64_t acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0;
     for (int j = 0; j < k; ++j) {
       const int64_t q = t * k + j;
       const int64_t r = pos ? int64_t(pos[q]) : q;
-      if (r >= 0) acc += int64_t(prob[q]) * int64_t(y[r * ldyp + h]);
+      if (r < 0) continue;
+      const int64_t pj = prob[q];
+      const int16_t* yr = y + r * ldyp + h0;
+      alignas(16) int16_t v[8];
+      if (vec) {
+        *reinterpret_cast<int4*>(v) = __ldg(reinterpret_cast<const int4*>(yr));
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = e < n ? yr[e] : int16_t(0);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += pj * int64_t(v[e]);
     }
-    int64_t v = rescale_i64_signed(acc, prob_frac);
-    if (shared) v += shared[t * ld_shared + h];
-    out[t * ldo + h] = int16_t(clamp_i64(v, -32768, 32767));
+    alignas(16) int16_t sv[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sv[e] = 0;
+    if (shared) {
+      const int16_t* sr = shared + t * ld_shared + h0;
+      if (vec) {
+        *reinterpret_cast<int4*>(sv) = __ldg(reinterpret_cast<const int4*>(sr));
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sv[e] = e < n ? sr[e] : int16_t(0);
+      }
+    }
+    alignas(16) int16_t o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      o[e] = int16_t(clamp_i64(rescale_i64_signed(acc[e], prob_frac) + sv[e], -32768, 32767));
+    int16_t* orow = out + t * ldo + h0;
+    if (vec) {
+      *reinterpret_cast<int4*>(orow) = *reinterpret_cast<const int4*>(o);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (e < n) orow[e] = o[e];
+    }
   }
 }
 

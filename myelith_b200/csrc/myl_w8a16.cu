@@ -74,6 +74,8 @@ struct DevBuf {
 struct myl_weight {
   int64_t N = 0, K = 0, ldp = 0;  // device copy is [N][ldp] int8, ldp = round_up(K, 16)
   int8_t* d_W = nullptr;
+  int32_t* d_wsum = nullptr;       // [N][wsum_ld]: per-row prefix sums over 128-byte K tiles
+  int64_t wsum_ld = 0;             // K tiles + 1
   std::vector<uint8_t> w_shifts;
   CUtensorMap tm128{};             // TMA map with a 128-row box (one channel tile)
   // Backend-trait cache key.
@@ -333,7 +335,10 @@ static int launch_tc_mode(myl_ctx* ctx, const myl_weight* w, const CUtensorMap& 
                                         : int64_t(work.tiles_n) * work.tiles_m * work.ksplit;
   const unsigned grid = unsigned(std::min<int64_t>(units, ctx->num_sms));
   const int64_t N = work.groups > 0 ? work.group_w_rows : w->N;  // channels per group
-  fn<<<grid, TC_THREADS, Cfg::SMEM_BYTES, st>>>(w->tm128, tm_xhi, tm_xlo, M, N, work, ep,
+  TcWork wk = work;
+  wk.wsum = w->d_wsum;
+  wk.wsum_ld = w->wsum_ld;
+  fn<<<grid, TC_THREADS, Cfg::SMEM_BYTES, st>>>(w->tm128, tm_xhi, tm_xlo, M, N, wk, ep,
                                                  slice_stride, ctx->d_err, ctx->timeout_ns,
                                                  ctx->inject_fault);
   CUDA_TRY(cudaGetLastError());
@@ -373,7 +378,7 @@ static int launch_tc_any(myl_ctx* ctx, const myl_weight* w, const CUtensorMap& t
 }
 
 static int launch_split(myl_ctx* ctx, const int16_t* x, int64_t M, int64_t K, int64_t ldx,
-                        int8_t* xhi, uint8_t* xlo, int64_t ldp, cudaStream_t st) {
+                        uint8_t* xhi, uint8_t* xlo, int64_t ldp, cudaStream_t st) {
   const int64_t groups = M * (ldp / 8);
   unsigned blocks = unsigned(std::min<int64_t>((groups + 255) / 256, int64_t(ctx->num_sms) * 16));
   split_hilo_kernel<<<blocks, 256, 0, st>>>(x, ldx, M, K, xhi, xlo, ldp);
@@ -383,7 +388,7 @@ static int launch_split(myl_ctx* ctx, const int16_t* x, int64_t M, int64_t K, in
 }
 
 // tcgen05 GEMM from hi/lo planes ([M][ldp] each, ldp a multiple of 16).
-static int launch_tc_planes(myl_ctx* ctx, const myl_weight* w, const int8_t* xhi, const uint8_t* xlo,
+static int launch_tc_planes(myl_ctx* ctx, const myl_weight* w, const uint8_t* xhi, const uint8_t* xlo,
                             int64_t ldp, int64_t M, const Epilogue& ep_final, cudaStream_t st) {
   const int64_t K = w->K;
   const int BN = tc_token_tile(ctx, M);
@@ -429,8 +434,8 @@ static int launch_tc(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_
                      const Epilogue& ep_final, cudaStream_t st) {
   const int64_t ldp = w->ldp;
   TRY(ensure(ctx->planes, size_t(2) * size_t(M) * size_t(ldp)));
-  int8_t* xhi = static_cast<int8_t*>(ctx->planes.p);
-  uint8_t* xlo = reinterpret_cast<uint8_t*>(xhi + M * ldp);
+  uint8_t* xhi = static_cast<uint8_t*>(ctx->planes.p);
+  uint8_t* xlo = xhi + M * ldp;
   TRY(launch_split(ctx, x, M, w->K, ldx, xhi, xlo, ldp, st));
   return launch_tc_planes(ctx, w, xhi, xlo, ldp, M, ep_final, st);
 }
@@ -598,7 +603,24 @@ int myl_weight_register(myl_ctx* ctx, const int8_t* W, int64_t out_features, int
   if (rc == MYL_OK && out_features > 0) {
     rc = encode_map(ctx, &w->tm128, w->d_W, w->K, w->N, w->ldp, 128);
   }
+  // Row sums per K tile for the tensor-core kernel's offset-binary correction.
+  const int k_tiles = int((in_features + TC_BK - 1) / TC_BK);
+  w->wsum_ld = k_tiles + 1;
+  if (rc == MYL_OK) {
+    const size_t wb = size_t(std::max<int64_t>(out_features, 1)) * size_t(w->wsum_ld) * 4;
+    if (cudaMalloc(&w->d_wsum, wb) != cudaSuccess) {
+      rc = fail(MYL_ERR_CUDA, "cudaMalloc of %zu row-sum bytes failed", wb);
+    } else if (out_features > 0) {
+      const unsigned blocks = unsigned(std::min<int64_t>(out_features, int64_t(ctx->num_sms) * 16));
+      weight_tile_sums_kernel<<<blocks, 128, 0, ctx->stream>>>(w->d_W, w->ldp, out_features,
+                                                                 in_features, k_tiles, w->d_wsum,
+                                                                 w->wsum_ld);
+      if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(ctx->stream) != cudaSuccess)
+        rc = fail(MYL_ERR_CUDA, "row-sum kernel failed: %s", cudaGetErrorString(cudaGetLastError()));
+    }
+  }
   if (rc != MYL_OK) {
+    if (w->d_wsum) cudaFree(w->d_wsum);
     cudaFree(w->d_W);
     delete w;
     return rc;
@@ -612,6 +634,7 @@ int myl_weight_release(myl_ctx* ctx, myl_weight* w) {
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->stream);
   if (w->d_W) cudaFree(w->d_W);
+  if (w->d_wsum) cudaFree(w->d_wsum);
   delete w;
   return MYL_OK;
 }
@@ -947,8 +970,8 @@ static int run_mlp(myl_ctx* ctx, const myl_mlp* mlp, const int16_t* x, int64_t M
     // down GEMM reads; h itself never goes to memory as int16.
     const int64_t ldp_h = mlp->w_down->ldp;
     TRY(ensure(ctx->hplanes, size_t(2) * size_t(M) * size_t(ldp_h)));
-    int8_t* hhi = static_cast<int8_t*>(ctx->hplanes.p);
-    uint8_t* hlo = reinterpret_cast<uint8_t*>(hhi + M * ldp_h);
+    uint8_t* hhi = static_cast<uint8_t*>(ctx->hplanes.p);
+    uint8_t* hlo = hhi + M * ldp_h;
     ep_gu.y = nullptr;  // only the planes are needed
     ep_gu.ldy = I;
     ep_gu.silu.h_hi = hhi;
@@ -1009,7 +1032,7 @@ int myl_mlp_int(myl_ctx* ctx, const myl_mlp* mlp, const int16_t* x, int64_t M, i
 }
 
 int myl_split_hilo_dev(myl_ctx* ctx, const int16_t* x, int64_t M, int64_t K, int64_t ldx,
-                       int8_t* xhi, uint8_t* xlo, int64_t ldp, void* stream) {
+                       uint8_t* xhi, uint8_t* xlo, int64_t ldp, void* stream) {
   if (!ctx || (M > 0 && (!x || !xhi || !xlo))) return fail(MYL_ERR_ARG, "null argument");
   if (M < 0 || K <= 0 || ldx < K || ldp < K || ldp % 16 != 0)
     return fail(MYL_ERR_SHAPE, "bad split shape (ldp must be a multiple of 16 and >= K)");
@@ -1021,7 +1044,7 @@ int myl_split_hilo_dev(myl_ctx* ctx, const int16_t* x, int64_t M, int64_t K, int
 }
 
 int myl_linear_planes_dev(myl_ctx* ctx, const myl_weight* w, const myl_requant* rq,
-                          const int8_t* xhi, const uint8_t* xlo, int64_t ldp, int64_t M, void* y,
+                          const uint8_t* xhi, const uint8_t* xlo, int64_t ldp, int64_t M, void* y,
                           int64_t ldy, void* stream) {
   if (!ctx || !w || (M > 0 && (!xhi || !xlo || !y))) return fail(MYL_ERR_ARG, "null argument");
   if (M < 0 || ldp < w->K || ldp % 16 != 0 || ldy < w->N)
@@ -1137,8 +1160,8 @@ extern "C" int myl_linear_noalloc_dev(myl_ctx* ctx, const myl_weight* w, const m
   void* scratch = nullptr;
   TRY(noalloc_scratch(ctx->device, &scratch));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  int8_t* xhi = static_cast<int8_t*>(scratch);
-  uint8_t* xlo = reinterpret_cast<uint8_t*>(xhi + M * w->ldp);
+  uint8_t* xhi = static_cast<uint8_t*>(scratch);
+  uint8_t* xlo = xhi + M * w->ldp;
   TRY(launch_split(ctx, x, M, w->K, ldx, xhi, xlo, w->ldp, st));
   // Same tile choice as the regular path, but always one K slice: no int64
   // partial buffer is needed.
@@ -1185,9 +1208,9 @@ struct MoeArena {
 struct MoeExpertsWs {
   int *counts, *row_start, *rows, *tile_a, *tile_b, *cursor;
   int32_t *src, *pos;
-  int8_t* xhi;
+  uint8_t* xhi;
   uint8_t* xlo;
-  int8_t* hhi;
+  uint8_t* hhi;
   uint8_t* hlo;
   int16_t* y_perm;
 };
@@ -1221,9 +1244,9 @@ static int moe_workspace(myl_ctx* ctx, const myl_moe* m, int64_t P, int64_t T, M
   w->ex.cursor = reinterpret_cast<int*>(b + o_cursor);
   w->ex.src = reinterpret_cast<int32_t*>(b + o_src);
   w->ex.pos = reinterpret_cast<int32_t*>(b + o_pos);
-  w->ex.xhi = reinterpret_cast<int8_t*>(b + o_xhi);
+  w->ex.xhi = b + o_xhi;
   w->ex.xlo = b + o_xlo;
-  w->ex.hhi = reinterpret_cast<int8_t*>(b + o_hhi);
+  w->ex.hhi = b + o_hhi;
   w->ex.hlo = b + o_hlo;
   w->ex.y_perm = reinterpret_cast<int16_t*>(b + o_y);
   w->logits = reinterpret_cast<int32_t*>(b + o_logits);
@@ -1236,6 +1259,13 @@ static int moe_workspace(myl_ctx* ctx, const myl_moe* m, int64_t P, int64_t T, M
 static unsigned grid_for(const myl_ctx* ctx, int64_t items, int per_sm = 8) {
   return unsigned(std::max<int64_t>(1, std::min<int64_t>((items + 255) / 256,
                                                          int64_t(ctx->num_sms) * per_sm)));
+}
+
+// Row-wise kernels: x covers a row with 8 elements per thread (256 threads),
+// y walks the rows (grid-stride beyond 65535).
+static dim3 rows_grid(int64_t cols, int64_t rows) {
+  return dim3(unsigned((cols + 8 * 256 - 1) / (8 * 256)),
+              unsigned(std::max<int64_t>(1, std::min<int64_t>(rows, 65535))));
 }
 
 // Token tile of the grouped GEMMs from the mean rows per expert.
@@ -1255,8 +1285,8 @@ static int moe_route(myl_ctx* ctx, const myl_moe* m, const int16_t* x, int64_t T
   ep.ldy = m->E;
   TRY(dispatch_linear(ctx, m->w_router, x, T, ldx, ep, st));
   MoeRouteParams rp{m->d_exp_lut, m->exp_lut_len, m->exp_lut_shift, m->prob_frac};
-  moe_route_kernel<<<grid_for(ctx, T), 256, 0, st>>>(logits, m->E, T, int(m->E), int(m->k), rp, idx,
-                                                      prob);
+  moe_route_kernel<<<grid_for(ctx, T * 32), 256, 0, st>>>(logits, m->E, T, int(m->E), int(m->k), rp,
+                                                           idx, prob);  // one warp per token
   CUDA_TRY(cudaGetLastError());
   ctx->launches++;
   return MYL_OK;
@@ -1284,8 +1314,8 @@ static int moe_experts(myl_ctx* ctx, const myl_moe* m, const int16_t* x, int64_t
                                                         w.src, w.pos);
   CUDA_TRY(cudaGetLastError());
   const int64_t H = m->H, ldp_h = m->w_gu->ldp, ldp_i = m->w_down->ldp;
-  moe_gather_split_kernel<<<grid_for(ctx, P * (ldp_h / 8), 16), 256, 0, st>>>(
-      x, ldx, P, H, w.src, w.xhi, w.xlo, ldp_h);
+  moe_gather_split_kernel<<<rows_grid(ldp_h, P), 256, 0, st>>>(x, ldx, P, H, w.src, w.xhi, w.xlo,
+                                                                ldp_h);
   CUDA_TRY(cudaGetLastError());
   ctx->launches += 4;
   // Gate/up: grouped GEMM with the SiLU pair epilogue into the down planes.
@@ -1502,7 +1532,7 @@ int myl_moe_combine_dev(myl_ctx* ctx, const myl_moe* m, const int16_t* y, int64_
   if (T == 0) return MYL_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   CUDA_TRY(cudaSetDevice(ctx->device));
-  moe_combine_kernel<<<grid_for(ctx, T * m->H), 256, 0, st>>>(y, ldy, nullptr, prob, shared_out,
+  moe_combine_kernel<<<rows_grid(m->H, T), 256, 0, st>>>(y, ldy, nullptr, prob, shared_out,
                                                                ld_shared, T, int(m->k), m->H,
                                                                m->prob_frac, out, ldo);
   CUDA_TRY(cudaGetLastError());
@@ -1533,7 +1563,7 @@ int myl_moe_dev(myl_ctx* ctx, const myl_moe* m, const int16_t* x, int64_t T, int
     TRY(run_mlp(ctx, m->shared, x, T, ldx, w.shared_out, m->H, st));
     shared_out = w.shared_out;
   }
-  moe_combine_kernel<<<grid_for(ctx, T * m->H), 256, 0, st>>>(w.ex.y_perm, m->H, w.ex.pos, prob,
+  moe_combine_kernel<<<rows_grid(m->H, T), 256, 0, st>>>(w.ex.y_perm, m->H, w.ex.pos, prob,
                                                                shared_out, m->H, T, int(m->k), m->H,
                                                                m->prob_frac, out, ldo);
   CUDA_TRY(cudaGetLastError());

@@ -193,3 +193,16 @@ def test_moe_config4_shape(ctx):
     sample = np.random.default_rng(41).choice(T, size=48, replace=False)
     ref = R.forward(p, s, x[sample])[0]
     assert np.array_equal(out[sample], ref)
+
+
+@pytest.mark.parametrize("H,I,T", [(100, 72, 45), (136, 40, 9)])
+def test_moe_ragged_hidden(ctx, H, I, T):
+    """hidden not a multiple of 8: the gather and combine take their
+    element-by-element paths; I not a multiple of 16 pads the h planes."""
+    p, s = R.problem(H=H, I=I, E=6, k=2, shared_I=24, seed=H + I)
+    x = R.activations(np.random.default_rng(H), T, H)
+    m = R.lib_moe(ctx, p, s)
+    out, idx, prob = _run_dev(m, x)
+    ref, ridx, rprob = R.forward(p, s, x)
+    assert np.array_equal(idx, ridx) and np.array_equal(prob, rprob)
+    assert np.array_equal(out, ref)
