@@ -83,6 +83,7 @@ struct TcCtl {
 // One work unit: a 128-channel x BN-token output tile over one K slice.
 struct TcUnit {
   int nt, ks, kt0, nkt;
+  int tail_slot;     // >= 0: a K slice of a tail tile, stored as int64 partials
   int64_t m_begin;   // first activation row (token) of the tile
   int64_t m_end;     // rows >= m_end are not stored (end of the group / of M)
   int64_t w_row;     // first weight row of the tile
@@ -108,11 +109,36 @@ struct TcWork {
   // tiles [0, t) (wrapping int32): the correction term of the offset-binary hi.
   const int32_t* wsum;
   int64_t wsum_ld;
+  // Dense tail split (ksplit == 1): tiles [full_units, full_units + tail_tiles)
+  // are the last, incomplete wave; each runs as tail_ks K slices of tail_per K
+  // tiles whose int64 partials go to tail_ws[slot][BN][128] (slot = slice *
+  // tail_tiles + tile) and are added by tail_reduce_kernel, so the final wave
+  // is short instead of mostly idle.
+  int full_units, tail_tiles, tail_ks, tail_per;
+  int64_t* tail_ws;
   __device__ __forceinline__ int units() const {
-    return groups > 0 ? tile_start[groups] : tiles_n * tiles_m * ksplit;
+    if (groups > 0) return tile_start[groups];
+    if (tail_tiles > 0) return full_units + tail_tiles * tail_ks;
+    return tiles_n * tiles_m * ksplit;
   }
   __device__ __forceinline__ TcUnit decode(int u, int BN, int64_t M) const {
     TcUnit w;
+    w.tail_slot = -1;
+    if (groups == 0 && tail_tiles > 0 && u >= full_units) {
+      const int v = u - full_units;
+      const int slice = v / tail_tiles, tl = v % tail_tiles;
+      const int t = full_units + tl;
+      w.nt = t % tiles_n;
+      w.ks = 0;
+      w.kt0 = slice * tail_per;
+      w.nkt = min(tail_per, k_tiles_total - w.kt0);
+      w.m_begin = int64_t(t / tiles_n) * BN;
+      w.m_end = M;
+      w.w_row = int64_t(w.nt) * 128;
+      w.p_off = 0;
+      w.tail_slot = slice * tail_tiles + tl;
+      return w;
+    }
     if (groups == 0) {
       w.nt = u % tiles_n;
       const int r = u / tiles_n;
@@ -416,6 +442,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         tmem_ld_pair<NC>(tq + c, tq + BN + c, hi, lo);
 #pragma unroll
         for (int j = 0; j < NC; ++j) hi[j] -= corr;
+        if (wu.tail_slot >= 0) {  // int64 partial of a tail tile's K slice
+          if (n < N) {
+            int64_t* tp = work.tail_ws + (int64_t(wu.tail_slot) * BN + col0 + c) * 128 + row;
+#pragma unroll
+            for (int j = 0; j < NC; ++j)
+              tp[int64_t(j) * 128] = int64_t(int32_t(hi[j])) * 256 + int64_t(int32_t(lo[j]));
+          }
+          continue;
+        }
         const int64_t mc = m0 + c;
         if (mode == EPI_SILU) {
           // Gate (even row) and up (odd row) of channel pair n/2 sit in
@@ -515,6 +550,39 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  }
+}
+
+// Adds the tail tiles' K-slice partials and applies the final epilogue.
+// One thread per (tile, token, channel pair): both rows of the pair, so the
+// SiLU mode can combine gate and up.
+__global__ void tail_reduce_kernel(const int64_t* __restrict__ ws, int tail_tiles, int tail_ks,
+                                   int first_tile, int tiles_n, int BN, int64_t M, int64_t N,
+                                   Epilogue ep) {
+  const int64_t total = int64_t(tail_tiles) * BN * 64;
+  for (int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+       e += int64_t(gridDim.x) * blockDim.x) {
+    const int pr = int(e % 64);
+    const int col = int((e / 64) % BN);
+    const int tl = int(e / (64 * int64_t(BN)));
+    const int t = first_tile + tl;
+    const int64_t m = int64_t(t / tiles_n) * BN + col;
+    const int64_t n0 = int64_t(t % tiles_n) * 128 + 2 * pr;
+    if (m >= M || n0 >= N) continue;
+    int64_t a0 = 0, a1 = 0;
+    for (int s = 0; s < tail_ks; ++s) {
+      const int64_t* p = ws + ((int64_t(s) * tail_tiles + tl) * BN + col) * 128 + 2 * pr;
+      a0 += p[0];
+      a1 += p[1];
+    }
+    if (ep.mode == EPI_SILU) {  // N is even: rows 2i / 2i + 1 are gate / up of pair i
+      const int32_t g = int32_t(requant_value(ep, n0, a0));
+      const int32_t u = int32_t(requant_value(ep, n0 + 1, a1));
+      silu_store(ep, m, n0 >> 1, silu_combine(ep.silu, g, u));
+    } else {
+      epilogue_store(ep, m, n0, a0);
+      if (n0 + 1 < N) epilogue_store(ep, m, n0 + 1, a1);
+    }
   }
 }
 

@@ -332,7 +332,9 @@ static int launch_tc_mode(myl_ctx* ctx, const myl_weight* w, const CUtensorMap& 
   // Grouped work is sized on the device (the router's tile table): one CTA per
   // SM, CTAs without a unit exit after setup.
   const int64_t units = work.groups > 0 ? int64_t(ctx->num_sms)
-                                        : int64_t(work.tiles_n) * work.tiles_m * work.ksplit;
+                        : work.tail_tiles > 0
+                            ? int64_t(work.full_units) + int64_t(work.tail_tiles) * work.tail_ks
+                            : int64_t(work.tiles_n) * work.tiles_m * work.ksplit;
   const unsigned grid = unsigned(std::min<int64_t>(units, ctx->num_sms));
   const int64_t N = work.groups > 0 ? work.group_w_rows : w->N;  // channels per group
   TcWork wk = work;
@@ -409,6 +411,33 @@ static int launch_tc_planes(myl_ctx* ctx, const myl_weight* w, const uint8_t* xh
   const int per = (k_tiles + ksplit - 1) / ksplit;
   ksplit = (k_tiles + per - 1) / per;  // no empty slice
   TcWork work{int((w->N + 127) / 128), int((M + BN - 1) / BN), ksplit, k_tiles, per};
+  // Tail split: when the tiles fill some waves and leave a small last wave,
+  // that wave's tiles run as K slices on all SMs (int64 partials, then
+  // tail_reduce_kernel), so the last wave costs a fraction of a full one.
+  const int64_t G = ctx->num_sms;
+  const int64_t R = tiles % G;
+  if (ksplit == 1 && ctx->force_split_k == 0 && tiles >= G && R > 0) {
+    const int ks = int(std::min<int64_t>({G / R, int64_t(k_tiles / 4), 16}));
+    if (ks >= 2) {
+      const int tper = (k_tiles + ks - 1) / ks;
+      work.full_units = int(tiles - R);
+      work.tail_tiles = int(R);
+      work.tail_ks = (k_tiles + tper - 1) / tper;
+      work.tail_per = tper;
+      TRY(ensure(ctx->part, size_t(R) * size_t(work.tail_ks) * size_t(BN) * 128 * 8));
+      work.tail_ws = static_cast<int64_t*>(ctx->part.p);
+    }
+  }
+  if (work.tail_tiles > 0) {
+    TRY(launch_tc_any(ctx, w, tm_xhi, tm_xlo, M, BN, work, ep_final, 0, st));
+    const int64_t total = int64_t(work.tail_tiles) * BN * 64;
+    const unsigned blocks = unsigned(std::min<int64_t>((total + 255) / 256, G * 8));
+    tail_reduce_kernel<<<blocks, 256, 0, st>>>(work.tail_ws, work.tail_tiles, work.tail_ks,
+                                                work.full_units, work.tiles_n, BN, M, w->N, ep_final);
+    CUDA_TRY(cudaGetLastError());
+    ctx->launches++;
+    return MYL_OK;
+  }
   Epilogue ep = ep_final;
   int64_t slice_stride = 0;
   if (ksplit > 1) {
