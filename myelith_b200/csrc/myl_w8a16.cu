@@ -19,6 +19,7 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -101,6 +102,8 @@ struct myl_mlp {
   int lut_hi = 0, offset = 0, s1 = 0, s2 = 0;
 };
 
+constexpr int MYL_PIPE = 8;  // chunks of a pipelined host-pointer call
+
 struct myl_ctx {
   int device = 0, sm = 0, num_sms = 0;
   cudaStream_t stream = nullptr;
@@ -111,6 +114,10 @@ struct myl_ctx {
   int64_t launches = 0;
   PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   DevBuf x, y, rq, planes, part, h, hplanes, moe;
+  // Host-pointer calls on page-locked memory: copy-in and copy-out streams
+  // and one event pair per chunk.
+  cudaStream_t s_in = nullptr, s_out = nullptr;
+  cudaEvent_t ev_in[MYL_PIPE] = {}, ev_comp[MYL_PIPE] = {};
   // The workspace buffers are shared by every call on the context; calls on
   // different streams are ordered through this event.
   cudaEvent_t ws_event = nullptr;
@@ -498,6 +505,15 @@ static int check_device_error(myl_ctx* ctx) {
   return MYL_OK;
 }
 
+static bool is_pinned(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeHost;
+}
+
 // Host-pointer linear: upload x and the requant table, run, download y.
 static int host_linear(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M, int mode,
                        int out_i32, const int8_t* shift, const int32_t* mult, void* y,
@@ -514,7 +530,6 @@ static int host_linear(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int6
   int32_t* d_bias = d_mult + N;
   int8_t* d_shift = reinterpret_cast<int8_t*>(d_bias + N);
   cudaStream_t st = ctx->stream;
-  CUDA_TRY(cudaMemcpyAsync(ctx->x.p, x, size_t(M) * size_t(K) * 2, cudaMemcpyHostToDevice, st));
   CUDA_TRY(cudaMemcpyAsync(d_shift, shift, size_t(N), cudaMemcpyHostToDevice, st));
   if (mult) CUDA_TRY(cudaMemcpyAsync(d_mult, mult, size_t(N) * 4, cudaMemcpyHostToDevice, st));
   if (bias) CUDA_TRY(cudaMemcpyAsync(d_bias, bias, size_t(N) * 4, cudaMemcpyHostToDevice, st));
@@ -526,8 +541,40 @@ static int host_linear(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int6
   ep.mult = mult ? d_mult : nullptr;
   ep.y = ctx->y.p;
   ep.ldy = N;
-  TRY(run_linear(ctx, w, static_cast<const int16_t*>(ctx->x.p), M, K, ep, st));
-  CUDA_TRY(cudaMemcpyAsync(y, ctx->y.p, size_t(M) * size_t(N) * osz, cudaMemcpyDeviceToHost, st));
+  // Page-locked x and y: the rows run in chunks on three streams, so the
+  // upload of chunk i+1 and the download of chunk i-1 overlap the kernels of
+  // chunk i (PCIe moves data both ways at once). Otherwise one pass.
+  int64_t nch = (is_pinned(x) && is_pinned(y)) ? std::min<int64_t>(MYL_PIPE, M / 128) : 1;
+  if (const char* env = std::getenv("MYL_HOST_CHUNKS"))  // tuning: chunk count, 1 = one pass
+    nch = std::max<int64_t>(1, std::min<int64_t>({int64_t(std::atoi(env)), int64_t(MYL_PIPE), M}));
+  if (nch < 2) {
+    CUDA_TRY(cudaMemcpyAsync(ctx->x.p, x, size_t(M) * size_t(K) * 2, cudaMemcpyHostToDevice, st));
+    TRY(run_linear(ctx, w, static_cast<const int16_t*>(ctx->x.p), M, K, ep, st));
+    CUDA_TRY(cudaMemcpyAsync(y, ctx->y.p, size_t(M) * size_t(N) * osz, cudaMemcpyDeviceToHost, st));
+    return check_device_error(ctx);
+  }
+  const int64_t rows = (M + nch - 1) / nch;
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  TRY(ws_acquire(ctx, st));
+  for (int64_t c = 0; c < nch; ++c) {
+    const int64_t r0 = c * rows, rc = std::min(rows, M - r0);
+    if (rc <= 0) break;
+    const int16_t* dx = static_cast<const int16_t*>(ctx->x.p) + r0 * K;
+    uint8_t* dy = static_cast<uint8_t*>(ctx->y.p) + size_t(r0) * size_t(N) * osz;
+    CUDA_TRY(cudaMemcpyAsync(const_cast<int16_t*>(dx), x + r0 * K, size_t(rc) * size_t(K) * 2,
+                             cudaMemcpyHostToDevice, ctx->s_in));
+    CUDA_TRY(cudaEventRecord(ctx->ev_in[c], ctx->s_in));
+    CUDA_TRY(cudaStreamWaitEvent(st, ctx->ev_in[c], 0));
+    Epilogue epc = ep;
+    epc.y = dy;
+    TRY(dispatch_linear(ctx, w, dx, rc, K, epc, st));
+    CUDA_TRY(cudaEventRecord(ctx->ev_comp[c], st));
+    CUDA_TRY(cudaStreamWaitEvent(ctx->s_out, ctx->ev_comp[c], 0));
+    CUDA_TRY(cudaMemcpyAsync(static_cast<uint8_t*>(y) + size_t(r0) * size_t(N) * osz, dy,
+                             size_t(rc) * size_t(N) * osz, cudaMemcpyDeviceToHost, ctx->s_out));
+  }
+  CUDA_TRY(cudaStreamSynchronize(ctx->s_out));
+  TRY(ws_release(ctx, st));
   return check_device_error(ctx);
 }
 
@@ -564,7 +611,12 @@ int myl_init(int device, myl_ctx** out) {
     return fail(MYL_ERR_CUDA, "cuTensorMapEncodeTiled not available from the driver");
   }
   c->encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-  if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+  bool ok = cudaStreamCreateWithFlags(&c->s_in, cudaStreamNonBlocking) == cudaSuccess &&
+            cudaStreamCreateWithFlags(&c->s_out, cudaStreamNonBlocking) == cudaSuccess;
+  for (int i = 0; ok && i < MYL_PIPE; ++i)
+    ok = cudaEventCreateWithFlags(&c->ev_in[i], cudaEventDisableTiming) == cudaSuccess &&
+         cudaEventCreateWithFlags(&c->ev_comp[i], cudaEventDisableTiming) == cudaSuccess;
+  if (!ok || cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaEventCreateWithFlags(&c->ws_event, cudaEventDisableTiming) != cudaSuccess ||
       cudaMalloc(&c->d_err, sizeof(int)) != cudaSuccess ||
       cudaMallocHost(&c->h_err, sizeof(int)) != cudaSuccess ||
@@ -588,6 +640,12 @@ int myl_destroy(myl_ctx* ctx) {
   if (ctx->d_err) cudaFree(ctx->d_err);
   if (ctx->h_err) cudaFreeHost(ctx->h_err);
   if (ctx->ws_event) cudaEventDestroy(ctx->ws_event);
+  for (int i = 0; i < MYL_PIPE; ++i) {
+    if (ctx->ev_in[i]) cudaEventDestroy(ctx->ev_in[i]);
+    if (ctx->ev_comp[i]) cudaEventDestroy(ctx->ev_comp[i]);
+  }
+  if (ctx->s_in) cudaStreamDestroy(ctx->s_in);
+  if (ctx->s_out) cudaStreamDestroy(ctx->s_out);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
   return MYL_OK;

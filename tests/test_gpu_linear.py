@@ -483,3 +483,25 @@ def test_launch_count_increases(ctx):
     w = ctx.weight(np.ones((16, 32), np.int8), 32, np.zeros(16, np.uint8))
     w.linear(np.ones((2, 32), np.int16), 0, 0)
     assert ctx.launch_count > n0
+
+
+@pytest.mark.parametrize("M", [256, 1000, 2048])
+def test_host_call_pinned_pipeline(ctx, M):
+    """Page-locked x and y: myl_linear_w8a16 runs the rows in chunks with the
+    copies overlapping the kernels; equal to the one-pass (pageable) call and
+    to the oracle."""
+    rng = np.random.default_rng(M)
+    K, N = 896, 4864
+    W = rng.integers(-127, 128, size=(N, K), dtype=np.int8)
+    ws = rng.integers(11, 14, size=N).astype(np.uint8)
+    x = normal_x(rng, M, K)
+    w = ctx.weight(W, K, ws)
+    L = myl.load_library()
+    xp = torch.from_numpy(x).pin_memory()
+    yp = torch.zeros((M, N), dtype=torch.int16).pin_memory()
+    myl._check("myl_linear_w8a16", L.myl_linear_w8a16(ctx.handle, w.handle, xp.data_ptr(), M, 8, 8,
+                                                      yp.data_ptr()))
+    plain = w.linear(x, 8, 8)
+    assert np.array_equal(yp.numpy(), plain)
+    rows = np.random.default_rng(1).choice(M, size=8, replace=False)
+    assert np.array_equal(plain[rows], O.linear_w8a16(x[rows], W.reshape(-1), K, ws, 8, 8))
