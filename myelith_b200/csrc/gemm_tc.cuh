@@ -591,14 +591,22 @@ __global__ void tail_reduce_kernel(const int64_t* __restrict__ ws, int tail_tile
 __global__ void weight_tile_sums_kernel(const int8_t* __restrict__ W, int64_t ldp, int64_t N,
                                         int64_t K, int k_tiles, int32_t* __restrict__ out,
                                         int64_t ld) {
+  // ldp is a multiple of 16 and the columns K..ldp-1 are zero, so a tile is
+  // summed in 16-byte loads (dp4a against ones adds four signed bytes).
   for (int64_t r = blockIdx.x; r < N; r += gridDim.x) {
     const int8_t* wr = W + r * ldp;
     int32_t* o = out + r * ld;
     for (int t = threadIdx.x; t < k_tiles; t += blockDim.x) {
       const int64_t k0 = int64_t(t) * TC_BK;
-      const int64_t k1 = k0 + TC_BK < K ? k0 + TC_BK : K;
+      const int64_t k1 = k0 + TC_BK < ldp ? k0 + TC_BK : ldp;
       int32_t sum = 0;
-      for (int64_t k = k0; k < k1; ++k) sum += wr[k];
+      for (int64_t k = k0; k < k1; k += 16) {
+        const int4 v = __ldg(reinterpret_cast<const int4*>(wr + k));
+        sum = __dp4a(v.x, 0x01010101, sum);
+        sum = __dp4a(v.y, 0x01010101, sum);
+        sum = __dp4a(v.z, 0x01010101, sum);
+        sum = __dp4a(v.w, 0x01010101, sum);
+      }
       o[t + 1] = sum;
     }
     __syncthreads();
