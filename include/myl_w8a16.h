@@ -90,6 +90,17 @@ int myl_linear_w8a16_pc(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int
 int myl_lm_head_w8a16_i32(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
                           uint8_t final_norm_frac, uint8_t logit_frac, int32_t* logits);
 
+/* LM head, path A (runtime/src/model.rs:285-296): int16 weights [N][K] with
+ * one shift per row (loader.rs:124-128), i64 dot, rescale to logit_frac,
+ * clamp to i32. The weight is registered with myl_weight16_register and
+ * stored as two int8 rows per int16 row (high byte, low byte - 128), so the
+ * same GEMV and tensor-core kernels run it; the device form is
+ * myl_linear_dev with a MYL_RQ_SHIFT_I32 plan of this weight. */
+int myl_weight16_register(myl_ctx* ctx, const int16_t* W, int64_t out_features, int64_t in_features,
+                          int64_t ldw, const uint8_t* w_shifts, myl_weight** out);
+int myl_lm_head_w16a16_i32(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
+                           uint8_t final_norm_frac, uint8_t logit_frac, int32_t* logits);
+
 /* linear_w8a16 followed by add_bias_i16 (linear.rs:132-145) as the runtime
  * does for q/k/v (runtime/src/model.rs:438-453), fused into one epilogue:
  * y = clamp_i16(clamp_i16(requant(acc)) + rescale(bias[r], bias_shifts[r], out_frac)). */

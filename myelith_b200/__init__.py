@@ -107,6 +107,8 @@ def load_library(path: str | None = None):
             "myl_set_dispatch": ([vp, i32, i32, i32], i32),
             "myl_launch_count": ([vp], i64),
             "myl_debug_inject_wait_fault": ([vp, i32], i32),
+            "myl_weight16_register": ([vp, vp, i64, i64, i64, vp, C.POINTER(vp)], i32),
+            "myl_lm_head_w16a16_i32": ([vp, vp, vp, i64, u8, u8, vp], i32),
             "myl_moe_register": ([vp, C.POINTER(MoeSpec), C.POINTER(vp)], i32),
             "myl_moe_release": ([vp, vp], i32),
             "myl_moe_forward": ([vp, vp, vp, i64, vp], i32),
@@ -190,6 +192,9 @@ class Context:
 
     def weight(self, W, in_features: int, w_shifts, ldw: int | None = None) -> "Weight":
         return Weight(self, W, in_features, w_shifts, ldw)
+
+    def weight16(self, W, in_features: int, w_shifts) -> "Weight16":
+        return Weight16(self, W, in_features, w_shifts)
 
     def split_hilo_dev(self, x, xhi, xlo, stream=None) -> None:
         """x [M, K] int16 (torch CUDA) -> byte planes xhi int8 / xlo uint8 [M, ldp]."""
@@ -317,6 +322,35 @@ class Weight:
         """acc[M, N] int64 = exact W x (no requant)."""
         _check("myl_linear_acc_dev", load_library().myl_linear_acc_dev(
             self.ctx.handle, self._h, _p(x), x.shape[0], x.stride(0), _p(acc), _stream_ptr(stream)))
+
+
+class Weight16(Weight):
+    """An int16 LM-head weight (runtime/src/loader.rs:124-128: int16 [vocab][hidden]
+    plus one shift per row), for path A of the LM head (model.rs:285-296)."""
+
+    def __init__(self, ctx: Context, W, in_features: int, w_shifts):
+        self.ctx = ctx
+        w_shifts = _c(w_shifts, np.uint8)
+        W = np.ascontiguousarray(np.asarray(W, dtype=np.int16)).reshape(-1)
+        N = w_shifts.size
+        if in_features <= 0 or W.size != N * in_features:
+            raise MylError("myl_weight16_register", MYL_ERR_SHAPE,
+                           f"{W.size} weights do not hold {N} rows of {in_features}")
+        h = C.c_void_p()
+        _check("myl_weight16_register", load_library().myl_weight16_register(
+            ctx.handle, _p(W), N, in_features, in_features, _p(w_shifts), C.byref(h)))
+        self._h = h
+        self.out_features = N
+        self.in_features = in_features
+        self.w_shifts = w_shifts
+
+    def lm_head(self, x, final_norm_frac: int, logit_frac: int) -> np.ndarray:
+        """LM head path A: i32 logits [M, vocab]."""
+        xs, single = self._rows(x)
+        y = np.zeros((xs.shape[0], self.out_features), np.int32)
+        _check("myl_lm_head_w16a16_i32", load_library().myl_lm_head_w16a16_i32(
+            self.ctx.handle, self._h, _p(xs), xs.shape[0], final_norm_frac, logit_frac, _p(y)))
+        return y[0] if single else y
 
 
 class Requant:

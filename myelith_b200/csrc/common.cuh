@@ -36,6 +36,8 @@ enum EpiMode : int {
   EPI_SHIFT = 1,      // reference requant (pure shift)
   EPI_MULT = 2,       // multiplier requant (i128 product)
   EPI_SILU = 3,       // MLP: rows 2i / 2i+1 are gate_i / up_i; store h_i (mlp.rs:49-64)
+  EPI_W16 = 4,        // int16 weights: rows 2i / 2i+1 are the high byte and the offset low
+                      // byte of row i; store int32 logits (model.rs:285-296)
 };
 
 // Parameters of the SiLU-LUT product of mlp.rs:52-64 (validated on the host).
@@ -59,6 +61,7 @@ struct Epilogue {
   int64_t ldy;
   const int32_t* bias;    // optional [N]: rescaled bias added after the i16 clamp (linear.rs:132-145)
   SiluParams silu;
+  const int64_t* xsum;    // EPI_W16: [M] sum of each activation row over K
 };
 
 // ---- requant -----------------------------------------------------------------
@@ -177,6 +180,18 @@ __device__ __forceinline__ int64_t requant_value(const Epilogue& ep, int64_t n, 
   else v = clamp_i64(rescale_i64_signed(acc, ep.shift[n]), lo, hi);
   if (ep.bias) v = clamp_i64(v + ep.bias[n], lo, hi);
   return v;
+}
+
+// EPI_W16: an int16 weight row w = 256*hi + lo with hi = w >> 8 and
+// lo_off = (w & 255) - 128 (both int8) gives
+//   sum_k w*x = 256*sum hi*x + sum lo_off*x + 128*sum x,
+// the exact i64 accumulator of the LM head's path A (model.rs:285-296), which
+// is rescaled by the row's shift and clamped to i32 (model.rs:293-295).
+__device__ __forceinline__ void w16_store(const Epilogue& ep, int64_t m, int64_t i, int64_t a_hi,
+                                          int64_t a_lo) {
+  const int64_t acc = a_hi * 256 + a_lo + 128 * ep.xsum[m];
+  static_cast<int32_t*>(ep.y)[m * ep.ldy + i] =
+      int32_t(clamp_i64(rescale_i64_signed(acc, ep.shift[i]), INT32_MIN, INT32_MAX));
 }
 
 // Applies the epilogue to one exact accumulator of output (m, n).

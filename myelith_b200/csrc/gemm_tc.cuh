@@ -423,12 +423,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       // Channel parameters, once per unit.
       int shift = 0;
       constexpr int mode = MODE;
-      if (n < N && mode != EPI_ACC_I64) shift = e.shift[n];
+      // (EPI_W16 reads the shift of weight row n/2 in w16_store.)
+      constexpr bool per_row = mode != EPI_ACC_I64 && mode != EPI_W16;
+      if (n < N && per_row) shift = e.shift[n];
       const bool fast = (mode == EPI_SHIFT || mode == EPI_SILU) && shift >= 8 && shift <= 38;
       Requant32 r32;
-      r32.init(fast ? shift : 8, e.out_i32 != 0, (n < N && e.bias) ? e.bias[n] : 0);
+      r32.init(fast ? shift : 8, e.out_i32 != 0, (n < N && per_row && e.bias) ? e.bias[n] : 0);
       ChannelRequant rq;
-      if (n < N && !fast && mode != EPI_ACC_I64) rq.load(e, n);
+      if (n < N && !fast && per_row) rq.load(e, n);
       // H = H' - 128 * S over this unit's K tiles (wrapping; the true H fits).
       uint32_t corr = 0;
       if (n < N) {
@@ -452,6 +454,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           continue;
         }
         const int64_t mc = m0 + c;
+        if (mode == EPI_W16) {
+          // High byte (even row) and offset low byte (odd row) of int16 weight
+          // row n/2 sit in adjacent lanes: as for the SiLU pairs, the even lane
+          // takes the first NC/2 tokens, the odd lane the last NC/2.
+          constexpr int NH = NC / 2;
+          const bool even = (row & 1) == 0;
+          int64_t a[NC];
+#pragma unroll
+          for (int j = 0; j < NC; ++j) a[j] = int64_t(int32_t(hi[j])) * 256 + int64_t(int32_t(lo[j]));
+          const int64_t mh = mc + (even ? 0 : NH);
+          const int64_t jlim = n < N ? Mend - mh : 0;
+#pragma unroll
+          for (int j = 0; j < NH; ++j) {
+            const int64_t mine = even ? a[j] : a[j + NH];
+            const int64_t other = __shfl_xor_sync(0xffffffffu, even ? a[j + NH] : a[j], 1);
+            if (j < jlim) w16_store(e, mh + j, n >> 1, even ? mine : other, even ? other : mine);
+          }
+          continue;
+        }
         if (mode == EPI_SILU) {
           // Gate (even row) and up (odd row) of channel pair n/2 sit in
           // adjacent lanes. One exchange per token pair gives the even lane
@@ -575,7 +596,9 @@ __global__ void tail_reduce_kernel(const int64_t* __restrict__ ws, int tail_tile
       a0 += p[0];
       a1 += p[1];
     }
-    if (ep.mode == EPI_SILU) {  // N is even: rows 2i / 2i + 1 are gate / up of pair i
+    if (ep.mode == EPI_W16) {  // rows 2i / 2i + 1: high and offset low byte of int16 row i
+      w16_store(ep, m, n0 >> 1, a0, a1);
+    } else if (ep.mode == EPI_SILU) {  // N is even: rows 2i / 2i + 1 are gate / up of pair i
       const int32_t g = int32_t(requant_value(ep, n0, a0));
       const int32_t u = int32_t(requant_value(ep, n0 + 1, a1));
       silu_store(ep, m, n0 >> 1, silu_combine(ep.silu, g, u));

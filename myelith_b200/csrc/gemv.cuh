@@ -186,7 +186,12 @@ __global__ void __launch_bounds__(GEMV_THREADS)
       __syncthreads();
     }
     if (kw == 0) {
-      if (e.mode == EPI_SILU) {
+      if (e.mode == EPI_W16) {
+        // Rows row0 (high byte) and row0 + 1 (low byte) of int16 row row0/2 (R == 2).
+#pragma unroll
+        for (int m = 0; m < MT; ++m)
+          if (R == 2 && lane == m && row0 + 1 < N) w16_store(e, m, row0 >> 1, acc[0][m], acc[R - 1][m]);
+      } else if (e.mode == EPI_SILU) {
         // Rows row0 (gate) and row0 + 1 (up) of channel pair row0/2 (R == 2).
 #pragma unroll
         for (int m = 0; m < MT; ++m)
@@ -206,10 +211,39 @@ __global__ void __launch_bounds__(GEMV_THREADS)
   }
 }
 
+// xsum[m] = sum_k x[m][k] (int64), one warp per row: the EPI_W16 correction.
+__global__ void x_row_sums_kernel(const int16_t* __restrict__ X, int64_t ldx, int64_t M, int64_t K,
+                                  int64_t* __restrict__ xsum) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t m = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); m < M; m += warps) {
+    const int16_t* xr = X + m * ldx;
+    int64_t s = 0;
+    for (int64_t k = lane; k < K; k += 32) s += xr[k];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (lane == 0) xsum[m] = s;
+  }
+}
+
 // Sums nsplit exact int64 partial slices [nsplit][M][N] (slice_stride apart)
 // and applies the epilogue. Summation order is irrelevant (exact integers).
 __global__ void reduce_requant_kernel(const int64_t* __restrict__ part, int nsplit,
                                       int64_t slice_stride, int64_t M, int64_t N, Epilogue ep) {
+  if (ep.mode == EPI_W16) {  // one thread per (token, int16 weight row)
+    const int64_t I = N / 2, total = M * I;
+    for (int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+         e += int64_t(gridDim.x) * blockDim.x) {
+      const int64_t m = e / I, i = e % I;
+      int64_t ah = 0, al = 0;
+      for (int k = 0; k < nsplit; ++k) {
+        ah += part[k * slice_stride + m * N + 2 * i];
+        al += part[k * slice_stride + m * N + 2 * i + 1];
+      }
+      w16_store(ep, m, i, ah, al);
+    }
+    return;
+  }
   if (ep.mode == EPI_SILU) {  // one thread per (token, channel pair)
     const int64_t I = N / 2, total = M * I;
     for (int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < total;

@@ -76,6 +76,10 @@ struct myl_weight {
   int64_t N = 0, K = 0, ldp = 0;  // device copy is [N][ldp] int8, ldp = round_up(K, 16)
   int8_t* d_W = nullptr;
   int32_t* d_wsum = nullptr;       // [N][wsum_ld]: per-row prefix sums over 128-byte K tiles
+  // int16 weights (myl_weight16_register): N = 2 * n16 int8 rows, row 2i = high
+  // byte and row 2i + 1 = low byte - 128 of int16 row i; w_shifts has n16 entries.
+  bool w16 = false;
+  int64_t n16 = 0;
   int64_t wsum_ld = 0;             // K tiles + 1
   std::vector<uint8_t> w_shifts;
   CUtensorMap tm128{};             // TMA map with a 128-row box (one channel tile)
@@ -113,7 +117,7 @@ struct myl_ctx {
   int gemv_max_m = 4, force_split_k = 0, force_tile = 0, inject_fault = 0;
   int64_t launches = 0;
   PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-  DevBuf x, y, rq, planes, part, h, hplanes, moe;
+  DevBuf x, y, rq, planes, part, h, hplanes, moe, xsum;
   // Host-pointer calls on page-locked memory: copy-in and copy-out streams
   // and one event pair per chunk.
   cudaStream_t s_in = nullptr, s_out = nullptr;
@@ -187,10 +191,12 @@ static int signed_total_shift(uint8_t w_shift, uint8_t act_frac, uint8_t out_fra
   return MYL_OK;
 }
 
+static int64_t out_features(const myl_weight* w) { return w->w16 ? w->n16 : w->N; }
+
 static int shift_plan(const myl_weight* w, uint8_t act_frac, const uint8_t* out_frac, int per_channel,
                       std::vector<int8_t>& s) {
-  s.resize(size_t(w->N));
-  for (int64_t r = 0; r < w->N; ++r)
+  s.resize(size_t(out_features(w)));
+  for (int64_t r = 0; r < out_features(w); ++r)
     TRY(signed_total_shift(w->w_shifts[size_t(r)], act_frac, per_channel ? out_frac[r] : out_frac[0],
                            &s[size_t(r)]));
   return MYL_OK;
@@ -368,6 +374,8 @@ static int launch_tc_variant(myl_ctx* ctx, const myl_weight* w, const CUtensorMa
       return launch_tc_mode<BN, EPI_MULT>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
     case EPI_SILU:
       return launch_tc_mode<BN, EPI_SILU>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
+    case EPI_W16:
+      return launch_tc_mode<BN, EPI_W16>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
     default:
       return fail(MYL_ERR_ARG, "unknown epilogue mode %d", ep.mode);
   }
@@ -477,7 +485,20 @@ static int launch_tc(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_
 }
 
 static int dispatch_linear(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
-                           int64_t ldx, const Epilogue& ep, cudaStream_t st) {
+                           int64_t ldx, const Epilogue& ep_in, cudaStream_t st) {
+  Epilogue ep = ep_in;
+  if (w->w16) {
+    // int16 weights: the LM head's path A, i32 logits (model.rs:285-296).
+    if (ep.mode != EPI_SHIFT || !ep.out_i32 || ep.bias)
+      return fail(MYL_ERR_ARG, "int16 weights take the LM-head requant (MYL_RQ_SHIFT_I32) only");
+    TRY(ensure(ctx->xsum, size_t(M) * 8));
+    const unsigned blocks = unsigned(std::min<int64_t>((M + 7) / 8, int64_t(ctx->num_sms) * 8));
+    x_row_sums_kernel<<<blocks, 256, 0, st>>>(x, ldx, M, w->K, static_cast<int64_t*>(ctx->xsum.p));
+    CUDA_TRY(cudaGetLastError());
+    ctx->launches++;
+    ep.mode = EPI_W16;
+    ep.xsum = static_cast<const int64_t*>(ctx->xsum.p);
+  }
   if (M <= ctx->gemv_max_m && M <= 4) return launch_gemv(ctx, w, x, M, ldx, ep, st);
   return launch_tc(ctx, w, x, M, ldx, ep, st);
 }
@@ -521,7 +542,7 @@ static int host_linear(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int6
   if (!ctx || !w || (M > 0 && (!x || !y))) return fail(MYL_ERR_ARG, "null argument");
   if (M < 0) return fail(MYL_ERR_SHAPE, "M = %lld is negative", (long long)M);
   if (M == 0 || w->N == 0) return MYL_OK;
-  const int64_t N = w->N, K = w->K;
+  const int64_t N = out_features(w), K = w->K;
   const size_t osz = out_i32 ? 4 : 2;
   TRY(ensure(ctx->x, size_t(M) * size_t(K) * 2));
   TRY(ensure(ctx->y, size_t(M) * size_t(N) * osz));
@@ -635,7 +656,7 @@ int myl_destroy(myl_ctx* ctx) {
   for (auto& kv : ctx->backend_cache) myl_weight_release(ctx, kv.second);
   ctx->backend_cache.clear();
   for (DevBuf* b : {&ctx->x, &ctx->y, &ctx->rq, &ctx->planes, &ctx->part, &ctx->h, &ctx->hplanes,
-                    &ctx->moe})
+                    &ctx->moe, &ctx->xsum})
     if (b->p) cudaFree(b->p);
   if (ctx->d_err) cudaFree(ctx->d_err);
   if (ctx->h_err) cudaFreeHost(ctx->h_err);
@@ -729,6 +750,7 @@ int myl_weight_release(myl_ctx* ctx, myl_weight* w) {
 int myl_linear_w8a16(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
                      uint8_t act_frac_bits, uint8_t out_frac_bits, int16_t* y) {
   if (!ctx || !w) return fail(MYL_ERR_ARG, "null argument");
+  if (w->w16) return fail(MYL_ERR_ARG, "int16 weight: use myl_lm_head_w16a16_i32 or myl_linear_dev");
   std::vector<int8_t> s;
   TRY(shift_plan(w, act_frac_bits, &out_frac_bits, 0, s));
   return host_linear(ctx, w, x, M, EPI_SHIFT, 0, s.data(), nullptr, y);
@@ -737,6 +759,7 @@ int myl_linear_w8a16(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_
 int myl_linear_w8a16_pc(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
                         uint8_t act_frac_bits, const uint8_t* out_frac_bits, int16_t* y) {
   if (!ctx || !w || (w->N > 0 && !out_frac_bits)) return fail(MYL_ERR_ARG, "null argument");
+  if (w->w16) return fail(MYL_ERR_ARG, "int16 weight: use myl_lm_head_w16a16_i32 or myl_linear_dev");
   std::vector<int8_t> s;
   TRY(shift_plan(w, act_frac_bits, out_frac_bits, 1, s));
   return host_linear(ctx, w, x, M, EPI_SHIFT, 0, s.data(), nullptr, y);
@@ -745,6 +768,48 @@ int myl_linear_w8a16_pc(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int
 int myl_lm_head_w8a16_i32(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
                           uint8_t final_norm_frac, uint8_t logit_frac, int32_t* logits) {
   if (!ctx || !w) return fail(MYL_ERR_ARG, "null argument");
+  if (w->w16) return fail(MYL_ERR_ARG, "int16 weight: use myl_lm_head_w16a16_i32 or myl_linear_dev");
+  std::vector<int8_t> s;
+  TRY(shift_plan(w, final_norm_frac, &logit_frac, 0, s));
+  return host_linear(ctx, w, x, M, EPI_SHIFT, 1, s.data(), nullptr, logits);
+}
+
+int myl_weight16_register(myl_ctx* ctx, const int16_t* W, int64_t out_features_, int64_t in_features,
+                          int64_t ldw, const uint8_t* w_shifts, myl_weight** out) {
+  if (!ctx || !out || (out_features_ > 0 && (!W || !w_shifts))) return fail(MYL_ERR_ARG, "null argument");
+  *out = nullptr;
+  if (in_features <= 0 || out_features_ < 0 || ldw < in_features)
+    return fail(MYL_ERR_SHAPE, "bad weight shape [%lld][%lld] ld %lld", (long long)out_features_,
+                (long long)in_features, (long long)ldw);
+  if (out_features_ > (int64_t(1) << 30))
+    return fail(MYL_ERR_UNSUPPORTED, "int16 weight with more than 2^30 rows");
+  // Row i of the int16 weight becomes int8 rows 2i (w >> 8) and 2i + 1
+  // ((w & 255) - 128), so w = 256 * row_2i + row_2i+1 + 128.
+  const int64_t N = out_features_, K = in_features;
+  std::vector<int8_t> w8(size_t(2 * N) * size_t(K));
+  for (int64_t i = 0; i < N; ++i) {
+    const int16_t* src = W + i * ldw;
+    int8_t* hi = &w8[size_t(2 * i) * size_t(K)];
+    int8_t* lo = hi + K;
+    for (int64_t k = 0; k < K; ++k) {
+      hi[k] = int8_t(src[k] >> 8);
+      lo[k] = int8_t(int(src[k] & 0xFF) - 128);
+    }
+  }
+  std::vector<uint8_t> zero(size_t(std::max<int64_t>(2 * N, 1)), 0);
+  myl_weight* w = nullptr;
+  TRY(myl_weight_register(ctx, w8.data(), 2 * N, K, K, zero.data(), &w));
+  w->w16 = true;
+  w->n16 = N;
+  w->w_shifts.assign(w_shifts, w_shifts + N);
+  *out = w;
+  return MYL_OK;
+}
+
+int myl_lm_head_w16a16_i32(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
+                           uint8_t final_norm_frac, uint8_t logit_frac, int32_t* logits) {
+  if (!ctx || !w) return fail(MYL_ERR_ARG, "null argument");
+  if (!w->w16) return fail(MYL_ERR_ARG, "weight is not int16 (myl_weight16_register)");
   std::vector<int8_t> s;
   TRY(shift_plan(w, final_norm_frac, &logit_frac, 0, s));
   return host_linear(ctx, w, x, M, EPI_SHIFT, 1, s.data(), nullptr, logits);
@@ -753,6 +818,7 @@ int myl_lm_head_w8a16_i32(myl_ctx* ctx, const myl_weight* w, const int16_t* x, i
 int myl_linear_w8a16_mult(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
                           const int32_t* mult, const uint8_t* shift, int16_t* y) {
   if (!ctx || !w || (w->N > 0 && (!mult || !shift))) return fail(MYL_ERR_ARG, "null argument");
+  if (w->w16) return fail(MYL_ERR_ARG, "int16 weight: use myl_lm_head_w16a16_i32 or myl_linear_dev");
   for (int64_t r = 0; r < w->N; ++r)
     if (shift[r] > 126) return fail(MYL_ERR_OVERFLOW, "multiplier shift %u > 126", unsigned(shift[r]));
   return host_linear(ctx, w, x, M, EPI_MULT, 0, reinterpret_cast<const int8_t*>(shift), mult, y);
@@ -800,7 +866,9 @@ int myl_requant_create(myl_ctx* ctx, const myl_weight* w, int mode, uint8_t act_
                        const uint8_t* shift, myl_requant** out) {
   if (!ctx || !w || !out) return fail(MYL_ERR_ARG, "null argument");
   *out = nullptr;
-  const int64_t N = w->N;
+  const int64_t N = out_features(w);
+  if (w->w16 && mode != MYL_RQ_SHIFT_I32)
+    return fail(MYL_ERR_ARG, "int16 weights take the LM-head requant (MYL_RQ_SHIFT_I32) only");
   std::vector<int8_t> s;
   std::vector<int32_t> m;
   if (mode == MYL_RQ_SHIFT_I16 || mode == MYL_RQ_SHIFT_I32) {
@@ -861,15 +929,17 @@ static Epilogue make_ep(const myl_requant* rq, void* y, int64_t ldy) {
 int myl_linear_dev(myl_ctx* ctx, const myl_weight* w, const myl_requant* rq, const int16_t* x,
                    int64_t M, int64_t ldx, void* y, int64_t ldy, void* stream) {
   if (!ctx || !w || !rq || (M > 0 && (!x || !y))) return fail(MYL_ERR_ARG, "null argument");
-  if (rq->N != w->N) return fail(MYL_ERR_SHAPE, "requant has %lld channels, weight %lld",
-                                 (long long)rq->N, (long long)w->N);
-  if (M < 0 || ldx < w->K || ldy < w->N) return fail(MYL_ERR_SHAPE, "bad M/ldx/ldy");
+  if (rq->N != out_features(w))
+    return fail(MYL_ERR_SHAPE, "requant has %lld channels, weight %lld", (long long)rq->N,
+                (long long)out_features(w));
+  if (M < 0 || ldx < w->K || ldy < out_features(w)) return fail(MYL_ERR_SHAPE, "bad M/ldx/ldy");
   return run_linear(ctx, w, x, M, ldx, make_ep(rq, y, ldy), static_cast<cudaStream_t>(stream));
 }
 
 int myl_linear_acc_dev(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M, int64_t ldx,
                        int64_t* acc, void* stream) {
   if (!ctx || !w || (M > 0 && (!x || !acc))) return fail(MYL_ERR_ARG, "null argument");
+  if (w->w16) return fail(MYL_ERR_ARG, "int16 weight: use myl_lm_head_w16a16_i32 or myl_linear_dev");
   if (M < 0 || ldx < w->K) return fail(MYL_ERR_SHAPE, "bad M/ldx");
   Epilogue ep{};
   ep.mode = EPI_ACC_I64;
@@ -921,6 +991,7 @@ int myl_linear_w8a16_bias(myl_ctx* ctx, const myl_weight* w, const int16_t* x, i
                           uint8_t act_frac_bits, uint8_t out_frac_bits, const int16_t* bias,
                           const uint8_t* bias_shifts, int16_t* y) {
   if (!ctx || !w || (w->N > 0 && (!bias || !bias_shifts))) return fail(MYL_ERR_ARG, "null argument");
+  if (w->w16) return fail(MYL_ERR_ARG, "int16 weight: use myl_lm_head_w16a16_i32 or myl_linear_dev");
   std::vector<int8_t> s;
   TRY(shift_plan(w, act_frac_bits, &out_frac_bits, 0, s));
   std::vector<int32_t> b;
@@ -1134,6 +1205,7 @@ int myl_linear_planes_dev(myl_ctx* ctx, const myl_weight* w, const myl_requant* 
                           const uint8_t* xhi, const uint8_t* xlo, int64_t ldp, int64_t M, void* y,
                           int64_t ldy, void* stream) {
   if (!ctx || !w || (M > 0 && (!xhi || !xlo || !y))) return fail(MYL_ERR_ARG, "null argument");
+  if (w->w16) return fail(MYL_ERR_ARG, "int16 weight: use myl_lm_head_w16a16_i32 or myl_linear_dev");
   if (M < 0 || ldp < w->K || ldp % 16 != 0 || ldy < w->N)
     return fail(MYL_ERR_SHAPE, "bad M/ldp/ldy");
   if ((reinterpret_cast<uintptr_t>(xhi) | reinterpret_cast<uintptr_t>(xlo)) & 15)
@@ -1230,6 +1302,7 @@ extern "C" int myl_linear_noalloc_dev(myl_ctx* ctx, const myl_weight* w, const m
                                       const int16_t* x, int64_t M, int64_t ldx, void* y,
                                       int64_t ldy, void* stream) {
   if (!ctx || !w || !rq || (M > 0 && (!x || !y))) return fail(MYL_ERR_ARG, "null argument");
+  if (w->w16) return fail(MYL_ERR_ARG, "int16 weight: use myl_lm_head_w16a16_i32 or myl_linear_dev");
   if (rq->N != w->N) return fail(MYL_ERR_SHAPE, "requant/weight channel mismatch");
   if (M < 0 || ldx < w->K || ldy < w->N) return fail(MYL_ERR_SHAPE, "bad M/ldx/ldy");
   if (w->K > 65536)

@@ -45,7 +45,9 @@ def build() -> str:
 def lib():
     global _lib
     if _lib is None:
-        if not os.path.exists(_LIB_PATH):
+        srcs = [os.path.join(_HERE, f) for f in ("myl_oracle.c", "myl_oracle.h")]
+        if not os.path.exists(_LIB_PATH) or any(
+                os.path.getmtime(f) > os.path.getmtime(_LIB_PATH) for f in srcs if os.path.exists(f)):
             build()
         L = C.CDLL(_LIB_PATH)
         i64, u8, i32 = C.c_int64, C.c_uint8, C.c_int32
@@ -70,6 +72,7 @@ def lib():
         L.mylo_linear_w8a16.argtypes = [p, i64, p, i64, i64, p, u8, u8, p]
         L.mylo_linear_w8a16_pc.argtypes = [p, i64, p, i64, i64, p, u8, p, p]
         L.mylo_lm_head_w8a16_i32.argtypes = [p, i64, p, i64, i64, p, u8, u8, p]
+        L.mylo_lm_head_w16a16_i32.argtypes = [p, i64, p, i64, i64, p, u8, u8, p]
         L.mylo_linear_w8a16_mult.argtypes = [p, i64, p, i64, i64, p, p, p]
         L.mylo_linear_acc_i64.argtypes = [p, i64, p, i64, i64, p]
         L.mylo_add_bias_i16.argtypes = [p, p, p, i64, u8]
@@ -200,6 +203,23 @@ def lm_head_w8a16_i32(x, W, in_features: int, w_shifts, final_norm_frac: int,
     xs, single = _rows(x, in_features)
     y = np.zeros((xs.shape[0], N), np.int32)
     _check("lm_head_w8a16_i32", lib().mylo_lm_head_w8a16_i32(
+        _ptr(xs), xs.shape[0], _ptr(W), in_features, N, _ptr(w_shifts), final_norm_frac, logit_frac,
+        _ptr(y)))
+    return y[0] if single else y
+
+
+def lm_head_w16a16_i32(x, W, in_features: int, w_shifts, final_norm_frac: int,
+                       logit_frac: int) -> np.ndarray:
+    """runtime/src/model.rs:285-296 (path A): int16 weights, i64 dot, rescale_i64,
+    clamp to i32."""
+    W = _c(W, np.int16).reshape(-1)
+    w_shifts = _c(w_shifts, np.uint8)
+    N = w_shifts.size
+    if in_features <= 0 or W.size != in_features * N:
+        raise OracleError("lm_head_w16a16_i32", ERR_SHAPE)
+    xs, single = _rows(x, in_features)
+    y = np.zeros((xs.shape[0], N), np.int32)
+    _check("lm_head_w16a16_i32", lib().mylo_lm_head_w16a16_i32(
         _ptr(xs), xs.shape[0], _ptr(W), in_features, N, _ptr(w_shifts), final_norm_frac, logit_frac,
         _ptr(y)))
     return y[0] if single else y

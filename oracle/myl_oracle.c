@@ -208,6 +208,29 @@ int mylo_lm_head_w8a16_i32(const int16_t* x, int64_t M, const int8_t* W, int64_t
   return MYLO_OK;
 }
 
+/* ---- LM head path A, runtime/src/model.rs:285-296 ---------------------------
+ * int16 weights, i64 products and accumulator, row_frac = shifts[row] +
+ * final_norm_frac (u8), rescale_i64 to logit_frac, clamp to i32. */
+int mylo_lm_head_w16a16_i32(const int16_t* x, int64_t M, const int16_t* W, int64_t K, int64_t N,
+                            const uint8_t* w_shifts, uint8_t final_norm_frac, uint8_t logit_frac,
+                            int32_t* logits) {
+  int rc = check_linear(M, K, N, w_shifts, final_norm_frac, NULL, logit_frac);
+  if (rc) return rc;
+  int64_t total = M * N;
+#pragma omp parallel for schedule(static)
+  for (int64_t e = 0; e < total; ++e) {
+    int64_t m = e / N, r = e % N;
+    const int16_t* wr = W + r * K;
+    const int16_t* xr = x + m * K;
+    int64_t acc = 0;
+    for (int64_t d = 0; d < K; ++d) acc += (int64_t)wr[d] * (int64_t)xr[d];
+    int64_t v = 0;
+    mylo_rescale_i64(acc, (uint8_t)(w_shifts[r] + final_norm_frac), logit_frac, &v);
+    logits[e] = mylo_clamp_i32(v);
+  }
+  return MYLO_OK;
+}
+
 /* ---- multiplier requant (generalisation; pow2 identity fixed_point.rs:365) */
 
 int mylo_linear_w8a16_mult(const int16_t* x, int64_t M, const int8_t* W, int64_t K, int64_t N,

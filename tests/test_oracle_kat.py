@@ -221,6 +221,35 @@ def test_lm_head_fixture_saturates():
     assert 0.3 < sat < 1.0  # the case exercises the i32 clamp
 
 
+def test_lm_head_w16a16_known_answers():
+    """model.rs:285-296 (path A): int16 x int16 products in i64, no i32 overflow."""
+    W = np.array([[32767, -32768], [1, -1]], np.int16)
+    x = np.array([32767, 1], np.int16)
+    y = O.lm_head_w16a16_i32(x, W, 2, [0, 0], 0, 0)
+    assert y.tolist() == [32767 * 32767 - 32768, 32766]
+    # logit_frac above the row's fraction: a left shift, then the i32 clamp
+    y = O.lm_head_w16a16_i32(x, W, 2, [0, 0], 0, 2)
+    assert y.tolist() == [2**31 - 1, 32766 * 4]
+    # round half to even on the rescale: acc = 6 -> 6 / 4 = 1.5 -> 2; acc = 10 -> 2.5 -> 2
+    y = O.lm_head_w16a16_i32(np.array([[3, 0], [5, 0]], np.int16), np.array([[2, 0]], np.int16), 2,
+                             [1], 1, 0)
+    assert y.tolist() == [[2], [2]]
+    # u8 overflow of shifts[row] + final_norm_frac panics in a debug build
+    with pytest.raises(O.OracleError):
+        O.lm_head_w16a16_i32(x, W, 2, [250, 0], 10, 0)
+
+
+@pytest.mark.parametrize("case", [c for c in fixtures.linear_cases() if c["kind"] == "lm_head"],
+                         ids=lambda c: c["name"])
+def test_lm_head_w16a16_equals_path_b_on_int8_range(case):
+    """With weights inside the int8 range both LM-head paths compute the same
+    i64 dot, so path A reproduces the path-B fixtures."""
+    c = case
+    W16 = np.asarray(c["W"], np.int8).astype(np.int16)
+    y = O.lm_head_w16a16_i32(c["x"], W16, c["K"], c["w_shifts"], c["act_frac"], c["out_frac"])
+    assert np.array_equal(y, c["y"])
+
+
 @pytest.mark.parametrize("case", fixtures.mlp_cases(), ids=lambda c: c["name"])
 def test_mlp_fixture(case):
     c, p = case, case["params"]
