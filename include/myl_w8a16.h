@@ -199,6 +199,21 @@ int myl_mlp_partial_dev(myl_ctx* ctx, const myl_mlp* mlp, const int16_t* x, int6
 int myl_mlp_requant_dev(myl_ctx* ctx, const myl_mlp* mlp, const int64_t* acc, int64_t M, int16_t* y,
                         int64_t ldy, void* stream);
 
+/* --- linear_backward (kernels/src/backward.rs:147-211) -----------------------------
+ * For each of M tokens, with g = dL/dy [N] int32 and x [K] int16:
+ *   gx[j] = clamp_i32(rescale_i64(clamp_i64(rne_i128(sum_i (g[i]*W[i][j])
+ *                     << (ref - w_shifts[i]), ref)), g_frac, gx_frac)),
+ *   ref = max_i w_shifts[i]  (the summands aligned to the largest shift,
+ *   rounded once at the end);
+ *   gw[i][j] = g[i] * x[j]   int64, [M][N][K] (NULL: not computed).
+ * Exact (i64 group sums of equal shift, an i128 accumulator). Limits:
+ * w_shifts <= 64, N < 2^24; int16 weights are not supported. */
+int myl_linear_backward(myl_ctx* ctx, const myl_weight* w, const int32_t* g, const int16_t* x,
+                        int64_t M, uint8_t g_frac, uint8_t gx_frac, int32_t* gx, int64_t* gw);
+int myl_linear_backward_dev(myl_ctx* ctx, const myl_weight* w, const int32_t* g, int64_t ldg,
+                            const int16_t* x, int64_t ldx, int64_t M, uint8_t g_frac,
+                            uint8_t gx_frac, int32_t* gx, int64_t ldgx, int64_t* gw, void* stream);
+
 /* --- MoE layer --------------------------------------------------------------------
  * No counterpart in the reference, which has no MoE; the layer is composed of
  * its primitives only:

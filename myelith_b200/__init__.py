@@ -108,6 +108,8 @@ def load_library(path: str | None = None):
             "myl_launch_count": ([vp], i64),
             "myl_debug_inject_wait_fault": ([vp, i32], i32),
             "myl_weight16_register": ([vp, vp, i64, i64, i64, vp, C.POINTER(vp)], i32),
+            "myl_linear_backward": ([vp, vp, vp, vp, i64, u8, u8, vp, vp], i32),
+            "myl_linear_backward_dev": ([vp, vp, vp, i64, vp, i64, i64, u8, u8, vp, i64, vp, vp], i32),
             "myl_lm_head_w16a16_i32": ([vp, vp, vp, i64, u8, u8, vp], i32),
             "myl_moe_register": ([vp, C.POINTER(MoeSpec), C.POINTER(vp)], i32),
             "myl_moe_release": ([vp, vp], i32),
@@ -304,6 +306,25 @@ class Weight:
     def requant(self, mode: int = RQ_SHIFT_I16, act_frac: int = 0, out_frac=0, mult=None,
                 shift=None) -> "Requant":
         return Requant(self, mode, act_frac, out_frac, mult, shift)
+
+    def backward(self, g, x, g_frac: int, gx_frac: int, want_gw: bool = True):
+        """linear_backward (kernels/src/backward.rs:147-211) on M tokens:
+        g [M, N] int32, x [M, K] int16 -> (gx [M, K] int32, gw [M, N, K] int64 or None)."""
+        g = np.ascontiguousarray(_c(g, np.int32).reshape(-1, self.out_features))
+        xs = np.ascontiguousarray(_c(x, np.int16).reshape(-1, self.in_features))
+        if xs.shape[0] != g.shape[0]:
+            raise MylError("myl_linear_backward", MYL_ERR_SHAPE, "g and x have different row counts")
+        M = g.shape[0]
+        gx = np.zeros((M, self.in_features), np.int32)
+        gw = np.zeros((M, self.out_features, self.in_features), np.int64) if want_gw else None
+        _check("myl_linear_backward", load_library().myl_linear_backward(
+            self.ctx.handle, self._h, _p(g), _p(xs), M, g_frac, gx_frac, _p(gx), _p(gw)))
+        return gx, gw
+
+    def backward_dev(self, g, x, g_frac: int, gx_frac: int, gx, gw=None, stream=None) -> None:
+        _check("myl_linear_backward_dev", load_library().myl_linear_backward_dev(
+            self.ctx.handle, self._h, _p(g), g.stride(0), _p(x), x.stride(0), g.shape[0], g_frac,
+            gx_frac, _p(gx), gx.stride(0), _p(gw), _stream_ptr(stream)))
 
     def linear_dev(self, rq: "Requant", x, y, stream=None) -> None:
         """y[M, N] = requant(W x) for torch CUDA tensors x [M, >=K] int16."""

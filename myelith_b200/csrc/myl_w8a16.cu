@@ -31,6 +31,7 @@
 #include "gemm_tc.cuh"
 #include "gemv.cuh"
 #include "moe.cuh"
+#include "backward.cuh"
 
 using namespace myl;
 
@@ -80,6 +81,12 @@ struct myl_weight {
   // byte and row 2i + 1 = low byte - 128 of int16 row i; w_shifts has n16 entries.
   bool w16 = false;
   int64_t n16 = 0;
+  // linear_backward: rows sorted by shift and the groups of equal shift,
+  // made on the first backward call.
+  int bwd_ref = -1;
+  int bwd_ngroups = 0;
+  int32_t* d_bwd_perm = nullptr;
+  BwdGroup* d_bwd_groups = nullptr;
   int64_t wsum_ld = 0;             // K tiles + 1
   std::vector<uint8_t> w_shifts;
   CUtensorMap tm128{};             // TMA map with a 128-row box (one channel tile)
@@ -743,6 +750,8 @@ int myl_weight_release(myl_ctx* ctx, myl_weight* w) {
   cudaStreamSynchronize(ctx->stream);
   if (w->d_W) cudaFree(w->d_W);
   if (w->d_wsum) cudaFree(w->d_wsum);
+  if (w->d_bwd_perm) cudaFree(w->d_bwd_perm);
+  if (w->d_bwd_groups) cudaFree(w->d_bwd_groups);
   delete w;
   return MYL_OK;
 }
@@ -1743,6 +1752,129 @@ int myl_moe_forward(myl_ctx* ctx, const myl_moe* m, const int16_t* x, int64_t T,
   TRY(myl_moe_dev(ctx, m, static_cast<const int16_t*>(ctx->x.p), T, m->H,
                   static_cast<int16_t*>(ctx->y.p), m->H, nullptr, nullptr, st));
   CUDA_TRY(cudaMemcpyAsync(out, ctx->y.p, bytes, cudaMemcpyDeviceToHost, st));
+  return check_device_error(ctx);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------
+// linear_backward (kernels/src/backward.rs:147-211)
+
+static int prepare_backward(myl_ctx* ctx, myl_weight* w) {
+  if (w->bwd_ref >= 0) return MYL_OK;
+  const int64_t N = w->N;
+  int ref = 0;
+  for (int64_t i = 0; i < N; ++i) ref = std::max(ref, int(w->w_shifts[size_t(i)]));
+  // The alignment shifts of the i128 sum stay below 64 bits (the reference's
+  // shifts are at most 20, quantize.py:15).
+  if (ref > 64)
+    return fail(MYL_ERR_UNSUPPORTED, "linear_backward: w_shift %d above 64", ref);
+  std::vector<int32_t> perm(static_cast<size_t>(N));
+  for (int64_t i = 0; i < N; ++i) perm[size_t(i)] = int32_t(i);
+  std::stable_sort(perm.begin(), perm.end(), [&](int32_t a, int32_t b) {
+    return w->w_shifts[size_t(a)] > w->w_shifts[size_t(b)];
+  });
+  std::vector<BwdGroup> groups;
+  for (int64_t r = 0; r < N;) {
+    const int sh = w->w_shifts[size_t(perm[size_t(r)])];
+    int64_t e = r;
+    while (e < N && w->w_shifts[size_t(perm[size_t(e)])] == sh) ++e;
+    groups.push_back(BwdGroup{ref - sh, int(r), int(e)});
+    r = e;
+  }
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  if (cudaMalloc(&w->d_bwd_perm, perm.size() * 4) != cudaSuccess ||
+      cudaMalloc(&w->d_bwd_groups, groups.size() * sizeof(BwdGroup)) != cudaSuccess ||
+      cudaMemcpy(w->d_bwd_perm, perm.data(), perm.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(w->d_bwd_groups, groups.data(), groups.size() * sizeof(BwdGroup),
+                 cudaMemcpyHostToDevice) != cudaSuccess)
+    return fail(MYL_ERR_CUDA, "linear_backward: upload of the row groups failed");
+  w->bwd_ngroups = int(groups.size());
+  w->bwd_ref = ref;
+  return MYL_OK;
+}
+
+static int run_backward(myl_ctx* ctx, myl_weight* w, const int32_t* g, int64_t ldg, const int16_t* x,
+                        int64_t ldx, int64_t M, int frac_shift, int32_t* gx, int64_t ldgx, int64_t* gw,
+                        cudaStream_t st) {
+  constexpr int MT = 4;
+  const int64_t K = w->K, N = w->N;
+  const unsigned gx_blocks = unsigned((K + BWD_THREADS * BWD_COLS - 1) / (BWD_THREADS * BWD_COLS));
+  for (int64_t m0 = 0; m0 < M; m0 += int64_t(MT) * 65535) {
+    const int64_t mc = std::min<int64_t>(M - m0, int64_t(MT) * 65535);
+    linear_backward_gx_kernel<MT><<<dim3(gx_blocks, unsigned((mc + MT - 1) / MT)), BWD_THREADS, 0, st>>>(
+        w->d_W, w->ldp, K, w->d_bwd_perm, w->d_bwd_groups, w->bwd_ngroups, w->bwd_ref, g + m0 * ldg,
+        ldg, mc, frac_shift, gx + m0 * ldgx, ldgx);
+    CUDA_TRY(cudaGetLastError());
+    ctx->launches++;
+  }
+  if (gw) {
+    const unsigned blocks = unsigned(std::min<int64_t>(M * N, int64_t(ctx->num_sms) * 32));
+    linear_backward_gw_kernel<<<blocks, 256, 0, st>>>(g, ldg, x, ldx, M, N, K, gw);
+    CUDA_TRY(cudaGetLastError());
+    ctx->launches++;
+  }
+  return MYL_OK;
+}
+
+static int check_backward(const myl_weight* w, uint8_t g_frac, uint8_t gx_frac, int* frac_shift) {
+  if (w->w16) return fail(MYL_ERR_ARG, "linear_backward: int16 weights are not supported");
+  if (w->N <= 0) return fail(MYL_ERR_SHAPE, "linear_backward: w_shifts is empty");
+  if (w->N >= (int64_t(1) << 24))
+    return fail(MYL_ERR_UNSUPPORTED, "linear_backward: 2^24 or more output rows");
+  // rescale_i64(., g_frac, gx_frac) with the debug-build checks (fixed_point.rs:184-191).
+  int8_t sh = 0;
+  TRY(signed_total_shift(0, g_frac, gx_frac, &sh));
+  *frac_shift = sh;
+  return MYL_OK;
+}
+
+extern "C" {
+
+int myl_linear_backward_dev(myl_ctx* ctx, const myl_weight* w, const int32_t* g, int64_t ldg,
+                            const int16_t* x, int64_t ldx, int64_t M, uint8_t g_frac,
+                            uint8_t gx_frac, int32_t* gx, int64_t ldgx, int64_t* gw, void* stream) {
+  if (!ctx || !w || (M > 0 && (!g || !gx || (gw && !x)))) return fail(MYL_ERR_ARG, "null argument");
+  int frac_shift = 0;
+  TRY(check_backward(w, g_frac, gx_frac, &frac_shift));
+  if (M < 0 || ldg < w->N || ldgx < w->K || (gw && ldx < w->K))
+    return fail(MYL_ERR_SHAPE, "bad M/ldg/ldx/ldgx");
+  if (M == 0) return MYL_OK;
+  myl_weight* wm = const_cast<myl_weight*>(w);
+  TRY(prepare_backward(ctx, wm));
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  return run_backward(ctx, wm, g, ldg, x, ldx, M, frac_shift, gx, ldgx, gw,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int myl_linear_backward(myl_ctx* ctx, const myl_weight* w, const int32_t* g, const int16_t* x,
+                        int64_t M, uint8_t g_frac, uint8_t gx_frac, int32_t* gx, int64_t* gw) {
+  if (!ctx || !w || (M > 0 && (!g || !x || !gx))) return fail(MYL_ERR_ARG, "null argument");
+  int frac_shift = 0;
+  TRY(check_backward(w, g_frac, gx_frac, &frac_shift));
+  if (M < 0) return fail(MYL_ERR_SHAPE, "M = %lld is negative", (long long)M);
+  if (M == 0) return MYL_OK;
+  myl_weight* wm = const_cast<myl_weight*>(w);
+  TRY(prepare_backward(ctx, wm));
+  const int64_t N = w->N, K = w->K;
+  const size_t gb = size_t(M) * size_t(N) * 4, xb = size_t(M) * size_t(K) * 2,
+               gxb = size_t(M) * size_t(K) * 4, gwb = gw ? size_t(M) * size_t(N) * size_t(K) * 8 : 0;
+  // workspace: g | x | gx | gw (256-byte aligned pieces)
+  MoeArena a;
+  const size_t og = a.take<int32_t>(M * N), ox = a.take<int16_t>(M * K), ogx = a.take<int32_t>(M * K),
+               ogw = gw ? a.take<int64_t>(M * N * K) : 0;
+  TRY(ensure(ctx->moe, a.off));
+  uint8_t* b = static_cast<uint8_t*>(ctx->moe.p);
+  cudaStream_t st = ctx->stream;
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  CUDA_TRY(cudaMemcpyAsync(b + og, g, gb, cudaMemcpyHostToDevice, st));
+  CUDA_TRY(cudaMemcpyAsync(b + ox, x, xb, cudaMemcpyHostToDevice, st));
+  TRY(run_backward(ctx, wm, reinterpret_cast<const int32_t*>(b + og), N,
+                   reinterpret_cast<const int16_t*>(b + ox), K, M, frac_shift,
+                   reinterpret_cast<int32_t*>(b + ogx), K, gw ? reinterpret_cast<int64_t*>(b + ogw) : nullptr,
+                   st));
+  CUDA_TRY(cudaMemcpyAsync(gx, b + ogx, gxb, cudaMemcpyDeviceToHost, st));
+  if (gw) CUDA_TRY(cudaMemcpyAsync(gw, b + ogw, gwb, cudaMemcpyDeviceToHost, st));
   return check_device_error(ctx);
 }
 

@@ -73,6 +73,7 @@ def lib():
         L.mylo_linear_w8a16_pc.argtypes = [p, i64, p, i64, i64, p, u8, p, p]
         L.mylo_lm_head_w8a16_i32.argtypes = [p, i64, p, i64, i64, p, u8, u8, p]
         L.mylo_lm_head_w16a16_i32.argtypes = [p, i64, p, i64, i64, p, u8, u8, p]
+        L.mylo_linear_backward.argtypes = [p, p, i64, p, i64, i64, p, u8, u8, p, p]
         L.mylo_linear_w8a16_mult.argtypes = [p, i64, p, i64, i64, p, p, p]
         L.mylo_linear_acc_i64.argtypes = [p, i64, p, i64, i64, p]
         L.mylo_add_bias_i16.argtypes = [p, p, p, i64, u8]
@@ -223,6 +224,32 @@ def lm_head_w16a16_i32(x, W, in_features: int, w_shifts, final_norm_frac: int,
         _ptr(xs), xs.shape[0], _ptr(W), in_features, N, _ptr(w_shifts), final_norm_frac, logit_frac,
         _ptr(y)))
     return y[0] if single else y
+
+
+def linear_backward(g, x, W, in_features: int, w_shifts, g_frac: int, gx_frac: int,
+                    want_gw: bool = True):
+    """kernels/src/backward.rs:147-211 on M tokens: g [M, N] int32, x [M, K] int16
+    -> (gx [M, K] int32, gw [M, N, K] int64 or None)."""
+    W = _c(W, np.int8).reshape(-1)
+    w_shifts = _c(w_shifts, np.uint8)
+    N = w_shifts.size
+    if N == 0 or in_features <= 0 or W.size != in_features * N:
+        raise OracleError("linear_backward", ERR_SHAPE)  # .max().expect(...) / chunks_exact
+    g = _c(g, np.int32)
+    single = g.ndim == 1
+    g = np.ascontiguousarray(g.reshape(-1, N))
+    xs = np.ascontiguousarray(_c(x, np.int16).reshape(-1, in_features))
+    if xs.shape[0] != g.shape[0]:
+        raise OracleError("linear_backward", ERR_SHAPE)
+    M = g.shape[0]
+    gx = np.zeros((M, in_features), np.int32)
+    gw = np.zeros((M, N, in_features), np.int64) if want_gw else None
+    _check("linear_backward", lib().mylo_linear_backward(
+        _ptr(g), _ptr(xs), M, _ptr(W), in_features, N, _ptr(w_shifts), g_frac, gx_frac, _ptr(gx),
+        _ptr(gw) if gw is not None else None))
+    if single:
+        return gx[0], (gw[0] if gw is not None else None)
+    return gx, gw
 
 
 def linear_w8a16_mult(x, W, in_features: int, mult, shift) -> np.ndarray:

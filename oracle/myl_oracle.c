@@ -231,6 +231,51 @@ int mylo_lm_head_w16a16_i32(const int16_t* x, int64_t M, const int16_t* W, int64
   return MYLO_OK;
 }
 
+/* ---- linear_backward, kernels/src/backward.rs:147-211 ------------------------
+ * Per token m (the reference takes one token):
+ *   ref = max_i w_shifts[i]                      (panics for an empty w_shifts)
+ *   acc[j] = sum_i (g[i] * W[i][j]) << (ref - w_shifts[i])     in i128
+ *   gx[j]  = clamp_i32(rescale_i64(clamp_i64(rshift_round_i128(acc[j], ref)),
+ *                                  g_frac, gx_frac))
+ *   gw[i][j] = g[i] * x[j]                       (i64, no scaling)
+ * Rust panics in a debug build when a shift reaches the i128 width; this
+ * restatement reports that as an overflow (ref >= 128). gw may be NULL. */
+int mylo_linear_backward(const int32_t* g, const int16_t* x, int64_t M, const int8_t* W, int64_t K,
+                         int64_t N, const uint8_t* w_shifts, uint8_t g_frac, uint8_t gx_frac,
+                         int32_t* gx, int64_t* gw) {
+  if (M < 0 || K <= 0 || N <= 0) return MYLO_ERR_SHAPE;
+  unsigned ref = 0;
+  for (int64_t i = 0; i < N; ++i)
+    if (w_shifts[i] > ref) ref = w_shifts[i];
+  if (ref >= 128) return MYLO_ERR_OVERFLOW;
+  int s;
+  if (signed_shift(g_frac, gx_frac, 64, &s)) return MYLO_ERR_OVERFLOW;
+  int64_t total = M * K;
+#pragma omp parallel for schedule(static)
+  for (int64_t e = 0; e < total; ++e) {
+    int64_t m = e / K, j = e % K;
+    __int128 acc = 0;
+    for (int64_t i = 0; i < N; ++i) {
+      __int128 gi = g[m * N + i];
+      if (gi == 0) continue;
+      acc += (gi * (__int128)W[i * K + j]) << (ref - w_shifts[i]);
+    }
+    __int128 q = rshift_round_i128(acc, ref);
+    int64_t lim = q > (__int128)INT64_MAX ? INT64_MAX : (q < (__int128)INT64_MIN ? INT64_MIN : (int64_t)q);
+    int64_t v = 0;
+    mylo_rescale_i64(lim, g_frac, gx_frac, &v);
+    gx[e] = mylo_clamp_i32(v);
+  }
+  if (gw) {
+#pragma omp parallel for schedule(static)
+    for (int64_t e = 0; e < M * N; ++e) {
+      int64_t m = e / N;
+      for (int64_t j = 0; j < K; ++j) gw[e * K + j] = (int64_t)g[e] * (int64_t)x[m * K + j];
+    }
+  }
+  return MYLO_OK;
+}
+
 /* ---- multiplier requant (generalisation; pow2 identity fixed_point.rs:365) */
 
 int mylo_linear_w8a16_mult(const int16_t* x, int64_t M, const int8_t* W, int64_t K, int64_t N,

@@ -75,6 +75,9 @@ int mylo_linear_w8a16_pc(const int16_t* x, int64_t M, const int8_t* W, int64_t K
 
 /* runtime/src/model.rs:297-307 (LM head, path B): i64 dot, rescale_i64,
  * clamp to i32 instead of i16. */
+int mylo_linear_backward(const int32_t* g, const int16_t* x, int64_t M, const int8_t* W, int64_t K,
+                         int64_t N, const uint8_t* w_shifts, uint8_t g_frac, uint8_t gx_frac,
+                         int32_t* gx, int64_t* gw);
 int mylo_lm_head_w16a16_i32(const int16_t* x, int64_t M, const int16_t* W, int64_t K, int64_t N,
                             const uint8_t* w_shifts, uint8_t final_norm_frac, uint8_t logit_frac,
                             int32_t* logits);

@@ -61,6 +61,10 @@ def op_vectors():
     return _load("op_vectors.json")
 
 
+def backward_cases():
+    return _load("backward_cases.json")
+
+
 def softmax_cases():
     return _load("softmax_cases.json")
 

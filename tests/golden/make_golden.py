@@ -20,6 +20,8 @@ Outputs written:
                       rshift_round and linear_w8a16_ref.
   op_vectors.json     the reference's op golden vector linear_w8a16_identity
                       (conformance/vectors/op/linear_w8a16_identity.golden.json)
+  backward_cases.json the op golden vector backward_linear
+                      (conformance/vectors/op/backward_linear.golden.json)
                       re-emitted in this repo's fixture format.
   splitmix_kat.json   the first outputs of the reference's splitmix64.
 """
@@ -278,6 +280,22 @@ def main():
                               op[0]["out_frac"]) == op[0]["y"]
     with open(os.path.join(HERE, "op_vectors.json"), "w") as f:
         json.dump(op, f, indent=1)
+
+    # linear_backward (kernels/src/backward.rs:147-211): the op golden vector
+    # backward_linear, transcribed as inputs and expected outputs.
+    bl_path = os.path.join(args.reference, "INTEGER_LLM", "conformance", "vectors", "op",
+                           "backward_linear.golden.json")
+    with open(bl_path) as f:
+        bv = json.load(f)
+    bwd = [{
+        "name": bv["name"], "in_features": bv["metadata"]["in_features"],
+        "w_shifts": bv["metadata"]["w_shifts"], "g_frac": bv["metadata"]["g_frac"],
+        "gx_frac": bv["metadata"]["gx_frac"], "g": bv["inputs"]["g"]["data"],
+        "x": bv["inputs"]["x"]["data"], "W": bv["inputs"]["W"]["data"],
+        "gx": bv["outputs"]["gx"]["data"], "gW": bv["outputs"]["gW"]["data"],
+    }]
+    with open(os.path.join(HERE, "backward_cases.json"), "w") as f:
+        json.dump(bwd, f, separators=(",", ":"))
 
     # softmax_int: the op golden vector softmax_basic plus cases computed by
     # generate.py:119 softmax_int_ref (its LUT's first entry equals 2^frac_bits,

@@ -250,6 +250,75 @@ def test_lm_head_w16a16_equals_path_b_on_int8_range(case):
     assert np.array_equal(y, c["y"])
 
 
+def test_linear_backward_golden_vector():  # conformance/vectors/op/backward_linear.golden.json
+    for c in fixtures.backward_cases():
+        gx, gw = O.linear_backward(c["g"], c["x"], c["W"], c["in_features"], c["w_shifts"],
+                                   c["g_frac"], c["gx_frac"])
+        assert gx.tolist() == c["gx"]
+        assert gw.reshape(-1).tolist() == c["gW"]
+
+
+def test_linear_backward_outer_product():  # backward.rs:678-685
+    _, gw = O.linear_backward([5, -2], [3, -7, 11], np.zeros(6, np.int8), 3, [0, 0], 0, 0)
+    assert gw.reshape(-1).tolist() == [15, -35, 55, -6, 14, -22]
+
+
+def test_linear_backward_aligns_before_one_shift():
+    """backward.rs:167-178: the summands are aligned to the largest shift and
+    rounded once. Six summands of -6 at shift 4 round to 0 one by one but to
+    round(-36 / 16) = -2 together; mixed shifts divide by each row's own scale."""
+    gx, _ = O.linear_backward([-6] * 6, [1], np.ones(6, np.int8), 1, [4] * 6, 6, 6, want_gw=False)
+    assert gx.tolist() == [-2]
+    gx, _ = O.linear_backward([1, 1], [0], np.array([8, 16], np.int8), 1, [2, 4], 0, 0, want_gw=False)
+    assert gx.tolist() == [3]  # 8 / 2^2 + 16 / 2^4
+    with pytest.raises(O.OracleError):  # empty w_shifts: .max().expect(...) panics
+        O.linear_backward(np.zeros((1, 0), np.int32), [1], np.zeros(0, np.int8), 1, [], 0, 0)
+
+
+def _linear_backward_py(g, W, shifts, g_frac, gx_frac):
+    """Python big-int restatement of backward.rs:180-199 for one token."""
+    ref = int(max(shifts))
+    acc = [0] * W.shape[1]
+    for i, gi in enumerate(g):
+        for j in range(W.shape[1]):
+            acc[j] += (int(gi) * int(W[i, j])) << (ref - int(shifts[i]))
+    out = []
+    for a in acc:
+        q = a >> ref
+        r = a - (q << ref)
+        h = (1 << (ref - 1)) if ref > 0 else 0
+        if ref > 0 and (r > h or (r == h and q & 1)):
+            q += 1
+        q = max(-(2**63), min(2**63 - 1, q))
+        s = g_frac - gx_frac
+        if s > 0:
+            qq = q >> s
+            rr = q - (qq << s)
+            hh = 1 << (s - 1)
+            if rr > hh or (rr == hh and qq & 1):
+                qq += 1
+            v = qq
+        else:
+            v = q << (-s)
+        out.append(max(-(2**31), min(2**31 - 1, v)))
+    return out
+
+
+def test_linear_backward_random_against_bigint():
+    rng = np.random.default_rng(77)
+    for trial in range(6):
+        N, K = int(rng.integers(1, 40)), int(rng.integers(1, 30))
+        W = rng.integers(-128, 128, size=(N, K), dtype=np.int8)
+        shifts = rng.integers(0, 21, size=N).astype(np.uint8)
+        g = rng.integers(-(2**31), 2**31, size=N, dtype=np.int64).astype(np.int32)
+        g[::3] = rng.integers(-50, 50, size=g[::3].size)
+        x = rng.integers(-32768, 32768, size=K, dtype=np.int16)
+        g_frac, gx_frac = int(rng.integers(0, 12)), int(rng.integers(0, 12))
+        gx, gw = O.linear_backward(g, x, W, K, shifts, g_frac, gx_frac)
+        assert gx.tolist() == _linear_backward_py(g, W, shifts, g_frac, gx_frac), trial
+        assert np.array_equal(gw, g.astype(np.int64)[:, None] * x.astype(np.int64)[None, :])
+
+
 @pytest.mark.parametrize("case", fixtures.mlp_cases(), ids=lambda c: c["name"])
 def test_mlp_fixture(case):
     c, p = case, case["params"]
