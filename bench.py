@@ -309,6 +309,8 @@ def main() -> None:
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-moe", action="store_true")
+    ap.add_argument("--sm-reserve", type=int, default=16,
+                    help="N>1: SMs left free for the overlapped collectives")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -400,6 +402,69 @@ def main() -> None:
         if tp > 1:
             dist.all_reduce(acc2, op=dist.ReduceOp.SUM)
             R2s[s].apply_acc_dev(acc2, y2, stream)
+
+    # Tensor-parallel step with the exchange overlapped: the down projection
+    # runs first, in row chunks, and each chunk's int64 partials go to a
+    # reduce-scatter (NCCL, async) while the next chunks and the gate/up
+    # projection compute on SMs the collective leaves free (myl_set_sm_limit);
+    # each rank requantises its share of the rows and an all-gather of the
+    # int16 rows gives every rank the full output, bit-identical to the
+    # all-reduce form above.
+    CH = 4 if tp > 1 and M % (4 * tp) == 0 else 1
+    mc = M // CH
+    if tp > 1:
+        acc_rs = torch.empty((CH, mc // tp, N2), dtype=torch.int64, device=dev)
+        y_own = torch.empty((CH, mc // tp, N2), dtype=torch.int16, device=dev)
+
+    def step_tp(i: int, record: bool) -> None:
+        s = i % nsets
+        ctx.split_hilo_dev(x2, p2h, p2l, stream)
+        if record:
+            e2 = torch.cuda.Event(enable_timing=True)
+            e2.record(stream)
+        works = []
+        for c in range(CH):
+            r = slice(c * mc, (c + 1) * mc)
+            W2s[s].linear_planes_dev(None, p2h[r], p2l[r], mc, acc2[r], stream)
+            works.append(dist.reduce_scatter_tensor(acc_rs[c], acc2[r], op=dist.ReduceOp.SUM,
+                                                    async_op=True))
+        if record:
+            e3 = torch.cuda.Event(enable_timing=True)
+            e3.record(stream)
+        ctx.split_hilo_dev(x1, p1h, p1l, stream)
+        if record:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        W1s[s].linear_planes_dev(R1s[s], p1h, p1l, M, y1, stream)
+        if record:
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record(stream)
+            gemm_events.append((e0, e1))
+            gemm_events.append((e2, e3))
+        gathers = []
+        for c in range(CH):
+            works[c].wait()
+            R2s[s].apply_acc_dev(acc_rs[c], y_own[c], stream)
+            gathers.append(dist.all_gather_into_tensor(
+                y2[c * mc:(c + 1) * mc].view(torch.uint8), y_own[c].view(torch.uint8), async_op=True))
+        for g in gathers:
+            g.wait()
+
+    tp_check = None
+    if tp > 1:
+        # the overlapped step must equal the all-reduce step bit for bit
+        with torch.cuda.stream(stream):
+            step(0, False)
+            ref_y2 = y2.clone()
+            y2.zero_()
+            step_tp(0, False)
+            same = torch.tensor([int(torch.equal(ref_y2, y2))], dtype=torch.int32, device=dev)
+        stream.synchronize()
+        dist.all_reduce(same, op=dist.ReduceOp.MIN)
+        tp_check = bool(same.item())
+        del ref_y2
+        ctx.set_sm_limit(max(1, ctx.num_sms - args.sm_reserve))
+        step = step_tp
 
     def barrier():
         if world > 1:
@@ -580,6 +645,7 @@ def main() -> None:
             "gemv": gemv,
             "sweep": sweep,
             "moe": moe,
+            "tp_check": tp_check,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -293,6 +293,11 @@ int myl_set_wait_timeout_ns(myl_ctx* ctx, uint64_t ns);
  * force_token_tile = 0 choose automatically (token tile 32, 64 or 128). */
 int myl_set_dispatch(myl_ctx* ctx, int gemv_max_m, int force_split_k, int force_token_tile);
 
+/* Caps the SMs the persistent kernels (tensor-core GEMM, balanced GEMV) of
+ * this context occupy, so that kernels on other streams (a collective that
+ * overlaps the GEMM) find free SMs; 0 = all SMs (the default). */
+int myl_set_sm_limit(myl_ctx* ctx, int max_sms);
+
 /* Number of this library's kernels launched on the context since init. */
 int64_t myl_launch_count(const myl_ctx* ctx);
 

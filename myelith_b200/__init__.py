@@ -106,6 +106,7 @@ def load_library(path: str | None = None):
             "myl_set_wait_timeout_ns": ([vp, C.c_uint64], i32),
             "myl_set_dispatch": ([vp, i32, i32, i32], i32),
             "myl_launch_count": ([vp], i64),
+            "myl_set_sm_limit": ([vp, i32], i32),
             "myl_debug_inject_wait_fault": ([vp, i32], i32),
             "myl_weight16_register": ([vp, vp, i64, i64, i64, vp, C.POINTER(vp)], i32),
             "myl_linear_backward": ([vp, vp, vp, vp, i64, u8, u8, vp, vp], i32),
@@ -183,6 +184,10 @@ class Context:
     def set_dispatch(self, gemv_max_m: int = 4, force_split_k: int = 0, force_token_tile: int = 0) -> None:
         _check("myl_set_dispatch",
                load_library().myl_set_dispatch(self._h, gemv_max_m, force_split_k, force_token_tile))
+
+    def set_sm_limit(self, max_sms: int) -> None:
+        """Persistent kernels use at most max_sms SMs (0: all)."""
+        _check("myl_set_sm_limit", load_library().myl_set_sm_limit(self._h, max_sms))
 
     def inject_wait_fault(self, on: bool) -> None:
         _check("myl_debug_inject_wait_fault",

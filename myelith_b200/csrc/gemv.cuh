@@ -211,6 +211,143 @@ __global__ void __launch_bounds__(GEMV_THREADS)
   }
 }
 
+// Balanced GEMV for few rows per warp: warp w of W warps finishes the whole
+// row pairs [w*P/W, (w+1)*P/W) (P = ceil(N/2)), so no SM holds more pairs
+// than another by more than one per warp, whatever N is; the weight loads of
+// a pair are software-pipelined one batch ahead of the products. Used where
+// the row-group kernel below would leave SMs with unequal block counts (long K
+// and few rows, e.g. the 7B down projection).
+// Epilogue of a finished row pair (rows 2p, 2p + 1; 2p + 1 may not exist).
+template <int MT>
+__device__ __forceinline__ void gemv_pair_epilogue(const Epilogue& ep, int64_t p, int64_t N,
+                                                   const int64_t (&a)[2][MT]) {
+  if (ep.mode == EPI_W16) {
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+      if (2 * p + 1 < N) w16_store(ep, m, p, a[0][m], a[1][m]);
+  } else if (ep.mode == EPI_SILU) {
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+      if (2 * p + 1 < N) {
+        const int32_t g = int32_t(requant_value(ep, 2 * p, a[0][m]));
+        const int32_t u = int32_t(requant_value(ep, 2 * p + 1, a[1][m]));
+        silu_store(ep, m, p, silu_combine(ep.silu, g, u));
+      }
+  } else {
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      epilogue_store(ep, m, 2 * p, a[0][m]);
+      if (2 * p + 1 < N) epilogue_store(ep, m, 2 * p + 1, a[1][m]);
+    }
+  }
+}
+
+// Exact sums of chunks [c0, c1) of rows w0 and w1 against the staged x,
+// loads software-pipelined one batch of U chunks ahead of the products.
+template <int MT, int U>
+__device__ __forceinline__ void gemv_pair_sums(const int8_t* __restrict__ w0,
+                                               const int8_t* __restrict__ w1,
+                                               const int16_t* __restrict__ xs, int KS, int C, int c0,
+                                               int c1, int lane, int64_t (&a)[2][MT]) {
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+#pragma unroll
+    for (int m = 0; m < MT; ++m) a[j][m] = 0;
+  int4 cur[U][2], nxt[U][2];
+  int c = c0 + lane;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int cc = c + 32 * u;
+    cur[u][0] = cc < c1 ? ldg_stream_v4(w0 + cc * 16) : make_int4(0, 0, 0, 0);
+    cur[u][1] = cc < c1 ? ldg_stream_v4(w1 + cc * 16) : make_int4(0, 0, 0, 0);
+  }
+  for (; c < c1; c += 32 * U) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int cc = c + 32 * (U + u);
+      nxt[u][0] = cc < c1 ? ldg_stream_v4(w0 + cc * 16) : make_int4(0, 0, 0, 0);
+      nxt[u][1] = cc < c1 ? ldg_stream_v4(w1 + cc * 16) : make_int4(0, 0, 0, 0);
+    }
+    int a32[2][MT];
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int m = 0; m < MT; ++m) a32[j][m] = 0;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int cc = c + 32 * u;
+      if (cc < c1) {
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          const int4* xp = reinterpret_cast<const int4*>(xs + m * KS);
+          const int4 xa = xp[cc], xb = xp[C + cc];
+          a32[0][m] = dot16_dp2a(cur[u][0], xa, xb, a32[0][m]);
+          a32[1][m] = dot16_dp2a(cur[u][1], xa, xb, a32[1][m]);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int m = 0; m < MT; ++m) a[j][m] += a32[j][m];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      cur[u][0] = nxt[u][0];
+      cur[u][1] = nxt[u][1];
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      int64_t v = a[j][m];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      a[j][m] = v;
+    }
+}
+
+template <int MT, int U>
+__global__ void __launch_bounds__(GEMV_THREADS, 2)
+    gemv_balanced_kernel(const int8_t* __restrict__ W, int64_t ldw, int64_t N,
+                         const int16_t* __restrict__ X, int64_t ldx, int64_t K, Epilogue ep) {
+  extern __shared__ __align__(16) int16_t xs[];  // [MT][KS], two 16-byte planes per chunk
+  const int KS = int((K + 15) & ~int64_t(15));
+  const int C = KS >> 4;
+  const bool vec_ok = ((reinterpret_cast<uintptr_t>(X) & 15) == 0) && (ldx % 8 == 0);
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+    const int16_t* xr = X + int64_t(m) * ldx;
+    int4* dst = reinterpret_cast<int4*>(xs + m * KS);
+    for (int hh = threadIdx.x; hh < (KS >> 3); hh += GEMV_THREADS) {
+      const int i = hh * 8;
+      int4 v;
+      if (vec_ok && i + 8 <= K) {
+        v = __ldg(reinterpret_cast<const int4*>(xr + i));
+      } else {
+        alignas(16) int16_t t[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) t[e] = (i + e < K) ? xr[i + e] : int16_t(0);
+        v = *reinterpret_cast<const int4*>(t);
+      }
+      dst[(hh & 1) * C + (hh >> 1)] = v;
+    }
+  }
+  __syncthreads();
+
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = int64_t(gridDim.x) * GEMV_WARPS;
+  const int64_t wid = int64_t(blockIdx.x) * GEMV_WARPS + (threadIdx.x >> 5);
+  const int64_t npairs = (N + 1) / 2;
+  const int64_t p_end = (wid + 1) * npairs / nwarps;
+  for (int64_t p = wid * npairs / nwarps; p < p_end; ++p) {
+    const int64_t r1 = (2 * p + 1 < N) ? 2 * p + 1 : 2 * p;  // odd N: duplicate, not stored
+    int64_t a[2][MT];
+    gemv_pair_sums<MT, U>(W + 2 * p * ldw, W + r1 * ldw, xs, KS, C, 0, C, lane, a);
+    if (lane == 0) gemv_pair_epilogue<MT>(ep, p, N, a);
+  }
+}
+
 // xsum[m] = sum_k x[m][k] (int64), one warp per row: the EPI_W16 correction.
 __global__ void x_row_sums_kernel(const int16_t* __restrict__ X, int64_t ldx, int64_t M, int64_t K,
                                   int64_t* __restrict__ xsum) {

@@ -122,6 +122,7 @@ struct myl_ctx {
   int* h_err = nullptr;  // pinned
   uint64_t timeout_ns = 2000000000ull;
   int gemv_max_m = 4, force_split_k = 0, force_tile = 0, inject_fault = 0;
+  int sm_limit = 0;  // persistent grids use at most this many SMs (0: all)
   int64_t launches = 0;
   PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   DevBuf x, y, rq, planes, part, h, hplanes, moe, xsum;
@@ -136,6 +137,12 @@ struct myl_ctx {
   bool ws_used = false;
   std::unordered_map<const int8_t*, myl_weight*> backend_cache;
 };
+
+// SMs the persistent kernels may occupy (myl_set_sm_limit leaves the rest to
+// kernels on other streams, e.g. a collective overlapping the GEMM).
+static int sms(const myl_ctx* ctx) {
+  return ctx->sm_limit > 0 ? std::min(ctx->sm_limit, ctx->num_sms) : ctx->num_sms;
+}
 
 static bool capturing(cudaStream_t st) {
   cudaStreamCaptureStatus s = cudaStreamCaptureStatusNone;
@@ -289,13 +296,53 @@ static constexpr int GEMV_SMEM_BUDGET = 100 * 1024;
 
 static inline int64_t round_up16(int64_t v) { return (v + 15) & ~int64_t(15); }
 
+template <int MT, int U>
+static void* gemv_balanced_ptr() {
+  return reinterpret_cast<void*>(&gemv_balanced_kernel<MT, U>);
+}
+
+// The balanced GEMV (one K slice): grid = resident blocks x SMs, every warp
+// an equal share of whole row pairs.
+static int launch_gemv_balanced(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
+                                int64_t ldx, const Epilogue& ep, cudaStream_t st) {
+  int64_t K = w->K, N = w->N;
+  void* fn = nullptr;
+  switch (M) {
+    case 1: fn = gemv_balanced_ptr<1, 4>(); break;
+    default: fn = gemv_balanced_ptr<2, 4>(); break;
+  }
+  const size_t smem = size_t(M) * size_t(round_up16(K)) * 2;
+  int resident = 0;
+  TRY(kernel_smem_occupancy(ctx->device, fn, GEMV_THREADS, smem, &resident));
+  const unsigned grid = unsigned(std::max(1, resident) * sms(ctx));
+  const int8_t* dW = w->d_W;
+  int64_t ldw = w->ldp;
+  Epilogue e = ep;
+  void* args[] = {(void*)&dW, (void*)&ldw, (void*)&N, (void*)&x, (void*)&ldx, (void*)&K, (void*)&e};
+  CUDA_TRY(cudaLaunchKernel(fn, dim3(grid), dim3(GEMV_THREADS), args, smem, st));
+  ctx->launches++;
+  return MYL_OK;
+}
+
+// The balanced kernel wins where the row-group kernel's blocks would fall
+// unevenly on the SMs: one or two activation rows and at most two row pairs
+// per warp of a full wave (measured on B200: 7B down projection 22.3 -> 18.8 us,
+// the gate/up shape with four pairs per warp stays on the row-group kernel).
+static bool use_balanced_gemv(const myl_ctx* ctx, const myl_weight* w, int64_t M) {
+  if (M > 2 || std::getenv("MYL_GEMV_CLASSIC")) return false;
+  const int64_t npairs = (w->N + 1) / 2, warps = int64_t(sms(ctx)) * 2 * GEMV_WARPS;
+  return npairs <= 2 * warps;
+}
+
 static int launch_gemv(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M, int64_t ldx,
                        const Epilogue& ep_final, cudaStream_t st) {
-  GemvVariant v = gemv_variant(int(M), w->K, w->N, ctx->num_sms);
+  GemvVariant v = gemv_variant(int(M), w->K, w->N, sms(ctx));
   const int64_t K = w->K;
   const int64_t ks_max = (GEMV_SMEM_BUDGET / (2 * M)) & ~int64_t(15);
   int ksplit = int((round_up16(K) + ks_max - 1) / ks_max);
   if (ctx->force_split_k > 0) ksplit = ctx->force_split_k;
+  if (ksplit == 1 && ctx->force_split_k == 0 && use_balanced_gemv(ctx, w, M))
+    return launch_gemv_balanced(ctx, w, x, M, ldx, ep_final, st);
   int64_t k_slice = round_up16((K + ksplit - 1) / ksplit);
   ksplit = int((K + k_slice - 1) / k_slice);
   const size_t smem = size_t(M) * size_t(k_slice) * 2;
@@ -304,7 +351,7 @@ static int launch_gemv(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int6
   const int64_t rows_per_block = int64_t(GEMV_WARPS / v.KW) * v.R;
   const int64_t row_blocks = (w->N + rows_per_block - 1) / rows_per_block;
   // Balanced grid: every block runs the same number of row-group iterations.
-  const int64_t per_slice = std::max<int64_t>(1, int64_t(std::max(resident, 1)) * ctx->num_sms / ksplit);
+  const int64_t per_slice = std::max<int64_t>(1, int64_t(std::max(resident, 1)) * sms(ctx) / ksplit);
   const int64_t iters = (row_blocks + per_slice - 1) / per_slice;
   dim3 grid(unsigned((row_blocks + iters - 1) / iters), unsigned(ksplit));
   Epilogue ep = ep_final;
@@ -351,11 +398,11 @@ static int launch_tc_mode(myl_ctx* ctx, const myl_weight* w, const CUtensorMap& 
                             Cfg::SMEM_BYTES, nullptr));
   // Grouped work is sized on the device (the router's tile table): one CTA per
   // SM, CTAs without a unit exit after setup.
-  const int64_t units = work.groups > 0 ? int64_t(ctx->num_sms)
+  const int64_t units = work.groups > 0 ? int64_t(sms(ctx))
                         : work.tail_tiles > 0
                             ? int64_t(work.full_units) + int64_t(work.tail_tiles) * work.tail_ks
                             : int64_t(work.tiles_n) * work.tiles_m * work.ksplit;
-  const unsigned grid = unsigned(std::min<int64_t>(units, ctx->num_sms));
+  const unsigned grid = unsigned(std::min<int64_t>(units, sms(ctx)));
   const int64_t N = work.groups > 0 ? work.group_w_rows : w->N;  // channels per group
   TcWork wk = work;
   wk.wsum = w->d_wsum;
@@ -425,8 +472,8 @@ static int launch_tc_planes(myl_ctx* ctx, const myl_weight* w, const uint8_t* xh
   int ksplit = 1;
   if (ctx->force_split_k > 0) {
     ksplit = ctx->force_split_k;
-  } else if (tiles < ctx->num_sms && k_tiles >= 8) {
-    ksplit = int(std::min<int64_t>(ctx->num_sms / tiles, k_tiles / 4));
+  } else if (tiles < sms(ctx) && k_tiles >= 8) {
+    ksplit = int(std::min<int64_t>(sms(ctx) / tiles, k_tiles / 4));
   }
   ksplit = std::max(ksplit, int((K + 65535) / 65536));
   ksplit = std::max(1, std::min(ksplit, k_tiles));
@@ -436,7 +483,7 @@ static int launch_tc_planes(myl_ctx* ctx, const myl_weight* w, const uint8_t* xh
   // Tail split: when the tiles fill some waves and leave a small last wave,
   // that wave's tiles run as K slices on all SMs (int64 partials, then
   // tail_reduce_kernel), so the last wave costs a fraction of a full one.
-  const int64_t G = ctx->num_sms;
+  const int64_t G = sms(ctx);
   const int64_t R = tiles % G;
   if (ksplit == 1 && ctx->force_split_k == 0 && tiles >= G && R > 0) {
     const int ks = int(std::min<int64_t>({G / R, int64_t(k_tiles / 4), 16}));
@@ -1253,6 +1300,12 @@ int myl_set_dispatch(myl_ctx* ctx, int gemv_max_m, int force_split_k, int force_
   ctx->gemv_max_m = gemv_max_m;
   ctx->force_split_k = force_split_k;
   ctx->force_tile = force_token_tile;
+  return MYL_OK;
+}
+
+int myl_set_sm_limit(myl_ctx* ctx, int max_sms) {
+  if (!ctx || max_sms < 0) return fail(MYL_ERR_ARG, "bad argument");
+  ctx->sm_limit = max_sms;
   return MYL_OK;
 }
 
