@@ -331,6 +331,9 @@ def main() -> None:
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
+        # the exchanges are tens of MB: NCCL's bandwidth protocol, not the
+        # low-latency one it picks otherwise for these int64 buffers
+        os.environ.setdefault("NCCL_PROTO", "Simple")
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     tp, r = world, rank
     ctx = myl.Context(local)
@@ -346,8 +349,10 @@ def main() -> None:
     n1, k2 = N1 // tp, K2 // tp
     per_set = n1 * K1 + N2 * k2
     nsets = max(2, math.ceil(4 * L2_BYTES / per_set))
-    s1 = rng.integers(kbits(K1) - 1, kbits(K1) + 2, size=N1).astype(np.uint8)[r * n1:(r + 1) * n1]
-    s2 = rng.integers(kbits(K2) - 1, kbits(K2) + 2, size=N2).astype(np.uint8)
+    # per-channel shifts belong to the full weight: the same on every rank
+    srng = np.random.default_rng(999)
+    s1 = srng.integers(kbits(K1) - 1, kbits(K1) + 2, size=N1).astype(np.uint8)[r * n1:(r + 1) * n1]
+    s2 = srng.integers(kbits(K2) - 1, kbits(K2) + 2, size=N2).astype(np.uint8)
     W1s, W2s, R1s, R2s = [], [], [], []
     for _ in range(nsets):
         w1 = ctx.weight(rng.integers(-127, 128, size=(n1, K1), dtype=np.int8), K1, s1)
@@ -403,18 +408,13 @@ def main() -> None:
             dist.all_reduce(acc2, op=dist.ReduceOp.SUM)
             R2s[s].apply_acc_dev(acc2, y2, stream)
 
-    # Tensor-parallel step with the exchange overlapped: the down projection
-    # runs first, in row chunks, and each chunk's int64 partials go to a
-    # reduce-scatter (NCCL, async) while the next chunks and the gate/up
-    # projection compute on SMs the collective leaves free (myl_set_sm_limit);
-    # each rank requantises its share of the rows and an all-gather of the
-    # int16 rows gives every rank the full output, bit-identical to the
-    # all-reduce form above.
-    CH = 4 if tp > 1 and M % (4 * tp) == 0 else 1
-    mc = M // CH
-    if tp > 1:
-        acc_rs = torch.empty((CH, mc // tp, N2), dtype=torch.int64, device=dev)
-        y_own = torch.empty((CH, mc // tp, N2), dtype=torch.int16, device=dev)
+    # Tensor-parallel step with the exchange overlapped: the row-parallel down
+    # projection runs first and its int64 partials go to a reduce-scatter
+    # (NCCL, async) while the column-parallel gate/up projection computes on
+    # the SMs the collective leaves free (myl_set_sm_limit); each rank
+    # requantises its share of the rows and an all-gather of the int16 rows
+    # gives every rank the full output, bit-identical to the all-reduce form.
+    from myelith_b200.tp import overlapped_row_parallel
 
     def step_tp(i: int, record: bool) -> None:
         s = i % nsets
@@ -422,33 +422,36 @@ def main() -> None:
         if record:
             e2 = torch.cuda.Event(enable_timing=True)
             e2.record(stream)
-        works = []
-        for c in range(CH):
-            r = slice(c * mc, (c + 1) * mc)
-            W2s[s].linear_planes_dev(None, p2h[r], p2l[r], mc, acc2[r], stream)
-            works.append(dist.reduce_scatter_tensor(acc_rs[c], acc2[r], op=dist.ReduceOp.SUM,
-                                                    async_op=True))
+
+        def compute_acc(r0, r1, out):  # alone on the GPU: all SMs
+            ctx.set_sm_limit(0)
+            W2s[s].linear_planes_dev(None, p2h[r0:r1], p2l[r0:r1], r1 - r0, out, stream)
+            ctx.set_sm_limit(max(1, ctx.num_sms - args.sm_reserve))
+
+        def requant(acc, y):
+            R2s[s].apply_acc_dev(acc, y, stream)
+
+        ev = {}
+
+        def gate_up():  # column-parallel, no exchange: overlaps the reduce-scatters
+            if record:
+                ev["e3"] = torch.cuda.Event(enable_timing=True)
+                ev["e3"].record(stream)
+            ctx.split_hilo_dev(x1, p1h, p1l, stream)
+            if record:
+                ev["e0"] = torch.cuda.Event(enable_timing=True)
+                ev["e0"].record(stream)
+            W1s[s].linear_planes_dev(R1s[s], p1h, p1l, M, y1, stream)
+            if record:
+                ev["e1"] = torch.cuda.Event(enable_timing=True)
+                ev["e1"].record(stream)
+
+        # one chunk: the down projection at full M keeps its tiles dense; its
+        # reduce-scatter overlaps the gate/up projection instead
+        y2.copy_(overlapped_row_parallel(compute_acc, requant, M, N2, tp, None, 1, dev, gate_up))
         if record:
-            e3 = torch.cuda.Event(enable_timing=True)
-            e3.record(stream)
-        ctx.split_hilo_dev(x1, p1h, p1l, stream)
-        if record:
-            e0 = torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-        W1s[s].linear_planes_dev(R1s[s], p1h, p1l, M, y1, stream)
-        if record:
-            e1 = torch.cuda.Event(enable_timing=True)
-            e1.record(stream)
-            gemm_events.append((e0, e1))
-            gemm_events.append((e2, e3))
-        gathers = []
-        for c in range(CH):
-            works[c].wait()
-            R2s[s].apply_acc_dev(acc_rs[c], y_own[c], stream)
-            gathers.append(dist.all_gather_into_tensor(
-                y2[c * mc:(c + 1) * mc].view(torch.uint8), y_own[c].view(torch.uint8), async_op=True))
-        for g in gathers:
-            g.wait()
+            gemm_events.append((ev["e0"], ev["e1"]))
+            gemm_events.append((e2, ev["e3"]))
 
     tp_check = None
     if tp > 1:
@@ -460,6 +463,10 @@ def main() -> None:
             step_tp(0, False)
             same = torch.tensor([int(torch.equal(ref_y2, y2))], dtype=torch.int32, device=dev)
         stream.synchronize()
+        if not bool(same.item()):
+            bad = (ref_y2 != y2).any(dim=1).nonzero().flatten().tolist()
+            print(f"rank {rank}: overlapped step differs in {len(bad)} rows, first {bad[:8]}",
+                  file=sys.stderr, flush=True)
         dist.all_reduce(same, op=dist.ReduceOp.MIN)
         tp_check = bool(same.item())
         del ref_y2
@@ -477,6 +484,23 @@ def main() -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    if os.environ.get("MYL_BENCH_TRACE") and world > 1:  # one traced step per rank (diagnostics)
+        from torch.profiler import ProfilerActivity, profile
+
+        with torch.cuda.stream(stream):
+            for i in range(3):
+                step(i, False)
+            stream.synchronize()
+            with profile(activities=[ProfilerActivity.CUDA]) as prof:
+                step(3, False)
+                stream.synchronize()
+        evs = sorted([e for e in prof.events() if e.device_type.name == "CUDA"],
+                     key=lambda e: e.time_range.start)
+        t0 = evs[0].time_range.start if evs else 0
+        with open(os.path.join(os.environ["MYL_BENCH_TRACE"], f"trace_rank{rank}.txt"), "w") as f:
+            for e in evs:
+                f.write(f"{(e.time_range.start - t0) / 1e3:9.3f} ms +{(e.time_range.end - e.time_range.start) / 1e3:8.3f}"
+                        f"  {e.name[:90]}\n")
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
             step(i, False)

@@ -169,6 +169,7 @@ class RowParallelLinear:
         N, K = spec.W.shape
         self.lo, self.hi = shard_range(K, rank, world)
         self.local, self.key, self.group, self.world = local, key, group, world
+        self.N = N
         # The column slice keeps every row, so the per-row shifts and the
         # requant plan are those of the full weight.
         local.add_linear(key, np.ascontiguousarray(spec.W[:, self.lo:self.hi]), self.hi - self.lo,
@@ -177,6 +178,21 @@ class RowParallelLinear:
     def x_shard(self, x):
         return x[:, self.lo:self.hi].contiguous()
 
+    def overlapped(self, x_shard, chunks: int = 4):
+        """As __call__, with the exchange overlapped (overlapped_row_parallel)."""
+        M = x_shard.shape[0]
+        if self.world == 1:
+            return self(x_shard)
+
+        def compute_acc(r0, r1, out):
+            out.copy_(self.local.acc(self.key, x_shard[r0:r1]))
+
+        def requant(acc, y):
+            y.copy_(self.local.requant(self.key, acc))
+
+        return overlapped_row_parallel(compute_acc, requant, M, self.N, self.world, self.group,
+                                       chunks, x_shard.device)
+
     def __call__(self, x_shard):
         import torch.distributed as dist
 
@@ -184,6 +200,61 @@ class RowParallelLinear:
         if self.world > 1:
             dist.all_reduce(acc, op=dist.ReduceOp.SUM, group=self.group)
         return self.local.requant(self.key, acc)
+
+
+def overlapped_row_parallel(compute_acc, requant, M: int, N: int, world: int, group=None,
+                            chunks: int = 4, device=None, between=None):
+    """Row-parallel exchange overlapped with the computation of later rows.
+
+    compute_acc(r0, r1, out) writes this rank's exact int64 partial sums of
+    rows [r0, r1) into out [r1 - r0, N]; requant(acc, y) requantises summed
+    rows into int16 y. The rows run in `chunks` groups; each group's partials
+    go to a reduce-scatter (async) while the next group computes, each rank
+    requantises its share of the summed rows, and an all-gather of the int16
+    rows gives every rank the full [M, N] output. Integer sums, one requant
+    after the sum: the result equals the all-reduce form bit for bit.
+    between(), if given, runs after the last reduce-scatter is issued (other
+    work that overlaps the exchange).
+    """
+    import torch
+    import torch.distributed as dist
+
+    if chunks < 1 or M % (chunks * world) != 0:
+        chunks = 1 if M % world == 0 else 0
+    if chunks == 0:  # rows do not split evenly: all-reduce form
+        acc = torch.empty((M, N), dtype=torch.int64, device=device)
+        compute_acc(0, M, acc)
+        work = dist.all_reduce(acc, op=dist.ReduceOp.SUM, group=group, async_op=True)
+        if between is not None:
+            between()
+        work.wait()
+        y = torch.empty((M, N), dtype=torch.int16, device=device)
+        requant(acc, y)
+        return y
+    mc = M // chunks
+    acc = torch.empty((M, N), dtype=torch.int64, device=device)
+    part = torch.empty((chunks, mc // world, N), dtype=torch.int64, device=device)
+    own = torch.empty((chunks, mc // world, N), dtype=torch.int16, device=device)
+    y = torch.empty((M, N), dtype=torch.int16, device=device)
+    works = []
+    for c in range(chunks):
+        r0, r1 = c * mc, (c + 1) * mc
+        compute_acc(r0, r1, acc[r0:r1])
+        works.append(dist.reduce_scatter_tensor(part[c], acc[r0:r1], op=dist.ReduceOp.SUM,
+                                                group=group, async_op=True))
+    if between is not None:
+        between()
+    gathers = []
+    for c in range(chunks):
+        works[c].wait()
+        requant(part[c], own[c])
+        # NCCL and gloo have no int16: the rows move as bytes
+        gathers.append(dist.all_gather_into_tensor(y[c * mc:(c + 1) * mc].view(torch.uint8),
+                                                   own[c].view(torch.uint8), group=group,
+                                                   async_op=True))
+    for g in gathers:
+        g.wait()
+    return y
 
 
 class ParallelMlp:

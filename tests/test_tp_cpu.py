@@ -109,6 +109,11 @@ def _worker(rank, world, port, results):
         y_col = col.gather(xt).numpy()
         row = tp.RowParallelLinear(local, "row", tp.LinearSpec(W, ws, 6, of), rank, world)
         y_row = row(row.x_shard(xt)).numpy()
+        # the overlapped exchange (reduce-scatter, requant, all-gather) in row chunks
+        x8 = torch.from_numpy(np.concatenate([x, x[::-1], x, x[::-1]])[: 4 * world * 2])
+        y_ov = row.overlapped(row.x_shard(x8), chunks=2).numpy()
+        ref_ov = O.linear_w8a16_pc(x8.numpy(), W.reshape(-1), K, ws, 6, of)
+        ov_ok = bool(np.array_equal(y_ov, ref_ov))
         pm = tp.ParallelMlp(local, "mlp", **{k: v for k, v in mlp.items() if k not in ("hidden", "intermediate")},
                             hidden=mlp["hidden"], intermediate=mlp["intermediate"], rank=rank, world=world)
         y_mlp = pm(torch.from_numpy(xm)).numpy()
@@ -118,7 +123,7 @@ def _worker(rank, world, port, results):
                             mlp["down_w_shifts"], mlp["silu_lut"], mlp["in_frac"], mlp["gate_out_frac"],
                             mlp["up_out_frac"], mlp["down_in_frac"], mlp["silu_in_frac"],
                             mlp["silu_lut_offset"], mlp["silu_out_frac"], mlp["out_frac"])
-        results[rank] = (bool(np.array_equal(y_col, ref)), bool(np.array_equal(y_row, ref)),
+        results[rank] = (bool(np.array_equal(y_col, ref)), bool(np.array_equal(y_row, ref) and ov_ok),
                          bool(np.array_equal(y_mlp, ref_mlp)), (col.lo, col.hi), (row.lo, row.hi))
     finally:
         dist.destroy_process_group()

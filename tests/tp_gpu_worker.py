@@ -67,6 +67,7 @@ def main():
         for Ms in (2, M):  # decode (GEMV) and prefill (tensor cores)
             y_col = col.gather(xt[:Ms]).cpu().numpy()
             y_row = row(row.x_shard(xt[:Ms])).cpu().numpy()
+            y_ov = row.overlapped(row.x_shard(xt[:Ms]), chunks=4).cpu().numpy()
             y_mlp = pm(xmt[:Ms]).cpu().numpy()
             single = ctx.weight(W, K, ws).linear(x[:Ms], 8, of)
             single_mlp = myl.Mlp(ctx, mlp["W_gate"], mlp["W_up"], mlp["W_down"], H, I,
@@ -74,6 +75,7 @@ def main():
                                  mlp["silu_lut"], 8, 7, 7, 7, 6, 8192, 8, mlp["out_frac"])(xm[:Ms])
             ref = O.linear_w8a16_pc(x[:Ms], W.reshape(-1), K, ws, 8, of)
             ok = dict(col=bool(np.array_equal(y_col, single)), row=bool(np.array_equal(y_row, single)),
+                      overlapped=bool(np.array_equal(y_ov, single)),
                       mlp=bool(np.array_equal(y_mlp, single_mlp)), oracle=bool(np.array_equal(single, ref)))
             # every rank holds the same bytes
             h = torch.tensor([int(np.frombuffer(y_mlp.tobytes(), np.uint8).astype(np.int64).sum()),
