@@ -28,6 +28,7 @@
 #ifndef MYL_W8A16_H
 #define MYL_W8A16_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -44,6 +45,8 @@ enum myl_status {
   MYL_ERR_ARG = 4,         /* null pointer, bad handle or bad enum */
   MYL_ERR_DEVICE = 5,      /* a kernel reported an error (e.g. a bounded wait ran out) */
   MYL_ERR_UNSUPPORTED = 6, /* device is not sm_100 or a size is beyond a kernel limit */
+  MYL_ERR_IO = 7,          /* an artifact file is missing, unreadable or not valid JSON */
+  MYL_ERR_CORRUPT = 8,     /* an artifact file disagrees with its manifest (size, hash, dtype) */
 };
 
 /* Requant modes (myl_requant_create). */
@@ -307,6 +310,29 @@ int64_t myl_launch_count(const myl_ctx* ctx);
  * error code, frees its resources and returns, and the next host-synchronising
  * call reports MYL_ERR_DEVICE. The context stays usable. */
 int myl_debug_inject_wait_fault(myl_ctx* ctx, int on);
+
+/* --- θ_v artifacts (runtime/src/loader.rs:322-560) --------------------------------
+ * myl_artifact_open reads weights_manifest.json and, if present, luts.json of
+ * an artifact directory into host memory, rejecting it as the reference
+ * does: unsupported dtype, int16 outside the LM head and *_bias, a file whose
+ * size disagrees with its shape, a SHA-256 that disagrees with the manifest,
+ * a shifts file with the wrong length or hash, a uniform shift outside
+ * 0..=255. No device is needed. myl_artifact_register uploads one 2-D tensor
+ * as a weight (int16: the LM head's path A, myl_weight16_register). Names are
+ * found by manifest key or original name ('.' read as '_', loader.rs:167-170).
+ * dtype: 1 = int8, 2 = int16 (little-endian); shape has up to 4 entries. */
+typedef struct myl_artifact myl_artifact;
+int myl_artifact_open(const char* dir, myl_artifact** out);
+int myl_artifact_close(myl_artifact* a);
+int64_t myl_artifact_count(const myl_artifact* a);
+int myl_artifact_find(const myl_artifact* a, const char* name, int64_t* index);
+int myl_artifact_tensor(const myl_artifact* a, int64_t index, const char** key,
+                        const char** original_name, int* dtype, int* ndim, int64_t* shape,
+                        const void** data, const uint8_t** shifts);
+int myl_artifact_register(myl_ctx* ctx, const myl_artifact* a, int64_t index, myl_weight** out);
+int myl_artifact_lut(const myl_artifact* a, const char* name, const int16_t** data, int64_t* len);
+/* SHA-256 (FIPS 180-4) as the loader checks it (sha2 0.10 in the reference). */
+int myl_sha256(const void* data, size_t len, uint8_t* out);
 
 /* --- Allocation-free variant ------------------------------------------------------
  * No counterpart in the reference: its CPU path never allocates device memory.

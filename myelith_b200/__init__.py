@@ -42,12 +42,15 @@ MYL_ERR_CUDA = 3
 MYL_ERR_ARG = 4
 MYL_ERR_DEVICE = 5
 MYL_ERR_UNSUPPORTED = 6
+MYL_ERR_IO = 7
+MYL_ERR_CORRUPT = 8
 
 RQ_SHIFT_I16 = 0
 RQ_SHIFT_I32 = 1
 RQ_MULT_I16 = 2
 
-_STATUS = {1: "shape", 2: "overflow", 3: "cuda", 4: "argument", 5: "device", 6: "unsupported"}
+_STATUS = {1: "shape", 2: "overflow", 3: "cuda", 4: "argument", 5: "device", 6: "unsupported",
+           7: "io", 8: "corrupt"}
 
 
 class MylError(RuntimeError):
@@ -112,6 +115,16 @@ def load_library(path: str | None = None):
             "myl_linear_backward": ([vp, vp, vp, vp, i64, u8, u8, vp, vp], i32),
             "myl_linear_backward_dev": ([vp, vp, vp, i64, vp, i64, i64, u8, u8, vp, i64, vp, vp], i32),
             "myl_lm_head_w16a16_i32": ([vp, vp, vp, i64, u8, u8, vp], i32),
+            "myl_sha256": ([vp, C.c_size_t, vp], i32),
+            "myl_artifact_open": ([C.c_char_p, C.POINTER(vp)], i32),
+            "myl_artifact_close": ([vp], i32),
+            "myl_artifact_count": ([vp], i64),
+            "myl_artifact_find": ([vp, C.c_char_p, C.POINTER(i64)], i32),
+            "myl_artifact_tensor": ([vp, i64, C.POINTER(C.c_char_p), C.POINTER(C.c_char_p),
+                                     C.POINTER(i32), C.POINTER(i32), C.POINTER(i64), C.POINTER(vp),
+                                     C.POINTER(vp)], i32),
+            "myl_artifact_register": ([vp, vp, i64, C.POINTER(vp)], i32),
+            "myl_artifact_lut": ([vp, C.c_char_p, C.POINTER(vp), C.POINTER(i64)], i32),
             "myl_moe_register": ([vp, C.POINTER(MoeSpec), C.POINTER(vp)], i32),
             "myl_moe_release": ([vp, vp], i32),
             "myl_moe_forward": ([vp, vp, vp, i64, vp], i32),
@@ -602,6 +615,83 @@ class Moe:
             self.ctx.handle, self._h, _p(y), y.stride(0), _p(topk_prob), _p(shared_out),
             shared_out.stride(0) if shared_out is not None else 0, out.shape[0], _p(out),
             out.stride(0), _stream_ptr(stream)))
+
+
+def sha256(data: bytes) -> bytes:
+    """SHA-256 (FIPS 180-4), the digest the artifact loader checks."""
+    out = (C.c_uint8 * 32)()
+    buf = C.create_string_buffer(bytes(data), len(data))
+    _check("myl_sha256", load_library().myl_sha256(C.cast(buf, C.c_void_p), len(data), out))
+    return bytes(out)
+
+
+class Artifact:
+    """A θ_v artifact directory (runtime/src/loader.rs:322-560): weights and
+    LUT manifests read and verified on the host; 2-D tensors register as
+    weights on a context."""
+
+    def __init__(self, path: str):
+        h = C.c_void_p()
+        _check("myl_artifact_open", load_library().myl_artifact_open(str(path).encode(), C.byref(h)))
+        self._h = h
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            load_library().myl_artifact_close(self._h)
+        self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __len__(self) -> int:
+        return int(load_library().myl_artifact_count(self._h))
+
+    def index(self, name: str) -> int:
+        i = C.c_int64()
+        _check("myl_artifact_find", load_library().myl_artifact_find(self._h, name.encode(), C.byref(i)))
+        return i.value
+
+    def tensor(self, name_or_index):
+        """(key, original_name, data ndarray int8/int16 of the manifest shape, shifts uint8)."""
+        i = name_or_index if isinstance(name_or_index, int) else self.index(name_or_index)
+        key, orig = C.c_char_p(), C.c_char_p()
+        dtype, ndim = C.c_int(), C.c_int()
+        shape = (C.c_int64 * 4)()
+        data, shifts = C.c_void_p(), C.c_void_p()
+        _check("myl_artifact_tensor", load_library().myl_artifact_tensor(
+            self._h, i, C.byref(key), C.byref(orig), C.byref(dtype), C.byref(ndim), shape,
+            C.byref(data), C.byref(shifts)))
+        shp = tuple(shape[j] for j in range(ndim.value))
+        n = int(np.prod(shp)) if shp else 0
+        ctype = C.c_int8 if dtype.value == 1 else C.c_int16
+        arr = np.ctypeslib.as_array((ctype * max(n, 1)).from_address(data.value or 0))[:n] if n else \
+            np.zeros(0, np.int8 if dtype.value == 1 else np.int16)
+        rows = shp[0] if shp else 0
+        sh = np.ctypeslib.as_array((C.c_uint8 * max(rows, 1)).from_address(shifts.value))[:rows] \
+            if rows and shifts.value else np.zeros(0, np.uint8)
+        return key.value.decode(), orig.value.decode(), arr.reshape(shp).copy(), sh.copy()
+
+    def register(self, ctx: "Context", name_or_index) -> "Weight":
+        """The tensor as a device weight (int16: LM head path A)."""
+        i = name_or_index if isinstance(name_or_index, int) else self.index(name_or_index)
+        _, _, arr, sh = self.tensor(i)
+        h = C.c_void_p()
+        _check("myl_artifact_register", load_library().myl_artifact_register(
+            ctx.handle, self._h, i, C.byref(h)))
+        w = Weight16.__new__(Weight16) if arr.dtype == np.int16 else Weight.__new__(Weight)
+        w.ctx, w._h, w.out_features, w.in_features, w.w_shifts = ctx, h, arr.shape[0], arr.shape[1], sh
+        return w
+
+    def lut(self, name: str) -> np.ndarray:
+        data, n = C.c_void_p(), C.c_int64()
+        _check("myl_artifact_lut", load_library().myl_artifact_lut(self._h, name.encode(), C.byref(data),
+                                                                     C.byref(n)))
+        if n.value == 0:
+            return np.zeros(0, np.int16)
+        return np.ctypeslib.as_array((C.c_int16 * n.value).from_address(data.value)).copy()
 
 
 def _stream_ptr(stream) -> int | None:

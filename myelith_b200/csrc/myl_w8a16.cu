@@ -1932,3 +1932,217 @@ int myl_linear_backward(myl_ctx* ctx, const myl_weight* w, const int32_t* g, con
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------
+// θ_v artifacts (runtime/src/loader.rs:322-560)
+
+#include "artifact.hpp"
+
+namespace {
+
+using namespace myl_artifact_detail;
+
+int load_weights_manifest(const std::string& dir, myl_artifact* a) {
+  std::vector<uint8_t> raw;
+  if (!read_file(dir + "/weights_manifest.json", raw))
+    return fail(MYL_ERR_IO, "cannot read %s/weights_manifest.json", dir.c_str());
+  const std::string text(raw.begin(), raw.end());
+  Json root;
+  JsonParser parser(text);
+  if (!parser.parse(root) || root.kind != Json::OBJ)
+    return fail(MYL_ERR_IO, "invalid weights_manifest.json: %s",
+                parser.err.empty() ? "not an object" : parser.err.c_str());
+  for (const auto& kv : root.obj) {
+    const std::string& name = kv.first;
+    const Json& e = kv.second;
+    const Json *file = e.get("file"), *shape = e.get("shape"), *dtype = e.get("dtype"),
+               *hash = e.get("hash"), *orig = e.get("original_name");
+    if (e.kind != Json::OBJ || !file || file->kind != Json::STR || !shape || shape->kind != Json::ARR ||
+        !dtype || dtype->kind != Json::STR || !hash || hash->kind != Json::STR)
+      return fail(MYL_ERR_IO, "%s: manifest entry lacks file/shape/dtype/hash", name.c_str());
+    ArtifactTensor t;
+    t.key = name;
+    t.original_name = (orig && orig->kind == Json::STR) ? orig->str : name;
+    t.file = file->str;
+    for (const Json& d : shape->arr) {
+      int64_t v = 0;
+      if (!as_int(&d, v) || v < 0) return fail(MYL_ERR_IO, "%s: bad shape", name.c_str());
+      t.shape.push_back(v);
+    }
+    int64_t numel = 1;
+    for (int64_t v : t.shape) numel *= v;
+    const Json* sf = e.get("shifts_file");
+    const Json* sh = e.get("shifts_hash");
+    if (dtype->str == "int16") {
+      // int16 only for the LM head and the attention biases (loader.rs:335-350).
+      const bool bias = name.size() >= 5 && name.compare(name.size() - 5, 5, "_bias") == 0;
+      if (name != "lm_head" && !bias)
+        return fail(MYL_ERR_CORRUPT, "%s: int16 is allowed for the LM head and attention biases only",
+                    name.c_str());
+      if (!sf || sf->kind != Json::STR)
+        return fail(MYL_ERR_CORRUPT, "%s: int16 entry without shifts_file", name.c_str());
+      if ((!bias && t.shape.size() != 2) || (bias && t.shape.size() != 1))
+        return fail(MYL_ERR_CORRUPT, "%s: %s expects a %s shape", name.c_str(),
+                    bias ? "bias" : "LM head", bias ? "one-dimensional" : "[vocab, hidden]");
+      t.dtype = 2;
+    } else if (dtype->str == "int8") {
+      if (t.shape.empty()) return fail(MYL_ERR_CORRUPT, "%s: empty shape in the manifest", name.c_str());
+      t.dtype = 1;
+    } else {
+      return fail(MYL_ERR_CORRUPT, "%s: unsupported dtype '%s' (int8 or int16)", name.c_str(),
+                  dtype->str.c_str());
+    }
+    if (!read_file(dir + "/" + t.file, t.bytes))
+      return fail(MYL_ERR_IO, "cannot read %s", t.file.c_str());
+    const int64_t want = numel * t.dtype;
+    if (int64_t(t.bytes.size()) != want)
+      return fail(MYL_ERR_CORRUPT, "%s: %zu bytes in '%s', shape expects %lld bytes", name.c_str(),
+                  t.bytes.size(), t.file.c_str(), (long long)want);
+    const std::string digest = sha256_hex(t.bytes);
+    if (digest != hash->str)
+      return fail(MYL_ERR_CORRUPT, "%s: SHA-256 %s does not match the manifest hash %s", name.c_str(),
+                  digest.c_str(), hash->str.c_str());
+    const int64_t rows = t.shape[0];
+    if (sf && sf->kind == Json::STR) {
+      if (!read_file(dir + "/" + sf->str, t.shifts))
+        return fail(MYL_ERR_IO, "cannot read %s", sf->str.c_str());
+      if (int64_t(t.shifts.size()) != rows)
+        return fail(MYL_ERR_CORRUPT, "%s: %zu shifts in '%s', %lld rows expected", name.c_str(),
+                    t.shifts.size(), sf->str.c_str(), (long long)rows);
+      if (sh && sh->kind == Json::STR && sha256_hex(t.shifts) != sh->str)
+        return fail(MYL_ERR_CORRUPT, "%s: SHA-256 of the shifts file does not match the manifest",
+                    name.c_str());
+    } else {
+      // Older artifacts: one uniform shift for every row (loader.rs:452-462).
+      int64_t shift = 0;
+      if (!as_int(e.get("shift"), shift) || shift < 0 || shift > 255)
+        return fail(MYL_ERR_CORRUPT, "%s: shift outside 0..=255 and no shifts_file", name.c_str());
+      t.shifts.assign(size_t(rows), uint8_t(shift));
+    }
+    a->tensors.push_back(std::move(t));
+  }
+  return MYL_OK;
+}
+
+int load_luts_manifest(const std::string& dir, myl_artifact* a) {
+  std::vector<uint8_t> raw;
+  if (!read_file(dir + "/luts.json", raw)) return MYL_OK;  // an artifact without tables
+  const std::string text(raw.begin(), raw.end());
+  Json root;
+  JsonParser parser(text);
+  if (!parser.parse(root) || root.kind != Json::OBJ)
+    return fail(MYL_ERR_IO, "invalid luts.json: %s", parser.err.empty() ? "not an object" : parser.err.c_str());
+  for (const auto& kv : root.obj) {
+    const std::string& name = kv.first;
+    const Json& e = kv.second;
+    const Json *file = e.get("file"), *dtype = e.get("dtype"), *hash = e.get("hash");
+    int64_t length = 0;
+    if (e.kind != Json::OBJ || !file || file->kind != Json::STR || !dtype || dtype->kind != Json::STR ||
+        !hash || hash->kind != Json::STR || !as_int(e.get("length"), length) || length < 0)
+      return fail(MYL_ERR_IO, "%s: luts.json entry lacks file/hash/length/dtype", name.c_str());
+    if (dtype->str != "int16")
+      return fail(MYL_ERR_CORRUPT, "%s: unsupported dtype '%s' (int16 expected)", name.c_str(),
+                  dtype->str.c_str());
+    std::vector<uint8_t> bytes;
+    if (!read_file(dir + "/" + file->str, bytes)) return fail(MYL_ERR_IO, "cannot read %s", file->str.c_str());
+    if (int64_t(bytes.size()) != 2 * length)
+      return fail(MYL_ERR_CORRUPT, "%s: %zu bytes in '%s', length %lld expects %lld bytes", name.c_str(),
+                  bytes.size(), file->str.c_str(), (long long)length, (long long)(2 * length));
+    if (sha256_hex(bytes) != hash->str)
+      return fail(MYL_ERR_CORRUPT, "%s: SHA-256 does not match the manifest hash", name.c_str());
+    std::vector<int16_t> table(static_cast<size_t>(length));
+    for (int64_t i = 0; i < length; ++i)
+      table[size_t(i)] = int16_t(uint16_t(bytes[size_t(2 * i)]) | (uint16_t(bytes[size_t(2 * i + 1)]) << 8));
+    a->luts[name] = std::move(table);
+  }
+  return MYL_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int myl_sha256(const void* data, size_t len, uint8_t* out) {
+  if ((!data && len) || !out) return fail(MYL_ERR_ARG, "null argument");
+  sha256(static_cast<const uint8_t*>(data), len, out);
+  return MYL_OK;
+}
+
+int myl_artifact_open(const char* dir, myl_artifact** out) {
+  if (!dir || !out) return fail(MYL_ERR_ARG, "null argument");
+  *out = nullptr;
+  myl_artifact* a = new myl_artifact();
+  int rc = load_weights_manifest(dir, a);
+  if (rc == MYL_OK) rc = load_luts_manifest(dir, a);
+  if (rc != MYL_OK) {
+    delete a;
+    return rc;
+  }
+  *out = a;
+  return MYL_OK;
+}
+
+int myl_artifact_close(myl_artifact* a) {
+  delete a;
+  return MYL_OK;
+}
+
+int64_t myl_artifact_count(const myl_artifact* a) { return a ? int64_t(a->tensors.size()) : -1; }
+
+int myl_artifact_find(const myl_artifact* a, const char* name, int64_t* index) {
+  if (!a || !name || !index) return fail(MYL_ERR_ARG, "null argument");
+  // Manifest keys are original names with '.' replaced by '_' (loader.rs:167-170).
+  std::string key(name);
+  for (char& c : key)
+    if (c == '.') c = '_';
+  for (size_t i = 0; i < a->tensors.size(); ++i)
+    if (a->tensors[i].key == name || a->tensors[i].key == key || a->tensors[i].original_name == name) {
+      *index = int64_t(i);
+      return MYL_OK;
+    }
+  return fail(MYL_ERR_ARG, "no tensor '%s' in the artifact", name);
+}
+
+int myl_artifact_tensor(const myl_artifact* a, int64_t index, const char** key,
+                        const char** original_name, int* dtype, int* ndim, int64_t* shape,
+                        const void** data, const uint8_t** shifts) {
+  if (!a || index < 0 || index >= int64_t(a->tensors.size())) return fail(MYL_ERR_ARG, "bad tensor index");
+  const ArtifactTensor& t = a->tensors[size_t(index)];
+  if (key) *key = t.key.c_str();
+  if (original_name) *original_name = t.original_name.c_str();
+  if (dtype) *dtype = t.dtype;
+  if (ndim) *ndim = int(t.shape.size());
+  if (shape)
+    for (size_t i = 0; i < t.shape.size() && i < 4; ++i) shape[i] = t.shape[i];
+  if (data) *data = t.bytes.data();
+  if (shifts) *shifts = t.shifts.data();
+  return MYL_OK;
+}
+
+int myl_artifact_register(myl_ctx* ctx, const myl_artifact* a, int64_t index, myl_weight** out) {
+  if (!ctx || !a || !out || index < 0 || index >= int64_t(a->tensors.size()))
+    return fail(MYL_ERR_ARG, "bad argument");
+  const ArtifactTensor& t = a->tensors[size_t(index)];
+  if (t.shape.size() != 2)
+    return fail(MYL_ERR_SHAPE, "%s: only 2-D tensors are registered as weights", t.key.c_str());
+  const int64_t N = t.shape[0], K = t.shape[1];
+  if (t.dtype == 2) {
+    std::vector<int16_t> w(static_cast<size_t>(N * K));
+    for (size_t i = 0; i < w.size(); ++i)
+      w[i] = int16_t(uint16_t(t.bytes[2 * i]) | (uint16_t(t.bytes[2 * i + 1]) << 8));
+    return myl_weight16_register(ctx, w.data(), N, K, K, t.shifts.data(), out);
+  }
+  return myl_weight_register(ctx, reinterpret_cast<const int8_t*>(t.bytes.data()), N, K, K,
+                             t.shifts.data(), out);
+}
+
+int myl_artifact_lut(const myl_artifact* a, const char* name, const int16_t** data, int64_t* len) {
+  if (!a || !name || !data || !len) return fail(MYL_ERR_ARG, "null argument");
+  auto it = a->luts.find(name);
+  if (it == a->luts.end()) return fail(MYL_ERR_ARG, "no table '%s' in luts.json", name);
+  *data = it->second.data();
+  *len = int64_t(it->second.size());
+  return MYL_OK;
+}
+
+}  // extern "C"
