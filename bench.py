@@ -84,8 +84,12 @@ def load_traffic() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+    """SM clocks, power and clock-event reasons sampled DURING the timed region.
 
+    NVML is polled from a thread every ~2 ms (a timed region of a few ms still
+    gets samples); without NVML, nvidia-smi every 200 ms."""
+
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -95,8 +99,41 @@ class ClockSampler:
         self.proc = None
         self.lines: list[str] = []
         self.thread = None
+        self.nvml = None
+        self.handle = None
+        self.stop_flag = threading.Event()
+        self.sm: list[float] = []
+        self.power: list[float] = []
+        self.reasons: set[str] = set()
+        self.sm_max = None
+
+    def _nvml_handle(self):
+        import pynvml
+
+        pynvml.nvmlInit()
+        self.nvml = pynvml
+        try:  # the CUDA device's UUID names the same GPU under any CUDA_VISIBLE_DEVICES
+            uuid = str(torch.cuda.get_device_properties(self.gpu).uuid)
+            return pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:
+            return pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
 
     def start(self):
+        try:
+            self.handle = self._nvml_handle()
+            n = self.nvml
+            self.sm_max = float(n.nvmlDeviceGetMaxClockInfo(self.handle, n.NVML_CLOCK_SM))
+            self.masks = {
+                "hw_slowdown": n.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": n.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": n.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": n.nvmlClocksEventReasonSwPowerCap,
+            }
+            self.thread = threading.Thread(target=self._poll_nvml, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.handle = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -108,11 +145,39 @@ class ClockSampler:
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
 
+    def _poll_nvml(self):
+        n, h = self.nvml, self.handle
+        i = 0
+        while not self.stop_flag.is_set():
+            try:
+                self.sm.append(float(n.nvmlDeviceGetClockInfo(h, n.NVML_CLOCK_SM)))
+                bits = n.nvmlDeviceGetCurrentClocksEventReasons(h)
+                for name, mask in self.masks.items():
+                    if bits & mask:
+                        self.reasons.add(name)
+                if i % 10 == 0:
+                    self.power.append(n.nvmlDeviceGetPowerUsage(h) / 1000.0)
+            except Exception:
+                pass
+            i += 1
+            self.stop_flag.wait(0.002)
+
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def stop(self) -> dict:
+        if self.handle is not None:
+            self.stop_flag.set()
+            self.thread.join(timeout=2)
+            try:
+                self.nvml.nvmlShutdown()
+            except Exception:
+                pass
+            return {"sm_mhz": statistics.median(self.sm) if self.sm else None,
+                    "sm_max_mhz": self.sm_max, "reasons": sorted(self.reasons),
+                    "samples": len(self.sm), "power_w_max": max(self.power) if self.power else None,
+                    "source": "nvml, every ~2 ms during the timed region"}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -123,7 +188,6 @@ class ClockSampler:
         if self.thread:
             self.thread.join(timeout=2)
         sm, smax, reasons, power = [], None, set(), []
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
@@ -134,12 +198,13 @@ class ClockSampler:
                 power.append(float(parts[3]))
             except ValueError:
                 continue
-            for n, v in zip(names, parts[5:9]):
+            for name, v in zip(self.NAMES, parts[5:9]):
                 if v.lower().startswith("active"):
-                    reasons.add(n)
+                    reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
                 "reasons": sorted(reasons), "samples": len(sm),
-                "power_w_max": max(power) if power else None}
+                "power_w_max": max(power) if power else None,
+                "source": "nvidia-smi every 200 ms"}
 
 
 # ---------------------------------------------------------------------------------------
@@ -509,7 +574,8 @@ def main() -> None:
         torch.cuda.synchronize()
         sampler = ClockSampler(local)
         sampler.start()
-        time.sleep(0.3)
+        if sampler.handle is None:
+            time.sleep(0.3)  # nvidia-smi needs a moment to start
         launches0 = ctx.launch_count
         t_start = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)

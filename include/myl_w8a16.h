@@ -301,6 +301,12 @@ int myl_set_dispatch(myl_ctx* ctx, int gemv_max_m, int force_split_k, int force_
  * overlaps the GEMM) find free SMs; 0 = all SMs (the default). */
 int myl_set_sm_limit(myl_ctx* ctx, int max_sms);
 
+/* Tensor-core GEMM variant, for tests and tuning: pair_mode = 1 (default) runs
+ * 128-token tiles on CTA pairs (one M = 256 MMA over two SMs, each SM loading
+ * one activation byte plane), 0 one CTA per 128-channel tile; xbox_rows (16,
+ * 32, 64 or 128; 0 = unchanged) is the row count of the activation TMA boxes. */
+int myl_set_tc_options(myl_ctx* ctx, int pair_mode, int xbox_rows);
+
 /* Number of this library's kernels launched on the context since init. */
 int64_t myl_launch_count(const myl_ctx* ctx);
 

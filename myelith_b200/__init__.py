@@ -110,6 +110,7 @@ def load_library(path: str | None = None):
             "myl_set_dispatch": ([vp, i32, i32, i32], i32),
             "myl_launch_count": ([vp], i64),
             "myl_set_sm_limit": ([vp, i32], i32),
+            "myl_set_tc_options": ([vp, i32, i32], i32),
             "myl_debug_inject_wait_fault": ([vp, i32], i32),
             "myl_weight16_register": ([vp, vp, i64, i64, i64, vp, C.POINTER(vp)], i32),
             "myl_linear_backward": ([vp, vp, vp, vp, i64, u8, u8, vp, vp], i32),
@@ -201,6 +202,12 @@ class Context:
     def set_sm_limit(self, max_sms: int) -> None:
         """Persistent kernels use at most max_sms SMs (0: all)."""
         _check("myl_set_sm_limit", load_library().myl_set_sm_limit(self._h, max_sms))
+
+    def set_tc_options(self, pair: bool = True, xbox_rows: int = 0) -> None:
+        """Tensor-core GEMM variant: CTA pairs for 128-token tiles (default) or
+        one CTA per tile; activation TMA box height (0 = unchanged)."""
+        _check("myl_set_tc_options",
+               load_library().myl_set_tc_options(self._h, 1 if pair else 0, xbox_rows))
 
     def inject_wait_fault(self, on: bool) -> None:
         _check("myl_debug_inject_wait_fault",

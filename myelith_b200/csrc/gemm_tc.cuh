@@ -52,14 +52,19 @@
 namespace myl {
 
 constexpr int TC_BK = 128;  // K bytes per stage = one 128-byte swizzle row
+constexpr int TC_XBOX = 128;  // default activation rows per TMA box (x tensor maps)
 constexpr int TC_EPI_WARPS = 16;  // four per TMEM lane quarter, each owning a quarter of the columns
 constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;
 
-template <int BN, int STAGES>
+// PAIR: a cluster of two CTAs runs one MMA of M = 256 (cta_group::2); the even
+// CTA holds weight rows 0..127 and the x_hi tile, the odd CTA rows 128..255 and
+// the x_lo tile, so each SM loads one activation plane instead of two.
+template <int BN, int STAGES, bool PAIR = false>
 struct TcCfg {
   static constexpr int W_BYTES = 128 * TC_BK;
   static constexpr int X_BYTES = BN * TC_BK;
-  static constexpr int STAGE_BYTES = W_BYTES + 2 * X_BYTES;
+  static constexpr int STAGE_BYTES = W_BYTES + (PAIR ? 1 : 2) * X_BYTES;
+  static constexpr int CT = PAIR ? 256 : 128;  // weight rows (channels) per work unit
   static constexpr int BUF_COLS = 2 * BN;  // H | L of one accumulator buffer
   static constexpr int TMEM_COLS = 2 * BUF_COLS <= 32 ? 32 : 2 * BUF_COLS;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack
@@ -67,7 +72,8 @@ struct TcCfg {
   static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM allocation");
   static_assert(STAGES >= 2 && STAGES <= 16, "stage ring");
   static_assert(SMEM_BYTES <= 227 * 1024 - 512, "shared memory");
-  static constexpr uint32_t IDESC = idesc_i8(128, 2 * BN, true, false);  // W s8 x [x_hi | x_lo] u8
+  // W s8 x [x_hi | x_lo] u8
+  static constexpr uint32_t IDESC = idesc_i8(PAIR ? 256 : 128, 2 * BN, true, false);
 };
 
 struct TcCtl {
@@ -80,7 +86,8 @@ struct TcCtl {
   int abort;
 };
 
-// One work unit: a 128-channel x BN-token output tile over one K slice.
+// One work unit: a 128-channel (256 for a CTA pair) x BN-token output tile
+// over one K slice.
 struct TcUnit {
   int nt, ks, kt0, nkt;
   int tail_slot;     // >= 0: a K slice of a tail tile, stored as int64 partials
@@ -111,17 +118,21 @@ struct TcWork {
   int64_t wsum_ld;
   // Dense tail split (ksplit == 1): tiles [full_units, full_units + tail_tiles)
   // are the last, incomplete wave; each runs as tail_ks K slices of tail_per K
-  // tiles whose int64 partials go to tail_ws[slot][BN][128] (slot = slice *
-  // tail_tiles + tile) and are added by tail_reduce_kernel, so the final wave
-  // is short instead of mostly idle.
+  // tiles whose int64 partials go to tail_ws[slot][ct / 128][BN][128] (slot =
+  // slice * tail_tiles + tile; the middle index is the CTA of a pair) and are
+  // added by tail_reduce_kernel, so the final wave is short instead of mostly
+  // idle.
   int full_units, tail_tiles, tail_ks, tail_per;
   int64_t* tail_ws;
+  // Rows per activation TMA box (the x tensor maps' box height; divides BN).
+  int xbox;
   __device__ __forceinline__ int units() const {
     if (groups > 0) return tile_start[groups];
     if (tail_tiles > 0) return full_units + tail_tiles * tail_ks;
     return tiles_n * tiles_m * ksplit;
   }
-  __device__ __forceinline__ TcUnit decode(int u, int BN, int64_t M) const {
+  // ct: weight rows per unit (128, or 256 for a CTA pair).
+  __device__ __forceinline__ TcUnit decode(int u, int BN, int64_t M, int ct) const {
     TcUnit w;
     w.tail_slot = -1;
     if (groups == 0 && tail_tiles > 0 && u >= full_units) {
@@ -134,7 +145,7 @@ struct TcWork {
       w.nkt = min(tail_per, k_tiles_total - w.kt0);
       w.m_begin = int64_t(t / tiles_n) * BN;
       w.m_end = M;
-      w.w_row = int64_t(w.nt) * 128;
+      w.w_row = int64_t(w.nt) * ct;
       w.p_off = 0;
       w.tail_slot = slice * tail_tiles + tl;
       return w;
@@ -148,7 +159,7 @@ struct TcWork {
       w.nkt = min(k_tiles_per_split, k_tiles_total - w.kt0);
       w.m_begin = int64_t(mt) * BN;
       w.m_end = M;
-      w.w_row = int64_t(w.nt) * 128;
+      w.w_row = int64_t(w.nt) * ct;
       w.p_off = 0;
       return w;
     }
@@ -166,7 +177,7 @@ struct TcWork {
     w.m_begin = int64_t(row_start[lo]) + int64_t(local / tiles_n) * BN;
     w.m_end = int64_t(row_start[lo]) + rows[lo];
     w.p_off = int64_t(lo) * group_w_rows;
-    w.w_row = w.p_off + int64_t(w.nt) * 128;
+    w.w_row = w.p_off + int64_t(w.nt) * ct;
     return w;
   }
 };
@@ -250,24 +261,39 @@ __device__ __forceinline__ void store_column(T* yp, int64_t ldy, int64_t m0, int
 
 // MODE (EpiMode) is a template parameter so that each instantiation carries
 // only its own epilogue: smaller code and fewer registers per kernel.
-template <int BN, int STAGES, int MODE>
+//
+// PAIR (launched as clusters of 2): both CTAs load their halves of each stage
+// and count the bytes on the even CTA's full barrier; the even CTA's MMA
+// thread issues the M = 256 MMAs and its commits reach the empty and
+// accumulator barriers of both CTAs; both epilogues report a drained
+// accumulator to the even CTA. A failed wait in either CTA also raises the
+// other's abort flag.
+template <int BN, int STAGES, int MODE, bool PAIR>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_w8a16_tc_kernel(const __grid_constant__ CUtensorMap tm_w,
                          const __grid_constant__ CUtensorMap tm_xhi,
                          const __grid_constant__ CUtensorMap tm_xlo, int64_t M, int64_t N,
                          TcWork work, Epilogue ep, int64_t slice_stride, int* err,
                          uint64_t timeout_ns, int inject_fault) {
-  using Cfg = TcCfg<BN, STAGES>;
+  using Cfg = TcCfg<BN, STAGES, PAIR>;
   extern __shared__ uint8_t dyn_smem[];
   __shared__ TcCtl ctl;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t smem_base = (smem_addr(dyn_smem) + 1023u) & ~1023u;
   auto sm_w = [&](int s) { return smem_base + uint32_t(s) * Cfg::STAGE_BYTES; };
-  auto sm_xh = [&](int s) { return sm_w(s) + Cfg::W_BYTES; };
+  auto sm_xh = [&](int s) { return sm_w(s) + Cfg::W_BYTES; };  // PAIR: this CTA's plane
   auto sm_xl = [&](int s) { return sm_w(s) + Cfg::W_BYTES + Cfg::X_BYTES; };
   volatile int* abort = &ctl.abort;
   const int units = work.units();
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int u0 = PAIR ? int(cluster_id_x()) : int(blockIdx.x);
+  const int ustep = PAIR ? int(cluster_count_x()) : int(gridDim.x);
+  auto fail = [&](int code) {
+    tc_fail(err, abort, code);
+    if (PAIR) st_shared_cluster_u32(mapa_shared(smem_addr(&ctl.abort), rank ^ 1u), 1u);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -276,7 +302,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_addr(&ctl.tfull[b]), 1);
-      mbar_init(smem_addr(&ctl.tempty[b]), TC_EPI_WARPS);
+      mbar_init(smem_addr(&ctl.tempty[b]), PAIR ? 2 * TC_EPI_WARPS : TC_EPI_WARPS);
     }
     mbar_init(smem_addr(&ctl.never), 1);
     ctl.abort = 0;
@@ -286,11 +312,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     prefetch_tensormap(&tm_xlo);
   }
   if (warp == 1) {
-    tmem_alloc(smem_addr(&ctl.tmem_base), Cfg::TMEM_COLS);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(smem_addr(&ctl.tmem_base), Cfg::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_addr(&ctl.tmem_base), Cfg::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  __syncwarp();
+  if (PAIR) cluster_sync_all();  // both CTAs' barriers exist before any remote signal
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ctl.tmem_base;
 
@@ -299,25 +332,60 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (lane == 0) {
       int g = 0;  // K steps issued by this CTA (ring position)
       bool stop = false;
-      for (int u = blockIdx.x; u < units && !stop; u += gridDim.x) {
-        const TcUnit wu = work.decode(u, BN, M);
+      for (int u = u0; u < units && !stop; u += ustep) {
+        const TcUnit wu = work.decode(u, BN, M, Cfg::CT);
+        const int32_t w_row = int32_t(wu.w_row + 128 * int64_t(rank));
         for (int i = 0; i < wu.nkt; ++i, ++g) {
           const int s = g % STAGES;
           const uint32_t ph = uint32_t(g / STAGES) & 1u;
           if (!mbar_wait_bounded(smem_addr(&ctl.empty[s]), ph ^ 1u, timeout_ns, abort)) {
-            tc_fail(err, abort, DEV_WAIT_PRODUCER);
+            fail(DEV_WAIT_PRODUCER);
             stop = true;
             break;
           }
           const uint32_t fb = smem_addr(&ctl.full[s]);
-          mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
+          // The activation tiles arrive as boxes of xb rows; a tile with
+          // fewer valid tokens (end of M or of an expert's rows) loads only
+          // the boxes that hold some, which covers every row its trimmed
+          // MMAs read (N = valid rounded up to 16).
+          const int xb = work.xbox;
+          const int64_t valid = wu.m_end - wu.m_begin;
+          const int nbox = valid >= BN ? BN / xb : int((valid + xb - 1) / xb);
           const int32_t kx = (wu.kt0 + i) * TC_BK;
-          tma_load_2d(sm_w(s), &tm_w, fb, kx, int32_t(wu.w_row));
-          tma_load_2d(sm_xh(s), &tm_xhi, fb, kx, int32_t(wu.m_begin));
-          tma_load_2d(sm_xl(s), &tm_xlo, fb, kx, int32_t(wu.m_begin));
+          if (PAIR) {
+            // Both CTAs' bytes complete on the even CTA's barrier, which only
+            // the even CTA arms (a completion that lands first leaves the
+            // phase open: its arrival is still pending).
+            const uint32_t fbc = mapa_shared(fb, 0);
+            if (leader) mbar_arrive_expect_tx(fb, uint32_t(2 * (Cfg::W_BYTES + nbox * xb * TC_BK)));
+            tma_load_2d_pair(sm_w(s), &tm_w, fbc, kx, w_row);
+            const CUtensorMap* tmx = leader ? &tm_xhi : &tm_xlo;
+            for (int bx = 0; bx < nbox; ++bx)
+              tma_load_2d_pair(sm_xh(s) + uint32_t(bx * xb * TC_BK), tmx, fbc, kx,
+                               int32_t(wu.m_begin + bx * xb));
+          } else {
+            mbar_arrive_expect_tx(fb, uint32_t(Cfg::W_BYTES + 2 * nbox * xb * TC_BK));
+            tma_load_2d(sm_w(s), &tm_w, fb, kx, w_row);
+            for (int bx = 0; bx < nbox; ++bx) {
+              const uint32_t off = uint32_t(bx * xb * TC_BK);
+              const int32_t row = int32_t(wu.m_begin + bx * xb);
+              tma_load_2d(sm_xh(s) + off, &tm_xhi, fb, kx, row);
+              tma_load_2d(sm_xl(s) + off, &tm_xlo, fb, kx, row);
+            }
+          }
         }
       }
-      if (*abort) {
+      if (PAIR && !*abort) {
+        // Every stage's last release (a commit of the even CTA) has landed
+        // here before this CTA can leave the cluster.
+        for (int s = 0; s < STAGES && s < g; ++s) {
+          const int last = s + ((g - 1 - s) / STAGES) * STAGES;
+          if (!mbar_wait_bounded(smem_addr(&ctl.empty[s]), uint32_t(last / STAGES) & 1u, timeout_ns,
+                                 nullptr))
+            atomicCAS(err, 0, DEV_WAIT_DRAIN);
+        }
+      }
+      if (*abort && leader) {
         // Drain: the last load issued into each stage must land before exit.
         for (int s = 0; s < STAGES && s < g; ++s) {
           const int last = s + ((g - 1 - s) / STAGES) * STAGES;
@@ -329,24 +397,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    if (lane == 0 && leader) {
       int g = 0, lt = 0;
       bool stop = false;
-      for (int u = blockIdx.x; u < units && !stop; u += gridDim.x, ++lt) {
-        const TcUnit wu = work.decode(u, BN, M);
+      for (int u = u0; u < units && !stop; u += ustep, ++lt) {
+        const TcUnit wu = work.decode(u, BN, M, Cfg::CT);
         const int nkt = wu.nkt;
         // A full tile runs one MMA of N = 2*BN over [x_hi | x_lo]. A tile with
         // fewer valid tokens than BN (the end of M or of an expert's rows) runs
         // one MMA per byte plane with N = valid rounded up to 16 (kind::i8
         // with M = 128 takes N in multiples of 16); columns above are never read.
+        // A pair runs one MMA of N = 2 * that (the x_hi rows from the even CTA,
+        // the x_lo rows from the odd one), so L starts at column nmma.
         const int64_t valid = wu.m_end - wu.m_begin;
         const bool full = valid >= BN;
         const uint32_t nmma = full ? uint32_t(BN) : uint32_t((valid + 15) & ~int64_t(15));
         const uint32_t idesc_part = (Cfg::IDESC & ~(0x3Fu << 17)) | ((nmma >> 3) << 17);
+        const uint32_t idesc_pair = (Cfg::IDESC & ~(0x3Fu << 17)) | (((2 * nmma) >> 3) << 17);
         const int b = lt & 1;
         const uint32_t tph = uint32_t(lt >> 1) & 1u;
         if (!mbar_wait_bounded(smem_addr(&ctl.tempty[b]), tph ^ 1u, timeout_ns, abort)) {
-          tc_fail(err, abort, DEV_WAIT_MMA);
+          fail(DEV_WAIT_MMA);
           break;
         }
         tc_fence_after();
@@ -355,7 +426,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           const int s = g % STAGES;
           const uint32_t ph = uint32_t(g / STAGES) & 1u;
           if (!mbar_wait_bounded(smem_addr(&ctl.full[s]), ph, timeout_ns, abort)) {
-            tc_fail(err, abort, DEV_WAIT_MMA);
+            fail(DEV_WAIT_MMA);
             stop = true;
             break;
           }
@@ -366,16 +437,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const uint32_t off = uint32_t(kk) * 32u;
             const uint64_t dw = smem_desc_k_sw128(aw + off);
             const uint32_t accum = (i > 0 || kk > 0) ? 1u : 0u;
-            if (full) {
+            if (PAIR) {
+              mma_i8_pair(d_hi, dw, smem_desc_k_sw128(axh + off), idesc_pair, accum);
+            } else if (full) {
               mma_i8(d_hi, dw, smem_desc_k_sw128(axh + off), Cfg::IDESC, accum);
             } else {
               mma_i8(d_hi, dw, smem_desc_k_sw128(axh + off), idesc_part, accum);
               mma_i8(d_lo, dw, smem_desc_k_sw128(axl + off), idesc_part, accum);
             }
           }
-          mma_commit(smem_addr(&ctl.empty[s]));  // frees the stage when these MMAs finish
+          // frees the stage (in both CTAs of a pair) when these MMAs finish
+          if (PAIR) mma_commit_pair_both(smem_addr(&ctl.empty[s]));
+          else mma_commit(smem_addr(&ctl.empty[s]));
         }
-        mma_commit(smem_addr(&ctl.tfull[b]));  // also signals on abort: the epilogue checks
+        // also signals on abort: the epilogue checks
+        if (PAIR) mma_commit_pair_both(smem_addr(&ctl.tfull[b]));
+        else mma_commit(smem_addr(&ctl.tfull[b]));
       }
       // The issuer itself sees its last MMAs finish before TMEM can be released.
       if (lt > 0) {
@@ -393,8 +470,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int col0 = ((warp - 2) >> 2) * QCOLS;
     const int row = q * 32 + lane;
     int lt = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x, ++lt) {
-      const TcUnit wu = work.decode(u, BN, M);
+    for (int u = u0; u < units; u += ustep, ++lt) {
+      const TcUnit wu = work.decode(u, BN, M, Cfg::CT);
       const int b = lt & 1;
       const uint32_t tph = uint32_t(lt >> 1) & 1u;
       bool ok = mbar_wait_bounded(smem_addr(&ctl.tfull[b]), tph, timeout_ns, abort);
@@ -404,15 +481,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         code = DEV_WAIT_INJECTED;
       }
       if (!ok) {
-        tc_fail(err, abort, code);
+        fail(code);
         break;
       }
       if (*abort) break;
       tc_fence_after();
-      const int64_t n = int64_t(wu.nt) * 128 + row;  // channel within the group
+      const int64_t n = int64_t(wu.nt) * Cfg::CT + 128 * int64_t(rank) + row;  // channel in the group
       const int64_t m0 = wu.m_begin + col0;
       const int64_t Mend = wu.m_end;
       const uint32_t tq = tmem + (uint32_t(q * 32) << 16) + uint32_t(b * Cfg::BUF_COLS + col0);
+      // Column of L: BN, or for a pair the MMA's N / 2 (valid tokens rounded up to 16).
+      const int64_t valid = Mend - wu.m_begin;
+      const uint32_t lo_col = (!PAIR || valid >= BN) ? uint32_t(BN)
+                                                     : uint32_t((valid + 15) & ~int64_t(15));
       Epilogue e = ep;
       if (MODE == EPI_ACC_I64) e.y = static_cast<int64_t*>(e.y) + int64_t(wu.ks) * slice_stride;
       if (wu.p_off) {  // per-channel parameters of this group
@@ -434,19 +515,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       // H = H' - 128 * S over this unit's K tiles (wrapping; the true H fits).
       uint32_t corr = 0;
       if (n < N) {
-        const int32_t* ws = work.wsum + (wu.w_row + row) * work.wsum_ld;
+        const int32_t* ws = work.wsum + (wu.w_row + 128 * int64_t(rank) + row) * work.wsum_ld;
         corr = (uint32_t(ws[wu.kt0 + wu.nkt]) - uint32_t(ws[wu.kt0])) << 7;
       }
 #pragma unroll 1
       for (int c = 0; c < QCOLS; c += NC) {
         if (m0 + c >= Mend) break;  // warp-uniform: no stored token left in this warp's columns
         uint32_t hi[NC], lo[NC];
-        tmem_ld_pair<NC>(tq + c, tq + BN + c, hi, lo);
+        tmem_ld_pair<NC>(tq + c, tq + lo_col + c, hi, lo);
 #pragma unroll
         for (int j = 0; j < NC; ++j) hi[j] -= corr;
         if (wu.tail_slot >= 0) {  // int64 partial of a tail tile's K slice
           if (n < N) {
-            int64_t* tp = work.tail_ws + (int64_t(wu.tail_slot) * BN + col0 + c) * 128 + row;
+            int64_t* tp = work.tail_ws +
+                          ((int64_t(wu.tail_slot) * (Cfg::CT / 128) + rank) * BN + col0 + c) * 128 + row;
 #pragma unroll
             for (int j = 0; j < NC; ++j)
               tp[int64_t(j) * 128] = int64_t(int32_t(hi[j])) * 256 + int64_t(int32_t(lo[j]));
@@ -559,40 +641,56 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
         }
       }
-      // Hand the buffer back to the MMA issuer.
+      // Hand the buffer back to the MMA issuer (the even CTA's, for a pair).
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_addr(&ctl.tempty[b]));
+      if (lane == 0) {
+        if (PAIR && !leader) mbar_arrive_cluster(mapa_shared(smem_addr(&ctl.tempty[b]), 0));
+        else mbar_arrive(smem_addr(&ctl.tempty[b]));
+      }
     }
     tc_fence_before();
   }
-  __syncthreads();
+  if (PAIR) {
+    // Every thread of both CTAs gets here (all waits above are bounded); the
+    // even CTA's MMAs are finished and both epilogues are done with TMEM.
+    __syncwarp();
+    cluster_sync_all();
+  } else {
+    __syncthreads();
+  }
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+    if (PAIR) tmem_dealloc_pair(tmem, Cfg::TMEM_COLS);
+    else tmem_dealloc(tmem, Cfg::TMEM_COLS);
   }
 }
 
 // Adds the tail tiles' K-slice partials and applies the final epilogue.
 // One thread per (tile, token, channel pair): both rows of the pair, so the
-// SiLU mode can combine gate and up.
+// SiLU mode can combine gate and up. ct: channels per tile (128, or 256 for
+// CTA pairs, whose halves are stored one after the other).
 __global__ void tail_reduce_kernel(const int64_t* __restrict__ ws, int tail_tiles, int tail_ks,
-                                   int first_tile, int tiles_n, int BN, int64_t M, int64_t N,
-                                   Epilogue ep) {
-  const int64_t total = int64_t(tail_tiles) * BN * 64;
+                                   int first_tile, int tiles_n, int BN, int ct, int64_t M,
+                                   int64_t N, Epilogue ep) {
+  const int hp = ct / 2;  // channel pairs per tile
+  const int halves = ct / 128;
+  const int64_t total = int64_t(tail_tiles) * BN * hp;
   for (int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
        e += int64_t(gridDim.x) * blockDim.x) {
-    const int pr = int(e % 64);
-    const int col = int((e / 64) % BN);
-    const int tl = int(e / (64 * int64_t(BN)));
+    const int pr = int(e % hp);
+    const int col = int((e / hp) % BN);
+    const int tl = int(e / (int64_t(hp) * BN));
     const int t = first_tile + tl;
     const int64_t m = int64_t(t / tiles_n) * BN + col;
-    const int64_t n0 = int64_t(t % tiles_n) * 128 + 2 * pr;
+    const int64_t n0 = int64_t(t % tiles_n) * ct + 2 * pr;
     if (m >= M || n0 >= N) continue;
+    const int half = (2 * pr) >> 7, r0 = (2 * pr) & 127;
     int64_t a0 = 0, a1 = 0;
     for (int s = 0; s < tail_ks; ++s) {
-      const int64_t* p = ws + ((int64_t(s) * tail_tiles + tl) * BN + col) * 128 + 2 * pr;
+      const int64_t* p =
+          ws + (((int64_t(s) * tail_tiles + tl) * halves + half) * BN + col) * 128 + r0;
       a0 += p[0];
       a1 += p[1];
     }

@@ -123,6 +123,9 @@ struct myl_ctx {
   uint64_t timeout_ns = 2000000000ull;
   int gemv_max_m = 4, force_split_k = 0, force_tile = 0, inject_fault = 0;
   int sm_limit = 0;  // persistent grids use at most this many SMs (0: all)
+  int xbox = TC_XBOX;  // activation rows per TMA box of the tensor-core GEMM
+  int pair_mode = 1;   // CTA-pair GEMM (M = 256 MMAs): 0 off, 1 for 128-token tiles
+  int pair_slots = 0;  // co-resident CTA pairs of the pair kernel (0: not yet queried)
   int64_t launches = 0;
   PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   DevBuf x, y, rq, planes, part, h, hplanes, moe, xsum;
@@ -380,59 +383,122 @@ static int launch_gemv(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int6
   return MYL_OK;
 }
 
+// Box height of the activation tensor maps for token tile BN (a power of two
+// that divides BN); the kernel receives the same number in TcWork::xbox.
+static int tc_xbox(const myl_ctx* ctx, int BN) { return std::min(ctx->xbox, BN); }
+
 // Stage-ring depth per token tile: 192 KB of smem (one CTA per SM).
 template <int BN>
 struct TcStages;
 template <> struct TcStages<32> { static constexpr int value = 8; };
 template <> struct TcStages<64> { static constexpr int value = 6; };
 template <> struct TcStages<128> { static constexpr int value = 4; };
+// CTA pair: each SM holds the weight tile and one activation plane per stage.
+constexpr int TC_PAIR_STAGES = 6;
 
-template <int BN, int MODE>
+// CTA pairs that can be resident at once for the pair kernel: SMs / 2, fewer
+// when the GPCs' SM counts are odd (a pair shares a GPC).
+template <typename Fn>
+static int pair_slots(myl_ctx* ctx, Fn fn, size_t smem) {
+  if (ctx->pair_slots > 0) return std::max(1, std::min(ctx->pair_slots, sms(ctx) / 2));
+  TRY(kernel_smem_occupancy(ctx->device, reinterpret_cast<const void*>(fn), TC_THREADS, smem, nullptr));
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(unsigned(2 * (ctx->num_sms / 2)));
+  cfg.blockDim = dim3(TC_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = ctx->num_sms / 2;
+  }
+  ctx->pair_slots = n;
+  return std::max(1, std::min(n, sms(ctx) / 2));
+}
+
+template <int BN, int MODE, bool PAIR>
 static int launch_tc_mode(myl_ctx* ctx, const myl_weight* w, const CUtensorMap& tm_xhi,
                           const CUtensorMap& tm_xlo, int64_t M, const TcWork& work,
                           const Epilogue& ep, int64_t slice_stride, cudaStream_t st) {
-  constexpr int STAGES = TcStages<BN>::value;
-  using Cfg = TcCfg<BN, STAGES>;
-  auto fn = gemm_w8a16_tc_kernel<BN, STAGES, MODE>;
+  constexpr int STAGES = PAIR ? TC_PAIR_STAGES : TcStages<BN>::value;
+  using Cfg = TcCfg<BN, STAGES, PAIR>;
+  auto fn = gemm_w8a16_tc_kernel<BN, STAGES, MODE, PAIR>;
   TRY(kernel_smem_occupancy(ctx->device, reinterpret_cast<const void*>(fn), TC_THREADS,
                             Cfg::SMEM_BYTES, nullptr));
-  // Grouped work is sized on the device (the router's tile table): one CTA per
-  // SM, CTAs without a unit exit after setup.
-  const int64_t units = work.groups > 0 ? int64_t(sms(ctx))
+  // Grouped work is sized on the device (the router's tile table): one CTA
+  // (pair) per SM (pair of SMs); those without a unit exit after setup.
+  const int64_t slots = PAIR ? pair_slots(ctx, fn, Cfg::SMEM_BYTES) : sms(ctx);
+  const int64_t units = work.groups > 0 ? slots
                         : work.tail_tiles > 0
                             ? int64_t(work.full_units) + int64_t(work.tail_tiles) * work.tail_ks
                             : int64_t(work.tiles_n) * work.tiles_m * work.ksplit;
-  const unsigned grid = unsigned(std::min<int64_t>(units, sms(ctx)));
   const int64_t N = work.groups > 0 ? work.group_w_rows : w->N;  // channels per group
   TcWork wk = work;
   wk.wsum = w->d_wsum;
   wk.wsum_ld = w->wsum_ld;
-  fn<<<grid, TC_THREADS, Cfg::SMEM_BYTES, st>>>(w->tm128, tm_xhi, tm_xlo, M, N, wk, ep,
-                                                 slice_stride, ctx->d_err, ctx->timeout_ns,
-                                                 ctx->inject_fault);
-  CUDA_TRY(cudaGetLastError());
+  wk.xbox = tc_xbox(ctx, BN);
+  const unsigned grid = unsigned(std::max<int64_t>(1, std::min<int64_t>(units, slots)));
+  if (PAIR) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * grid);
+    cfg.blockDim = dim3(TC_THREADS);
+    cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, fn, w->tm128, tm_xhi, tm_xlo, M, N, wk, ep, slice_stride,
+                                ctx->d_err, ctx->timeout_ns, ctx->inject_fault));
+  } else {
+    fn<<<grid, TC_THREADS, Cfg::SMEM_BYTES, st>>>(w->tm128, tm_xhi, tm_xlo, M, N, wk, ep,
+                                                   slice_stride, ctx->d_err, ctx->timeout_ns,
+                                                   ctx->inject_fault);
+    CUDA_TRY(cudaGetLastError());
+  }
   ctx->launches++;
   return MYL_OK;
 }
 
-template <int BN>
+template <int BN, bool PAIR>
 static int launch_tc_variant(myl_ctx* ctx, const myl_weight* w, const CUtensorMap& tm_xhi,
                              const CUtensorMap& tm_xlo, int64_t M, const TcWork& work,
                              const Epilogue& ep, int64_t slice_stride, cudaStream_t st) {
   switch (ep.mode) {
     case EPI_ACC_I64:
-      return launch_tc_mode<BN, EPI_ACC_I64>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
+      return launch_tc_mode<BN, EPI_ACC_I64, PAIR>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
     case EPI_SHIFT:
-      return launch_tc_mode<BN, EPI_SHIFT>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
+      return launch_tc_mode<BN, EPI_SHIFT, PAIR>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
     case EPI_MULT:
-      return launch_tc_mode<BN, EPI_MULT>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
+      return launch_tc_mode<BN, EPI_MULT, PAIR>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
     case EPI_SILU:
-      return launch_tc_mode<BN, EPI_SILU>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
+      return launch_tc_mode<BN, EPI_SILU, PAIR>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
     case EPI_W16:
-      return launch_tc_mode<BN, EPI_W16>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
+      return launch_tc_mode<BN, EPI_W16, PAIR>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
     default:
       return fail(MYL_ERR_ARG, "unknown epilogue mode %d", ep.mode);
   }
+}
+
+// The CTA-pair kernel runs 128-token tiles (the M = 256 MMA then reads one
+// 16 KB activation plane per SM and stage instead of two).
+static bool tc_pair(const myl_ctx* ctx, int BN) { return ctx->pair_mode != 0 && BN == 128; }
+
+// Work slots of one wave: SMs, or co-resident CTA pairs.
+static int tc_slots(myl_ctx* ctx, bool pair) {
+  if (!pair) return sms(ctx);
+  constexpr int S = TC_PAIR_STAGES;
+  return pair_slots(ctx, gemm_w8a16_tc_kernel<128, S, EPI_SHIFT, true>,
+                    size_t(TcCfg<128, S, true>::SMEM_BYTES));
 }
 
 static int tc_token_tile(const myl_ctx* ctx, int64_t M) {
@@ -440,12 +506,18 @@ static int tc_token_tile(const myl_ctx* ctx, int64_t M) {
   return M <= 32 ? 32 : (M <= 64 ? 64 : 128);
 }
 
+// pair: launch the CTA-pair kernel (BN = 128 only; work laid out in 256-channel units).
 static int launch_tc_any(myl_ctx* ctx, const myl_weight* w, const CUtensorMap& tm_xhi,
-                         const CUtensorMap& tm_xlo, int64_t M, int BN, const TcWork& work,
-                         const Epilogue& ep, int64_t slice_stride, cudaStream_t st) {
-  if (BN == 32) return launch_tc_variant<32>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
-  if (BN == 64) return launch_tc_variant<64>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
-  return launch_tc_variant<128>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
+                         const CUtensorMap& tm_xlo, int64_t M, int BN, bool pair,
+                         const TcWork& work, const Epilogue& ep, int64_t slice_stride,
+                         cudaStream_t st) {
+  if (pair) {
+    if (BN != 128) return fail(MYL_ERR_ARG, "CTA-pair GEMM needs 128-token tiles");
+    return launch_tc_variant<128, true>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
+  }
+  if (BN == 32) return launch_tc_variant<32, false>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
+  if (BN == 64) return launch_tc_variant<64, false>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
+  return launch_tc_variant<128, false>(ctx, w, tm_xhi, tm_xlo, M, work, ep, slice_stride, st);
 }
 
 static int launch_split(myl_ctx* ctx, const int16_t* x, int64_t M, int64_t K, int64_t ldx,
@@ -464,26 +536,28 @@ static int launch_tc_planes(myl_ctx* ctx, const myl_weight* w, const uint8_t* xh
   const int64_t K = w->K;
   const int BN = tc_token_tile(ctx, M);
   CUtensorMap tm_xhi, tm_xlo;
-  TRY(encode_map(ctx, &tm_xhi, xhi, K, M, ldp, BN));
-  TRY(encode_map(ctx, &tm_xlo, xlo, K, M, ldp, BN));
+  TRY(encode_map(ctx, &tm_xhi, xhi, K, M, ldp, tc_xbox(ctx, BN)));
+  TRY(encode_map(ctx, &tm_xlo, xlo, K, M, ldp, tc_xbox(ctx, BN)));
   // K split: enough work units for the SMs, and int32-exact slices (<= 65536).
+  const bool pair = tc_pair(ctx, BN);
+  const int ct = pair ? 256 : 128;  // channels per work unit
+  const int64_t G = tc_slots(ctx, pair);
   const int k_tiles = int((K + TC_BK - 1) / TC_BK);
-  const int64_t tiles = ((w->N + 127) / 128) * ((M + BN - 1) / BN);
+  const int64_t tiles = ((w->N + ct - 1) / ct) * ((M + BN - 1) / BN);
   int ksplit = 1;
   if (ctx->force_split_k > 0) {
     ksplit = ctx->force_split_k;
-  } else if (tiles < sms(ctx) && k_tiles >= 8) {
-    ksplit = int(std::min<int64_t>(sms(ctx) / tiles, k_tiles / 4));
+  } else if (tiles < G && k_tiles >= 8) {
+    ksplit = int(std::min<int64_t>(G / tiles, k_tiles / 4));
   }
   ksplit = std::max(ksplit, int((K + 65535) / 65536));
   ksplit = std::max(1, std::min(ksplit, k_tiles));
   const int per = (k_tiles + ksplit - 1) / ksplit;
   ksplit = (k_tiles + per - 1) / per;  // no empty slice
-  TcWork work{int((w->N + 127) / 128), int((M + BN - 1) / BN), ksplit, k_tiles, per};
+  TcWork work{int((w->N + ct - 1) / ct), int((M + BN - 1) / BN), ksplit, k_tiles, per};
   // Tail split: when the tiles fill some waves and leave a small last wave,
   // that wave's tiles run as K slices on all SMs (int64 partials, then
   // tail_reduce_kernel), so the last wave costs a fraction of a full one.
-  const int64_t G = sms(ctx);
   const int64_t R = tiles % G;
   if (ksplit == 1 && ctx->force_split_k == 0 && tiles >= G && R > 0) {
     const int ks = int(std::min<int64_t>({G / R, int64_t(k_tiles / 4), 16}));
@@ -493,16 +567,17 @@ static int launch_tc_planes(myl_ctx* ctx, const myl_weight* w, const uint8_t* xh
       work.tail_tiles = int(R);
       work.tail_ks = (k_tiles + tper - 1) / tper;
       work.tail_per = tper;
-      TRY(ensure(ctx->part, size_t(R) * size_t(work.tail_ks) * size_t(BN) * 128 * 8));
+      TRY(ensure(ctx->part, size_t(R) * size_t(work.tail_ks) * size_t(BN) * size_t(ct) * 8));
       work.tail_ws = static_cast<int64_t*>(ctx->part.p);
     }
   }
   if (work.tail_tiles > 0) {
-    TRY(launch_tc_any(ctx, w, tm_xhi, tm_xlo, M, BN, work, ep_final, 0, st));
-    const int64_t total = int64_t(work.tail_tiles) * BN * 64;
-    const unsigned blocks = unsigned(std::min<int64_t>((total + 255) / 256, G * 8));
+    TRY(launch_tc_any(ctx, w, tm_xhi, tm_xlo, M, BN, pair, work, ep_final, 0, st));
+    const int64_t total = int64_t(work.tail_tiles) * BN * (ct / 2);
+    const unsigned blocks = unsigned(std::min<int64_t>((total + 255) / 256, int64_t(sms(ctx)) * 8));
     tail_reduce_kernel<<<blocks, 256, 0, st>>>(work.tail_ws, work.tail_tiles, work.tail_ks,
-                                                work.full_units, work.tiles_n, BN, M, w->N, ep_final);
+                                                work.full_units, work.tiles_n, BN, ct, M, w->N,
+                                                ep_final);
     CUDA_TRY(cudaGetLastError());
     ctx->launches++;
     return MYL_OK;
@@ -516,7 +591,7 @@ static int launch_tc_planes(myl_ctx* ctx, const myl_weight* w, const uint8_t* xh
     ep.ldy = w->N;
     slice_stride = M * w->N;
   }
-  TRY(launch_tc_any(ctx, w, tm_xhi, tm_xlo, M, BN, work, ep, slice_stride, st));
+  TRY(launch_tc_any(ctx, w, tm_xhi, tm_xlo, M, BN, pair, work, ep, slice_stride, st));
   if (ksplit > 1) {
     const int64_t total = M * w->N;
     unsigned blocks = unsigned(std::min<int64_t>((total + 255) / 256, int64_t(ctx->num_sms) * 8));
@@ -677,6 +752,12 @@ int myl_init(int device, myl_ctx** out) {
   c->device = device;
   c->sm = prop.major * 10 + prop.minor;
   c->num_sms = prop.multiProcessorCount;
+  if (const char* env = std::getenv("MYL_TC_XBOX")) {  // tuning: 16, 32, 64 or 128 rows per box
+    const int v = std::atoi(env);
+    if (v == 16 || v == 32 || v == 64 || v == 128) c->xbox = v;
+  }
+  if (const char* env = std::getenv("MYL_TC_PAIR"))  // tuning: 0 = one CTA per tile only
+    c->pair_mode = std::atoi(env) != 0 ? 1 : 0;
   cudaDriverEntryPointQueryResult q;
   void* fn = nullptr;
   cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000,
@@ -1153,8 +1234,16 @@ int myl_mlp_register(myl_ctx* ctx, const int8_t* W_gate, const int8_t* W_up, con
 
 // y != nullptr: requantised output; otherwise acc receives the exact int64
 // down-projection sums (tensor-parallel partials).
+// Byte planes of an activation that several projections read (split once).
+struct XPlanes {
+  const uint8_t* hi = nullptr;
+  const uint8_t* lo = nullptr;
+  int64_t ldp = 0;
+};
+
 static int run_mlp(myl_ctx* ctx, const myl_mlp* mlp, const int16_t* x, int64_t M, int64_t ldx,
-                   int16_t* y, int64_t ldy, cudaStream_t st, int64_t* acc = nullptr) {
+                   int16_t* y, int64_t ldy, cudaStream_t st, int64_t* acc = nullptr,
+                   const XPlanes& xp = XPlanes()) {
   if (M == 0) return MYL_OK;
   const int64_t I = mlp->I;
   Epilogue ep_gu{};
@@ -1191,7 +1280,8 @@ static int run_mlp(myl_ctx* ctx, const myl_mlp* mlp, const int16_t* x, int64_t M
     ep_gu.silu.h_hi = hhi;
     ep_gu.silu.h_lo = hlo;
     ep_gu.silu.ldp = ldp_h;
-    TRY(launch_tc(ctx, mlp->w_gu, x, M, ldx, ep_gu, st));
+    if (xp.hi) TRY(launch_tc_planes(ctx, mlp->w_gu, xp.hi, xp.lo, xp.ldp, M, ep_gu, st));
+    else TRY(launch_tc(ctx, mlp->w_gu, x, M, ldx, ep_gu, st));
     TRY(launch_tc_planes(ctx, mlp->w_down, hhi, hlo, ldp_h, M, ep_down, st));
   }
   return ws_release(ctx, st);
@@ -1309,6 +1399,17 @@ int myl_set_sm_limit(myl_ctx* ctx, int max_sms) {
   return MYL_OK;
 }
 
+int myl_set_tc_options(myl_ctx* ctx, int pair_mode, int xbox_rows) {
+  if (!ctx) return fail(MYL_ERR_ARG, "ctx is null");
+  if (pair_mode != 0 && pair_mode != 1) return fail(MYL_ERR_ARG, "pair_mode must be 0 or 1");
+  if (xbox_rows != 0 && xbox_rows != 16 && xbox_rows != 32 && xbox_rows != 64 && xbox_rows != 128)
+    return fail(MYL_ERR_ARG, "xbox_rows must be 0, 16, 32, 64 or 128");
+  CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  ctx->pair_mode = pair_mode;
+  if (xbox_rows) ctx->xbox = xbox_rows;
+  return MYL_OK;
+}
+
 int myl_debug_inject_wait_fault(myl_ctx* ctx, int on) {
   if (!ctx) return fail(MYL_ERR_ARG, "ctx is null");
   ctx->inject_fault = on ? 1 : 0;
@@ -1389,11 +1490,13 @@ extern "C" int myl_linear_noalloc_dev(myl_ctx* ctx, const myl_weight* w, const m
   // partial buffer is needed.
   const int BN = tc_token_tile(ctx, M);
   CUtensorMap tm_xhi, tm_xlo;
-  TRY(encode_map(ctx, &tm_xhi, xhi, w->K, M, w->ldp, BN));
-  TRY(encode_map(ctx, &tm_xlo, xlo, w->K, M, w->ldp, BN));
+  TRY(encode_map(ctx, &tm_xhi, xhi, w->K, M, w->ldp, tc_xbox(ctx, BN)));
+  TRY(encode_map(ctx, &tm_xlo, xlo, w->K, M, w->ldp, tc_xbox(ctx, BN)));
   const int k_tiles = int((w->K + TC_BK - 1) / TC_BK);
-  const TcWork work{int((w->N + 127) / 128), int((M + BN - 1) / BN), 1, k_tiles, k_tiles};
-  return launch_tc_any(ctx, w, tm_xhi, tm_xlo, M, BN, work, make_ep(rq, y, ldy), 0, st);
+  const bool pair = tc_pair(ctx, BN);
+  const int ct = pair ? 256 : 128;
+  const TcWork work{int((w->N + ct - 1) / ct), int((M + BN - 1) / BN), 1, k_tiles, k_tiles};
+  return launch_tc_any(ctx, w, tm_xhi, tm_xlo, M, BN, pair, work, make_ep(rq, y, ldy), 0, st);
 }
 
 // ---------------------------------------------------------------------------------
@@ -1498,14 +1601,16 @@ static int moe_token_tile(const myl_ctx* ctx, int64_t P, int64_t L) {
 }
 
 static int moe_route(myl_ctx* ctx, const myl_moe* m, const int16_t* x, int64_t T, int64_t ldx,
-                     int32_t* logits, int32_t* idx, int32_t* prob, cudaStream_t st) {
+                     int32_t* logits, int32_t* idx, int32_t* prob, cudaStream_t st,
+                     const XPlanes& xp = XPlanes()) {
   Epilogue ep{};
   ep.mode = EPI_SHIFT;
   ep.out_i32 = 1;
   ep.shift = m->rq_router->d_shift;
   ep.y = logits;
   ep.ldy = m->E;
-  TRY(dispatch_linear(ctx, m->w_router, x, T, ldx, ep, st));
+  if (xp.hi) TRY(launch_tc_planes(ctx, m->w_router, xp.hi, xp.lo, xp.ldp, T, ep, st));
+  else TRY(dispatch_linear(ctx, m->w_router, x, T, ldx, ep, st));
   MoeRouteParams rp{m->d_exp_lut, m->exp_lut_len, m->exp_lut_shift, m->prob_frac};
   moe_route_kernel<<<grid_for(ctx, T * 32), 256, 0, st>>>(logits, m->E, T, int(m->E), int(m->k), rp,
                                                            idx, prob);  // one warp per token
@@ -1521,7 +1626,9 @@ static int moe_experts(myl_ctx* ctx, const myl_moe* m, const int16_t* x, int64_t
                        cudaStream_t st) {
   const int L = int(m->L);
   const int BN = moe_token_tile(ctx, P, L);
-  const int tiles_gu = int((2 * m->I + 127) / 128), tiles_down = int((m->H + 127) / 128);
+  const bool pair = tc_pair(ctx, BN);
+  const int ct = pair ? 256 : 128;  // channels per work unit
+  const int tiles_gu = int((2 * m->I + ct - 1) / ct), tiles_down = int((m->H + ct - 1) / ct);
   CUDA_TRY(cudaMemsetAsync(w.counts, 0, size_t(L) * sizeof(int), st));
   moe_count_kernel<<<grid_for(ctx, P, 2), 256, 0, st>>>(ids, P, int(m->first), L, w.counts,
                                                         ctx->d_err);
@@ -1542,10 +1649,11 @@ static int moe_experts(myl_ctx* ctx, const myl_moe* m, const int16_t* x, int64_t
   ctx->launches += 4;
   // Gate/up: grouped GEMM with the SiLU pair epilogue into the down planes.
   CUtensorMap tm_xhi, tm_xlo, tm_hhi, tm_hlo;
-  TRY(encode_map(ctx, &tm_xhi, w.xhi, H, P, ldp_h, BN));
-  TRY(encode_map(ctx, &tm_xlo, w.xlo, H, P, ldp_h, BN));
-  TRY(encode_map(ctx, &tm_hhi, w.hhi, m->I, P, ldp_i, BN));
-  TRY(encode_map(ctx, &tm_hlo, w.hlo, m->I, P, ldp_i, BN));
+  const int xb = tc_xbox(ctx, BN);
+  TRY(encode_map(ctx, &tm_xhi, w.xhi, H, P, ldp_h, xb));
+  TRY(encode_map(ctx, &tm_xlo, w.xlo, H, P, ldp_h, xb));
+  TRY(encode_map(ctx, &tm_hhi, w.hhi, m->I, P, ldp_i, xb));
+  TRY(encode_map(ctx, &tm_hlo, w.hlo, m->I, P, ldp_i, xb));
   TcWork wk{};
   wk.tiles_n = tiles_gu;
   wk.tiles_m = 1;
@@ -1569,7 +1677,7 @@ static int moe_experts(myl_ctx* ctx, const myl_moe* m, const int16_t* x, int64_t
   ep_gu.silu.h_lo = w.hlo;
   ep_gu.silu.ldp = ldp_i;
   ep_gu.ldy = m->I;
-  TRY(launch_tc_any(ctx, m->w_gu, tm_xhi, tm_xlo, P, BN, wk, ep_gu, 0, st));
+  TRY(launch_tc_any(ctx, m->w_gu, tm_xhi, tm_xlo, P, BN, pair, wk, ep_gu, 0, st));
   // Down: grouped GEMM, reference requant, rows in expert order.
   wk.tiles_n = tiles_down;
   wk.k_tiles_total = int((m->I + TC_BK - 1) / TC_BK);
@@ -1581,7 +1689,7 @@ static int moe_experts(myl_ctx* ctx, const myl_moe* m, const int16_t* x, int64_t
   ep_down.shift = m->d_shift_down;
   ep_down.y = w.y_perm;
   ep_down.ldy = H;
-  return launch_tc_any(ctx, m->w_down, tm_hhi, tm_hlo, P, BN, wk, ep_down, 0, st);
+  return launch_tc_any(ctx, m->w_down, tm_hhi, tm_hlo, P, BN, pair, wk, ep_down, 0, st);
 }
 
 extern "C" {
@@ -1778,11 +1886,22 @@ int myl_moe_dev(myl_ctx* ctx, const myl_moe* m, const int16_t* x, int64_t T, int
   TRY(moe_workspace(ctx, m, P, T, &w));
   int32_t* idx = topk_idx ? topk_idx : w.topk_idx;
   int32_t* prob = topk_prob ? topk_prob : w.topk_prob;
-  TRY(moe_route(ctx, m, x, T, ldx, w.logits, idx, prob, st));
+  // Prefill: the router and the shared expert read x from one split.
+  XPlanes xp;
+  if (!(T <= ctx->gemv_max_m && T <= 4)) {
+    const int64_t ldp = m->w_router->ldp;
+    TRY(ensure(ctx->planes, size_t(2) * size_t(T) * size_t(ldp)));
+    uint8_t* hi = static_cast<uint8_t*>(ctx->planes.p);
+    TRY(launch_split(ctx, x, T, m->H, ldx, hi, hi + T * ldp, ldp, st));
+    xp.hi = hi;
+    xp.lo = hi + T * ldp;
+    xp.ldp = ldp;
+  }
+  TRY(moe_route(ctx, m, x, T, ldx, w.logits, idx, prob, st, xp));
   TRY(moe_experts(ctx, m, x, ldx, idx, P, int(m->k), w.ex, st));
   const int16_t* shared_out = nullptr;
   if (m->shared) {
-    TRY(run_mlp(ctx, m->shared, x, T, ldx, w.shared_out, m->H, st));
+    TRY(run_mlp(ctx, m->shared, x, T, ldx, w.shared_out, m->H, st, nullptr, xp));
     shared_out = w.shared_out;
   }
   moe_combine_kernel<<<rows_grid(m->H, T), 256, 0, st>>>(w.ex.y_perm, m->H, w.ex.pos, prob,
