@@ -46,7 +46,8 @@ enum myl_status {
   MYL_ERR_DEVICE = 5,      /* a kernel reported an error (e.g. a bounded wait ran out) */
   MYL_ERR_UNSUPPORTED = 6, /* device is not sm_100 or a size is beyond a kernel limit */
   MYL_ERR_IO = 7,          /* an artifact file is missing, unreadable or not valid JSON */
-  MYL_ERR_CORRUPT = 8,     /* an artifact file disagrees with its manifest (size, hash, dtype) */
+  MYL_ERR_CORRUPT = 8,     /* an artifact file disagrees with its manifest (size, hash, dtype),
+                              or a wire frame is malformed (magic, length, CRC) */
 };
 
 /* Requant modes (myl_requant_create). */
@@ -103,6 +104,16 @@ int myl_weight16_register(myl_ctx* ctx, const int16_t* W, int64_t out_features, 
                           int64_t ldw, const uint8_t* w_shifts, myl_weight** out);
 int myl_lm_head_w16a16_i32(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
                            uint8_t final_norm_frac, uint8_t logit_frac, int32_t* logits);
+
+/* Greedy selection (argmax_int, sampling.rs:8-18: lowest index among the
+ * maxima) over int32 logits [M][V] (row stride ld, device pointers) whose
+ * column j is vocab index index_base + j: keys[m] = v * 2^32 + (2^32 - 1 - i)
+ * for the winning logit v at index i, or INT64_MIN when V = 0. The largest key
+ * over vocab shards is the global winner, so tensor-parallel ranks combine
+ * with one int64 max all-reduce; token = 2^32 - 1 - (key & 0xFFFFFFFF),
+ * logit = key >> 32. index_base + V must not exceed 2^32. */
+int myl_argmax_keys_dev(myl_ctx* ctx, const int32_t* logits, int64_t M, int64_t V, int64_t ld,
+                        int64_t index_base, int64_t* keys, void* stream);
 
 /* linear_w8a16 followed by add_bias_i16 (linear.rs:132-145) as the runtime
  * does for q/k/v (runtime/src/model.rs:438-453), fused into one epilogue:
@@ -339,6 +350,51 @@ int myl_artifact_register(myl_ctx* ctx, const myl_artifact* a, int64_t index, my
 int myl_artifact_lut(const myl_artifact* a, const char* name, const int16_t** data, int64_t* len);
 /* SHA-256 (FIPS 180-4) as the loader checks it (sha2 0.10 in the reference). */
 int myl_sha256(const void* data, size_t len, uint8_t* out);
+
+/* --- Pipeline wire format (INTEGER_LLM/pipeline/src/codec.rs) -----------------------
+ * Frames carry a stage's int16 activations (or packed token ids) between
+ * pipeline stages: "IINTPIPE", nine little-endian u64 fields, the CRC-32
+ * (crc32fast 1.3: reflected 0xEDB88320, init and final XOR 0xFFFFFFFF) of the
+ * payload, the payload (int16 little-endian) and zero padding to a multiple of
+ * 8 bytes (codec.rs:86-111). Decoding rejects, as decode_message does
+ * (codec.rs:113-178), a buffer shorter than the header, a wrong magic, a
+ * payload length that overflows or runs past the buffer, a CRC mismatch and an
+ * odd payload length, each with MYL_ERR_CORRUPT. The encoder writes
+ * payload_len = 2 * n whatever meta->payload_len holds, as encode_message does.
+ * The _dev forms keep the payload in device memory and compute its CRC on the
+ * GPU (they synchronise the stream to report the result). */
+#define MYL_WIRE_HEADER_BYTES 84
+#define MYL_WIRE_FLAG_STARTS_GENERATION 0x1ull
+#define MYL_WIRE_FLAG_ABORT 0x2ull
+#define MYL_WIRE_FLAG_TOKEN_INPUT 0x4ull
+typedef struct myl_wire_meta {
+  uint64_t version, theta_v_hash, request_id, sequence_id, stage_id, token_position;
+  uint64_t payload_len, flags, reserved;
+  uint32_t crc;
+} myl_wire_meta;
+/* Frame size in bytes for n int16 values (header + payload + padding). */
+uint64_t myl_wire_frame_bytes(uint64_t n_values);
+uint32_t myl_crc32(const void* data, uint64_t len);
+int myl_wire_encode(const myl_wire_meta* meta, const int16_t* values, uint64_t n, uint8_t* out,
+                    uint64_t cap, uint64_t* out_len);
+/* values may be NULL with cap 0 to learn n; a payload larger than cap values
+ * is MYL_ERR_SHAPE. */
+int myl_wire_decode(const uint8_t* buf, uint64_t len, myl_wire_meta* meta, int16_t* values,
+                    uint64_t cap, uint64_t* n);
+/* CRC-32 of len bytes at a device pointer. */
+int myl_crc32_dev(myl_ctx* ctx, const void* data, uint64_t len, uint32_t* crc, void* stream);
+/* Header checks on the host, the payload copied once into dev_values, its CRC
+ * checked on the GPU. */
+int myl_wire_decode_dev(myl_ctx* ctx, const uint8_t* buf, uint64_t len, myl_wire_meta* meta,
+                        int16_t* dev_values, uint64_t cap, uint64_t* n, void* stream);
+/* Frame from n int16 values at a device pointer: CRC on the GPU, payload
+ * copied once into the host frame. */
+int myl_wire_encode_dev(myl_ctx* ctx, const myl_wire_meta* meta, const int16_t* dev_values,
+                        uint64_t n, uint8_t* out, uint64_t cap, uint64_t* out_len, void* stream);
+/* Token ids as the payload of a FLAG_TOKEN_INPUT frame (codec.rs:38-63): two
+ * int16 per id (low half, high half); unpacking an odd count is MYL_ERR_SHAPE. */
+int myl_wire_pack_tokens(const uint32_t* tokens, uint64_t n, int16_t* out);
+int myl_wire_unpack_tokens(const int16_t* values, uint64_t n_values, uint32_t* tokens);
 
 /* --- Allocation-free variant ------------------------------------------------------
  * No counterpart in the reference: its CPU path never allocates device memory.

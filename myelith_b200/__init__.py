@@ -111,6 +111,16 @@ def load_library(path: str | None = None):
             "myl_launch_count": ([vp], i64),
             "myl_set_sm_limit": ([vp, i32], i32),
             "myl_set_tc_options": ([vp, i32, i32], i32),
+            "myl_argmax_keys_dev": ([vp, vp, i64, i64, i64, i64, vp, vp], i32),
+            "myl_wire_frame_bytes": ([C.c_uint64], C.c_uint64),
+            "myl_crc32": ([vp, C.c_uint64], C.c_uint32),
+            "myl_wire_encode": ([vp, vp, C.c_uint64, vp, C.c_uint64, C.POINTER(C.c_uint64)], i32),
+            "myl_wire_decode": ([vp, C.c_uint64, vp, vp, C.c_uint64, C.POINTER(C.c_uint64)], i32),
+            "myl_crc32_dev": ([vp, vp, C.c_uint64, C.POINTER(C.c_uint32), vp], i32),
+            "myl_wire_decode_dev": ([vp, vp, C.c_uint64, vp, vp, C.c_uint64, C.POINTER(C.c_uint64), vp], i32),
+            "myl_wire_encode_dev": ([vp, vp, vp, C.c_uint64, vp, C.c_uint64, C.POINTER(C.c_uint64), vp], i32),
+            "myl_wire_pack_tokens": ([vp, C.c_uint64, vp], i32),
+            "myl_wire_unpack_tokens": ([vp, C.c_uint64, vp], i32),
             "myl_debug_inject_wait_fault": ([vp, i32], i32),
             "myl_weight16_register": ([vp, vp, i64, i64, i64, vp, C.POINTER(vp)], i32),
             "myl_linear_backward": ([vp, vp, vp, vp, i64, u8, u8, vp, vp], i32),
@@ -202,6 +212,43 @@ class Context:
     def set_sm_limit(self, max_sms: int) -> None:
         """Persistent kernels use at most max_sms SMs (0: all)."""
         _check("myl_set_sm_limit", load_library().myl_set_sm_limit(self._h, max_sms))
+
+    def crc32_dev(self, data, stream=None) -> int:
+        """CRC-32 (crc32fast / zlib) of a torch CUDA tensor's bytes, on the GPU."""
+        out = C.c_uint32()
+        _check("myl_crc32_dev", load_library().myl_crc32_dev(
+            self._h, _p(data), data.numel() * data.element_size(), C.byref(out), _stream_ptr(stream)))
+        return out.value
+
+    def wire_decode_dev(self, frame: bytes, values, stream=None) -> tuple[dict, int]:
+        """Decodes an IINTPIPE frame into the int16 CUDA tensor values (payload
+        CRC checked on the GPU); returns (meta, number of values)."""
+        m = WireMeta()
+        n = C.c_uint64()
+        buf = np.frombuffer(frame, np.uint8)
+        _check("myl_wire_decode_dev", load_library().myl_wire_decode_dev(
+            self._h, _p(buf), buf.size, C.byref(m), _p(values), values.numel(), C.byref(n),
+            _stream_ptr(stream)))
+        return m.as_dict(), n.value
+
+    def wire_encode_dev(self, meta: dict, values, stream=None) -> bytes:
+        """IINTPIPE frame of the int16 CUDA tensor values (CRC on the GPU)."""
+        n = values.numel()
+        out = np.zeros(load_library().myl_wire_frame_bytes(n), np.uint8)
+        ln = C.c_uint64()
+        m = WireMeta.from_dict(meta)
+        _check("myl_wire_encode_dev", load_library().myl_wire_encode_dev(
+            self._h, C.byref(m), _p(values), n, _p(out), out.size, C.byref(ln), _stream_ptr(stream)))
+        return out[: ln.value].tobytes()
+
+    def argmax_keys_dev(self, logits, keys, index_base: int = 0, stream=None) -> None:
+        """keys[M] int64 = greedy selection keys of int32 logits [M, V] (torch
+        CUDA tensors) whose column j is vocab index index_base + j; see
+        keys_to_tokens."""
+        M, V = (logits.shape[0], logits.shape[1]) if logits.dim() == 2 else (1, logits.shape[0])
+        ld = logits.stride(0) if logits.dim() == 2 else V
+        _check("myl_argmax_keys_dev", load_library().myl_argmax_keys_dev(
+            self._h, _p(logits), M, V, ld, index_base, _p(keys), _stream_ptr(stream)))
 
     def set_tc_options(self, pair: bool = True, xbox_rows: int = 0) -> None:
         """Tensor-core GEMM variant: CTA pairs for 128-token tiles (default) or
@@ -699,6 +746,92 @@ class Artifact:
         if n.value == 0:
             return np.zeros(0, np.int16)
         return np.ctypeslib.as_array((C.c_int16 * n.value).from_address(data.value)).copy()
+
+
+WIRE_HEADER_BYTES = 84
+WIRE_FLAG_STARTS_GENERATION = 0x1
+WIRE_FLAG_ABORT = 0x2
+WIRE_FLAG_TOKEN_INPUT = 0x4
+_WIRE_FIELDS = ("version", "theta_v_hash", "request_id", "sequence_id", "stage_id",
+                "token_position", "payload_len", "flags", "reserved")
+
+
+class WireMeta(C.Structure):
+    """myl_wire_meta: the header fields of a pipeline frame (codec.rs:15-29)."""
+
+    _fields_ = [(f, C.c_uint64) for f in _WIRE_FIELDS] + [("crc", C.c_uint32)]
+
+    def as_dict(self) -> dict:
+        return {f: getattr(self, f) for f in _WIRE_FIELDS + ("crc",)}
+
+    @classmethod
+    def from_dict(cls, d: dict) -> "WireMeta":
+        m = cls()
+        for f in _WIRE_FIELDS + ("crc",):
+            setattr(m, f, int(d.get(f, 0)))
+        return m
+
+
+def crc32(data) -> int:
+    """CRC-32 of bytes (host)."""
+    b = np.frombuffer(bytes(data), np.uint8)
+    return int(load_library().myl_crc32(_p(b) if b.size else None, b.size))
+
+
+def wire_encode(meta: dict, values) -> bytes:
+    """encode_message (codec.rs:86-111): the frame of int16 values."""
+    v = _c(np.asarray(values).reshape(-1), np.int16)
+    out = np.zeros(load_library().myl_wire_frame_bytes(v.size), np.uint8)
+    ln = C.c_uint64()
+    m = WireMeta.from_dict(meta)
+    _check("myl_wire_encode", load_library().myl_wire_encode(
+        C.byref(m), _p(v) if v.size else None, v.size, _p(out), out.size, C.byref(ln)))
+    return out[: ln.value].tobytes()
+
+
+def wire_decode(frame: bytes) -> tuple[dict, np.ndarray]:
+    """decode_message (codec.rs:113-178): (meta, int16 values); malformed
+    frames raise MylError with MYL_ERR_CORRUPT."""
+    buf = np.frombuffer(bytes(frame), np.uint8)
+    m = WireMeta()
+    n = C.c_uint64()
+    L = load_library()
+    _check("myl_wire_decode", L.myl_wire_decode(_p(buf) if buf.size else None, buf.size,
+                                                C.byref(m), None, 0, C.byref(n)))
+    v = np.zeros(n.value, np.int16)
+    _check("myl_wire_decode", L.myl_wire_decode(_p(buf), buf.size, C.byref(m),
+                                                _p(v) if v.size else None, v.size, C.byref(n)))
+    return m.as_dict(), v
+
+
+def pack_tokens(tokens) -> np.ndarray:
+    """Token ids as int16 payload values (codec.rs:38-47)."""
+    t = _c(np.asarray(tokens, dtype=np.uint64).astype(np.uint32), np.uint32)
+    out = np.zeros(2 * t.size, np.int16)
+    _check("myl_wire_pack_tokens", load_library().myl_wire_pack_tokens(
+        _p(t) if t.size else None, t.size, _p(out) if out.size else None))
+    return out
+
+
+def unpack_tokens(values) -> np.ndarray:
+    """Inverse of pack_tokens (codec.rs:49-63); an odd count raises."""
+    v = _c(np.asarray(values).reshape(-1), np.int16)
+    out = np.zeros(v.size // 2, np.uint32)
+    _check("myl_wire_unpack_tokens", load_library().myl_wire_unpack_tokens(
+        _p(v) if v.size else None, v.size, _p(out) if out.size else None))
+    return out
+
+
+def selection_key(logit: int, index: int) -> int:
+    """The key myl_argmax_keys_dev gives logit at vocab index: larger logit
+    first, then the lower index (argmax_int, sampling.rs:8-18)."""
+    return int(logit) * (1 << 32) + (0xFFFFFFFF - int(index))
+
+
+def keys_to_tokens(keys):
+    """(token ids, winning logits) of selection keys (numpy or torch int64)."""
+    low = keys & 0xFFFFFFFF
+    return 0xFFFFFFFF - low, keys >> 32
 
 
 def _stream_ptr(stream) -> int | None:

@@ -14,7 +14,8 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libmyl_w8a16.so")
 SOURCES = ["myl_w8a16.cu"]
-HEADERS = ["common.cuh", "gemv.cuh", "gemm_tc.cuh", "moe.cuh", "backward.cuh", "artifact.hpp"]
+HEADERS = ["common.cuh", "gemv.cuh", "gemm_tc.cuh", "moe.cuh", "backward.cuh", "select.cuh",
+           "wire.cuh", "artifact.hpp"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -32,6 +32,8 @@
 #include "gemv.cuh"
 #include "moe.cuh"
 #include "backward.cuh"
+#include "select.cuh"
+#include "wire.cuh"
 
 using namespace myl;
 
@@ -128,7 +130,7 @@ struct myl_ctx {
   int pair_slots = 0;  // co-resident CTA pairs of the pair kernel (0: not yet queried)
   int64_t launches = 0;
   PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-  DevBuf x, y, rq, planes, part, h, hplanes, moe, xsum;
+  DevBuf x, y, rq, planes, part, h, hplanes, moe, xsum, crc;
   // Host-pointer calls on page-locked memory: copy-in and copy-out streams
   // and one event pair per chunk.
   cudaStream_t s_in = nullptr, s_out = nullptr;
@@ -791,7 +793,7 @@ int myl_destroy(myl_ctx* ctx) {
   for (auto& kv : ctx->backend_cache) myl_weight_release(ctx, kv.second);
   ctx->backend_cache.clear();
   for (DevBuf* b : {&ctx->x, &ctx->y, &ctx->rq, &ctx->planes, &ctx->part, &ctx->h, &ctx->hplanes,
-                    &ctx->moe, &ctx->xsum})
+                    &ctx->moe, &ctx->xsum, &ctx->crc})
     if (b->p) cudaFree(b->p);
   if (ctx->d_err) cudaFree(ctx->d_err);
   if (ctx->h_err) cudaFreeHost(ctx->h_err);
@@ -950,6 +952,27 @@ int myl_lm_head_w16a16_i32(myl_ctx* ctx, const myl_weight* w, const int16_t* x, 
   std::vector<int8_t> s;
   TRY(shift_plan(w, final_norm_frac, &logit_frac, 0, s));
   return host_linear(ctx, w, x, M, EPI_SHIFT, 1, s.data(), nullptr, logits);
+}
+
+int myl_argmax_keys_dev(myl_ctx* ctx, const int32_t* logits, int64_t M, int64_t V, int64_t ld,
+                        int64_t index_base, int64_t* keys, void* stream) {
+  if (!ctx || (M > 0 && (!keys || (V > 0 && !logits)))) return fail(MYL_ERR_ARG, "null argument");
+  if (M < 0 || V < 0 || (M > 0 && V > 0 && ld < V) || index_base < 0 ||
+      index_base + V > (int64_t(1) << 32))
+    return fail(MYL_ERR_SHAPE, "bad M/V/ld/index_base");
+  if (M == 0) return MYL_OK;
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  select_init_kernel<<<unsigned(std::min<int64_t>((M + 255) / 256, 1024)), 256, 0, st>>>(keys, M);
+  CUDA_TRY(cudaGetLastError());
+  ctx->launches++;
+  if (V == 0) return MYL_OK;
+  const dim3 grid(unsigned((V + SELECT_CHUNK - 1) / SELECT_CHUNK),
+                  unsigned(std::min<int64_t>(M, 65535)));
+  select_keys_kernel<<<grid, SELECT_THREADS, 0, st>>>(logits, M, V, ld, index_base, keys);
+  CUDA_TRY(cudaGetLastError());
+  ctx->launches++;
+  return MYL_OK;
 }
 
 int myl_linear_w8a16_mult(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
@@ -2261,6 +2284,221 @@ int myl_artifact_lut(const myl_artifact* a, const char* name, const int16_t** da
   if (it == a->luts.end()) return fail(MYL_ERR_ARG, "no table '%s' in luts.json", name);
   *data = it->second.data();
   *len = int64_t(it->second.size());
+  return MYL_OK;
+}
+
+}  // extern "C"
+
+// ---- pipeline wire format (codec.rs) ------------------------------------------
+namespace {
+
+const CrcTables& crc_tables() {
+  static const CrcTables t = [] {
+    CrcTables v;
+    crc_tables_host(&v);
+    return v;
+  }();
+  return t;
+}
+
+bool host_little_endian() {
+  const uint16_t one = 1;
+  uint8_t b;
+  std::memcpy(&b, &one, 1);
+  return b == 1;
+}
+
+// decode_message's checks up to the payload bounds (codec.rs:113-157).
+int wire_header(const uint8_t* buf, uint64_t len, myl_wire_meta* m) {
+  if (len < WIRE_HEADER)
+    return fail(MYL_ERR_CORRUPT, "buffer too small: %llu < %llu", (unsigned long long)len,
+                (unsigned long long)WIRE_HEADER);
+  if (std::memcmp(buf, "IINTPIPE", 8) != 0) return fail(MYL_ERR_CORRUPT, "bad magic");
+  uint64_t f[9];
+  for (int i = 0; i < 9; ++i) f[i] = wire_get_u64(buf + 8 + 8 * i);
+  m->version = f[0];
+  m->theta_v_hash = f[1];
+  m->request_id = f[2];
+  m->sequence_id = f[3];
+  m->stage_id = f[4];
+  m->token_position = f[5];
+  m->payload_len = f[6];
+  m->flags = f[7];
+  m->reserved = f[8];
+  m->crc = uint32_t(buf[80]) | (uint32_t(buf[81]) << 8) | (uint32_t(buf[82]) << 16) |
+           (uint32_t(buf[83]) << 24);
+  if (m->payload_len > len - WIRE_HEADER)  // also catches offsets that would overflow
+    return fail(MYL_ERR_CORRUPT, "payload of %llu bytes runs past the buffer (%llu bytes)",
+                (unsigned long long)m->payload_len, (unsigned long long)len);
+  return MYL_OK;
+}
+
+void wire_write_header(const myl_wire_meta* meta, uint64_t payload_len, uint32_t crc, uint8_t* out) {
+  std::memcpy(out, "IINTPIPE", 8);
+  const uint64_t f[9] = {meta->version, meta->theta_v_hash, meta->request_id, meta->sequence_id,
+                         meta->stage_id, meta->token_position, payload_len, meta->flags,
+                         meta->reserved};
+  for (int i = 0; i < 9; ++i) wire_put_u64(out + 8 + 8 * i, f[i]);
+  for (int i = 0; i < 4; ++i) out[80 + i] = uint8_t(crc >> (8 * i));
+}
+
+void wire_values_to_bytes(const int16_t* v, uint64_t n, uint8_t* out) {
+  if (host_little_endian()) {
+    std::memcpy(out, v, size_t(n) * 2);
+    return;
+  }
+  for (uint64_t i = 0; i < n; ++i) {
+    out[2 * i] = uint8_t(uint16_t(v[i]) & 0xFF);
+    out[2 * i + 1] = uint8_t(uint16_t(v[i]) >> 8);
+  }
+}
+
+void wire_bytes_to_values(const uint8_t* p, uint64_t n, int16_t* v) {
+  if (host_little_endian()) {
+    std::memcpy(v, p, size_t(n) * 2);
+    return;
+  }
+  for (uint64_t i = 0; i < n; ++i) v[i] = int16_t(uint16_t(p[2 * i]) | (uint16_t(p[2 * i + 1]) << 8));
+}
+
+// CRC-32 of len device bytes (enqueued on st; synchronises st).
+int crc32_device(myl_ctx* ctx, const uint8_t* data, uint64_t len, cudaStream_t st, uint32_t* out) {
+  if (len == 0) {
+    *out = 0;
+    return MYL_OK;
+  }
+  TRY(ensure(ctx->crc, 4));
+  uint32_t* acc = static_cast<uint32_t*>(ctx->crc.p);
+  CUDA_TRY(cudaMemsetAsync(acc, 0, 4, st));
+  const uint64_t pad = (uint64_t(CRC_BLOCK) - len % uint64_t(CRC_BLOCK)) % uint64_t(CRC_BLOCK);
+  const uint64_t nblocks = (len + pad) / uint64_t(CRC_BLOCK);
+  const unsigned grid = unsigned(std::min<uint64_t>(nblocks, uint64_t(ctx->num_sms) * 8));
+  crc32_blocks_kernel<<<grid, CRC_THREADS, 0, st>>>(data, len, pad, nblocks, crc_tables(), acc);
+  CUDA_TRY(cudaGetLastError());
+  ctx->launches++;
+  uint32_t raw = 0;
+  CUDA_TRY(cudaMemcpyAsync(&raw, acc, 4, cudaMemcpyDeviceToHost, st));
+  CUDA_TRY(cudaStreamSynchronize(st));
+  *out = raw ^ gf2_mulmod(0xFFFFFFFFu, gf2_x8n(len)) ^ 0xFFFFFFFFu;
+  return MYL_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+uint64_t myl_wire_frame_bytes(uint64_t n_values) { return wire_frame_bytes(n_values); }
+
+uint32_t myl_crc32(const void* data, uint64_t len) {
+  if (!data) return 0u;
+  return crc32_host(static_cast<const uint8_t*>(data), len);
+}
+
+int myl_wire_encode(const myl_wire_meta* meta, const int16_t* values, uint64_t n, uint8_t* out,
+                    uint64_t cap, uint64_t* out_len) {
+  if (!meta || (n && !values) || !out_len) return fail(MYL_ERR_ARG, "null argument");
+  if (n > (uint64_t(1) << 60)) return fail(MYL_ERR_SHAPE, "payload too large");
+  const uint64_t need = wire_frame_bytes(n);
+  *out_len = need;
+  if (cap < need || !out)
+    return fail(MYL_ERR_SHAPE, "frame needs %llu bytes, buffer holds %llu",
+                (unsigned long long)need, (unsigned long long)cap);
+  wire_values_to_bytes(values, n, out + WIRE_HEADER);
+  const uint32_t crc = crc32_host(out + WIRE_HEADER, 2 * n);
+  wire_write_header(meta, 2 * n, crc, out);
+  std::memset(out + WIRE_HEADER + 2 * n, 0, size_t(need - WIRE_HEADER - 2 * n));
+  return MYL_OK;
+}
+
+int myl_wire_decode(const uint8_t* buf, uint64_t len, myl_wire_meta* meta, int16_t* values,
+                    uint64_t cap, uint64_t* n) {
+  if ((!buf && len) || !meta || !n) return fail(MYL_ERR_ARG, "null argument");
+  myl_wire_meta m{};
+  TRY(wire_header(buf, len, &m));
+  const uint8_t* payload = buf + WIRE_HEADER;
+  const uint32_t crc = crc32_host(payload, m.payload_len);
+  if (crc != m.crc)
+    return fail(MYL_ERR_CORRUPT, "CRC mismatch: %08x != %08x", unsigned(m.crc), unsigned(crc));
+  if (m.payload_len % 2) return fail(MYL_ERR_CORRUPT, "odd payload length %llu",
+                                     (unsigned long long)m.payload_len);
+  *meta = m;
+  *n = m.payload_len / 2;
+  if (!values && cap == 0) return MYL_OK;
+  if (!values || cap < *n)
+    return fail(MYL_ERR_SHAPE, "payload has %llu values, buffer holds %llu",
+                (unsigned long long)*n, (unsigned long long)cap);
+  wire_bytes_to_values(payload, *n, values);
+  return MYL_OK;
+}
+
+int myl_crc32_dev(myl_ctx* ctx, const void* data, uint64_t len, uint32_t* crc, void* stream) {
+  if (!ctx || (len && !data) || !crc) return fail(MYL_ERR_ARG, "null argument");
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  return crc32_device(ctx, static_cast<const uint8_t*>(data), len,
+                      static_cast<cudaStream_t>(stream), crc);
+}
+
+int myl_wire_decode_dev(myl_ctx* ctx, const uint8_t* buf, uint64_t len, myl_wire_meta* meta,
+                        int16_t* dev_values, uint64_t cap, uint64_t* n, void* stream) {
+  if (!ctx || (!buf && len) || !meta || !n) return fail(MYL_ERR_ARG, "null argument");
+  if (!host_little_endian()) return fail(MYL_ERR_UNSUPPORTED, "big-endian host");
+  myl_wire_meta m{};
+  TRY(wire_header(buf, len, &m));
+  const uint64_t nv = (m.payload_len + 1) / 2;
+  if (nv > cap || (nv && !dev_values))
+    return fail(MYL_ERR_SHAPE, "payload has %llu values, buffer holds %llu",
+                (unsigned long long)nv, (unsigned long long)cap);
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (m.payload_len)
+    CUDA_TRY(cudaMemcpyAsync(dev_values, buf + WIRE_HEADER, size_t(m.payload_len),
+                             cudaMemcpyHostToDevice, st));
+  uint32_t crc = 0;
+  TRY(crc32_device(ctx, reinterpret_cast<const uint8_t*>(dev_values), m.payload_len, st, &crc));
+  if (crc != m.crc)
+    return fail(MYL_ERR_CORRUPT, "CRC mismatch: %08x != %08x", unsigned(m.crc), unsigned(crc));
+  if (m.payload_len % 2) return fail(MYL_ERR_CORRUPT, "odd payload length %llu",
+                                     (unsigned long long)m.payload_len);
+  *meta = m;
+  *n = m.payload_len / 2;
+  return MYL_OK;
+}
+
+int myl_wire_encode_dev(myl_ctx* ctx, const myl_wire_meta* meta, const int16_t* dev_values,
+                        uint64_t n, uint8_t* out, uint64_t cap, uint64_t* out_len, void* stream) {
+  if (!ctx || !meta || (n && !dev_values) || !out_len) return fail(MYL_ERR_ARG, "null argument");
+  if (!host_little_endian()) return fail(MYL_ERR_UNSUPPORTED, "big-endian host");
+  if (n > (uint64_t(1) << 60)) return fail(MYL_ERR_SHAPE, "payload too large");
+  const uint64_t need = wire_frame_bytes(n);
+  *out_len = need;
+  if (cap < need || !out)
+    return fail(MYL_ERR_SHAPE, "frame needs %llu bytes, buffer holds %llu",
+                (unsigned long long)need, (unsigned long long)cap);
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (n)
+    CUDA_TRY(cudaMemcpyAsync(out + WIRE_HEADER, dev_values, size_t(2 * n), cudaMemcpyDeviceToHost, st));
+  uint32_t crc = 0;
+  TRY(crc32_device(ctx, reinterpret_cast<const uint8_t*>(dev_values), 2 * n, st, &crc));
+  wire_write_header(meta, 2 * n, crc, out);
+  std::memset(out + WIRE_HEADER + 2 * n, 0, size_t(need - WIRE_HEADER - 2 * n));
+  return MYL_OK;
+}
+
+int myl_wire_pack_tokens(const uint32_t* tokens, uint64_t n, int16_t* out) {
+  if ((n && (!tokens || !out))) return fail(MYL_ERR_ARG, "null argument");
+  for (uint64_t i = 0; i < n; ++i) {
+    out[2 * i] = int16_t(uint16_t(tokens[i] & 0xFFFFu));
+    out[2 * i + 1] = int16_t(uint16_t(tokens[i] >> 16));
+  }
+  return MYL_OK;
+}
+
+int myl_wire_unpack_tokens(const int16_t* values, uint64_t n_values, uint32_t* tokens) {
+  if (n_values % 2) return fail(MYL_ERR_SHAPE, "token payload needs an even number of int16");
+  if (n_values && (!values || !tokens)) return fail(MYL_ERR_ARG, "null argument");
+  for (uint64_t i = 0; i < n_values / 2; ++i)
+    tokens[i] = uint32_t(uint16_t(values[2 * i])) | (uint32_t(uint16_t(values[2 * i + 1])) << 16);
   return MYL_OK;
 }
 

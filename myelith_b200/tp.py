@@ -15,6 +15,11 @@ exact integer:
                    the very end requires (fixed_point.rs:184-191);
   MLP              gate/up column-parallel and down row-parallel over the same
                    intermediate channels, so h never leaves its rank.
+  LM head          vocab-parallel (column-parallel over vocab rows); greedy
+                   selection needs no logits exchange: each rank reduces its
+                   logits to one int64 key per token (logit, then lowest
+                   index; argmax_int, sampling.rs:8-18) and one int64 MAX
+                   all-reduce gives the global token.
 
 int32 is not wide enough for the partial sums (up to ~1e10 for 7B shapes).
 
@@ -58,6 +63,15 @@ class Local:
         raise NotImplementedError
 
     def requant(self, key, acc):  # requant of summed int64 accumulators
+        raise NotImplementedError
+
+    def add_lm_head(self, key, W, in_features, w_shifts, final_norm_frac, logit_frac):
+        raise NotImplementedError
+
+    def lm_head_logits(self, key, x):  # int32 logits of a vocab shard
+        raise NotImplementedError
+
+    def lm_head_keys(self, key, x, index_base):  # int64 selection key per token
         raise NotImplementedError
 
 
@@ -123,6 +137,25 @@ class LibLocal(Local):
         else:
             self.plans[key].apply_acc_dev(acc, y)
         return y
+
+    def add_lm_head(self, key, W, in_features, w_shifts, final_norm_frac, logit_frac):
+        import myelith_b200 as myl
+
+        w = myl.Weight(self.ctx, W, in_features, w_shifts)
+        self.weights[key] = w
+        self.plans[key] = w.requant(myl.RQ_SHIFT_I32, final_norm_frac, logit_frac)
+
+    def lm_head_logits(self, key, x):
+        w = self.weights[key]
+        y = self.torch.empty((x.shape[0], w.out_features), dtype=self.torch.int32, device=x.device)
+        w.linear_dev(self.plans[key], x, y)
+        return y
+
+    def lm_head_keys(self, key, x, index_base):
+        logits = self.lm_head_logits(key, x)
+        keys = self.torch.empty((x.shape[0],), dtype=self.torch.int64, device=x.device)
+        self.ctx.argmax_keys_dev(logits, keys, index_base)
+        return keys
 
 
 class ColumnParallelLinear:
@@ -200,6 +233,33 @@ class RowParallelLinear:
         if self.world > 1:
             dist.all_reduce(acc, op=dist.ReduceOp.SUM, group=self.group)
         return self.local.requant(self.key, acc)
+
+
+class VocabParallelLMHead:
+    """LM head path B (runtime/src/model.rs:297-307) with the vocab rows
+    sharded over the ranks; greedy() returns the global argmax_int token of
+    every row of x (and its logit) from one int64 MAX all-reduce."""
+
+    def __init__(self, local: Local, key, W, w_shifts, final_norm_frac: int, logit_frac: int,
+                 rank: int, world: int, group=None):
+        V, K = W.shape
+        self.lo, self.hi = shard_range(V, rank, world)
+        self.local, self.key, self.group, self.world = local, key, group, world
+        local.add_lm_head(key, np.ascontiguousarray(W[self.lo:self.hi]), K,
+                          np.asarray(w_shifts)[self.lo:self.hi], final_norm_frac, logit_frac)
+
+    def logits(self, x):
+        """int32 logits of this rank's vocab rows [lo, hi)."""
+        return self.local.lm_head_logits(self.key, x)
+
+    def greedy(self, x):
+        """(tokens int64 [M], logits int64 [M]) of the whole vocab."""
+        import torch.distributed as dist
+
+        keys = self.local.lm_head_keys(self.key, x, self.lo)
+        if self.world > 1:
+            dist.all_reduce(keys, op=dist.ReduceOp.MAX, group=self.group)
+        return (0xFFFFFFFF - (keys & 0xFFFFFFFF)), keys >> 32
 
 
 def overlapped_row_parallel(compute_acc, requant, M: int, N: int, world: int, group=None,

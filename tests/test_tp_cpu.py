@@ -19,7 +19,7 @@ import torch.multiprocessing as mp
 import gen
 import oracle as O
 from make_golden import silu_lut_spec
-from myelith_b200 import tp
+from myelith_b200 import selection_key, tp
 
 
 def rne_shift_np(acc, s):
@@ -74,6 +74,21 @@ class OracleLocal(tp.Local):
         return torch.from_numpy(np.clip(rne_shift_np(acc.numpy(), s[None, :]), -32768, 32767)
                                 .astype(np.int16))
 
+    def add_lm_head(self, key, W, in_features, w_shifts, final_norm_frac, logit_frac):
+        self.lin[key] = (np.asarray(W, np.int8), in_features, np.asarray(w_shifts, np.uint8),
+                         final_norm_frac, logit_frac)
+
+    def lm_head_logits(self, key, x):
+        W, K, ws, nf, lf = self.lin[key]
+        return torch.from_numpy(O.lm_head_w8a16_i32(x.numpy(), W.reshape(-1), K, ws, nf, lf))
+
+    def lm_head_keys(self, key, x, index_base):
+        logits = self.lm_head_logits(key, x).numpy()
+        if logits.shape[1] == 0:
+            return torch.full((logits.shape[0],), -(2**63), dtype=torch.int64)
+        keys = [selection_key(int(r.max()), index_base + O.argmax_int(r)) for r in logits]
+        return torch.tensor(keys, dtype=torch.int64)
+
 
 def _problem(seed=3):
     rng = np.random.default_rng(seed)
@@ -95,6 +110,18 @@ def _problem(seed=3):
                out_frac=rng.integers(3, 7, size=H).astype(np.uint8))
     xm = rng.integers(-3000, 3000, size=(M, H), dtype=np.int16)
     return W, ws, of, x, mlp, xm
+
+
+def _lm_head_problem(seed=4):
+    """Vocab 41 (uneven shards) whose second half repeats rows of the first, so
+    the maximum of a token often sits in two shards: the lower index wins."""
+    rng = np.random.default_rng(seed)
+    V, K, M = 41, 19, 6
+    W = rng.integers(-8, 8, size=(V, K), dtype=np.int8)
+    W[21:] = W[:20]
+    ws = np.full(V, 3, np.uint8)
+    x = rng.integers(-40, 40, size=(M, K), dtype=np.int16)
+    return W, ws, x
 
 
 def _worker(rank, world, port, results):
@@ -123,8 +150,16 @@ def _worker(rank, world, port, results):
                             mlp["down_w_shifts"], mlp["silu_lut"], mlp["in_frac"], mlp["gate_out_frac"],
                             mlp["up_out_frac"], mlp["down_in_frac"], mlp["silu_in_frac"],
                             mlp["silu_lut_offset"], mlp["silu_out_frac"], mlp["out_frac"])
+        # vocab-parallel greedy selection: one int64 MAX all-reduce
+        Wl, wsl, xl = _lm_head_problem()
+        head = tp.VocabParallelLMHead(local, "head", Wl, wsl, 2, 1, rank, world)
+        tok, best = head.greedy(torch.from_numpy(xl))
+        full = O.lm_head_w8a16_i32(xl, Wl.reshape(-1), Wl.shape[1], wsl, 2, 1)
+        ref_tok = [O.argmax_int(r) for r in full]
+        head_ok = tok.tolist() == ref_tok and best.tolist() == [int(r.max()) for r in full]
         results[rank] = (bool(np.array_equal(y_col, ref)), bool(np.array_equal(y_row, ref) and ov_ok),
-                         bool(np.array_equal(y_mlp, ref_mlp)), (col.lo, col.hi), (row.lo, row.hi))
+                         bool(np.array_equal(y_mlp, ref_mlp) and head_ok), (col.lo, col.hi),
+                         (row.lo, row.hi))
     finally:
         dist.destroy_process_group()
 
@@ -147,7 +182,7 @@ def test_tensor_parallel_layers_gloo(world):
     for rank, (col_ok, row_ok, mlp_ok, _, _) in res.items():
         assert col_ok, f"rank {rank}: column-parallel output differs"
         assert row_ok, f"rank {rank}: row-parallel output differs"
-        assert mlp_ok, f"rank {rank}: parallel MLP output differs"
+        assert mlp_ok, f"rank {rank}: parallel MLP or vocab-parallel greedy output differs"
     # shards tile the dimension exactly
     cols = sorted(r[3] for r in res.values())
     assert cols[0][0] == 0 and cols[-1][1] == 33 and all(a[1] == b[0] for a, b in zip(cols, cols[1:]))

@@ -57,8 +57,14 @@ def main():
                    out_frac=rng.integers(3, 7, size=H).astype(np.uint8))
         xm = np.clip(np.rint(rng.normal(0, 1500, size=(M, H))), -32767, 32767).astype(np.int16)
 
+        V = 5003  # vocab-parallel LM head: uneven shards, a repeated half for cross-shard ties
+        Wl = rng.integers(-127, 128, size=(V, K), dtype=np.int8)
+        Wl[2502:5002] = Wl[:2500]
+        wsl = rng.integers(12, 14, size=V).astype(np.uint8)
+
         local = tp.LibLocal(ctx)
         spec = tp.LinearSpec(W, ws, 8, of)
+        head = tp.VocabParallelLMHead(local, "head", Wl, wsl, 8, 6, rank, world)
         col = tp.ColumnParallelLinear(local, "col", spec, rank, world)
         row = tp.RowParallelLinear(local, "row", spec, rank, world)
         pm = tp.ParallelMlp(local, "mlp", hidden=H, intermediate=I, rank=rank, world=world, **mlp)
@@ -74,9 +80,13 @@ def main():
                                  mlp["gate_w_shifts"], mlp["up_w_shifts"], mlp["down_w_shifts"],
                                  mlp["silu_lut"], 8, 7, 7, 7, 6, 8192, 8, mlp["out_frac"])(xm[:Ms])
             ref = O.linear_w8a16_pc(x[:Ms], W.reshape(-1), K, ws, 8, of)
+            tok, best = head.greedy(xt[:Ms])
+            logits = ctx.weight(Wl, K, wsl).lm_head(x[:Ms], 8, 6)
             ok = dict(col=bool(np.array_equal(y_col, single)), row=bool(np.array_equal(y_row, single)),
                       overlapped=bool(np.array_equal(y_ov, single)),
-                      mlp=bool(np.array_equal(y_mlp, single_mlp)), oracle=bool(np.array_equal(single, ref)))
+                      mlp=bool(np.array_equal(y_mlp, single_mlp)), oracle=bool(np.array_equal(single, ref)),
+                      greedy=tok.cpu().tolist() == [O.argmax_int(r) for r in logits]
+                      and best.cpu().tolist() == [int(r.max()) for r in logits])
             # every rank holds the same bytes
             h = torch.tensor([int(np.frombuffer(y_mlp.tobytes(), np.uint8).astype(np.int64).sum()),
                               int(np.frombuffer(y_row.tobytes(), np.uint8).astype(np.int64).sum())],
