@@ -270,7 +270,7 @@ def run_reference(args, rank: int, world: int) -> None:
         "note": "CPU restatement of the reference's Rust loop (dot_scalar + rescale_i64 + clamp), "
                 "OpenMP over output rows; the Rust crate cannot be built in this image",
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ---------------------------------------------------------------------------------------
@@ -364,7 +364,28 @@ def bench_moe(ctx, dev, stream, rank: int, world: int, local: int, steps: int, w
 # GPU arm
 
 
+_JSON_FD = None
+
+
+def emit(line: dict) -> None:
+    """Prints the one JSON line on the process's real stdout (everything else
+    that reaches file descriptor 1, e.g. NCCL's version banner, goes to
+    stderr; see main)."""
+    s = (json.dumps(line) + "\n").encode()
+    if _JSON_FD is None:
+        sys.stdout.write(s.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_JSON_FD, s)
+
+
 def main() -> None:
+    global _JSON_FD
+    # Native libraries print to file descriptor 1 (NCCL's banner on rank 0):
+    # point it at stderr and keep the real stdout for the JSON line alone.
+    sys.stdout.flush()
+    _JSON_FD = os.dup(1)
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
@@ -737,7 +758,7 @@ def main() -> None:
             "moe": moe,
             "tp_check": tp_check,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         dist.destroy_process_group()
 
