@@ -396,7 +396,10 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-moe", action="store_true")
     ap.add_argument("--sm-reserve", type=int, default=16,
-                    help="N>1: SMs left free for the overlapped collectives")
+                    help="N>1 with --exchange nccl: SMs left free for the overlapped collectives")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="N>1: row-parallel exchange through peer memory from the GEMM epilogue "
+                         "(p2p) or NCCL reduce-scatter + all-gather overlapped with the gate/up GEMM")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -539,25 +542,61 @@ def main() -> None:
             gemm_events.append((ev["e0"], ev["e1"]))
             gemm_events.append((e2, ev["e3"]))
 
+    # Tensor-parallel step with the peer-memory exchange: the down projection's
+    # GEMM stores its int64 partial rows into the owning ranks' receive
+    # buffers (NVLink) from its epilogue; gate/up computes before the ranks
+    # synchronise; then each rank sums and requantises its rows and writes
+    # them into every rank's output (tp.PeerExchange).
+    xchg = None
+    p2p_out: dict = {}
+    if tp > 1 and args.exchange == "p2p":
+        from myelith_b200.tp import PeerExchange
+
+        with torch.cuda.stream(stream):
+            xchg = PeerExchange(ctx, M, N2, rank, world)
+
+    def step_p2p(i: int, record: bool) -> None:
+        s = i % nsets
+        ev = {}
+
+        def gate_up():
+            ctx.split_hilo_dev(x1, p1h, p1l, stream)
+            if record:
+                ev["e0"] = torch.cuda.Event(enable_timing=True)
+                ev["e0"].record(stream)
+            W1s[s].linear_planes_dev(R1s[s], p1h, p1l, M, y1, stream)
+            if record:
+                ev["e1"] = torch.cuda.Event(enable_timing=True)
+                ev["e1"].record(stream)
+
+        p2p_out["y2"] = xchg(W2s[s], R2s[s], x2, stream, between=gate_up)  # a view, no copy
+        if record:  # the gate/up GEMM carries the same work per rank as the down GEMM
+            gemm_events.append((ev["e0"], ev["e1"]))
+
     tp_check = None
     if tp > 1:
-        # the overlapped step must equal the all-reduce step bit for bit
+        # the tensor-parallel step must equal the all-reduce step bit for bit
+        step_x = step_p2p if xchg is not None else step_tp
+        if xchg is not None:
+            ctx.set_sm_limit(0)
         with torch.cuda.stream(stream):
             step(0, False)
             ref_y2 = y2.clone()
             y2.zero_()
-            step_tp(0, False)
-            same = torch.tensor([int(torch.equal(ref_y2, y2))], dtype=torch.int32, device=dev)
+            step_x(0, False)
+            got = p2p_out.get("y2", y2)
+            same = torch.tensor([int(torch.equal(ref_y2, got))], dtype=torch.int32, device=dev)
         stream.synchronize()
         if not bool(same.item()):
-            bad = (ref_y2 != y2).any(dim=1).nonzero().flatten().tolist()
+            bad = (ref_y2 != got).any(dim=1).nonzero().flatten().tolist()
             print(f"rank {rank}: overlapped step differs in {len(bad)} rows, first {bad[:8]}",
                   file=sys.stderr, flush=True)
         dist.all_reduce(same, op=dist.ReduceOp.MIN)
         tp_check = bool(same.item())
         del ref_y2
-        ctx.set_sm_limit(max(1, ctx.num_sms - args.sm_reserve))
-        step = step_tp
+        if xchg is None:
+            ctx.set_sm_limit(max(1, ctx.num_sms - args.sm_reserve))
+        step = step_x
 
     def barrier():
         if world > 1:
@@ -736,7 +775,11 @@ def main() -> None:
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "int8xint16->int64", "data": "synthetic",
             "config": {"workload": "config1: W8A16 linear at Qwen2.5-7B MLP shapes, gate/up + down per step",
-                       "M": M, "shapes_KN": SHAPES, "parallelism": f"tp{tp}",
+                       "M": M, "shapes_KN": SHAPES,
+                       "parallelism": f"tp{tp}" if tp == 1 else
+                       f"tp{tp}, row-parallel exchange: " + ("peer memory from the GEMM epilogue"
+                                                             if xchg is not None else
+                                                             "NCCL reduce-scatter + all-gather"),
                        "l2": f"inputs larger than L2: {nsets} rotating weight sets "
                              f"({nsets * per_set / 2**20:.0f} MiB per rank)"},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(eff_peak, 1),
@@ -759,6 +802,8 @@ def main() -> None:
             "tp_check": tp_check,
         }
         emit(line)
+    if xchg is not None:
+        xchg.close()
     if world > 1:
         dist.destroy_process_group()
 

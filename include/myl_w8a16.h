@@ -165,6 +165,45 @@ int myl_linear_acc_dev(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int6
 int myl_requant_acc_dev(myl_ctx* ctx, const myl_requant* rq, const int64_t* acc, int64_t M,
                         void* y, int64_t ldy, void* stream);
 
+/* Row-parallel exchange over peer memory (one process per GPU on one node,
+ * buffers shared with myl_ipc_*), replacing the int64 all-reduce:
+ *  1. myl_linear_acc_exchange_dev: the GEMM's epilogue stores the exact int64
+ *     partial of output row m straight into the receive buffer of the rank
+ *     that owns it, o = m / rows_per_rank, as row rank * rows_per_rank +
+ *     m % rows_per_rank (dst[o]: [world * rows_per_rank][N] int64, peer
+ *     memory over NVLink). rows_per_rank is a multiple of 16 and
+ *     M <= world * rows_per_rank.
+ *  2. all ranks' step 1 finished (a barrier on the stream, e.g. a one-element
+ *     all-reduce);
+ *  3. myl_exchange_reduce_dev on every rank: sums the world slabs of its own
+ *     rows in recv, requantises (plan rq) and writes the int16/int32 rows into
+ *     every rank's output buffer out[o] ([M][ldo]) at their global row;
+ *  4. a barrier again before the outputs are read.
+ * The sums are exact integers, so the result equals the single-GPU layer bit
+ * for bit. At most 8 ranks. */
+int myl_linear_acc_exchange_dev(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
+                                int64_t ldx, int64_t* const* dst, int world, int rank,
+                                int64_t rows_per_rank, void* stream);
+int myl_exchange_reduce_dev(myl_ctx* ctx, const myl_requant* rq, const int64_t* recv, int world,
+                            int rank, int64_t rows_per_rank, int64_t M, void* const* out, int64_t ldo,
+                            void* stream);
+/* Barrier of steps 2 and 4 on the stream, without a collective library:
+ * flags[o] is rank o's array of world 64-bit flag words (peer memory, zero at
+ * allocation); this rank stores `epoch` into flags[o][rank] for every o and
+ * waits until flags[rank][o] >= epoch for every o. epoch grows by one per
+ * call on every rank. The wait is bounded (myl_set_wait_timeout_ns): a peer
+ * that does not arrive is reported as MYL_ERR_DEVICE at the next check. */
+int myl_exchange_barrier_dev(myl_ctx* ctx, unsigned long long* const* flags, int world, int rank,
+                             unsigned long long epoch, void* stream);
+/* Device buffers shared between the processes of one node: allocation with
+ * its IPC handle (MYL_IPC_HANDLE_BYTES bytes, to send to the other ranks),
+ * opening a peer's handle (not one's own), and their release. */
+#define MYL_IPC_HANDLE_BYTES 64
+int myl_ipc_alloc(myl_ctx* ctx, size_t bytes, void** ptr, void* handle);
+int myl_ipc_open(myl_ctx* ctx, const void* handle, void** ptr);
+int myl_ipc_close(myl_ctx* ctx, void* ptr);
+int myl_ipc_free(myl_ctx* ctx, void* ptr);
+
 /* Splits int16 activations into the byte planes the tensor-core GEMM reads:
  * two unsigned bytes hi = (x >> 8) + 128 (offset binary) and lo = x & 255,
  * x = 256*hi + lo - 32768; planes are [M][ldp] (ldp a multiple of 16,

@@ -112,6 +112,13 @@ def load_library(path: str | None = None):
             "myl_set_sm_limit": ([vp, i32], i32),
             "myl_set_tc_options": ([vp, i32, i32], i32),
             "myl_argmax_keys_dev": ([vp, vp, i64, i64, i64, i64, vp, vp], i32),
+            "myl_linear_acc_exchange_dev": ([vp, vp, vp, i64, i64, vp, i32, i32, i64, vp], i32),
+            "myl_exchange_reduce_dev": ([vp, vp, vp, i32, i32, i64, i64, vp, i64, vp], i32),
+            "myl_exchange_barrier_dev": ([vp, vp, i32, i32, C.c_uint64, vp], i32),
+            "myl_ipc_alloc": ([vp, C.c_size_t, C.POINTER(vp), vp], i32),
+            "myl_ipc_open": ([vp, vp, C.POINTER(vp)], i32),
+            "myl_ipc_close": ([vp, vp], i32),
+            "myl_ipc_free": ([vp, vp], i32),
             "myl_wire_frame_bytes": ([C.c_uint64], C.c_uint64),
             "myl_crc32": ([vp, C.c_uint64], C.c_uint32),
             "myl_wire_encode": ([vp, vp, C.c_uint64, vp, C.c_uint64, C.POINTER(C.c_uint64)], i32),
@@ -212,6 +219,33 @@ class Context:
     def set_sm_limit(self, max_sms: int) -> None:
         """Persistent kernels use at most max_sms SMs (0: all)."""
         _check("myl_set_sm_limit", load_library().myl_set_sm_limit(self._h, max_sms))
+
+    def ipc_alloc(self, nbytes: int) -> tuple[int, bytes]:
+        """Device buffer shareable with the other processes of the node:
+        (device pointer, IPC handle bytes)."""
+        ptr = C.c_void_p()
+        h = (C.c_uint8 * IPC_HANDLE_BYTES)()
+        _check("myl_ipc_alloc", load_library().myl_ipc_alloc(self._h, nbytes, C.byref(ptr), h))
+        return int(ptr.value), bytes(h)
+
+    def ipc_open(self, handle: bytes) -> int:
+        """Maps another process's buffer (its IPC handle) into this one."""
+        ptr = C.c_void_p()
+        h = (C.c_uint8 * IPC_HANDLE_BYTES).from_buffer_copy(handle)
+        _check("myl_ipc_open", load_library().myl_ipc_open(self._h, h, C.byref(ptr)))
+        return int(ptr.value)
+
+    def exchange_barrier_dev(self, flag_ptrs, rank: int, epoch: int, stream=None) -> None:
+        """Device-side barrier of a peer-memory exchange (myl_exchange_barrier_dev)."""
+        arr = (C.c_void_p * len(flag_ptrs))(*flag_ptrs)
+        _check("myl_exchange_barrier_dev", load_library().myl_exchange_barrier_dev(
+            self._h, arr, len(flag_ptrs), rank, epoch, _stream_ptr(stream)))
+
+    def ipc_close(self, ptr: int) -> None:
+        _check("myl_ipc_close", load_library().myl_ipc_close(self._h, C.c_void_p(ptr)))
+
+    def ipc_free(self, ptr: int) -> None:
+        _check("myl_ipc_free", load_library().myl_ipc_free(self._h, C.c_void_p(ptr)))
 
     def crc32_dev(self, data, stream=None) -> int:
         """CRC-32 (crc32fast / zlib) of a torch CUDA tensor's bytes, on the GPU."""
@@ -411,6 +445,15 @@ class Weight:
             self.ctx.handle, self._h, None if rq is None else rq.handle, _p(xhi), _p(xlo),
             xhi.stride(0), M, _p(y), y.stride(0), _stream_ptr(stream)))
 
+    def acc_exchange_dev(self, x, dst_ptrs, rank: int, rows_per_rank: int, stream=None) -> None:
+        """Exact int64 partials of W x stored into the owning ranks' receive
+        buffers (myl_linear_acc_exchange_dev; dst_ptrs: one device pointer per
+        rank)."""
+        arr = (C.c_void_p * len(dst_ptrs))(*dst_ptrs)
+        _check("myl_linear_acc_exchange_dev", load_library().myl_linear_acc_exchange_dev(
+            self.ctx.handle, self._h, _p(x), x.shape[0], x.stride(0), arr, len(dst_ptrs), rank,
+            rows_per_rank, _stream_ptr(stream)))
+
     def linear_acc_dev(self, x, acc, stream=None) -> None:
         """acc[M, N] int64 = exact W x (no requant)."""
         _check("myl_linear_acc_dev", load_library().myl_linear_acc_dev(
@@ -461,6 +504,16 @@ class Requant:
             C.byref(h)))
         self._h = h
         self.mode = mode
+
+    def exchange_reduce_dev(self, recv_ptr: int, world: int, rank: int, rows_per_rank: int, M: int,
+                            out_ptrs, ldo: int, stream=None) -> None:
+        """Sums this rank's slabs of the exchange's receive buffer, requantises
+        and writes the rows into every rank's output buffer
+        (myl_exchange_reduce_dev)."""
+        arr = (C.c_void_p * len(out_ptrs))(*out_ptrs)
+        _check("myl_exchange_reduce_dev", load_library().myl_exchange_reduce_dev(
+            self.w.ctx.handle, self._h, C.c_void_p(recv_ptr), world, rank, rows_per_rank, M, arr,
+            ldo, _stream_ptr(stream)))
 
     @property
     def handle(self):
@@ -748,6 +801,7 @@ class Artifact:
         return np.ctypeslib.as_array((C.c_int16 * n.value).from_address(data.value)).copy()
 
 
+IPC_HANDLE_BYTES = 64
 WIRE_HEADER_BYTES = 84
 WIRE_FLAG_STARTS_GENERATION = 0x1
 WIRE_FLAG_ABORT = 0x2

@@ -27,6 +27,7 @@ enum DeviceError : int {
   DEV_WAIT_EPILOGUE = 0x103,  // epilogue gave up waiting for the accumulator
   DEV_WAIT_DRAIN = 0x104,     // clean-up gave up waiting for copies / MMAs in flight
   DEV_WAIT_INJECTED = 0x105,  // test hook: a wait on a barrier nothing arrives at
+  DEV_WAIT_PEER = 0x106,      // a peer rank did not reach an exchange barrier in time
   DEV_BAD_EXPERT = 0x201,     // an expert id outside the experts this object holds
 };
 
@@ -52,6 +53,8 @@ struct SiluParams {
   int64_t ldp;
 };
 
+constexpr int MYL_XCHG_MAX = 8;  // ranks of a peer-memory exchange
+
 struct Epilogue {
   int mode;               // EpiMode
   int out_i32;            // 1: clamp to i32 and store int32, 0: clamp to i16, store int16
@@ -62,6 +65,18 @@ struct Epilogue {
   const int32_t* bias;    // optional [N]: rescaled bias added after the i16 clamp (linear.rs:132-145)
   SiluParams silu;
   const int64_t* xsum;    // EPI_W16: [M] sum of each activation row over K
+  // Exchange of a tensor-parallel row-parallel layer over peer memory.
+  // Scatter (EPI_ACC_I64, xs_world > 0): the exact partial of output row m
+  // goes to rank o = m / xs_rows, into xs_dst[o] at row xs_rank * xs_rows +
+  // m % xs_rows (every receive buffer holds one slab of xs_rows rows per
+  // sender). Gather (requant modes, xg_world > 0): the requantised row m goes
+  // to every xg_dst[o] at row xg_row0 + m.
+  void* xs_dst[MYL_XCHG_MAX];
+  int64_t xs_rows;
+  int xs_rank, xs_world;
+  void* xg_dst[MYL_XCHG_MAX];
+  int64_t xg_row0;
+  int xg_world;
 };
 
 // ---- requant -----------------------------------------------------------------
@@ -198,10 +213,24 @@ __device__ __forceinline__ void w16_store(const Epilogue& ep, int64_t m, int64_t
 __device__ __forceinline__ void epilogue_store(const Epilogue& ep, int64_t m, int64_t n,
                                                int64_t acc) {
   if (ep.mode == EPI_ACC_I64) {
-    static_cast<int64_t*>(ep.y)[m * ep.ldy + n] = acc;
+    if (ep.xs_world > 0) {
+      const int64_t o = m / ep.xs_rows;
+      static_cast<int64_t*>(ep.xs_dst[o])[(ep.xs_rank * ep.xs_rows + (m - o * ep.xs_rows)) * ep.ldy + n] =
+          acc;
+    } else {
+      static_cast<int64_t*>(ep.y)[m * ep.ldy + n] = acc;
+    }
     return;
   }
   const int64_t v = requant_value(ep, n, acc);
+  if (ep.xg_world > 0) {
+    const int64_t idx = (ep.xg_row0 + m) * ep.ldy + n;
+    for (int o = 0; o < ep.xg_world; ++o) {
+      if (ep.out_i32) static_cast<int32_t*>(ep.xg_dst[o])[idx] = int32_t(v);
+      else static_cast<int16_t*>(ep.xg_dst[o])[idx] = int16_t(v);
+    }
+    return;
+  }
   if (ep.out_i32) static_cast<int32_t*>(ep.y)[m * ep.ldy + n] = int32_t(v);
   else static_cast<int16_t*>(ep.y)[m * ep.ldy + n] = int16_t(v);
 }

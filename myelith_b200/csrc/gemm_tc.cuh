@@ -608,7 +608,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         if (n >= N) continue;
         if (mode == EPI_ACC_I64) {
-          store_column<NC>(static_cast<int64_t*>(e.y) + mc * e.ldy + n, e.ldy, mc, Mend, [&](int j) {
+          int64_t* yb;
+          if (e.xs_world > 0) {  // exchange: the owning rank's receive buffer (peer memory)
+            // xs_rows is a multiple of 16 >= NC, so the NC tokens share one owner
+            const int64_t o = mc / e.xs_rows;
+            yb = static_cast<int64_t*>(e.xs_dst[o]) +
+                 (e.xs_rank * e.xs_rows + (mc - o * e.xs_rows)) * e.ldy + n;
+          } else {
+            yb = static_cast<int64_t*>(e.y) + mc * e.ldy + n;
+          }
+          store_column<NC>(yb, e.ldy, mc, Mend, [&](int j) {
             return int64_t(int32_t(hi[j])) * 256 + int64_t(int32_t(lo[j]));
           });
         } else if (fast) {

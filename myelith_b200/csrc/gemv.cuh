@@ -409,4 +409,80 @@ __global__ void reduce_requant_kernel(const int64_t* __restrict__ part, int nspl
   }
 }
 
+// Exchange reduce of a row-parallel layer (myl_exchange_reduce_dev): thread g
+// sums 8 consecutive columns of one of this rank's rows over the world slabs
+// of recv (exact int64), requantises them and stores the 8 results with one
+// 16-byte (int16) or two (int32) stores into every rank's output buffer.
+// N and ep.ldy are multiples of 8.
+__global__ void xchg_reduce_kernel(const int64_t* __restrict__ recv, int world, int64_t slab,
+                                   int64_t rows, int64_t N, Epilogue ep) {
+  const int64_t per_row = N >> 3, total = rows * per_row;
+  for (int64_t g = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; g < total;
+       g += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t m = g / per_row, n0 = (g - m * per_row) * 8;
+    int64_t s[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j] = 0;
+    for (int r = 0; r < world; ++r) {
+      const longlong2* p = reinterpret_cast<const longlong2*>(recv + r * slab + m * N + n0);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const longlong2 v = __ldg(p + q);
+        s[2 * q] += v.x;
+        s[2 * q + 1] += v.y;
+      }
+    }
+    int32_t v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = int32_t(requant_value(ep, n0 + j, s[j]));
+    const int64_t idx = (ep.xg_row0 + m) * ep.ldy + n0;
+    if (ep.out_i32) {
+      const int4 a = make_int4(v[0], v[1], v[2], v[3]), b = make_int4(v[4], v[5], v[6], v[7]);
+      for (int o = 0; o < ep.xg_world; ++o) {
+        int4* d = reinterpret_cast<int4*>(static_cast<int32_t*>(ep.xg_dst[o]) + idx);
+        d[0] = a;
+        d[1] = b;
+      }
+    } else {
+      int4 h;
+      h.x = int((uint32_t(uint16_t(v[0]))) | (uint32_t(uint16_t(v[1])) << 16));
+      h.y = int((uint32_t(uint16_t(v[2]))) | (uint32_t(uint16_t(v[3])) << 16));
+      h.z = int((uint32_t(uint16_t(v[4]))) | (uint32_t(uint16_t(v[5])) << 16));
+      h.w = int((uint32_t(uint16_t(v[6]))) | (uint32_t(uint16_t(v[7])) << 16));
+      for (int o = 0; o < ep.xg_world; ++o)
+        *reinterpret_cast<int4*>(static_cast<int16_t*>(ep.xg_dst[o]) + idx) = h;
+    }
+  }
+}
+
+// Barrier of the ranks of a peer-memory exchange: thread t < world stores
+// `epoch` into rank t's flag word for this rank (system-scope release after
+// a system fence, so everything this rank's earlier kernels wrote is visible
+// first), then waits until this rank's flag word of sender t has reached the
+// epoch (acquire; bounded: a peer that does not arrive within timeout_ns
+// sets DEV_WAIT_PEER and the kernel returns).
+struct XchgFlags {
+  unsigned long long* p[MYL_XCHG_MAX];  // each rank's flag words (one per sender)
+};
+
+__global__ void xchg_barrier_kernel(XchgFlags flags, int world, int rank, unsigned long long epoch,
+                                    int* err, uint64_t timeout_ns) {
+  const int t = threadIdx.x;
+  if (t >= world) return;
+  __threadfence_system();
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(flags.p[t] + rank), "l"(epoch) : "memory");
+  const unsigned long long* mine = flags.p[rank] + t;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(mine) : "memory");
+    if (v >= epoch) return;
+    if (globaltimer_ns() - t0 > timeout_ns) {
+      atomicCAS(err, 0, DEV_WAIT_PEER);
+      return;
+    }
+    __nanosleep(64);
+  }
+}
+
 }  // namespace myl

@@ -366,6 +366,8 @@ static int launch_gemv(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int6
     ep.mode = EPI_ACC_I64;
     ep.y = ctx->part.p;
     ep.ldy = w->N;
+    ep.xs_world = 0;  // slice partials stay local; the final pass exchanges
+    ep.xg_world = 0;
     slice_stride = M * w->N;
   }
   const int8_t* dW = w->d_W;
@@ -591,6 +593,8 @@ static int launch_tc_planes(myl_ctx* ctx, const myl_weight* w, const uint8_t* xh
     ep.mode = EPI_ACC_I64;
     ep.y = ctx->part.p;
     ep.ldy = w->N;
+    ep.xs_world = 0;  // slice partials stay local; the final pass exchanges
+    ep.xg_world = 0;
     slice_stride = M * w->N;
   }
   TRY(launch_tc_any(ctx, w, tm_xhi, tm_xlo, M, BN, pair, work, ep, slice_stride, st));
@@ -1106,6 +1110,120 @@ int myl_linear_acc_dev(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int6
   ep.y = acc;
   ep.ldy = w->N;
   return run_linear(ctx, w, x, M, ldx, ep, static_cast<cudaStream_t>(stream));
+}
+
+int myl_linear_acc_exchange_dev(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M,
+                                int64_t ldx, int64_t* const* dst, int world, int rank,
+                                int64_t rows_per_rank, void* stream) {
+  if (!ctx || !w || !dst || (M > 0 && !x)) return fail(MYL_ERR_ARG, "null argument");
+  if (w->w16) return fail(MYL_ERR_ARG, "int16 weight: the exchange carries int8-weight partials");
+  if (world < 1 || world > MYL_XCHG_MAX || rank < 0 || rank >= world)
+    return fail(MYL_ERR_ARG, "world %d / rank %d (at most %d ranks)", world, rank, MYL_XCHG_MAX);
+  if (M < 0 || ldx < w->K || rows_per_rank <= 0 || rows_per_rank % 16 != 0 ||
+      M > int64_t(world) * rows_per_rank)
+    return fail(MYL_ERR_SHAPE, "bad M/ldx/rows_per_rank (a multiple of 16 covering M over the ranks)");
+  for (int o = 0; o < world; ++o)
+    if (!dst[o]) return fail(MYL_ERR_ARG, "null receive buffer of rank %d", o);
+  Epilogue ep{};
+  ep.mode = EPI_ACC_I64;
+  ep.y = dst[rank];
+  ep.ldy = w->N;
+  for (int o = 0; o < world; ++o) ep.xs_dst[o] = dst[o];
+  ep.xs_rows = rows_per_rank;
+  ep.xs_rank = rank;
+  ep.xs_world = world;
+  return run_linear(ctx, w, x, M, ldx, ep, static_cast<cudaStream_t>(stream));
+}
+
+int myl_exchange_reduce_dev(myl_ctx* ctx, const myl_requant* rq, const int64_t* recv, int world,
+                            int rank, int64_t rows_per_rank, int64_t M, void* const* out, int64_t ldo,
+                            void* stream) {
+  if (!ctx || !rq || !recv || !out) return fail(MYL_ERR_ARG, "null argument");
+  if (world < 1 || world > MYL_XCHG_MAX || rank < 0 || rank >= world)
+    return fail(MYL_ERR_ARG, "world %d / rank %d (at most %d ranks)", world, rank, MYL_XCHG_MAX);
+  if (M < 0 || rows_per_rank <= 0 || M > int64_t(world) * rows_per_rank || ldo < rq->N)
+    return fail(MYL_ERR_SHAPE, "bad M/rows_per_rank/ldo");
+  for (int o = 0; o < world; ++o)
+    if (!out[o]) return fail(MYL_ERR_ARG, "null output buffer of rank %d", o);
+  // this rank's rows: [rank * R, min((rank + 1) * R, M))
+  const int64_t own = std::max<int64_t>(0, std::min(rows_per_rank, M - int64_t(rank) * rows_per_rank));
+  if (own == 0 || rq->N == 0) return MYL_OK;
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  Epilogue ep = make_ep(rq, out[rank], ldo);
+  for (int o = 0; o < world; ++o) ep.xg_dst[o] = out[o];
+  ep.xg_row0 = int64_t(rank) * rows_per_rank;
+  ep.xg_world = world;
+  bool vec = rq->N % 8 == 0 && ldo % 8 == 0 && (reinterpret_cast<uintptr_t>(recv) & 15) == 0;
+  for (int o = 0; o < world; ++o) vec = vec && (reinterpret_cast<uintptr_t>(out[o]) & 15) == 0;
+  const int64_t total = vec ? own * (rq->N / 8) : own * rq->N;
+  unsigned blocks = unsigned(std::min<int64_t>((total + 255) / 256, int64_t(ctx->num_sms) * 8));
+  // recv holds world slabs of rows_per_rank rows: the sender index is the K-slice index
+  if (vec)
+    xchg_reduce_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        recv, world, rows_per_rank * rq->N, own, rq->N, ep);
+  else
+    reduce_requant_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        recv, world, rows_per_rank * rq->N, own, rq->N, ep);
+  CUDA_TRY(cudaGetLastError());
+  ctx->launches++;
+  return MYL_OK;
+}
+
+int myl_exchange_barrier_dev(myl_ctx* ctx, unsigned long long* const* flags, int world, int rank,
+                             unsigned long long epoch, void* stream) {
+  if (!ctx || !flags) return fail(MYL_ERR_ARG, "null argument");
+  if (world < 1 || world > MYL_XCHG_MAX || rank < 0 || rank >= world)
+    return fail(MYL_ERR_ARG, "world %d / rank %d (at most %d ranks)", world, rank, MYL_XCHG_MAX);
+  for (int o = 0; o < world; ++o)
+    if (!flags[o]) return fail(MYL_ERR_ARG, "null flag array of rank %d", o);
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  XchgFlags fp{};  // the pointers travel by value in the kernel's arguments
+  for (int o = 0; o < world; ++o) fp.p[o] = flags[o];
+  xchg_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(fp, world, rank, epoch,
+                                                                       ctx->d_err, ctx->timeout_ns);
+  CUDA_TRY(cudaGetLastError());
+  ctx->launches++;
+  return MYL_OK;
+}
+
+int myl_ipc_alloc(myl_ctx* ctx, size_t bytes, void** ptr, void* handle) {
+  if (!ctx || !ptr || !handle || bytes == 0) return fail(MYL_ERR_ARG, "bad argument");
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  CUDA_TRY(cudaMalloc(ptr, bytes));
+  CUDA_TRY(cudaMemset(*ptr, 0, bytes));  // flag words start at epoch 0
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, *ptr);
+  if (e != cudaSuccess) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return fail(MYL_ERR_CUDA, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+  }
+  static_assert(sizeof(h) == MYL_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle, &h, sizeof(h));
+  return MYL_OK;
+}
+
+int myl_ipc_open(myl_ctx* ctx, const void* handle, void** ptr) {
+  if (!ctx || !ptr || !handle) return fail(MYL_ERR_ARG, "null argument");
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  CUDA_TRY(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return MYL_OK;
+}
+
+int myl_ipc_close(myl_ctx* ctx, void* ptr) {
+  if (!ctx || !ptr) return fail(MYL_ERR_ARG, "null argument");
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  CUDA_TRY(cudaIpcCloseMemHandle(ptr));
+  return MYL_OK;
+}
+
+int myl_ipc_free(myl_ctx* ctx, void* ptr) {
+  if (!ctx || !ptr) return fail(MYL_ERR_ARG, "null argument");
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  CUDA_TRY(cudaFree(ptr));
+  return MYL_OK;
 }
 
 int myl_requant_acc_dev(myl_ctx* ctx, const myl_requant* rq, const int64_t* acc, int64_t M, void* y,

@@ -23,6 +23,17 @@ exact integer:
 
 int32 is not wide enough for the partial sums (up to ~1e10 for 7B shapes).
 
+Row-parallel exchange without a collective library in the data path
+(PeerExchange): the down/o projection's GEMM stores each exact int64 partial
+row straight into the receive buffer of the rank that owns the row (peer
+memory over NVLink, buffers shared through CUDA IPC), a one-element
+barrier orders the ranks (flag words in peer memory, written and polled by a
+one-block kernel on the stream), each rank sums its rows' slabs, requantises
+and writes the int16 rows into every rank's output buffer, and a second
+barrier orders the ranks again. The transfers ride inside the GEMM's epilogue
+instead of a separate reduce-scatter and all-gather, and no collective
+library is on the data path.
+
 The per-rank arithmetic is behind ``Local``: ``LibLocal`` calls the sm_100a
 kernels (torch CUDA tensors, NCCL); tests can supply another implementation
 of the same three methods to run the sharding and exchange logic with gloo on
@@ -226,6 +237,10 @@ class RowParallelLinear:
         return overlapped_row_parallel(compute_acc, requant, M, self.N, self.world, self.group,
                                        chunks, x_shard.device)
 
+    def exchanged(self, x_shard, xchg: "PeerExchange", stream=None, between=None):
+        """As __call__, through a PeerExchange (LibLocal only)."""
+        return xchg(self.local.weights[self.key], self.local.plans[self.key], x_shard, stream, between)
+
     def __call__(self, x_shard):
         import torch.distributed as dist
 
@@ -260,6 +275,99 @@ class VocabParallelLMHead:
         if self.world > 1:
             dist.all_reduce(keys, op=dist.ReduceOp.MAX, group=self.group)
         return (0xFFFFFFFF - (keys & 0xFFFFFFFF)), keys >> 32
+
+
+class _CudaBuffer:
+    """__cuda_array_interface__ of a library buffer, for a torch view."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (ptr, False), "version": 3, "strides": None}
+
+
+class PeerExchange:
+    """Buffers of one row-parallel layer shape (M tokens, N output channels)
+    shared by the ranks of a node, and the exchange step (see the module
+    notes). Rank o owns output rows [o R, min((o + 1) R, M)), R = ceil(M /
+    world) rounded up to 16. Collective: every rank constructs it, calls it
+    and closes it in the same order."""
+
+    def __init__(self, ctx, M: int, N: int, rank: int, world: int, group=None, out_i32: bool = False):
+        import torch
+        import torch.distributed as dist
+
+        from myelith_b200 import IPC_HANDLE_BYTES
+
+        self.ctx, self.M, self.N, self.rank, self.world, self.group = ctx, M, N, rank, world, group
+        self.R = ((M + world - 1) // world + 15) // 16 * 16
+        esize = 4 if out_i32 else 2
+        dev = torch.device("cuda", torch.cuda.current_device())
+        recv_bytes = world * self.R * N * 8
+        # the barrier's flag words (one per sender) follow the receive slabs
+        self.recv_ptr, h_recv = ctx.ipc_alloc(recv_bytes + 256)
+        self.out_ptr, h_out = ctx.ipc_alloc(world * self.R * N * esize)
+        mine = torch.tensor(list(h_recv + h_out), dtype=torch.uint8, device=dev)
+        allh = torch.empty((world, 2 * IPC_HANDLE_BYTES), dtype=torch.uint8, device=dev)
+        dist.all_gather_into_tensor(allh, mine, group=group)
+        allh = allh.cpu().numpy()
+        self.recv_ptrs, self.out_ptrs, self._opened = [], [], []
+        for o in range(world):
+            if o == rank:
+                self.recv_ptrs.append(self.recv_ptr)
+                self.out_ptrs.append(self.out_ptr)
+                continue
+            rp = ctx.ipc_open(bytes(allh[o, :IPC_HANDLE_BYTES]))
+            op = ctx.ipc_open(bytes(allh[o, IPC_HANDLE_BYTES:]))
+            self._opened += [rp, op]
+            self.recv_ptrs.append(rp)
+            self.out_ptrs.append(op)
+        self.flag_ptrs = [p + recv_bytes for p in self.recv_ptrs]
+        self.epoch = 0
+        self.out = torch.as_tensor(_CudaBuffer(self.out_ptr, (world * self.R, N),
+                                               "<i4" if out_i32 else "<i2"), device=dev)[:M]
+        self._flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._host_barrier()
+
+    def _host_barrier(self):
+        """Set-up and tear-down: a one-element all-reduce on the current stream."""
+        import torch.distributed as dist
+
+        dist.all_reduce(self._flag, group=self.group)
+
+    def barrier(self, stream=None):
+        """Orders the ranks' work on the stream (flag words in peer memory)."""
+        self.epoch += 1
+        self.ctx.exchange_barrier_dev(self.flag_ptrs, self.rank, self.epoch, stream)
+
+    def __call__(self, weight, requant, x_shard, stream=None, between=None):
+        """Row-parallel output [M, N] (a view of this rank's output buffer,
+        valid until the next call) of weight shard x x_shard; `between` runs
+        after this rank's GEMM, before the ranks synchronise."""
+        M = x_shard.shape[0]
+        if M > self.M:
+            raise ValueError(f"{M} rows, the exchange holds {self.M}")
+        weight.acc_exchange_dev(x_shard, self.recv_ptrs, self.rank, self.R, stream)
+        if between is not None:
+            between()
+        self.barrier(stream)
+        requant.exchange_reduce_dev(self.recv_ptr, self.world, self.rank, self.R, M, self.out_ptrs,
+                                    self.N, stream)
+        self.barrier(stream)
+        return self.out[:M]
+
+    def close(self):
+        import torch
+
+        torch.cuda.synchronize()
+        self._host_barrier()  # no rank still writes into another's buffers
+        torch.cuda.synchronize()
+        for p in self._opened:
+            self.ctx.ipc_close(p)
+        self._opened = []
+        self._host_barrier()  # every peer mapping is gone before the memory is freed
+        torch.cuda.synchronize()
+        self.ctx.ipc_free(self.recv_ptr)
+        self.ctx.ipc_free(self.out_ptr)
 
 
 def overlapped_row_parallel(compute_acc, requant, M: int, N: int, world: int, group=None,

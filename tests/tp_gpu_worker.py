@@ -65,6 +65,7 @@ def main():
         local = tp.LibLocal(ctx)
         spec = tp.LinearSpec(W, ws, 8, of)
         head = tp.VocabParallelLMHead(local, "head", Wl, wsl, 8, 6, rank, world)
+        xchg = tp.PeerExchange(ctx, M, N, rank, world)  # peer-memory row-parallel exchange
         col = tp.ColumnParallelLinear(local, "col", spec, rank, world)
         row = tp.RowParallelLinear(local, "row", spec, rank, world)
         pm = tp.ParallelMlp(local, "mlp", hidden=H, intermediate=I, rank=rank, world=world, **mlp)
@@ -81,10 +82,12 @@ def main():
                                  mlp["silu_lut"], 8, 7, 7, 7, 6, 8192, 8, mlp["out_frac"])(xm[:Ms])
             ref = O.linear_w8a16_pc(x[:Ms], W.reshape(-1), K, ws, 8, of)
             tok, best = head.greedy(xt[:Ms])
+            y_x = row.exchanged(row.x_shard(xt[:Ms]), xchg).cpu().numpy()
             logits = ctx.weight(Wl, K, wsl).lm_head(x[:Ms], 8, 6)
             ok = dict(col=bool(np.array_equal(y_col, single)), row=bool(np.array_equal(y_row, single)),
                       overlapped=bool(np.array_equal(y_ov, single)),
                       mlp=bool(np.array_equal(y_mlp, single_mlp)), oracle=bool(np.array_equal(single, ref)),
+                      exchange=bool(np.array_equal(y_x, single)),
                       greedy=tok.cpu().tolist() == [O.argmax_int(r) for r in logits]
                       and best.cpu().tolist() == [int(r.max()) for r in logits])
             # every rank holds the same bytes
@@ -101,6 +104,7 @@ def main():
             ok["all_ranks"] = bool(flag.item())
             verdict[f"M{Ms}"] = ok
         ctx.synchronize()
+        xchg.close()
     finally:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
