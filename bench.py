@@ -330,6 +330,10 @@ def bench_moe(ctx, dev, stream, rank: int, world: int, local: int, steps: int, w
         launches = ctx.launch_count - l0
     ctx.synchronize()
     ms = max_over_ranks(a.elapsed_time(b) / steps)
+    if world > 1:  # the expert-parallel layer routes internally: route once more for the load
+        with torch.cuda.stream(stream):
+            idx, _ = epl.local.route(x)
+        stream.synchronize()
     load = torch.bincount(idx.reshape(-1).long(), minlength=E).cpu().numpy()
     res = {"workload": "config4: MoE layer, hidden 2048, 64 experts x MLP 1408, top-4, shared "
                        "expert 5632, 4096 tokens per step",
