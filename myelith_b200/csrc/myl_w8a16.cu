@@ -313,7 +313,7 @@ static int launch_gemv_balanced(myl_ctx* ctx, const myl_weight* w, const int16_t
   int64_t K = w->K, N = w->N;
   void* fn = nullptr;
   switch (M) {
-    case 1: fn = gemv_balanced_ptr<1, 4>(); break;
+    case 1: fn = gemv_balanced_ptr<1, 6>(); break;  // 124 registers, two blocks per SM
     default: fn = gemv_balanced_ptr<2, 4>(); break;
   }
   const size_t smem = size_t(M) * size_t(round_up16(K)) * 2;
