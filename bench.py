@@ -284,7 +284,7 @@ def moe_ops(T: int) -> float:
 
 
 def bench_moe(ctx, dev, stream, rank: int, world: int, local: int, steps: int, warmup: int,
-              max_over_ranks, barrier) -> dict:
+              max_over_ranks, barrier, peer: bool = True) -> dict:
     """The MoE layer at config 4: 4096 tokens per step in total. One GPU: the
     fused layer (myl_moe_dev). N GPUs: expert parallelism, each rank holds
     E/N experts and 4096/N tokens, NCCL all_to_all dispatch and return."""
@@ -309,7 +309,11 @@ def bench_moe(ctx, dev, stream, rank: int, world: int, local: int, steps: int, w
         def layer():
             moe.dev(x, out, idx, prob, stream)
     else:
-        epl = ep.ExpertParallelMoe(ep.LibMoeLocal(moe, shared), E, k, H, rank, world)
+        if peer:  # dispatch and return through peer memory
+            epl = ep.PeerExpertParallelMoe(ctx, ep.LibMoeLocal(moe, shared), E, k, H, rank, world,
+                                           max_tokens=Tr)
+        else:
+            epl = ep.ExpertParallelMoe(ep.LibMoeLocal(moe, shared), E, k, H, rank, world)
 
         def layer():
             out.copy_(epl(x))
@@ -337,7 +341,8 @@ def bench_moe(ctx, dev, stream, rank: int, world: int, local: int, steps: int, w
     load = torch.bincount(idx.reshape(-1).long(), minlength=E).cpu().numpy()
     res = {"workload": "config4: MoE layer, hidden 2048, 64 experts x MLP 1408, top-4, shared "
                        "expert 5632, 4096 tokens per step",
-           "parallelism": "single GPU (myl_moe_dev)" if world == 1 else f"ep{world} (NCCL all_to_all)",
+           "parallelism": "single GPU (myl_moe_dev)" if world == 1 else
+           f"ep{world} ({'peer-memory dispatch and return' if peer else 'NCCL all_to_all'})",
            "tokens_per_rank": Tr, "ms_per_layer": round(ms, 4),
            "tops": round(moe_ops(T) / (ms * 1e-3) / 1e12, 2),
            "tokens_per_s": round(T / (ms * 1e-3), 1),
@@ -361,6 +366,8 @@ def bench_moe(ctx, dev, stream, rank: int, world: int, local: int, steps: int, w
                       "h2d_bytes_per_step": int(x_h.nbytes), "d2h_bytes_per_step": int(yp.nbytes)}
     moe.release()
     shared.release()
+    if world > 1 and peer:
+        epl.close()
     return res
 
 
@@ -761,7 +768,7 @@ def main() -> None:
     moe = None
     if not args.no_moe:
         moe = bench_moe(ctx, dev, stream, rank, world, local, max(3, args.steps // 2), args.warmup,
-                        max_over_ranks, barrier)
+                        max_over_ranks, barrier, peer=args.exchange == "p2p")
 
     # ---- CPU baseline (rank 0, N=1) ----
     cpu = None

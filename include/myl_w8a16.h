@@ -195,6 +195,28 @@ int myl_exchange_reduce_dev(myl_ctx* ctx, const myl_requant* rq, const int64_t* 
  * that does not arrive is reported as MYL_ERR_DEVICE at the next check. */
 int myl_exchange_barrier_dev(myl_ctx* ctx, unsigned long long* const* flags, int world, int rank,
                              unsigned long long epoch, void* stream);
+/* Expert-parallel MoE over peer memory (no collective library on the data
+ * path). Experts are split over the ranks in contiguous shard ranges.
+ *  - myl_ep_dispatch_dev: pair q = t * k + j of this rank's tokens (x [T][ldx],
+ *    expert ids idx [T][k] from the router) takes slot s = atomicAdd(
+ *    counters[o]) on the rank o owning expert idx[q] (system scope, over
+ *    NVLink) and stores its row at rows[o] + s * H, idx[q] at ids[o][s] and
+ *    rank << 24 | q at src[o][s]. Slots >= capacity are not written and raise
+ *    MYL_ERR_DEVICE at the next check (as do expert ids out of range).
+ *  - after a barrier, rank o runs its experts on its counters[o] received rows
+ *    (myl_moe_experts_dev; the order of the rows does not matter: each output
+ *    row depends on its own input row only) and resets its counter;
+ *  - myl_ep_return_dev: received row i goes back to back[src >> 24] at row
+ *    src & 0xFFFFFF, i.e. in (token, choice) order on its home rank;
+ *  - after a barrier, the home rank combines (myl_moe_combine_dev).
+ * The arithmetic is the single-GPU layer's, so the output is bit-identical. */
+int myl_ep_dispatch_dev(myl_ctx* ctx, const int16_t* x, int64_t T, int64_t ldx, int64_t H,
+                        const int32_t* idx, int k, int E, int world, int rank, int16_t* const* rows,
+                        int32_t* const* ids, int32_t* const* src, int32_t* const* counters,
+                        int64_t capacity, void* stream);
+int myl_ep_return_dev(myl_ctx* ctx, const int16_t* y, int64_t count, int64_t H, const int32_t* src,
+                      int16_t* const* back, int world, void* stream);
+
 /* Device buffers shared between the processes of one node: allocation with
  * its IPC handle (MYL_IPC_HANDLE_BYTES bytes, to send to the other ranks),
  * opening a peer's handle (not one's own), and their release. */

@@ -115,6 +115,9 @@ def load_library(path: str | None = None):
             "myl_linear_acc_exchange_dev": ([vp, vp, vp, i64, i64, vp, i32, i32, i64, vp], i32),
             "myl_exchange_reduce_dev": ([vp, vp, vp, i32, i32, i64, i64, vp, i64, vp], i32),
             "myl_exchange_barrier_dev": ([vp, vp, i32, i32, C.c_uint64, vp], i32),
+            "myl_ep_dispatch_dev": ([vp, vp, i64, i64, i64, vp, i32, i32, i32, i32, vp, vp, vp, vp,
+                                     i64, vp], i32),
+            "myl_ep_return_dev": ([vp, vp, i64, i64, vp, vp, i32, vp], i32),
             "myl_ipc_alloc": ([vp, C.c_size_t, C.POINTER(vp), vp], i32),
             "myl_ipc_open": ([vp, vp, C.POINTER(vp)], i32),
             "myl_ipc_close": ([vp, vp], i32),
@@ -240,6 +243,22 @@ class Context:
         arr = (C.c_void_p * len(flag_ptrs))(*flag_ptrs)
         _check("myl_exchange_barrier_dev", load_library().myl_exchange_barrier_dev(
             self._h, arr, len(flag_ptrs), rank, epoch, _stream_ptr(stream)))
+
+    def ep_dispatch_dev(self, x, idx, num_experts: int, rank: int, rows, ids, src, counters,
+                        capacity: int, stream=None) -> None:
+        """Expert-parallel dispatch over peer memory (myl_ep_dispatch_dev); rows,
+        ids, src, counters: one device pointer per rank."""
+        w = len(rows)
+        arr = [(C.c_void_p * w)(*a) for a in (rows, ids, src, counters)]
+        _check("myl_ep_dispatch_dev", load_library().myl_ep_dispatch_dev(
+            self._h, _p(x), x.shape[0], x.stride(0), x.shape[1], _p(idx), idx.shape[1], num_experts,
+            w, rank, arr[0], arr[1], arr[2], arr[3], capacity, _stream_ptr(stream)))
+
+    def ep_return_dev(self, y, count: int, src, back, stream=None) -> None:
+        """Returns received expert outputs to their home ranks (myl_ep_return_dev)."""
+        arr = (C.c_void_p * len(back))(*back)
+        _check("myl_ep_return_dev", load_library().myl_ep_return_dev(
+            self._h, _p(y), count, y.shape[1], _p(src), arr, len(back), _stream_ptr(stream)))
 
     def ipc_close(self, ptr: int) -> None:
         _check("myl_ipc_close", load_library().myl_ipc_close(self._h, C.c_void_p(ptr)))

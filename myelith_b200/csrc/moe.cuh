@@ -288,4 +288,80 @@ __global__ void moe_combine_kernel(const int16_t* __restrict__ y, int64_t ldyp,
   }
 }
 
+// ---- expert parallelism over peer memory ----------------------------------------
+// Buffers of every rank, passed by value (pointers into peer memory).
+struct EpPeers {
+  int16_t* rows[MYL_XCHG_MAX];   // received rows [capacity][H]
+  int32_t* ids[MYL_XCHG_MAX];    // their expert ids
+  int32_t* src[MYL_XCHG_MAX];    // their origin: rank << 24 | pair index
+  int32_t* count[MYL_XCHG_MAX];  // slot counter of the receiving rank
+  int16_t* back[MYL_XCHG_MAX];   // returned expert outputs [pairs][H] of the home rank
+};
+
+// Rank owning expert e when E experts are split in contiguous shard ranges
+// (the first E % world ranks hold one more).
+__device__ __forceinline__ int ep_owner(int e, int E, int world) {
+  const int base = E / world, extra = E % world;
+  const int big = extra * (base + 1);
+  return e < big ? e / (base + 1) : extra + (e - big) / max(base, 1);
+}
+
+// One warp per (token, choice) pair q = t * k + j: a slot on the owner's
+// counter (system-scope atomic over NVLink), then the row (H int16), the
+// expert id and the origin stored into the owner's buffers. A slot at or
+// beyond capacity is not written and raises DEV_BAD_EXPERT.
+__global__ void ep_dispatch_kernel(const int16_t* __restrict__ x, int64_t T, int64_t ldx, int64_t H,
+                                   const int32_t* __restrict__ idx, int k, int E, int world,
+                                   int rank, EpPeers peers, int64_t capacity, int* err) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
+  const int64_t P = T * k;
+  for (int64_t q = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); q < P; q += warps) {
+    const int e = idx[q];
+    if (e < 0 || e >= E) {
+      if (lane == 0) atomicCAS(err, 0, DEV_BAD_EXPERT);
+      continue;
+    }
+    const int o = ep_owner(e, E, world);
+    int slot = 0;
+    if (lane == 0) slot = atomicAdd_system(peers.count[o], 1);
+    slot = __shfl_sync(0xffffffffu, slot, 0);
+    if (slot >= capacity) {
+      if (lane == 0) atomicCAS(err, 0, DEV_BAD_EXPERT);
+      continue;
+    }
+    const int16_t* xr = x + (q / k) * ldx;
+    int16_t* dst = peers.rows[o] + int64_t(slot) * H;
+    if ((H % 8) == 0 && (reinterpret_cast<uintptr_t>(xr) & 15) == 0) {
+      for (int64_t c = lane; c < H / 8; c += 32)
+        reinterpret_cast<int4*>(dst)[c] = __ldg(reinterpret_cast<const int4*>(xr) + c);
+    } else {
+      for (int64_t c = lane; c < H; c += 32) dst[c] = xr[c];
+    }
+    if (lane == 0) {
+      peers.ids[o][slot] = e;
+      peers.src[o][slot] = (rank << 24) | int32_t(q);
+    }
+  }
+}
+
+// Received row i < count returns to its origin: y[i] -> back[src >> 24] row
+// (src & 0xFFFFFF), one warp per row.
+__global__ void ep_return_kernel(const int16_t* __restrict__ y, int64_t count, int64_t H,
+                                 const int32_t* __restrict__ src, EpPeers peers) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t i = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); i < count; i += warps) {
+    const int32_t s = src[i];
+    int16_t* dst = peers.back[s >> 24] + int64_t(s & 0xFFFFFF) * H;
+    const int16_t* yr = y + i * H;
+    if ((H % 8) == 0) {
+      for (int64_t c = lane; c < H / 8; c += 32)
+        reinterpret_cast<int4*>(dst)[c] = __ldg(reinterpret_cast<const int4*>(yr) + c);
+    } else {
+      for (int64_t c = lane; c < H; c += 32) dst[c] = yr[c];
+    }
+  }
+}
+
 }  // namespace myl

@@ -1186,6 +1186,54 @@ int myl_exchange_barrier_dev(myl_ctx* ctx, unsigned long long* const* flags, int
   return MYL_OK;
 }
 
+int myl_ep_dispatch_dev(myl_ctx* ctx, const int16_t* x, int64_t T, int64_t ldx, int64_t H,
+                        const int32_t* idx, int k, int E, int world, int rank, int16_t* const* rows,
+                        int32_t* const* ids, int32_t* const* src, int32_t* const* counters,
+                        int64_t capacity, void* stream) {
+  if (!ctx || !rows || !ids || !src || !counters || (T > 0 && (!x || !idx)))
+    return fail(MYL_ERR_ARG, "null argument");
+  if (world < 1 || world > MYL_XCHG_MAX || rank < 0 || rank >= world)
+    return fail(MYL_ERR_ARG, "world %d / rank %d (at most %d ranks)", world, rank, MYL_XCHG_MAX);
+  if (T < 0 || H <= 0 || ldx < H || k < 1 || E < world || capacity < 0 || T * k >= (int64_t(1) << 24))
+    return fail(MYL_ERR_SHAPE, "bad T/H/ldx/k/E/capacity");
+  EpPeers pe{};
+  for (int o = 0; o < world; ++o) {
+    if (!rows[o] || !ids[o] || !src[o] || !counters[o])
+      return fail(MYL_ERR_ARG, "null buffer of rank %d", o);
+    pe.rows[o] = rows[o];
+    pe.ids[o] = ids[o];
+    pe.src[o] = src[o];
+    pe.count[o] = counters[o];
+  }
+  if (T == 0) return MYL_OK;
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  const unsigned blocks = unsigned(std::min<int64_t>((T * k + 7) / 8, int64_t(ctx->num_sms) * 8));
+  ep_dispatch_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, T, ldx, H, idx, k, E, world, rank, pe, capacity, ctx->d_err);
+  CUDA_TRY(cudaGetLastError());
+  ctx->launches++;
+  return MYL_OK;
+}
+
+int myl_ep_return_dev(myl_ctx* ctx, const int16_t* y, int64_t count, int64_t H, const int32_t* src,
+                      int16_t* const* back, int world, void* stream) {
+  if (!ctx || !back || (count > 0 && (!y || !src))) return fail(MYL_ERR_ARG, "null argument");
+  if (world < 1 || world > MYL_XCHG_MAX) return fail(MYL_ERR_ARG, "world %d", world);
+  if (count < 0 || H <= 0) return fail(MYL_ERR_SHAPE, "bad count/H");
+  EpPeers pe{};
+  for (int o = 0; o < world; ++o) {
+    if (!back[o]) return fail(MYL_ERR_ARG, "null return buffer of rank %d", o);
+    pe.back[o] = back[o];
+  }
+  if (count == 0) return MYL_OK;
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  const unsigned blocks = unsigned(std::min<int64_t>((count + 7) / 8, int64_t(ctx->num_sms) * 8));
+  ep_return_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(y, count, H, src, pe);
+  CUDA_TRY(cudaGetLastError());
+  ctx->launches++;
+  return MYL_OK;
+}
+
 int myl_ipc_alloc(myl_ctx* ctx, size_t bytes, void** ptr, void* handle) {
   if (!ctx || !ptr || !handle || bytes == 0) return fail(MYL_ERR_ARG, "bad argument");
   CUDA_TRY(cudaSetDevice(ctx->device));

@@ -159,3 +159,102 @@ class ExpertParallelMoe:
         y_recv = self.local.experts(rx, rid)
         y = self.gather_back(y_recv, order, send_l, recv_l, idx.numel())
         return self.local.combine(y, prob, self.local.shared(x))
+
+
+class PeerExpertParallelMoe:
+    """The expert-parallel layer without a collective library on the data
+    path: dispatch and return through peer memory (myl_ep_dispatch_dev /
+    myl_ep_return_dev), device-side barriers between them, one host read of
+    the received row count per layer. Same arithmetic and combine order as
+    ExpertParallelMoe, so the output is bit-identical. Collective: every rank
+    constructs, calls and closes it in the same order."""
+
+    def __init__(self, ctx, local: "LibMoeLocal", num_experts: int, top_k: int, hidden: int,
+                 rank: int, world: int, max_tokens: int, group=None):
+        import torch
+        import torch.distributed as dist
+
+        from myelith_b200 import IPC_HANDLE_BYTES
+        from myelith_b200.tp import _CudaBuffer
+
+        self.ctx, self.local, self.E, self.k, self.H = ctx, local, num_experts, top_k, hidden
+        self.rank, self.world, self.group, self.max_tokens = rank, world, group, max_tokens
+        self.capacity = world * max_tokens * top_k  # every pair of every rank, worst case
+
+        def up(n):
+            return (n + 255) // 256 * 256
+
+        cap, H = self.capacity, hidden
+        off_rows, off_ids = 0, up(cap * H * 2)
+        off_src = off_ids + up(cap * 4)
+        off_cnt = off_src + up(cap * 4)
+        off_flag = off_cnt + 256
+        total = off_flag + 256
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.buf, h1 = ctx.ipc_alloc(total)
+        self.back, h2 = ctx.ipc_alloc(max(1, max_tokens * top_k) * H * 2)
+        mine = torch.tensor(list(h1 + h2), dtype=torch.uint8, device=dev)
+        allh = torch.empty((world, 2 * IPC_HANDLE_BYTES), dtype=torch.uint8, device=dev)
+        dist.all_gather_into_tensor(allh, mine, group=group)
+        allh = allh.cpu().numpy()
+        bases, backs, self._opened = [], [], []
+        for o in range(world):
+            if o == rank:
+                bases.append(self.buf)
+                backs.append(self.back)
+                continue
+            b = ctx.ipc_open(bytes(allh[o, :IPC_HANDLE_BYTES]))
+            bk = ctx.ipc_open(bytes(allh[o, IPC_HANDLE_BYTES:]))
+            self._opened += [b, bk]
+            bases.append(b)
+            backs.append(bk)
+        self.rows_p = [b + off_rows for b in bases]
+        self.ids_p = [b + off_ids for b in bases]
+        self.src_p = [b + off_src for b in bases]
+        self.cnt_p = [b + off_cnt for b in bases]
+        self.flag_p = [b + off_flag for b in bases]
+        self.back_p = backs
+        self.epoch = 0
+        view = lambda ptr, shape, t: torch.as_tensor(_CudaBuffer(ptr, shape, t), device=dev)  # noqa: E731
+        self.rows_t = view(self.buf + off_rows, (cap, H), "<i2")
+        self.ids_t = view(self.buf + off_ids, (cap,), "<i4")
+        self.src_t = view(self.buf + off_src, (cap,), "<i4")
+        self.cnt_t = view(self.buf + off_cnt, (1,), "<i4")
+        self.back_t = view(self.back, (max(1, max_tokens * top_k), H), "<i2")
+        self._flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        dist.all_reduce(self._flag, group=group)
+
+    def barrier(self):
+        self.epoch += 1
+        self.ctx.exchange_barrier_dev(self.flag_p, self.rank, self.epoch)
+
+    def __call__(self, x):
+        T = x.shape[0]
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens, the layer holds {self.max_tokens}")
+        idx, prob = self.local.route(x)
+        self.ctx.ep_dispatch_dev(x, idx, self.E, self.rank, self.rows_p, self.ids_p, self.src_p,
+                                 self.cnt_p, self.capacity)
+        shared = self.local.shared(x)  # this rank's shared expert while the peers dispatch
+        self.barrier()
+        n = int(self.cnt_t.item())
+        self.cnt_t.zero_()  # peers dispatch again only after the closing barrier
+        y = self.local.experts(self.rows_t[:n], self.ids_t[:n])
+        self.ctx.ep_return_dev(y, n, self.src_t, self.back_p)
+        self.barrier()
+        return self.local.combine(self.back_t[: T * self.k], prob, shared)
+
+    def close(self):
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.synchronize()
+        dist.all_reduce(self._flag, group=self.group)
+        torch.cuda.synchronize()
+        for p in self._opened:
+            self.ctx.ipc_close(p)
+        self._opened = []
+        dist.all_reduce(self._flag, group=self.group)
+        torch.cuda.synchronize()
+        self.ctx.ipc_free(self.buf)
+        self.ctx.ipc_free(self.back)

@@ -51,11 +51,20 @@ def main():
         xt = torch.from_numpy(x).to(dev)
         out = layer(xt).cpu().numpy()
         out2 = layer(xt).cpu().numpy()
+        # the same layer over peer memory (no collective library on the data path);
+        # every rank passes the same token bound
+        peer = ep.PeerExpertParallelMoe(ctx, ep.LibMoeLocal(part, shared), E, k, H, rank, world,
+                                        max_tokens=args.tokens + 37 * (world - 1))
+        outp = peer(xt).cpu().numpy()
+        outp2 = peer(xt).cpu().numpy()
+        ctx.synchronize()
+        peer.close()
         full = R.lib_moe(ctx, p, s)
         single = full(x)
         sample = np.random.default_rng(7 + rank).choice(T, size=12, replace=False)
         ref = R.forward(p, s, x[sample])[0]
         ok = dict(single=bool(np.array_equal(out, single)), repeat=bool(np.array_equal(out, out2)),
+                  peer=bool(np.array_equal(outp, single) and np.array_equal(outp2, single)),
                   oracle=bool(np.array_equal(out[sample], ref)))
         ok["all"] = all(ok.values())
         flag = torch.tensor([1 if ok["all"] else 0], dtype=torch.int32, device=dev)
