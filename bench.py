@@ -12,9 +12,20 @@ synthetic, seeded, random-init.
 
 N GPUs (torchrun): Megatron tensor parallelism of the same step. The gate/up
 shape is column-parallel (N split), the down shape row-parallel (K split):
-each rank writes exact int64 partial sums, NCCL sums them (int64 all-reduce)
-and the requant runs once after the sum, so the result is bit-identical at
-every GPU count. Total work is fixed: strong scaling.
+each rank produces exact int64 partial sums that are summed across the ranks
+before the requant runs once, so the result is bit-identical at every GPU
+count (tp_check compares the step with an int64 all-reduce step). With
+--exchange p2p (default) the down GEMM's epilogue stores its partial rows
+into the owning ranks' buffers over NVLink and a reduce kernel requantises and
+all-gathers through peer memory (device barriers, no collective library on
+the data path); --exchange nccl overlaps an NCCL reduce-scatter with the
+gate/up GEMM and all-gathers after the requant. Total work is fixed: strong
+scaling.
+
+moe        the config-4 MoE layer (4096 tokens, 64 experts, top-4, shared
+           expert): one GPU runs the fused layer; N GPUs split the experts
+           (expert parallelism, dispatch and return through peer memory, or
+           NCCL all_to_all with --exchange nccl), each rank 4096/N tokens.
 
 value      whole-job algorithmic int TOPS (2*M*K*N per linear) over the timed
            steps, device time, max over ranks. Inputs are resident in HBM.
