@@ -294,6 +294,100 @@ def moe_ops(T: int) -> float:
     return 2.0 * T * (E * H + k * 3 * I * H + 3 * Is * H)
 
 
+DECODE = dict(H=3584, I=18944, KV=512, V=152064, layers=28, distinct=4)
+
+
+def bench_decode(ctx, dev, steps: int, warmup: int, hbm_gbs: float) -> dict:
+    """Qwen2.5-7B-shaped integer decode at batch 1, the W8A16 linears of one
+    token: per layer q (3584 -> 3584), k and v (3584 -> 512), o (3584 -> 3584)
+    and the MLP (gate/up 3584 -> 2 x 18944 with the SiLU epilogue, down 18944 ->
+    3584), 28 layers, then the LM head (3584 -> 152064, int32 logits); all
+    GEMVs at M = 1, replayed as one CUDA graph. Attention, norms, RoPE and the
+    embedding are outside the W8A16 path and not included. Weights: 4 distinct
+    random layers cycled over the 28 (933 MB, larger than L2) plus the LM head."""
+    import torch
+
+    import myelith_b200 as myl
+
+    H, I, KV, V, L, D = (DECODE[n] for n in ("H", "I", "KV", "V", "layers", "distinct"))
+    rng = np.random.default_rng(77)
+
+    def lin(n, k):
+        w = ctx.weight(rng.integers(-127, 128, size=(n, k), dtype=np.int8), k,
+                       rng.integers(kbits(k) - 1, kbits(k) + 2, size=n).astype(np.uint8))
+        return w, w.requant(myl.RQ_SHIFT_I16, ACT_FRAC, OUT_FRAC)
+
+    layers = []
+    for _ in range(D):
+        mlp = myl.Mlp(ctx, rng.integers(-127, 128, size=(I, H), dtype=np.int8),
+                      rng.integers(-127, 128, size=(I, H), dtype=np.int8),
+                      rng.integers(-127, 128, size=(H, I), dtype=np.int8), H, I,
+                      np.full(I, kbits(H), np.uint8), np.full(I, kbits(H), np.uint8),
+                      np.full(H, kbits(I), np.uint8),
+                      np.clip(np.arange(-8192, 8192) // 2, -32768, 32767).astype(np.int16),
+                      8, 7, 7, 7, 6, 8192, 8, np.full(H, 8, np.uint8))
+        layers.append(dict(q=lin(H, H), k=lin(KV, H), v=lin(KV, H), o=lin(H, H), mlp=mlp))
+    head = ctx.weight(rng.integers(-127, 128, size=(V, H), dtype=np.int8), H,
+                      np.full(V, kbits(H), np.uint8))
+    head_rq = head.requant(myl.RQ_SHIFT_I32, 8, 6)
+    x = torch.from_numpy(np.clip(np.rint(rng.normal(0, 1024, size=(1, H))), -32767, 32767)
+                         .astype(np.int16)).to(dev)
+    a = x.clone()  # stands for the attention output that o reads
+    q, k_, v_, o_, m_ = (torch.empty((1, n), dtype=torch.int16, device=dev) for n in (H, KV, KV, H, H))
+    logits = torch.empty((1, V), dtype=torch.int32, device=dev)
+    weight_bytes = L * (2 * H * H + 2 * KV * H + 3 * I * H) + V * H
+    l0 = ctx.launch_count
+
+    def token():
+        for j in range(L):
+            ly = layers[j % D]
+            ly["q"][0].linear_dev(ly["q"][1], x, q)
+            ly["k"][0].linear_dev(ly["k"][1], x, k_)
+            ly["v"][0].linear_dev(ly["v"][1], x, v_)
+            ly["o"][0].linear_dev(ly["o"][1], a, o_)
+            ly["mlp"].dev(x, m_)
+        head.linear_dev(head_rq, x, logits)
+
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for _ in range(max(warmup, 1)):
+            token()
+    s.synchronize()
+    launches = (ctx.launch_count - l0) / max(warmup, 1)
+    graph = torch.cuda.CUDAGraph()
+    try:
+        with torch.cuda.graph(graph, stream=s):
+            token()
+        replay, graphed = graph.replay, True
+    except Exception:  # capture refused: time the eager launches instead
+        torch.cuda.synchronize()
+        replay, graphed = token, False
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(steps):
+            replay()
+        e1.record(s)
+    s.synchronize()
+    ctx.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    # the replayed graph computes what the eager launches compute
+    with torch.cuda.stream(s):
+        replay()
+        got = (logits.clone(), m_.clone())
+        token()
+        same = bool(torch.equal(got[0], logits) and torch.equal(got[1], m_))
+    s.synchronize()
+    return {"workload": "Qwen2.5-7B-shaped decode, batch 1: q/k/v/o, MLP (SiLU epilogue) x 28 layers "
+                        "+ LM head, all W8A16 GEMVs at M=1 (attention, norms, embedding not included)",
+            "tok_s": round(1e3 / ms, 1), "ms_per_token": round(ms, 4),
+            "weight_bytes_per_token": weight_bytes, "gbs": round(weight_bytes / (ms * 1e-3) / 1e9, 1),
+            "frac_of_hbm": round(weight_bytes / (ms * 1e-3) / 1e9 / hbm_gbs, 3),
+            "launches_per_token": launches, "cuda_graph": graphed, "graph_matches_eager": same}
+
+
 def bench_moe(ctx, dev, stream, rank: int, world: int, local: int, steps: int, warmup: int,
               max_over_ranks, barrier, peer: bool = True) -> dict:
     """The MoE layer at config 4: 4096 tokens per step in total. One GPU: the
@@ -417,6 +511,7 @@ def main() -> None:
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-moe", action="store_true")
+    ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--sm-reserve", type=int, default=16,
                     help="N>1 with --exchange nccl: SMs left free for the overlapped collectives")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
@@ -775,6 +870,11 @@ def main() -> None:
                 "per_shape_gbs": [round(g, 1) for g in gemv_gbs],
                 "bytes": "N*K weights + 2K act + 2N out + N shift bytes per launch"}
 
+    # ---- 7B-shaped decode (N=1) ----
+    decode = None
+    if tp == 1 and not args.no_decode:
+        decode = bench_decode(ctx, dev, max(10, args.steps), args.warmup, peaks["hbm_gbs"])
+
     # ---- MoE layer (config 4): every rank takes part (all_to_all at N > 1) ----
     moe = None
     if not args.no_moe:
@@ -821,6 +921,7 @@ def main() -> None:
             "gemv": gemv,
             "sweep": sweep,
             "moe": moe,
+            "decode": decode,
             "tp_check": tp_check,
         }
         emit(line)
