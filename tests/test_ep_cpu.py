@@ -114,3 +114,20 @@ def test_expert_parallel_ranks_without_rows():
 def test_expert_owner():
     assert ep.expert_owner(8, 2).tolist() == [0, 0, 0, 0, 1, 1, 1, 1]
     assert ep.expert_owner(5, 3).tolist() == [0, 0, 1, 1, 2]
+
+
+def test_device_owner_formula_matches_shard_ranges():
+    """ep_dispatch_kernel finds the rank owning expert e without a table:
+    with base, extra = divmod(E, world), experts below extra * (base + 1)
+    belong to rank e // (base + 1), the rest to extra + (e - that) // base.
+    The same integer steps here against the shard ranges of expert_owner."""
+    from myelith_b200.ep import expert_owner
+
+    for E in (1, 2, 3, 7, 8, 63, 64, 65, 100, 256):
+        for world in range(1, 9):
+            if E < world:
+                continue
+            base, extra = divmod(E, world)
+            big = extra * (base + 1)
+            own = [e // (base + 1) if e < big else extra + (e - big) // max(base, 1) for e in range(E)]
+            assert own == expert_owner(E, world).tolist(), (E, world)
