@@ -397,6 +397,19 @@ __global__ void reduce_requant_kernel(const int64_t* __restrict__ part, int nspl
     }
     return;
   }
+  if (N < int64_t(blockDim.x)) {
+    // Narrow rows (a router's few experts): threads walk the flat
+    // (row, column) index so that no thread of a block idles.
+    const int64_t total = M * N;
+    for (int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+         e += int64_t(gridDim.x) * blockDim.x) {
+      const int64_t m = e / N, n = e - m * N;
+      int64_t s = 0;
+      for (int i = 0; i < nsplit; ++i) s += part[i * slice_stride + m * N + n];
+      epilogue_store(ep, m, n, s);
+    }
+    return;
+  }
   // Blocks walk (row, 256-column segment) pairs, threads the columns of a
   // segment: one 64-bit division per segment instead of per element.
   const int64_t segs = (N + blockDim.x - 1) / blockDim.x;
