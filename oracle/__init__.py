@@ -45,7 +45,8 @@ def build() -> str:
 def lib():
     global _lib
     if _lib is None:
-        srcs = [os.path.join(_HERE, f) for f in ("myl_oracle.c", "myl_oracle.h")]
+        srcs = [os.path.join(_HERE, f)
+                for f in ("myl_oracle.c", "myl_oracle.h", "myl_forward.c", "myl_forward.h")]
         if not os.path.exists(_LIB_PATH) or any(
                 os.path.getmtime(f) > os.path.getmtime(_LIB_PATH) for f in srcs if os.path.exists(f)):
             build()
@@ -84,6 +85,18 @@ def lib():
         L.mylo_mlp_hidden.argtypes = [p, i64, p, p, i64, i64, p, p, p, i64,
                                       u8, u8, u8, u8, u8, C.c_int16, u8, p, p]
         L.mylo_softmax_int.argtypes = [p, i64, p, i64, u8, u8, p]
+        L.mylo_silu_product.argtypes = [p, p, i64, p, i64, u8, u8, u8, u8, C.c_int16, u8, p, p]
+        L.mylo_inv_n_q20.argtypes = [i64]
+        L.mylo_inv_n_q20.restype = i64
+        L.mylo_isqrt_round.argtypes = [C.c_uint64]
+        L.mylo_isqrt_round.restype = C.c_uint64
+        L.mylo_inv_sqrt_q15.argtypes = [i64]
+        L.mylo_inv_sqrt_q15.restype = i64
+        L.mylo_rmsnorm_i16.argtypes = [p, i64, p, p, p, p, i64, u8, u8, i64, u8, p]
+        L.mylo_rotate_half_split_i16.argtypes = [p, i64, p, p, u8, p]
+        L.mylo_attention_int.argtypes = [p, i64, p, p, i64, i64, p, i64, u8, p, i64, u8, u8, p]
+        L.mylo_forward.argtypes = [p, p, p, i64, p, i64, i64, p]
+        L.mylo_generate.argtypes = [p, p, p, i64, p, i64, i64, p, p]
         L.mylo_moe_route.argtypes = [p, i64, i64, i64, p, i64, u8, u8, p, p]
         L.mylo_moe_combine.argtypes = [p, p, p, i64, i64, i64, u8, p]
         L.mylo_argmax_i32.argtypes = [p, i64]
@@ -395,3 +408,177 @@ def num_threads() -> int:
 
 def set_num_threads(n: int) -> None:
     lib().mylo_set_num_threads(n)
+
+
+# ---- forward pass (myl_forward.c) ---------------------------------------------
+
+def inv_n_q20(n: int) -> int:
+    return lib().mylo_inv_n_q20(n)
+
+
+def isqrt_round(n: int) -> int:
+    return lib().mylo_isqrt_round(n)
+
+
+def inv_sqrt_q15(head_dim: int) -> int:
+    return lib().mylo_inv_sqrt_q15(head_dim)
+
+
+def rmsnorm_i16(x, x_shifts, gamma, gamma_shifts, rsqrt_lut, lut_input_shift: int,
+                lut_output_frac: int, inv_n: int, out_frac_bits: int) -> np.ndarray:
+    """rmsnorm.rs:61-153 on one row [n] or on each row of [M, n]."""
+    x = _c(x, np.int16)
+    rows = x.reshape(-1, x.shape[-1])
+    n = rows.shape[1]
+    xs, g, gs = _c(x_shifts, np.uint8), _c(gamma, np.int8), _c(gamma_shifts, np.uint8)
+    lut = _c(rsqrt_lut, np.int16)
+    if len(xs) != n or len(g) != n or len(gs) != n:
+        raise OracleError("rmsnorm_i16", ERR_SHAPE)
+    out = np.zeros_like(rows)
+    for r in range(rows.shape[0]):
+        _check("rmsnorm_i16", lib().mylo_rmsnorm_i16(
+            _ptr(rows[r]), n, _ptr(xs), _ptr(g), _ptr(gs), _ptr(lut), len(lut), lut_input_shift,
+            lut_output_frac, inv_n, out_frac_bits, _ptr(out[r])))
+    return out.reshape(x.shape)
+
+
+def rotate_half_split_i16(vec, cos_row, sin_row, frac_bits: int) -> np.ndarray:
+    """rope.rs:17-32."""
+    v = _c(vec, np.int16)
+    c, s = _c(cos_row, np.int16), _c(sin_row, np.int16)
+    if len(c) != len(v) // 2 or len(s) != len(v) // 2:
+        raise OracleError("rotate_half_split_i16", ERR_SHAPE)
+    out = np.zeros_like(v)
+    _check("rotate_half_split_i16", lib().mylo_rotate_half_split_i16(
+        _ptr(v), len(v), _ptr(c), _ptr(s), frac_bits, _ptr(out)))
+    return out
+
+
+def attention_int(q, k, v, mask, score_mult: int, score_shift: int, exp_lut, lut_shift: int,
+                  prob_frac_bits: int) -> np.ndarray:
+    """attention.rs:42-94; q [q_len][d], k/v [kv_len][d], mask [q_len][kv_len] bools or None."""
+    q, k, v = _c(q, np.int16), _c(k, np.int16), _c(v, np.int16)
+    lut = _c(exp_lut, np.int16)
+    mk = None if mask is None else _c(mask, np.uint8)
+    out = np.zeros_like(q)
+    _check("attention_int", lib().mylo_attention_int(
+        _ptr(q), q.shape[0], _ptr(k), _ptr(v), k.shape[0], q.shape[1],
+        None if mk is None else _ptr(mk), score_mult, score_shift, _ptr(lut), len(lut), lut_shift,
+        prob_frac_bits, _ptr(out)))
+    return out
+
+
+class _Layer(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in (
+        "ln1_gamma", "ln1_gamma_shifts", "ln2_gamma", "ln2_gamma_shifts",
+        "wq", "wk", "wv", "wo", "wg", "wu", "wd",
+        "sq", "sk", "sv", "so", "sg", "su", "sd", "bq", "bk", "bv",
+        "bq_shifts", "bk_shifts", "bv_shifts")] + [(n, C.c_uint8) for n in (
+        "norm_attn_frac", "q_frac", "k_frac", "v_frac", "attn_out_frac", "norm_mlp_frac",
+        "gate_frac", "up_frac", "down_in_frac")] + [
+        ("residual_in_frac", C.c_void_p), ("residual_mid_frac", C.c_void_p)]
+
+
+class _Model(C.Structure):
+    _fields_ = [(n, C.c_int64) for n in (
+        "vocab", "hidden", "num_layers", "num_heads", "num_kv_heads", "head_dim",
+        "intermediate")] + [(n, C.c_void_p) for n in (
+        "embed", "embed_shifts", "lm_head", "lm_head_shifts", "lm_head16", "lm_head16_shifts",
+        "final_gamma", "final_gamma_shifts")] + [
+        ("final_norm_frac", C.c_uint8), ("final_residual_frac", C.c_void_p),
+        ("layers", C.c_void_p), ("cos_lut", C.c_void_p), ("sin_lut", C.c_void_p),
+        ("rope_len", C.c_int64), ("exp_lut", C.c_void_p), ("exp_len", C.c_int64),
+        ("silu_lut", C.c_void_p), ("silu_len", C.c_int64), ("rsqrt_lut", C.c_void_p),
+        ("rsqrt_len", C.c_int64)] + [(n, C.c_uint8) for n in (
+        "score_frac_bits", "exp_input_frac", "prob_frac_bits", "rope_frac_bits", "silu_in_frac",
+        "silu_out_frac", "rsqrt_input_shift", "rsqrt_output_frac", "logit_frac_bits")] + [
+        ("silu_lut_offset", C.c_int16)]
+
+
+_LAYER_ARRAYS = {
+    "ln1_gamma": np.int8, "ln1_gamma_shifts": np.uint8, "ln2_gamma": np.int8,
+    "ln2_gamma_shifts": np.uint8, "wq": np.int8, "wk": np.int8, "wv": np.int8, "wo": np.int8,
+    "wg": np.int8, "wu": np.int8, "wd": np.int8, "sq": np.uint8, "sk": np.uint8, "sv": np.uint8,
+    "so": np.uint8, "sg": np.uint8, "su": np.uint8, "sd": np.uint8, "bq": np.int16,
+    "bk": np.int16, "bv": np.int16, "bq_shifts": np.uint8, "bk_shifts": np.uint8,
+    "bv_shifts": np.uint8, "residual_in_frac": np.uint8, "residual_mid_frac": np.uint8}
+
+
+class OracleModel:
+    """The reference IntegerModel (runtime/src/model.rs) on the CPU, built from
+    any object with ModelSpec's attributes (vocab, hidden, ..., layers, luts,
+    constants). Holds the KV cache of one sequence (kv_cache.rs)."""
+
+    def __init__(self, spec, max_positions: int):
+        self._keep = []
+        H = spec.hidden
+
+        def arr(a, dt):
+            if a is None:
+                return None
+            a = _c(a, dt)
+            self._keep.append(a)
+            return _ptr(a)
+
+        layers = (_Layer * spec.num_layers)()
+        for i, Ls in enumerate(spec.layers):
+            L = layers[i]
+            for name, dt in _LAYER_ARRAYS.items():
+                setattr(L, name, arr(getattr(Ls, name), dt))
+            for name in ("norm_attn_frac", "q_frac", "k_frac", "v_frac", "attn_out_frac",
+                         "norm_mlp_frac", "gate_frac", "up_frac", "down_in_frac"):
+                setattr(L, name, int(getattr(Ls, name)))
+        self._layers = layers
+        m = _Model()
+        for n in ("vocab", "hidden", "num_layers", "num_heads", "num_kv_heads", "head_dim",
+                  "intermediate"):
+            setattr(m, n, int(getattr(spec, n)))
+        m.embed = arr(spec.embed, np.int8)
+        m.embed_shifts = arr(spec.embed_shifts, np.uint8)
+        if spec.lm_head is None:
+            m.lm_head, m.lm_head_shifts = m.embed, m.embed_shifts
+        else:
+            m.lm_head = arr(spec.lm_head, np.int8)
+            m.lm_head_shifts = arr(spec.lm_head_shifts, np.uint8)
+        m.lm_head16 = arr(spec.lm_head16, np.int16)
+        m.lm_head16_shifts = arr(spec.lm_head16_shifts, np.uint8)
+        m.final_gamma = arr(spec.final_gamma, np.int8)
+        m.final_gamma_shifts = arr(spec.final_gamma_shifts, np.uint8)
+        m.final_norm_frac = int(spec.final_norm_frac)
+        m.final_residual_frac = arr(spec.final_residual_frac, np.uint8)
+        m.layers = C.cast(layers, C.c_void_p)
+        for name in ("cos_lut", "sin_lut", "exp_lut", "silu_lut", "rsqrt_lut"):
+            a = _c(getattr(spec, name), np.int16)
+            self._keep.append(a)
+            setattr(m, name, _ptr(a))
+            setattr(m, {"cos_lut": "rope_len", "sin_lut": "rope_len", "exp_lut": "exp_len",
+                        "silu_lut": "silu_len", "rsqrt_lut": "rsqrt_len"}[name], len(a))
+        for n, v in spec.constants.items():
+            setattr(m, n, int(v))
+        self._m = m
+        self.spec = spec
+        self.max_positions = int(max_positions)
+        shape = (spec.num_layers, spec.num_kv_heads, self.max_positions, spec.head_dim)
+        self.k_cache = np.zeros(shape, np.int16)
+        self.v_cache = np.zeros(shape, np.int16)
+        self.vocab = spec.vocab
+        self.hidden = H
+
+    def forward(self, tokens, pos0: int, want_logits: bool = True):
+        """forward_token for consecutive tokens at pos0.. (logits of the last)."""
+        t = _c(tokens, np.int32).reshape(-1)
+        logits = np.zeros(self.vocab, np.int32) if want_logits else None
+        _check("forward", lib().mylo_forward(
+            C.byref(self._m), _ptr(self.k_cache), _ptr(self.v_cache), self.max_positions, _ptr(t),
+            len(t), pos0, None if logits is None else _ptr(logits)))
+        return logits
+
+    def generate(self, prompt, max_new: int, keep_logits: bool = True):
+        """dekodieren_mit_digest, greedy: (tokens [max_new], step logits or None)."""
+        p = _c(prompt, np.int32).reshape(-1)
+        out = np.zeros(max_new, np.int32)
+        lg = np.zeros((max_new, self.vocab), np.int32) if keep_logits else None
+        _check("generate", lib().mylo_generate(
+            C.byref(self._m), _ptr(self.k_cache), _ptr(self.v_cache), self.max_positions, _ptr(p),
+            len(p), max_new, _ptr(out), None if lg is None else _ptr(lg)))
+        return out, lg

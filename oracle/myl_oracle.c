@@ -361,8 +361,28 @@ int mylo_mlp_hidden(const int16_t* x, int64_t M, const int8_t* W_gate, const int
   int16_t* up = (int16_t*)malloc(sizeof(int16_t) * (size_t)(M * I));
   linear_rows(x, M, W_gate, H, I, gate_w_shifts, in_frac, NULL, gate_out_frac, gate);
   linear_rows(x, M, W_up, H, I, up_w_shifts, in_frac, NULL, up_out_frac, up);
+  rc = mylo_silu_product(gate, up, M * I, silu_lut, silu_lut_len, gate_out_frac, up_out_frac,
+                         down_in_frac, silu_in_frac, silu_lut_offset, silu_out_frac, h, silu_wraps);
+  free(gate);
+  free(up);
+  return rc;
+}
+
+/* ---- mlp.rs:52-64: h from the gate and up projections ---------------------- */
+
+int mylo_silu_product(const int16_t* gate, const int16_t* up, int64_t n, const int16_t* silu_lut,
+                      int64_t silu_lut_len, uint8_t gate_out_frac, uint8_t up_out_frac,
+                      uint8_t down_in_frac, uint8_t silu_in_frac, int16_t silu_lut_offset,
+                      uint8_t silu_out_frac, int16_t* h, int64_t* silu_wraps) {
+  int s;
+  if (n < 0 || silu_lut_len <= 0) return MYLO_ERR_SHAPE;
+  if (signed_shift(gate_out_frac, silu_in_frac, 32, &s)) return MYLO_ERR_OVERFLOW;
+  uint8_t prod_frac;
+  if (in_frac_of(silu_out_frac, up_out_frac, &prod_frac)) return MYLO_ERR_OVERFLOW;
+  if (signed_shift(prod_frac, down_in_frac, 64, &s)) return MYLO_ERR_OVERFLOW;
   int64_t wraps = 0;
-  for (int64_t e = 0; e < M * I; ++e) {
+#pragma omp parallel for schedule(static) reduction(+ : wraps)
+  for (int64_t e = 0; e < n; ++e) {
     int32_t g_dom = 0;
     mylo_rescale((int32_t)gate[e], gate_out_frac, silu_in_frac, &g_dom);
     int16_t g16 = (int16_t)(uint16_t)(uint32_t)g_dom; /* `g_dom as i16` */
@@ -374,8 +394,6 @@ int mylo_mlp_hidden(const int16_t* x, int64_t M, const int8_t* W_gate, const int
     mylo_rescale_i64(prod, prod_frac, down_in_frac, &v);
     h[e] = mylo_clamp_i16_from_i64(v);
   }
-  free(gate);
-  free(up);
   if (silu_wraps) *silu_wraps = wraps;
   return MYLO_OK;
 }

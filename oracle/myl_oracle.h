@@ -125,6 +125,13 @@ int mylo_mlp_hidden(const int16_t* x, int64_t M, const int8_t* W_gate, const int
                     uint8_t silu_in_frac, int16_t silu_lut_offset, uint8_t silu_out_frac,
                     int16_t* h, int64_t* silu_wraps);
 
+/* mlp.rs:52-64 on n elements: h = clamp_i16(rescale_i64(silu_lut[idx(gate)] * up,
+ * silu_out + up_out, down_in)), the SiLU index in wrapping i16 arithmetic. */
+int mylo_silu_product(const int16_t* gate, const int16_t* up, int64_t n, const int16_t* silu_lut,
+                      int64_t silu_lut_len, uint8_t gate_out_frac, uint8_t up_out_frac,
+                      uint8_t down_in_frac, uint8_t silu_in_frac, int16_t silu_lut_offset,
+                      uint8_t silu_out_frac, int16_t* h, int64_t* silu_wraps);
+
 /* softmax.rs:24-64 (exp LUT lookup softmax.rs:12-21, RNE division). */
 int mylo_softmax_int(const int32_t* logits, int64_t n, const int16_t* exp_lut, int64_t lut_len,
                      uint8_t lut_shift, uint8_t frac_bits, int32_t* out);
