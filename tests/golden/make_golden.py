@@ -20,6 +20,11 @@ Outputs written:
                       rshift_round and linear_w8a16_ref.
   op_vectors.json     the reference's op golden vector linear_w8a16_identity
                       (conformance/vectors/op/linear_w8a16_identity.golden.json)
+  forward_cases.json  rmsnorm_i16: the op golden vector rmsnorm_basic and seeded
+                      rows computed by generate.py:66 rmsnorm_i16_ref (the
+                      uniform-shift form of rmsnorm.rs:61); the SHA-256 of the
+                      LUT files shipped in scale_packs/qwen2.5-{0.5b,7b}/
+                      (luts.json), which the LUT generators are checked against.
   backward_cases.json the op golden vector backward_linear
                       (conformance/vectors/op/backward_linear.golden.json)
                       re-emitted in this repo's fixture format.
@@ -245,6 +250,39 @@ def make_backend_parity(G):
     return [lin, mlp]
 
 
+def make_forward(G, ref_root: str):
+    """RMSNorm cases and the scale packs' LUT hashes (see the module docstring)."""
+    vp = os.path.join(ref_root, "INTEGER_LLM", "conformance", "vectors", "op",
+                      "rmsnorm_basic.golden.json")
+    with open(vp) as f:
+        v = json.load(f)
+    md = v["metadata"]
+    cases = [{
+        "name": v["name"], "x": v["inputs"]["x"]["data"], "gamma": v["inputs"]["gamma"]["data"],
+        "x_shift": 0, "gamma_shift": md["gamma_shift"], "lut": md["rsqrt_lut"],
+        "lut_input_shift": md["lut_input_shift"], "lut_output_frac": md["lut_output_frac"],
+        "inv_n_q20": md["inv_n_q20"], "out_frac": md["out_frac"], "y": v["outputs"]["y"]["data"]}]
+    lut = G.spec_rsqrt_lut(32768)
+    rng = np.random.default_rng(7)
+    for i, (n, sigma, out_frac, gshift) in enumerate(
+            ((896, 3000, 10, 6), (896, 40, 12, 6), (64, 30000, 8, 5), (3584, 800, 11, 7),
+             (7, 1, 14, 6), (128, 12000, 6, 4), (896, 0, 10, 6))):
+        x = np.clip(np.rint(rng.normal(0, sigma, size=n)), -32768, 32767).astype(int).tolist()
+        gamma = rng.integers(-128, 128, size=n).astype(int).tolist()
+        y = G.rmsnorm_i16_ref(x, gamma, gshift, lut, 8, 8, G.inv_n_q20(n), out_frac)
+        cases.append({"name": f"rmsnorm_ref_{i}", "x": x, "gamma": gamma,
+                      "x_shift": int(rng.integers(0, 16)), "gamma_shift": gshift,
+                      "lut": "spec_rsqrt_32768", "lut_sha256": sha(np.array(lut, "<i2")),
+                      "lut_input_shift": 8, "lut_output_frac": 8, "inv_n_q20": G.inv_n_q20(n),
+                      "out_frac": out_frac, "y": [int(t) for t in y]})
+    packs = {}
+    for pack in ("qwen2.5-0.5b", "qwen2.5-7b"):
+        with open(os.path.join(ref_root, "INTEGER_LLM", "scale_packs", pack, "luts.json")) as f:
+            packs[pack] = {k: {"length": e["length"], "sha256": e["hash"]}
+                           for k, e in json.load(f).items()}
+    return {"rmsnorm": cases, "scale_pack_luts": packs}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="root of the Myelith checkout")
@@ -323,6 +361,8 @@ def main():
         json.dump(make_mlp(G), f, separators=(",", ":"))
     with open(os.path.join(HERE, "backend_parity.json"), "w") as f:
         json.dump(make_backend_parity(G), f, separators=(",", ":"))
+    with open(os.path.join(HERE, "forward_cases.json"), "w") as f:
+        json.dump(make_forward(G, args.reference), f, separators=(",", ":"))
     print("fixtures written to", HERE)
 
 
