@@ -457,6 +457,114 @@ int myl_wire_encode_dev(myl_ctx* ctx, const myl_wire_meta* meta, const int16_t* 
 int myl_wire_pack_tokens(const uint32_t* tokens, uint64_t n, int16_t* out);
 int myl_wire_unpack_tokens(const int16_t* values, uint64_t n_values, uint32_t* tokens);
 
+/* --- Integer decoder forward (runtime/src/model.rs, generate.rs) ------------------
+ * The model of the reference's IntegerModel (model.rs:120-163): embedding,
+ * num_layers transformer layers (forward_layer, model.rs:401-674: RMSNorm,
+ * q/k/v with int16 biases, RoPE, KV cache, GQA attention with softmax_int,
+ * o_proj onto the coarser residual scale, residual add, RMSNorm, mlp_int,
+ * residual add), final RMSNorm and the LM head (path A int16 or path B int8,
+ * i32 logits). All tensors are host arrays in the artifact layout (row-major
+ * [out][in], one power-of-two shift per row; per-channel residual shifts);
+ * myl_model_create validates every shift as the reference's debug build would
+ * and uploads the model once. Results are bit-identical to the reference. */
+typedef struct myl_layer_spec {
+  const int8_t* ln1_gamma;          /* input_layernorm [hidden] */
+  const uint8_t* ln1_gamma_shifts;
+  const int8_t* ln2_gamma;          /* post_attention_layernorm [hidden] */
+  const uint8_t* ln2_gamma_shifts;
+  const int8_t* wq;                 /* [heads*head_dim][hidden] */
+  const int8_t* wk;                 /* [kv_heads*head_dim][hidden] */
+  const int8_t* wv;
+  const int8_t* wo;                 /* [hidden][heads*head_dim] */
+  const int8_t* wg;                 /* [intermediate][hidden] */
+  const int8_t* wu;
+  const int8_t* wd;                 /* [hidden][intermediate] */
+  const uint8_t *sq, *sk, *sv, *so, *sg, *su, *sd; /* per-row weight shifts */
+  const int16_t *bq, *bk, *bv;      /* int16 biases, NULL: no attention bias */
+  const uint8_t *bq_shifts, *bk_shifts, *bv_shifts;
+  uint8_t norm_attn_frac, q_frac, k_frac, v_frac, attn_out_frac;
+  uint8_t norm_mlp_frac, gate_frac, up_frac, down_in_frac;
+  const uint8_t* residual_in_frac;  /* [hidden] per channel */
+  const uint8_t* residual_mid_frac; /* [hidden] */
+} myl_layer_spec;
+
+typedef struct myl_model_spec {
+  int64_t vocab, hidden, num_layers, num_heads, num_kv_heads, head_dim, intermediate;
+  const int8_t* embed;              /* [vocab][hidden] */
+  const uint8_t* embed_shifts;      /* [vocab] */
+  const int8_t* lm_head;            /* path B [vocab][hidden]; NULL: tied to embed */
+  const uint8_t* lm_head_shifts;
+  const int16_t* lm_head16;         /* path A [vocab][hidden] int16 (used when set) */
+  const uint8_t* lm_head16_shifts;
+  const int8_t* final_gamma;
+  const uint8_t* final_gamma_shifts;
+  uint8_t final_norm_frac;
+  const uint8_t* final_residual_frac; /* [hidden] */
+  const myl_layer_spec* layers;     /* [num_layers] */
+  const int16_t* cos_lut;           /* [rope_len] = [n_pos][head_dim/2] */
+  const int16_t* sin_lut;
+  int64_t rope_len;
+  const int16_t* exp_lut;
+  int64_t exp_len;
+  const int16_t* silu_lut;
+  int64_t silu_len;
+  const int16_t* rsqrt_lut;
+  int64_t rsqrt_len;
+  /* ModelConfig (model.rs:166-203) from theta_v/spec.json (loader.rs:654-682) */
+  uint8_t score_frac_bits, exp_input_frac, prob_frac_bits, rope_frac_bits;
+  uint8_t silu_in_frac, silu_out_frac, rsqrt_input_shift, rsqrt_output_frac, logit_frac_bits;
+  int16_t silu_lut_offset;
+} myl_model_spec;
+
+typedef struct myl_model myl_model;
+typedef struct myl_session myl_session;
+
+/* loader.rs:709-851 build_model: validates and uploads the model. */
+int myl_model_create(myl_ctx* ctx, const myl_model_spec* spec, myl_model** out);
+int myl_model_release(myl_ctx* ctx, myl_model* model);
+/* KV caches of `batch` independent sequences of up to max_positions tokens
+ * each (kv_cache.rs:13-36), plus the work buffers of the forward. */
+int myl_session_create(myl_ctx* ctx, const myl_model* model, int64_t batch, int64_t max_positions,
+                       myl_session** out);
+int myl_session_release(myl_ctx* ctx, myl_session* s);
+/* Empties the caches: the next token goes to position 0. */
+int myl_session_reset(myl_ctx* ctx, myl_session* s);
+/* Number of positions the session's sequences hold. */
+int64_t myl_session_position(const myl_session* s);
+
+/* forward_token (model.rs:229-311) for T tokens of each of the session's B
+ * sequences at the next T positions (host tokens [B][T]); logits [B][vocab]
+ * (host, NULL: not computed) receives each sequence's last-token logits. The
+ * prompt tokens may come in one call: the result equals T single-token calls. */
+int myl_forward(myl_ctx* ctx, const myl_model* model, myl_session* s, const int32_t* tokens,
+                int64_t T, int32_t* logits);
+/* Greedy generation (generate.rs:76-116 / :161-200): from an empty cache,
+ * prefill prompt [B][P], then max_new steps of (argmax_int of the logits,
+ * forward of the chosen token). out_tokens [B][max_new]. digests [B][32]
+ * (NULL: not computed) receives dekodieren_mit_digest's SHA-256 per sequence:
+ * per step the logits as i32 little-endian, then the token as u32
+ * little-endian. step_logits [B][max_new][vocab] (NULL: not kept) receives
+ * the hashed logits. Without digests and step_logits the decode steps run as
+ * one CUDA graph per step with no host synchronisation in between. */
+int myl_generate(myl_ctx* ctx, const myl_model* model, myl_session* s, const int32_t* prompt,
+                 int64_t P, int64_t max_new, int32_t* out_tokens, uint8_t* digests,
+                 int32_t* step_logits);
+
+/* Building blocks on the device (the reference functions they restate). */
+/* rmsnorm_i16 (rmsnorm.rs:61-153) on M rows [M][ldx] -> [M][ldo]; the
+ * parameters are host arrays [n]. */
+int myl_rmsnorm_i16(myl_ctx* ctx, const int16_t* x, int64_t M, int64_t n, const uint8_t* x_shifts,
+                    const int8_t* gamma, const uint8_t* gamma_shifts, const int16_t* rsqrt_lut,
+                    int64_t lut_len, uint8_t lut_input_shift, uint8_t lut_output_frac,
+                    int64_t inv_n_q20, uint8_t out_frac_bits, int16_t* out);
+/* attention_int (attention.rs:42-94), host arrays: q [q_len][head_dim],
+ * k/v [kv_len][head_dim], mask [q_len][kv_len] bytes (nonzero: attend; NULL:
+ * all), out [q_len][head_dim]. */
+int myl_attention_int(myl_ctx* ctx, const int16_t* q, int64_t q_len, const int16_t* k,
+                      const int16_t* v, int64_t kv_len, int64_t head_dim, const uint8_t* mask,
+                      int64_t score_mult, uint8_t score_shift, const int16_t* exp_lut,
+                      int64_t exp_len, uint8_t lut_shift, uint8_t prob_frac_bits, int16_t* out);
+
 /* --- Allocation-free variant ------------------------------------------------------
  * No counterpart in the reference: its CPU path never allocates device memory.
  *

@@ -6,7 +6,9 @@
 // Included by myl_w8a16.cu (uses its fail() / TRY machinery).
 #pragma once
 
+#include <algorithm>
 #include <cstdio>
+#include <cstring>
 #include <fstream>
 #include <map>
 #include <sstream>
@@ -57,27 +59,24 @@ static const Sha256Tables& sha_tables() {
 
 static inline uint32_t rotr(uint32_t x, int r) { return (x >> r) | (x << (32 - r)); }
 
-static void sha256(const uint8_t* data, size_t len, uint8_t out[32]) {
-  const Sha256Tables& T = sha_tables();
+// Incremental form: update() any number of times, then finish().
+struct Sha256Stream {
   uint32_t h[8];
-  for (int i = 0; i < 8; ++i) h[i] = T.h0[i];
-  const uint64_t bits = uint64_t(len) * 8;
-  const size_t padded = ((len + 9 + 63) / 64) * 64;
-  uint8_t block[64];
-  for (size_t off = 0; off < padded; off += 64) {
-    for (int i = 0; i < 64; ++i) {
-      const size_t pos = off + size_t(i);
-      uint8_t b;
-      if (pos < len) b = data[pos];
-      else if (pos == len) b = 0x80;
-      else if (pos >= padded - 8) b = uint8_t(bits >> (8 * (padded - 1 - pos)));
-      else b = 0;
-      block[i] = b;
-    }
+  uint8_t buf[64];
+  size_t fill = 0;
+  uint64_t total = 0;
+
+  Sha256Stream() {
+    const Sha256Tables& T = sha_tables();
+    for (int i = 0; i < 8; ++i) h[i] = T.h0[i];
+  }
+
+  void block(const uint8_t* blk) {
+    const Sha256Tables& T = sha_tables();
     uint32_t w[64];
     for (int i = 0; i < 16; ++i)
-      w[i] = (uint32_t(block[4 * i]) << 24) | (uint32_t(block[4 * i + 1]) << 16) |
-             (uint32_t(block[4 * i + 2]) << 8) | uint32_t(block[4 * i + 3]);
+      w[i] = (uint32_t(blk[4 * i]) << 24) | (uint32_t(blk[4 * i + 1]) << 16) |
+             (uint32_t(blk[4 * i + 2]) << 8) | uint32_t(blk[4 * i + 3]);
     for (int i = 16; i < 64; ++i) {
       const uint32_t s0 = rotr(w[i - 15], 7) ^ rotr(w[i - 15], 18) ^ (w[i - 15] >> 3);
       const uint32_t s1 = rotr(w[i - 2], 17) ^ rotr(w[i - 2], 19) ^ (w[i - 2] >> 10);
@@ -95,8 +94,43 @@ static void sha256(const uint8_t* data, size_t len, uint8_t out[32]) {
     }
     h[0] += a; h[1] += b; h[2] += c; h[3] += d; h[4] += e; h[5] += f; h[6] += g; h[7] += hh;
   }
-  for (int i = 0; i < 8; ++i)
-    for (int j = 0; j < 4; ++j) out[4 * i + j] = uint8_t(h[i] >> (24 - 8 * j));
+
+  void update(const uint8_t* data, size_t len) {
+    total += len;
+    if (fill) {
+      const size_t take = std::min(len, size_t(64) - fill);
+      std::memcpy(buf + fill, data, take);
+      fill += take;
+      data += take;
+      len -= take;
+      if (fill < 64) return;
+      block(buf);
+      fill = 0;
+    }
+    for (; len >= 64; data += 64, len -= 64) block(data);
+    if (len) {
+      std::memcpy(buf, data, len);
+      fill = len;
+    }
+  }
+
+  void finish(uint8_t out[32]) {
+    const uint64_t bits = total * 8;
+    const uint8_t one = 0x80, zero = 0;
+    update(&one, 1);
+    while (fill != 56) update(&zero, 1);
+    uint8_t len_be[8];
+    for (int i = 0; i < 8; ++i) len_be[i] = uint8_t(bits >> (56 - 8 * i));
+    update(len_be, 8);
+    for (int i = 0; i < 8; ++i)
+      for (int j = 0; j < 4; ++j) out[4 * i + j] = uint8_t(h[i] >> (24 - 8 * j));
+  }
+};
+
+static void sha256(const uint8_t* data, size_t len, uint8_t out[32]) {
+  Sha256Stream st;
+  st.update(data, len);
+  st.finish(out);
 }
 
 static std::string sha256_hex(const std::vector<uint8_t>& v) {

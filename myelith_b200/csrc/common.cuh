@@ -29,6 +29,7 @@ enum DeviceError : int {
   DEV_WAIT_INJECTED = 0x105,  // test hook: a wait on a barrier nothing arrives at
   DEV_WAIT_PEER = 0x106,      // a peer rank did not reach an exchange barrier in time
   DEV_BAD_EXPERT = 0x201,     // an expert id outside the experts this object holds
+  DEV_BAD_TOKEN = 0x202,      // a token id outside the vocabulary (device-side ids)
 };
 
 // Epilogue modes.

@@ -34,6 +34,7 @@
 #include "backward.cuh"
 #include "select.cuh"
 #include "wire.cuh"
+#include "forward.cuh"
 
 using namespace myl;
 
@@ -168,8 +169,13 @@ static int ws_release(myl_ctx* ctx, cudaStream_t st) {
   return MYL_OK;
 }
 
+// Bumped whenever a workspace buffer moves, so that a captured CUDA graph
+// holding the old address is captured again before its next replay.
+static uint64_t g_ws_epoch = 1;
+
 static int ensure(DevBuf& b, size_t bytes) {
   if (b.cap >= bytes) return MYL_OK;
+  ++g_ws_epoch;
   if (b.p) CUDA_TRY(cudaFree(b.p));
   b.p = nullptr;
   b.cap = 0;
@@ -655,8 +661,9 @@ static int check_device_error(myl_ctx* ctx) {
     CUDA_TRY(cudaMemsetAsync(ctx->d_err, 0, sizeof(int), ctx->stream));
     CUDA_TRY(cudaStreamSynchronize(ctx->stream));
     return fail(MYL_ERR_DEVICE, "kernel reported error 0x%x (%s)", e,
-                e == DEV_BAD_EXPERT ? "an expert id outside this object's experts"
-                                    : "a bounded wait ran out");
+                e == DEV_BAD_EXPERT  ? "an expert id outside this object's experts"
+                : e == DEV_BAD_TOKEN ? "a token id outside the vocabulary"
+                                     : "a bounded wait ran out");
   }
   return MYL_OK;
 }
@@ -2669,3 +2676,5 @@ int myl_wire_unpack_tokens(const int16_t* values, uint64_t n_values, uint32_t* t
 }
 
 }  // extern "C"
+
+#include "model.cuh"
