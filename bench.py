@@ -222,6 +222,19 @@ class ClockSampler:
 # CPU oracle (the reference's algorithm): bounded samples
 
 
+def config1(tp: int, exchange: str = "p2p") -> dict:
+    """The config object of the config-1 line, the same for both arms."""
+    n1, k2 = SHAPES[0][1] // tp, SHAPES[1][0] // tp
+    per_set = n1 * SHAPES[0][0] + SHAPES[1][1] * k2
+    nsets = max(2, math.ceil(4 * L2_BYTES / per_set))
+    par = f"tp{tp}" if tp == 1 else (f"tp{tp}, row-parallel exchange: " + (
+        "peer memory from the GEMM epilogue" if exchange == "p2p" else "NCCL reduce-scatter + all-gather"))
+    return {"workload": "config1: W8A16 linear at Qwen2.5-7B MLP shapes, gate/up + down per step",
+            "M": M_HEAD, "shapes_KN": SHAPES, "parallelism": par,
+            "l2": f"inputs larger than L2: {nsets} rotating weight sets "
+                  f"({nsets * per_set / 2**20:.0f} MiB per rank)"}
+
+
 def cpu_sample_tops(target_s: float, rng) -> dict:
     """Times the oracle's linear_w8a16 on a row sample of the step (both shapes),
     sized to about target_s seconds, on all host threads."""
@@ -273,8 +286,7 @@ def run_reference(args, rank: int, world: int) -> None:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * secs / args.steps,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "int8xint16->int64", "data": "synthetic",
-        "config": {"workload": "config1: W8A16 linear, Qwen2.5-7B MLP shapes", "M": M_HEAD,
-                   "shapes_KN": SHAPES, "parallelism": "cpu"},
+        "config": config1(world, args.exchange),
         "cpu_baseline": {"value": v, "unit": "TOPS", "cores": O.num_threads(), "kind": "port",
                          "sample": r["sample"]},
         "e2e": {"value": v, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -294,98 +306,99 @@ def moe_ops(T: int) -> float:
     return 2.0 * T * (E * H + k * 3 * I * H + 3 * Is * H)
 
 
-DECODE = dict(H=3584, I=18944, KV=512, V=152064, layers=28, distinct=4)
+FWD_CFG2 = dict(variant="qwen2.5-0.5b", prompt=512, new=128, batch=(1,))
+FWD_CFG3 = dict(variant="qwen2.5-7b", prompt=2048, new=256, batch=(1, 8, 32))
 
 
-def bench_decode(ctx, dev, steps: int, warmup: int, hbm_gbs: float) -> dict:
-    """Qwen2.5-7B-shaped integer decode at batch 1, the W8A16 linears of one
-    token: per layer q (3584 -> 3584), k and v (3584 -> 512), o (3584 -> 3584)
-    and the MLP (gate/up 3584 -> 2 x 18944 with the SiLU epilogue, down 18944 ->
-    3584), 28 layers, then the LM head (3584 -> 152064, int32 logits); all
-    GEMVs at M = 1, replayed as one CUDA graph. Attention, norms, RoPE and the
-    embedding are outside the W8A16 path and not included. Weights: 4 distinct
-    random layers cycled over the 28 (933 MB, larger than L2) plus the LM head."""
-    import torch
+def bench_forward(ctx, cfg: dict, steps: int, warmup: int, hbm_gbs: float, check_tokens: int,
+                  check_new: int) -> dict:
+    """The integer decoder forward (runtime/src/model.rs forward_token,
+    generate.rs greedy) on one GPU: random-init int8 weights of the named
+    Qwen2.5 architecture (myelith_b200.synthetic.synthetic_model), uniform
+    random prompt token ids. Per batch size B: prefill of B x prompt tokens
+    (myl_forward, device time), then `new` greedy decode steps
+    (myl_decode_greedy, one CUDA graph per step, device time), and the whole
+    generate call from host prompt to host tokens (wall clock, e2e).
 
-    import myelith_b200 as myl
+    Parity, in the same run: the CPU oracle's generate (tokens and the
+    SHA-256 logits digest of dekodieren_mit_digest) on sequence 0, with the
+    full workload when check_tokens >= prompt, else a shortened prompt of
+    check_tokens and check_new steps on the same model; the timed decode's
+    tokens must equal the checked run's, and sequence 0's tokens must not
+    depend on the batch size."""
+    import oracle as O
+    from myelith_b200 import model as MD
+    from myelith_b200 import synthetic as SY
 
-    H, I, KV, V, L, D = (DECODE[n] for n in ("H", "I", "KV", "V", "layers", "distinct"))
-    rng = np.random.default_rng(77)
-
-    def lin(n, k):
-        w = ctx.weight(rng.integers(-127, 128, size=(n, k), dtype=np.int8), k,
-                       rng.integers(kbits(k) - 1, kbits(k) + 2, size=n).astype(np.uint8))
-        return w, w.requant(myl.RQ_SHIFT_I16, ACT_FRAC, OUT_FRAC)
-
-    layers = []
-    for _ in range(D):
-        mlp = myl.Mlp(ctx, rng.integers(-127, 128, size=(I, H), dtype=np.int8),
-                      rng.integers(-127, 128, size=(I, H), dtype=np.int8),
-                      rng.integers(-127, 128, size=(H, I), dtype=np.int8), H, I,
-                      np.full(I, kbits(H), np.uint8), np.full(I, kbits(H), np.uint8),
-                      np.full(H, kbits(I), np.uint8),
-                      np.clip(np.arange(-8192, 8192) // 2, -32768, 32767).astype(np.int16),
-                      8, 7, 7, 7, 6, 8192, 8, np.full(H, 8, np.uint8))
-        layers.append(dict(q=lin(H, H), k=lin(KV, H), v=lin(KV, H), o=lin(H, H), mlp=mlp))
-    head = ctx.weight(rng.integers(-127, 128, size=(V, H), dtype=np.int8), H,
-                      np.full(V, kbits(H), np.uint8))
-    head_rq = head.requant(myl.RQ_SHIFT_I32, 8, 6)
-    x = torch.from_numpy(np.clip(np.rint(rng.normal(0, 1024, size=(1, H))), -32767, 32767)
-                         .astype(np.int16)).to(dev)
-    a = x.clone()  # stands for the attention output that o reads
-    q, k_, v_, o_, m_ = (torch.empty((1, n), dtype=torch.int16, device=dev) for n in (H, KV, KV, H, H))
-    logits = torch.empty((1, V), dtype=torch.int32, device=dev)
-    weight_bytes = L * (2 * H * H + 2 * KV * H + 3 * I * H) + V * H
-    l0 = ctx.launch_count
-
-    def token():
-        for j in range(L):
-            ly = layers[j % D]
-            ly["q"][0].linear_dev(ly["q"][1], x, q)
-            ly["k"][0].linear_dev(ly["k"][1], x, k_)
-            ly["v"][0].linear_dev(ly["v"][1], x, v_)
-            ly["o"][0].linear_dev(ly["o"][1], a, o_)
-            ly["mlp"].dev(x, m_)
-        head.linear_dev(head_rq, x, logits)
-
-    s = torch.cuda.Stream()
-    with torch.cuda.stream(s):
-        for _ in range(max(warmup, 1)):
-            token()
-    s.synchronize()
-    launches = (ctx.launch_count - l0) / max(warmup, 1)
-    graph = torch.cuda.CUDAGraph()
-    try:
-        with torch.cuda.graph(graph, stream=s):
-            token()
-        replay, graphed = graph.replay, True
-    except Exception:  # capture refused: time the eager launches instead
-        torch.cuda.synchronize()
-        replay, graphed = token, False
-    with torch.cuda.stream(s):
-        for _ in range(3):
-            replay()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(s)
-        for _ in range(steps):
-            replay()
-        e1.record(s)
-    s.synchronize()
-    ctx.synchronize()
-    ms = e0.elapsed_time(e1) / steps
-    # the replayed graph computes what the eager launches compute
-    with torch.cuda.stream(s):
-        replay()
-        got = (logits.clone(), m_.clone())
-        token()
-        same = bool(torch.equal(got[0], logits) and torch.equal(got[1], m_))
-    s.synchronize()
-    return {"workload": "Qwen2.5-7B-shaped decode, batch 1: q/k/v/o, MLP (SiLU epilogue) x 28 layers "
-                        "+ LM head, all W8A16 GEMVs at M=1 (attention, norms, embedding not included)",
-            "tok_s": round(1e3 / ms, 1), "ms_per_token": round(ms, 4),
-            "weight_bytes_per_token": weight_bytes, "gbs": round(weight_bytes / (ms * 1e-3) / 1e9, 1),
-            "frac_of_hbm": round(weight_bytes / (ms * 1e-3) / 1e9 / hbm_gbs, 3),
-            "launches_per_token": launches, "cuda_graph": graphed, "graph_matches_eager": same}
+    t0 = time.perf_counter()
+    spec = SY.synthetic_model(cfg["variant"], seed=2)
+    gm = MD.IntegerModel(ctx, spec)
+    build_s = time.perf_counter() - t0
+    P, N = cfg["prompt"], cfg["new"]
+    prompts = {b: SY.prompt_tokens(spec.vocab, P, seed=100 + b) for b in range(max(cfg["batch"]))}
+    # ---- parity against the oracle (sequence 0) ----
+    cP, cN = (P, N) if check_tokens >= P else (check_tokens, check_new)
+    t0 = time.perf_counter()
+    om = O.OracleModel(spec, cP + cN)
+    otok, olg = om.generate(prompts[0][:cP], cN)
+    o_digest = MD.digest(olg, otok)
+    oracle_s = time.perf_counter() - t0
+    del om, olg
+    gtok, gdig, _ = gm.generate(prompts[0][:cP], cN, digest=True)
+    parity = bool(np.array_equal(gtok[0], otok)) and gdig[0] == o_digest
+    out = {"workload": f"{cfg['variant']} architecture, random-init int8 weights, {P} random prompt "
+                       f"tokens then {N} greedy decode steps",
+           "weight_bytes_per_token": int(spec.weight_bytes_per_token()),
+           "model_build_s": round(build_s, 1),
+           "parity": parity,
+           "parity_check": {"sequence": 0, "prompt": cP, "new": cN, "oracle_s": round(oracle_s, 1),
+                            "tokens_equal": bool(np.array_equal(gtok[0], otok)),
+                            "digest": o_digest, "digest_equal": gdig[0] == o_digest,
+                            "cores": O.num_threads()},
+           "batches": []}
+    seq0 = None
+    for B in cfg["batch"]:
+        pr = np.stack([prompts[b] for b in range(B)])
+        sess = gm.session(B, P + N)
+        pre, dec, e2e, toks = [], [], [], None
+        for it in range(warmup + steps):
+            sess.reset()
+            sess.forward(pr, want_logits=False)
+            tk, _, _ = sess.decode(N)
+            pms, dms = sess.timing()
+            if it >= warmup:
+                pre.append(pms)
+                dec.append(dms)
+            toks = tk if toks is None else toks
+            if not np.array_equal(tk, toks):
+                parity = False
+        for it in range(max(1, steps // 2)):
+            w0 = time.perf_counter()
+            tk, _, _ = gm.generate(pr, N, session=sess)
+            e2e.append(time.perf_counter() - w0)
+            if not np.array_equal(tk, toks):
+                parity = False
+        if seq0 is None:
+            seq0 = toks[0].copy()
+        elif not np.array_equal(toks[0], seq0):
+            parity = False
+        if cP == P and cN == N and not np.array_equal(toks[0], otok):
+            parity = False
+        if cP == P and cN < N and not np.array_equal(toks[0][:cN], otok):
+            parity = False
+        sess.release()
+        pms, dms = statistics.median(pre), statistics.median(dec)
+        wb = spec.weight_bytes_per_token()
+        out["batches"].append({
+            "batch": B, "prefill_tok_s": round(B * P / (pms * 1e-3), 1), "prefill_ms": round(pms, 3),
+            "decode_tok_s": round(B * N / (dms * 1e-3), 1), "decode_ms_per_step": round(dms / N, 4),
+            "decode_weight_gbs": round(wb * N / (dms * 1e-3) / 1e9, 1),
+            "decode_frac_of_hbm": round(wb * N / (dms * 1e-3) / 1e9 / hbm_gbs, 3),
+            "e2e_generate_tok_s": round(B * N / statistics.median(e2e), 1),
+            "e2e_generate_s": round(statistics.median(e2e), 4)})
+    out["parity"] = parity
+    gm.release()
+    return out
 
 
 def bench_moe(ctx, dev, stream, rank: int, world: int, local: int, steps: int, warmup: int,
@@ -511,7 +524,7 @@ def main() -> None:
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-moe", action="store_true")
-    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-forward", action="store_true")
     ap.add_argument("--sm-reserve", type=int, default=16,
                     help="N>1 with --exchange nccl: SMs left free for the overlapped collectives")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
@@ -559,10 +572,13 @@ def main() -> None:
     srng = np.random.default_rng(999)
     s1 = srng.integers(kbits(K1) - 1, kbits(K1) + 2, size=N1).astype(np.uint8)[r * n1:(r + 1) * n1]
     s2 = srng.integers(kbits(K2) - 1, kbits(K2) + 2, size=N2).astype(np.uint8)
-    W1s, W2s, R1s, R2s = [], [], [], []
+    W1s, W2s, R1s, R2s, host_w = [], [], [], [], []
     for _ in range(nsets):
-        w1 = ctx.weight(rng.integers(-127, 128, size=(n1, K1), dtype=np.int8), K1, s1)
-        w2 = ctx.weight(rng.integers(-127, 128, size=(N2, k2), dtype=np.int8), k2, s2)
+        h1 = rng.integers(-127, 128, size=(n1, K1), dtype=np.int8)
+        h2 = rng.integers(-127, 128, size=(N2, k2), dtype=np.int8)
+        host_w.append((h1, h2))  # kept for the parity check of the timed step
+        w1 = ctx.weight(h1, K1, s1)
+        w2 = ctx.weight(h2, k2, s2)
         W1s.append(w1)
         W2s.append(w2)
         R1s.append(w1.requant(myl.RQ_SHIFT_I16, ACT_FRAC, OUT_FRAC))
@@ -770,6 +786,33 @@ def main() -> None:
     ctx.synchronize()
     dev_ms = t_start.elapsed_time(t_end)
     dev_ms = max_over_ranks(dev_ms)
+
+    # ---- parity of the last timed step: every output element against the oracle ----
+    import oracle as O
+
+    O.set_num_threads(max(1, (os.cpu_count() or 1) // world))
+    t0 = time.perf_counter()
+    s_last = (args.warmup + args.steps - 1) % nsets
+    h1, h2 = host_w[s_last]
+    want1 = O.linear_w8a16_fast(x1_h, h1.reshape(-1), K1, s1, ACT_FRAC, OUT_FRAC)
+    got1 = y1.cpu().numpy()
+    if tp == 1:
+        want2 = O.linear_w8a16_fast(x2_h, h2.reshape(-1), k2, s2, ACT_FRAC, OUT_FRAC)
+    else:  # row-parallel: the ranks' exact partials, summed, requantised once
+        acc = torch.from_numpy(O.linear_acc_fast(x2_h, h2.reshape(-1), k2, N2)).to(dev)
+        dist.all_reduce(acc, op=dist.ReduceOp.SUM)
+        want2 = O.requant_acc(acc.cpu().numpy(), s2, ACT_FRAC, OUT_FRAC)
+    got2 = p2p_out.get("y2", y2).cpu().numpy()
+    ok = int(np.array_equal(got1, want1) and np.array_equal(got2, want2))
+    if world > 1:
+        t = torch.tensor([ok], dtype=torch.int32, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        ok = int(t.item())
+    parity = {"ok": bool(ok), "elements": int(want1.size + want2.size) * (world if tp > 1 else 1),
+              "checked": "every output of the last timed step, both shapes, against the CPU oracle"
+                         + (" (row-parallel: the ranks' int64 partials summed)" if tp > 1 else ""),
+              "oracle_s": round(time.perf_counter() - t0, 1)}
+    del want1, want2, got1, got2
     ops_step = 2.0 * M * sum(K * N for K, N in SHAPES)
     value = ops_step * args.steps / (dev_ms * 1e-3) / 1e12
     gemm_ms = [a.elapsed_time(b) for a, b in gemm_events]
@@ -803,10 +846,29 @@ def main() -> None:
         for i in range(args.steps):
             e2e_step(i)
         e2e_s = time.perf_counter() - t0
+        # pageable host memory, as a Rust caller's Vec<i16> (linear.rs:43) is
+        y1_pg = np.empty((M, n1), np.int16)
+        y2_pg = np.empty((M, N2), np.int16)
+
+        def e2e_pageable(i):
+            s = i % nsets
+            myl._check("myl_linear_w8a16", L.myl_linear_w8a16(
+                ctx.handle, W1s[s].handle, x1_h.ctypes.data, M, ACT_FRAC, OUT_FRAC, y1_pg.ctypes.data))
+            myl._check("myl_linear_w8a16", L.myl_linear_w8a16(
+                ctx.handle, W2s[s].handle, x2_h.ctypes.data, M, ACT_FRAC, OUT_FRAC, y2_pg.ctypes.data))
+
+        for i in range(args.warmup):
+            e2e_pageable(i)
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            e2e_pageable(i)
+        pg_s = time.perf_counter() - t0
         e2e = {"value": ops_step * args.steps / e2e_s / 1e12, "unit": "TOPS",
                "h2d_bytes_per_step": int(x1_h.nbytes + x2_h.nbytes),
                "d2h_bytes_per_step": int(y1_pin.nbytes + y2_pin.nbytes),
-               "path": "myl_linear_w8a16 (host pointers, pinned), both shapes"}
+               "path": "myl_linear_w8a16 (host pointers, pinned), both shapes",
+               "pageable": {"value": round(ops_step * args.steps / pg_s / 1e12, 3), "unit": "TOPS",
+                            "path": "myl_linear_w8a16 on pageable numpy buffers (a Vec<i16>)"}}
     else:
         x1_pin = torch.from_numpy(x1_h).pin_memory()
         x2_pin = torch.from_numpy(x2_h).pin_memory()
@@ -870,10 +932,16 @@ def main() -> None:
                 "per_shape_gbs": [round(g, 1) for g in gemv_gbs],
                 "bytes": "N*K weights + 2K act + 2N out + N shift bytes per launch"}
 
-    # ---- 7B-shaped decode (N=1) ----
-    decode = None
-    if tp == 1 and not args.no_decode:
-        decode = bench_decode(ctx, dev, max(10, args.steps), args.warmup, peaks["hbm_gbs"])
+    # ---- the integer forward, configs 2 and 3 (N=1) ----
+    forward = None
+    if tp == 1 and not args.no_forward:
+        fs, fw = max(1, min(args.steps, 3)), 1
+        forward = {
+            "config2": bench_forward(ctx, FWD_CFG2, fs, fw, peaks["hbm_gbs"], 1 << 30, 0),
+            "config3": bench_forward(ctx, FWD_CFG3, fs, fw, peaks["hbm_gbs"],
+                                     int(os.environ.get("MYL_CFG3_CHECK_PROMPT", "64")),
+                                     int(os.environ.get("MYL_CFG3_CHECK_NEW", "16"))),
+        }
 
     # ---- MoE layer (config 4): every rank takes part (all_to_all at N > 1) ----
     moe = None
@@ -890,20 +958,16 @@ def main() -> None:
 
     if world > 1:
         barrier()
+    all_parity = parity["ok"] and (forward is None or all(f["parity"] for f in forward.values()))
     if rank == 0:
         line = {
-            "metric": METRIC, "value": round(value, 3), "unit": "TOPS", "n_gpus": world,
+            "metric": METRIC, "value": round(value, 3) if all_parity else None, "unit": "TOPS",
+            "n_gpus": world, "parity": bool(all_parity), "parity_config1": parity,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "int8xint16->int64", "data": "synthetic",
-            "config": {"workload": "config1: W8A16 linear at Qwen2.5-7B MLP shapes, gate/up + down per step",
-                       "M": M, "shapes_KN": SHAPES,
-                       "parallelism": f"tp{tp}" if tp == 1 else
-                       f"tp{tp}, row-parallel exchange: " + ("peer memory from the GEMM epilogue"
-                                                             if xchg is not None else
-                                                             "NCCL reduce-scatter + all-gather"),
-                       "l2": f"inputs larger than L2: {nsets} rotating weight sets "
-                             f"({nsets * per_set / 2**20:.0f} MiB per rank)"},
+            "config": config1(tp, "p2p" if xchg is not None else "nccl") if M == M_HEAD else
+            dict(config1(tp, "p2p" if xchg is not None else "nccl"), M=M),
             "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(eff_peak, 1),
                          "unit": "TFLOP/s", "frac": round(achieved / eff_peak, 4),
                          "traffic": traffic,
@@ -921,7 +985,7 @@ def main() -> None:
             "gemv": gemv,
             "sweep": sweep,
             "moe": moe,
-            "decode": decode,
+            "forward": forward,
             "tp_check": tp_check,
         }
         emit(line)
@@ -929,6 +993,8 @@ def main() -> None:
         xchg.close()
     if world > 1:
         dist.destroy_process_group()
+    if not all_parity:
+        sys.exit(1)  # no number without a passing parity check in the same run
 
 
 if __name__ == "__main__":

@@ -549,6 +549,14 @@ int myl_forward(myl_ctx* ctx, const myl_model* model, myl_session* s, const int3
 int myl_generate(myl_ctx* ctx, const myl_model* model, myl_session* s, const int32_t* prompt,
                  int64_t P, int64_t max_new, int32_t* out_tokens, uint8_t* digests,
                  int32_t* step_logits);
+/* The decode loop of myl_generate alone (generate.rs:101-113), continuing the
+ * session after myl_forward of the prompt: max_new greedy steps from the
+ * last logits. */
+int myl_decode_greedy(myl_ctx* ctx, const myl_model* model, myl_session* s, int64_t max_new,
+                      int32_t* out_tokens, uint8_t* digests, int32_t* step_logits);
+/* Device time (CUDA events on the launching stream) of the session's last
+ * prompt pass (myl_forward or the prefill of myl_generate) and decode loop. */
+int myl_session_timing(const myl_session* s, float* prefill_ms, float* decode_ms);
 
 /* Building blocks on the device (the reference functions they restate). */
 /* rmsnorm_i16 (rmsnorm.rs:61-153) on M rows [M][ldx] -> [M][ldo]; the

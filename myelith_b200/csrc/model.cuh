@@ -96,6 +96,10 @@ struct myl_session {
   int32_t* h_logits = nullptr;    // pinned [B][V]
   cudaGraphExec_t graph = nullptr;
   uint64_t graph_epoch = 0;
+  // device time of the last prefill (myl_forward) and decode loop, CUDA
+  // events on the launching stream
+  cudaEvent_t ev[4] = {};
+  float prefill_ms = 0.f, decode_ms = 0.f;
   std::vector<void*> allocs;
 };
 
@@ -304,6 +308,7 @@ int session_alloc(myl_ctx* ctx, myl_session* s) {
   TRY(dev_alloc(A, &s->next_tok, size_t(B)));
   TRY(dev_alloc(A, &s->last_rows, size_t(B)));
   TRY(dev_alloc(A, &s->out_tokens, size_t(B * s->max_pos)));
+  for (auto& e : s->ev) CUDA_TRY(cudaEventCreate(&e));
   CUDA_TRY(cudaMallocHost(&s->h_pos, sizeof(int64_t)));
   CUDA_TRY(cudaMallocHost(&s->h_tokens, size_t(R) * 4));
   CUDA_TRY(cudaMallocHost(&s->h_logits, size_t(B * m->V) * 4));
@@ -314,6 +319,8 @@ int session_alloc(myl_ctx* ctx, myl_session* s) {
 void release_session(myl_ctx* ctx, myl_session* s) {
   if (ctx) cudaSetDevice(ctx->device);
   if (s->graph) cudaGraphExecDestroy(s->graph);
+  for (auto& e : s->ev)
+    if (e) cudaEventDestroy(e);
   for (void* p : s->allocs) cudaFree(p);
   if (s->h_pos) cudaFreeHost(s->h_pos);
   if (s->h_tokens) cudaFreeHost(s->h_tokens);
@@ -697,34 +704,27 @@ int myl_forward(myl_ctx* ctx, const myl_model* m, myl_session* s, const int32_t*
   CUDA_TRY(cudaSetDevice(ctx->device));
   cudaStream_t st = ctx->stream;
   TRY(ws_acquire(ctx, st));
-  TRY(prefill(ctx, m, s, tokens, T, logits != nullptr, st));
+  CUDA_TRY(cudaEventRecord(s->ev[0], st));
+  TRY(prefill(ctx, m, s, tokens, T, true, st));
+  CUDA_TRY(cudaEventRecord(s->ev[1], st));
   TRY(ws_release(ctx, st));
   if (logits)
     CUDA_TRY(cudaMemcpyAsync(logits, s->logits, size_t(s->B * m->V) * 4, cudaMemcpyDeviceToHost, st));
-  return check_device_error(ctx);
+  TRY(check_device_error(ctx));
+  CUDA_TRY(cudaEventElapsedTime(&s->prefill_ms, s->ev[0], s->ev[1]));
+  return MYL_OK;
 }
 
-int myl_generate(myl_ctx* ctx, const myl_model* m, myl_session* s, const int32_t* prompt, int64_t P,
-                 int64_t max_new, int32_t* out_tokens, uint8_t* digests, int32_t* step_logits) {
-  if (!ctx || !m || !s || s->m != m || !prompt || (max_new > 0 && !out_tokens))
-    return fail(MYL_ERR_ARG, "null argument");
-  if (P <= 0 || max_new < 0) return fail(MYL_ERR_SHAPE, "P = %lld, max_new = %lld", (long long)P,
-                                         (long long)max_new);
-  if (P + max_new > s->max_pos)
-    return fail(MYL_ERR_SHAPE, "%lld positions beyond the session's %lld", (long long)(P + max_new),
-                (long long)s->max_pos);
-  for (int64_t i = 0; i < s->B * P; ++i)
-    if (prompt[i] < 0 || prompt[i] >= m->V)
-      return fail(MYL_ERR_SHAPE, "token id %d outside the vocabulary", prompt[i]);
-  CUDA_TRY(cudaSetDevice(ctx->device));
+// The greedy decode loop from the session's current logits (after a prefill).
+static int decode_loop(myl_ctx* ctx, const myl_model* m, myl_session* s, int64_t max_new,
+                       int32_t* out_tokens, uint8_t* digests, int32_t* step_logits) {
   cudaStream_t st = ctx->stream;
-  TRY(ws_acquire(ctx, st));
-  TRY(set_pos(s, 0, st));
-  TRY(prefill(ctx, m, s, prompt, P, true, st));
+  const int64_t P = s->pos;
   CUDA_TRY(cudaMemsetAsync(s->d_step, 0, 8, st));
   const bool host_steps = digests || step_logits;
   std::vector<Sha256Stream> sha(digests ? size_t(s->B) : 0);
   const size_t lbytes = size_t(m->V) * 4;
+  CUDA_TRY(cudaEventRecord(s->ev[2], st));
   for (int64_t k = 0; k < max_new; ++k) {
     if (host_steps) {
       // the logits this step selects from (generate.rs:182-184), then the token
@@ -773,14 +773,63 @@ int myl_generate(myl_ctx* ctx, const myl_model* m, myl_session* s, const int32_t
       CUDA_TRY(cudaGraphLaunch(s->graph, st));
     }
   }
+  CUDA_TRY(cudaEventRecord(s->ev[3], st));
   s->pos = P + max_new;
-  TRY(ws_release(ctx, st));
   if (max_new > 0) {
     CUDA_TRY(cudaMemcpy2DAsync(out_tokens, size_t(max_new) * 4, s->out_tokens, size_t(s->max_pos) * 4,
                                size_t(max_new) * 4, size_t(s->B), cudaMemcpyDeviceToHost, st));
   }
   TRY(check_device_error(ctx));
+  CUDA_TRY(cudaEventElapsedTime(&s->decode_ms, s->ev[2], s->ev[3]));
   for (int64_t b = 0; b < (digests ? s->B : 0); ++b) sha[size_t(b)].finish(digests + 32 * b);
+  return MYL_OK;
+}
+
+int myl_generate(myl_ctx* ctx, const myl_model* m, myl_session* s, const int32_t* prompt, int64_t P,
+                 int64_t max_new, int32_t* out_tokens, uint8_t* digests, int32_t* step_logits) {
+  if (!ctx || !m || !s || s->m != m || !prompt || (max_new > 0 && !out_tokens))
+    return fail(MYL_ERR_ARG, "null argument");
+  if (P <= 0 || max_new < 0) return fail(MYL_ERR_SHAPE, "P = %lld, max_new = %lld", (long long)P,
+                                         (long long)max_new);
+  if (P + max_new > s->max_pos)
+    return fail(MYL_ERR_SHAPE, "%lld positions beyond the session's %lld", (long long)(P + max_new),
+                (long long)s->max_pos);
+  for (int64_t i = 0; i < s->B * P; ++i)
+    if (prompt[i] < 0 || prompt[i] >= m->V)
+      return fail(MYL_ERR_SHAPE, "token id %d outside the vocabulary", prompt[i]);
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  cudaStream_t st = ctx->stream;
+  TRY(ws_acquire(ctx, st));
+  TRY(set_pos(s, 0, st));
+  CUDA_TRY(cudaEventRecord(s->ev[0], st));
+  TRY(prefill(ctx, m, s, prompt, P, true, st));
+  CUDA_TRY(cudaEventRecord(s->ev[1], st));
+  const int rc = decode_loop(ctx, m, s, max_new, out_tokens, digests, step_logits);
+  CUDA_TRY(cudaEventElapsedTime(&s->prefill_ms, s->ev[0], s->ev[1]));
+  TRY(ws_release(ctx, st));
+  return rc;
+}
+
+int myl_decode_greedy(myl_ctx* ctx, const myl_model* m, myl_session* s, int64_t max_new,
+                      int32_t* out_tokens, uint8_t* digests, int32_t* step_logits) {
+  if (!ctx || !m || !s || s->m != m || (max_new > 0 && !out_tokens))
+    return fail(MYL_ERR_ARG, "null argument");
+  if (s->pos <= 0) return fail(MYL_ERR_ARG, "the session holds no prompt (run myl_forward first)");
+  if (max_new < 0 || s->pos + max_new > s->max_pos)
+    return fail(MYL_ERR_SHAPE, "%lld positions beyond the session's %lld", (long long)(s->pos + max_new),
+                (long long)s->max_pos);
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  TRY(ws_acquire(ctx, ctx->stream));
+  TRY(set_pos(s, s->pos, ctx->stream));
+  const int rc = decode_loop(ctx, m, s, max_new, out_tokens, digests, step_logits);
+  TRY(ws_release(ctx, ctx->stream));
+  return rc;
+}
+
+int myl_session_timing(const myl_session* s, float* prefill_ms, float* decode_ms) {
+  if (!s) return fail(MYL_ERR_ARG, "null argument");
+  if (prefill_ms) *prefill_ms = s->prefill_ms;
+  if (decode_ms) *decode_ms = s->decode_ms;
   return MYL_OK;
 }
 

@@ -5,10 +5,11 @@ Host-side mirror of the reference runtime's model API
 libmyl_w8a16.so (``myl_model_*``, include/myl_w8a16.h):
 
   IntegerModel(ctx, spec)                  loader.rs:709-851 build_model
-  IntegerModel.forward_token(tok, pos, s)  model.rs:229-311
-  IntegerModel.generate(prompt, n)         generate.rs:13-67 (greedy)
-  IntegerModel.generate_with_digest(...)   generate.rs:161-200 dekodieren_mit_digest
   Session(model, batch, max_positions)     kv_cache.rs:13-36 KVCache::new
+  Session.forward(tokens)                  model.rs:229-311 forward_token (T tokens)
+  Session.decode(n, digest=...)            generate.rs:101-113 / :181-196 (greedy)
+  IntegerModel.generate(prompt, n,         generate.rs:76-116 generate (greedy) and,
+                        digest=True)       :161-200 dekodieren_mit_digest
 
 ``ModelSpec`` / ``LayerSpec`` hold the tensors and calibrated scales the
 reference's IntegerModel / TransformerLayer hold (model.rs:62-163), as numpy
@@ -197,6 +198,8 @@ def _lib():
                 ("myl_session_position", [vp], i64),
                 ("myl_forward", [vp, vp, vp, vp, i64, vp], i32),
                 ("myl_generate", [vp, vp, vp, vp, i64, i64, vp, vp, vp], i32),
+                ("myl_decode_greedy", [vp, vp, vp, i64, vp, vp, vp], i32),
+                ("myl_session_timing", [vp, C.POINTER(C.c_float), C.POINTER(C.c_float)], i32),
                 ("myl_rmsnorm_i16", [vp, vp, i64, i64, vp, vp, vp, vp, i64, C.c_uint8, C.c_uint8,
                                      i64, C.c_uint8, vp], i32),
                 ("myl_attention_int", [vp, vp, i64, vp, vp, i64, i64, vp, i64, C.c_uint8, vp, i64,
@@ -344,6 +347,24 @@ class Session:
             self.model.ctx.handle, self.model.handle, self._h, t.ctypes.data, t.shape[1],
             None if lg is None else lg.ctypes.data))
         return lg
+
+    def decode(self, max_new: int, digest: bool = False, keep_logits: bool = False):
+        """The greedy decode loop (generate.rs:101-113) after forward() of the
+        prompt: (tokens [B][max_new], digests or None, step logits or None)."""
+        B, V = self.batch, self.model.vocab
+        out = np.zeros((B, max_new), np.int32)
+        dg = np.zeros((B, 32), np.uint8) if digest else None
+        lg = np.zeros((B, max_new, V), np.int32) if keep_logits else None
+        _check("myl_decode_greedy", _lib().myl_decode_greedy(
+            self.model.ctx.handle, self.model.handle, self._h, max_new, out.ctypes.data,
+            None if dg is None else dg.ctypes.data, None if lg is None else lg.ctypes.data))
+        return out, (None if dg is None else [bytes(d).hex() for d in dg]), lg
+
+    def timing(self) -> tuple[float, float]:
+        """Device ms of the last prompt pass and of the last decode loop."""
+        a, b = C.c_float(), C.c_float()
+        _check("myl_session_timing", _lib().myl_session_timing(self._h, C.byref(a), C.byref(b)))
+        return float(a.value), float(b.value)
 
     def release(self) -> None:
         if self._h:

@@ -96,6 +96,9 @@ def lib():
         L.mylo_rotate_half_split_i16.argtypes = [p, i64, p, p, u8, p]
         L.mylo_attention_int.argtypes = [p, i64, p, p, i64, i64, p, i64, u8, p, i64, u8, u8, p]
         L.mylo_forward.argtypes = [p, p, p, i64, p, i64, i64, p]
+        L.mylo_linear_w8a16_pc_fast.argtypes = [p, i64, p, i64, i64, p, u8, p, p]
+        L.mylo_linear_acc_fast.argtypes = [p, i64, p, i64, i64, p]
+        L.mylo_requant_acc.argtypes = [p, i64, i64, p, u8, p, p]
         L.mylo_generate.argtypes = [p, p, p, i64, p, i64, i64, p, p]
         L.mylo_moe_route.argtypes = [p, i64, i64, i64, p, i64, u8, u8, p, p]
         L.mylo_moe_combine.argtypes = [p, p, p, i64, i64, i64, u8, p]
@@ -411,6 +414,62 @@ def set_num_threads(n: int) -> None:
 
 
 # ---- forward pass (myl_forward.c) ---------------------------------------------
+
+def linear_w8a16_fast(x, W, in_features: int, w_shifts, act_frac: int, out_frac) -> np.ndarray:
+    """linear_w8a16 / linear_w8a16_pc with the blocked exact dot (same outputs
+    as linear_w8a16_pc; out_frac scalar or per channel)."""
+    x = _c(x, np.int16).reshape(-1, in_features)
+    W = _c(W, np.int8)
+    ws = _c(w_shifts, np.uint8)
+    N = len(ws)
+    of = _c(np.broadcast_to(np.asarray(out_frac, np.uint8), (N,)), np.uint8)
+    y = np.zeros((x.shape[0], N), np.int16)
+    _check("linear_w8a16_pc_fast", lib().mylo_linear_w8a16_pc_fast(
+        _ptr(x), x.shape[0], _ptr(W), in_features, N, _ptr(ws), act_frac, _ptr(of), _ptr(y)))
+    return y
+
+
+def mlp_int_fast(x, W_gate, W_up, W_down, hidden_size: int, intermediate_size: int,
+                 gate_w_shifts, up_w_shifts, down_w_shifts, silu_lut, in_frac_bits: int,
+                 gate_out_frac: int, up_out_frac: int, down_in_frac: int, silu_in_frac: int,
+                 silu_lut_offset: int, silu_out_frac: int, out_frac_bits) -> np.ndarray:
+    """mlp_int (mlp.rs:28-74) composed of the blocked-dot linears and the SiLU
+    product: the same outputs as mlp_int, for full-size checks."""
+    H, I = hidden_size, intermediate_size
+    x = _c(x, np.int16).reshape(-1, H)
+    gate = linear_w8a16_fast(x, np.asarray(W_gate).reshape(-1), H, gate_w_shifts, in_frac_bits,
+                             gate_out_frac)
+    up = linear_w8a16_fast(x, np.asarray(W_up).reshape(-1), H, up_w_shifts, in_frac_bits, up_out_frac)
+    lut = _c(silu_lut, np.int16)
+    h = np.zeros_like(gate)
+    _check("silu_product", lib().mylo_silu_product(
+        _ptr(gate), _ptr(up), gate.size, _ptr(lut), len(lut), gate_out_frac, up_out_frac,
+        down_in_frac, silu_in_frac, silu_lut_offset, silu_out_frac, _ptr(h), None))
+    return linear_w8a16_fast(h, np.asarray(W_down).reshape(-1), I, down_w_shifts, down_in_frac,
+                             out_frac_bits)
+
+
+def linear_acc_fast(x, W, in_features: int, out_features: int) -> np.ndarray:
+    """Exact int64 accumulators [M][N] (blocked dot)."""
+    x = _c(x, np.int16).reshape(-1, in_features)
+    W = _c(W, np.int8)
+    acc = np.zeros((x.shape[0], out_features), np.int64)
+    _check("linear_acc_fast", lib().mylo_linear_acc_fast(
+        _ptr(x), x.shape[0], _ptr(W), in_features, out_features, _ptr(acc)))
+    return acc
+
+
+def requant_acc(acc, w_shifts, act_frac: int, out_frac) -> np.ndarray:
+    """clamp_i16(rescale_i64(acc, w_shift + act_frac, out_frac)) per channel."""
+    acc = _c(acc, np.int64)
+    ws = _c(w_shifts, np.uint8)
+    N = len(ws)
+    of = _c(np.broadcast_to(np.asarray(out_frac, np.uint8), (N,)), np.uint8)
+    y = np.zeros(acc.shape, np.int16)
+    _check("requant_acc", lib().mylo_requant_acc(_ptr(acc), acc.shape[0], N, _ptr(ws), act_frac,
+                                                 _ptr(of), _ptr(y)))
+    return y
+
 
 def inv_n_q20(n: int) -> int:
     return lib().mylo_inv_n_q20(n)

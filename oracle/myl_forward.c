@@ -220,6 +220,47 @@ static void linear_fast(const int16_t* x, int64_t M, const int8_t* W, int64_t K,
   }
 }
 
+int mylo_linear_w8a16_pc_fast(const int16_t* x, int64_t M, const int8_t* W, int64_t K, int64_t N,
+                              const uint8_t* w_shifts, uint8_t act_frac, const uint8_t* out_frac,
+                              int16_t* y) {
+  if (M < 0 || N < 0 || K <= 0) return MYLO_ERR_SHAPE;
+  for (int64_t r = 0; r < N; ++r) {
+    unsigned in_frac = (unsigned)w_shifts[r] + act_frac;
+    if (in_frac > 255u) return MYLO_ERR_OVERFLOW;
+    int d = (int)(int8_t)(uint8_t)in_frac - (int)(int8_t)out_frac[r];
+    if (d < -128 || d > 127 || d > 62 || d < -63) return MYLO_ERR_OVERFLOW;
+  }
+  linear_fast(x, M, W, K, N, w_shifts, act_frac, out_frac, 0, y);
+  return MYLO_OK;
+}
+
+int mylo_linear_acc_fast(const int16_t* x, int64_t M, const int8_t* W, int64_t K, int64_t N,
+                         int64_t* acc) {
+  if (M < 0 || N < 0 || K <= 0) return MYLO_ERR_SHAPE;
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < N; ++r)
+    for (int64_t m = 0; m < M; ++m) acc[m * N + r] = dot_blocked(W + r * K, x + m * K, K);
+  return MYLO_OK;
+}
+
+int mylo_requant_acc(const int64_t* acc, int64_t M, int64_t N, const uint8_t* w_shifts,
+                     uint8_t act_frac, const uint8_t* out_frac, int16_t* y) {
+  if (M < 0 || N < 0) return MYLO_ERR_SHAPE;
+  for (int64_t r = 0; r < N; ++r) {
+    unsigned in_frac = (unsigned)w_shifts[r] + act_frac;
+    if (in_frac > 255u) return MYLO_ERR_OVERFLOW;
+    int d = (int)(int8_t)(uint8_t)in_frac - (int)(int8_t)out_frac[r];
+    if (d < -128 || d > 127 || d > 62 || d < -63) return MYLO_ERR_OVERFLOW;
+  }
+#pragma omp parallel for schedule(static)
+  for (int64_t e = 0; e < M * N; ++e) {
+    int64_t r = e % N, v = 0;
+    mylo_rescale_i64(acc[e], (uint8_t)(w_shifts[r] + act_frac), out_frac[r], &v);
+    y[e] = mylo_clamp_i16_from_i64(v);
+  }
+  return MYLO_OK;
+}
+
 /* The debug-build overflow checks of linear.rs:66 / :115 (u8 add) and of
  * rescale_i64 (i8 difference, shift width) for every row. */
 static int check_shifts(int64_t N, const uint8_t* w_shifts, uint8_t act_frac, const uint8_t* out_pc,

@@ -66,6 +66,21 @@ int mylo_attention_int(const int16_t* q, int64_t q_len, const int16_t* k, const 
                        uint8_t score_shift, const int16_t* exp_lut, int64_t exp_len,
                        uint8_t lut_shift, uint8_t prob_frac_bits, int16_t* out);
 
+/* linear_w8a16_pc (linear.rs:87-119) on M rows with the blocked exact dot:
+ * the same outputs as mylo_linear_w8a16_pc, faster (for full-size checks). */
+int mylo_linear_w8a16_pc_fast(const int16_t* x, int64_t M, const int8_t* W, int64_t K, int64_t N,
+                              const uint8_t* w_shifts, uint8_t act_frac, const uint8_t* out_frac,
+                              int16_t* y);
+
+/* acc[M][N] = dot(W[n], x[m]) in i64 (blocked exact dot), and the requant of
+ * such sums, clamp_i16(rescale_i64(acc, w_shift + act_frac, out_frac[n]))
+ * (linear.rs:61-68): the row-parallel check sums the partials of the ranks'
+ * K slices and requantises once. */
+int mylo_linear_acc_fast(const int16_t* x, int64_t M, const int8_t* W, int64_t K, int64_t N,
+                         int64_t* acc);
+int mylo_requant_acc(const int64_t* acc, int64_t M, int64_t N, const uint8_t* w_shifts,
+                     uint8_t act_frac, const uint8_t* out_frac, int16_t* y);
+
 /* One transformer layer's tensors and calibrated scales (model.rs:62-117). */
 typedef struct mylo_layer {
   const int8_t* ln1_gamma;          /* input_layernorm [hidden] */

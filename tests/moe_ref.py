@@ -7,7 +7,8 @@ oracle result is that composition on the CPU oracle:
   topk, p = moe_route(logits, k, exp_lut, lut_shift, prob_frac)
            (k x argmax with the lowest index on ties, sampling.rs:8-18; softmax_int,
            softmax.rs:24-64)
-  y[t][j] = mlp_int(x[t], expert topk[t][j])               (mlp.rs:28-74)
+  y[t][j] = mlp_int(x[t], expert topk[t][j])               (mlp.rs:28-74; the oracle's
+           blocked-dot composition mlp_int_fast, equal to mlp_int, test_oracle_kat.py)
   out     = moe_combine(y, p, mlp_int(x, shared expert) or 0, prob_frac)
 """
 from __future__ import annotations
@@ -74,14 +75,14 @@ def problem(H, I, E, k, shared_I=0, seed=1, tie_pairs=(), prob_frac=14):
 
 def expert_mlp(p, e, x):
     H, I = p["hidden"], p["intermediate"]
-    return O.mlp_int(x, p["W_gate"][e], p["W_up"][e], p["W_down"][e], H, I, p["gate_w_shifts"][e],
+    return O.mlp_int_fast(x, p["W_gate"][e], p["W_up"][e], p["W_down"][e], H, I, p["gate_w_shifts"][e],
                      p["up_w_shifts"][e], p["down_w_shifts"][e], p["silu_lut"], p["in_frac"],
                      p["gate_out_frac"], p["up_out_frac"], p["down_in_frac"], p["silu_in_frac"],
                      p["silu_lut_offset"], p["silu_out_frac"], p["out_frac"][e])
 
 
 def shared_mlp(s, x):
-    return O.mlp_int(x, s["W_gate"], s["W_up"], s["W_down"], s["hidden_size"], s["intermediate_size"],
+    return O.mlp_int_fast(x, s["W_gate"], s["W_up"], s["W_down"], s["hidden_size"], s["intermediate_size"],
                      s["gate_w_shifts"], s["up_w_shifts"], s["down_w_shifts"], s["silu_lut"],
                      s["in_frac_bits"], s["gate_out_frac"], s["up_out_frac"], s["down_in_frac"],
                      s["silu_in_frac"], s["silu_lut_offset"], s["silu_out_frac"], s["out_frac_bits"])

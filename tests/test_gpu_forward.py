@@ -240,3 +240,23 @@ def test_config2_full_generate_matches_oracle(ctx):
     assert dg[0] == M.digest(wl, wt)
     toks2, _, _ = gm.generate(p, 128)   # graph-replayed decode
     assert np.array_equal(toks2[0], wt)
+
+
+def test_config3_full_generate_matches_oracle(ctx):
+    """BASELINE config 3 at batch 1: Qwen2.5-7B architecture (28 layers, hidden
+    3584, 28/4 heads of 128, MLP 18944, vocab 152064, untied LM head), 2048
+    random prompt tokens and 256 greedy steps; positions 2048..2303 wrap the
+    2048-row RoPE table (model.rs:470-471). Tokens and digest equal the
+    oracle's; at batch 8 the same prompt in sequence 0 gives the same tokens."""
+    spec = S.synthetic_model("qwen2.5-7b", seed=2)
+    gm = M.IntegerModel(ctx, spec)
+    p = S.prompt_tokens(spec.vocab, 2048, seed=100)
+    toks, dg, _ = gm.generate(p, 256, digest=True)
+    om = oracle.OracleModel(spec, 2304)
+    wt, wl = om.generate(p, 256)
+    assert np.array_equal(toks[0], wt)
+    assert dg[0] == M.digest(wl, wt)
+    del om, wl
+    prompts = np.stack([p] + [S.prompt_tokens(spec.vocab, 2048, seed=101 + b) for b in range(7)])
+    tb, _, _ = gm.generate(prompts, 256)
+    assert np.array_equal(tb[0], wt)

@@ -181,8 +181,7 @@ def test_moe_deterministic(ctx):
 
 def test_moe_config4_shape(ctx):
     """hidden 2048, 64 experts x MLP 1408, top-4, shared expert 5632, 4096
-    tokens: the routing of every token against the oracle, the output of a
-    sample of tokens (every token is computed independently of the others)."""
+    tokens: the routing and the output of every token against the oracle."""
     p, s = R.problem(H=2048, I=1408, E=64, k=4, shared_I=5632, seed=4)
     T = 4096
     x = R.activations(np.random.default_rng(40), T, 2048)
@@ -190,9 +189,8 @@ def test_moe_config4_shape(ctx):
     out, idx, prob = _run_dev(m, x)
     ridx, rprob = R.route(p, x)
     assert np.array_equal(idx, ridx) and np.array_equal(prob, rprob)
-    sample = np.random.default_rng(41).choice(T, size=48, replace=False)
-    ref = R.forward(p, s, x[sample])[0]
-    assert np.array_equal(out[sample], ref)
+    ref = R.forward(p, s, x)[0]
+    assert np.array_equal(out, ref)
 
 
 @pytest.mark.parametrize("H,I,T", [(100, 72, 45), (136, 40, 9)])

@@ -368,3 +368,35 @@ def test_thread_count_does_not_change_results():
     finally:
         O.set_num_threads(n0)
     assert np.array_equal(a, b)
+
+
+def test_fast_oracle_paths_equal_the_scalar_restatement():
+    """The blocked-dot helpers used by the full-size checks (linear_w8a16_fast,
+    linear_acc_fast, requant_acc, mlp_int_fast) give the scalar restatement's
+    outputs, extremes included."""
+    import numpy as np
+
+    import oracle as O
+    from make_golden import silu_lut_spec
+
+    rng = np.random.default_rng(12)
+    for M, K, N in ((3, 1000, 40), (2, 18944, 24), (4, 257, 33), (1, 7, 5)):
+        x = rng.integers(-32768, 32768, size=(M, K)).astype(np.int16)
+        x[0] = -32768
+        W = rng.integers(-128, 128, size=N * K, dtype=np.int8)
+        W[:K] = -128
+        s = rng.integers(8, 16, size=N).astype(np.uint8)
+        of = rng.integers(0, 12, size=N).astype(np.uint8)
+        ref = O.linear_w8a16_pc(x, W, K, s, 8, of)
+        assert np.array_equal(O.linear_w8a16_fast(x, W, K, s, 8, of), ref)
+        acc = O.linear_acc_fast(x, W, K, N)
+        assert np.array_equal(acc, O.linear_acc_i64(x, W, K, N))
+        assert np.array_equal(O.requant_acc(acc, s, 8, of), ref)
+    H, I = 64, 96
+    args = (rng.integers(-127, 128, size=(I, H), dtype=np.int8), rng.integers(-127, 128, size=(I, H), dtype=np.int8),
+            rng.integers(-127, 128, size=(H, I), dtype=np.int8), H, I,
+            rng.integers(9, 12, size=I).astype(np.uint8), rng.integers(9, 12, size=I).astype(np.uint8),
+            rng.integers(9, 12, size=H).astype(np.uint8), silu_lut_spec(), 8, 7, 7, 7, 6, 8192, 8,
+            rng.integers(3, 8, size=H).astype(np.uint8))
+    x = rng.integers(-20000, 20000, size=(5, H)).astype(np.int16)
+    assert np.array_equal(O.mlp_int_fast(x, *args), O.mlp_int(x, *args))
