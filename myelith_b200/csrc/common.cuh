@@ -80,6 +80,17 @@ struct Epilogue {
   int xg_world;
 };
 
+// ---- programmatic dependent launch ---------------------------------------------
+// Every kernel of the library starts with pdl_wait(): when it is launched with
+// programmatic stream serialization it may be scheduled before its
+// predecessor grid has finished, and griddepcontrol.wait holds it until that
+// grid has completed and its memory is visible; launched normally, the wait
+// returns at once. pdl_launch() then lets the kernel's own successor launch
+// early (it waits in turn). No global memory is read or written before the
+// wait.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 // ---- requant -----------------------------------------------------------------
 
 // fixed_point.rs:57-71: RNE right shift of a two's-complement value, s in [1, 62].

@@ -51,6 +51,8 @@ __global__ void embed_kernel(const int32_t* __restrict__ tokens, int64_t rows,
                              const uint8_t* __restrict__ embed_shifts,
                              const uint8_t* __restrict__ rin0, int64_t H, int64_t V,
                              int16_t* __restrict__ hidden, int64_t ldh, int* err) {
+  pdl_wait();
+  pdl_launch();
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const int32_t tok = tokens[r];
     int16_t* out = hidden + r * ldh;
@@ -115,6 +117,8 @@ __global__ void __launch_bounds__(NORM_THREADS)
     resid_rmsnorm_kernel(const int16_t* __restrict__ x, int64_t ldx, int64_t rows, ResidParams rp,
                          NormParams np, int16_t* __restrict__ out, int64_t ldo,
                          const int64_t* __restrict__ out_rows, int64_t n_out_rows) {
+  pdl_wait();
+  pdl_launch();
   extern __shared__ int16_t s_row[];  // [H]
   __shared__ __int128 s_part[NORM_THREADS / 32];
   __shared__ int64_t s_lut_val;
@@ -181,6 +185,128 @@ __global__ void __launch_bounds__(NORM_THREADS)
   }
 }
 
+// The same, for hidden sizes that are a multiple of 8 up to 8 * NORM_THREADS *
+// NORM_NV: every thread issues all loads of its 16-byte vectors (the row, the
+// added projection output, and the per-channel parameters) before using any,
+// so one row costs about one memory latency instead of one per element.
+constexpr int NORM_NV = 4;
+
+__device__ __forceinline__ int16_t lane16(const uint4& v, int e) {
+  const uint32_t w = e < 2 ? v.x : e < 4 ? v.y : e < 6 ? v.z : v.w;
+  return int16_t(uint16_t(w >> (16 * (e & 1))));
+}
+__device__ __forceinline__ int8_t lane8(const uint2& v, int e) {
+  return int8_t(uint8_t((e < 4 ? v.x : v.y) >> (8 * (e & 3))));
+}
+__device__ __forceinline__ uint4 pack16(const int16_t (&a)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) w[i] = uint32_t(uint16_t(a[2 * i])) | (uint32_t(uint16_t(a[2 * i + 1])) << 16);
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__global__ void __launch_bounds__(NORM_THREADS)
+    resid_rmsnorm_vec_kernel(const int16_t* __restrict__ x, int64_t ldx, int64_t rows, ResidParams rp,
+                             NormParams np, int16_t* __restrict__ out, int64_t ldo,
+                             const int64_t* __restrict__ out_rows, int64_t n_out_rows) {
+  pdl_wait();
+  pdl_launch();
+  __shared__ __int128 s_part[NORM_THREADS / 32];
+  __shared__ int64_t s_lut_val;
+  __shared__ int s_nf;
+  const int nv = int(np.H / 8);
+  const int64_t nrows = out_rows ? n_out_rows : rows;
+  for (int64_t rr = blockIdx.x; rr < nrows; rr += gridDim.x) {
+    const int64_t r = out_rows ? out_rows[rr] : rr;
+    uint4 xv[NORM_NV], av[NORM_NV], sbv[NORM_NV];
+    uint2 s1v[NORM_NV], s2v[NORM_NV], alv[NORM_NV], gv[NORM_NV];
+#pragma unroll
+    for (int k = 0; k < NORM_NV; ++k) {
+      const int v = threadIdx.x + k * NORM_THREADS;
+      if (v < nv) {
+        xv[k] = *reinterpret_cast<const uint4*>(x + r * ldx + 8 * v);
+        if (rp.add) {
+          av[k] = *reinterpret_cast<const uint4*>(rp.add + r * rp.ld_add + 8 * v);
+          s1v[k] = *reinterpret_cast<const uint2*>(rp.s1 + 8 * v);
+          s2v[k] = *reinterpret_cast<const uint2*>(rp.s2 + 8 * v);
+        }
+        alv[k] = *reinterpret_cast<const uint2*>(np.align2 + 8 * v);
+        gv[k] = *reinterpret_cast<const uint2*>(np.gamma + 8 * v);
+        sbv[k] = *reinterpret_cast<const uint4*>(np.sbase + 8 * v);
+      }
+    }
+    int16_t val[NORM_NV][8];
+    __int128 acc = 0;
+#pragma unroll
+    for (int k = 0; k < NORM_NV; ++k) {
+      const int v = threadIdx.x + k * NORM_THREADS;
+      if (v < nv) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          int64_t t = lane16(xv[k], e);
+          if (rp.add) {
+            const int64_t h = rescale_i64_signed(t, lane8(s1v[k], e)) + int64_t(lane16(av[k], e));
+            t = clamp16(rescale_i64_signed(h, lane8(s2v[k], e)));
+          }
+          val[k][e] = int16_t(t);
+          acc += (__int128)(t * t) << uint8_t(lane8(alv[k], e));
+        }
+        if (rp.add && rp.resid_out)
+          *reinterpret_cast<uint4*>(rp.resid_out + r * rp.ld_res + 8 * v) = pack16(val[k]);
+      }
+    }
+    acc = warp_sum_i128(acc);
+    if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __int128 a = 0;
+      for (int w = 0; w < NORM_THREADS / 32; ++w) a += s_part[w];
+      if (a == 0) {
+        s_nf = -1000;  // all zero: the row is zeros (rmsnorm.rs:99-101)
+        s_lut_val = 0;
+      } else {
+        const __int128 m = (a * (__int128)np.inv_n) >> 20;
+        const __int128 max_idx = np.lut_len - 1;
+        int q = 0;
+        while ((m >> q) > max_idx) q += 2;
+        __int128 idx = rne_i128(m, q);
+        if (idx > max_idx) idx = max_idx;
+        s_lut_val = np.lut[int64_t(idx)];
+        s_nf = np.frac0 + q / 2;
+      }
+    }
+    __syncthreads();
+    const int nf = s_nf;
+    const int64_t lv = s_lut_val;
+#pragma unroll
+    for (int k = 0; k < NORM_NV; ++k) {
+      const int v = threadIdx.x + k * NORM_THREADS;
+      if (v < nv) {
+        int16_t y[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          y[e] = 0;
+          if (nf != -1000) {
+            const int64_t prod = int64_t(val[k][e]) * lv * int64_t(lane8(gv[k], e));
+            const int sh = nf + lane16(sbv[k], e);
+            int64_t t;
+            if (sh >= 63) t = 0;
+            else if (sh > 0) t = rshift_rne_i64(prod, sh);
+            else if (sh == 0) t = prod;
+            else {
+              const __int128 w = (__int128)((unsigned __int128)(__int128)prod << (-sh));
+              t = w < (__int128)INT32_MIN ? INT32_MIN : (w > (__int128)INT32_MAX ? INT32_MAX : (int64_t)w);
+            }
+            y[e] = clamp16(t);
+          }
+        }
+        *reinterpret_cast<uint4*>(out + rr * ldo + 8 * v) = pack16(y);
+      }
+    }
+    __syncthreads();
+  }
+}
+
 // ---- RoPE + KV-cache write (model.rs:469-503, rope.rs:17-32) ----------------------
 // Row r = b * T + t is token t of sequence b at position pos = pos0 + t; it
 // uses LUT row pos % n_pos. Pair j of a head is (x_j, x_{j+half}):
@@ -204,20 +330,27 @@ __global__ void rope_kv_kernel(int16_t* __restrict__ qkv, int64_t ldq, int64_t r
                                const int64_t* __restrict__ pos0_dev, int nq, int nkv, int hd,
                                const int16_t* __restrict__ cos_l, const int16_t* __restrict__ sin_l,
                                int64_t n_pos, int frac, KvCache kc, int layer) {
+  pdl_wait();
+  pdl_launch();
+  // grid.x: row; grid.y * blockDim.x covers one item per thread: the rotation
+  // pairs of the q and k heads, then the values (8 per item when hd % 8 == 0)
   const int half = hd / 2;
   const int n_rot = (nq + nkv) * half;
+  const bool vec = (hd & 7) == 0;
+  const int n_v = vec ? nkv * hd / 8 : nkv * hd;
+  const int e = int(blockIdx.y) * blockDim.x + threadIdx.x;
+  if (e >= n_rot + n_v) return;
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const int64_t b = r / T, t = r % T;
     const int64_t pos = pos0_dev[0] + t;
-    const int64_t idx = pos % n_pos;
-    const int16_t* c = cos_l + idx * half;
-    const int16_t* s = sin_l + idx * half;
     int16_t* row = qkv + r * ldq;
     const int64_t cache_off = b * kc.seq_stride + int64_t(layer) * kc.layer_stride + pos * hd;
-    for (int e = threadIdx.x; e < n_rot; e += blockDim.x) {
+    if (e < n_rot) {
       const int h = e / half, j = e % half;
+      const int64_t idx = pos % n_pos;
       int16_t* v = row + int64_t(h) * hd;  // q heads, then k heads (contiguous in qkv)
-      const uint32_t cj = uint32_t(int32_t(c[j])), sj = uint32_t(int32_t(s[j]));
+      const uint32_t cj = uint32_t(int32_t(cos_l[idx * half + j]));
+      const uint32_t sj = uint32_t(int32_t(sin_l[idx * half + j]));
       const uint32_t x0 = uint32_t(int32_t(v[j])), x1 = uint32_t(int32_t(v[j + half]));
       const int16_t o0 = rope_out(int32_t(x0 * cj - x1 * sj), frac);
       const int16_t o1 = rope_out(int32_t(x1 * cj + x0 * sj), frac);
@@ -229,11 +362,17 @@ __global__ void rope_kv_kernel(int16_t* __restrict__ qkv, int64_t ldq, int64_t r
         kd[j] = o0;
         kd[j + half] = o1;
       }
-    }
-    const int16_t* vrow = row + int64_t(nq + nkv) * hd;
-    for (int e = threadIdx.x; e < nkv * hd; e += blockDim.x) {
-      const int h = e / hd, d = e % hd;
-      kc.v[cache_off + int64_t(h) * kc.head_stride + d] = vrow[e];
+    } else {
+      const int i = e - n_rot;
+      const int16_t* vrow = row + int64_t(nq + nkv) * hd;
+      if (vec) {
+        const int h = (8 * i) / hd, d = (8 * i) % hd;
+        *reinterpret_cast<uint4*>(kc.v + cache_off + int64_t(h) * kc.head_stride + d) =
+            *reinterpret_cast<const uint4*>(vrow + 8 * i);
+      } else {
+        const int h = i / hd, d = i % hd;
+        kc.v[cache_off + int64_t(h) * kc.head_stride + d] = vrow[i];
+      }
     }
   }
 }
@@ -307,13 +446,22 @@ __device__ __forceinline__ int dp2a_hi_su(uint32_t a, uint32_t b, int c) {
 
 // grid.x: (row group) = ((b * T + t) * nkv + g) * gsub + sub; grid.y: key chunk of ATT_KEYS;
 // sub-groups of ATT_MAXG query heads of the KV head g. Dynamic shared memory:
-// key planes [ATT_KEYS][hd4 + 4] bytes x 2 and queries [ATT_MAXG][hd4] int16.
+// key planes [ATT_KEYS][hd8 + 8] bytes x 2 (hd8 = head_dim rounded up to 8;
+// the 8-byte pad makes the per-key 8-byte reads of a half-warp hit distinct
+// banks) and queries [ATT_MAXG][hd8] int16.
+__host__ __device__ constexpr int att_hd8(int hd) { return (hd + 7) & ~7; }
+__host__ __device__ constexpr size_t att_scores_smem(int hd) {
+  return size_t(2 * ATT_KEYS * (att_hd8(hd) + 8)) + size_t(ATT_MAXG * att_hd8(hd) * 2);
+}
+
 __global__ void __launch_bounds__(ATT_THREADS) attn_scores_kernel(AttnParams p, int gsub) {
+  pdl_wait();
+  pdl_launch();
   extern __shared__ __align__(16) uint8_t smem[];
-  const int hd = p.hd, hd4 = (hd + 3) & ~3, kst = hd4 + 4;
+  const int hd = p.hd, hd8 = att_hd8(hd), kst = hd8 + 8, qw = hd8 / 2;
   uint8_t* s_kh = smem;
   uint8_t* s_kl = s_kh + ATT_KEYS * kst;
-  uint32_t* s_q = reinterpret_cast<uint32_t*>(s_kl + ATT_KEYS * kst);  // [ATT_MAXG][hd4/2]
+  uint32_t* s_q = reinterpret_cast<uint32_t*>(s_kl + ATT_KEYS * kst);  // [ATT_MAXG][hd8/2]
   const int group = p.nq / p.nkv;
   const int64_t gy = blockIdx.x;
   const int sub = int(gy % gsub);
@@ -326,9 +474,9 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_scores_kernel(AttnParams p, 
   if (j0 >= len) return;
   const int h0 = g * group + sub * ATT_MAXG;
   const int nrow = min(ATT_MAXG, g * group + group - h0);
-  // queries of the sub-group, zero-padded to hd4
-  for (int e = threadIdx.x; e < ATT_MAXG * (hd4 / 2); e += ATT_THREADS) {
-    const int rr = e / (hd4 / 2), w = e % (hd4 / 2);
+  // queries of the sub-group as int16 pairs, zero-padded to hd8
+  for (int e = threadIdx.x; e < ATT_MAXG * qw; e += ATT_THREADS) {
+    const int rr = e / qw, w = e % qw;
     uint32_t v = 0;
     if (rr < nrow) {
       const int16_t* q = p.qkv + r * p.ldq + int64_t(h0 + rr) * hd;
@@ -338,22 +486,29 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_scores_kernel(AttnParams p, 
     }
     s_q[e] = v;
   }
-  // key rows j0.. as two byte planes (high byte signed, low byte unsigned)
+  // key rows j0.. as two byte planes (high byte signed, low byte unsigned),
+  // 8 elements per step: one 16-byte load, two byte permutes, two 8-byte stores
   const int16_t* kbase = p.kc.k + b * p.kc.seq_stride + int64_t(p.layer) * p.kc.layer_stride +
                          int64_t(g) * p.kc.head_stride;
   const int nkeys = int(min(int64_t(ATT_KEYS), len - j0));
-  for (int e = threadIdx.x; e < ATT_KEYS * (hd4 / 2); e += ATT_THREADS) {
-    const int jj = e / (hd4 / 2), w = e % (hd4 / 2), d = 2 * w;
-    int16_t k0 = 0, k1 = 0;
+  const bool vec = (hd & 7) == 0;
+  for (int e = threadIdx.x; e < ATT_KEYS * (hd8 / 8); e += ATT_THREADS) {
+    const int jj = e / (hd8 / 8), d = 8 * (e % (hd8 / 8));
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
     if (jj < nkeys) {
-      const int16_t* kr = kbase + (j0 + jj) * hd;
-      if (d < hd) k0 = kr[d];
-      if (d + 1 < hd) k1 = kr[d + 1];
+      const int16_t* kr = kbase + (j0 + jj) * hd + d;
+      if (vec) {
+        v = *reinterpret_cast<const uint4*>(kr);
+      } else {
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+        for (int i = 0; i < 8 && d + i < hd; ++i) w[i / 2] |= uint32_t(uint16_t(kr[i])) << (16 * (i & 1));
+        v = make_uint4(w[0], w[1], w[2], w[3]);
+      }
     }
-    s_kh[jj * kst + d] = uint8_t(uint16_t(k0) >> 8);
-    s_kh[jj * kst + d + 1] = uint8_t(uint16_t(k1) >> 8);
-    s_kl[jj * kst + d] = uint8_t(k0);
-    s_kl[jj * kst + d + 1] = uint8_t(k1);
+    *reinterpret_cast<uint2*>(s_kh + jj * kst + d) =
+        make_uint2(__byte_perm(v.x, v.y, 0x7531), __byte_perm(v.z, v.w, 0x7531));
+    *reinterpret_cast<uint2*>(s_kl + jj * kst + d) =
+        make_uint2(__byte_perm(v.x, v.y, 0x6420), __byte_perm(v.z, v.w, 0x6420));
   }
   __syncthreads();
   const int jj = threadIdx.x;
@@ -361,16 +516,18 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_scores_kernel(AttnParams p, 
   int acc_h[ATT_MAXG], acc_l[ATT_MAXG];
 #pragma unroll
   for (int i = 0; i < ATT_MAXG; ++i) acc_h[i] = acc_l[i] = 0;
-  const uint32_t* kh4 = reinterpret_cast<const uint32_t*>(s_kh + jj * kst);
-  const uint32_t* kl4 = reinterpret_cast<const uint32_t*>(s_kl + jj * kst);
-  for (int w4 = 0; w4 < hd4 / 4; ++w4) {
-    const uint32_t kh = kh4[w4], kl = kl4[w4];
+  const uint2* kh8 = reinterpret_cast<const uint2*>(s_kh + jj * kst);
+  const uint2* kl8 = reinterpret_cast<const uint2*>(s_kl + jj * kst);
+  for (int w8 = 0; w8 < hd8 / 8; ++w8) {
+    const uint2 kh = kh8[w8], kl = kl8[w8];
 #pragma unroll
     for (int i = 0; i < ATT_MAXG; ++i) {
       if (i < nrow) {
-        const uint32_t q01 = s_q[i * (hd4 / 2) + 2 * w4], q23 = s_q[i * (hd4 / 2) + 2 * w4 + 1];
-        acc_h[i] = dp2a_hi_ss(q23, kh, dp2a_lo_ss(q01, kh, acc_h[i]));
-        acc_l[i] = dp2a_hi_su(q23, kl, dp2a_lo_su(q01, kl, acc_l[i]));
+        const uint4 q = *reinterpret_cast<const uint4*>(s_q + i * qw + 4 * w8);
+        acc_h[i] = dp2a_hi_ss(q.y, kh.x, dp2a_lo_ss(q.x, kh.x, acc_h[i]));
+        acc_h[i] = dp2a_hi_ss(q.w, kh.y, dp2a_lo_ss(q.z, kh.y, acc_h[i]));
+        acc_l[i] = dp2a_hi_su(q.y, kl.x, dp2a_lo_su(q.x, kl.x, acc_l[i]));
+        acc_l[i] = dp2a_hi_su(q.w, kl.y, dp2a_lo_su(q.z, kl.y, acc_l[i]));
       }
     }
   }
@@ -404,6 +561,8 @@ __device__ __forceinline__ int32_t exp_lookup(int32_t x, const int16_t* lut, int
 // grid.x: query row (b * T + t) * nq + h; grid.y: key chunk of `chunk` keys
 // (a multiple of ATT_CHUNK; one chunk per row when rows are plentiful).
 __global__ void __launch_bounds__(ATT_THREADS) attn_pv_kernel(AttnParams p, int64_t chunk) {
+  pdl_wait();
+  pdl_launch();
   extern __shared__ __align__(16) int64_t s_acc[];  // [ATT_THREADS / 32][hd]
   __shared__ int64_t s_red[ATT_THREADS / 32];
   __shared__ int32_t s_p[ATT_CHUNK];
@@ -530,6 +689,161 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_pv_kernel(AttnParams p, int6
   if (nch > 1 && threadIdx.x == 0) p.counters[row] = 0;
 }
 
+// The softmax of one attention row (softmax.rs:24-64): its maximum and the
+// sum of the exponentials, loads unrolled four deep.
+__device__ __forceinline__ void attn_row_stats(const int32_t* __restrict__ sc, int64_t len,
+                                               const AttnParams& p, int32_t lut_one, int64_t* s_red,
+                                               int32_t* m_out, int32_t* S_out) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int32_t m = INT32_MIN;
+  for (int64_t j = threadIdx.x; j < len; j += 4 * ATT_THREADS) {
+    int32_t v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t jj = j + u * ATT_THREADS;
+      v[u] = jj < len ? sc[jj] : INT32_MIN;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) m = max(m, v[u]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) s_red[warp] = m;
+  __syncthreads();
+  m = int32_t(s_red[0]);
+  for (int w = 1; w < ATT_THREADS / 32; ++w) m = max(m, int32_t(s_red[w]));
+  __syncthreads();
+  int64_t s = 0;
+  for (int64_t j = threadIdx.x; j < len; j += 4 * ATT_THREADS) {
+    int32_t v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t jj = j + u * ATT_THREADS;
+      v[u] = jj < len ? sc[jj] : m;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (j + u * ATT_THREADS < len) {
+        const int64_t d = int64_t(m) - int64_t(v[u]);
+        s += exp_lookup(d > INT32_MAX ? INT32_MAX : int32_t(d), p.exp_lut, p.exp_len, p.lut_shift, lut_one);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) s_red[warp] = s;
+  __syncthreads();
+  s = 0;
+  for (int w = 0; w < ATT_THREADS / 32; ++w) s += s_red[w];
+  *m_out = m;
+  *S_out = int32_t(s);
+}
+
+// Pass 2 for head_dim a multiple of 8 (<= 256): hd / 8 threads per value row,
+// each a 16-byte vector, ATT_THREADS * 8 / hd rows in flight per step and four
+// steps unrolled; the rows' int64 partial sums meet in shared memory.
+__global__ void __launch_bounds__(ATT_THREADS) attn_pv_vec_kernel(AttnParams p, int64_t chunk) {
+  pdl_wait();
+  pdl_launch();
+  extern __shared__ __align__(16) int64_t s_acc[];  // [keys per step][hd] = ATT_THREADS * 8
+  __shared__ int64_t s_red[ATT_THREADS / 32];
+  __shared__ int32_t s_p[ATT_CHUNK];
+  __shared__ bool s_last;
+  const int64_t row = blockIdx.x;
+  const int64_t r = row / p.nq;
+  const int h = int(row % p.nq);
+  const int64_t b = r / p.T, t = r % p.T;
+  const int64_t pos = p.pos0[0] + t;
+  const int64_t len = p.mask ? p.lds : pos + 1;
+  const int64_t nch = (len + chunk - 1) / chunk;
+  const int64_t c = blockIdx.y;
+  if (c >= nch) return;
+  const int32_t* sc = p.scores + row * p.lds;
+  const int32_t lut_one = p.exp_lut[0];
+  int32_t m, S;
+  attn_row_stats(sc, len, p, lut_one, s_red, &m, &S);
+  const int32_t one = int32_t(1) << p.prob_frac;
+  const int hd = p.hd, tpk = hd / 8, kpi = ATT_THREADS / tpk;
+  const int kg = threadIdx.x / tpk, dv = threadIdx.x % tpk;
+  const int16_t* vbase = p.kc.v + b * p.kc.seq_stride + int64_t(p.layer) * p.kc.layer_stride +
+                         int64_t(h / (p.nq / p.nkv)) * p.kc.head_stride + 8 * dv;
+  int64_t acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0;
+  const int64_t jend = min(len, (c + 1) * chunk);
+  for (int64_t jc0 = c * chunk; jc0 < jend; jc0 += ATT_CHUNK) {
+    const int nj = int(min(int64_t(ATT_CHUNK), jend - jc0));
+    __syncthreads();  // s_p of the previous piece is consumed
+    if (threadIdx.x < nj) {
+      const int64_t j = jc0 + threadIdx.x;
+      int32_t pj;
+      if (S == 0) {
+        const int32_t base = one / int32_t(len), rem = one - base * int32_t(len);
+        pj = base + (j < rem ? 1 : 0);
+      } else {
+        const int64_t d = int64_t(m) - int64_t(sc[j]);
+        const int32_t e = exp_lookup(d > INT32_MAX ? INT32_MAX : int32_t(d), p.exp_lut, p.exp_len,
+                                     p.lut_shift, lut_one);
+        const int32_t num = e * one;
+        int32_t q = num / S;
+        const int32_t rm = num % S;
+        const int32_t twice = (rm < 0 ? -rm : rm) * 2, den = S < 0 ? -S : S;
+        if (twice > den || (twice == den && (q & 1))) q = ((num > 0) == (S > 0)) ? q + 1 : q - 1;
+        pj = q;
+      }
+      s_p[threadIdx.x] = pj;
+    }
+    __syncthreads();
+    for (int jj = kg; jj < nj; jj += 4 * kpi) {
+      int32_t pp[4];
+      uint4 vv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j2 = jj + u * kpi;
+        pp[u] = j2 < nj ? s_p[j2] : 0;
+        vv[u] = pp[u] != 0 ? *reinterpret_cast<const uint4*>(vbase + (jc0 + j2) * hd)
+                           : make_uint4(0u, 0u, 0u, 0u);  // attention.rs:79 skips p = 0
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] += int64_t(pp[u]) * int64_t(lane16(vv[u], e));
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int e = 0; e < 8; ++e) s_acc[kg * hd + 8 * dv + e] = acc[e];
+  __syncthreads();
+  int64_t* part = p.part + (row * p.max_chunks) * hd;
+  int64_t tot = 0;
+  const int d = threadIdx.x;
+  if (d < hd) {
+    for (int g = 0; g < kpi; ++g) tot += s_acc[g * hd + d];
+    if (nch > 1) part[c * hd + d] = tot;
+  }
+  if (nch > 1) {
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const unsigned prev = atomicAdd(p.counters + row, 1u);
+      s_last = (prev + 1 == unsigned(nch));
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (d < hd) {
+      tot = 0;
+      for (int64_t cc = 0; cc < nch; ++cc) tot += __ldcg(part + cc * hd + d);
+    }
+  }
+  if (d < hd) {
+    int32_t o = clamp16(p.prob_frac > 0 ? rshift_rne_i64(tot, p.prob_frac) : tot);
+    if (p.out_shift != 0) o = clamp16(rescale_i32_s(o, p.out_shift));
+    p.out[r * p.ldo + int64_t(h) * hd + d] = int16_t(o);
+  }
+  if (nch > 1 && threadIdx.x == 0) p.counters[row] = 0;
+}
+
 // ---- greedy selection into the token stream -----------------------------------------
 // keys[b] (select_key) -> token = 2^32 - 1 - (key & 0xFFFFFFFF); written to the
 // next-step token buffer and to out_tokens[b * ld_out + step], step from the
@@ -539,6 +853,8 @@ __global__ void greedy_commit_kernel(const int64_t* __restrict__ keys, int64_t B
                                      int32_t* __restrict__ out_tokens, int64_t ld_out,
                                      int64_t* __restrict__ step, int64_t* __restrict__ pos,
                                      int64_t pos_advance) {
+  pdl_wait();
+  pdl_launch();
   const int64_t s = step[0];
   for (int64_t b = threadIdx.x; b < B; b += blockDim.x) {
     const int32_t tok = int32_t(int64_t(0xFFFFFFFFll) - (keys[b] & 0xFFFFFFFFll));

@@ -275,6 +275,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                          const __grid_constant__ CUtensorMap tm_xlo, int64_t M, int64_t N,
                          TcWork work, Epilogue ep, int64_t slice_stride, int* err,
                          uint64_t timeout_ns, int inject_fault) {
+  pdl_wait();
+  pdl_launch();
   using Cfg = TcCfg<BN, STAGES, PAIR>;
   extern __shared__ uint8_t dyn_smem[];
   __shared__ TcCtl ctl;
@@ -683,6 +685,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 __global__ void tail_reduce_kernel(const int64_t* __restrict__ ws, int tail_tiles, int tail_ks,
                                    int first_tile, int tiles_n, int BN, int ct, int64_t M,
                                    int64_t N, Epilogue ep) {
+  pdl_wait();
+  pdl_launch();
   const int hp = ct / 2;  // channel pairs per tile
   const int halves = ct / 128;
   const int64_t total = int64_t(tail_tiles) * BN * hp;
@@ -770,6 +774,8 @@ __device__ __forceinline__ void split8(const int16_t (&v)[8], uint2& hi, uint2& 
 
 __global__ void split_hilo_kernel(const int16_t* __restrict__ X, int64_t ldx, int64_t M, int64_t K,
                                   uint8_t* __restrict__ Xhi, uint8_t* __restrict__ Xlo, int64_t ldp) {
+  pdl_wait();
+  pdl_launch();
   const int64_t groups = ldp >> 3;  // 8 elements per thread step
   const int64_t total = M * groups;
   const bool vec = ((reinterpret_cast<uintptr_t>(X) & 15) == 0) && (ldx % 8 == 0);

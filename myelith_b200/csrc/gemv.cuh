@@ -58,6 +58,8 @@ __global__ void __launch_bounds__(GEMV_THREADS)
     gemv_w8a16_kernel(const int8_t* __restrict__ W, int64_t ldw, int64_t N,
                       const int16_t* __restrict__ X, int64_t ldx, int64_t K, int64_t k_slice,
                       Epilogue ep, int64_t slice_stride) {
+  pdl_wait();
+  pdl_launch();
   static_assert(GEMV_WARPS % KW == 0, "warps per row group");
   extern __shared__ __align__(16) int16_t xs[];  // [MT][KS]
   __shared__ int64_t red[GEMV_WARPS][R][MT];
@@ -311,6 +313,8 @@ template <int MT, int U>
 __global__ void __launch_bounds__(GEMV_THREADS, 2)
     gemv_balanced_kernel(const int8_t* __restrict__ W, int64_t ldw, int64_t N,
                          const int16_t* __restrict__ X, int64_t ldx, int64_t K, Epilogue ep) {
+  pdl_wait();
+  pdl_launch();
   extern __shared__ __align__(16) int16_t xs[];  // [MT][KS], two 16-byte planes per chunk
   const int KS = int((K + 15) & ~int64_t(15));
   const int C = KS >> 4;
@@ -351,6 +355,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2)
 // xsum[m] = sum_k x[m][k] (int64), one warp per row: the EPI_W16 correction.
 __global__ void x_row_sums_kernel(const int16_t* __restrict__ X, int64_t ldx, int64_t M, int64_t K,
                                   int64_t* __restrict__ xsum) {
+  pdl_wait();
+  pdl_launch();
   const int lane = threadIdx.x & 31;
   const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
   for (int64_t m = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); m < M; m += warps) {
@@ -367,6 +373,8 @@ __global__ void x_row_sums_kernel(const int16_t* __restrict__ X, int64_t ldx, in
 // and applies the epilogue. Summation order is irrelevant (exact integers).
 __global__ void reduce_requant_kernel(const int64_t* __restrict__ part, int nsplit,
                                       int64_t slice_stride, int64_t M, int64_t N, Epilogue ep) {
+  pdl_wait();
+  pdl_launch();
   if (ep.mode == EPI_W16) {  // one thread per (token, int16 weight row)
     const int64_t I = N / 2, total = M * I;
     for (int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < total;

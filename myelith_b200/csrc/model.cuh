@@ -338,6 +338,8 @@ int set_pos(myl_session* s, int64_t pos, cudaStream_t st) {
 }
 
 __global__ void advance_kernel(int64_t* pos, int64_t n) {
+  pdl_wait();
+  pdl_launch();
   if (threadIdx.x == 0 && blockIdx.x == 0) pos[0] += n;
 }
 
@@ -372,18 +374,22 @@ int run_attention(myl_ctx* ctx, const myl_model* m, myl_session* s, const ModelL
   p.ldo = m->QD;
   const int group = int(m->nq / m->nkv);
   const int gsub = (group + ATT_MAXG - 1) / ATT_MAXG;
-  const int hd4 = (int(m->hd) + 3) & ~3;
-  const size_t smem1 = size_t(2 * ATT_KEYS * (hd4 + 4)) + size_t(ATT_MAXG * hd4 * 2);
+  const size_t smem1 = att_scores_smem(int(m->hd));
   const int64_t kchunks = (lds_len + ATT_KEYS - 1) / ATT_KEYS;
   const dim3 g1 = dim3(unsigned(rows * m->nkv * gsub), unsigned(kchunks));
-  attn_scores_kernel<<<g1, ATT_THREADS, smem1, st>>>(p, gsub);
-  CUDA_TRY(cudaGetLastError());
+  LaunchCfg l1(ctx, g1, dim3(ATT_THREADS), smem1, st);
+  CUDA_TRY(cudaLaunchKernelEx(&l1.cfg, attn_scores_kernel, p, gsub));
   // pass 2: split the keys of few rows over several blocks, one block per row otherwise
   const bool split = rows <= s->part_rows && rows * m->nq < 4 * int64_t(ctx->num_sms);
   const int64_t chunk = split ? ATT_CHUNK : ((lds_len + ATT_CHUNK - 1) / ATT_CHUNK) * ATT_CHUNK;
   const dim3 g2 = dim3(unsigned(rows * m->nq), unsigned((lds_len + chunk - 1) / chunk));
-  attn_pv_kernel<<<g2, ATT_THREADS, size_t(ATT_THREADS / 32) * size_t(m->hd) * 8, st>>>(p, chunk);
-  CUDA_TRY(cudaGetLastError());
+  if (m->hd % 8 == 0) {
+    LaunchCfg l2(ctx, g2, dim3(ATT_THREADS), size_t(ATT_THREADS) * 8 * 8, st);
+    CUDA_TRY(cudaLaunchKernelEx(&l2.cfg, attn_pv_vec_kernel, p, chunk));
+  } else {
+    LaunchCfg l2(ctx, g2, dim3(ATT_THREADS), size_t(ATT_THREADS / 32) * size_t(m->hd) * 8, st);
+    CUDA_TRY(cudaLaunchKernelEx(&l2.cfg, attn_pv_kernel, p, chunk));
+  }
   ctx->launches += 2;
   return MYL_OK;
 }
@@ -393,9 +399,15 @@ int launch_norm(myl_ctx* ctx, const myl_model* m, const int16_t* x, int64_t rows
   const int64_t n = out_rows ? n_out : rows;
   if (n == 0) return MYL_OK;
   const unsigned blocks = unsigned(std::min<int64_t>(n, 65535));
-  resid_rmsnorm_kernel<<<blocks, NORM_THREADS, size_t(m->H) * 2, st>>>(
-      x, m->H, rows, rp, norm_params(m, nd), out, m->H, out_rows, n_out);
-  CUDA_TRY(cudaGetLastError());
+  if (m->H % 8 == 0 && m->H <= 8 * NORM_THREADS * NORM_NV) {
+    LaunchCfg lc(ctx, dim3(blocks), dim3(NORM_THREADS), 0, st);
+    CUDA_TRY(cudaLaunchKernelEx(&lc.cfg, resid_rmsnorm_vec_kernel, x, m->H, rows, rp,
+                                norm_params(m, nd), out, m->H, out_rows, n_out));
+  } else {
+    LaunchCfg lc(ctx, dim3(blocks), dim3(NORM_THREADS), size_t(m->H) * 2, st);
+    CUDA_TRY(cudaLaunchKernelEx(&lc.cfg, resid_rmsnorm_kernel, x, m->H, rows, rp, norm_params(m, nd),
+                                out, m->H, out_rows, n_out));
+  }
   ctx->launches++;
   return MYL_OK;
 }
@@ -407,10 +419,13 @@ int launch_norm(myl_ctx* ctx, const myl_model* m, const int16_t* x, int64_t rows
 int model_forward(myl_ctx* ctx, const myl_model* m, myl_session* s, const int32_t* tokens, int64_t T,
                   bool want_logits, int64_t lds_len, cudaStream_t st) {
   const int64_t rows = s->B * T, H = m->H;
-  embed_kernel<<<unsigned(std::min<int64_t>(rows, 65535)), 256, 0, st>>>(
-      tokens, rows, m->embed_rows, m->lde, m->d_embed_shifts, m->d_rin0, H, m->V, s->hid, H,
-      ctx->d_err);
-  CUDA_TRY(cudaGetLastError());
+  {
+    LaunchCfg lc(ctx, dim3(unsigned(std::min<int64_t>(rows, 65535))), dim3(256), 0, st);
+    CUDA_TRY(cudaLaunchKernelEx(&lc.cfg, embed_kernel, tokens, rows, m->embed_rows, m->lde,
+                                static_cast<const uint8_t*>(m->d_embed_shifts),
+                                static_cast<const uint8_t*>(m->d_rin0), H, m->V, s->hid, H,
+                                ctx->d_err));
+  }
   ctx->launches++;
   for (int64_t l = 0; l < m->L; ++l) {
     const ModelLayer& L = m->layers[size_t(l)];
@@ -428,10 +443,16 @@ int model_forward(myl_ctx* ctx, const myl_model* m, myl_session* s, const int32_
       TRY(launch_norm(ctx, m, s->hid, rows, rp, L.norm1, s->xn, nullptr, 0, st));
     }
     TRY(dispatch_linear(ctx, L.w_qkv, s->xn, rows, H, make_ep(L.rq_qkv, s->qkv, m->ldq), st));
-    rope_kv_kernel<<<unsigned(std::min<int64_t>(rows, 65535)), 256, 0, st>>>(
-        s->qkv, m->ldq, rows, T, s->d_pos, int(m->nq), int(m->nkv), int(m->hd), m->d_cos, m->d_sin,
-        m->n_pos, m->rope_frac, s->cache, int(l));
-    CUDA_TRY(cudaGetLastError());
+    {
+      const int64_t items = (m->nq + m->nkv) * (m->hd / 2) + m->nkv * m->hd / ((m->hd % 8) ? 1 : 8);
+      LaunchCfg lc(ctx, dim3(unsigned(std::min<int64_t>(rows, 65535)), unsigned((items + 255) / 256)),
+                   dim3(256), 0, st);
+      CUDA_TRY(cudaLaunchKernelEx(&lc.cfg, rope_kv_kernel, s->qkv, m->ldq, rows, T,
+                                  static_cast<const int64_t*>(s->d_pos), int(m->nq), int(m->nkv),
+                                  int(m->hd), static_cast<const int16_t*>(m->d_cos),
+                                  static_cast<const int16_t*>(m->d_sin), m->n_pos, int(m->rope_frac),
+                                  s->cache, int(l)));
+    }
     ctx->launches++;
     TRY(run_attention(ctx, m, s, L, int(l), rows, T, lds_len, st));
     TRY(dispatch_linear(ctx, L.w_o, s->attn, rows, m->QD, make_ep(L.rq_o, s->o, H), st));
@@ -471,22 +492,39 @@ int model_forward(myl_ctx* ctx, const myl_model* m, myl_session* s, const int32_
 
 // Greedy selection of s->logits into s->next_tok and out_tokens[:, step].
 int launch_select(myl_ctx* ctx, const myl_model* m, myl_session* s, cudaStream_t st) {
-  select_init_kernel<<<1, 64, 0, st>>>(s->keys, s->B);
+  LaunchCfg l0(ctx, dim3(1), dim3(64), 0, st);
+  CUDA_TRY(cudaLaunchKernelEx(&l0.cfg, select_init_kernel, s->keys, s->B));
   const dim3 grid = dim3(unsigned((m->V + SELECT_CHUNK - 1) / SELECT_CHUNK), unsigned(std::min<int64_t>(s->B, 65535)));
-  select_keys_kernel<<<grid, SELECT_THREADS, 0, st>>>(s->logits, s->B, m->V, m->V, 0, s->keys);
-  greedy_commit_kernel<<<1, 256, 0, st>>>(s->keys, s->B, s->next_tok, s->out_tokens, s->max_pos,
-                                          s->d_step, s->d_pos, 0);
-  CUDA_TRY(cudaGetLastError());
+  LaunchCfg l1(ctx, grid, dim3(SELECT_THREADS), 0, st);
+  CUDA_TRY(cudaLaunchKernelEx(&l1.cfg, select_keys_kernel, static_cast<const int32_t*>(s->logits),
+                              s->B, m->V, m->V, int64_t(0), s->keys));
+  LaunchCfg l2(ctx, dim3(1), dim3(256), 0, st);
+  CUDA_TRY(cudaLaunchKernelEx(&l2.cfg, greedy_commit_kernel, static_cast<const int64_t*>(s->keys),
+                              s->B, s->next_tok, s->out_tokens, s->max_pos, s->d_step, s->d_pos,
+                              int64_t(0)));
   ctx->launches += 3;
   return MYL_OK;
 }
 
+// ctx->pdl for the lifetime of a scope (the forward's kernel chains);
+// MYL_PDL=0 turns it off.
+struct PdlScope {
+  myl_ctx* ctx;
+  int saved;
+  explicit PdlScope(myl_ctx* c) : ctx(c), saved(c->pdl) {
+    const char* e = std::getenv("MYL_PDL");
+    ctx->pdl = (e && e[0] == '0') ? 0 : 1;
+  }
+  ~PdlScope() { ctx->pdl = saved; }
+};
+
 // One decode step: select, forward of the chosen tokens, position + 1.
 int decode_step(myl_ctx* ctx, const myl_model* m, myl_session* s, cudaStream_t st) {
+  PdlScope pdl(ctx);
   TRY(launch_select(ctx, m, s, st));
   TRY(model_forward(ctx, m, s, s->next_tok, 1, true, s->max_pos, st));
-  advance_kernel<<<1, 32, 0, st>>>(s->d_pos, 1);
-  CUDA_TRY(cudaGetLastError());
+  LaunchCfg lc(ctx, dim3(1), dim3(32), 0, st);
+  CUDA_TRY(cudaLaunchKernelEx(&lc.cfg, advance_kernel, s->d_pos, int64_t(1)));
   ctx->launches++;
   return MYL_OK;
 }
@@ -503,6 +541,7 @@ int prefill(myl_ctx* ctx, const myl_model* m, myl_session* s, const int32_t* pro
       std::memcpy(s->h_tokens + b * T, prompt + b * P + t0, size_t(T) * 4);
     CUDA_TRY(cudaMemcpyAsync(s->tok_in, s->h_tokens, size_t(s->B * T) * 4, cudaMemcpyHostToDevice, st));
     TRY(set_pos(s, s->pos, st));
+    PdlScope pdl(ctx);
     TRY(model_forward(ctx, m, s, s->tok_in, T, want_logits && t0 + T == P, s->pos + T, st));
     s->pos += T;
   }
@@ -933,8 +972,7 @@ int myl_attention_int(myl_ctx* ctx, const int16_t* q, int64_t q_len, const int16
       rc = dev_upload(A, &dmask, ones.data(), ones.size());
       p.mask = dmask;
     }
-    const int hd4 = (int(head_dim) + 3) & ~3;
-    const size_t smem1 = size_t(2 * ATT_KEYS * (hd4 + 4)) + size_t(ATT_MAXG * hd4 * 2);
+    const size_t smem1 = att_scores_smem(int(head_dim));
     if (rc == MYL_OK && cudaFuncSetAttribute(attn_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              160 * 1024) != cudaSuccess)
       rc = fail(MYL_ERR_CUDA, "smem attribute");
@@ -942,7 +980,10 @@ int myl_attention_int(myl_ctx* ctx, const int16_t* q, int64_t q_len, const int16
       const dim3 g1 = dim3(unsigned(q_len), unsigned((kv_len + ATT_KEYS - 1) / ATT_KEYS));
       attn_scores_kernel<<<g1, ATT_THREADS, smem1, st>>>(p, 1);
       const dim3 g2 = dim3(unsigned(q_len), unsigned(max_chunks));
-      attn_pv_kernel<<<g2, ATT_THREADS, size_t(ATT_THREADS / 32) * size_t(head_dim) * 8, st>>>(p, ATT_CHUNK);
+      if (head_dim % 8 == 0)
+        attn_pv_vec_kernel<<<g2, ATT_THREADS, size_t(ATT_THREADS) * 8 * 8, st>>>(p, ATT_CHUNK);
+      else
+        attn_pv_kernel<<<g2, ATT_THREADS, size_t(ATT_THREADS / 32) * size_t(head_dim) * 8, st>>>(p, ATT_CHUNK);
       if (cudaGetLastError() != cudaSuccess) rc = fail(MYL_ERR_CUDA, "attention launch");
       ctx->launches += 2;
     }

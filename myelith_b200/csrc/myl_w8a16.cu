@@ -129,6 +129,7 @@ struct myl_ctx {
   int xbox = TC_XBOX;  // activation rows per TMA box of the tensor-core GEMM
   int pair_mode = 1;   // CTA-pair GEMM (M = 256 MMAs): 0 off, 1 for 128-token tiles
   int pair_slots = 0;  // co-resident CTA pairs of the pair kernel (0: not yet queried)
+  int pdl = 0;         // launch with programmatic stream serialization (the forward's chains)
   int64_t launches = 0;
   PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   DevBuf x, y, rq, planes, part, h, hplanes, moe, xsum, crc;
@@ -149,6 +150,35 @@ struct myl_ctx {
 static int sms(const myl_ctx* ctx) {
   return ctx->sm_limit > 0 ? std::min(ctx->sm_limit, ctx->num_sms) : ctx->num_sms;
 }
+
+// Launch configuration; with ctx->pdl the kernel may start while its
+// predecessor on the stream finishes (every kernel begins with pdl_wait()).
+struct LaunchCfg {
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[2];
+  LaunchCfg(const myl_ctx* ctx, dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+            unsigned cluster_x = 0) {
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    unsigned n = 0;
+    if (cluster_x) {
+      attr[n].id = cudaLaunchAttributeClusterDimension;
+      attr[n].val.clusterDim.x = cluster_x;
+      attr[n].val.clusterDim.y = 1;
+      attr[n].val.clusterDim.z = 1;
+      ++n;
+    }
+    if (ctx->pdl) {
+      attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[n].val.programmaticStreamSerializationAllowed = 1;
+      ++n;
+    }
+    cfg.numAttrs = n;
+  }
+};
 
 static bool capturing(cudaStream_t st) {
   cudaStreamCaptureStatus s = cudaStreamCaptureStatusNone;
@@ -330,7 +360,8 @@ static int launch_gemv_balanced(myl_ctx* ctx, const myl_weight* w, const int16_t
   int64_t ldw = w->ldp;
   Epilogue e = ep;
   void* args[] = {(void*)&dW, (void*)&ldw, (void*)&N, (void*)&x, (void*)&ldx, (void*)&K, (void*)&e};
-  CUDA_TRY(cudaLaunchKernel(fn, dim3(grid), dim3(GEMV_THREADS), args, smem, st));
+  LaunchCfg lc(ctx, dim3(grid), dim3(GEMV_THREADS), smem, st);
+  CUDA_TRY(cudaLaunchKernelExC(&lc.cfg, fn, args));
   ctx->launches++;
   return MYL_OK;
 }
@@ -380,14 +411,16 @@ static int launch_gemv(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int6
   int64_t ldw = w->ldp, N = w->N;
   void* args[] = {(void*)&dW, (void*)&ldw, (void*)&N, (void*)&x, (void*)&ldx,
                   (void*)&K, (void*)&k_slice, (void*)&ep, (void*)&slice_stride};
-  CUDA_TRY(cudaLaunchKernel(v.fn, grid, dim3(GEMV_THREADS), args, smem, st));
+  LaunchCfg lc(ctx, grid, dim3(GEMV_THREADS), smem, st);
+  CUDA_TRY(cudaLaunchKernelExC(&lc.cfg, v.fn, args));
   ctx->launches++;
   if (ksplit > 1) {
     const int64_t total = M * w->N;
     unsigned blocks = unsigned(std::min<int64_t>((total + 255) / 256, int64_t(ctx->num_sms) * 8));
-    reduce_requant_kernel<<<blocks, 256, 0, st>>>(static_cast<const int64_t*>(ctx->part.p), ksplit,
-                                                   slice_stride, M, w->N, ep_final);
-    CUDA_TRY(cudaGetLastError());
+    LaunchCfg lr(ctx, dim3(blocks), dim3(256), 0, st);
+    CUDA_TRY(cudaLaunchKernelEx(&lr.cfg, reduce_requant_kernel,
+                                static_cast<const int64_t*>(ctx->part.p), ksplit, slice_stride, M,
+                                w->N, ep_final));
     ctx->launches++;
   }
   return MYL_OK;
@@ -454,27 +487,9 @@ static int launch_tc_mode(myl_ctx* ctx, const myl_weight* w, const CUtensorMap& 
   wk.wsum_ld = w->wsum_ld;
   wk.xbox = tc_xbox(ctx, BN);
   const unsigned grid = unsigned(std::max<int64_t>(1, std::min<int64_t>(units, slots)));
-  if (PAIR) {
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.gridDim = dim3(2 * grid);
-    cfg.blockDim = dim3(TC_THREADS);
-    cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
-    cfg.stream = st;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    CUDA_TRY(cudaLaunchKernelEx(&cfg, fn, w->tm128, tm_xhi, tm_xlo, M, N, wk, ep, slice_stride,
-                                ctx->d_err, ctx->timeout_ns, ctx->inject_fault));
-  } else {
-    fn<<<grid, TC_THREADS, Cfg::SMEM_BYTES, st>>>(w->tm128, tm_xhi, tm_xlo, M, N, wk, ep,
-                                                   slice_stride, ctx->d_err, ctx->timeout_ns,
-                                                   ctx->inject_fault);
-    CUDA_TRY(cudaGetLastError());
-  }
+  LaunchCfg lc(ctx, dim3(PAIR ? 2 * grid : grid), dim3(TC_THREADS), Cfg::SMEM_BYTES, st, PAIR ? 2u : 0u);
+  CUDA_TRY(cudaLaunchKernelEx(&lc.cfg, fn, w->tm128, tm_xhi, tm_xlo, M, N, wk, ep, slice_stride,
+                              ctx->d_err, ctx->timeout_ns, ctx->inject_fault));
   ctx->launches++;
   return MYL_OK;
 }
@@ -534,8 +549,8 @@ static int launch_split(myl_ctx* ctx, const int16_t* x, int64_t M, int64_t K, in
                         uint8_t* xhi, uint8_t* xlo, int64_t ldp, cudaStream_t st) {
   const int64_t groups = M * (ldp / 8);
   unsigned blocks = unsigned(std::min<int64_t>((groups + 255) / 256, int64_t(ctx->num_sms) * 16));
-  split_hilo_kernel<<<blocks, 256, 0, st>>>(x, ldx, M, K, xhi, xlo, ldp);
-  CUDA_TRY(cudaGetLastError());
+  LaunchCfg lc(ctx, dim3(blocks), dim3(256), 0, st);
+  CUDA_TRY(cudaLaunchKernelEx(&lc.cfg, split_hilo_kernel, x, ldx, M, K, xhi, xlo, ldp));
   ctx->launches++;
   return MYL_OK;
 }
@@ -585,10 +600,10 @@ static int launch_tc_planes(myl_ctx* ctx, const myl_weight* w, const uint8_t* xh
     TRY(launch_tc_any(ctx, w, tm_xhi, tm_xlo, M, BN, pair, work, ep_final, 0, st));
     const int64_t total = int64_t(work.tail_tiles) * BN * (ct / 2);
     const unsigned blocks = unsigned(std::min<int64_t>((total + 255) / 256, int64_t(sms(ctx)) * 8));
-    tail_reduce_kernel<<<blocks, 256, 0, st>>>(work.tail_ws, work.tail_tiles, work.tail_ks,
-                                                work.full_units, work.tiles_n, BN, ct, M, w->N,
-                                                ep_final);
-    CUDA_TRY(cudaGetLastError());
+    LaunchCfg lc(ctx, dim3(blocks), dim3(256), 0, st);
+    CUDA_TRY(cudaLaunchKernelEx(&lc.cfg, tail_reduce_kernel, work.tail_ws, work.tail_tiles,
+                                work.tail_ks, work.full_units, work.tiles_n, BN, ct, M, w->N,
+                                ep_final));
     ctx->launches++;
     return MYL_OK;
   }
@@ -607,9 +622,10 @@ static int launch_tc_planes(myl_ctx* ctx, const myl_weight* w, const uint8_t* xh
   if (ksplit > 1) {
     const int64_t total = M * w->N;
     unsigned blocks = unsigned(std::min<int64_t>((total + 255) / 256, int64_t(ctx->num_sms) * 8));
-    reduce_requant_kernel<<<blocks, 256, 0, st>>>(static_cast<const int64_t*>(ctx->part.p), ksplit,
-                                                   slice_stride, M, w->N, ep_final);
-    CUDA_TRY(cudaGetLastError());
+    LaunchCfg lc(ctx, dim3(blocks), dim3(256), 0, st);
+    CUDA_TRY(cudaLaunchKernelEx(&lc.cfg, reduce_requant_kernel,
+                                static_cast<const int64_t*>(ctx->part.p), ksplit, slice_stride, M,
+                                w->N, ep_final));
     ctx->launches++;
   }
   return MYL_OK;
@@ -634,8 +650,9 @@ static int dispatch_linear(myl_ctx* ctx, const myl_weight* w, const int16_t* x, 
       return fail(MYL_ERR_ARG, "int16 weights take the LM-head requant (MYL_RQ_SHIFT_I32) only");
     TRY(ensure(ctx->xsum, size_t(M) * 8));
     const unsigned blocks = unsigned(std::min<int64_t>((M + 7) / 8, int64_t(ctx->num_sms) * 8));
-    x_row_sums_kernel<<<blocks, 256, 0, st>>>(x, ldx, M, w->K, static_cast<int64_t*>(ctx->xsum.p));
-    CUDA_TRY(cudaGetLastError());
+    LaunchCfg lc(ctx, dim3(blocks), dim3(256), 0, st);
+    CUDA_TRY(cudaLaunchKernelEx(&lc.cfg, x_row_sums_kernel, x, ldx, M, w->K,
+                                static_cast<int64_t*>(ctx->xsum.p)));
     ctx->launches++;
     ep.mode = EPI_W16;
     ep.xsum = static_cast<const int64_t*>(ctx->xsum.p);

@@ -22,6 +22,8 @@ __device__ __forceinline__ int64_t select_key(int32_t v, int64_t i) {
 }
 
 __global__ void select_init_kernel(int64_t* __restrict__ keys, int64_t M) {
+  pdl_wait();
+  pdl_launch();
   for (int64_t m = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; m < M;
        m += int64_t(gridDim.x) * blockDim.x)
     keys[m] = INT64_MIN;  // below every key: a shard without logits never wins
@@ -32,6 +34,8 @@ __global__ void select_init_kernel(int64_t* __restrict__ keys, int64_t M) {
 __global__ void __launch_bounds__(SELECT_THREADS)
     select_keys_kernel(const int32_t* __restrict__ logits, int64_t M, int64_t V, int64_t ld,
                        int64_t index_base, int64_t* __restrict__ keys) {
+  pdl_wait();
+  pdl_launch();
   __shared__ int64_t part[SELECT_THREADS / 32];
   const int64_t j0 = int64_t(blockIdx.x) * SELECT_CHUNK;
   for (int64_t m = blockIdx.y; m < M; m += gridDim.y) {
