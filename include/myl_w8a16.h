@@ -554,6 +554,30 @@ int myl_generate(myl_ctx* ctx, const myl_model* model, myl_session* s, const int
  * last logits. */
 int myl_decode_greedy(myl_ctx* ctx, const myl_model* model, myl_session* s, int64_t max_new,
                       int32_t* out_tokens, uint8_t* digests, int32_t* step_logits);
+/* Tensor parallelism over `world` GPUs of one node, one process per GPU
+ * (Megatron style, every rank calls the same entry points in the same order):
+ * rank r's model holds an even share of the query heads and the KV heads they
+ * read (uneven head counts, e.g. 28 heads on 8 ranks, give some ranks one
+ * more head and share a KV head between two ranks), of the MLP's intermediate
+ * channels (gate/up rows, down columns) and of the vocabulary rows of the LM
+ * head; embedding, norms and the residual stream are replicated. The
+ * row-parallel projections (o_proj, down) write exact int64 partial sums
+ * straight into every rank's receive region over NVLink (peer memory); after a
+ * bounded device barrier every rank sums the slabs and requantises once, so
+ * the result is bit-identical to the single-GPU model (integer addition is
+ * exact and associative). Greedy selection takes the largest
+ * (logit, lowest index) key over the ranks' vocabulary shares.
+ * Setup: myl_model_create_tp with the whole model spec; a session; a region of
+ * myl_session_tp_bytes bytes per rank shared with myl_ipc_alloc/myl_ipc_open;
+ * myl_session_set_tp with every rank's region base (index = rank), then a host
+ * barrier of the ranks. myl_forward's logits are this rank's vocabulary rows
+ * [B][v1 - v0]; digests and step logits are world-1 only. */
+int myl_model_create_tp(myl_ctx* ctx, const myl_model_spec* spec, int world, int rank,
+                        myl_model** out);
+/* info[10] = world, rank, q0, q1, kv0, kv1, i0, i1, v0, v1 (this rank's ranges). */
+int myl_model_shard(const myl_model* model, int64_t* info);
+int64_t myl_session_tp_bytes(const myl_session* s);
+int myl_session_set_tp(myl_ctx* ctx, myl_session* s, void* const* bases);
 /* Device time (CUDA events on the launching stream) of the session's last
  * prompt pass (myl_forward or the prefill of myl_generate) and decode loop. */
 int myl_session_timing(const myl_session* s, float* prefill_ms, float* decode_ms);

@@ -78,6 +78,12 @@ struct Epilogue {
   void* xg_dst[MYL_XCHG_MAX];
   int64_t xg_row0;
   int xg_world;
+  // Broadcast (EPI_ACC_I64, xb_world > 0): the exact partial of output (m, n)
+  // goes to every rank o, into xb_dst[o] at xb_rank * xb_slab + m * ldy + n
+  // (tensor-parallel decode: each rank then sums all slabs locally).
+  void* xb_dst[MYL_XCHG_MAX];
+  int64_t xb_slab;
+  int xb_rank, xb_world;
 };
 
 // ---- programmatic dependent launch ---------------------------------------------
@@ -225,7 +231,10 @@ __device__ __forceinline__ void w16_store(const Epilogue& ep, int64_t m, int64_t
 __device__ __forceinline__ void epilogue_store(const Epilogue& ep, int64_t m, int64_t n,
                                                int64_t acc) {
   if (ep.mode == EPI_ACC_I64) {
-    if (ep.xs_world > 0) {
+    if (ep.xb_world > 0) {
+      const int64_t idx = ep.xb_rank * ep.xb_slab + m * ep.ldy + n;
+      for (int o = 0; o < ep.xb_world; ++o) static_cast<int64_t*>(ep.xb_dst[o])[idx] = acc;
+    } else if (ep.xs_world > 0) {
       const int64_t o = m / ep.xs_rows;
       static_cast<int64_t*>(ep.xs_dst[o])[(ep.xs_rank * ep.xs_rows + (m - o * ep.xs_rows)) * ep.ldy + n] =
           acc;

@@ -96,6 +96,14 @@ struct ResidParams {
   const int8_t* s2;        // [H]
   int16_t* resid_out;      // [rows][ld_res] the new residual stream (may be the input)
   int64_t ld_res;
+  // Tensor parallelism: the added projection output is the requant of the
+  // exact sum of nparts int64 partial slabs (parts + o * part_slab, rows of H),
+  // clamp_i16(rescale_i64(sum, part_shift[i])) (linear.rs:61-68 after the
+  // row-parallel sum); `add` is then ignored.
+  const int64_t* parts;
+  int nparts;
+  int64_t part_slab;
+  const int8_t* part_shift;
 };
 
 constexpr int NORM_THREADS = 256;
@@ -205,6 +213,39 @@ __device__ __forceinline__ uint4 pack16(const int16_t (&a)[8]) {
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+// rmsnorm.rs:140-151 for one channel: the product shifted by sh, then the i32
+// and i16 clamps. Left shifts (negative sh) go through i128, out of line: they
+// are rare, and the code stays small for the single-block decode launches.
+__device__ __noinline__ int16_t norm_out_left(int64_t prod, int sh) {
+  const __int128 w = (__int128)((unsigned __int128)(__int128)prod << (-sh));
+  const int64_t t = w < (__int128)INT32_MIN ? INT32_MIN : (w > (__int128)INT32_MAX ? INT32_MAX : (int64_t)w);
+  return clamp16(t);
+}
+__device__ __forceinline__ int16_t norm_out(int64_t prod, int sh) {
+  if (sh >= 63) return 0;  // |prod| < 2^37 rounds to zero
+  if (sh > 0) return clamp16(rshift_rne_i64(prod, sh));
+  if (sh == 0) return clamp16(prod);
+  return norm_out_left(prod, sh);
+}
+
+// The root-mean-square normaliser of one row from its square sum: the LUT
+// value and norm_frac (rmsnorm.rs:99-125), or nf = -1000 for an all-zero row.
+__device__ __noinline__ void norm_scale(__int128 a, const NormParams& np, int64_t* lut_val, int* nf) {
+  if (a == 0) {
+    *nf = -1000;
+    *lut_val = 0;
+    return;
+  }
+  const __int128 m = (a * (__int128)np.inv_n) >> 20;
+  const __int128 max_idx = np.lut_len - 1;
+  int q = 0;
+  while ((m >> q) > max_idx) q += 2;
+  __int128 idx = rne_i128(m, q);
+  if (idx > max_idx) idx = max_idx;
+  *lut_val = np.lut[int64_t(idx)];
+  *nf = np.frac0 + q / 2;
+}
+
 __global__ void __launch_bounds__(NORM_THREADS)
     resid_rmsnorm_vec_kernel(const int16_t* __restrict__ x, int64_t ldx, int64_t rows, ResidParams rp,
                              NormParams np, int16_t* __restrict__ out, int64_t ldo,
@@ -218,62 +259,80 @@ __global__ void __launch_bounds__(NORM_THREADS)
   const int64_t nrows = out_rows ? n_out_rows : rows;
   for (int64_t rr = blockIdx.x; rr < nrows; rr += gridDim.x) {
     const int64_t r = out_rows ? out_rows[rr] : rr;
-    uint4 xv[NORM_NV], av[NORM_NV], sbv[NORM_NV];
-    uint2 s1v[NORM_NV], s2v[NORM_NV], alv[NORM_NV], gv[NORM_NV];
+    uint4 xv[NORM_NV], av[NORM_NV];
+    uint2 s1v[NORM_NV], s2v[NORM_NV], alv[NORM_NV];
+    // every load of this thread's vectors first
 #pragma unroll
     for (int k = 0; k < NORM_NV; ++k) {
       const int v = threadIdx.x + k * NORM_THREADS;
       if (v < nv) {
         xv[k] = *reinterpret_cast<const uint4*>(x + r * ldx + 8 * v);
-        if (rp.add) {
+        if (rp.parts) {
+          int64_t sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+          for (int o = 0; o < rp.nparts; ++o) {
+            const longlong2* pp =
+                reinterpret_cast<const longlong2*>(rp.parts + o * rp.part_slab + r * np.H + 8 * v);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const longlong2 t2 = __ldcg(pp + q);
+              sum[2 * q] += t2.x;
+              sum[2 * q + 1] += t2.y;
+            }
+          }
+          const uint2 ps = *reinterpret_cast<const uint2*>(rp.part_shift + 8 * v);
+          int16_t a16[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) a16[e] = clamp16(rescale_i64_signed(sum[e], lane8(ps, e)));
+          av[k] = pack16(a16);
+        } else if (rp.add) {
           av[k] = *reinterpret_cast<const uint4*>(rp.add + r * rp.ld_add + 8 * v);
+        }
+        if (rp.add || rp.parts) {
           s1v[k] = *reinterpret_cast<const uint2*>(rp.s1 + 8 * v);
           s2v[k] = *reinterpret_cast<const uint2*>(rp.s2 + 8 * v);
         }
         alv[k] = *reinterpret_cast<const uint2*>(np.align2 + 8 * v);
-        gv[k] = *reinterpret_cast<const uint2*>(np.gamma + 8 * v);
-        sbv[k] = *reinterpret_cast<const uint4*>(np.sbase + 8 * v);
       }
     }
-    int16_t val[NORM_NV][8];
-    __int128 acc = 0;
+    // residual add, then the square sum: squares (< 2^31) shifted by at most
+    // 20 bits are summed in int64 (8192 of them stay below 2^63), wider
+    // alignments in i128
+    int64_t acc64 = 0;
+    __int128 acc128 = 0;
 #pragma unroll
     for (int k = 0; k < NORM_NV; ++k) {
       const int v = threadIdx.x + k * NORM_THREADS;
       if (v < nv) {
+        int16_t val[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           int64_t t = lane16(xv[k], e);
-          if (rp.add) {
+          if (rp.add || rp.parts) {
             const int64_t h = rescale_i64_signed(t, lane8(s1v[k], e)) + int64_t(lane16(av[k], e));
             t = clamp16(rescale_i64_signed(h, lane8(s2v[k], e)));
           }
-          val[k][e] = int16_t(t);
-          acc += (__int128)(t * t) << uint8_t(lane8(alv[k], e));
+          val[e] = int16_t(t);
+          const int a = uint8_t(lane8(alv[k], e));
+          if (a <= 20) acc64 += (t * t) << a;
+          else acc128 += (__int128)(t * t) << a;
         }
-        if (rp.add && rp.resid_out)
-          *reinterpret_cast<uint4*>(rp.resid_out + r * rp.ld_res + 8 * v) = pack16(val[k]);
+        xv[k] = pack16(val);  // the row after the residual add
+        if ((rp.add || rp.parts) && rp.resid_out)
+          *reinterpret_cast<uint4*>(rp.resid_out + r * rp.ld_res + 8 * v) = xv[k];
       }
     }
+    __int128 acc = (__int128)acc64 + acc128;
     acc = warp_sum_i128(acc);
     if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = acc;
     __syncthreads();
     if (threadIdx.x == 0) {
       __int128 a = 0;
       for (int w = 0; w < NORM_THREADS / 32; ++w) a += s_part[w];
-      if (a == 0) {
-        s_nf = -1000;  // all zero: the row is zeros (rmsnorm.rs:99-101)
-        s_lut_val = 0;
-      } else {
-        const __int128 m = (a * (__int128)np.inv_n) >> 20;
-        const __int128 max_idx = np.lut_len - 1;
-        int q = 0;
-        while ((m >> q) > max_idx) q += 2;
-        __int128 idx = rne_i128(m, q);
-        if (idx > max_idx) idx = max_idx;
-        s_lut_val = np.lut[int64_t(idx)];
-        s_nf = np.frac0 + q / 2;
-      }
+      int64_t lv;
+      int nf;
+      norm_scale(a, np, &lv, &nf);
+      s_lut_val = lv;
+      s_nf = nf;
     }
     __syncthreads();
     const int nf = s_nf;
@@ -282,24 +341,14 @@ __global__ void __launch_bounds__(NORM_THREADS)
     for (int k = 0; k < NORM_NV; ++k) {
       const int v = threadIdx.x + k * NORM_THREADS;
       if (v < nv) {
+        const uint2 gv = *reinterpret_cast<const uint2*>(np.gamma + 8 * v);
+        const uint4 sbv = *reinterpret_cast<const uint4*>(np.sbase + 8 * v);
         int16_t y[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          y[e] = 0;
-          if (nf != -1000) {
-            const int64_t prod = int64_t(val[k][e]) * lv * int64_t(lane8(gv[k], e));
-            const int sh = nf + lane16(sbv[k], e);
-            int64_t t;
-            if (sh >= 63) t = 0;
-            else if (sh > 0) t = rshift_rne_i64(prod, sh);
-            else if (sh == 0) t = prod;
-            else {
-              const __int128 w = (__int128)((unsigned __int128)(__int128)prod << (-sh));
-              t = w < (__int128)INT32_MIN ? INT32_MIN : (w > (__int128)INT32_MAX ? INT32_MAX : (int64_t)w);
-            }
-            y[e] = clamp16(t);
-          }
-        }
+        for (int e = 0; e < 8; ++e)
+          y[e] = nf == -1000 ? int16_t(0)
+                             : norm_out(int64_t(lane16(xv[k], e)) * lv * int64_t(lane8(gv, e)),
+                                        nf + lane16(sbv, e));
         *reinterpret_cast<uint4*>(out + rr * ldo + 8 * v) = pack16(y);
       }
     }
@@ -397,7 +446,8 @@ struct AttnParams {
   int64_t T;               // tokens per sequence in this call
   int64_t rows;            // B * T
   const int64_t* pos0;     // device: position of token 0 of the call
-  int nq, nkv, hd;
+  int nq, nkv, hd;          // this rank's query and KV heads
+  int q_head0, kv_head0, G;  // global index of local head 0 / KV head 0, global group size
   KvCache kc;
   int layer;
   int64_t score_mult;
@@ -450,8 +500,8 @@ __device__ __forceinline__ int dp2a_hi_su(uint32_t a, uint32_t b, int c) {
 // the 8-byte pad makes the per-key 8-byte reads of a half-warp hit distinct
 // banks) and queries [ATT_MAXG][hd8] int16.
 __host__ __device__ constexpr int att_hd8(int hd) { return (hd + 7) & ~7; }
-__host__ __device__ constexpr size_t att_scores_smem(int hd) {
-  return size_t(2 * ATT_KEYS * (att_hd8(hd) + 8)) + size_t(ATT_MAXG * att_hd8(hd) * 2);
+__host__ __device__ constexpr size_t att_scores_smem(int hd, int keys = ATT_KEYS) {
+  return size_t(2 * keys * (att_hd8(hd) + 8)) + size_t(ATT_MAXG * att_hd8(hd) * 2);
 }
 
 __global__ void __launch_bounds__(ATT_THREADS) attn_scores_kernel(AttnParams p, int gsub) {
@@ -459,10 +509,10 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_scores_kernel(AttnParams p, 
   pdl_launch();
   extern __shared__ __align__(16) uint8_t smem[];
   const int hd = p.hd, hd8 = att_hd8(hd), kst = hd8 + 8, qw = hd8 / 2;
+  const int nk = blockDim.x;  // keys per block (<= ATT_KEYS)
   uint8_t* s_kh = smem;
-  uint8_t* s_kl = s_kh + ATT_KEYS * kst;
-  uint32_t* s_q = reinterpret_cast<uint32_t*>(s_kl + ATT_KEYS * kst);  // [ATT_MAXG][hd8/2]
-  const int group = p.nq / p.nkv;
+  uint8_t* s_kl = s_kh + nk * kst;
+  uint32_t* s_q = reinterpret_cast<uint32_t*>(s_kl + nk * kst);  // [ATT_MAXG][hd8/2]
   const int64_t gy = blockIdx.x;
   const int sub = int(gy % gsub);
   const int g = int((gy / gsub) % p.nkv);
@@ -470,12 +520,16 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_scores_kernel(AttnParams p, 
   const int64_t b = r / p.T, t = r % p.T;
   const int64_t pos = p.pos0[0] + t;
   const int64_t len = p.mask ? p.lds : pos + 1;
-  const int64_t j0 = int64_t(blockIdx.y) * ATT_KEYS;
+  const int64_t j0 = int64_t(blockIdx.y) * nk;
   if (j0 >= len) return;
-  const int h0 = g * group + sub * ATT_MAXG;
-  const int nrow = min(ATT_MAXG, g * group + group - h0);
+  // local query heads of KV head g (GQA: global head q reads KV head q / G)
+  const int hs = max(0, (p.kv_head0 + g) * p.G - p.q_head0);
+  const int he = min(p.nq, (p.kv_head0 + g + 1) * p.G - p.q_head0);
+  const int h0 = hs + sub * ATT_MAXG;
+  const int nrow = min(ATT_MAXG, he - h0);
+  if (nrow <= 0) return;
   // queries of the sub-group as int16 pairs, zero-padded to hd8
-  for (int e = threadIdx.x; e < ATT_MAXG * qw; e += ATT_THREADS) {
+  for (int e = threadIdx.x; e < ATT_MAXG * qw; e += nk) {
     const int rr = e / qw, w = e % qw;
     uint32_t v = 0;
     if (rr < nrow) {
@@ -490,9 +544,9 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_scores_kernel(AttnParams p, 
   // 8 elements per step: one 16-byte load, two byte permutes, two 8-byte stores
   const int16_t* kbase = p.kc.k + b * p.kc.seq_stride + int64_t(p.layer) * p.kc.layer_stride +
                          int64_t(g) * p.kc.head_stride;
-  const int nkeys = int(min(int64_t(ATT_KEYS), len - j0));
+  const int nkeys = int(min(int64_t(nk), len - j0));
   const bool vec = (hd & 7) == 0;
-  for (int e = threadIdx.x; e < ATT_KEYS * (hd8 / 8); e += ATT_THREADS) {
+  for (int e = threadIdx.x; e < nk * (hd8 / 8); e += nk) {
     const int jj = e / (hd8 / 8), d = 8 * (e % (hd8 / 8));
     uint4 v = make_uint4(0u, 0u, 0u, 0u);
     if (jj < nkeys) {
@@ -606,7 +660,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_pv_kernel(AttnParams p, int6
   const int32_t one = int32_t(1) << p.prob_frac;
   const int hd = p.hd;
   const int16_t* vbase = p.kc.v + b * p.kc.seq_stride + int64_t(p.layer) * p.kc.layer_stride +
-                         int64_t(h / (p.nq / p.nkv)) * p.kc.head_stride;
+                         int64_t((p.q_head0 + h) / p.G - p.kv_head0) * p.kc.head_stride;
   int64_t acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0;
@@ -766,7 +820,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_pv_vec_kernel(AttnParams p, 
   const int hd = p.hd, tpk = hd / 8, kpi = ATT_THREADS / tpk;
   const int kg = threadIdx.x / tpk, dv = threadIdx.x % tpk;
   const int16_t* vbase = p.kc.v + b * p.kc.seq_stride + int64_t(p.layer) * p.kc.layer_stride +
-                         int64_t(h / (p.nq / p.nkv)) * p.kc.head_stride + 8 * dv;
+                         int64_t((p.q_head0 + h) / p.G - p.kv_head0) * p.kc.head_stride + 8 * dv;
   int64_t acc[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) acc[e] = 0;
@@ -844,6 +898,51 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_pv_vec_kernel(AttnParams p, 
   if (nch > 1 && threadIdx.x == 0) p.counters[row] = 0;
 }
 
+// ---- tensor-parallel barrier ----------------------------------------------------
+// All ranks call it the same number of times in the same order; each call's
+// epoch is this rank's device counter + 1 (so a captured graph replays it
+// with a fresh epoch). Optionally first copies `n` int64 values from `src`
+// into every rank's slot dst[o] + rank * n. Thread t < world: system fence,
+// release store of the epoch into rank t's flag word of this rank, then a
+// bounded acquire wait for this rank's flag word of sender t (a peer that
+// does not arrive within timeout_ns sets DEV_WAIT_PEER and the kernel returns).
+struct TpPeers {
+  unsigned long long* flags[MYL_XCHG_MAX];  // each rank's flag words (one per sender)
+  int64_t* keys[MYL_XCHG_MAX];              // each rank's key slots [world][B]
+};
+
+__global__ void tp_barrier_kernel(TpPeers peers, int world, int rank,
+                                  unsigned long long* __restrict__ epoch_ctr,
+                                  const int64_t* __restrict__ src, int64_t n, int* err,
+                                  uint64_t timeout_ns) {
+  pdl_wait();
+  pdl_launch();
+  const int t = threadIdx.x;
+  const unsigned long long epoch = epoch_ctr[0] + 1ull;
+  if (src)
+    for (int o = 0; o < world; ++o)
+      for (int64_t i = t; i < n; i += blockDim.x) peers.keys[o][int64_t(rank) * n + i] = src[i];
+  __syncthreads();
+  if (t < world) {
+    __threadfence_system();
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(peers.flags[t] + rank), "l"(epoch) : "memory");
+    const unsigned long long* mine = peers.flags[rank] + t;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+      unsigned long long v;
+      asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(mine) : "memory");
+      if (v >= epoch) break;
+      if (globaltimer_ns() - t0 > timeout_ns) {
+        atomicCAS(err, 0, DEV_WAIT_PEER);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncthreads();
+  if (t == 0) epoch_ctr[0] = epoch;
+}
+
 // ---- greedy selection into the token stream -----------------------------------------
 // keys[b] (select_key) -> token = 2^32 - 1 - (key & 0xFFFFFFFF); written to the
 // next-step token buffer and to out_tokens[b * ld_out + step], step from the
@@ -852,12 +951,15 @@ __global__ void greedy_commit_kernel(const int64_t* __restrict__ keys, int64_t B
                                      int32_t* __restrict__ next_tokens,
                                      int32_t* __restrict__ out_tokens, int64_t ld_out,
                                      int64_t* __restrict__ step, int64_t* __restrict__ pos,
-                                     int64_t pos_advance) {
+                                     int64_t pos_advance, int nslots) {
   pdl_wait();
   pdl_launch();
   const int64_t s = step[0];
   for (int64_t b = threadIdx.x; b < B; b += blockDim.x) {
-    const int32_t tok = int32_t(int64_t(0xFFFFFFFFll) - (keys[b] & 0xFFFFFFFFll));
+    // the largest key over the vocabulary shards' slots [nslots][B]
+    int64_t key = keys[b];
+    for (int o = 1; o < nslots; ++o) key = max(key, keys[int64_t(o) * B + b]);
+    const int32_t tok = int32_t(int64_t(0xFFFFFFFFll) - (key & 0xFFFFFFFFll));
     next_tokens[b] = tok;
     if (out_tokens) out_tokens[b * ld_out + s] = tok;
   }

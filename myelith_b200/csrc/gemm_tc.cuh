@@ -609,7 +609,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           continue;
         }
         if (n >= N) continue;
-        if (mode == EPI_ACC_I64) {
+        if (mode == EPI_ACC_I64 && e.xb_world > 0) {  // broadcast to every rank's slab
+          for (int o = 0; o < e.xb_world; ++o) {
+            int64_t* yb = static_cast<int64_t*>(e.xb_dst[o]) + e.xb_rank * e.xb_slab + mc * e.ldy + n;
+            store_column<NC>(yb, e.ldy, mc, Mend, [&](int j) {
+              return int64_t(int32_t(hi[j])) * 256 + int64_t(int32_t(lo[j]));
+            });
+          }
+        } else if (mode == EPI_ACC_I64) {
           int64_t* yb;
           if (e.xs_world > 0) {  // exchange: the owning rank's receive buffer (peer memory)
             // xs_rows is a multiple of 16 >= NC, so the NC tokens share one owner

@@ -51,7 +51,13 @@ struct ModelLayer {
 }  // namespace
 
 struct myl_model {
+  // V, nq, nkv, I (and QD, KD) are this rank's shares under tensor parallelism
   int64_t V = 0, H = 0, L = 0, nq = 0, nkv = 0, hd = 0, I = 0, QD = 0, KD = 0, ldq = 0;
+  int world = 1, rank = 0;
+  // global index of this rank's first query head, KV head, intermediate
+  // channel and vocabulary row; global query heads per KV head
+  int64_t q0 = 0, kv0 = 0, i0 = 0, v0 = 0, G = 1;
+  int64_t V_global = 0;
   uint8_t final_norm_frac = 0, logit_frac = 0, prob_frac = 0, rope_frac = 0;
   int8_t* d_embed = nullptr;  // own table when the LM head is not the embedding
   const int8_t* embed_rows = nullptr;
@@ -100,6 +106,15 @@ struct myl_session {
   // events on the launching stream
   cudaEvent_t ev[4] = {};
   float prefill_ms = 0.f, decode_ms = 0.f;
+  // tensor parallelism: one peer-memory region per rank (myl_session_set_tp)
+  // holding two receive regions [world][rows_cap][H] int64 (o_proj and down
+  // projection partials), key slots [world][B] int64 and flag words [world].
+  bool tp_ready = false;
+  int64_t* recv[2] = {nullptr, nullptr};
+  void* peer_recv[2][MYL_XCHG_MAX] = {};
+  int64_t* key_slots = nullptr;
+  TpPeers peers{};
+  unsigned long long* d_epoch = nullptr;
   std::vector<void*> allocs;
 };
 
@@ -211,7 +226,10 @@ void release_model(myl_ctx* ctx, myl_model* m) {
 int build_layer(myl_ctx* ctx, myl_model* m, const myl_model_spec* sp, int64_t l) {
   const myl_layer_spec& ls = sp->layers[l];
   ModelLayer& L = m->layers[size_t(l)];
-  const int64_t H = m->H, QD = m->QD, KD = m->KD, I = m->I;
+  const int64_t H = m->H, QD = m->QD, KD = m->KD, I = m->I, hd = m->hd;
+  // this rank's rows of q/k/v, columns of o_proj, channels of the MLP
+  const int64_t qr0 = m->q0 * hd, kr0 = m->kv0 * hd, QDg = sp->num_heads * hd,
+                Ig = sp->intermediate;
   const uint8_t* out_res = l + 1 < m->L ? sp->layers[l + 1].residual_in_frac : sp->final_residual_frac;
   if (!ls.ln1_gamma || !ls.ln1_gamma_shifts || !ls.ln2_gamma || !ls.ln2_gamma_shifts || !ls.wq ||
       !ls.wk || !ls.wv || !ls.wo || !ls.wg || !ls.wu || !ls.wd || !ls.sq || !ls.sk || !ls.sv ||
@@ -225,12 +243,12 @@ int build_layer(myl_ctx* ctx, myl_model* m, const myl_model_spec* sp, int64_t l)
   const int64_t NQKV = QD + 2 * KD;
   std::vector<int8_t> w(size_t(NQKV) * size_t(H));
   std::vector<uint8_t> ws(static_cast<size_t>(NQKV)), of(static_cast<size_t>(NQKV));
-  std::memcpy(w.data(), ls.wq, size_t(QD * H));
-  std::memcpy(w.data() + QD * H, ls.wk, size_t(KD * H));
-  std::memcpy(w.data() + (QD + KD) * H, ls.wv, size_t(KD * H));
-  std::memcpy(ws.data(), ls.sq, size_t(QD));
-  std::memcpy(ws.data() + QD, ls.sk, size_t(KD));
-  std::memcpy(ws.data() + QD + KD, ls.sv, size_t(KD));
+  std::memcpy(w.data(), ls.wq + qr0 * H, size_t(QD * H));
+  std::memcpy(w.data() + QD * H, ls.wk + kr0 * H, size_t(KD * H));
+  std::memcpy(w.data() + (QD + KD) * H, ls.wv + kr0 * H, size_t(KD * H));
+  std::memcpy(ws.data(), ls.sq + qr0, size_t(QD));
+  std::memcpy(ws.data() + QD, ls.sk + kr0, size_t(KD));
+  std::memcpy(ws.data() + QD + KD, ls.sv + kr0, size_t(KD));
   std::fill(of.begin(), of.begin() + QD, ls.q_frac);
   std::fill(of.begin() + QD, of.begin() + QD + KD, ls.k_frac);
   std::fill(of.begin() + QD + KD, of.end(), ls.v_frac);
@@ -240,11 +258,11 @@ int build_layer(myl_ctx* ctx, myl_model* m, const myl_model_spec* sp, int64_t l)
   if (bias) {
     // add_bias_i16 (linear.rs:132-145) per segment, rescaled to its out_frac
     std::vector<int32_t> b(static_cast<size_t>(NQKV)), seg;
-    TRY(rescale_bias(ls.bq, ls.bq_shifts, QD, ls.q_frac, seg));
+    TRY(rescale_bias(ls.bq + qr0, ls.bq_shifts + qr0, QD, ls.q_frac, seg));
     std::copy(seg.begin(), seg.end(), b.begin());
-    TRY(rescale_bias(ls.bk, ls.bk_shifts, KD, ls.k_frac, seg));
+    TRY(rescale_bias(ls.bk + kr0, ls.bk_shifts + kr0, KD, ls.k_frac, seg));
     std::copy(seg.begin(), seg.end(), b.begin() + QD);
-    TRY(rescale_bias(ls.bv, ls.bv_shifts, KD, ls.v_frac, seg));
+    TRY(rescale_bias(ls.bv + kr0, ls.bv_shifts + kr0, KD, ls.v_frac, seg));
     std::copy(seg.begin(), seg.end(), b.begin() + QD + KD);
     CUDA_TRY(cudaMalloc(&L.rq_qkv->d_bias, size_t(NQKV) * 4));
     CUDA_TRY(cudaMemcpy(L.rq_qkv->d_bias, b.data(), size_t(NQKV) * 4, cudaMemcpyHostToDevice));
@@ -259,13 +277,22 @@ int build_layer(myl_ctx* ctx, myl_model* m, const myl_model_spec* sp, int64_t l)
   std::vector<uint8_t> acc_attn, acc_mlp;
   TRY(make_resid(m, ls.residual_in_frac, ls.residual_mid_frac, &L.add_attn, &acc_attn));
   TRY(make_resid(m, ls.residual_mid_frac, out_res, &L.add_mlp, &acc_mlp));
-  TRY(myl_weight_register(ctx, ls.wo, H, QD, QD, ls.so, &L.w_o));
+  TRY(myl_weight_register(ctx, ls.wo + qr0, H, QD, QDg, ls.so, &L.w_o));
   TRY(myl_requant_create(ctx, L.w_o, MYL_RQ_SHIFT_I16, ls.attn_out_frac, acc_attn.data(), 1, nullptr,
                          nullptr, &L.rq_o));
-  TRY(myl_mlp_register(ctx, ls.wg, ls.wu, ls.wd, H, I, ls.sg, ls.su, ls.sd, sp->silu_lut,
-                       sp->silu_len, ls.norm_mlp_frac, ls.gate_frac, ls.up_frac, ls.down_in_frac,
-                       sp->silu_in_frac, sp->silu_lut_offset, sp->silu_out_frac, acc_mlp.data(),
-                       &L.mlp));
+  // the down projection's columns of this rank's channels, contiguous
+  std::vector<int8_t> wd_local;
+  const int8_t* wd = ls.wd;
+  if (I != Ig) {
+    wd_local.resize(size_t(H) * size_t(I));
+    for (int64_t r = 0; r < H; ++r)
+      std::memcpy(wd_local.data() + r * I, ls.wd + r * Ig + m->i0, size_t(I));
+    wd = wd_local.data();
+  }
+  TRY(myl_mlp_register(ctx, ls.wg + m->i0 * H, ls.wu + m->i0 * H, wd, H, I, ls.sg + m->i0,
+                       ls.su + m->i0, ls.sd, sp->silu_lut, sp->silu_len, ls.norm_mlp_frac,
+                       ls.gate_frac, ls.up_frac, ls.down_in_frac, sp->silu_in_frac,
+                       sp->silu_lut_offset, sp->silu_out_frac, acc_mlp.data(), &L.mlp));
   TRY(make_norm(m, ls.residual_in_frac, ls.ln1_gamma, ls.ln1_gamma_shifts, sp->rsqrt_input_shift,
                 sp->rsqrt_output_frac, ls.norm_attn_frac, &L.norm1));
   TRY(make_norm(m, ls.residual_mid_frac, ls.ln2_gamma, ls.ln2_gamma_shifts, sp->rsqrt_input_shift,
@@ -298,7 +325,7 @@ int session_alloc(myl_ctx* ctx, myl_session* s) {
   TRY(dev_alloc(A, &s->attn, size_t(R * m->QD)));
   TRY(dev_alloc(A, &s->xf, size_t(B * H)));
   TRY(dev_alloc(A, &s->scores, size_t(R * m->nq) * size_t(s->max_pos)));
-  s->max_chunks = int((s->max_pos + ATT_CHUNK - 1) / ATT_CHUNK);
+  s->max_chunks = int((s->max_pos + ATT_CHUNK / 2 - 1) / (ATT_CHUNK / 2));
   TRY(dev_alloc(A, &s->part, size_t(s->part_rows * m->nq) * size_t(s->max_chunks) * size_t(m->hd)));
   TRY(dev_alloc(A, &s->counters, size_t(s->part_rows * m->nq)));
   CUDA_TRY(cudaMemset(s->counters, 0, size_t(s->part_rows * m->nq) * sizeof(unsigned)));
@@ -355,6 +382,9 @@ int run_attention(myl_ctx* ctx, const myl_model* m, myl_session* s, const ModelL
   p.nq = int(m->nq);
   p.nkv = int(m->nkv);
   p.hd = int(m->hd);
+  p.q_head0 = int(m->q0);
+  p.kv_head0 = int(m->kv0);
+  p.G = int(m->G);
   p.kc = s->cache;
   p.layer = layer;
   p.score_mult = m->score_mult;
@@ -372,16 +402,17 @@ int run_attention(myl_ctx* ctx, const myl_model* m, myl_session* s, const ModelL
   p.counters = s->counters;
   p.out = s->attn;
   p.ldo = m->QD;
-  const int group = int(m->nq / m->nkv);
-  const int gsub = (group + ATT_MAXG - 1) / ATT_MAXG;
-  const size_t smem1 = att_scores_smem(int(m->hd));
-  const int64_t kchunks = (lds_len + ATT_KEYS - 1) / ATT_KEYS;
-  const dim3 g1 = dim3(unsigned(rows * m->nkv * gsub), unsigned(kchunks));
-  LaunchCfg l1(ctx, g1, dim3(ATT_THREADS), smem1, st);
-  CUDA_TRY(cudaLaunchKernelEx(&l1.cfg, attn_scores_kernel, p, gsub));
-  // pass 2: split the keys of few rows over several blocks, one block per row otherwise
+  const int gsub = int((m->G + ATT_MAXG - 1) / ATT_MAXG);
+  // few rows (decode): small key blocks and chunks, so that the keys of a
+  // long context spread over many SMs; many rows: one block per row for pass 2
   const bool split = rows <= s->part_rows && rows * m->nq < 4 * int64_t(ctx->num_sms);
-  const int64_t chunk = split ? ATT_CHUNK : ((lds_len + ATT_CHUNK - 1) / ATT_CHUNK) * ATT_CHUNK;
+  const int kb = split ? 64 : ATT_KEYS;
+  const size_t smem1 = att_scores_smem(int(m->hd), kb);
+  const int64_t kchunks = (lds_len + kb - 1) / kb;
+  const dim3 g1 = dim3(unsigned(rows * m->nkv * gsub), unsigned(kchunks));
+  LaunchCfg l1(ctx, g1, dim3(kb), smem1, st);
+  CUDA_TRY(cudaLaunchKernelEx(&l1.cfg, attn_scores_kernel, p, gsub));
+  const int64_t chunk = split ? ATT_CHUNK / 2 : ((lds_len + ATT_CHUNK - 1) / ATT_CHUNK) * ATT_CHUNK;
   const dim3 g2 = dim3(unsigned(rows * m->nq), unsigned((lds_len + chunk - 1) / chunk));
   if (m->hd % 8 == 0) {
     LaunchCfg l2(ctx, g2, dim3(ATT_THREADS), size_t(ATT_THREADS) * 8 * 8, st);
@@ -412,6 +443,41 @@ int launch_norm(myl_ctx* ctx, const myl_model* m, const int16_t* x, int64_t rows
   return MYL_OK;
 }
 
+// Tensor parallelism: the bounded barrier of all ranks (optionally carrying
+// the B greedy keys of this rank into every rank's key slots).
+int tp_barrier(myl_ctx* ctx, myl_session* s, const int64_t* keys, int64_t n, cudaStream_t st) {
+  const myl_model* m = s->m;
+  LaunchCfg lc(ctx, dim3(1), dim3(32), 0, st);
+  CUDA_TRY(cudaLaunchKernelEx(&lc.cfg, tp_barrier_kernel, s->peers, m->world, m->rank, s->d_epoch,
+                              keys, n, ctx->d_err, ctx->timeout_ns));
+  ctx->launches++;
+  return MYL_OK;
+}
+
+// The epilogue of a row-parallel projection under tensor parallelism: exact
+// int64 partials broadcast into slab `rank` of receive region `which` on
+// every rank (rows of H).
+Epilogue tp_partial_ep(const myl_session* s, int which) {
+  Epilogue e{};
+  e.mode = EPI_ACC_I64;
+  e.ldy = s->m->H;
+  e.xb_world = s->m->world;
+  e.xb_rank = s->m->rank;
+  e.xb_slab = s->rows_cap * s->m->H;
+  for (int o = 0; o < s->m->world; ++o) e.xb_dst[o] = s->peer_recv[which][o];
+  return e;
+}
+
+// The residual add of a row-parallel projection under tensor parallelism:
+// the ranks' partial slabs of receive region `which`, requantised with shift.
+void tp_parts(const myl_session* s, int which, const int8_t* shift, ResidParams* rp) {
+  rp->add = nullptr;
+  rp->parts = s->recv[which];
+  rp->nparts = s->m->world;
+  rp->part_slab = s->rows_cap * s->m->H;
+  rp->part_shift = shift;
+}
+
 // The forward of T tokens per sequence (rows = B * T, tokens on the device,
 // positions from s->d_pos). want_logits: the last token's logits into
 // s->logits. lds_len bounds the keys any row reads (the attention grids cover
@@ -423,10 +489,11 @@ int model_forward(myl_ctx* ctx, const myl_model* m, myl_session* s, const int32_
     LaunchCfg lc(ctx, dim3(unsigned(std::min<int64_t>(rows, 65535))), dim3(256), 0, st);
     CUDA_TRY(cudaLaunchKernelEx(&lc.cfg, embed_kernel, tokens, rows, m->embed_rows, m->lde,
                                 static_cast<const uint8_t*>(m->d_embed_shifts),
-                                static_cast<const uint8_t*>(m->d_rin0), H, m->V, s->hid, H,
+                                static_cast<const uint8_t*>(m->d_rin0), H, m->V_global, s->hid, H,
                                 ctx->d_err));
   }
   ctx->launches++;
+  const bool tp = m->world > 1;
   for (int64_t l = 0; l < m->L; ++l) {
     const ModelLayer& L = m->layers[size_t(l)];
     ResidParams rp{};
@@ -438,6 +505,7 @@ int model_forward(myl_ctx* ctx, const myl_model* m, myl_session* s, const int32_
       rp.s2 = P.add_mlp.s2;
       rp.resid_out = s->hid;
       rp.ld_res = H;
+      if (tp) tp_parts(s, 1, P.mlp->d_shift_down, &rp);
       TRY(launch_norm(ctx, m, s->mid, rows, rp, L.norm1, s->xn, nullptr, 0, st));
     } else {
       TRY(launch_norm(ctx, m, s->hid, rows, rp, L.norm1, s->xn, nullptr, 0, st));
@@ -455,16 +523,29 @@ int model_forward(myl_ctx* ctx, const myl_model* m, myl_session* s, const int32_
     }
     ctx->launches++;
     TRY(run_attention(ctx, m, s, L, int(l), rows, T, lds_len, st));
-    TRY(dispatch_linear(ctx, L.w_o, s->attn, rows, m->QD, make_ep(L.rq_o, s->o, H), st));
     ResidParams ra{};
-    ra.add = s->o;
     ra.ld_add = H;
     ra.s1 = L.add_attn.s1;
     ra.s2 = L.add_attn.s2;
     ra.resid_out = s->mid;
     ra.ld_res = H;
+    if (tp) {
+      // row-parallel o_proj: partials to every rank, barrier, sum + requant in the norm
+      TRY(dispatch_linear(ctx, L.w_o, s->attn, rows, m->QD, tp_partial_ep(s, 0), st));
+      TRY(tp_barrier(ctx, s, nullptr, 0, st));
+      tp_parts(s, 0, L.rq_o->d_shift, &ra);
+    } else {
+      TRY(dispatch_linear(ctx, L.w_o, s->attn, rows, m->QD, make_ep(L.rq_o, s->o, H), st));
+      ra.add = s->o;
+    }
     TRY(launch_norm(ctx, m, s->hid, rows, ra, L.norm2, s->xn, nullptr, 0, st));
-    TRY(run_mlp(ctx, L.mlp, s->xn, rows, H, s->mlp_out, H, st));
+    if (tp) {
+      const Epilogue down = tp_partial_ep(s, 1);
+      TRY(run_mlp(ctx, L.mlp, s->xn, rows, H, nullptr, H, st, nullptr, XPlanes(), &down));
+      TRY(tp_barrier(ctx, s, nullptr, 0, st));
+    } else {
+      TRY(run_mlp(ctx, L.mlp, s->xn, rows, H, s->mlp_out, H, st));
+    }
   }
   if (want_logits) {
     const ModelLayer& P = m->layers[size_t(m->L - 1)];
@@ -473,6 +554,7 @@ int model_forward(myl_ctx* ctx, const myl_model* m, myl_session* s, const int32_
     rp.ld_add = H;
     rp.s1 = P.add_mlp.s1;
     rp.s2 = P.add_mlp.s2;
+    if (tp) tp_parts(s, 1, P.mlp->d_shift_down, &rp);
     const int64_t* sel = nullptr;
     if (T > 1) {
       if (s->last_rows_T != T) {
@@ -497,11 +579,15 @@ int launch_select(myl_ctx* ctx, const myl_model* m, myl_session* s, cudaStream_t
   const dim3 grid = dim3(unsigned((m->V + SELECT_CHUNK - 1) / SELECT_CHUNK), unsigned(std::min<int64_t>(s->B, 65535)));
   LaunchCfg l1(ctx, grid, dim3(SELECT_THREADS), 0, st);
   CUDA_TRY(cudaLaunchKernelEx(&l1.cfg, select_keys_kernel, static_cast<const int32_t*>(s->logits),
-                              s->B, m->V, m->V, int64_t(0), s->keys));
+                              s->B, m->V, m->V, m->v0, s->keys));
+  const int64_t* keys = s->keys;
+  if (m->world > 1) {  // every rank's best key of its vocabulary rows, then the largest
+    TRY(tp_barrier(ctx, s, s->keys, s->B, st));
+    keys = s->key_slots;
+  }
   LaunchCfg l2(ctx, dim3(1), dim3(256), 0, st);
-  CUDA_TRY(cudaLaunchKernelEx(&l2.cfg, greedy_commit_kernel, static_cast<const int64_t*>(s->keys),
-                              s->B, s->next_tok, s->out_tokens, s->max_pos, s->d_step, s->d_pos,
-                              int64_t(0)));
+  CUDA_TRY(cudaLaunchKernelEx(&l2.cfg, greedy_commit_kernel, keys, s->B, s->next_tok, s->out_tokens,
+                              s->max_pos, s->d_step, s->d_pos, int64_t(0), m->world));
   ctx->launches += 3;
   return MYL_OK;
 }
@@ -553,8 +639,22 @@ int prefill(myl_ctx* ctx, const myl_model* m, myl_session* s, const int32_t* pro
 extern "C" {
 
 int myl_model_create(myl_ctx* ctx, const myl_model_spec* sp, myl_model** out) {
+  return myl_model_create_tp(ctx, sp, 1, 0, out);
+}
+
+// The share of rank r of n items split as evenly as possible (the first
+// n % world ranks take one more): [begin, end).
+static void even_share(int64_t n, int world, int rank, int64_t* b, int64_t* e) {
+  const int64_t base = n / world, extra = n % world;
+  *b = rank * base + std::min<int64_t>(rank, extra);
+  *e = *b + base + (rank < extra ? 1 : 0);
+}
+
+int myl_model_create_tp(myl_ctx* ctx, const myl_model_spec* sp, int world, int rank, myl_model** out) {
   if (!ctx || !sp || !out) return fail(MYL_ERR_ARG, "null argument");
   *out = nullptr;
+  if (world < 1 || world > MYL_XCHG_MAX || rank < 0 || rank >= world)
+    return fail(MYL_ERR_ARG, "rank %d of world %d (at most %d ranks)", rank, world, MYL_XCHG_MAX);
   if (sp->vocab <= 0 || sp->hidden <= 0 || sp->num_layers <= 0 || sp->num_heads <= 0 ||
       sp->num_kv_heads <= 0 || sp->head_dim <= 0 || sp->intermediate <= 0)
     return fail(MYL_ERR_SHAPE, "model dimensions must be positive");
@@ -580,14 +680,31 @@ int myl_model_create(myl_ctx* ctx, const myl_model_spec* sp, myl_model** out) {
   if ((int64_t(exp_max) << sp->prob_frac_bits) > INT32_MAX)
     return fail(MYL_ERR_OVERFLOW, "exp LUT values times 2^prob_frac_bits overflow i32");
   CUDA_TRY(cudaSetDevice(ctx->device));
+  if (world > 1) {
+    if (sp->num_heads < world || sp->intermediate < world || sp->vocab < world)
+      return fail(MYL_ERR_SHAPE, "%d ranks for %lld heads", world, (long long)sp->num_heads);
+    if (sp->hidden % 8 || sp->hidden > 8 * NORM_THREADS * NORM_NV)
+      return fail(MYL_ERR_UNSUPPORTED, "tensor parallelism needs hidden %% 8 == 0, <= %d",
+                  8 * NORM_THREADS * NORM_NV);
+  }
   myl_model* m = new myl_model();
-  m->V = sp->vocab;
+  m->world = world;
+  m->rank = rank;
+  m->V_global = sp->vocab;
+  m->G = sp->num_heads / sp->num_kv_heads;
+  int64_t q1, i1, v1;
+  even_share(sp->num_heads, world, rank, &m->q0, &q1);
+  even_share(sp->intermediate, world, rank, &m->i0, &i1);
+  even_share(sp->vocab, world, rank, &m->v0, &v1);
+  m->kv0 = m->q0 / m->G;  // the KV heads this rank's query heads read
+  const int64_t kv1 = (q1 - 1) / m->G + 1;
+  m->V = v1 - m->v0;
   m->H = sp->hidden;
   m->L = sp->num_layers;
-  m->nq = sp->num_heads;
-  m->nkv = sp->num_kv_heads;
+  m->nq = q1 - m->q0;
+  m->nkv = kv1 - m->kv0;
   m->hd = sp->head_dim;
-  m->I = sp->intermediate;
+  m->I = i1 - m->i0;
   m->QD = m->nq * m->hd;
   m->KD = m->nkv * m->hd;
   m->ldq = m->QD + 2 * m->KD;
@@ -617,7 +734,7 @@ int myl_model_create(myl_ctx* ctx, const myl_model_spec* sp, myl_model** out) {
   // embedding rescale (model.rs:241-248): every (row shift, channel shift) pair
   {
     bool es_seen[256] = {}, rs_seen[256] = {};
-    for (int64_t v = 0; v < m->V; ++v) es_seen[sp->embed_shifts[v]] = true;
+    for (int64_t v = 0; v < sp->vocab; ++v) es_seen[sp->embed_shifts[v]] = true;
     for (int64_t i = 0; i < m->H; ++i) rs_seen[sp->layers[0].residual_in_frac[i]] = true;
     for (int a = 0; a < 256 && rc == MYL_OK; ++a)
       for (int b = 0; b < 256 && rc == MYL_OK; ++b)
@@ -633,14 +750,17 @@ int myl_model_create(myl_ctx* ctx, const myl_model_spec* sp, myl_model** out) {
   // LM head (model.rs:284-308): path A (int16) if present, else path B (int8,
   // the embedding when tied); i32 logits at logit_frac_bits.
   if (rc == MYL_OK) {
+    const int64_t v0 = m->v0, H = m->H;
     if (sp->lm_head16) {
       if (!sp->lm_head16_shifts) rc = fail(MYL_ERR_ARG, "lm_head16 shifts");
-      else rc = myl_weight16_register(ctx, sp->lm_head16, m->V, m->H, m->H, sp->lm_head16_shifts, &m->head);
+      else rc = myl_weight16_register(ctx, sp->lm_head16 + v0 * H, m->V, H, H, sp->lm_head16_shifts + v0,
+                                      &m->head);
     } else if (sp->lm_head) {
       if (!sp->lm_head_shifts) rc = fail(MYL_ERR_ARG, "lm_head shifts");
-      else rc = myl_weight_register(ctx, sp->lm_head, m->V, m->H, m->H, sp->lm_head_shifts, &m->head);
+      else rc = myl_weight_register(ctx, sp->lm_head + v0 * H, m->V, H, H, sp->lm_head_shifts + v0,
+                                    &m->head);
     } else {
-      rc = myl_weight_register(ctx, sp->embed, m->V, m->H, m->H, sp->embed_shifts, &m->head);
+      rc = myl_weight_register(ctx, sp->embed + v0 * H, m->V, H, H, sp->embed_shifts + v0, &m->head);
     }
   }
   if (rc == MYL_OK) {
@@ -648,18 +768,19 @@ int myl_model_create(myl_ctx* ctx, const myl_model_spec* sp, myl_model** out) {
     rc = myl_requant_create(ctx, m->head, MYL_RQ_SHIFT_I32, sp->final_norm_frac, &lf, 0, nullptr,
                             nullptr, &m->rq_head);
   }
-  // embedding rows: the LM head's device rows when tied to it, else an own table
+  // embedding rows (every rank holds the whole table): the LM head's device
+  // rows when it is the embedding itself, else an own table
   if (rc == MYL_OK) {
-    if (!sp->lm_head16 && !sp->lm_head) {
+    if (!sp->lm_head16 && !sp->lm_head && world == 1) {
       m->embed_rows = m->head->d_W;
       m->lde = m->head->ldp;
     } else {
-      rc = dev_upload(m->allocs, &m->d_embed, sp->embed, size_t(m->V * m->H));
+      rc = dev_upload(m->allocs, &m->d_embed, sp->embed, size_t(sp->vocab * m->H));
       m->embed_rows = m->d_embed;
       m->lde = m->H;
     }
   }
-  if (rc == MYL_OK) rc = dev_upload(m->allocs, &m->d_embed_shifts, sp->embed_shifts, size_t(m->V));
+  if (rc == MYL_OK) rc = dev_upload(m->allocs, &m->d_embed_shifts, sp->embed_shifts, size_t(sp->vocab));
   if (rc == MYL_OK)
     rc = dev_upload(m->allocs, &m->d_rin0, sp->layers[0].residual_in_frac, size_t(m->H));
   if (rc == MYL_OK) rc = dev_upload(m->allocs, &m->d_cos, sp->cos_lut, size_t(sp->rope_len));
@@ -730,15 +851,73 @@ int myl_session_reset(myl_ctx* ctx, myl_session* s) {
 
 int64_t myl_session_position(const myl_session* s) { return s ? s->pos : -1; }
 
+// Layout of a rank's tensor-parallel region: two receive regions, key slots,
+// flag words; each part 256-byte aligned.
+static void tp_layout(const myl_session* s, size_t off[4], size_t* total) {
+  const size_t w = size_t(s->m->world);
+  auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+  const size_t recv = up(w * size_t(s->rows_cap) * size_t(s->m->H) * 8);
+  off[0] = 0;
+  off[1] = recv;
+  off[2] = 2 * recv;
+  off[3] = off[2] + up(w * size_t(s->B) * 8);
+  *total = off[3] + up(w * 8);
+}
+
+int64_t myl_session_tp_bytes(const myl_session* s) {
+  if (!s) return -1;
+  size_t off[4], total;
+  tp_layout(s, off, &total);
+  return int64_t(total);
+}
+
+int myl_session_set_tp(myl_ctx* ctx, myl_session* s, void* const* bases) {
+  if (!ctx || !s || !bases) return fail(MYL_ERR_ARG, "null argument");
+  const myl_model* m = s->m;
+  if (m->world < 2) return fail(MYL_ERR_ARG, "the session's model is not tensor-parallel");
+  for (int o = 0; o < m->world; ++o)
+    if (!bases[o]) return fail(MYL_ERR_ARG, "null region of rank %d", o);
+  size_t off[4], total;
+  tp_layout(s, off, &total);
+  CUDA_TRY(cudaSetDevice(ctx->device));
+  auto at = [&](int o, int part) { return static_cast<uint8_t*>(bases[o]) + off[part]; };
+  for (int w = 0; w < 2; ++w) {
+    s->recv[w] = reinterpret_cast<int64_t*>(at(m->rank, w));
+    for (int o = 0; o < m->world; ++o) s->peer_recv[w][o] = at(o, w);
+  }
+  s->key_slots = reinterpret_cast<int64_t*>(at(m->rank, 2));
+  for (int o = 0; o < m->world; ++o) {
+    s->peers.keys[o] = reinterpret_cast<int64_t*>(at(o, 2));
+    s->peers.flags[o] = reinterpret_cast<unsigned long long*>(at(o, 3));
+  }
+  // this rank's flag words and epoch start at zero; the caller synchronises
+  // the ranks (on the host) before the first forward
+  CUDA_TRY(cudaMemset(at(m->rank, 3), 0, size_t(m->world) * 8));
+  if (!s->d_epoch) TRY(dev_alloc(s->allocs, &s->d_epoch, 1));
+  CUDA_TRY(cudaMemset(s->d_epoch, 0, 8));
+  CUDA_TRY(cudaDeviceSynchronize());
+  s->tp_ready = true;
+  return MYL_OK;
+}
+
+int myl_model_shard(const myl_model* m, int64_t* info) {
+  if (!m || !info) return fail(MYL_ERR_ARG, "null argument");
+  const int64_t v[10] = {m->world, m->rank, m->q0, m->q0 + m->nq, m->kv0, m->kv0 + m->nkv,
+                         m->i0, m->i0 + m->I, m->v0, m->v0 + m->V};
+  std::memcpy(info, v, sizeof(v));
+  return MYL_OK;
+}
+
 int myl_forward(myl_ctx* ctx, const myl_model* m, myl_session* s, const int32_t* tokens, int64_t T,
                 int32_t* logits) {
   if (!ctx || !m || !s || s->m != m || (T > 0 && !tokens)) return fail(MYL_ERR_ARG, "null argument");
+  if (m->world > 1 && !s->tp_ready) return fail(MYL_ERR_ARG, "tensor-parallel session without myl_session_set_tp");
   if (T <= 0) return fail(MYL_ERR_SHAPE, "T = %lld", (long long)T);
   if (s->pos + T > s->max_pos)
     return fail(MYL_ERR_SHAPE, "position %lld beyond the session's %lld", (long long)(s->pos + T),
                 (long long)s->max_pos);
   for (int64_t i = 0; i < s->B * T; ++i)
-    if (tokens[i] < 0 || tokens[i] >= m->V)
+    if (tokens[i] < 0 || tokens[i] >= m->V_global)
       return fail(MYL_ERR_SHAPE, "token id %d outside the vocabulary", tokens[i]);
   CUDA_TRY(cudaSetDevice(ctx->device));
   cudaStream_t st = ctx->stream;
@@ -758,6 +937,8 @@ int myl_forward(myl_ctx* ctx, const myl_model* m, myl_session* s, const int32_t*
 static int decode_loop(myl_ctx* ctx, const myl_model* m, myl_session* s, int64_t max_new,
                        int32_t* out_tokens, uint8_t* digests, int32_t* step_logits) {
   cudaStream_t st = ctx->stream;
+  if (m->world > 1 && (digests || step_logits))
+    return fail(MYL_ERR_UNSUPPORTED, "digests and step logits need the whole vocabulary (world 1)");
   const int64_t P = s->pos;
   CUDA_TRY(cudaMemsetAsync(s->d_step, 0, 8, st));
   const bool host_steps = digests || step_logits;
@@ -833,8 +1014,9 @@ int myl_generate(myl_ctx* ctx, const myl_model* m, myl_session* s, const int32_t
   if (P + max_new > s->max_pos)
     return fail(MYL_ERR_SHAPE, "%lld positions beyond the session's %lld", (long long)(P + max_new),
                 (long long)s->max_pos);
+  if (m->world > 1 && !s->tp_ready) return fail(MYL_ERR_ARG, "tensor-parallel session without myl_session_set_tp");
   for (int64_t i = 0; i < s->B * P; ++i)
-    if (prompt[i] < 0 || prompt[i] >= m->V)
+    if (prompt[i] < 0 || prompt[i] >= m->V_global)
       return fail(MYL_ERR_SHAPE, "token id %d outside the vocabulary", prompt[i]);
   CUDA_TRY(cudaSetDevice(ctx->device));
   cudaStream_t st = ctx->stream;

@@ -405,6 +405,7 @@ static int launch_gemv(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int6
     ep.ldy = w->N;
     ep.xs_world = 0;  // slice partials stay local; the final pass exchanges
     ep.xg_world = 0;
+    ep.xb_world = 0;
     slice_stride = M * w->N;
   }
   const int8_t* dW = w->d_W;
@@ -616,6 +617,7 @@ static int launch_tc_planes(myl_ctx* ctx, const myl_weight* w, const uint8_t* xh
     ep.ldy = w->N;
     ep.xs_world = 0;  // slice partials stay local; the final pass exchanges
     ep.xg_world = 0;
+    ep.xb_world = 0;
     slice_stride = M * w->N;
   }
   TRY(launch_tc_any(ctx, w, tm_xhi, tm_xlo, M, BN, pair, work, ep, slice_stride, st));
@@ -1456,7 +1458,7 @@ struct XPlanes {
 
 static int run_mlp(myl_ctx* ctx, const myl_mlp* mlp, const int16_t* x, int64_t M, int64_t ldx,
                    int16_t* y, int64_t ldy, cudaStream_t st, int64_t* acc = nullptr,
-                   const XPlanes& xp = XPlanes()) {
+                   const XPlanes& xp = XPlanes(), const Epilogue* down_ep = nullptr) {
   if (M == 0) return MYL_OK;
   const int64_t I = mlp->I;
   Epilogue ep_gu{};
@@ -1472,6 +1474,7 @@ static int run_mlp(myl_ctx* ctx, const myl_mlp* mlp, const int16_t* x, int64_t M
   ep_down.shift = mlp->d_shift_down;
   ep_down.y = acc ? static_cast<void*>(acc) : static_cast<void*>(y);
   ep_down.ldy = acc ? mlp->H : ldy;
+  if (down_ep) ep_down = *down_ep;  // e.g. tensor-parallel partials broadcast to every rank
   CUDA_TRY(cudaSetDevice(ctx->device));
   TRY(ws_acquire(ctx, st));
   if (M <= ctx->gemv_max_m && M <= 4) {

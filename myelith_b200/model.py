@@ -199,6 +199,10 @@ def _lib():
                 ("myl_forward", [vp, vp, vp, vp, i64, vp], i32),
                 ("myl_generate", [vp, vp, vp, vp, i64, i64, vp, vp, vp], i32),
                 ("myl_decode_greedy", [vp, vp, vp, i64, vp, vp, vp], i32),
+                ("myl_model_create_tp", [vp, C.POINTER(_ModelSpecC), i32, i32, C.POINTER(vp)], i32),
+                ("myl_model_shard", [vp, C.POINTER(i64)], i32),
+                ("myl_session_tp_bytes", [vp], i64),
+                ("myl_session_set_tp", [vp, vp, C.POINTER(vp)], i32),
                 ("myl_session_timing", [vp, C.POINTER(C.c_float), C.POINTER(C.c_float)], i32),
                 ("myl_rmsnorm_i16", [vp, vp, i64, i64, vp, vp, vp, vp, i64, C.c_uint8, C.c_uint8,
                                      i64, C.c_uint8, vp], i32),
@@ -222,7 +226,7 @@ class IntegerModel:
     model.rs:229-311 forward_token, generate.rs greedy generation). Tensors are
     uploaded once; the numpy spec may be dropped afterwards."""
 
-    def __init__(self, ctx, spec: ModelSpec):
+    def __init__(self, ctx, spec: ModelSpec, world: int = 1, rank: int = 0):
         L = _lib()
         keep = []
 
@@ -266,9 +270,17 @@ class IntegerModel:
         for n, v in spec.constants.items():
             setattr(ms, n, int(v))
         h = C.c_void_p()
-        _check("myl_model_create", L.myl_model_create(ctx.handle, C.byref(ms), C.byref(h)))
+        _check("myl_model_create_tp", L.myl_model_create_tp(ctx.handle, C.byref(ms), world, rank,
+                                                            C.byref(h)))
         self._h = h
         self.ctx = ctx
+        self.world, self.rank = world, rank
+        info = (C.c_int64 * 10)()
+        _check("myl_model_shard", L.myl_model_shard(h, info))
+        # this rank's ranges: query heads, KV heads, MLP channels, vocabulary rows
+        self.shard = dict(q=(info[2], info[3]), kv=(info[4], info[5]), mlp=(info[6], info[7]),
+                          vocab=(info[8], info[9]))
+        self.vocab_local = info[9] - info[8]
         self.vocab = spec.vocab
         self.hidden = spec.hidden
         self.num_layers = spec.num_layers
@@ -340,9 +352,28 @@ class Session:
     def reset(self) -> None:
         _check("myl_session_reset", _lib().myl_session_reset(self.model.ctx.handle, self._h))
 
+    def setup_tp(self, group=None) -> None:
+        """Tensor parallelism: shares this rank's peer-memory region with the
+        other ranks of the torch.distributed group (one process per GPU) and
+        hands every rank's region to the session (myl_session_set_tp)."""
+        import torch.distributed as dist
+
+        L = _lib()
+        world, rank = self.model.world, self.model.rank
+        nbytes = int(L.myl_session_tp_bytes(self._h))
+        ptr, handle = self.model.ctx.ipc_alloc(nbytes)
+        handles = [None] * world
+        dist.all_gather_object(handles, handle, group=group)
+        self._tp_ptrs = [ptr if o == rank else self.model.ctx.ipc_open(handles[o]) for o in range(world)]
+        self._tp_own = ptr
+        bases = (C.c_void_p * world)(*self._tp_ptrs)
+        _check("myl_session_set_tp", L.myl_session_set_tp(self.model.ctx.handle, self._h, bases))
+        dist.barrier(group=group)
+
     def forward(self, tokens, want_logits: bool = True):
+        """The logits of this rank's vocabulary rows (all of them at world 1)."""
         t = np.ascontiguousarray(np.asarray(tokens, np.int32)).reshape(self.batch, -1)
-        lg = np.zeros((self.batch, self.model.vocab), np.int32) if want_logits else None
+        lg = np.zeros((self.batch, self.model.vocab_local), np.int32) if want_logits else None
         _check("myl_forward", _lib().myl_forward(
             self.model.ctx.handle, self.model.handle, self._h, t.ctypes.data, t.shape[1],
             None if lg is None else lg.ctypes.data))
@@ -370,6 +401,13 @@ class Session:
         if self._h:
             _lib().myl_session_release(self.model.ctx.handle, self._h)
             self._h = None
+        ctx = self.model.ctx
+        for o, ptr in enumerate(getattr(self, "_tp_ptrs", [])):
+            if ptr != self._tp_own:
+                ctx.ipc_close(ptr)
+        if getattr(self, "_tp_own", None):
+            ctx.ipc_free(self._tp_own)
+        self._tp_ptrs, self._tp_own = [], None
 
     def __del__(self):
         try:
