@@ -401,6 +401,91 @@ def bench_forward(ctx, cfg: dict, steps: int, warmup: int, hbm_gbs: float, check
     return out
 
 
+def bench_forward_tp(ctx, cfg: dict, steps: int, warmup: int, rank: int, world: int, max_over_ranks,
+                     check_tokens: int, check_new: int) -> dict:
+    """The integer forward tensor-parallel over the job's GPUs (one process per
+    GPU, myl_model_create_tp): every rank holds an even share of the query
+    heads (and the KV heads they read), of the MLP channels and of the LM
+    head's vocabulary rows; row-parallel partial sums go to every rank over
+    peer memory and are summed and requantised once, so tokens are
+    bit-identical to one GPU. Per batch size: prefill and decode device time
+    (max over ranks). Parity: a shortened generate (check_tokens prompt
+    tokens, check_new steps) on the same model against the CPU oracle (rank 0),
+    and sequence 0's tokens independent of the batch size."""
+    import torch
+    import torch.distributed as dist
+
+    import oracle as O
+    from myelith_b200 import model as MD
+    from myelith_b200 import synthetic as SY
+
+    t0 = time.perf_counter()
+    spec = SY.synthetic_model(cfg["variant"], seed=2)
+    gm = MD.IntegerModel(ctx, spec, world, rank)
+    build_s = time.perf_counter() - t0
+    P, N = cfg["prompt"], cfg["new"]
+    prompts = {b: SY.prompt_tokens(spec.vocab, P, seed=100 + b) for b in range(max(cfg["batch"]))}
+    cP, cN = check_tokens, check_new
+    s = gm.session(1, cP + cN)
+    s.setup_tp()
+    gtok, _, _ = gm.generate(prompts[0][:cP], cN, session=s)
+    s.release()
+    ok = 1
+    oracle_s = None
+    if rank == 0:
+        t0 = time.perf_counter()
+        om = O.OracleModel(spec, cP + cN)
+        otok, _ = om.generate(prompts[0][:cP], cN, keep_logits=False)
+        oracle_s = time.perf_counter() - t0
+        ok = int(np.array_equal(gtok[0], otok))
+        del om
+    wb = spec.weight_bytes_per_token()
+    del spec
+    out = {"workload": f"{cfg['variant']} architecture, random-init int8 weights, {P} random prompt "
+                       f"tokens then {N} greedy decode steps, tensor-parallel over {world} GPUs",
+           "parallelism": f"tp{world}: heads, MLP channels and vocabulary rows split; row-parallel "
+                          "int64 partials over peer memory",
+           "weight_bytes_per_token": int(wb), "model_build_s": round(build_s, 1),
+           "parity_check": {"sequence": 0, "prompt": cP, "new": cN, "against": "CPU oracle",
+                            "oracle_s": None if oracle_s is None else round(oracle_s, 1)},
+           "shard": gm.shard, "batches": []}
+    seq0 = None
+    for B in cfg["batch"]:
+        pr = np.stack([prompts[b] for b in range(B)])
+        sess = gm.session(B, P + N)
+        sess.setup_tp()
+        pre, dec, toks = [], [], None
+        for it in range(warmup + steps):
+            dist.barrier()
+            sess.reset()
+            sess.forward(pr, want_logits=False)
+            tk, _, _ = sess.decode(N)
+            pms, dms = sess.timing()
+            if it >= warmup:
+                pre.append(max_over_ranks(pms))
+                dec.append(max_over_ranks(dms))
+            toks = tk if toks is None else toks
+            if not np.array_equal(tk, toks):
+                ok = 0
+        if seq0 is None:
+            seq0 = toks[0].copy()
+        elif not np.array_equal(toks[0], seq0):
+            ok = 0
+        if not np.array_equal(toks[0][:cN], gtok[0]) and cP == P:
+            ok = 0
+        sess.release()
+        pms, dms = statistics.median(pre), statistics.median(dec)
+        out["batches"].append({
+            "batch": B, "prefill_tok_s": round(B * P / (pms * 1e-3), 1), "prefill_ms": round(pms, 3),
+            "decode_tok_s": round(B * N / (dms * 1e-3), 1), "decode_ms_per_step": round(dms / N, 4)})
+    t = torch.tensor([ok], dtype=torch.int32, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    out["parity"] = bool(t.item())
+    out["parity_check"]["tokens_equal"] = out["parity"]
+    gm.release()
+    return out
+
+
 def bench_moe(ctx, dev, stream, rank: int, world: int, local: int, steps: int, warmup: int,
               max_over_ranks, barrier, peer: bool = True) -> dict:
     """The MoE layer at config 4: 4096 tokens per step in total. One GPU: the
@@ -932,8 +1017,13 @@ def main() -> None:
                 "per_shape_gbs": [round(g, 1) for g in gemv_gbs],
                 "bytes": "N*K weights + 2K act + 2N out + N shift bytes per launch"}
 
-    # ---- the integer forward, configs 2 and 3 (N=1) ----
+    # ---- the integer forward, configs 2 and 3 (N=1), config 3 tensor-parallel (N>1) ----
     forward = None
+    if tp > 1 and not args.no_forward:
+        forward = {"config3": bench_forward_tp(
+            ctx, FWD_CFG3, max(1, min(args.steps, 3)), 1, rank, world, max_over_ranks,
+            int(os.environ.get("MYL_CFG3_CHECK_PROMPT", "64")),
+            int(os.environ.get("MYL_CFG3_CHECK_NEW", "16")))}
     if tp == 1 and not args.no_forward:
         fs, fw = max(1, min(args.steps, 3)), 1
         forward = {

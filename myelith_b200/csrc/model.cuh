@@ -1126,6 +1126,9 @@ int myl_attention_int(myl_ctx* ctx, const int16_t* q, int64_t q_len, const int16
     p.pos0 = dpos;
     p.nq = 1;
     p.nkv = 1;
+    p.q_head0 = 0;
+    p.kv_head0 = 0;
+    p.G = 1;
     p.hd = int(head_dim);
     p.kc.k = dk;
     p.kc.v = dv;

@@ -397,7 +397,15 @@ class Session:
         _check("myl_session_timing", _lib().myl_session_timing(self._h, C.byref(a), C.byref(b)))
         return float(a.value), float(b.value)
 
-    def release(self) -> None:
+    def release(self, _from_del: bool = False) -> None:
+        if getattr(self, "_tp_ptrs", None) and not _from_del:
+            # the other ranks' last kernels may still store into this rank's
+            # region: every rank reaches this point before any region is freed
+            import torch
+            import torch.distributed as dist
+
+            torch.cuda.synchronize()
+            dist.barrier()
         if self._h:
             _lib().myl_session_release(self.model.ctx.handle, self._h)
             self._h = None
@@ -411,7 +419,8 @@ class Session:
 
     def __del__(self):
         try:
-            self.release()
+            if not getattr(self, "_tp_ptrs", None):  # shared regions need release() on every rank
+                self.release(_from_del=True)
         except Exception:
             pass
 
