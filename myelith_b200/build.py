@@ -15,7 +15,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libmyl_w8a16.so")
 SOURCES = ["myl_w8a16.cu"]
 HEADERS = ["common.cuh", "gemv.cuh", "gemm_tc.cuh", "moe.cuh", "backward.cuh", "select.cuh",
-           "wire.cuh", "artifact.hpp", "forward.cuh", "model.cuh"]
+           "wire.cuh", "artifact.hpp", "forward.cuh", "model.cuh", "rownorm.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

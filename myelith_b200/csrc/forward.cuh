@@ -17,30 +17,9 @@
 #pragma once
 
 #include "common.cuh"
+#include "rownorm.cuh"
 
 namespace myl {
-
-// fixed_point.rs:173-180 (i32 rescale) with the host-validated signed shift
-// s = in - out in [-31, 30]; a left shift wraps as in a release build.
-__device__ __forceinline__ int32_t rescale_i32_s(int32_t v, int s) {
-  if (s > 0) return rshift_rne_i32(v, s);
-  if (s == 0) return v;
-  return int32_t(uint32_t(v) << (-s));
-}
-
-__device__ __forceinline__ int16_t clamp16(int64_t v) {
-  return int16_t(v < -32768 ? -32768 : (v > 32767 ? 32767 : v));
-}
-
-// fixed_point.rs:155-169 on i128, s in [0, 127].
-__device__ __forceinline__ __int128 rne_i128(__int128 v, int s) {
-  if (s == 0) return v;
-  const __int128 one = 1;
-  const __int128 q = v >> s;
-  const __int128 r = v & ((one << s) - 1);
-  const __int128 h = one << (s - 1);
-  return q + (((r > h) || (r == h && (q & 1))) ? 1 : 0);
-}
 
 // ---- embedding (model.rs:241-248) -------------------------------------------------
 // hidden[r][i] = clamp_i16(rescale(embed[tok][i], embed_shift[tok], rin0[i])).
@@ -66,57 +45,6 @@ __global__ void embed_kernel(const int32_t* __restrict__ tokens, int64_t rows,
     for (int64_t i = threadIdx.x; i < H; i += blockDim.x)
       out[i] = clamp16(rescale_i32_s(int32_t(row[i]), es - int(int8_t(rin0[i]))));
   }
-}
-
-// ---- residual add + RMSNorm -----------------------------------------------------
-// Residual add (model.rs:588-593, :666-671), optional:
-//   r[i] = clamp_i16(rescale_i64(rescale_i64(h[i], seg_in[i], acc[i]) + add[i], acc[i], seg_out[i]))
-//   with s1[i] = seg_in - acc and s2[i] = acc - seg_out (signed, [-63, 62]).
-// rmsnorm_i16 (rmsnorm.rs:61-153) of r with the channel shifts of seg_out:
-//   ref = max x_shift; acc = sum r_i^2 << align2[i] (i128), align2 = 2 (ref - x_shift[i]);
-//   M = (acc * inv_n) >> 20; q = least even shift with (M >> q) <= lut_len - 1;
-//   lut_val = lut[min(rne(M, q), lut_len - 1)];
-//   y_i = clamp_i16(clamp_i32(shifted(r_i * lut_val * gamma_i, norm_frac + sbase[i]))),
-//   norm_frac = lut_out + lut_in / 2 + q / 2, sbase[i] = gamma_shift[i] + x_shift[i] - ref - out.
-struct NormParams {
-  const uint8_t* align2;   // [H]
-  const int8_t* gamma;     // [H]
-  const int16_t* sbase;    // [H]
-  const int16_t* lut;
-  int32_t lut_len;
-  int32_t frac0;           // lut_output_frac + lut_input_shift / 2
-  int64_t inv_n;
-  int64_t H;
-};
-
-struct ResidParams {
-  const int16_t* add;      // [rows][ld_add], null: no residual add (plain RMSNorm)
-  int64_t ld_add;
-  const int8_t* s1;        // [H]
-  const int8_t* s2;        // [H]
-  int16_t* resid_out;      // [rows][ld_res] the new residual stream (may be the input)
-  int64_t ld_res;
-  // Tensor parallelism: the added projection output is the requant of the
-  // exact sum of nparts int64 partial slabs (parts + o * part_slab, rows of H),
-  // clamp_i16(rescale_i64(sum, part_shift[i])) (linear.rs:61-68 after the
-  // row-parallel sum); `add` is then ignored.
-  const int64_t* parts;
-  int nparts;
-  int64_t part_slab;
-  const int8_t* part_shift;
-};
-
-constexpr int NORM_THREADS = 256;
-
-__device__ __forceinline__ __int128 warp_sum_i128(__int128 v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const unsigned long long lo = (unsigned long long)(v), hi = (unsigned long long)(v >> 64);
-    const unsigned long long lo2 = __shfl_xor_sync(0xffffffffu, lo, o);
-    const unsigned long long hi2 = __shfl_xor_sync(0xffffffffu, hi, o);
-    v += (__int128)(((unsigned __int128)hi2 << 64) | (unsigned __int128)lo2);
-  }
-  return v;
 }
 
 // One block per row; x [rows][ldx]; out [rows][ldo]. out_sel (nullable): only
@@ -193,166 +121,21 @@ __global__ void __launch_bounds__(NORM_THREADS)
   }
 }
 
-// The same, for hidden sizes that are a multiple of 8 up to 8 * NORM_THREADS *
-// NORM_NV: every thread issues all loads of its 16-byte vectors (the row, the
-// added projection output, and the per-channel parameters) before using any,
-// so one row costs about one memory latency instead of one per element.
-constexpr int NORM_NV = 4;
-
-__device__ __forceinline__ int16_t lane16(const uint4& v, int e) {
-  const uint32_t w = e < 2 ? v.x : e < 4 ? v.y : e < 6 ? v.z : v.w;
-  return int16_t(uint16_t(w >> (16 * (e & 1))));
-}
-__device__ __forceinline__ int8_t lane8(const uint2& v, int e) {
-  return int8_t(uint8_t((e < 4 ? v.x : v.y) >> (8 * (e & 3))));
-}
-__device__ __forceinline__ uint4 pack16(const int16_t (&a)[8]) {
-  uint32_t w[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) w[i] = uint32_t(uint16_t(a[2 * i])) | (uint32_t(uint16_t(a[2 * i + 1])) << 16);
-  return make_uint4(w[0], w[1], w[2], w[3]);
-}
-
-// rmsnorm.rs:140-151 for one channel: the product shifted by sh, then the i32
-// and i16 clamps. Left shifts (negative sh) go through i128, out of line: they
-// are rare, and the code stays small for the single-block decode launches.
-__device__ __noinline__ int16_t norm_out_left(int64_t prod, int sh) {
-  const __int128 w = (__int128)((unsigned __int128)(__int128)prod << (-sh));
-  const int64_t t = w < (__int128)INT32_MIN ? INT32_MIN : (w > (__int128)INT32_MAX ? INT32_MAX : (int64_t)w);
-  return clamp16(t);
-}
-__device__ __forceinline__ int16_t norm_out(int64_t prod, int sh) {
-  if (sh >= 63) return 0;  // |prod| < 2^37 rounds to zero
-  if (sh > 0) return clamp16(rshift_rne_i64(prod, sh));
-  if (sh == 0) return clamp16(prod);
-  return norm_out_left(prod, sh);
-}
-
-// The root-mean-square normaliser of one row from its square sum: the LUT
-// value and norm_frac (rmsnorm.rs:99-125), or nf = -1000 for an all-zero row.
-__device__ __noinline__ void norm_scale(__int128 a, const NormParams& np, int64_t* lut_val, int* nf) {
-  if (a == 0) {
-    *nf = -1000;
-    *lut_val = 0;
-    return;
-  }
-  const __int128 m = (a * (__int128)np.inv_n) >> 20;
-  const __int128 max_idx = np.lut_len - 1;
-  int q = 0;
-  while ((m >> q) > max_idx) q += 2;
-  __int128 idx = rne_i128(m, q);
-  if (idx > max_idx) idx = max_idx;
-  *lut_val = np.lut[int64_t(idx)];
-  *nf = np.frac0 + q / 2;
-}
-
+// The residual add and RMSNorm for hidden sizes that are a multiple of 8 up
+// to 8 * NORM_THREADS * NORM_NV (block_row_norm), one block per row.
 __global__ void __launch_bounds__(NORM_THREADS)
     resid_rmsnorm_vec_kernel(const int16_t* __restrict__ x, int64_t ldx, int64_t rows, ResidParams rp,
                              NormParams np, int16_t* __restrict__ out, int64_t ldo,
                              const int64_t* __restrict__ out_rows, int64_t n_out_rows) {
   pdl_wait();
   pdl_launch();
-  __shared__ __int128 s_part[NORM_THREADS / 32];
-  __shared__ int64_t s_lut_val;
-  __shared__ int s_nf;
-  const int nv = int(np.H / 8);
+  __shared__ RowNormSmem sm;
   const int64_t nrows = out_rows ? n_out_rows : rows;
   for (int64_t rr = blockIdx.x; rr < nrows; rr += gridDim.x) {
     const int64_t r = out_rows ? out_rows[rr] : rr;
-    uint4 xv[NORM_NV], av[NORM_NV];
-    uint2 s1v[NORM_NV], s2v[NORM_NV], alv[NORM_NV];
-    // every load of this thread's vectors first
-#pragma unroll
-    for (int k = 0; k < NORM_NV; ++k) {
-      const int v = threadIdx.x + k * NORM_THREADS;
-      if (v < nv) {
-        xv[k] = *reinterpret_cast<const uint4*>(x + r * ldx + 8 * v);
-        if (rp.parts) {
-          int64_t sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-          for (int o = 0; o < rp.nparts; ++o) {
-            const longlong2* pp =
-                reinterpret_cast<const longlong2*>(rp.parts + o * rp.part_slab + r * np.H + 8 * v);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const longlong2 t2 = __ldcg(pp + q);
-              sum[2 * q] += t2.x;
-              sum[2 * q + 1] += t2.y;
-            }
-          }
-          const uint2 ps = *reinterpret_cast<const uint2*>(rp.part_shift + 8 * v);
-          int16_t a16[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) a16[e] = clamp16(rescale_i64_signed(sum[e], lane8(ps, e)));
-          av[k] = pack16(a16);
-        } else if (rp.add) {
-          av[k] = *reinterpret_cast<const uint4*>(rp.add + r * rp.ld_add + 8 * v);
-        }
-        if (rp.add || rp.parts) {
-          s1v[k] = *reinterpret_cast<const uint2*>(rp.s1 + 8 * v);
-          s2v[k] = *reinterpret_cast<const uint2*>(rp.s2 + 8 * v);
-        }
-        alv[k] = *reinterpret_cast<const uint2*>(np.align2 + 8 * v);
-      }
-    }
-    // residual add, then the square sum: squares (< 2^31) shifted by at most
-    // 20 bits are summed in int64 (8192 of them stay below 2^63), wider
-    // alignments in i128
-    int64_t acc64 = 0;
-    __int128 acc128 = 0;
-#pragma unroll
-    for (int k = 0; k < NORM_NV; ++k) {
-      const int v = threadIdx.x + k * NORM_THREADS;
-      if (v < nv) {
-        int16_t val[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          int64_t t = lane16(xv[k], e);
-          if (rp.add || rp.parts) {
-            const int64_t h = rescale_i64_signed(t, lane8(s1v[k], e)) + int64_t(lane16(av[k], e));
-            t = clamp16(rescale_i64_signed(h, lane8(s2v[k], e)));
-          }
-          val[e] = int16_t(t);
-          const int a = uint8_t(lane8(alv[k], e));
-          if (a <= 20) acc64 += (t * t) << a;
-          else acc128 += (__int128)(t * t) << a;
-        }
-        xv[k] = pack16(val);  // the row after the residual add
-        if ((rp.add || rp.parts) && rp.resid_out)
-          *reinterpret_cast<uint4*>(rp.resid_out + r * rp.ld_res + 8 * v) = xv[k];
-      }
-    }
-    __int128 acc = (__int128)acc64 + acc128;
-    acc = warp_sum_i128(acc);
-    if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = acc;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      __int128 a = 0;
-      for (int w = 0; w < NORM_THREADS / 32; ++w) a += s_part[w];
-      int64_t lv;
-      int nf;
-      norm_scale(a, np, &lv, &nf);
-      s_lut_val = lv;
-      s_nf = nf;
-    }
-    __syncthreads();
-    const int nf = s_nf;
-    const int64_t lv = s_lut_val;
-#pragma unroll
-    for (int k = 0; k < NORM_NV; ++k) {
-      const int v = threadIdx.x + k * NORM_THREADS;
-      if (v < nv) {
-        const uint2 gv = *reinterpret_cast<const uint2*>(np.gamma + 8 * v);
-        const uint4 sbv = *reinterpret_cast<const uint4*>(np.sbase + 8 * v);
-        int16_t y[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-          y[e] = nf == -1000 ? int16_t(0)
-                             : norm_out(int64_t(lane16(xv[k], e)) * lv * int64_t(lane8(gv, e)),
-                                        nf + lane16(sbv, e));
-        *reinterpret_cast<uint4*>(out + rr * ldo + 8 * v) = pack16(y);
-      }
-    }
-    __syncthreads();
+    int16_t* orow = out + rr * ldo;
+    block_row_norm(x + r * ldx, r, rp, np, true, sm,
+                   [&](int v, const uint4& y) { *reinterpret_cast<uint4*>(orow + 8 * v) = y; });
   }
 }
 

@@ -497,6 +497,7 @@ int model_forward(myl_ctx* ctx, const myl_model* m, myl_session* s, const int32_
   for (int64_t l = 0; l < m->L; ++l) {
     const ModelLayer& L = m->layers[size_t(l)];
     ResidParams rp{};
+    const int16_t* x1 = s->hid;
     if (l > 0) {
       const ModelLayer& P = m->layers[size_t(l - 1)];
       rp.add = s->mlp_out;
@@ -506,10 +507,9 @@ int model_forward(myl_ctx* ctx, const myl_model* m, myl_session* s, const int32_
       rp.resid_out = s->hid;
       rp.ld_res = H;
       if (tp) tp_parts(s, 1, P.mlp->d_shift_down, &rp);
-      TRY(launch_norm(ctx, m, s->mid, rows, rp, L.norm1, s->xn, nullptr, 0, st));
-    } else {
-      TRY(launch_norm(ctx, m, s->hid, rows, rp, L.norm1, s->xn, nullptr, 0, st));
+      x1 = s->mid;
     }
+    TRY(launch_norm(ctx, m, x1, rows, rp, L.norm1, s->xn, nullptr, 0, st));
     TRY(dispatch_linear(ctx, L.w_qkv, s->xn, rows, H, make_ep(L.rq_qkv, s->qkv, m->ldq), st));
     {
       const int64_t items = (m->nq + m->nkv) * (m->hd / 2) + m->nkv * m->hd / ((m->hd % 8) ? 1 : 8);
