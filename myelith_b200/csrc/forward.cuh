@@ -139,6 +139,65 @@ __global__ void __launch_bounds__(NORM_THREADS)
   }
 }
 
+// The same over clusters of NORM_CL CTAs, one row per cluster at a time
+// (H % 8 == 0, H <= 8 * NORM_CL * NORM_CL_THREADS). Launched with the cluster
+// dimension NORM_CL; grid.x is a multiple of NORM_CL.
+__global__ void __launch_bounds__(NORM_CL_THREADS)
+    resid_rmsnorm_cluster_kernel(const int16_t* __restrict__ x, int64_t ldx, int64_t rows, ResidParams rp,
+                                 NormParams np, int16_t* __restrict__ out, int64_t ldo,
+                                 const int64_t* __restrict__ out_rows, int64_t n_out_rows) {
+  pdl_wait();
+  pdl_launch();
+  __shared__ __int128 s_part[NORM_CL_THREADS / 32];
+  __shared__ __align__(16) unsigned long long s_cta[2];  // this CTA's square sum (lo, hi)
+  __shared__ int64_t s_lv;
+  __shared__ int s_nf;
+  const int rank = int(cluster_ctarank());
+  const int nv = int(np.H / 8);
+  const int vpc = (nv + NORM_CL - 1) / NORM_CL;  // vectors per CTA
+  const int v = rank * vpc + int(threadIdx.x);
+  const bool active = int(threadIdx.x) < vpc && v < nv;
+  const bool radd = rp.add || rp.parts;
+  const int64_t nrows = out_rows ? n_out_rows : rows;
+  for (int64_t rr = cluster_id_x(); rr < nrows; rr += cluster_count_x()) {
+    const int64_t r = out_rows ? out_rows[rr] : rr;
+    NormVec vec;
+    int64_t acc64 = 0;
+    __int128 acc128 = 0;
+    if (active) {
+      norm_vec_load(vec, x + r * ldx, r, v, rp, np);
+      norm_vec_resid(vec, radd, acc64, acc128);
+      if (radd && rp.resid_out) *reinterpret_cast<uint4*>(rp.resid_out + r * rp.ld_res + 8 * v) = vec.x;
+    }
+    const __int128 acc = warp_sum_i128((__int128)acc64 + acc128);
+    if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __int128 a = 0;
+      for (int w = 0; w < NORM_CL_THREADS / 32; ++w) a += s_part[w];
+      s_cta[0] = (unsigned long long)a;
+      s_cta[1] = (unsigned long long)(a >> 64);
+    }
+    cluster_sync_all();  // every CTA's sum is visible to the cluster
+    if (threadIdx.x == 0) {
+      const uint32_t local = static_cast<uint32_t>(__cvta_generic_to_shared(s_cta));
+      __int128 a = 0;
+      for (int k = 0; k < NORM_CL; ++k) {
+        const uint32_t remote = mapa_shared(local, uint32_t(k));
+        const unsigned long long lo = ld_shared_cluster_u64(remote), hi = ld_shared_cluster_u64(remote + 8);
+        a += (__int128)(((unsigned __int128)hi << 64) | (unsigned __int128)lo);
+      }
+      int64_t lv;
+      int nf;
+      norm_scale(a, np, &lv, &nf);
+      s_lv = lv;
+      s_nf = nf;
+    }
+    cluster_sync_all();  // the remote reads are done; s_lv and s_nf are visible in the CTA
+    if (active) *reinterpret_cast<uint4*>(out + rr * ldo + 8 * v) = norm_vec_out(vec, s_lv, s_nf);
+  }
+}
+
 // ---- RoPE + KV-cache write (model.rs:469-503, rope.rs:17-32) ----------------------
 // Row r = b * T + t is token t of sequence b at position pos = pos0 + t; it
 // uses LUT row pos % n_pos. Pair j of a head is (x_j, x_{j+half}):
@@ -211,18 +270,20 @@ __global__ void rope_kv_kernel(int16_t* __restrict__ qkv, int64_t ldq, int64_t r
 
 // ---- attention (attention.rs:42-94, model.rs:508-567) -----------------------------
 // Query row (b, t, h) attends the cache entries 0..=pos of KV head h / group.
-// Pass 1 (attn_scores_kernel): scores[row][j] = rne_i64(dot(q, k_j) * mult, shift) as i32.
+// Pass 1 (attn_scores_kernel): scores[row][j] = rne_i64(dot(q, k_j) * mult, shift) as i32,
+//   and the row maximum (softmax.rs:27) by an atomic max per warp into rowmax.
 //   The int16 x int16 dot is exact in two int32 sums: k = 256 kh + kl with kh
 //   the signed high byte and kl the unsigned low byte, so
 //   dot = 256 * sum q*kh + sum q*kl, |sum q*kh| <= hd * 2^22 and
 //   sum q*kl <= hd * 2^23 (both exact in int32 for hd <= 255); each sum is a
 //   chain of dp2a (two int16 x int8 products per instruction).
-// Pass 2 (attn_pv_kernel): softmax_int over the row (softmax.rs:24-64: max,
+// Pass 2 (attn_pv_*_kernel): softmax_int over the row (softmax.rs:24-64: max,
 //   exp LUT of the saturating difference, i32 sum, round-half-even division),
 //   then sum_j p_j * v_j in int64 over a chunk of keys; the chunks of a row are
 //   added (exact) by the last of its blocks, rounded by prob_frac and clamped
 //   (attention.rs:83-90), then rescaled from the V scale to the o_proj input
-//   scale (model.rs:563-567).
+//   scale (model.rs:563-567). The last block of a row sets its rowmax word back
+//   to the empty value for the next call.
 struct AttnParams {
   const int16_t* qkv;      // [rows][ldq]
   int64_t ldq;
@@ -238,6 +299,15 @@ struct AttnParams {
   int32_t* scores;         // [rows * nq][lds]
   int64_t lds;
   const uint8_t* mask;     // op form only: [rows][kv] bytes (0 = masked), else null
+  // row maxima [rows * nq] as max_j (score ^ 0x80000000) over unsigned words:
+  // zero (= INT32_MIN) between calls
+  unsigned* rowmax;
+  // pass 1 with the decode RoPE (T == 1): LUT rows [n_pos][hd / 2], frac bits
+  int rope;
+  const int16_t* rope_cos;
+  const int16_t* rope_sin;
+  int64_t n_pos;
+  int rope_frac;
   // pass 2
   const int16_t* exp_lut;
   int32_t exp_len;
@@ -251,10 +321,15 @@ struct AttnParams {
   int64_t ldo;
 };
 
-constexpr int ATT_KEYS = 256;     // keys per block of pass 1 (one per thread)
-constexpr int ATT_MAXG = 8;       // query rows per block of pass 1
-constexpr int ATT_CHUNK = 256;    // keys per block of pass 2
 constexpr int ATT_THREADS = 256;
+constexpr int ATT_TPK = 8;                          // pass 1: threads per key
+constexpr int ATT_SKEYS = ATT_THREADS / ATT_TPK;    // pass 1: keys per block
+constexpr int ATT_MAXG = 8;                         // pass 1: query heads per block (= ATT_TPK)
+constexpr int ATT_KCH = 4;                          // pass 1: 8-element chunks per thread (hd <= 256)
+constexpr int ATT_CHUNK = 256;                      // pass 2 (many rows): keys per piece
+constexpr int ATT_DTHREADS = 512;                   // pass 2 (decode): threads per block
+constexpr int ATT_DCHUNK = 512;                     // pass 2 (decode): keys per block
+static_assert(ATT_MAXG == ATT_TPK, "one query head per thread of a key after the reduce-scatter");
 
 __device__ __forceinline__ int dp2a_lo_ss(uint32_t a, uint32_t b, int c) {
   int d;
@@ -277,33 +352,67 @@ __device__ __forceinline__ int dp2a_hi_su(uint32_t a, uint32_t b, int c) {
   return d;
 }
 
-// grid.x: (row group) = ((b * T + t) * nkv + g) * gsub + sub; grid.y: key chunk of ATT_KEYS;
-// sub-groups of ATT_MAXG query heads of the KV head g. Dynamic shared memory:
-// key planes [ATT_KEYS][hd8 + 8] bytes x 2 (hd8 = head_dim rounded up to 8;
-// the 8-byte pad makes the per-key 8-byte reads of a half-warp hit distinct
-// banks) and queries [ATT_MAXG][hd8] int16.
 __host__ __device__ constexpr int att_hd8(int hd) { return (hd + 7) & ~7; }
-__host__ __device__ constexpr size_t att_scores_smem(int hd, int keys = ATT_KEYS) {
-  return size_t(2 * keys * (att_hd8(hd) + 8)) + size_t(ATT_MAXG * att_hd8(hd) * 2);
+// pass 1 dynamic shared memory: the queries [ATT_MAXG][hd8] and the rotated
+// new key [hd8], int16
+__host__ __device__ constexpr size_t att_scores_smem(int hd) {
+  return size_t((ATT_MAXG + 1) * att_hd8(hd) * 2);
 }
 
+// RoPE of one pair (rope.rs:17-32): (x0, x1) -> (x0 c - x1 s, x1 c + x0 s),
+// i32 wrapping, round-half-even by frac, clamped to i16.
+__device__ __forceinline__ void rope_pair(int16_t a, int16_t b, int16_t c, int16_t s, int frac, int16_t* o0,
+                                          int16_t* o1) {
+  const uint32_t x0 = uint32_t(int32_t(a)), x1 = uint32_t(int32_t(b));
+  const uint32_t cj = uint32_t(int32_t(c)), sj = uint32_t(int32_t(s));
+  *o0 = rope_out(int32_t(x0 * cj - x1 * sj), frac);
+  *o1 = rope_out(int32_t(x1 * cj + x0 * sj), frac);
+}
+
+// The int32 sums of ATT_MAXG heads over the ATT_TPK = 8 threads of a key,
+// reduce-scattered: afterwards thread `part` holds the full sum of head `part`.
+__device__ __forceinline__ int att_reduce_scatter8(const int (&a)[ATT_MAXG], int part) {
+  const bool b2 = part & 4, b1 = part & 2, b0 = part & 1;
+  int k4[4], k2[2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int keep = b2 ? a[4 + i] : a[i], send = b2 ? a[i] : a[4 + i];
+    k4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int keep = b1 ? k4[2 + i] : k4[i], send = b1 ? k4[i] : k4[2 + i];
+    k2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+  }
+  const int keep = b0 ? k2[1] : k2[0], send = b0 ? k2[0] : k2[1];
+  return keep + __shfl_xor_sync(0xffffffffu, send, 1);
+}
+
+// grid.x: (row group) = ((b * T + t) * nkv + g) * gsub + sub; grid.y: key block of
+// ATT_SKEYS keys; sub-groups of ATT_MAXG query heads of the KV head g.
+// Thread (key jj, part s) holds the 8-element chunks s, s + 8, ... of key row
+// jj in registers as two byte planes, issued before its first product; the
+// parts' int32 sums are reduce-scattered so that part s finishes head s.
+// With p.rope (decode, T == 1) the RoPE of the row's queries and new key is
+// done here (model.rs:469-503): the queries are rotated while staged, the
+// block holding key pos rotates the new key into shared memory instead of
+// reading the cache, and sub-group 0 of that block writes the key and the
+// value row to the cache at pos.
 __global__ void __launch_bounds__(ATT_THREADS) attn_scores_kernel(AttnParams p, int gsub) {
   pdl_wait();
   pdl_launch();
-  extern __shared__ __align__(16) uint8_t smem[];
-  const int hd = p.hd, hd8 = att_hd8(hd), kst = hd8 + 8, qw = hd8 / 2;
-  const int nk = blockDim.x;  // keys per block (<= ATT_KEYS)
-  uint8_t* s_kh = smem;
-  uint8_t* s_kl = s_kh + nk * kst;
-  uint32_t* s_q = reinterpret_cast<uint32_t*>(s_kl + nk * kst);  // [ATT_MAXG][hd8/2]
-  const int64_t gy = blockIdx.x;
-  const int sub = int(gy % gsub);
-  const int g = int((gy / gsub) % p.nkv);
-  const int64_t r = gy / gsub / p.nkv;  // token row b * T + t
-  const int64_t b = r / p.T, t = r % p.T;
+  extern __shared__ __align__(16) int16_t s_q16[];  // [ATT_MAXG][hd8] queries, then [hd8] new key
+  __shared__ int32_t s_mx[ATT_THREADS / 32][ATT_MAXG];
+  const int hd = p.hd, hd8 = att_hd8(hd), nc8 = hd8 / 8, half = hd / 2;
+  const int gy = int(blockIdx.x);
+  const int sub = gy % gsub;
+  const int g = (gy / gsub) % p.nkv;
+  const int r = gy / gsub / p.nkv;  // token row b * T + t
+  const int T = int(p.T);
+  const int b = r / T, t = r % T;
   const int64_t pos = p.pos0[0] + t;
   const int64_t len = p.mask ? p.lds : pos + 1;
-  const int64_t j0 = int64_t(blockIdx.y) * nk;
+  const int64_t j0 = int64_t(blockIdx.y) * ATT_SKEYS;
   if (j0 >= len) return;
   // local query heads of KV head g (GQA: global head q reads KV head q / G)
   const int hs = max(0, (p.kv_head0 + g) * p.G - p.q_head0);
@@ -311,79 +420,125 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_scores_kernel(AttnParams p, 
   const int h0 = hs + sub * ATT_MAXG;
   const int nrow = min(ATT_MAXG, he - h0);
   if (nrow <= 0) return;
-  // queries of the sub-group as int16 pairs, zero-padded to hd8
-  for (int e = threadIdx.x; e < ATT_MAXG * qw; e += nk) {
-    const int rr = e / qw, w = e % qw;
-    uint32_t v = 0;
-    if (rr < nrow) {
-      const int16_t* q = p.qkv + r * p.ldq + int64_t(h0 + rr) * hd;
-      const int d = 2 * w;
-      const uint32_t lo = d < hd ? uint16_t(q[d]) : 0u, hi = d + 1 < hd ? uint16_t(q[d + 1]) : 0u;
-      v = lo | (hi << 16);
-    }
-    s_q[e] = v;
-  }
-  // key rows j0.. as two byte planes (high byte signed, low byte unsigned),
-  // 8 elements per step: one 16-byte load, two byte permutes, two 8-byte stores
-  const int16_t* kbase = p.kc.k + b * p.kc.seq_stride + int64_t(p.layer) * p.kc.layer_stride +
-                         int64_t(g) * p.kc.head_stride;
-  const int nkeys = int(min(int64_t(nk), len - j0));
+  const int jj = int(threadIdx.x) / ATT_TPK, part = int(threadIdx.x) % ATT_TPK;
+  const int64_t j = j0 + jj;
+  const bool live = j < len;
+  const bool newkey = p.rope && j == pos;  // rotated in shared memory below
+  const int64_t cache_off = int64_t(b) * p.kc.seq_stride + int64_t(p.layer) * p.kc.layer_stride +
+                            int64_t(g) * p.kc.head_stride;
+  const int16_t* kr = p.kc.k + cache_off + (live ? j : j0) * hd;
   const bool vec = (hd & 7) == 0;
-  for (int e = threadIdx.x; e < nk * (hd8 / 8); e += nk) {
-    const int jj = e / (hd8 / 8), d = 8 * (e % (hd8 / 8));
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (jj < nkeys) {
-      const int16_t* kr = kbase + (j0 + jj) * hd + d;
+  uint4 kv[ATT_KCH];
+#pragma unroll
+  for (int i = 0; i < ATT_KCH; ++i) {
+    const int w8 = part + ATT_TPK * i;
+    kv[i] = make_uint4(0u, 0u, 0u, 0u);
+    if (live && !newkey && w8 < nc8) {
       if (vec) {
-        v = *reinterpret_cast<const uint4*>(kr);
+        kv[i] = *reinterpret_cast<const uint4*>(kr + 8 * w8);
       } else {
         uint32_t w[4] = {0u, 0u, 0u, 0u};
-        for (int i = 0; i < 8 && d + i < hd; ++i) w[i / 2] |= uint32_t(uint16_t(kr[i])) << (16 * (i & 1));
-        v = make_uint4(w[0], w[1], w[2], w[3]);
+        for (int e = 0; e < 8 && 8 * w8 + e < hd; ++e)
+          w[e / 2] |= uint32_t(uint16_t(kr[8 * w8 + e])) << (16 * (e & 1));
+        kv[i] = make_uint4(w[0], w[1], w[2], w[3]);
       }
     }
-    *reinterpret_cast<uint2*>(s_kh + jj * kst + d) =
-        make_uint2(__byte_perm(v.x, v.y, 0x7531), __byte_perm(v.z, v.w, 0x7531));
-    *reinterpret_cast<uint2*>(s_kl + jj * kst + d) =
-        make_uint2(__byte_perm(v.x, v.y, 0x6420), __byte_perm(v.z, v.w, 0x6420));
+  }
+  // queries of the sub-group (rotated with p.rope), zero-padded to hd8
+  const int16_t* qrow = p.qkv + int64_t(r) * p.ldq;
+  int16_t* s_k16 = s_q16 + ATT_MAXG * hd8;
+  if (p.rope) {
+    const int64_t lrow = (pos % p.n_pos) * half;
+    for (int e = threadIdx.x; e < nrow * half; e += ATT_THREADS) {
+      const int rr = e / half, d = e % half;
+      const int16_t* q = qrow + int64_t(h0 + rr) * hd;
+      rope_pair(q[d], q[d + half], p.rope_cos[lrow + d], p.rope_sin[lrow + d], p.rope_frac,
+                s_q16 + rr * hd8 + d, s_q16 + rr * hd8 + d + half);
+    }
+    if (j0 <= pos && pos < j0 + ATT_SKEYS) {
+      // the new key of KV head g, and (sub-group 0) key and value to the cache
+      const int16_t* k = qrow + int64_t(p.nq + g) * hd;
+      int16_t* kc = p.kc.k + cache_off + pos * hd;
+      for (int d = threadIdx.x; d < half; d += ATT_THREADS) {
+        int16_t o0, o1;
+        rope_pair(k[d], k[d + half], p.rope_cos[lrow + d], p.rope_sin[lrow + d], p.rope_frac, &o0, &o1);
+        s_k16[d] = o0;
+        s_k16[d + half] = o1;
+        if (sub == 0) {
+          kc[d] = o0;
+          kc[d + half] = o1;
+        }
+      }
+      for (int d = hd + threadIdx.x; d < hd8; d += ATT_THREADS) s_k16[d] = 0;
+      if (sub == 0) {
+        const int16_t* v = qrow + int64_t(p.nq + p.nkv + g) * hd;
+        int16_t* vc = p.kc.v + cache_off + pos * hd;
+        for (int d = threadIdx.x; d < hd; d += ATT_THREADS) vc[d] = v[d];
+      }
+    }
+    for (int e = threadIdx.x; e < nrow * (hd8 - hd); e += ATT_THREADS)
+      s_q16[(e / (hd8 - hd)) * hd8 + hd + e % (hd8 - hd)] = 0;
+  } else {
+    for (int e = threadIdx.x; e < nrow * hd8; e += ATT_THREADS) {
+      const int rr = e / hd8, d = e % hd8;
+      s_q16[rr * hd8 + d] = d < hd ? qrow[int64_t(h0 + rr) * hd + d] : int16_t(0);
+    }
   }
   __syncthreads();
-  const int jj = threadIdx.x;
-  if (jj >= nkeys) return;
+  if (newkey) {
+#pragma unroll
+    for (int i = 0; i < ATT_KCH; ++i) {
+      const int w8 = part + ATT_TPK * i;
+      if (w8 < nc8) kv[i] = *reinterpret_cast<const uint4*>(s_k16 + 8 * w8);
+    }
+  }
+  const uint32_t* s_q = reinterpret_cast<const uint32_t*>(s_q16);
+  const int qw = hd8 / 2;
   int acc_h[ATT_MAXG], acc_l[ATT_MAXG];
 #pragma unroll
   for (int i = 0; i < ATT_MAXG; ++i) acc_h[i] = acc_l[i] = 0;
-  const uint2* kh8 = reinterpret_cast<const uint2*>(s_kh + jj * kst);
-  const uint2* kl8 = reinterpret_cast<const uint2*>(s_kl + jj * kst);
-  for (int w8 = 0; w8 < hd8 / 8; ++w8) {
-    const uint2 kh = kh8[w8], kl = kl8[w8];
 #pragma unroll
-    for (int i = 0; i < ATT_MAXG; ++i) {
-      if (i < nrow) {
-        const uint4 q = *reinterpret_cast<const uint4*>(s_q + i * qw + 4 * w8);
-        acc_h[i] = dp2a_hi_ss(q.y, kh.x, dp2a_lo_ss(q.x, kh.x, acc_h[i]));
-        acc_h[i] = dp2a_hi_ss(q.w, kh.y, dp2a_lo_ss(q.z, kh.y, acc_h[i]));
-        acc_l[i] = dp2a_hi_su(q.y, kl.x, dp2a_lo_su(q.x, kl.x, acc_l[i]));
-        acc_l[i] = dp2a_hi_su(q.w, kl.y, dp2a_lo_su(q.z, kl.y, acc_l[i]));
+  for (int i = 0; i < ATT_KCH; ++i) {
+    const int w8 = part + ATT_TPK * i;
+    if (w8 < nc8) {
+      const uint32_t khx = __byte_perm(kv[i].x, kv[i].y, 0x7531), khy = __byte_perm(kv[i].z, kv[i].w, 0x7531);
+      const uint32_t klx = __byte_perm(kv[i].x, kv[i].y, 0x6420), kly = __byte_perm(kv[i].z, kv[i].w, 0x6420);
+#pragma unroll
+      for (int h = 0; h < ATT_MAXG; ++h) {
+        if (h < nrow) {
+          const uint4 q = *reinterpret_cast<const uint4*>(s_q + h * qw + 4 * w8);
+          acc_h[h] = dp2a_hi_ss(q.y, khx, dp2a_lo_ss(q.x, khx, acc_h[h]));
+          acc_h[h] = dp2a_hi_ss(q.w, khy, dp2a_lo_ss(q.z, khy, acc_h[h]));
+          acc_l[h] = dp2a_hi_su(q.y, klx, dp2a_lo_su(q.x, klx, acc_l[h]));
+          acc_l[h] = dp2a_hi_su(q.w, kly, dp2a_lo_su(q.z, kly, acc_l[h]));
+        }
       }
     }
   }
-  const int64_t j = j0 + jj;
+  const int ah = att_reduce_scatter8(acc_h, part), al = att_reduce_scatter8(acc_l, part);
+  // this thread: head h0 + part of key j
+  int32_t sc = INT32_MIN;
+  const bool mine = live && part < nrow;
+  const int64_t row = int64_t(r) * p.nq + h0 + part;
+  if (mine && !(p.mask && !p.mask[int64_t(r) * p.lds + j])) {
+    const int64_t dot = int64_t(ah) * 256 + int64_t(al);
+    const uint64_t prod = uint64_t(dot) * uint64_t(p.score_mult);  // i64 (wrapping)
+    const int64_t s = p.score_shift > 0 ? rshift_rne_i64(int64_t(prod), p.score_shift) : int64_t(prod);
+    sc = int32_t(uint32_t(uint64_t(s)));  // `as i32`
+  }
+  if (mine) p.scores[row * p.lds + j] = sc;
+  // the block's maximum per head, one atomic per head and block
+  int32_t mx = sc;
 #pragma unroll
-  for (int i = 0; i < ATT_MAXG; ++i) {
-    if (i < nrow) {
-      const int64_t row = r * p.nq + h0 + i;
-      int32_t sc;
-      if (p.mask && !p.mask[r * p.lds + j]) {
-        sc = INT32_MIN;
-      } else {
-        const int64_t dot = int64_t(acc_h[i]) * 256 + int64_t(acc_l[i]);
-        const uint64_t prod = uint64_t(dot) * uint64_t(p.score_mult);  // i64 (wrapping)
-        const int64_t s = p.score_shift > 0 ? rshift_rne_i64(int64_t(prod), p.score_shift) : int64_t(prod);
-        sc = int32_t(uint32_t(uint64_t(s)));  // `as i32`
-      }
-      p.scores[row * p.lds + j] = sc;
-    }
+  for (int o = ATT_TPK; o < 32; o <<= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane < ATT_TPK) s_mx[warp][lane] = mx;
+  __syncthreads();
+  if (int(threadIdx.x) < nrow) {
+    int32_t m = s_mx[0][threadIdx.x];
+#pragma unroll
+    for (int w = 1; w < ATT_THREADS / 32; ++w) m = max(m, s_mx[w][threadIdx.x]);
+    atomicMax(p.rowmax + int64_t(r) * p.nq + h0 + threadIdx.x, uint32_t(m) ^ 0x80000000u);
   }
 }
 
@@ -395,8 +550,112 @@ __device__ __forceinline__ int32_t exp_lookup(int32_t x, const int16_t* lut, int
   return lut[idx];
 }
 
+// exp LUT entry of the saturating difference max - s (softmax.rs:33-38)
+// (m >= s: m is the row maximum, so the u32 difference is exact)
+__device__ __forceinline__ int32_t exp_of(int32_t m, int32_t s, const AttnParams& p, int32_t lut_one) {
+  const uint32_t d = min(uint32_t(m) - uint32_t(s), uint32_t(INT32_MAX));
+  return exp_lookup(int32_t(d), p.exp_lut, p.exp_len, p.lut_shift, lut_one);
+}
+
+// softmax.rs:41-62: the probability of exponential e in a row of `len` keys
+// with exponential sum S (key index j for the uniform row of an all-zero sum).
+__device__ __forceinline__ int32_t softmax_prob(int32_t e, int32_t S, int64_t j, int64_t len, int32_t one) {
+  if (S == 0) {
+    const int32_t base = one / int32_t(len), rem = one - base * int32_t(len);
+    return base + (j < rem ? 1 : 0);
+  }
+  const int32_t num = e * one;
+  int32_t q = num / S;
+  const int32_t rm = num % S;
+  const int32_t twice = (rm < 0 ? -rm : rm) * 2, den = S < 0 ? -S : S;
+  if (twice > den || (twice == den && (q & 1))) q = ((num > 0) == (S > 0)) ? q + 1 : q - 1;
+  return q;
+}
+
+// The sum of the exponentials of a row of `len` scores with maximum m, loads
+// issued eight deep; the exponentials of keys [e0, e0 + ne) also go to s_e.
+// Ends with the block synchronised (s_e complete). NT: threads of the block.
+template <int NT>
+__device__ __forceinline__ int32_t attn_row_sum(const int32_t* __restrict__ sc, int64_t len, int32_t m,
+                                                const AttnParams& p, int32_t lut_one, int64_t* s_red,
+                                                int32_t* s_e, int64_t e0, int ne) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int n = int(len);  // rows are shorter than 2^31 keys
+  const int f0 = int(e0);
+  int64_t s = 0;
+  for (int j = threadIdx.x; j < n; j += 8 * NT) {
+    int32_t v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int jj = j + u * NT;
+      v[u] = jj < n ? sc[jj] : m;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int jj = j + u * NT;
+      if (jj < n) {
+        const int32_t e = exp_of(m, v[u], p, lut_one);
+        s += e;
+        if (unsigned(jj - f0) < unsigned(ne)) s_e[jj - f0] = e;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) s_red[warp] = s;
+  __syncthreads();
+  s = 0;
+#pragma unroll
+  for (int w = 0; w < NT / 32; ++w) s += s_red[w];
+  return int32_t(s);  // i32 in the reference; the host bounds len so that it cannot overflow
+}
+
+// The chunk combination of pass 2: block c of a row with nch chunks holds
+// `tot` (column d < hd). With one chunk it is the row's sum; otherwise the
+// partials go to p.part and the last block of the row adds them. That block
+// writes the output columns and resets the row's counter and rowmax words.
+__device__ __forceinline__ void attn_finish(const AttnParams& p, int64_t row, int64_t c, int64_t nch,
+                                            int64_t tot, bool* s_last) {
+  const int hd = p.hd;
+  const int d = threadIdx.x;
+  int64_t* part = p.part + (row * p.max_chunks) * hd;
+  if (nch > 1) {
+    if (d < hd) part[c * hd + d] = tot;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const unsigned prev = atomicAdd(p.counters + row, 1u);
+      *s_last = (prev + 1 == unsigned(nch));
+    }
+    __syncthreads();
+    if (!*s_last) return;
+    __threadfence();
+    if (d < hd) {
+      int64_t a[4] = {0, 0, 0, 0};
+      int64_t cc = 0;
+      for (; cc + 4 <= nch; cc += 4) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) a[u] += __ldcg(part + (cc + u) * hd + d);
+      }
+      for (; cc < nch; ++cc) a[0] += __ldcg(part + cc * hd + d);
+      tot = a[0] + a[1] + a[2] + a[3];
+    }
+  }
+  const int64_t r = row / p.nq;
+  const int h = int(row % p.nq);
+  if (d < hd) {
+    int32_t o = clamp16(p.prob_frac > 0 ? rshift_rne_i64(tot, p.prob_frac) : tot);
+    if (p.out_shift != 0) o = clamp16(rescale_i32_s(o, p.out_shift));
+    p.out[r * p.ldo + int64_t(h) * hd + d] = int16_t(o);
+  }
+  if (threadIdx.x == 0) {
+    if (nch > 1) p.counters[row] = 0;
+    p.rowmax[row] = 0u;
+  }
+}
+
 // grid.x: query row (b * T + t) * nq + h; grid.y: key chunk of `chunk` keys
-// (a multiple of ATT_CHUNK; one chunk per row when rows are plentiful).
+// (a multiple of ATT_CHUNK). Any head_dim <= 254.
 __global__ void __launch_bounds__(ATT_THREADS) attn_pv_kernel(AttnParams p, int64_t chunk) {
   pdl_wait();
   pdl_launch();
@@ -415,31 +674,9 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_pv_kernel(AttnParams p, int6
   if (c >= nch) return;
   const int32_t* sc = p.scores + row * p.lds;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  // max over the row
-  int32_t m = INT32_MIN;
-  for (int64_t j = threadIdx.x; j < len; j += ATT_THREADS) m = max(m, sc[j]);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if (lane == 0) s_red[warp] = m;
-  __syncthreads();
-  m = int32_t(s_red[0]);
-  for (int w = 1; w < ATT_THREADS / 32; ++w) m = max(m, int32_t(s_red[w]));
-  __syncthreads();
+  const int32_t m = int32_t(p.rowmax[row] ^ 0x80000000u);
   const int32_t lut_one = p.exp_lut[0];
-  // sum of the exponentials (i32 in the reference; the host bounds the row
-  // length so that it cannot overflow)
-  int64_t s = 0;
-  for (int64_t j = threadIdx.x; j < len; j += ATT_THREADS) {
-    const int64_t d = int64_t(m) - int64_t(sc[j]);
-    s += exp_lookup(d > INT32_MAX ? INT32_MAX : int32_t(d), p.exp_lut, p.exp_len, p.lut_shift, lut_one);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  if (lane == 0) s_red[warp] = s;
-  __syncthreads();
-  s = 0;
-  for (int w = 0; w < ATT_THREADS / 32; ++w) s += s_red[w];
-  const int32_t S = int32_t(s);
+  const int32_t S = attn_row_sum<ATT_THREADS>(sc, len, m, p, lut_one, s_red, s_p, 0, 0);
   const int32_t one = int32_t(1) << p.prob_frac;
   const int hd = p.hd;
   const int16_t* vbase = p.kc.v + b * p.kc.seq_stride + int64_t(p.layer) * p.kc.layer_stride +
@@ -451,25 +688,9 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_pv_kernel(AttnParams p, int6
   for (int64_t jc0 = c * chunk; jc0 < jend; jc0 += ATT_CHUNK) {
     const int nj = int(min(int64_t(ATT_CHUNK), jend - jc0));
     __syncthreads();  // s_p of the previous piece is consumed
-    // probabilities of this piece (softmax.rs:41-62)
     if (threadIdx.x < nj) {
       const int64_t j = jc0 + threadIdx.x;
-      int32_t pj;
-      if (S == 0) {
-        const int32_t base = one / int32_t(len), rem = one - base * int32_t(len);
-        pj = base + (j < rem ? 1 : 0);
-      } else {
-        const int64_t d = int64_t(m) - int64_t(sc[j]);
-        const int32_t e = exp_lookup(d > INT32_MAX ? INT32_MAX : int32_t(d), p.exp_lut, p.exp_len,
-                                     p.lut_shift, lut_one);
-        const int32_t num = e * one;
-        int32_t q = num / S;
-        const int32_t rm = num % S;
-        const int32_t twice = (rm < 0 ? -rm : rm) * 2, den = S < 0 ? -S : S;
-        if (twice > den || (twice == den && (q & 1))) q = ((num > 0) == (S > 0)) ? q + 1 : q - 1;
-        pj = q;
-      }
-      s_p[threadIdx.x] = pj;
+      s_p[threadIdx.x] = softmax_prob(exp_of(m, sc[j], p, lut_one), S, j, len, one);
     }
     __syncthreads();
     // sum_j p_j v_j[d]: warp w takes keys w, w + 8, ...; lane takes d = lane, lane + 32, ...
@@ -490,95 +711,15 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_pv_kernel(AttnParams p, int6
     if (d < hd) s_acc[warp * hd + d] = acc[i];
   }
   __syncthreads();
-  int64_t* part = p.part + (row * p.max_chunks) * hd;
-  for (int d = threadIdx.x; d < hd; d += ATT_THREADS) {
-    int64_t v = 0;
-    for (int w = 0; w < ATT_THREADS / 32; ++w) v += s_acc[w * hd + d];
-    s_acc[d] = v;  // thread d alone reads column d of every warp, then writes slot d
-    if (nch > 1) part[c * hd + d] = v;
-  }
-  if (nch > 1) {
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      const unsigned prev = atomicAdd(p.counters + row, 1u);
-      s_last = (prev + 1 == unsigned(nch));
-    }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-  } else {
-    __syncthreads();
-  }
-  int16_t* out = p.out + r * p.ldo + int64_t(h) * hd;
-  for (int d = threadIdx.x; d < hd; d += ATT_THREADS) {
-    int64_t v;
-    if (nch > 1) {
-      v = 0;
-      for (int64_t cc = 0; cc < nch; ++cc) v += __ldcg(part + cc * hd + d);
-    } else {
-      v = s_acc[d];
-    }
-    int32_t o = clamp16(p.prob_frac > 0 ? rshift_rne_i64(v, p.prob_frac) : v);
-    if (p.out_shift != 0) o = clamp16(rescale_i32_s(o, p.out_shift));
-    out[d] = int16_t(o);
-  }
-  if (nch > 1 && threadIdx.x == 0) p.counters[row] = 0;
+  int64_t tot = 0;
+  if (threadIdx.x < hd)
+    for (int w = 0; w < ATT_THREADS / 32; ++w) tot += s_acc[w * hd + threadIdx.x];
+  attn_finish(p, row, c, nch, tot, &s_last);
 }
 
-// The softmax of one attention row (softmax.rs:24-64): its maximum and the
-// sum of the exponentials, loads unrolled four deep.
-__device__ __forceinline__ void attn_row_stats(const int32_t* __restrict__ sc, int64_t len,
-                                               const AttnParams& p, int32_t lut_one, int64_t* s_red,
-                                               int32_t* m_out, int32_t* S_out) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int32_t m = INT32_MIN;
-  for (int64_t j = threadIdx.x; j < len; j += 4 * ATT_THREADS) {
-    int32_t v[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int64_t jj = j + u * ATT_THREADS;
-      v[u] = jj < len ? sc[jj] : INT32_MIN;
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) m = max(m, v[u]);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if (lane == 0) s_red[warp] = m;
-  __syncthreads();
-  m = int32_t(s_red[0]);
-  for (int w = 1; w < ATT_THREADS / 32; ++w) m = max(m, int32_t(s_red[w]));
-  __syncthreads();
-  int64_t s = 0;
-  for (int64_t j = threadIdx.x; j < len; j += 4 * ATT_THREADS) {
-    int32_t v[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int64_t jj = j + u * ATT_THREADS;
-      v[u] = jj < len ? sc[jj] : m;
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      if (j + u * ATT_THREADS < len) {
-        const int64_t d = int64_t(m) - int64_t(v[u]);
-        s += exp_lookup(d > INT32_MAX ? INT32_MAX : int32_t(d), p.exp_lut, p.exp_len, p.lut_shift, lut_one);
-      }
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  if (lane == 0) s_red[warp] = s;
-  __syncthreads();
-  s = 0;
-  for (int w = 0; w < ATT_THREADS / 32; ++w) s += s_red[w];
-  *m_out = m;
-  *S_out = int32_t(s);
-}
-
-// Pass 2 for head_dim a multiple of 8 (<= 256): hd / 8 threads per value row,
-// each a 16-byte vector, ATT_THREADS * 8 / hd rows in flight per step and four
-// steps unrolled; the rows' int64 partial sums meet in shared memory.
+// Pass 2 for head_dim a multiple of 8 (<= 256), many rows: hd / 8 threads per
+// value row, each a 16-byte vector, ATT_THREADS * 8 / hd rows in flight per
+// step and four steps unrolled; the rows' int64 partial sums meet in shared memory.
 __global__ void __launch_bounds__(ATT_THREADS) attn_pv_vec_kernel(AttnParams p, int64_t chunk) {
   pdl_wait();
   pdl_launch();
@@ -596,9 +737,12 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_pv_vec_kernel(AttnParams p, 
   const int64_t c = blockIdx.y;
   if (c >= nch) return;
   const int32_t* sc = p.scores + row * p.lds;
+  const int32_t m = int32_t(p.rowmax[row] ^ 0x80000000u);
   const int32_t lut_one = p.exp_lut[0];
-  int32_t m, S;
-  attn_row_stats(sc, len, p, lut_one, s_red, &m, &S);
+  const int64_t jfirst = c * chunk;
+  const int nfirst = int(min(int64_t(ATT_CHUNK), len - jfirst));
+  // the first piece's exponentials come with the sum
+  const int32_t S = attn_row_sum<ATT_THREADS>(sc, len, m, p, lut_one, s_red, s_p, jfirst, nfirst);
   const int32_t one = int32_t(1) << p.prob_frac;
   const int hd = p.hd, tpk = hd / 8, kpi = ATT_THREADS / tpk;
   const int kg = threadIdx.x / tpk, dv = threadIdx.x % tpk;
@@ -608,27 +752,13 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_pv_vec_kernel(AttnParams p, 
 #pragma unroll
   for (int e = 0; e < 8; ++e) acc[e] = 0;
   const int64_t jend = min(len, (c + 1) * chunk);
-  for (int64_t jc0 = c * chunk; jc0 < jend; jc0 += ATT_CHUNK) {
+  for (int64_t jc0 = jfirst; jc0 < jend; jc0 += ATT_CHUNK) {
     const int nj = int(min(int64_t(ATT_CHUNK), jend - jc0));
-    __syncthreads();  // s_p of the previous piece is consumed
+    if (jc0 != jfirst) __syncthreads();  // s_p of the previous piece is consumed
     if (threadIdx.x < nj) {
       const int64_t j = jc0 + threadIdx.x;
-      int32_t pj;
-      if (S == 0) {
-        const int32_t base = one / int32_t(len), rem = one - base * int32_t(len);
-        pj = base + (j < rem ? 1 : 0);
-      } else {
-        const int64_t d = int64_t(m) - int64_t(sc[j]);
-        const int32_t e = exp_lookup(d > INT32_MAX ? INT32_MAX : int32_t(d), p.exp_lut, p.exp_len,
-                                     p.lut_shift, lut_one);
-        const int32_t num = e * one;
-        int32_t q = num / S;
-        const int32_t rm = num % S;
-        const int32_t twice = (rm < 0 ? -rm : rm) * 2, den = S < 0 ? -S : S;
-        if (twice > den || (twice == den && (q & 1))) q = ((num > 0) == (S > 0)) ? q + 1 : q - 1;
-        pj = q;
-      }
-      s_p[threadIdx.x] = pj;
+      const int32_t e = jc0 == jfirst ? s_p[threadIdx.x] : exp_of(m, sc[j], p, lut_one);
+      s_p[threadIdx.x] = softmax_prob(e, S, j, len, one);
     }
     __syncthreads();
     for (int jj = kg; jj < nj; jj += 4 * kpi) {
@@ -651,34 +781,72 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_pv_vec_kernel(AttnParams p, 
 #pragma unroll
   for (int e = 0; e < 8; ++e) s_acc[kg * hd + 8 * dv + e] = acc[e];
   __syncthreads();
-  int64_t* part = p.part + (row * p.max_chunks) * hd;
   int64_t tot = 0;
-  const int d = threadIdx.x;
-  if (d < hd) {
-    for (int g = 0; g < kpi; ++g) tot += s_acc[g * hd + d];
-    if (nch > 1) part[c * hd + d] = tot;
+  if (threadIdx.x < hd)
+    for (int g = 0; g < kpi; ++g) tot += s_acc[g * hd + threadIdx.x];
+  attn_finish(p, row, c, nch, tot, &s_last);
+}
+
+// Pass 2 for few rows (decode): ATT_DTHREADS threads, chunks of ATT_DCHUNK
+// keys, head_dim a multiple of 8 and at most 128 (so that the
+// ATT_DTHREADS / (hd / 8) >= 32 value-row groups cover a chunk in at most 16
+// rows each). The chunk's value rows are loaded before the softmax
+// statistics, which need the row maximum from pass 1 and one pass over the
+// row's scores.
+__global__ void __launch_bounds__(ATT_DTHREADS) attn_pv_dec_kernel(AttnParams p) {
+  pdl_wait();
+  pdl_launch();
+  constexpr int VR = ATT_DCHUNK / 32;  // value rows per thread (at most)
+  __shared__ __align__(16) int64_t s_acc[ATT_DTHREADS * 8];  // [value-row groups][hd]
+  __shared__ int64_t s_red[ATT_DTHREADS / 32];
+  __shared__ int32_t s_e[ATT_DCHUNK];
+  __shared__ bool s_last;
+  const int row = int(blockIdx.x);
+  const int r = row / p.nq, h = row % p.nq;
+  const int T = int(p.T);
+  const int b = r / T, t = r % T;
+  const int64_t pos = p.pos0[0] + t;
+  const int len = int(p.mask ? p.lds : pos + 1);
+  const int nch = (len + ATT_DCHUNK - 1) / ATT_DCHUNK;
+  const int c = int(blockIdx.y);
+  if (c >= nch) return;
+  const int jc0 = c * ATT_DCHUNK;
+  const int nj = min(ATT_DCHUNK, len - jc0);
+  const int hd = p.hd, tpk = hd / 8, kpi = ATT_DTHREADS / tpk;
+  const int kg = int(threadIdx.x) / tpk, dv = int(threadIdx.x) % tpk;
+  const int16_t* vbase = p.kc.v + int64_t(b) * p.kc.seq_stride + int64_t(p.layer) * p.kc.layer_stride +
+                         int64_t((p.q_head0 + h) / p.G - p.kv_head0) * p.kc.head_stride +
+                         int64_t(jc0) * hd + 8 * dv;
+  uint4 vv[VR];
+#pragma unroll
+  for (int u = 0; u < VR; ++u) {
+    const int jj = kg + u * kpi;
+    vv[u] = jj < nj ? *reinterpret_cast<const uint4*>(vbase + int64_t(jj) * hd) : make_uint4(0u, 0u, 0u, 0u);
   }
-  if (nch > 1) {
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      const unsigned prev = atomicAdd(p.counters + row, 1u);
-      s_last = (prev + 1 == unsigned(nch));
-    }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    if (d < hd) {
-      tot = 0;
-      for (int64_t cc = 0; cc < nch; ++cc) tot += __ldcg(part + cc * hd + d);
-    }
+  const int32_t* sc = p.scores + int64_t(row) * p.lds;
+  const int32_t m = int32_t(p.rowmax[row] ^ 0x80000000u);
+  const int32_t lut_one = p.exp_lut[0];
+  const int32_t S = attn_row_sum<ATT_DTHREADS>(sc, len, m, p, lut_one, s_red, s_e, jc0, nj);
+  const int32_t one = int32_t(1) << p.prob_frac;
+  if (int(threadIdx.x) < nj) s_e[threadIdx.x] = softmax_prob(s_e[threadIdx.x], S, jc0 + threadIdx.x, len, one);
+  __syncthreads();
+  int64_t acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0;
+#pragma unroll
+  for (int u = 0; u < VR; ++u) {
+    const int jj = kg + u * kpi;
+    const int32_t pj = jj < nj ? s_e[jj] : 0;  // p = 0 adds nothing (attention.rs:79)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] += int64_t(pj) * int64_t(lane16(vv[u], e));
   }
-  if (d < hd) {
-    int32_t o = clamp16(p.prob_frac > 0 ? rshift_rne_i64(tot, p.prob_frac) : tot);
-    if (p.out_shift != 0) o = clamp16(rescale_i32_s(o, p.out_shift));
-    p.out[r * p.ldo + int64_t(h) * hd + d] = int16_t(o);
-  }
-  if (nch > 1 && threadIdx.x == 0) p.counters[row] = 0;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) s_acc[kg * hd + 8 * dv + e] = acc[e];
+  __syncthreads();
+  int64_t tot = 0;
+  if (int(threadIdx.x) < hd)
+    for (int g = 0; g < kpi; ++g) tot += s_acc[g * hd + threadIdx.x];
+  attn_finish(p, row, c, nch, tot, &s_last);
 }
 
 // ---- tensor-parallel barrier ----------------------------------------------------

@@ -26,11 +26,21 @@
 
 namespace myl {
 
-__device__ __forceinline__ int4 ldg_stream_v4(const void* p) {
+// Weight rows are read once per call: they bypass L1 and enter L2 as the first
+// lines to evict, so a decode step's weight stream (hundreds of MB per layer
+// pass) does not push the KV cache, the activations, the LUTs and the kernels'
+// code out of L2.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+__device__ __forceinline__ int4 ldg_stream_v4(const void* p, uint64_t pol) {
   int4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.s32 {%0,%1,%2,%3}, [%4], %5;"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
+               : "l"(p), "l"(pol));
   return v;
 }
 
@@ -123,6 +133,7 @@ __global__ void __launch_bounds__(GEMV_THREADS)
       wrow[j] = W + r * ldw + k0;
     }
 
+    const uint64_t pol = l2_evict_first_policy();
     for (int c = c_begin + lane; c < c_end; c += 32 * U) {
       int4 wv[U][R];
 #pragma unroll
@@ -130,7 +141,7 @@ __global__ void __launch_bounds__(GEMV_THREADS)
         const int cc = c + 32 * u;
 #pragma unroll
         for (int j = 0; j < R; ++j)
-          wv[u][j] = (cc < c_end) ? ldg_stream_v4(wrow[j] + cc * 16) : make_int4(0, 0, 0, 0);
+          wv[u][j] = (cc < c_end) ? ldg_stream_v4(wrow[j] + cc * 16, pol) : make_int4(0, 0, 0, 0);
       }
       int a32[R][MT];
 #pragma unroll
@@ -257,18 +268,19 @@ __device__ __forceinline__ void gemv_pair_sums(const int8_t* __restrict__ w0,
     for (int m = 0; m < MT; ++m) a[j][m] = 0;
   int4 cur[U][2], nxt[U][2];
   int c = c0 + lane;
+  const uint64_t pol = l2_evict_first_policy();
 #pragma unroll
   for (int u = 0; u < U; ++u) {
     const int cc = c + 32 * u;
-    cur[u][0] = cc < c1 ? ldg_stream_v4(w0 + cc * 16) : make_int4(0, 0, 0, 0);
-    cur[u][1] = cc < c1 ? ldg_stream_v4(w1 + cc * 16) : make_int4(0, 0, 0, 0);
+    cur[u][0] = cc < c1 ? ldg_stream_v4(w0 + cc * 16, pol) : make_int4(0, 0, 0, 0);
+    cur[u][1] = cc < c1 ? ldg_stream_v4(w1 + cc * 16, pol) : make_int4(0, 0, 0, 0);
   }
   for (; c < c1; c += 32 * U) {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int cc = c + 32 * (U + u);
-      nxt[u][0] = cc < c1 ? ldg_stream_v4(w0 + cc * 16) : make_int4(0, 0, 0, 0);
-      nxt[u][1] = cc < c1 ? ldg_stream_v4(w1 + cc * 16) : make_int4(0, 0, 0, 0);
+      nxt[u][0] = cc < c1 ? ldg_stream_v4(w0 + cc * 16, pol) : make_int4(0, 0, 0, 0);
+      nxt[u][1] = cc < c1 ? ldg_stream_v4(w1 + cc * 16, pol) : make_int4(0, 0, 0, 0);
     }
     int a32[2][MT];
 #pragma unroll

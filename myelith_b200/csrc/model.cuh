@@ -8,6 +8,7 @@
 //   q/k/v: one W8A16 GEMV/GEMM over the rows [wq; wk; wv] with the
 //          per-segment out_frac and the rescaled int16 biases fused  run_linear
 //   RoPE of q and k, k and v into the cache                        rope_kv_kernel
+//          (decode: inside attn_scores_kernel)
 //   scores, softmax_int + probability-weighted values + rescale     attn_scores/pv_kernel
 //   o_proj onto min(residual_in, residual_mid) per channel          run_linear
 //   residual add + post-attention RMSNorm                          resid_rmsnorm_kernel
@@ -90,6 +91,7 @@ struct myl_session {
   int32_t* scores = nullptr;
   int64_t* part = nullptr;
   unsigned* counters = nullptr;
+  unsigned* rowmax = nullptr;  // [rows_cap * nq] attention row maxima, zero between calls
   int max_chunks = 0;
   int32_t* logits = nullptr;
   int64_t* keys = nullptr;
@@ -325,10 +327,12 @@ int session_alloc(myl_ctx* ctx, myl_session* s) {
   TRY(dev_alloc(A, &s->attn, size_t(R * m->QD)));
   TRY(dev_alloc(A, &s->xf, size_t(B * H)));
   TRY(dev_alloc(A, &s->scores, size_t(R * m->nq) * size_t(s->max_pos)));
-  s->max_chunks = int((s->max_pos + ATT_CHUNK / 2 - 1) / (ATT_CHUNK / 2));
+  s->max_chunks = int((s->max_pos + ATT_CHUNK - 1) / ATT_CHUNK);
   TRY(dev_alloc(A, &s->part, size_t(s->part_rows * m->nq) * size_t(s->max_chunks) * size_t(m->hd)));
   TRY(dev_alloc(A, &s->counters, size_t(s->part_rows * m->nq)));
   CUDA_TRY(cudaMemset(s->counters, 0, size_t(s->part_rows * m->nq) * sizeof(unsigned)));
+  TRY(dev_alloc(A, &s->rowmax, size_t(R * m->nq)));
+  CUDA_TRY(cudaMemset(s->rowmax, 0, size_t(R * m->nq) * sizeof(unsigned)));
   TRY(dev_alloc(A, &s->logits, size_t(B * m->V)));
   TRY(dev_alloc(A, &s->keys, size_t(B)));
   TRY(dev_alloc(A, &s->tok_in, size_t(R)));
@@ -400,19 +404,29 @@ int run_attention(myl_ctx* ctx, const myl_model* m, myl_session* s, const ModelL
   p.part = s->part;
   p.max_chunks = s->max_chunks;
   p.counters = s->counters;
+  p.rowmax = s->rowmax;
+  p.rope = T == 1;
+  p.rope_cos = m->d_cos;
+  p.rope_sin = m->d_sin;
+  p.n_pos = m->n_pos;
+  p.rope_frac = m->rope_frac;
   p.out = s->attn;
   p.ldo = m->QD;
   const int gsub = int((m->G + ATT_MAXG - 1) / ATT_MAXG);
-  // few rows (decode): small key blocks and chunks, so that the keys of a
-  // long context spread over many SMs; many rows: one block per row for pass 2
-  const bool split = rows <= s->part_rows && rows * m->nq < 4 * int64_t(ctx->num_sms);
-  const int kb = split ? 64 : ATT_KEYS;
-  const size_t smem1 = att_scores_smem(int(m->hd), kb);
-  const int64_t kchunks = (lds_len + kb - 1) / kb;
-  const dim3 g1 = dim3(unsigned(rows * m->nkv * gsub), unsigned(kchunks));
-  LaunchCfg l1(ctx, g1, dim3(kb), smem1, st);
+  const dim3 g1 = dim3(unsigned(rows * m->nkv * gsub), unsigned((lds_len + ATT_SKEYS - 1) / ATT_SKEYS));
+  LaunchCfg l1(ctx, g1, dim3(ATT_THREADS), att_scores_smem(int(m->hd)), st);
   CUDA_TRY(cudaLaunchKernelEx(&l1.cfg, attn_scores_kernel, p, gsub));
-  const int64_t chunk = split ? ATT_CHUNK / 2 : ((lds_len + ATT_CHUNK - 1) / ATT_CHUNK) * ATT_CHUNK;
+  // few rows (decode): chunks of ATT_DCHUNK keys, so that the keys of a long
+  // context spread over many SMs; many rows: one block per row for pass 2
+  const bool split = rows <= s->part_rows && rows * m->nq < 4 * int64_t(ctx->num_sms);
+  if (split && m->hd % 8 == 0 && m->hd <= 128) {
+    const dim3 g2 = dim3(unsigned(rows * m->nq), unsigned((lds_len + ATT_DCHUNK - 1) / ATT_DCHUNK));
+    LaunchCfg l2(ctx, g2, dim3(ATT_DTHREADS), 0, st);
+    CUDA_TRY(cudaLaunchKernelEx(&l2.cfg, attn_pv_dec_kernel, p));
+    ctx->launches += 2;
+    return MYL_OK;
+  }
+  const int64_t chunk = split ? ATT_CHUNK : ((lds_len + ATT_CHUNK - 1) / ATT_CHUNK) * ATT_CHUNK;
   const dim3 g2 = dim3(unsigned(rows * m->nq), unsigned((lds_len + chunk - 1) / chunk));
   if (m->hd % 8 == 0) {
     LaunchCfg l2(ctx, g2, dim3(ATT_THREADS), size_t(ATT_THREADS) * 8 * 8, st);
@@ -430,7 +444,12 @@ int launch_norm(myl_ctx* ctx, const myl_model* m, const int16_t* x, int64_t rows
   const int64_t n = out_rows ? n_out : rows;
   if (n == 0) return MYL_OK;
   const unsigned blocks = unsigned(std::min<int64_t>(n, 65535));
-  if (m->H % 8 == 0 && m->H <= 8 * NORM_THREADS * NORM_NV) {
+  if (m->H % 8 == 0 && m->H <= 8 * NORM_CL * NORM_CL_THREADS && n <= 64) {
+    // few rows (decode): each row over a cluster of SMs
+    LaunchCfg lc(ctx, dim3(unsigned(n) * NORM_CL), dim3(NORM_CL_THREADS), 0, st, NORM_CL);
+    CUDA_TRY(cudaLaunchKernelEx(&lc.cfg, resid_rmsnorm_cluster_kernel, x, m->H, rows, rp,
+                                norm_params(m, nd), out, m->H, out_rows, n_out));
+  } else if (m->H % 8 == 0 && m->H <= 8 * NORM_THREADS * NORM_NV) {
     LaunchCfg lc(ctx, dim3(blocks), dim3(NORM_THREADS), 0, st);
     CUDA_TRY(cudaLaunchKernelEx(&lc.cfg, resid_rmsnorm_vec_kernel, x, m->H, rows, rp,
                                 norm_params(m, nd), out, m->H, out_rows, n_out));
@@ -511,7 +530,7 @@ int model_forward(myl_ctx* ctx, const myl_model* m, myl_session* s, const int32_
     }
     TRY(launch_norm(ctx, m, x1, rows, rp, L.norm1, s->xn, nullptr, 0, st));
     TRY(dispatch_linear(ctx, L.w_qkv, s->xn, rows, H, make_ep(L.rq_qkv, s->qkv, m->ldq), st));
-    {
+    if (T > 1) {  // decode (T == 1): the RoPE runs inside the scores kernel
       const int64_t items = (m->nq + m->nkv) * (m->hd / 2) + m->nkv * m->hd / ((m->hd % 8) ? 1 : 8);
       LaunchCfg lc(ctx, dim3(unsigned(std::min<int64_t>(rows, 65535)), unsigned((items + 255) / 256)),
                    dim3(256), 0, st);
@@ -520,8 +539,8 @@ int model_forward(myl_ctx* ctx, const myl_model* m, myl_session* s, const int32_
                                   int(m->hd), static_cast<const int16_t*>(m->d_cos),
                                   static_cast<const int16_t*>(m->d_sin), m->n_pos, int(m->rope_frac),
                                   s->cache, int(l)));
+      ctx->launches++;
     }
-    ctx->launches++;
     TRY(run_attention(ctx, m, s, L, int(l), rows, T, lds_len, st));
     ResidParams ra{};
     ra.ld_add = H;
@@ -823,11 +842,7 @@ int myl_session_create(myl_ctx* ctx, const myl_model* m, int64_t batch, int64_t 
   const int64_t cap = std::max<int64_t>(1, (int64_t(1) << 30) / score_row_bytes);
   s->rows_cap = std::max<int64_t>(batch, std::min<int64_t>(4096, cap));
   s->part_rows = std::max<int64_t>(batch, (4 * int64_t(ctx->num_sms) + m->nq - 1) / m->nq);
-  int rc = session_alloc(ctx, s);
-  if (rc == MYL_OK &&
-      cudaFuncSetAttribute(attn_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           160 * 1024) != cudaSuccess)
-    rc = fail(MYL_ERR_CUDA, "attention shared-memory attribute");
+  const int rc = session_alloc(ctx, s);
   if (rc != MYL_OK) {
     release_session(ctx, s);
     return rc;
@@ -1102,7 +1117,7 @@ int myl_attention_int(myl_ctx* ctx, const int16_t* q, int64_t q_len, const int16
   uint8_t* dmask = nullptr;
   int32_t* dsc = nullptr;
   int64_t *dpart = nullptr, *dpos = nullptr;
-  unsigned* dcnt = nullptr;
+  unsigned *dcnt = nullptr, *dmax = nullptr;
   const int64_t zero = 0;
   const int max_chunks = int((kv_len + ATT_CHUNK - 1) / ATT_CHUNK);
   int rc = dev_upload(A, &dq, q, size_t(q_len * head_dim));
@@ -1115,7 +1130,10 @@ int myl_attention_int(myl_ctx* ctx, const int16_t* q, int64_t q_len, const int16
   if (rc == MYL_OK) rc = dev_alloc(A, &dsc, size_t(q_len * kv_len));
   if (rc == MYL_OK) rc = dev_alloc(A, &dpart, size_t(q_len * max_chunks * head_dim));
   if (rc == MYL_OK) rc = dev_alloc(A, &dcnt, size_t(q_len));
-  if (rc == MYL_OK && cudaMemset(dcnt, 0, size_t(q_len) * 4) != cudaSuccess) rc = fail(MYL_ERR_CUDA, "memset");
+  if (rc == MYL_OK) rc = dev_alloc(A, &dmax, size_t(q_len));
+  if (rc == MYL_OK && (cudaMemset(dcnt, 0, size_t(q_len) * 4) != cudaSuccess ||
+                       cudaMemset(dmax, 0, size_t(q_len) * 4) != cudaSuccess))
+    rc = fail(MYL_ERR_CUDA, "memset");
   if (rc == MYL_OK) {
     // one "sequence" of q_len query rows, one head; the K/V arrays are the cache
     AttnParams p{};
@@ -1148,6 +1166,7 @@ int myl_attention_int(myl_ctx* ctx, const int16_t* q, int64_t q_len, const int16
     p.part = dpart;
     p.max_chunks = max_chunks;
     p.counters = dcnt;
+    p.rowmax = dmax;
     p.out = dout;
     p.ldo = head_dim;
     // every query sees all kv_len keys: a pseudo-position with pos + 1 = kv_len
@@ -1157,13 +1176,9 @@ int myl_attention_int(myl_ctx* ctx, const int16_t* q, int64_t q_len, const int16
       rc = dev_upload(A, &dmask, ones.data(), ones.size());
       p.mask = dmask;
     }
-    const size_t smem1 = att_scores_smem(int(head_dim));
-    if (rc == MYL_OK && cudaFuncSetAttribute(attn_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             160 * 1024) != cudaSuccess)
-      rc = fail(MYL_ERR_CUDA, "smem attribute");
     if (rc == MYL_OK) {
-      const dim3 g1 = dim3(unsigned(q_len), unsigned((kv_len + ATT_KEYS - 1) / ATT_KEYS));
-      attn_scores_kernel<<<g1, ATT_THREADS, smem1, st>>>(p, 1);
+      const dim3 g1 = dim3(unsigned(q_len), unsigned((kv_len + ATT_SKEYS - 1) / ATT_SKEYS));
+      attn_scores_kernel<<<g1, ATT_THREADS, att_scores_smem(int(head_dim)), st>>>(p, 1);
       const dim3 g2 = dim3(unsigned(q_len), unsigned(max_chunks));
       if (head_dim % 8 == 0)
         attn_pv_vec_kernel<<<g2, ATT_THREADS, size_t(ATT_THREADS) * 8 * 8, st>>>(p, ATT_CHUNK);

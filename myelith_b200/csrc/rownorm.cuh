@@ -104,6 +104,18 @@ __device__ __forceinline__ uint4 pack16(const int16_t (&a)[8]) {
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+// rescale_i64 (fixed_point.rs:184-191) with the signed shift s in [-63, 62],
+// without branches: a left shift wraps as in a release build, a right shift
+// rounds half to even.
+__device__ __forceinline__ int64_t rescale_s64(int64_t v, int s) {
+  const int l = s < 0 ? -s : 0, rs = s > 0 ? s : 0;
+  const int64_t w = int64_t(uint64_t(v) << l);
+  const int64_t q = w >> rs;
+  const int64_t rem = w - int64_t(uint64_t(q) << rs);  // [0, 2^rs)
+  const int64_t half = (int64_t(1) << rs) >> 1;         // 0 when rs = 0
+  return q + ((rem > half) | ((rem == half) & (rs > 0) & (q & 1)));
+}
+
 // rmsnorm.rs:140-151 for one channel: the product shifted by sh, then the i32
 // and i16 clamps. Left shifts (negative sh) go through i128, out of line: they
 // are rare, and the code stays small for the single-block decode launches.
@@ -137,6 +149,72 @@ __device__ __noinline__ void norm_scale(__int128 a, const NormParams& np, int64_
   *nf = np.frac0 + q / 2;
 }
 
+// One 8-channel vector of a row: its loads (all issued at once), the residual
+// add with the square sum, and the normalised output.
+struct NormVec {
+  uint4 x, a, sb;
+  uint2 s1, s2, al, g;
+};
+
+__device__ __forceinline__ void norm_vec_load(NormVec& nv, const int16_t* __restrict__ xr, int64_t r,
+                                              int v, const ResidParams& rp, const NormParams& np) {
+  nv.x = *reinterpret_cast<const uint4*>(xr + 8 * v);
+  if (rp.parts) {
+    int64_t sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int o = 0; o < rp.nparts; ++o) {
+      const longlong2* pp = reinterpret_cast<const longlong2*>(rp.parts + o * rp.part_slab + r * np.H + 8 * v);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const longlong2 t2 = __ldcg(pp + q);
+        sum[2 * q] += t2.x;
+        sum[2 * q + 1] += t2.y;
+      }
+    }
+    const uint2 ps = *reinterpret_cast<const uint2*>(rp.part_shift + 8 * v);
+    int16_t a16[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) a16[e] = clamp16(rescale_s64(sum[e], lane8(ps, e)));
+    nv.a = pack16(a16);
+  } else if (rp.add) {
+    nv.a = *reinterpret_cast<const uint4*>(rp.add + r * rp.ld_add + 8 * v);
+  }
+  if (rp.add || rp.parts) {
+    nv.s1 = *reinterpret_cast<const uint2*>(rp.s1 + 8 * v);
+    nv.s2 = *reinterpret_cast<const uint2*>(rp.s2 + 8 * v);
+  }
+  nv.al = *reinterpret_cast<const uint2*>(np.align2 + 8 * v);
+  nv.g = *reinterpret_cast<const uint2*>(np.gamma + 8 * v);
+  nv.sb = *reinterpret_cast<const uint4*>(np.sbase + 8 * v);
+}
+
+// residual add (nv.x becomes the row after the add), then the square sum:
+// squares (< 2^31) shifted by at most 20 bits are summed in int64 (8192 of
+// them stay below 2^63), wider alignments in i128
+__device__ __forceinline__ void norm_vec_resid(NormVec& nv, bool radd, int64_t& acc64, __int128& acc128) {
+  int16_t val[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    int64_t t = lane16(nv.x, e);
+    if (radd) {
+      const int64_t h = rescale_s64(t, lane8(nv.s1, e)) + int64_t(lane16(nv.a, e));
+      t = clamp16(rescale_s64(h, lane8(nv.s2, e)));
+    }
+    val[e] = int16_t(t);
+    const int a = uint8_t(lane8(nv.al, e));
+    if (a <= 20) acc64 += (t * t) << a;
+    else acc128 += (__int128)(t * t) << a;
+  }
+  nv.x = pack16(val);
+}
+
+__device__ __forceinline__ uint4 norm_vec_out(const NormVec& nv, int64_t lv, int nf) {
+  int16_t y[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e)
+    y[e] = nf == -1000 ? int16_t(0)
+                       : norm_out(int64_t(lane16(nv.x, e)) * lv * int64_t(lane8(nv.g, e)), nf + lane16(nv.sb, e));
+  return pack16(y);
+}
 
 // Shared memory of block_row_norm.
 struct RowNormSmem {
@@ -150,72 +228,27 @@ struct RowNormSmem {
 // the residual stream; rp the optional residual add (as ResidParams, row r of
 // `add` or of the partial slabs); with write_resid the row after the add goes
 // to rp.resid_out. Each normalised 8-element vector v goes to store(v, packed).
-// Every thread issues all loads of its vectors before using any.
 template <class Store>
 __device__ __forceinline__ void block_row_norm(const int16_t* __restrict__ xr, int64_t r,
                                                const ResidParams& rp, const NormParams& np,
                                                bool write_resid, RowNormSmem& sm, Store store) {
   const int nv = int(np.H / 8);
-  uint4 xv[NORM_NV], av[NORM_NV];
-  uint2 s1v[NORM_NV], s2v[NORM_NV], alv[NORM_NV];
+  NormVec vecs[NORM_NV];
   const bool radd = rp.add || rp.parts;
 #pragma unroll
   for (int k = 0; k < NORM_NV; ++k) {
     const int v = threadIdx.x + k * NORM_THREADS;
-    if (v < nv) {
-      xv[k] = *reinterpret_cast<const uint4*>(xr + 8 * v);
-      if (rp.parts) {
-        int64_t sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        for (int o = 0; o < rp.nparts; ++o) {
-          const longlong2* pp =
-              reinterpret_cast<const longlong2*>(rp.parts + o * rp.part_slab + r * np.H + 8 * v);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const longlong2 t2 = __ldcg(pp + q);
-            sum[2 * q] += t2.x;
-            sum[2 * q + 1] += t2.y;
-          }
-        }
-        const uint2 ps = *reinterpret_cast<const uint2*>(rp.part_shift + 8 * v);
-        int16_t a16[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) a16[e] = clamp16(rescale_i64_signed(sum[e], lane8(ps, e)));
-        av[k] = pack16(a16);
-      } else if (rp.add) {
-        av[k] = *reinterpret_cast<const uint4*>(rp.add + r * rp.ld_add + 8 * v);
-      }
-      if (radd) {
-        s1v[k] = *reinterpret_cast<const uint2*>(rp.s1 + 8 * v);
-        s2v[k] = *reinterpret_cast<const uint2*>(rp.s2 + 8 * v);
-      }
-      alv[k] = *reinterpret_cast<const uint2*>(np.align2 + 8 * v);
-    }
+    if (v < nv) norm_vec_load(vecs[k], xr, r, v, rp, np);
   }
-  // residual add, then the square sum: squares (< 2^31) shifted by at most
-  // 20 bits are summed in int64 (8192 of them stay below 2^63), wider
-  // alignments in i128
   int64_t acc64 = 0;
   __int128 acc128 = 0;
 #pragma unroll
   for (int k = 0; k < NORM_NV; ++k) {
     const int v = threadIdx.x + k * NORM_THREADS;
     if (v < nv) {
-      int16_t val[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        int64_t t = lane16(xv[k], e);
-        if (radd) {
-          const int64_t h = rescale_i64_signed(t, lane8(s1v[k], e)) + int64_t(lane16(av[k], e));
-          t = clamp16(rescale_i64_signed(h, lane8(s2v[k], e)));
-        }
-        val[e] = int16_t(t);
-        const int a = uint8_t(lane8(alv[k], e));
-        if (a <= 20) acc64 += (t * t) << a;
-        else acc128 += (__int128)(t * t) << a;
-      }
-      xv[k] = pack16(val);  // the row after the residual add
+      norm_vec_resid(vecs[k], radd, acc64, acc128);
       if (radd && write_resid && rp.resid_out)
-        *reinterpret_cast<uint4*>(rp.resid_out + r * rp.ld_res + 8 * v) = xv[k];
+        *reinterpret_cast<uint4*>(rp.resid_out + r * rp.ld_res + 8 * v) = vecs[k].x;
     }
   }
   __int128 acc = (__int128)acc64 + acc128;
@@ -237,19 +270,23 @@ __device__ __forceinline__ void block_row_norm(const int16_t* __restrict__ xr, i
 #pragma unroll
   for (int k = 0; k < NORM_NV; ++k) {
     const int v = threadIdx.x + k * NORM_THREADS;
-    if (v < nv) {
-      const uint2 gv = *reinterpret_cast<const uint2*>(np.gamma + 8 * v);
-      const uint4 sbv = *reinterpret_cast<const uint4*>(np.sbase + 8 * v);
-      int16_t y[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e)
-        y[e] = nf == -1000 ? int16_t(0)
-                           : norm_out(int64_t(lane16(xv[k], e)) * lv * int64_t(lane8(gv, e)),
-                                      nf + lane16(sbv, e));
-      store(v, pack16(y));
-    }
+    if (v < nv) store(v, norm_vec_out(vecs[k], lv, nf));
   }
   __syncthreads();  // sm is reused by the next row
+}
+
+// ---- one row over a cluster of CTAs (few rows: decode) ---------------------------
+// A row's vectors are split over the NORM_CL CTAs of a cluster (NORM_CL_THREADS
+// threads each, one vector per thread); each CTA's int128 square sum is read
+// by every CTA of the cluster from distributed shared memory, so the per-row
+// work is spread over NORM_CL SMs instead of one.
+constexpr int NORM_CL = 8;
+constexpr int NORM_CL_THREADS = 128;
+
+__device__ __forceinline__ unsigned long long ld_shared_cluster_u64(uint32_t cluster_addr) {
+  unsigned long long v;
+  asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(cluster_addr) : "memory");
+  return v;
 }
 
 }  // namespace myl
