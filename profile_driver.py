@@ -1,7 +1,12 @@
-"""Runs one W8A16 linear shape repeatedly, for profiler captures (ncu).
+"""Runs one W8A16 linear shape, the config-4 MoE layer or an integer forward
+repeatedly, for profiler captures (ncu). A measurement harness beside
+bench.py, not part of the library.
 
-    python -m myelith_b200.profile_driver --M 1 --K 3584 --N 18944 --iters 6
-    python -m myelith_b200.profile_driver --moe --iters 4      (config-4 MoE layer)
+    python profile_driver.py --M 1 --K 3584 --N 18944 --iters 6
+    python profile_driver.py --moe --iters 4                 (config-4 MoE layer)
+    python profile_driver.py --forward qwen2.5-7b --prompt 2048 --new 8 [--batch B] [--layers L]
+        (synthetic model: prefill of the prompt, then greedy decode steps,
+         twice; prints the prefill and decode times of each repetition)
 
 Uses the device path (myl_linear_dev) with rotating weight sets whose total
 size exceeds the 126 MB L2, so that DRAM counters reflect HBM traffic. Three
@@ -26,9 +31,17 @@ def main() -> None:
     ap.add_argument("--sets", type=int, default=0, help="weight sets (0: enough to exceed 2x L2)")
     ap.add_argument("--moe", action="store_true", help="the config-4 MoE layer (myl_moe_dev)")
     ap.add_argument("--tokens", type=int, default=0, help="MoE tokens (0: 4096)")
+    ap.add_argument("--forward", default="", help="synthetic model variant (qwen2.5-0.5b, qwen2.5-7b)")
+    ap.add_argument("--prompt", type=int, default=512)
+    ap.add_argument("--new", type=int, default=8)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=0, help="0: the variant's layer count")
+    ap.add_argument("--reps", type=int, default=2)
     args = ap.parse_args()
     if args.moe:
         return moe(args)
+    if args.forward:
+        return forward(args)
 
     import torch
 
@@ -86,6 +99,23 @@ def moe(args) -> None:
     ctx.synchronize()
     print(f"moe T={T}: {a.elapsed_time(b) / args.iters * 1e3:.2f} us/layer, "
           f"{ctx.launch_count} launches")
+
+
+def forward(args) -> None:
+    import myelith_b200 as myl
+    from myelith_b200 import model as M, synthetic as S
+
+    ctx = myl.Context(0)
+    spec = S.synthetic_model(args.forward, seed=2, num_layers=args.layers or None)
+    gm = M.IntegerModel(ctx, spec)
+    prompts = np.stack([S.prompt_tokens(spec.vocab, args.prompt, seed=100 + b) for b in range(args.batch)])
+    sess = gm.session(args.batch, args.prompt + args.new)
+    for rep in range(args.reps):
+        sess.reset()
+        sess.forward(prompts, want_logits=False)
+        sess.decode(args.new)
+        pre, dec = sess.timing()
+        print(f"rep {rep}: prefill {pre:.3f} ms, decode {dec:.3f} ms for {args.new} steps", flush=True)
 
 
 if __name__ == "__main__":
