@@ -44,6 +44,20 @@ __device__ __forceinline__ int4 ldg_stream_v4(const void* p, uint64_t pol) {
   return v;
 }
 
+// Asynchronous bulk prefetch of a contiguous weight range into L2 (no
+// registers, no shared memory; bytes a multiple of 16). The GEMV kernels issue
+// it for their first rows before the programmatic dependency wait: weights do
+// not depend on the previous kernel (they are written only at registration,
+// which synchronises), so their first bytes come while that kernel finishes.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, int64_t bytes) {
+  while (bytes > 0) {
+    const uint32_t b = uint32_t(bytes < 65536 ? bytes : 65536);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(b) : "memory");
+    p = static_cast<const int8_t*>(p) + b;
+    bytes -= b;
+  }
+}
+
 __device__ __forceinline__ int dot16_dp2a(const int4 w, const int4 xa, const int4 xb, int acc) {
   // w bytes 4q..4q+3 pair with x words 2q (lo half of w) and 2q+1 (hi half).
   acc = __dp2a_lo(xa.x, w.x, acc);
@@ -68,6 +82,15 @@ __global__ void __launch_bounds__(GEMV_THREADS)
     gemv_w8a16_kernel(const int8_t* __restrict__ W, int64_t ldw, int64_t N,
                       const int16_t* __restrict__ X, int64_t ldx, int64_t K, int64_t k_slice,
                       Epilogue ep, int64_t slice_stride) {
+  {  // this warp's first rows into L2 (one K slice of R rows)
+    const int warp = threadIdx.x >> 5;
+    const int64_t row0 = int64_t(blockIdx.x) * (GEMV_WARPS / KW) * R + int64_t(warp / KW) * R;
+    if ((threadIdx.x & 31) == 0 && warp % KW == 0 && row0 < N) {
+      const int64_t k0 = int64_t(blockIdx.y) * k_slice;
+      const int64_t kb = ((min(K - k0, k_slice) + 15) & ~int64_t(15));
+      for (int j = 0; j < R && row0 + j < N; ++j) prefetch_l2_bulk(W + (row0 + j) * ldw + k0, kb);
+    }
+  }
   pdl_wait();
   pdl_launch();
   static_assert(GEMV_WARPS % KW == 0, "warps per row group");
@@ -325,6 +348,13 @@ template <int MT, int U>
 __global__ void __launch_bounds__(GEMV_THREADS, 2)
     gemv_balanced_kernel(const int8_t* __restrict__ W, int64_t ldw, int64_t N,
                          const int16_t* __restrict__ X, int64_t ldx, int64_t K, Epilogue ep) {
+  {  // this warp's first row pair into L2
+    const int64_t nw = int64_t(gridDim.x) * GEMV_WARPS;
+    const int64_t w = int64_t(blockIdx.x) * GEMV_WARPS + (threadIdx.x >> 5);
+    const int64_t np = (N + 1) / 2, p = w * np / nw;
+    if ((threadIdx.x & 31) == 0 && p < (w + 1) * np / nw)
+      prefetch_l2_bulk(W + 2 * p * ldw, (2 * p + 1 < N ? 2 : 1) * ldw);
+  }
   pdl_wait();
   pdl_launch();
   extern __shared__ __align__(16) int16_t xs[];  // [MT][KS], two 16-byte planes per chunk
