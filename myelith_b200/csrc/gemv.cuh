@@ -394,6 +394,99 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2)
   }
 }
 
+// Streaming GEMV for one activation row and rows of at most 32 * CPL
+// chunks (K <= 512 * CPL; CPL <= 8 keeps the three slots in registers): warp w finishes the whole row pairs
+// [w*P/W, (w+1)*P/W) one row at a time, each row's CPL chunks per lane loaded
+// in one batch, and the loads of the next two rows in flight while a row's
+// products run (three register slots: the pair's even and odd row and the next
+// pair's even row). Two blocks per SM, 16 warps: ~7 KB of weight loads in
+// flight per warp for K = 3584.
+template <int CPL>
+__device__ __forceinline__ void gemv_row_load(int4 (&v)[CPL], const int8_t* __restrict__ row, int C, int lane,
+                                              uint64_t pol) {
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const int c = lane + 32 * i;
+    v[i] = c < C ? ldg_stream_v4(row + 16 * c, pol) : make_int4(0, 0, 0, 0);
+  }
+}
+
+template <int CPL>
+__device__ __forceinline__ int64_t gemv_row_dot(const int4 (&v)[CPL], const int4* __restrict__ xa,
+                                                const int4* __restrict__ xb, int C, int lane) {
+  int a = 0;  // CPL <= 31 chunks of 16 products of at most 2^22: exact in int32
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const int c = lane + 32 * i;
+    if (c < C) a = dot16_dp2a(v[i], xa[c], xb[c], a);
+  }
+  return a;
+}
+
+template <int CPL>
+__global__ void __launch_bounds__(GEMV_THREADS, 2)
+    gemv_stream_kernel(const int8_t* __restrict__ W, int64_t ldw, int64_t N,
+                       const int16_t* __restrict__ X, int64_t K, Epilogue ep) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = int64_t(gridDim.x) * GEMV_WARPS;
+  const int64_t w = int64_t(blockIdx.x) * GEMV_WARPS + (threadIdx.x >> 5);
+  const int64_t np = (N + 1) / 2;
+  const int64_t p_begin = w * np / nw, p_end = (w + 1) * np / nw;
+  const uint64_t pol = l2_evict_first_policy();
+  const int KS = int((K + 15) & ~int64_t(15));
+  const int C = KS >> 4;
+  // the first pair's rows do not depend on the previous kernel: loads issued
+  // before the programmatic dependency wait
+  int4 e[CPL], o[CPL], n[CPL];
+  auto row_ptr = [&](int64_t r) { return W + (r < N ? r : N - 1) * ldw; };  // odd N: duplicate, not stored
+  if (p_begin < p_end) {
+    gemv_row_load<CPL>(e, row_ptr(2 * p_begin), C, lane, pol);
+    gemv_row_load<CPL>(o, row_ptr(2 * p_begin + 1), C, lane, pol);
+  }
+  pdl_wait();
+  pdl_launch();
+  extern __shared__ __align__(16) int16_t xs[];  // [KS], two 16-byte planes per chunk
+  {
+    const bool vec_ok = (reinterpret_cast<uintptr_t>(X) & 15) == 0;
+    int4* dst = reinterpret_cast<int4*>(xs);
+    for (int hh = threadIdx.x; hh < (KS >> 3); hh += GEMV_THREADS) {
+      const int i = hh * 8;
+      int4 v;
+      if (vec_ok && i + 8 <= K) {
+        v = __ldg(reinterpret_cast<const int4*>(X + i));
+      } else {
+        alignas(16) int16_t t[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) t[q] = (i + q < K) ? X[i + q] : int16_t(0);
+        v = *reinterpret_cast<const int4*>(t);
+      }
+      dst[(hh & 1) * C + (hh >> 1)] = v;
+    }
+  }
+  __syncthreads();
+  const int4* xa = reinterpret_cast<const int4*>(xs);
+  const int4* xb = xa + C;
+  for (int64_t p = p_begin; p < p_end; ++p) {
+    const bool more = p + 1 < p_end;
+    if (more) gemv_row_load<CPL>(n, row_ptr(2 * p + 2), C, lane, pol);
+    int64_t a[2][1];
+    a[0][0] = gemv_row_dot<CPL>(e, xa, xb, C, lane);
+    if (more) gemv_row_load<CPL>(e, row_ptr(2 * p + 3), C, lane, pol);  // e is free: the next odd row
+    a[1][0] = gemv_row_dot<CPL>(o, xa, xb, C, lane);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      a[0][0] += __shfl_xor_sync(0xffffffffu, a[0][0], off);
+      a[1][0] += __shfl_xor_sync(0xffffffffu, a[1][0], off);
+    }
+    if (lane == 0) gemv_pair_epilogue<1>(ep, p, N, a);
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) {
+      o[i] = e[i];
+      e[i] = n[i];
+    }
+  }
+}
+
 // xsum[m] = sum_k x[m][k] (int64), one warp per row: the EPI_W16 correction.
 __global__ void x_row_sums_kernel(const int16_t* __restrict__ X, int64_t ldx, int64_t M, int64_t K,
                                   int64_t* __restrict__ xsum) {

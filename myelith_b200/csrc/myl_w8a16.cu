@@ -376,8 +376,42 @@ static bool use_balanced_gemv(const myl_ctx* ctx, const myl_weight* w, int64_t M
   return npairs <= 2 * warps;
 }
 
+template <int CPL>
+static void* gemv_stream_ptr() {
+  return reinterpret_cast<void*>(&gemv_stream_kernel<CPL>);
+}
+
+// The streaming GEMV (one activation row, rows of at most 8 * 32 chunks):
+// grid = resident blocks x SMs, every warp an equal share of whole row pairs.
+// Returns false (nothing launched) for other shapes.
+static bool gemv_stream_fits(const myl_weight* w, int64_t M) {
+  return M == 1 && (w->K + 15) / 16 <= 8 * 32 && !std::getenv("MYL_GEMV_CLASSIC");
+}
+
+static int launch_gemv_stream(myl_ctx* ctx, const myl_weight* w, const int16_t* x, const Epilogue& ep,
+                              cudaStream_t st) {
+  int64_t K = w->K, N = w->N;
+  const int64_t C = (K + 15) / 16;
+  void* fn = C <= 64 ? gemv_stream_ptr<2>() : C <= 128 ? gemv_stream_ptr<4>() : gemv_stream_ptr<8>();
+  const size_t smem = size_t(round_up16(K)) * 2;
+  int resident = 0;
+  TRY(kernel_smem_occupancy(ctx->device, fn, GEMV_THREADS, smem, &resident));
+  const int64_t pairs = (N + 1) / 2;
+  const unsigned grid = unsigned(std::min<int64_t>(std::max(1, resident) * int64_t(sms(ctx)),
+                                                   (pairs + GEMV_WARPS - 1) / GEMV_WARPS));
+  const int8_t* dW = w->d_W;
+  int64_t ldw = w->ldp;
+  Epilogue e = ep;
+  void* args[] = {(void*)&dW, (void*)&ldw, (void*)&N, (void*)&x, (void*)&K, (void*)&e};
+  LaunchCfg lc(ctx, dim3(grid), dim3(GEMV_THREADS), smem, st);
+  CUDA_TRY(cudaLaunchKernelExC(&lc.cfg, fn, args));
+  ctx->launches++;
+  return MYL_OK;
+}
+
 static int launch_gemv(myl_ctx* ctx, const myl_weight* w, const int16_t* x, int64_t M, int64_t ldx,
                        const Epilogue& ep_final, cudaStream_t st) {
+  if (ctx->force_split_k == 0 && gemv_stream_fits(w, M)) return launch_gemv_stream(ctx, w, x, ep_final, st);
   GemvVariant v = gemv_variant(int(M), w->K, w->N, sms(ctx));
   const int64_t K = w->K;
   const int64_t ks_max = (GEMV_SMEM_BUDGET / (2 * M)) & ~int64_t(15);
