@@ -278,26 +278,35 @@ __device__ __forceinline__ void gemv_pair_epilogue(const Epilogue& ep, int64_t p
   }
 }
 
-// Exact sums of chunks [c0, c1) of rows w0 and w1 against the staged x,
-// loads software-pipelined one batch of U chunks ahead of the products.
-template <int MT, int U>
-__device__ __forceinline__ void gemv_pair_sums(const int8_t* __restrict__ w0,
-                                               const int8_t* __restrict__ w1,
-                                               const int16_t* __restrict__ xs, int KS, int C, int c0,
-                                               int c1, int lane, int64_t (&a)[2][MT]) {
-#pragma unroll
-  for (int j = 0; j < 2; ++j)
-#pragma unroll
-    for (int m = 0; m < MT; ++m) a[j][m] = 0;
-  int4 cur[U][2], nxt[U][2];
-  int c = c0 + lane;
-  const uint64_t pol = l2_evict_first_policy();
+// The first batch of U chunks per lane of rows w0 and w1 from chunk c on.
+template <int U>
+__device__ __forceinline__ void gemv_pair_first_batch(const int8_t* __restrict__ w0, const int8_t* __restrict__ w1,
+                                                      int c, int c1, uint64_t pol, int4 (&cur)[U][2]) {
 #pragma unroll
   for (int u = 0; u < U; ++u) {
     const int cc = c + 32 * u;
     cur[u][0] = cc < c1 ? ldg_stream_v4(w0 + cc * 16, pol) : make_int4(0, 0, 0, 0);
     cur[u][1] = cc < c1 ? ldg_stream_v4(w1 + cc * 16, pol) : make_int4(0, 0, 0, 0);
   }
+}
+
+// Exact sums of chunks [c0, c1) of rows w0 and w1 against the staged x,
+// loads software-pipelined one batch of U chunks ahead of the products
+// (the first batch already in cur when `loaded`).
+template <int MT, int U>
+__device__ __forceinline__ void gemv_pair_sums(const int8_t* __restrict__ w0,
+                                               const int8_t* __restrict__ w1,
+                                               const int16_t* __restrict__ xs, int KS, int C, int c0,
+                                               int c1, int lane, int64_t (&a)[2][MT], int4 (&cur)[U][2],
+                                               bool loaded) {
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+#pragma unroll
+    for (int m = 0; m < MT; ++m) a[j][m] = 0;
+  int4 nxt[U][2];
+  int c = c0 + lane;
+  const uint64_t pol = l2_evict_first_policy();
+  if (!loaded) gemv_pair_first_batch<U>(w0, w1, c, c1, pol, cur);
   for (; c < c1; c += 32 * U) {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -348,18 +357,25 @@ template <int MT, int U>
 __global__ void __launch_bounds__(GEMV_THREADS, 2)
     gemv_balanced_kernel(const int8_t* __restrict__ W, int64_t ldw, int64_t N,
                          const int16_t* __restrict__ X, int64_t ldx, int64_t K, Epilogue ep) {
-  {  // this warp's first row pair into L2
-    const int64_t nw = int64_t(gridDim.x) * GEMV_WARPS;
-    const int64_t w = int64_t(blockIdx.x) * GEMV_WARPS + (threadIdx.x >> 5);
-    const int64_t np = (N + 1) / 2, p = w * np / nw;
-    if ((threadIdx.x & 31) == 0 && p < (w + 1) * np / nw)
-      prefetch_l2_bulk(W + 2 * p * ldw, (2 * p + 1 < N ? 2 : 1) * ldw);
+  const int KS = int((K + 15) & ~int64_t(15));
+  const int C = KS >> 4;
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = int64_t(gridDim.x) * GEMV_WARPS;
+  const int64_t wid = int64_t(blockIdx.x) * GEMV_WARPS + (threadIdx.x >> 5);
+  const int64_t npairs = (N + 1) / 2;
+  const int64_t p_begin = wid * npairs / nwarps, p_end = (wid + 1) * npairs / nwarps;
+  // this warp's first row pair: the rest into L2 and the first batch into
+  // registers before the programmatic dependency wait
+  int4 cur[U][2];
+  if (p_begin < p_end) {
+    const int8_t* w0 = W + 2 * p_begin * ldw;
+    const int8_t* w1 = (2 * p_begin + 1 < N) ? w0 + ldw : w0;
+    if (lane == 0) prefetch_l2_bulk(w0, (2 * p_begin + 1 < N ? 2 : 1) * ldw);
+    gemv_pair_first_batch<U>(w0, w1, lane, C, l2_evict_first_policy(), cur);
   }
   pdl_wait();
   pdl_launch();
   extern __shared__ __align__(16) int16_t xs[];  // [MT][KS], two 16-byte planes per chunk
-  const int KS = int((K + 15) & ~int64_t(15));
-  const int C = KS >> 4;
   const bool vec_ok = ((reinterpret_cast<uintptr_t>(X) & 15) == 0) && (ldx % 8 == 0);
 #pragma unroll
   for (int m = 0; m < MT; ++m) {
@@ -381,15 +397,10 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2)
   }
   __syncthreads();
 
-  const int lane = threadIdx.x & 31;
-  const int64_t nwarps = int64_t(gridDim.x) * GEMV_WARPS;
-  const int64_t wid = int64_t(blockIdx.x) * GEMV_WARPS + (threadIdx.x >> 5);
-  const int64_t npairs = (N + 1) / 2;
-  const int64_t p_end = (wid + 1) * npairs / nwarps;
-  for (int64_t p = wid * npairs / nwarps; p < p_end; ++p) {
+  for (int64_t p = p_begin; p < p_end; ++p) {
     const int64_t r1 = (2 * p + 1 < N) ? 2 * p + 1 : 2 * p;  // odd N: duplicate, not stored
     int64_t a[2][MT];
-    gemv_pair_sums<MT, U>(W + 2 * p * ldw, W + r1 * ldw, xs, KS, C, 0, C, lane, a);
+    gemv_pair_sums<MT, U>(W + 2 * p * ldw, W + r1 * ldw, xs, KS, C, 0, C, lane, a, cur, p == p_begin);
     if (lane == 0) gemv_pair_epilogue<MT>(ep, p, N, a);
   }
 }
