@@ -425,13 +425,27 @@ __device__ __forceinline__ void gemv_row_load(int4 (&v)[CPL], const int8_t* __re
 template <int CPL>
 __device__ __forceinline__ int64_t gemv_row_dot(const int4 (&v)[CPL], const int4* __restrict__ xa,
                                                 const int4* __restrict__ xb, int C, int lane) {
-  int a = 0;  // CPL <= 31 chunks of 16 products of at most 2^22: exact in int32
+  // four independent dp2a chains (CPL <= 31 chunks of 16 products of at most
+  // 2^22: every partial is exact in int32)
+  int a[4] = {0, 0, 0, 0};
 #pragma unroll
   for (int i = 0; i < CPL; ++i) {
     const int c = lane + 32 * i;
-    if (c < C) a = dot16_dp2a(v[i], xa[c], xb[c], a);
+    if (c < C) {
+      const int4 w = v[i], x0 = xa[c], x1 = xb[c];
+      int& p = a[2 * (i & 1)];
+      int& q = a[2 * (i & 1) + 1];
+      p = __dp2a_lo(x0.x, w.x, p);
+      q = __dp2a_lo(x1.x, w.z, q);
+      p = __dp2a_hi(x0.y, w.x, p);
+      q = __dp2a_hi(x1.y, w.z, q);
+      p = __dp2a_lo(x0.z, w.y, p);
+      q = __dp2a_lo(x1.z, w.w, q);
+      p = __dp2a_hi(x0.w, w.y, p);
+      q = __dp2a_hi(x1.w, w.w, q);
+    }
   }
-  return a;
+  return int64_t(a[0]) + a[1] + a[2] + a[3];
 }
 
 template <int CPL>

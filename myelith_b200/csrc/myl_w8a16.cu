@@ -392,7 +392,10 @@ static int launch_gemv_stream(myl_ctx* ctx, const myl_weight* w, const int16_t* 
                               cudaStream_t st) {
   int64_t K = w->K, N = w->N;
   const int64_t C = (K + 15) / 16;
-  void* fn = C <= 64 ? gemv_stream_ptr<2>() : C <= 128 ? gemv_stream_ptr<4>() : gemv_stream_ptr<8>();
+  void* fn = C <= 64    ? gemv_stream_ptr<2>()
+           : C <= 128 ? gemv_stream_ptr<4>()
+           : C <= 224 ? gemv_stream_ptr<7>()  // K = 3584: no idle chunk slot
+                      : gemv_stream_ptr<8>();
   const size_t smem = size_t(round_up16(K)) * 2;
   int resident = 0;
   TRY(kernel_smem_occupancy(ctx->device, fn, GEMV_THREADS, smem, &resident));
