@@ -92,8 +92,9 @@ struct Epilogue {
 // predecessor grid has finished, and griddepcontrol.wait holds it until that
 // grid has completed and its memory is visible; launched normally, the wait
 // returns at once. pdl_launch() then lets the kernel's own successor launch
-// early (it waits in turn). No global memory is read or written before the
-// wait.
+// early (it waits in turn). Before the wait a kernel writes no global memory
+// and reads none that an earlier kernel writes (the GEMVs read their weights,
+// which only registration writes, before it).
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 

@@ -253,29 +253,29 @@ __global__ void __launch_bounds__(GEMV_THREADS)
 // a pair are software-pipelined one batch ahead of the products. Used where
 // the row-group kernel below would leave SMs with unequal block counts (long K
 // and few rows, e.g. the 7B down projection).
-// Epilogue of a finished row pair (rows 2p, 2p + 1; 2p + 1 may not exist).
+// Epilogue of a finished row pair (rows 2p, 2p + 1; 2p + 1 may not exist)
+// for activation row m: exact sums a0 (row 2p) and a1 (row 2p + 1).
+__device__ __forceinline__ void pair_epilogue_m(const Epilogue& ep, int64_t m, int64_t p, int64_t N,
+                                                int64_t a0, int64_t a1) {
+  if (ep.mode == EPI_W16) {
+    if (2 * p + 1 < N) w16_store(ep, m, p, a0, a1);
+  } else if (ep.mode == EPI_SILU) {
+    if (2 * p + 1 < N) {
+      const int32_t g = int32_t(requant_value(ep, 2 * p, a0));
+      const int32_t u = int32_t(requant_value(ep, 2 * p + 1, a1));
+      silu_store(ep, m, p, silu_combine(ep.silu, g, u));
+    }
+  } else {
+    epilogue_store(ep, m, 2 * p, a0);
+    if (2 * p + 1 < N) epilogue_store(ep, m, 2 * p + 1, a1);
+  }
+}
+
 template <int MT>
 __device__ __forceinline__ void gemv_pair_epilogue(const Epilogue& ep, int64_t p, int64_t N,
                                                    const int64_t (&a)[2][MT]) {
-  if (ep.mode == EPI_W16) {
 #pragma unroll
-    for (int m = 0; m < MT; ++m)
-      if (2 * p + 1 < N) w16_store(ep, m, p, a[0][m], a[1][m]);
-  } else if (ep.mode == EPI_SILU) {
-#pragma unroll
-    for (int m = 0; m < MT; ++m)
-      if (2 * p + 1 < N) {
-        const int32_t g = int32_t(requant_value(ep, 2 * p, a[0][m]));
-        const int32_t u = int32_t(requant_value(ep, 2 * p + 1, a[1][m]));
-        silu_store(ep, m, p, silu_combine(ep.silu, g, u));
-      }
-  } else {
-#pragma unroll
-    for (int m = 0; m < MT; ++m) {
-      epilogue_store(ep, m, 2 * p, a[0][m]);
-      if (2 * p + 1 < N) epilogue_store(ep, m, 2 * p + 1, a[1][m]);
-    }
-  }
+  for (int m = 0; m < MT; ++m) pair_epilogue_m(ep, m, p, N, a[0][m], a[1][m]);
 }
 
 // The first batch of U chunks per lane of rows w0 and w1 from chunk c on.
