@@ -787,6 +787,353 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_pv_vec_kernel(AttnParams p, 
   attn_finish(p, row, c, nch, tot, &s_last);
 }
 
+// Pass 2 for many rows (prefill), tiled: block (64 consecutive query rows of
+// one sequence, one head) walks the keys in tiles of ATT_TK: the tile's value
+// rows and the 64 x ATT_TK probabilities are staged in shared memory once and
+// used by every row, instead of every row reading every value row. Phase 1:
+// each row's exponential sum (a warp per row, from the row maximum of pass 1).
+// Phase 2: per tile, p = softmax_prob(...) for keys j <= pos of each row (0
+// beyond), then thread (row group, 8-dim group) adds p * v for RPT rows and 8
+// dimensions in int64 (hd = 32 * RPT, multiple of 8). Phase 3: round by
+// prob_frac, clamp, rescale, store; the rows' maxima are set back to zero.
+constexpr int ATT_TQ = 64;   // query rows per block
+constexpr int ATT_TK = 64;   // keys per tile
+
+template <int RPT>
+__global__ void __launch_bounds__(ATT_THREADS) attn_pv_tile_kernel(AttnParams p) {
+  pdl_wait();
+  pdl_launch();
+  constexpr int HD = 32 * RPT;
+  __shared__ __align__(16) int16_t s_v[ATT_TK][HD];
+  __shared__ int32_t s_p[ATT_TQ][ATT_TK + 1];
+  __shared__ int32_t s_m[ATT_TQ], s_S[ATT_TQ];
+  __shared__ int64_t s_len[ATT_TQ];
+  const int T = int(p.T);
+  const int tiles_per_seq = (T + ATT_TQ - 1) / ATT_TQ;
+  const int b = int(blockIdx.x) / tiles_per_seq, t0 = (int(blockIdx.x) % tiles_per_seq) * ATT_TQ;
+  const int h = int(blockIdx.y);
+  const int nrows = min(ATT_TQ, T - t0);
+  const int64_t pos0 = p.pos0[0];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int32_t lut_one = p.exp_lut[0];
+  const int32_t one = int32_t(1) << p.prob_frac;
+  auto row_index = [&](int i) { return (int64_t(b) * T + t0 + i) * p.nq + h; };  // scores / rowmax row
+  if (threadIdx.x < ATT_TQ) {
+    const int i = threadIdx.x;
+    s_len[i] = i < nrows ? pos0 + t0 + i + 1 : 0;
+    s_m[i] = i < nrows ? int32_t(p.rowmax[row_index(i)] ^ 0x80000000u) : 0;
+  }
+  __syncthreads();
+  // phase 1: exponential sums, warp w takes rows w, w + 8, ...
+  for (int i = warp; i < nrows; i += ATT_THREADS / 32) {
+    const int32_t* sc = p.scores + row_index(i) * p.lds;
+    const int n = int(s_len[i]);
+    const int32_t m = s_m[i];
+    int64_t S = 0;
+    for (int j0 = lane; j0 < n; j0 += 32 * 8) {
+      int32_t v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = j0 + 32 * u < n ? sc[j0 + 32 * u] : m;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (j0 + 32 * u < n) S += exp_of(m, v[u], p, lut_one);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
+    if (lane == 0) s_S[i] = int32_t(S);  // i32 in the reference; the host bounds len
+  }
+  __syncthreads();
+  if (threadIdx.x < nrows) p.rowmax[row_index(threadIdx.x)] = 0u;  // every reader is done
+  // phase 2
+  constexpr int DG = HD / 8;                 // 8-dim groups
+  constexpr int RG = ATT_THREADS / DG;       // row groups (ATT_TQ / RPT)
+  static_assert(RG * RPT == ATT_TQ, "row tiling");
+  const int dg = threadIdx.x % DG, rg = threadIdx.x / DG;
+  int64_t acc[RPT][8];
+#pragma unroll
+  for (int i = 0; i < RPT; ++i)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[i][e] = 0;
+  const int16_t* vbase = p.kc.v + int64_t(b) * p.kc.seq_stride + int64_t(p.layer) * p.kc.layer_stride +
+                         int64_t((p.q_head0 + h) / p.G - p.kv_head0) * p.kc.head_stride;
+  const int64_t kend = s_len[nrows - 1];  // the longest row of the block
+  for (int64_t j0 = 0; j0 < kend; j0 += ATT_TK) {
+    const int nk = int(min(int64_t(ATT_TK), kend - j0));
+    __syncthreads();  // the previous tile is consumed
+    // all loads of the tile first: value rows (16 B) and scores (4 x 4 B) per item
+    constexpr int VIT = ATT_TK * DG / ATT_THREADS;       // value vectors per thread
+    constexpr int SIT = ATT_TQ * ATT_TK / 4 / ATT_THREADS;  // score quads per thread
+    uint4 vreg[VIT];
+    int32_t sreg[SIT][4];
+#pragma unroll
+    for (int q = 0; q < VIT; ++q) {
+      const int e = threadIdx.x + q * ATT_THREADS, jj = e / DG, d8 = e % DG;
+      vreg[q] = jj < nk ? *reinterpret_cast<const uint4*>(vbase + (j0 + jj) * HD + 8 * d8)
+                        : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int q = 0; q < SIT; ++q) {
+      const int e = threadIdx.x + q * ATT_THREADS, i = e / (ATT_TK / 4), j4 = 4 * (e % (ATT_TK / 4));
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t j = j0 + j4 + u;
+        sreg[q][u] = (i < nrows && j < s_len[i]) ? p.scores[row_index(i) * p.lds + j] : 0;
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < VIT; ++q) {
+      const int e = threadIdx.x + q * ATT_THREADS, jj = e / DG, d8 = e % DG;
+      *reinterpret_cast<uint4*>(&s_v[jj][8 * d8]) = vreg[q];
+    }
+#pragma unroll
+    for (int q = 0; q < SIT; ++q) {
+      const int e = threadIdx.x + q * ATT_THREADS, i = e / (ATT_TK / 4), j4 = 4 * (e % (ATT_TK / 4));
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t j = j0 + j4 + u;
+        s_p[i][j4 + u] = (i < nrows && j < s_len[i])
+                             ? softmax_prob(exp_of(s_m[i], sreg[q][u], p, lut_one), s_S[i], j, s_len[i], one)
+                             : 0;
+      }
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int jj = 0; jj < nk; ++jj) {
+      const uint4 vv = *reinterpret_cast<const uint4*>(&s_v[jj][8 * dg]);
+#pragma unroll
+      for (int i = 0; i < RPT; ++i) {
+        const int64_t pj = s_p[rg * RPT + i][jj];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[i][e] += pj * int64_t(lane16(vv, e));
+      }
+    }
+  }
+  // phase 3
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) {
+    const int r = rg * RPT + i;
+    if (r >= nrows) continue;
+    int16_t o8[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      int32_t o = clamp16(p.prob_frac > 0 ? rshift_rne_i64(acc[i][e], p.prob_frac) : acc[i][e]);
+      if (p.out_shift != 0) o = clamp16(rescale_i32_s(o, p.out_shift));
+      o8[e] = int16_t(o);
+    }
+    *reinterpret_cast<uint4*>(p.out + (int64_t(b) * T + t0 + r) * p.ldo + int64_t(h) * HD + 8 * dg) = pack16(o8);
+  }
+}
+
+// The same tiling with the products on the integer MMA path (mma.sync
+// m16n8k32, u8 x u8) for head_dim 64 or 128 and p <= 32768 (prob_frac <= 15).
+// p = 256 ph + pl and v + 32768 = 256 vh + vl (vh = (v >> 8) + 128, vl =
+// v & 255) are unsigned bytes, so per tile
+//   sum_j p_j v_j = 65536 HH + 256 (HL + LH) + LL - 32768 sum_j p_j
+// with HH = sum ph*vh etc. exact in int32 over 64 keys (<= 6.2e6) and added to
+// int64 accumulators after every tile. The probabilities are stored as two
+// byte planes [row][key]; the value tile transposed into two byte planes
+// [dim][key], so both MMA operands are 4-key words (rows padded to 80 bytes:
+// the 8 x 4 words a fragment load touches fall into distinct banks). Warp
+// task = 16 rows x 32 dims (4 n-tiles); HD / 64 tasks per warp.
+__device__ __forceinline__ void mma_u8u8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+constexpr int ATT_PK = 80;  // bytes per padded plane row (64 keys)
+
+template <int HD>
+__global__ void __launch_bounds__(ATT_THREADS) attn_pv_mma_kernel(AttnParams p) {
+  pdl_wait();
+  pdl_launch();
+  static_assert(HD == 64 || HD == 128, "head_dim");
+  constexpr int TPW = HD / 64;  // warp tasks per warp
+  __shared__ __align__(16) uint8_t s_ph[ATT_TQ][ATT_PK], s_pl[ATT_TQ][ATT_PK];
+  __shared__ __align__(16) uint8_t s_vh[HD][ATT_PK], s_vl[HD][ATT_PK];
+  __shared__ int32_t s_m[ATT_TQ], s_S[ATT_TQ], s_P[ATT_TQ];
+  __shared__ int64_t s_len[ATT_TQ];
+  const int T = int(p.T);
+  const int tiles_per_seq = (T + ATT_TQ - 1) / ATT_TQ;
+  const int b = int(blockIdx.x) / tiles_per_seq, t0 = (int(blockIdx.x) % tiles_per_seq) * ATT_TQ;
+  const int h = int(blockIdx.y);
+  const int nrows = min(ATT_TQ, T - t0);
+  const int64_t pos0 = p.pos0[0];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, c = lane & 3;
+  const int32_t lut_one = p.exp_lut[0];
+  const int32_t one = int32_t(1) << p.prob_frac;
+  auto row_index = [&](int i) { return (int64_t(b) * T + t0 + i) * p.nq + h; };
+  if (threadIdx.x < ATT_TQ) {
+    const int i = threadIdx.x;
+    s_len[i] = i < nrows ? pos0 + t0 + i + 1 : 0;
+    s_m[i] = i < nrows ? int32_t(p.rowmax[row_index(i)] ^ 0x80000000u) : 0;
+  }
+  __syncthreads();
+  // phase 1: exponential sums, warp w takes rows w, w + 8, ...
+  for (int i = warp; i < nrows; i += ATT_THREADS / 32) {
+    const int32_t* sc = p.scores + row_index(i) * p.lds;
+    const int n = int(s_len[i]);
+    const int32_t m = s_m[i];
+    int64_t S = 0;
+    for (int j0 = lane; j0 < n; j0 += 32 * 8) {
+      int32_t v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = j0 + 32 * u < n ? sc[j0 + 32 * u] : m;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (j0 + 32 * u < n) S += exp_of(m, v[u], p, lut_one);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
+    if (lane == 0) s_S[i] = int32_t(S);  // i32 in the reference; the host bounds len
+  }
+  __syncthreads();
+  if (threadIdx.x < nrows) p.rowmax[row_index(threadIdx.x)] = 0u;  // every reader is done
+  const int16_t* vbase = p.kc.v + int64_t(b) * p.kc.seq_stride + int64_t(p.layer) * p.kc.layer_stride +
+                         int64_t((p.q_head0 + h) / p.G - p.kv_head0) * p.kc.head_stride;
+  int64_t acc[TPW][4][4];
+#pragma unroll
+  for (int t = 0; t < TPW; ++t)
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[t][n][i] = 0;
+  const int64_t kend = s_len[nrows - 1];  // the longest row of the block
+  for (int64_t j0 = 0; j0 < kend; j0 += ATT_TK) {
+    const int nk = int(min(int64_t(ATT_TK), kend - j0));
+    __syncthreads();  // the previous tile is consumed
+    // loads first: thread (key quad q, 8-dim group d8) reads 4 value vectors;
+    // thread (row i, key quad j4) reads 4 scores
+    constexpr int DG = HD / 8;
+    const int vq = threadIdx.x % 16, vd8 = threadIdx.x / 16;
+    const bool vact = vd8 < DG;
+    uint4 vreg[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int jj = 4 * vq + u;
+      vreg[u] = (vact && jj < nk) ? *reinterpret_cast<const uint4*>(vbase + (j0 + jj) * HD + 8 * vd8)
+                                  : make_uint4(0u, 0u, 0u, 0u);
+    }
+    int32_t sreg[4][4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int e = threadIdx.x + q * ATT_THREADS, i = e / 16, j4 = 4 * (e % 16);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t j = j0 + j4 + u;
+        sreg[q][u] = (i < nrows && j < s_len[i]) ? p.scores[row_index(i) * p.lds + j] : 0;
+      }
+    }
+    // value planes, transposed: word (dim, keys 4vq..4vq+3)
+    if (vact) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        uint32_t wh = 0, wl = 0;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int32_t v = lane16(vreg[u], e);
+          wh |= uint32_t((v >> 8) + 128) << (8 * u);
+          wl |= uint32_t(v & 255) << (8 * u);
+        }
+        *reinterpret_cast<uint32_t*>(&s_vh[8 * vd8 + e][4 * vq]) = wh;
+        *reinterpret_cast<uint32_t*>(&s_vl[8 * vd8 + e][4 * vq]) = wl;
+      }
+    }
+    // probability planes and the tile's row sums of p
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int e = threadIdx.x + q * ATT_THREADS, i = e / 16, j4 = 4 * (e % 16);
+      uint32_t wh = 0, wl = 0;
+      int32_t psum = 0;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t j = j0 + j4 + u;
+        int32_t pj = 0;
+        if (i < nrows && j < s_len[i]) pj = softmax_prob(exp_of(s_m[i], sreg[q][u], p, lut_one), s_S[i], j, s_len[i], one);
+        psum += pj;
+        wh |= uint32_t(pj >> 8) << (8 * u);
+        wl |= uint32_t(pj & 255) << (8 * u);
+      }
+      *reinterpret_cast<uint32_t*>(&s_ph[i][j4]) = wh;
+      *reinterpret_cast<uint32_t*>(&s_pl[i][j4]) = wl;
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);  // 16 lanes of a row
+      if ((lane & 15) == 0) s_P[i] = psum;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int t = 0; t < TPW; ++t) {
+      const int task = warp * TPW + t;
+      const int r0 = (task % 4) * 16, d0 = (task / 4) * 32;
+      int hh[4][4], hl[4][4], ll[4][4];
+#pragma unroll
+      for (int n = 0; n < 4; ++n)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) hh[n][i] = hl[n][i] = ll[n][i] = 0;
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks) {
+        const int k0 = 32 * ks + 4 * c;
+        const uint32_t ah0 = *reinterpret_cast<const uint32_t*>(&s_ph[r0 + g][k0]);
+        const uint32_t ah1 = *reinterpret_cast<const uint32_t*>(&s_ph[r0 + g + 8][k0]);
+        const uint32_t ah2 = *reinterpret_cast<const uint32_t*>(&s_ph[r0 + g][k0 + 16]);
+        const uint32_t ah3 = *reinterpret_cast<const uint32_t*>(&s_ph[r0 + g + 8][k0 + 16]);
+        const uint32_t al0 = *reinterpret_cast<const uint32_t*>(&s_pl[r0 + g][k0]);
+        const uint32_t al1 = *reinterpret_cast<const uint32_t*>(&s_pl[r0 + g + 8][k0]);
+        const uint32_t al2 = *reinterpret_cast<const uint32_t*>(&s_pl[r0 + g][k0 + 16]);
+        const uint32_t al3 = *reinterpret_cast<const uint32_t*>(&s_pl[r0 + g + 8][k0 + 16]);
+#pragma unroll
+        for (int n = 0; n < 4; ++n) {
+          const int dn = d0 + 8 * n + g;
+          const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(&s_vh[dn][k0]);
+          const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(&s_vh[dn][k0 + 16]);
+          const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(&s_vl[dn][k0]);
+          const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(&s_vl[dn][k0 + 16]);
+          mma_u8u8_16832(hh[n], ah0, ah1, ah2, ah3, bh0, bh1);
+          mma_u8u8_16832(hl[n], ah0, ah1, ah2, ah3, bl0, bl1);
+          mma_u8u8_16832(hl[n], al0, al1, al2, al3, bh0, bh1);
+          mma_u8u8_16832(ll[n], al0, al1, al2, al3, bl0, bl1);
+        }
+      }
+      const int64_t PA = s_P[r0 + g], PB = s_P[r0 + g + 8];
+#pragma unroll
+      for (int n = 0; n < 4; ++n)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          acc[t][n][i] += 65536 * int64_t(hh[n][i]) + 256 * int64_t(hl[n][i]) + int64_t(ll[n][i]) -
+                          32768 * (i < 2 ? PA : PB);
+    }
+  }
+  // phase 3: lane (g, c) of task t holds rows r0 + g (i = 0, 1) and r0 + g + 8
+  // (i = 2, 3), dims d0 + 8n + 2c + (i & 1)
+#pragma unroll
+  for (int t = 0; t < TPW; ++t) {
+    const int task = warp * TPW + t;
+    const int r0 = (task % 4) * 16, d0 = (task / 4) * 32;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int r = r0 + g + 8 * half;
+      if (r >= nrows) continue;
+      int16_t* orow = p.out + (int64_t(b) * T + t0 + r) * p.ldo + int64_t(h) * HD;
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        int16_t o2[2];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const int64_t a = acc[t][n][2 * half + q];
+          int32_t o = clamp16(p.prob_frac > 0 ? rshift_rne_i64(a, p.prob_frac) : a);
+          if (p.out_shift != 0) o = clamp16(rescale_i32_s(o, p.out_shift));
+          o2[q] = int16_t(o);
+        }
+        *reinterpret_cast<uint32_t*>(orow + d0 + 8 * n + 2 * c) =
+            uint32_t(uint16_t(o2[0])) | (uint32_t(uint16_t(o2[1])) << 16);
+      }
+    }
+  }
+}
+
 // Pass 2 for few rows (decode): ATT_DTHREADS threads, chunks of ATT_DCHUNK
 // keys, head_dim a multiple of 8 and at most 128 (so that the
 // ATT_DTHREADS / (hd / 8) >= 32 value-row groups cover a chunk in at most 16

@@ -426,6 +426,22 @@ int run_attention(myl_ctx* ctx, const myl_model* m, myl_session* s, const ModelL
     ctx->launches += 2;
     return MYL_OK;
   }
+  const int64_t tile_blocks = (rows / T) * ((T + ATT_TQ - 1) / ATT_TQ) * m->nq;
+  if (!split && T >= 64 && tile_blocks >= 2 * int64_t(ctx->num_sms) &&
+      (m->hd == 32 || m->hd == 64 || m->hd == 128)) {
+    // prefill: 64-row x 64-key tiles, value rows and probabilities staged once per tile
+    const int64_t B = rows / T;
+    const dim3 g2 = dim3(unsigned(B * ((T + ATT_TQ - 1) / ATT_TQ)), unsigned(m->nq));
+    LaunchCfg l2(ctx, g2, dim3(ATT_THREADS), 0, st);
+    const bool mma = m->prob_frac <= 15;  // p <= 32768: two unsigned bytes
+    if (mma && m->hd == 128) CUDA_TRY(cudaLaunchKernelEx(&l2.cfg, attn_pv_mma_kernel<128>, p));
+    else if (mma && m->hd == 64) CUDA_TRY(cudaLaunchKernelEx(&l2.cfg, attn_pv_mma_kernel<64>, p));
+    else if (m->hd == 128) CUDA_TRY(cudaLaunchKernelEx(&l2.cfg, attn_pv_tile_kernel<4>, p));
+    else if (m->hd == 64) CUDA_TRY(cudaLaunchKernelEx(&l2.cfg, attn_pv_tile_kernel<2>, p));
+    else CUDA_TRY(cudaLaunchKernelEx(&l2.cfg, attn_pv_tile_kernel<1>, p));
+    ctx->launches += 2;
+    return MYL_OK;
+  }
   const int64_t chunk = split ? ATT_CHUNK : ((lds_len + ATT_CHUNK - 1) / ATT_CHUNK) * ATT_CHUNK;
   const dim3 g2 = dim3(unsigned(rows * m->nq), unsigned((lds_len + chunk - 1) / chunk));
   if (m->hd % 8 == 0) {
