@@ -329,6 +329,8 @@ constexpr int ATT_KCH = 4;                          // pass 1: 8-element chunks 
 constexpr int ATT_CHUNK = 256;                      // pass 2 (many rows): keys per piece
 constexpr int ATT_DTHREADS = 512;                   // pass 2 (decode): threads per block
 constexpr int ATT_DCHUNK = 512;                     // pass 2 (decode): keys per block
+constexpr int ATT_TQ = 64;                          // prefill tiles: query rows per block
+constexpr int ATT_TK = 64;                          // prefill tiles: keys per tile
 static_assert(ATT_MAXG == ATT_TPK, "one query head per thread of a key after the reduce-scatter");
 
 __device__ __forceinline__ int dp2a_lo_ss(uint32_t a, uint32_t b, int c) {
@@ -539,6 +541,174 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_scores_kernel(AttnParams p, 
 #pragma unroll
     for (int w = 1; w < ATT_THREADS / 32; ++w) m = max(m, s_mx[w][threadIdx.x]);
     atomicMax(p.rowmax + int64_t(r) * p.nq + h0 + threadIdx.x, uint32_t(m) ^ 0x80000000u);
+  }
+}
+
+// m16n8k32 integer MMA with the signedness of A and B as template flags.
+template <bool AS, bool BS>
+__device__ __forceinline__ void mma_i8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+  if constexpr (AS && BS)
+    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  else if constexpr (AS && !BS)
+    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  else if constexpr (!AS && BS)
+    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  else
+    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Pass 1 for many rows (prefill) on the integer MMA path, head_dim 64 or 128:
+// block (64 consecutive query rows of one sequence, one query head) walks the
+// keys 0..pos in tiles of 64. q = 256 qh + ql and k = 256 kh + kl with the high
+// bytes signed and the low bytes unsigned, so
+//   dot = 65536 sum qh*kh + 256 (sum qh*kl + sum ql*kh) + sum ql*kl
+// from four m16n8k32 MMAs (s8.s8, s8.u8, u8.s8, u8.u8) whose int32 sums are
+// exact (|each| <= 255 * 128 * 128 < 2^23). The query planes are staged once,
+// the key tile's planes per tile (keys [key][dim] are already the B operand's
+// column layout); rows padded to HD + 16 bytes so fragment loads hit distinct
+// banks. Warp task = 16 rows x 32 keys; each score is rescaled as in
+// attn_scores_kernel and stored for keys <= pos; the row maximum is kept in
+// registers over all tiles and written once (this block alone owns the row).
+template <int HD>
+__global__ void __launch_bounds__(ATT_THREADS) attn_scores_mma_kernel(AttnParams p) {
+  pdl_wait();
+  pdl_launch();
+  static_assert(HD == 64 || HD == 128, "head_dim");
+  constexpr int RS = HD + 16;  // padded plane row, bytes
+  __shared__ __align__(16) uint8_t s_qh[ATT_TQ][RS], s_ql[ATT_TQ][RS];
+  __shared__ __align__(16) uint8_t s_kh[ATT_TK][RS], s_kl[ATT_TK][RS];
+  __shared__ int32_t s_mx[2][ATT_TQ];
+  const int T = int(p.T);
+  const int tiles_per_seq = (T + ATT_TQ - 1) / ATT_TQ;
+  const int b = int(blockIdx.x) / tiles_per_seq, t0 = (int(blockIdx.x) % tiles_per_seq) * ATT_TQ;
+  const int h = int(blockIdx.y);
+  const int nrows = min(ATT_TQ, T - t0);
+  const int64_t pos0 = p.pos0[0];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, c = lane & 3;
+  const int16_t* kbase = p.kc.k + int64_t(b) * p.kc.seq_stride + int64_t(p.layer) * p.kc.layer_stride +
+                         int64_t((p.q_head0 + h) / p.G - p.kv_head0) * p.kc.head_stride;
+  constexpr int DG = HD / 8;  // 16-byte (8-element) vectors per row
+  // query planes: 64 rows x DG vectors
+  for (int e = threadIdx.x; e < ATT_TQ * DG; e += ATT_THREADS) {
+    const int i = e / DG, d8 = e % DG;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (i < nrows) v = *reinterpret_cast<const uint4*>(p.qkv + (int64_t(b) * T + t0 + i) * p.ldq + int64_t(h) * HD + 8 * d8);
+    *reinterpret_cast<uint2*>(&s_qh[i][8 * d8]) = make_uint2(__byte_perm(v.x, v.y, 0x7531), __byte_perm(v.z, v.w, 0x7531));
+    *reinterpret_cast<uint2*>(&s_ql[i][8 * d8]) = make_uint2(__byte_perm(v.x, v.y, 0x6420), __byte_perm(v.z, v.w, 0x6420));
+  }
+  // warp task: rows r0..r0+15, keys k0..k0+31 of each tile
+  const int r0 = (warp % 4) * 16, kq0 = (warp / 4) * 32;
+  const int64_t lenA = r0 + g < nrows ? pos0 + t0 + r0 + g + 1 : 0;  // keys of row r0 + g
+  const int64_t lenB = r0 + g + 8 < nrows ? pos0 + t0 + r0 + g + 9 : 0;
+  int32_t mxA = INT32_MIN, mxB = INT32_MIN;
+  const int64_t kend = pos0 + t0 + nrows;  // the longest row of the block
+  for (int64_t j0 = 0; j0 < kend; j0 += ATT_TK) {
+    const int nk = int(min(int64_t(ATT_TK), kend - j0));
+    __syncthreads();  // the previous key tile is consumed (and the query planes are written)
+    {
+      constexpr int KIT = ATT_TK * DG / ATT_THREADS;
+      uint4 kv[KIT];
+#pragma unroll
+      for (int q = 0; q < KIT; ++q) {
+        const int e = threadIdx.x + q * ATT_THREADS, jj = e / DG, d8 = e % DG;
+        kv[q] = jj < nk ? *reinterpret_cast<const uint4*>(kbase + (j0 + jj) * HD + 8 * d8) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int q = 0; q < KIT; ++q) {
+        const int e = threadIdx.x + q * ATT_THREADS, jj = e / DG, d8 = e % DG;
+        *reinterpret_cast<uint2*>(&s_kh[jj][8 * d8]) =
+            make_uint2(__byte_perm(kv[q].x, kv[q].y, 0x7531), __byte_perm(kv[q].z, kv[q].w, 0x7531));
+        *reinterpret_cast<uint2*>(&s_kl[jj][8 * d8]) =
+            make_uint2(__byte_perm(kv[q].x, kv[q].y, 0x6420), __byte_perm(kv[q].z, kv[q].w, 0x6420));
+      }
+    }
+    __syncthreads();
+    int hh[4][4], x[4][4], ll[4][4];
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) hh[n][i] = x[n][i] = ll[n][i] = 0;
+#pragma unroll
+    for (int ks = 0; ks < HD / 32; ++ks) {
+      const int d = 32 * ks + 4 * c;
+      const uint32_t ah0 = *reinterpret_cast<const uint32_t*>(&s_qh[r0 + g][d]);
+      const uint32_t ah1 = *reinterpret_cast<const uint32_t*>(&s_qh[r0 + g + 8][d]);
+      const uint32_t ah2 = *reinterpret_cast<const uint32_t*>(&s_qh[r0 + g][d + 16]);
+      const uint32_t ah3 = *reinterpret_cast<const uint32_t*>(&s_qh[r0 + g + 8][d + 16]);
+      const uint32_t al0 = *reinterpret_cast<const uint32_t*>(&s_ql[r0 + g][d]);
+      const uint32_t al1 = *reinterpret_cast<const uint32_t*>(&s_ql[r0 + g + 8][d]);
+      const uint32_t al2 = *reinterpret_cast<const uint32_t*>(&s_ql[r0 + g][d + 16]);
+      const uint32_t al3 = *reinterpret_cast<const uint32_t*>(&s_ql[r0 + g + 8][d + 16]);
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        const int kn = kq0 + 8 * n + g;
+        const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(&s_kh[kn][d]);
+        const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(&s_kh[kn][d + 16]);
+        const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(&s_kl[kn][d]);
+        const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(&s_kl[kn][d + 16]);
+        mma_i8_16832<true, true>(hh[n], ah0, ah1, ah2, ah3, bh0, bh1);
+        mma_i8_16832<true, false>(x[n], ah0, ah1, ah2, ah3, bl0, bl1);
+        mma_i8_16832<false, true>(x[n], al0, al1, al2, al3, bh0, bh1);
+        mma_i8_16832<false, false>(ll[n], al0, al1, al2, al3, bl0, bl1);
+      }
+    }
+    // scores of rows r0 + g (i = 0, 1) and r0 + g + 8 (i = 2, 3), keys kq0 + 8n + 2c + (i & 1)
+#pragma unroll
+    for (int n = 0; n < 4; ++n) {
+      int32_t sc[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int64_t dot = 65536 * int64_t(hh[n][i]) + 256 * int64_t(x[n][i]) + int64_t(ll[n][i]);
+        const uint64_t prod = uint64_t(dot) * uint64_t(p.score_mult);  // i64 (wrapping)
+        const int64_t v = p.score_shift > 0 ? rshift_rne_i64(int64_t(prod), p.score_shift) : int64_t(prod);
+        sc[i] = int32_t(uint32_t(uint64_t(v)));  // `as i32`
+      }
+      const int64_t j = j0 + kq0 + 8 * n + 2 * c;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int64_t len = half ? lenB : lenA;
+        const int r = r0 + g + 8 * half;
+        if (j >= len) continue;
+        int32_t* dst = p.scores + ((int64_t(b) * T + t0 + r) * p.nq + h) * p.lds + j;
+        int32_t& mx = half ? mxB : mxA;
+        mx = max(mx, sc[2 * half]);
+        if (j + 1 < len) {
+          mx = max(mx, sc[2 * half + 1]);
+          if ((p.lds & 1) == 0) {
+            *reinterpret_cast<int2*>(dst) = make_int2(sc[2 * half], sc[2 * half + 1]);  // 8-byte aligned
+          } else {
+            dst[0] = sc[2 * half];
+            dst[1] = sc[2 * half + 1];
+          }
+        } else {
+          dst[0] = sc[2 * half];
+        }
+      }
+    }
+  }
+  // row maxima: the 4 lanes of a row, then the two warps of a row group
+#pragma unroll
+  for (int o = 1; o < 4; o <<= 1) {
+    mxA = max(mxA, __shfl_xor_sync(0xffffffffu, mxA, o));
+    mxB = max(mxB, __shfl_xor_sync(0xffffffffu, mxB, o));
+  }
+  if (c == 0) {
+    s_mx[warp / 4][r0 + g] = mxA;
+    s_mx[warp / 4][r0 + g + 8] = mxB;
+  }
+  __syncthreads();
+  if (threadIdx.x < nrows) {
+    const int32_t m = max(s_mx[0][threadIdx.x], s_mx[1][threadIdx.x]);
+    p.rowmax[(int64_t(b) * T + t0 + threadIdx.x) * p.nq + h] = uint32_t(m) ^ 0x80000000u;
   }
 }
 
@@ -796,8 +966,6 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_pv_vec_kernel(AttnParams p, 
 // beyond), then thread (row group, 8-dim group) adds p * v for RPT rows and 8
 // dimensions in int64 (hd = 32 * RPT, multiple of 8). Phase 3: round by
 // prob_frac, clamp, rescale, store; the rows' maxima are set back to zero.
-constexpr int ATT_TQ = 64;   // query rows per block
-constexpr int ATT_TK = 64;   // keys per tile
 
 template <int RPT>
 __global__ void __launch_bounds__(ATT_THREADS) attn_pv_tile_kernel(AttnParams p) {

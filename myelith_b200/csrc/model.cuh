@@ -412,13 +412,24 @@ int run_attention(myl_ctx* ctx, const myl_model* m, myl_session* s, const ModelL
   p.rope_frac = m->rope_frac;
   p.out = s->attn;
   p.ldo = m->QD;
-  const int gsub = int((m->G + ATT_MAXG - 1) / ATT_MAXG);
-  const dim3 g1 = dim3(unsigned(rows * m->nkv * gsub), unsigned((lds_len + ATT_SKEYS - 1) / ATT_SKEYS));
-  LaunchCfg l1(ctx, g1, dim3(ATT_THREADS), att_scores_smem(int(m->hd)), st);
-  CUDA_TRY(cudaLaunchKernelEx(&l1.cfg, attn_scores_kernel, p, gsub));
   // few rows (decode): chunks of ATT_DCHUNK keys, so that the keys of a long
   // context spread over many SMs; many rows: one block per row for pass 2
   const bool split = rows <= s->part_rows && rows * m->nq < 4 * int64_t(ctx->num_sms);
+  // prefill of enough rows: both passes in 64-row tiles
+  const int64_t tile_blocks = (rows / T) * ((T + ATT_TQ - 1) / ATT_TQ) * m->nq;
+  const bool tiled = !split && T >= 64 && tile_blocks >= 2 * int64_t(ctx->num_sms) &&
+                     (m->hd == 32 || m->hd == 64 || m->hd == 128);
+  if (tiled && (m->hd == 64 || m->hd == 128)) {
+    const dim3 g1 = dim3(unsigned((rows / T) * ((T + ATT_TQ - 1) / ATT_TQ)), unsigned(m->nq));
+    LaunchCfg l1(ctx, g1, dim3(ATT_THREADS), 0, st);
+    if (m->hd == 128) CUDA_TRY(cudaLaunchKernelEx(&l1.cfg, attn_scores_mma_kernel<128>, p));
+    else CUDA_TRY(cudaLaunchKernelEx(&l1.cfg, attn_scores_mma_kernel<64>, p));
+  } else {
+    const int gsub = int((m->G + ATT_MAXG - 1) / ATT_MAXG);
+    const dim3 g1 = dim3(unsigned(rows * m->nkv * gsub), unsigned((lds_len + ATT_SKEYS - 1) / ATT_SKEYS));
+    LaunchCfg l1(ctx, g1, dim3(ATT_THREADS), att_scores_smem(int(m->hd)), st);
+    CUDA_TRY(cudaLaunchKernelEx(&l1.cfg, attn_scores_kernel, p, gsub));
+  }
   if (split && m->hd % 8 == 0 && m->hd <= 128) {
     const dim3 g2 = dim3(unsigned(rows * m->nq), unsigned((lds_len + ATT_DCHUNK - 1) / ATT_DCHUNK));
     LaunchCfg l2(ctx, g2, dim3(ATT_DTHREADS), 0, st);
@@ -426,9 +437,7 @@ int run_attention(myl_ctx* ctx, const myl_model* m, myl_session* s, const ModelL
     ctx->launches += 2;
     return MYL_OK;
   }
-  const int64_t tile_blocks = (rows / T) * ((T + ATT_TQ - 1) / ATT_TQ) * m->nq;
-  if (!split && T >= 64 && tile_blocks >= 2 * int64_t(ctx->num_sms) &&
-      (m->hd == 32 || m->hd == 64 || m->hd == 128)) {
+  if (tiled) {
     // prefill: 64-row x 64-key tiles, value rows and probabilities staged once per tile
     const int64_t B = rows / T;
     const dim3 g2 = dim3(unsigned(B * ((T + ATT_TQ - 1) / ATT_TQ)), unsigned(m->nq));
