@@ -130,9 +130,12 @@ int myl_linear_w8a16_mult(myl_ctx* ctx, const myl_weight* w, const int16_t* x, i
 
 /* Backend::linear_w8a16 (kernels/src/backend.rs:39-49), same arguments and
  * meaning: one activation row, raw host weight pointer. The weight is
- * uploaded on first use and found again by (W, in, out, w_shifts) address and
- * length; a caller that changes a weight's bytes in place must call
- * myl_backend_forget(ctx, W) first. */
+ * uploaded on first use and found again by (W, in, out, w_shifts) address,
+ * length and shift table, and by a 64-bit digest of the weight bytes computed
+ * on every call (one pass over W, as the reference's own call reads all of W),
+ * so a reused address with new contents is uploaded again. Callers that keep
+ * weights fixed and want no per-call pass register them (myl_weight_register).
+ * myl_backend_forget(ctx, W) drops a cached upload. */
 int myl_backend_linear_w8a16(myl_ctx* ctx, const int16_t* x, const int8_t* W, int16_t* out,
                              uint64_t in_features, uint64_t out_features, const uint8_t* w_shifts,
                              uint8_t act_frac, uint8_t out_frac);
@@ -616,7 +619,14 @@ int myl_attention_int(myl_ctx* ctx, const int16_t* q, int64_t q_len, const int16
  *    device; make that first call before any stream capture.
  *  - The array is shared by all calls on a device and keeps the last call's
  *    contents; calls whose work overlaps on the GPU (different streams or
- *    host threads) race on it and must be serialised by the caller. */
+ *    host threads) race on it and must be serialised by the caller.
+ *  - Every call runs the tensor-core kernel over one K slice with no tail
+ *    split, so a small-M call on a narrow weight (e.g. M = 5, N = 2048: 16
+ *    tiles) fills few of the SMs and can take several times as long as
+ *    myl_linear_dev, which uses the GEMV or splits K for such shapes.
+ *  - The array's device address is looked up once per device index and kept:
+ *    the entry point assumes the device's primary context (the one the CUDA
+ *    runtime uses) for the life of the process, and no cudaDeviceReset. */
 #define MYL_NOALLOC_SCRATCH_BYTES (16 * 1024 * 1024)
 int myl_linear_noalloc_dev(myl_ctx* ctx, const myl_weight* w, const myl_requant* rq,
                            const int16_t* x, int64_t M, int64_t ldx, void* y, int64_t ldy,

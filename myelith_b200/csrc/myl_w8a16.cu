@@ -93,9 +93,11 @@ struct myl_weight {
   int64_t wsum_ld = 0;             // K tiles + 1
   std::vector<uint8_t> w_shifts;
   CUtensorMap tm128{};             // TMA map with a 128-row box (one channel tile)
-  // Backend-trait cache key.
+  // Backend-trait cache key: the host address, and a digest of the bytes
+  // (checked on every hit, so a reused address with new contents re-registers).
   const int8_t* host_W = nullptr;
   const uint8_t* host_shifts = nullptr;
+  uint64_t host_digest = 0;
 };
 
 struct myl_requant {
@@ -1051,16 +1053,41 @@ int myl_linear_w8a16_mult(myl_ctx* ctx, const myl_weight* w, const int16_t* x, i
   return host_linear(ctx, w, x, M, EPI_MULT, 0, reinterpret_cast<const int8_t*>(shift), mult, y);
 }
 
+// 64-bit digest of the weight bytes for the Backend cache: four interleaved
+// multiply-xorshift lanes over 8-byte words (one pass at memory speed), then
+// the tail bytes and the length. Not cryptographic: it tells a changed weight
+// matrix from the cached one.
+static uint64_t weight_digest(const int8_t* W, uint64_t bytes) {
+  const uint64_t k = 0x9E3779B97F4A7C15ull;
+  uint64_t h[4] = {1, 2, 3, 4};
+  const uint8_t* p = reinterpret_cast<const uint8_t*>(W);
+  uint64_t i = 0;
+  for (; i + 32 <= bytes; i += 32) {
+    for (int l = 0; l < 4; ++l) {
+      uint64_t v;
+      std::memcpy(&v, p + i + 8 * l, 8);
+      h[l] = (h[l] ^ v) * k;
+      h[l] ^= h[l] >> 29;
+    }
+  }
+  uint64_t t = bytes;
+  for (; i < bytes; ++i) t = (t ^ p[i]) * k;
+  uint64_t d = t;
+  for (int l = 0; l < 4; ++l) d = (d ^ h[l]) * k + uint64_t(l);
+  return d ^ (d >> 31);
+}
+
 int myl_backend_linear_w8a16(myl_ctx* ctx, const int16_t* x, const int8_t* W, int16_t* out,
                              uint64_t in_features, uint64_t out_features, const uint8_t* w_shifts,
                              uint8_t act_frac, uint8_t out_frac) {
   if (!ctx || !W || !x || !out || !w_shifts) return fail(MYL_ERR_ARG, "null argument");
   myl_weight* w = nullptr;
+  const uint64_t digest = weight_digest(W, in_features * out_features);
   auto it = ctx->backend_cache.find(W);
   if (it != ctx->backend_cache.end()) {
     myl_weight* c = it->second;
     if (uint64_t(c->K) == in_features && uint64_t(c->N) == out_features &&
-        c->host_shifts == w_shifts &&
+        c->host_shifts == w_shifts && c->host_digest == digest &&
         std::memcmp(c->w_shifts.data(), w_shifts, size_t(out_features)) == 0) {
       w = c;
     } else {
@@ -1073,6 +1100,7 @@ int myl_backend_linear_w8a16(myl_ctx* ctx, const int16_t* x, const int8_t* W, in
                             int64_t(in_features), w_shifts, &w));
     w->host_W = W;
     w->host_shifts = w_shifts;
+    w->host_digest = digest;
     ctx->backend_cache[W] = w;
   }
   return myl_linear_w8a16(ctx, w, x, 1, act_frac, out_frac, out);

@@ -362,6 +362,12 @@ def test_cuda_backend_trait(ctx):
     out = np.zeros(N, np.int16)
     be.linear_w8a16(x, W, out, K, N, ws2, 8, 8)
     assert np.array_equal(out, O.linear_w8a16(x, W, K, ws2, 8, 8))
+    # new weight bytes at the same address and the same shift table: re-uploaded
+    W[:] = rng.integers(-127, 128, size=N * K, dtype=np.int8)
+    W[7] = np.int8(-128)
+    out = np.zeros(N, np.int16)
+    be.linear_w8a16(x, W, out, K, N, ws2, 8, 8)
+    assert np.array_equal(out, O.linear_w8a16(x, W, K, ws2, 8, 8))
 
 
 def test_free_functions(ctx):

@@ -76,6 +76,38 @@ def test_noalloc_matches_regular_path_twice(ctx, M, K, N):
     assert np.array_equal(y_na.cpu().numpy(), ref)
 
 
+@pytest.mark.parametrize("M,mode", [(1, "shift16"), (4, "shift16"), (19, "mult16"), (7, "shift32"),
+                                    (SCRATCH_BYTES // (2 * 3584), "shift16")])
+def test_noalloc_every_requant_mode_and_size(ctx, M, mode):
+    """M = 1 and 4 (where the regular path takes the GEMV), the multiplier and
+    i32 requants, and a call that fills the fixed array exactly."""
+    rng = np.random.default_rng(M * 13 + len(mode))
+    K, N = 3584, 640
+    W = rng.integers(-127, 128, size=(N, K), dtype=np.int8)
+    if mode == "mult16":
+        w = ctx.weight(W, K, np.zeros(N, np.uint8))
+        mult = rng.integers(1 << 30, (1 << 31) - 1, size=N, endpoint=True).astype(np.int32)
+        rq = w.requant(myl.RQ_MULT_I16, mult=mult, shift=rng.integers(20, 28, size=N).astype(np.uint8))
+        dt = torch.int16
+    else:
+        w = ctx.weight(W, K, rng.integers(11, 14, size=N).astype(np.uint8))
+        rq = w.requant(myl.RQ_SHIFT_I32 if mode == "shift32" else myl.RQ_SHIFT_I16, act_frac=8,
+                       out_frac=rng.integers(6, 10, size=N).astype(np.uint8))
+        dt = torch.int32 if mode == "shift32" else torch.int16
+    assert 2 * M * K <= SCRATCH_BYTES
+    x = torch.from_numpy(_inputs(rng, M, K)).cuda()
+    y_ref = torch.empty((M, N), dtype=dt, device="cuda")
+    y_na = torch.empty((M, N), dtype=dt, device="cuda")
+    stream = torch.cuda.current_stream()
+    w.linear_dev(rq, x, y_ref, stream)
+    rc = noalloc_fn()(ctx.handle, w.handle, rq.handle, x.data_ptr(), M, x.stride(0), y_na.data_ptr(),
+                      y_na.stride(0), stream.cuda_stream or None)
+    assert rc == 0, myl.load_library().myl_last_error()
+    torch.cuda.synchronize()
+    ctx.synchronize()
+    assert torch.equal(y_na, y_ref)
+
+
 def test_noalloc_leaves_free_memory_unchanged(ctx):
     rng = np.random.default_rng(3)
     M, K, N = 128, 3584, 4096
