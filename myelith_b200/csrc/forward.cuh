@@ -742,6 +742,24 @@ __device__ __forceinline__ int32_t softmax_prob(int32_t e, int32_t S, int64_t j,
   return q;
 }
 
+// softmax_prob for a positive sum S and a non-negative exponential e with the
+// division by S done as a multiplication: with R = ceil(2^63 / S) (one
+// division per row), floor(num / S) = floor(2 num R / 2^64) exactly for
+// num = e * one < 2^31 and S < 2^31 (the error of R, num / 2^63, stays below
+// 1 / S because num * S < 2^62); then the same round-half-even step.
+__device__ __forceinline__ uint64_t softmax_recip(int32_t S) {
+  return S > 0 ? ((uint64_t(1) << 63) + uint64_t(S) - 1) / uint64_t(S) : 0;
+}
+__device__ __forceinline__ int32_t softmax_prob_r(int32_t e, int32_t S, uint64_t R, int64_t j, int64_t len,
+                                                  int32_t one) {
+  if (S <= 0 || e < 0) return softmax_prob(e, S, j, len, one);
+  const uint32_t num = uint32_t(e) * uint32_t(one);
+  uint32_t q = uint32_t(__umul64hi(uint64_t(num) << 1, R));
+  const uint32_t twice = 2 * (num - q * uint32_t(S));  // 2r < 2S < 2^32
+  if (twice > uint32_t(S) || (twice == uint32_t(S) && (q & 1))) ++q;
+  return int32_t(q);
+}
+
 // The sum of the exponentials of a row of `len` scores with maximum m, loads
 // issued eight deep; the exponentials of keys [e0, e0 + ne) also go to s_e.
 // Ends with the block synchronised (s_e complete). NT: threads of the block.
@@ -1124,6 +1142,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_pv_mma_kernel(AttnParams p) 
   __shared__ __align__(16) uint8_t s_vh[HD][ATT_PK], s_vl[HD][ATT_PK];
   __shared__ int32_t s_m[ATT_TQ], s_S[ATT_TQ], s_P[ATT_TQ];
   __shared__ int64_t s_len[ATT_TQ];
+  __shared__ uint64_t s_R[ATT_TQ];
   const int T = int(p.T);
   const int tiles_per_seq = (T + ATT_TQ - 1) / ATT_TQ;
   const int b = int(blockIdx.x) / tiles_per_seq, t0 = (int(blockIdx.x) % tiles_per_seq) * ATT_TQ;
@@ -1156,7 +1175,10 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_pv_mma_kernel(AttnParams p) 
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
-    if (lane == 0) s_S[i] = int32_t(S);  // i32 in the reference; the host bounds len
+    if (lane == 0) {
+      s_S[i] = int32_t(S);  // i32 in the reference; the host bounds len
+      s_R[i] = softmax_recip(int32_t(S));
+    }
   }
   __syncthreads();
   if (threadIdx.x < nrows) p.rowmax[row_index(threadIdx.x)] = 0u;  // every reader is done
@@ -1220,7 +1242,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_pv_mma_kernel(AttnParams p) 
       for (int u = 0; u < 4; ++u) {
         const int64_t j = j0 + j4 + u;
         int32_t pj = 0;
-        if (i < nrows && j < s_len[i]) pj = softmax_prob(exp_of(s_m[i], sreg[q][u], p, lut_one), s_S[i], j, s_len[i], one);
+        if (i < nrows && j < s_len[i])
+          pj = softmax_prob_r(exp_of(s_m[i], sreg[q][u], p, lut_one), s_S[i], s_R[i], j, s_len[i], one);
         psum += pj;
         wh |= uint32_t(pj >> 8) << (8 * u);
         wl |= uint32_t(pj & 255) << (8 * u);
