@@ -512,6 +512,127 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2)
   }
 }
 
+// GEMV for one activation row and long rows (the down projections): a block
+// takes GKS_PAIRS row pairs at a time and each of its warps a quarter of their
+// K range, so a weight matrix of few rows still spreads evenly over every
+// warp; the quarters' exact sums meet in shared memory. Each warp's next loads
+// go out right after its products, before the reduction and the epilogue;
+// the first ones before the programmatic dependency wait.
+constexpr int GKS_Q = 4;                           // K quarters per row pair
+constexpr int GKS_PAIRS = GEMV_WARPS / GKS_Q;      // row pairs per block step
+
+template <int CPL>
+__device__ __forceinline__ void gks_load(int4 (&v)[CPL], const int8_t* __restrict__ row, int c0, int c1, int lane,
+                                         uint64_t pol) {
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const int c = c0 + lane + 32 * i;
+    v[i] = c < c1 ? ldg_stream_v4(row + 16 * c, pol) : make_int4(0, 0, 0, 0);
+  }
+}
+
+template <int CPL>
+__device__ __forceinline__ int64_t gks_dot(const int4 (&v)[CPL], const int4* __restrict__ xa,
+                                           const int4* __restrict__ xb, int c0, int c1, int lane) {
+  int a[4] = {0, 0, 0, 0};  // CPL <= 31 chunks: every partial exact in int32
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const int c = c0 + lane + 32 * i;
+    if (c < c1) {
+      const int4 w = v[i], x0 = xa[c], x1 = xb[c];
+      int& p = a[2 * (i & 1)];
+      int& q = a[2 * (i & 1) + 1];
+      p = __dp2a_lo(x0.x, w.x, p);
+      q = __dp2a_lo(x1.x, w.z, q);
+      p = __dp2a_hi(x0.y, w.x, p);
+      q = __dp2a_hi(x1.y, w.z, q);
+      p = __dp2a_lo(x0.z, w.y, p);
+      q = __dp2a_lo(x1.z, w.w, q);
+      p = __dp2a_hi(x0.w, w.y, p);
+      q = __dp2a_hi(x1.w, w.w, q);
+    }
+  }
+  return int64_t(a[0]) + a[1] + a[2] + a[3];
+}
+
+template <int CPL>
+__global__ void __launch_bounds__(GEMV_THREADS, 2)
+    gemv_ksplit_kernel(const int8_t* __restrict__ W, int64_t ldw, int64_t N,
+                       const int16_t* __restrict__ X, int64_t K, Epilogue ep) {
+  __shared__ int64_t red[GEMV_WARPS][2];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int q = warp % GKS_Q, pw = warp / GKS_Q;
+  const int KS = int((K + 15) & ~int64_t(15));
+  const int C = KS >> 4;
+  const int c0 = q * C / GKS_Q, c1 = (q + 1) * C / GKS_Q;  // this warp's chunks, <= 32 * CPL of them
+  const int64_t np = (N + 1) / 2;
+  const int64_t pstep = int64_t(gridDim.x) * GKS_PAIRS;
+  const uint64_t pol = l2_evict_first_policy();
+  auto row_ptr = [&](int64_t r) { return W + (r < N ? r : N - 1) * ldw; };  // odd N: duplicate, not stored
+  int4 e[CPL], o[CPL];
+  int64_t p = int64_t(blockIdx.x) * GKS_PAIRS + pw;
+  if (p < np) {  // weights do not depend on the previous kernel
+    gks_load<CPL>(e, row_ptr(2 * p), c0, c1, lane, pol);
+    gks_load<CPL>(o, row_ptr(2 * p + 1), c0, c1, lane, pol);
+  }
+  pdl_wait();
+  pdl_launch();
+  extern __shared__ __align__(16) int16_t xs[];  // [KS], two 16-byte planes per chunk
+  {
+    const bool vec_ok = (reinterpret_cast<uintptr_t>(X) & 15) == 0;
+    int4* dst = reinterpret_cast<int4*>(xs);
+    for (int hh = threadIdx.x; hh < (KS >> 3); hh += GEMV_THREADS) {
+      const int i = hh * 8;
+      int4 v;
+      if (vec_ok && i + 8 <= K) {
+        v = __ldg(reinterpret_cast<const int4*>(X + i));
+      } else {
+        alignas(16) int16_t t[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) t[u] = (i + u < K) ? X[i + u] : int16_t(0);
+        v = *reinterpret_cast<const int4*>(t);
+      }
+      dst[(hh & 1) * C + (hh >> 1)] = v;
+    }
+  }
+  __syncthreads();
+  const int4* xa = reinterpret_cast<const int4*>(xs);
+  const int4* xb = xa + C;
+  for (int64_t base = int64_t(blockIdx.x) * GKS_PAIRS; base < np; base += pstep) {  // uniform per block
+    p = base + pw;
+    int64_t s0 = 0, s1 = 0;
+    if (p < np) {
+      s0 = gks_dot<CPL>(e, xa, xb, c0, c1, lane);
+      s1 = gks_dot<CPL>(o, xa, xb, c0, c1, lane);
+    }
+    const int64_t pn = p + pstep;
+    if (pn < np) {
+      gks_load<CPL>(e, row_ptr(2 * pn), c0, c1, lane, pol);
+      gks_load<CPL>(o, row_ptr(2 * pn + 1), c0, c1, lane, pol);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      s0 += __shfl_xor_sync(0xffffffffu, s0, off);
+      s1 += __shfl_xor_sync(0xffffffffu, s1, off);
+    }
+    if (lane == 0) {
+      red[warp][0] = s0;
+      red[warp][1] = s1;
+    }
+    __syncthreads();
+    if (q == 0 && lane == 0 && p < np) {
+      int64_t a[2][1] = {{0}, {0}};
+#pragma unroll
+      for (int k = 0; k < GKS_Q; ++k) {
+        a[0][0] += red[warp + k][0];
+        a[1][0] += red[warp + k][1];
+      }
+      gemv_pair_epilogue<1>(ep, p, N, a);
+    }
+    __syncthreads();  // red is rewritten next step
+  }
+}
+
 // xsum[m] = sum_k x[m][k] (int64), one warp per row: the EPI_W16 correction.
 __global__ void x_row_sums_kernel(const int16_t* __restrict__ X, int64_t ldx, int64_t M, int64_t K,
                                   int64_t* __restrict__ xsum) {
