@@ -34,7 +34,9 @@ e2e        the same metric through the reference-facing host-pointer C ABI
            and output copies around the tensor-parallel device step).
 roofline   the tcgen05 GEMM kernel: algorithmic TOPS per launch from CUDA
            events around each launch, against the effective split-byte peak.
-gemv       decode GEMV (M=1) at both shapes: weight-streaming GB/s vs HBM.
+gemv       decode GEMV (M=1) at both shapes: weight-streaming GB/s vs HBM; and
+           mlp_decode, the decode MLP as the forward runs it (interleaved
+           gate/up GEMV with the SiLU epilogue, then down) at the 7B shapes.
 cpu_baseline  the CPU oracle (C restatement of the reference's Rust loop) on a
            bounded row sample, all host cores, rank 0 at N=1.
 L2: 4 rotating weight sets per shape (>= 4x the 126 MB L2 per step cycle), so
@@ -593,6 +595,44 @@ def emit(line: dict) -> None:
         os.write(_JSON_FD, s)
 
 
+def mlp_decode_gemv(ctx, stream, peaks) -> dict:
+    """The decode MLP as the forward runs it (M=1, 7B shapes): the gate/up
+    GEMV over the interleaved [2I][H] weight with the SiLU pair epilogue, then
+    the down GEMV; two MLPs (407 MB) rotate so the weights stream from HBM."""
+    from myelith_b200.synthetic import kbits, silu_lut_spec
+    H, I = SHAPES[0][0], SHAPES[0][1]
+    rng = np.random.default_rng(11)
+    mlps = []
+    for _ in range(2):
+        mlps.append(myl.Mlp(
+            ctx, rng.integers(-127, 128, size=(I, H), dtype=np.int8),
+            rng.integers(-127, 128, size=(I, H), dtype=np.int8),
+            rng.integers(-127, 128, size=(H, I), dtype=np.int8), H, I,
+            np.full(I, kbits(H), np.uint8), np.full(I, kbits(H), np.uint8), np.full(H, kbits(I), np.uint8),
+            silu_lut_spec(), 8, 7, 7, 7, 6, 8192, 8, np.full(H, 6, np.uint8)))
+    x = torch.from_numpy(np.clip(np.rint(rng.normal(0, 1024, size=(1, H))), -32767, 32767)
+                         .astype(np.int16)).to("cuda")
+    y = torch.empty((1, H), dtype=torch.int16, device="cuda")
+    iters = 20
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            mlps[i % 2].dev(x, y, stream)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for i in range(iters):
+            mlps[i % 2].dev(x, y, stream)
+        b.record(stream)
+        stream.synchronize()
+    us = a.elapsed_time(b) / iters * 1e3
+    wbytes = 3 * H * I
+    for m in mlps:
+        m.release()
+    return {"us": round(us, 2), "weight_gbs": round(wbytes / (us * 1e-6) / 1e9, 1),
+            "frac": round(wbytes / (us * 1e-6) / 1e9 / peaks["hbm_gbs"], 3),
+            "launches": 2, "bytes": "gate/up + down weights (3 * H * I) per call"}
+
+
 def main() -> None:
     global _JSON_FD
     # Native libraries print to file descriptor 1 (NCCL's banner on rank 0):
@@ -1015,7 +1055,12 @@ def main() -> None:
         gemv = {"gbs": round(statistics.mean(gemv_gbs), 1), "peak_gbs": peaks["hbm_gbs"],
                 "frac": round(statistics.mean(gemv_gbs) / peaks["hbm_gbs"], 3),
                 "per_shape_gbs": [round(g, 1) for g in gemv_gbs],
-                "bytes": "N*K weights + 2K act + 2N out + N shift bytes per launch"}
+                "bytes": "N*K weights + 2K act + 2N out + N shift bytes per launch",
+                "mlp_decode": None}
+        try:
+            gemv["mlp_decode"] = mlp_decode_gemv(ctx, stream, peaks)
+        except myl.MylError as e:  # a measurement side leg: report, do not abort the bench
+            gemv["mlp_decode"] = {"error": str(e)}
 
     # ---- the integer forward, configs 2 and 3 (N=1), config 3 tensor-parallel (N>1) ----
     forward = None
