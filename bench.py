@@ -599,6 +599,9 @@ def mlp_decode_gemv(ctx, stream, peaks) -> dict:
     """The decode MLP as the forward runs it (M=1, 7B shapes): the gate/up
     GEMV over the interleaved [2I][H] weight with the SiLU pair epilogue, then
     the down GEMV; two MLPs (407 MB) rotate so the weights stream from HBM."""
+    import torch
+
+    import myelith_b200 as myl
     from myelith_b200.synthetic import kbits, silu_lut_spec
     H, I = SHAPES[0][0], SHAPES[0][1]
     rng = np.random.default_rng(11)
