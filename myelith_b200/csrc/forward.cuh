@@ -149,7 +149,11 @@ __global__ void __launch_bounds__(NORM_CL_THREADS)
   pdl_wait();
   pdl_launch();
   __shared__ __int128 s_part[NORM_CL_THREADS / 32];
-  __shared__ __align__(16) unsigned long long s_cta[2];  // this CTA's square sum (lo, hi)
+  // the cluster's CTA sums of a row, pushed here by every CTA (slot = its
+  // rank, lo and hi words); two sets by row parity, so that a CTA writing the
+  // next row's sum cannot overwrite one still being read (the cluster barrier
+  // of every row keeps the CTAs at most one row apart)
+  __shared__ __align__(16) unsigned long long s_slot[2][NORM_CL][2];
   __shared__ int64_t s_lv;
   __shared__ int s_nf;
   const int rank = int(cluster_ctarank());
@@ -159,7 +163,8 @@ __global__ void __launch_bounds__(NORM_CL_THREADS)
   const bool active = int(threadIdx.x) < vpc && v < nv;
   const bool radd = rp.add || rp.parts;
   const int64_t nrows = out_rows ? n_out_rows : rows;
-  for (int64_t rr = cluster_id_x(); rr < nrows; rr += cluster_count_x()) {
+  int par = 0;
+  for (int64_t rr = cluster_id_x(); rr < nrows; rr += cluster_count_x(), par ^= 1) {
     const int64_t r = out_rows ? out_rows[rr] : rr;
     NormVec vec;
     int64_t acc64 = 0;
@@ -172,28 +177,26 @@ __global__ void __launch_bounds__(NORM_CL_THREADS)
     const __int128 acc = warp_sum_i128((__int128)acc64 + acc128);
     if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = acc;
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (threadIdx.x < NORM_CL) {  // thread k pushes this CTA's sum into CTA k
       __int128 a = 0;
       for (int w = 0; w < NORM_CL_THREADS / 32; ++w) a += s_part[w];
-      s_cta[0] = (unsigned long long)a;
-      s_cta[1] = (unsigned long long)(a >> 64);
+      const uint32_t remote =
+          mapa_shared(static_cast<uint32_t>(__cvta_generic_to_shared(&s_slot[par][rank][0])), threadIdx.x);
+      st_shared_cluster_u64(remote, (unsigned long long)a);
+      st_shared_cluster_u64(remote + 8, (unsigned long long)(a >> 64));
     }
-    cluster_sync_all();  // every CTA's sum is visible to the cluster
+    cluster_sync_all();  // every CTA's sum has landed in every CTA (release / acquire)
     if (threadIdx.x == 0) {
-      const uint32_t local = static_cast<uint32_t>(__cvta_generic_to_shared(s_cta));
       __int128 a = 0;
-      for (int k = 0; k < NORM_CL; ++k) {
-        const uint32_t remote = mapa_shared(local, uint32_t(k));
-        const unsigned long long lo = ld_shared_cluster_u64(remote), hi = ld_shared_cluster_u64(remote + 8);
-        a += (__int128)(((unsigned __int128)hi << 64) | (unsigned __int128)lo);
-      }
+      for (int k = 0; k < NORM_CL; ++k)
+        a += (__int128)(((unsigned __int128)s_slot[par][k][1] << 64) | (unsigned __int128)s_slot[par][k][0]);
       int64_t lv;
       int nf;
       norm_scale(a, np, &lv, &nf);
       s_lv = lv;
       s_nf = nf;
     }
-    cluster_sync_all();  // the remote reads are done; s_lv and s_nf are visible in the CTA
+    __syncthreads();  // s_lv and s_nf
     if (active) *reinterpret_cast<uint4*>(out + rr * ldo + 8 * v) = norm_vec_out(vec, s_lv, s_nf);
   }
 }

@@ -421,7 +421,6 @@ static int launch_gemv_stream(myl_ctx* ctx, const myl_weight* w, const int16_t* 
 static int launch_gemv_ksplit(myl_ctx* ctx, const myl_weight* w, const int16_t* x, const Epilogue& ep,
                               cudaStream_t st) {
   int64_t K = w->K, N = w->N;
-  const int64_t C = (K + 15) / 16;
   void* fn = reinterpret_cast<void*>(&gemv_ksplit_kernel<3>);
   const size_t smem = size_t(round_up16(K)) * 2;
   int resident = 0;

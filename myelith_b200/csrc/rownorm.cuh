@@ -278,10 +278,14 @@ __device__ __forceinline__ void block_row_norm(const int16_t* __restrict__ xr, i
 // ---- one row over a cluster of CTAs (few rows: decode) ---------------------------
 // A row's vectors are split over the NORM_CL CTAs of a cluster (NORM_CL_THREADS
 // threads each, one vector per thread); each CTA's int128 square sum is read
-// by every CTA of the cluster from distributed shared memory, so the per-row
-// work is spread over NORM_CL SMs instead of one.
+// pushed into every CTA of the cluster through distributed shared memory, so
+// the per-row work is spread over NORM_CL SMs instead of one.
 constexpr int NORM_CL = 8;
 constexpr int NORM_CL_THREADS = 128;
+
+__device__ __forceinline__ void st_shared_cluster_u64(uint32_t cluster_addr, unsigned long long v) {
+  asm volatile("st.shared::cluster.u64 [%0], %1;" ::"r"(cluster_addr), "l"(v) : "memory");
+}
 
 __device__ __forceinline__ unsigned long long ld_shared_cluster_u64(uint32_t cluster_addr) {
   unsigned long long v;
