@@ -258,3 +258,32 @@ def test_generate_is_deterministic_and_records_its_inputs():
     om = oracle.OracleModel(spec, 32)
     lg = om.forward(np.r_[p, t1[:3]], 0)
     assert np.array_equal(lg, l1[3])
+
+
+def test_softmax_division_by_reciprocal_is_exact():
+    """The prefill and decode PV kernels divide num = e * one (< 2^31) by the
+    row's exponential sum S (< 2^31) as floor(2 * num * R / 2^64) with
+    R = ceil(2^63 / S), then apply softmax.rs:41-62's round-half-even step.
+    Checked here against exact integer division on random and edge values
+    (u64 / u32 arithmetic emulated with Python integers)."""
+    def exact(num, S):
+        q, r = divmod(num, S)
+        return q + (1 if (2 * r > S or (2 * r == S and q & 1)) else 0)
+
+    def recip(num, S):
+        R = ((1 << 63) + S - 1) // S
+        q = (((num << 1) * R) >> 64) & 0xFFFFFFFF
+        twice = (2 * ((num - q * S) & 0xFFFFFFFF)) & 0xFFFFFFFF
+        return q + (1 if (twice > S or (twice == S and q & 1)) else 0)
+
+    rng = np.random.default_rng(2024)
+    for _ in range(200000):
+        frac = int(rng.integers(0, 31))
+        one = 1 << frac
+        e = int(rng.integers(0, (2**31 - 1) // one + 1))
+        S = int(rng.integers(1, 2**31)) if rng.random() < 0.5 else int(rng.integers(1, 70000))
+        assert recip(e * one, S) == exact(e * one, S), (e, S, one)
+    for S in (1, 2, 3, 5, 16384, 2**30, 2**31 - 1):
+        for num in (0, 1, S - 1, S, S // 2, (S // 2) * 3, 2**31 - 1):
+            if 0 <= num < 2**31:
+                assert recip(num, S) == exact(num, S), (num, S)
