@@ -1328,6 +1328,69 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_pv_mma_kernel(AttnParams p) 
   }
 }
 
+// Pass 2 for few rows (decode), one block per query row for rows of at most
+// ATT_RCAP keys (head_dim a multiple of 8, at most 128): the row's statistics
+// are computed once, every probability is kept in shared memory, and the
+// block's warps walk all value rows (8 loads in flight per thread); no
+// cross-block combination, no fence or counter.
+constexpr int ATT_RCAP = 4096;
+constexpr int ATT_RSHORT = 1024;  // sessions the one-block-per-row kernel is used for
+
+__global__ void __launch_bounds__(ATT_DTHREADS) attn_pv_row_kernel(AttnParams p) {
+  pdl_wait();
+  pdl_launch();
+  __shared__ __align__(16) int64_t s_buf[ATT_DTHREADS * 8];  // probabilities [ATT_RCAP] int32, then the partials
+  __shared__ int64_t s_red[ATT_DTHREADS / 32];
+  int32_t* s_pr = reinterpret_cast<int32_t*>(s_buf);
+  const int row = int(blockIdx.x);
+  const int r = row / p.nq, h = row % p.nq;
+  const int T = int(p.T);
+  const int b = r / T, t = r % T;
+  const int len = int(p.pos0[0] + t + 1);
+  const int hd = p.hd, tpk = hd / 8, kpi = ATT_DTHREADS / tpk;
+  const int kg = int(threadIdx.x) / tpk, dv = int(threadIdx.x) % tpk;
+  const int32_t* sc = p.scores + int64_t(row) * p.lds;
+  const int32_t m = int32_t(p.rowmax[row] ^ 0x80000000u);
+  const int32_t lut_one = p.exp_lut[0];
+  const int32_t S = attn_row_sum<ATT_DTHREADS>(sc, len, m, p, lut_one, s_red, s_pr, 0, len);
+  if (threadIdx.x == 0) p.rowmax[row] = 0u;  // every thread has read it (the sum's barrier)
+  const int32_t one = int32_t(1) << p.prob_frac;
+  const uint64_t R = softmax_recip(S);
+  for (int j = threadIdx.x; j < len; j += ATT_DTHREADS) s_pr[j] = softmax_prob_r(s_pr[j], S, R, j, len, one);
+  __syncthreads();
+  const int16_t* vbase = p.kc.v + int64_t(b) * p.kc.seq_stride + int64_t(p.layer) * p.kc.layer_stride +
+                         int64_t((p.q_head0 + h) / p.G - p.kv_head0) * p.kc.head_stride + 8 * dv;
+  int64_t acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0;
+  for (int j0 = kg; j0 < len; j0 += 8 * kpi) {
+    uint4 vv[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int j = j0 + u * kpi;
+      vv[u] = j < len ? *reinterpret_cast<const uint4*>(vbase + int64_t(j) * hd) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int j = j0 + u * kpi;
+      const int32_t pj = j < len ? s_pr[j] : 0;  // p = 0 adds nothing (attention.rs:79)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += int64_t(pj) * int64_t(lane16(vv[u], e));
+    }
+  }
+  __syncthreads();  // the probabilities are consumed; s_buf takes the partials
+#pragma unroll
+  for (int e = 0; e < 8; ++e) s_buf[kg * hd + 8 * dv + e] = acc[e];
+  __syncthreads();
+  if (int(threadIdx.x) < hd) {
+    int64_t tot = 0;
+    for (int g = 0; g < kpi; ++g) tot += s_buf[g * hd + threadIdx.x];
+    int32_t o = clamp16(p.prob_frac > 0 ? rshift_rne_i64(tot, p.prob_frac) : tot);
+    if (p.out_shift != 0) o = clamp16(rescale_i32_s(o, p.out_shift));
+    p.out[int64_t(r) * p.ldo + int64_t(h) * hd + threadIdx.x] = int16_t(o);
+  }
+}
+
 // Pass 2 for few rows (decode): ATT_DTHREADS threads, chunks of ATT_DCHUNK
 // keys, head_dim a multiple of 8 and at most 128 (so that the
 // ATT_DTHREADS / (hd / 8) >= 32 value-row groups cover a chunk in at most 16

@@ -430,6 +430,15 @@ int run_attention(myl_ctx* ctx, const myl_model* m, myl_session* s, const ModelL
     LaunchCfg l1(ctx, g1, dim3(ATT_THREADS), att_scores_smem(int(m->hd)), st);
     CUDA_TRY(cudaLaunchKernelEx(&l1.cfg, attn_scores_kernel, p, gsub));
   }
+  if (split && m->hd % 8 == 0 && m->hd <= 128 && s->max_pos <= ATT_RSHORT && T == 1) {
+    // short rows (decode of a session of at most ATT_RSHORT positions): one
+    // block per query row. Measured: 0.5B shape at ~600 positions 6 % less
+    // decode time than the chunked kernel; 7B shape at ~2100 positions 21 % more.
+    LaunchCfg l2(ctx, dim3(unsigned(rows * m->nq)), dim3(ATT_DTHREADS), 0, st);
+    CUDA_TRY(cudaLaunchKernelEx(&l2.cfg, attn_pv_row_kernel, p));
+    ctx->launches += 2;
+    return MYL_OK;
+  }
   if (split && m->hd % 8 == 0 && m->hd <= 128) {
     const dim3 g2 = dim3(unsigned(rows * m->nq), unsigned((lds_len + ATT_DCHUNK - 1) / ATT_DCHUNK));
     LaunchCfg l2(ctx, g2, dim3(ATT_DTHREADS), 0, st);
